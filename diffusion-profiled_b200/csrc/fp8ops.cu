@@ -1,0 +1,669 @@
+// fp8ops.cu — host side of the C ABI declared in include/fp8ops.h.
+//
+// One translation unit holds every kernel (quantize.cuh, gemm_kmajor.cuh,
+// gemm_wgrad.cuh) so that they share one device error word.  Host code here
+// validates arguments, encodes TMA tensor maps, picks tile configurations and
+// launches on the caller's stream.  It allocates nothing.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "fp8ops.h"
+#include "gemm_kmajor.cuh"
+#include "gemm_wgrad.cuh"
+#include "quantize.cuh"
+
+using namespace fp8b;
+
+// Device-side error word (one per device that loads this library).
+__device__ int g_fp8_device_error = 0;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+thread_local int t_last_status = FP8_OK;
+thread_local char t_last_msg[512] = {0};
+
+int set_error(int status, const char* fmt, ...) {
+  t_last_status = status;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_msg, sizeof(t_last_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int ok() {
+  t_last_status = FP8_OK;
+  t_last_msg[0] = 0;
+  return FP8_OK;
+}
+
+#define FP8_CUDA_TRY(expr)                                                                       \
+  do {                                                                                           \
+    cudaError_t e_ = (expr);                                                                     \
+    if (e_ != cudaSuccess)                                                                       \
+      return set_error(FP8_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_),     \
+                       __FILE__, __LINE__);                                                      \
+  } while (0)
+
+#define FP8_REQUIRE(cond, status, ...)         \
+  do {                                         \
+    if (!(cond)) return set_error(status, __VA_ARGS__); \
+  } while (0)
+
+// ------------------------------------------------------------------ per-device state
+struct DeviceState {
+  int sm_count = 0;
+  int* err_ptr = nullptr;
+  bool init = false;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  FP8_CUDA_TRY(cudaGetDevice(&dev));
+  FP8_REQUIRE(dev >= 0 && dev < kMaxDevices, FP8_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    if (!st.init) {
+      FP8_CUDA_TRY(cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev));
+      void* p = nullptr;
+      FP8_CUDA_TRY(cudaGetSymbolAddress(&p, g_fp8_device_error));
+      st.err_ptr = static_cast<int*>(p);
+      st.init = true;
+    }
+  }
+  *out = &st;
+  return FP8_OK;
+}
+
+// ------------------------------------------------------------------ TMA tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t status = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    status = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (status == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  FP8_REQUIRE(fn != nullptr, FP8_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(status));
+  *out = fn;
+  return FP8_OK;
+}
+
+// 2-D byte matrix [rows][cols] (cols contiguous), box = 128 bytes x box_rows, 128B swizzle.
+int make_map_2d(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn enc;
+  if (int s = get_encode_fn(&enc)) return s;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
+  cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FP8_REQUIRE(r == CUDA_SUCCESS, FP8_ERR_CUDA, "cuTensorMapEncodeTiled(2d %lldx%lld) failed: %d", (long long)rows,
+              (long long)cols, (int)r);
+  return FP8_OK;
+}
+
+// Conv geometry: 128-pixel tiles that cover whole image rows (or whole images).
+struct ConvTile {
+  int rows;  // image rows per 128-pixel tile
+  int imgs;  // images per 128-pixel tile
+};
+
+bool conv_tile(int height, int width, ConvTile* t) {
+  if (width <= 0 || height <= 0 || width > 128 || 128 % width != 0) return false;
+  const int hw = height * width;
+  if (hw >= 128) {
+    const int rows = 128 / width;
+    if (height % rows != 0) return false;
+    *t = {rows, 1};
+  } else {
+    if (128 % hw != 0) return false;
+    *t = {height, 128 / hw};
+  }
+  return true;
+}
+
+// 4-D NHWC byte tensor [B][H][W][C]; box = 128 channels x W x rows x imgs, 128B swizzle.
+// Out-of-range coordinates (the conv padding ring, images past the batch) read as 0.
+int make_map_conv(CUtensorMap* map, const void* ptr, int batch, int height, int width, int channels,
+                  const ConvTile& t) {
+  EncodeTiledFn enc;
+  if (int s = get_encode_fn(&enc)) return s;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(width),
+                        static_cast<cuuint64_t>(height), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(width) * channels,
+                           static_cast<cuuint64_t>(height) * width * channels};
+  cuuint32_t box[4] = {128u, static_cast<cuuint32_t>(width), static_cast<cuuint32_t>(t.rows),
+                       static_cast<cuuint32_t>(t.imgs)};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FP8_REQUIRE(r == CUDA_SUCCESS, FP8_ERR_CUDA, "cuTensorMapEncodeTiled(conv %dx%dx%dx%d) failed: %d", batch,
+              height, width, channels, (int)r);
+  return FP8_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ------------------------------------------------------------------ tuning overrides
+int g_override_bm_sub = 0;
+int g_override_bn = 0;
+int g_override_group = 0;
+
+// ------------------------------------------------------------------ K-major GEMM launch
+template <int BM_SUB, int BN, int STAGES>
+int launch_kgemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb, KGemmParams p, int sm_count,
+                     cudaStream_t stream) {
+  using Cfg = KGemmConfig<BM_SUB, BN, STAGES>;
+  auto kern = kgemm_fp8_kernel<BM_SUB, BN, STAGES>;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  const int grid = p.num_tiles < sm_count ? p.num_tiles : sm_count;
+  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mb, p);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
+}
+
+struct KGemmShape {
+  int64_t M, N;
+  int k_blocks;
+};
+
+void choose_kgemm_tile(const KGemmShape& s, int sm_count, int* bm_sub, int* bn) {
+  if (g_override_bn > 0 && s.N % g_override_bn == 0) {
+    *bn = g_override_bn;
+    *bm_sub = g_override_bm_sub > 0 ? g_override_bm_sub : 1;
+    if (*bm_sub == 2 && *bn == 256) *bm_sub = 1;
+    if (*bm_sub == 2 && *bn == 64) *bm_sub = 1;
+    return;
+  }
+  const int64_t m_tiles = (s.M + 127) / 128;
+  *bm_sub = 1;
+  for (int cand : {256, 128, 64}) {
+    if (s.N % cand != 0 && !(cand == 64 && s.N % 32 == 0)) continue;
+    const int64_t tiles = m_tiles * ((s.N + cand - 1) / cand);
+    *bn = cand;
+    if (tiles >= sm_count) return;
+  }
+}
+
+int launch_kgemm(const CUtensorMap& ma, const CUtensorMap& mb, KGemmParams p, int bm_sub, int bn, int sm_count,
+                 cudaStream_t stream) {
+  const int64_t m_tiles = (static_cast<int64_t>(p.M) + 128 * bm_sub - 1) / (128 * bm_sub);
+  p.num_n_tiles = (p.N + bn - 1) / bn;
+  const int64_t tiles = m_tiles * p.num_n_tiles;
+  FP8_REQUIRE(tiles < (1ll << 31), FP8_ERR_UNSUPPORTED, "too many tiles");
+  p.num_tiles = static_cast<int>(tiles);
+  if (bm_sub == 1 && bn == 64) return launch_kgemm_cfg<1, 64, 8>(ma, mb, p, sm_count, stream);
+  if (bm_sub == 1 && bn == 128) return launch_kgemm_cfg<1, 128, 6>(ma, mb, p, sm_count, stream);
+  if (bm_sub == 1 && bn == 256) return launch_kgemm_cfg<1, 256, 4>(ma, mb, p, sm_count, stream);
+  if (bm_sub == 2 && bn == 128) return launch_kgemm_cfg<2, 128, 4>(ma, mb, p, sm_count, stream);
+  return set_error(FP8_ERR_UNSUPPORTED, "no K-major GEMM instance for bm_sub=%d bn=%d", bm_sub, bn);
+}
+
+int check_scale_ptrs(const float* a, const float* b) {
+  FP8_REQUIRE(a != nullptr && b != nullptr, FP8_ERR_INVALID_ARGUMENT, "scale pointers must be non-NULL");
+  FP8_REQUIRE(aligned(a, 4) && aligned(b, 4), FP8_ERR_INVALID_ARGUMENT, "scale pointers must be 4-byte aligned");
+  return FP8_OK;
+}
+
+int check_conv_args(int batch, int height, int width, int cin, int cout, ConvTile* t) {
+  FP8_REQUIRE(batch > 0 && height > 0 && width > 0 && cin > 0 && cout > 0, FP8_ERR_INVALID_ARGUMENT,
+              "conv sizes must be positive (B=%d H=%d W=%d Cin=%d Cout=%d)", batch, height, width, cin, cout);
+  FP8_REQUIRE(cin % 128 == 0 && cout % 128 == 0, FP8_ERR_UNSUPPORTED,
+              "conv channels must be multiples of 128 (Cin=%d Cout=%d)", cin, cout);
+  FP8_REQUIRE(conv_tile(height, width, t), FP8_ERR_UNSUPPORTED,
+              "conv spatial %dx%d not tileable into 128-pixel row/image tiles", height, width);
+  FP8_REQUIRE(static_cast<int64_t>(batch) * height * width < (1ll << 31), FP8_ERR_UNSUPPORTED,
+              "conv pixel count too large");
+  return FP8_OK;
+}
+
+// ------------------------------------------------------------------ weight-gradient launch
+template <int G>
+int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, cudaStream_t stream) {
+  using Cfg = WGradConfig<G>;
+  auto kern = wgrad_fp8_kernel<G>;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  kern<<<p.num_tiles * p.splits, kGemmThreads, Cfg::kSmemBytes, stream>>>(mdy, mb, p);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
+}
+
+struct WGradPlan {
+  int group;
+  int num_groups;
+  int num_tiles;
+  int splits;
+  int k_blocks;
+};
+
+WGradPlan plan_wgrad(int64_t m_rows, int64_t n_cols, int64_t pixels, int split_k, int sm_count) {
+  WGradPlan w{};
+  const int boxes = static_cast<int>(n_cols / 128);
+  w.group = 1;
+  if (g_override_group > 0 && boxes % g_override_group == 0) w.group = g_override_group;
+  w.num_groups = boxes / w.group;
+  w.num_tiles = static_cast<int>(m_rows / 128) * w.num_groups;
+  w.k_blocks = static_cast<int>((pixels + 127) / 128);
+  int s = split_k;
+  if (s <= 0) {
+    s = sm_count / w.num_tiles;
+    if (s < 1) s = 1;
+  }
+  if (s > w.k_blocks) s = w.k_blocks;
+  w.splits = s;
+  return w;
+}
+
+int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, int group, cudaStream_t stream) {
+  if (group == 1) return launch_wgrad_cfg<1>(mdy, mb, p, stream);
+  if (group == 2) return launch_wgrad_cfg<2>(mdy, mb, p, stream);
+  if (group == 3) return launch_wgrad_cfg<3>(mdy, mb, p, stream);
+  return set_error(FP8_ERR_UNSUPPORTED, "no weight-gradient instance for group=%d", group);
+}
+
+int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const float* sa, const float* sb,
+                        void* out, int sm_count, cudaStream_t stream) {
+  const int64_t n4 = count / 4;
+  int64_t blocks = (n4 + 255) / 256;
+  if (blocks > 4 * sm_count) blocks = 4 * sm_count;
+  if (blocks < 1) blocks = 1;
+  wgrad_reduce_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(partials, splits, count, sa, sb,
+                                                                    static_cast<__nv_bfloat16*>(out));
+  FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
+}
+
+// ------------------------------------------------------------------ quantize launch helpers
+int quant_partials(int64_t n, int sm_count) {
+  const int64_t vec_threads = (n / 8 + 3) / 4;  // ~4 vectors per thread in the amax pass
+  int64_t blocks = (vec_threads + kQuantThreads - 1) / kQuantThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+int quant_cast_blocks(int64_t n, int sm_count) {
+  int64_t blocks = (n / 8 + 2 * kQuantThreads - 1) / (2 * kQuantThreads);
+  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+}  // namespace
+
+// ======================================================================== C ABI
+extern "C" {
+
+int fp8_abi_version(void) { return 1; }
+
+int fp8_last_error(char* buf, size_t len) {
+  if (buf != nullptr && len > 0) {
+    strncpy(buf, t_last_msg, len - 1);
+    buf[len - 1] = 0;
+  }
+  return t_last_status;
+}
+
+int fp8_device_error(int* code_out, fp8_stream_t stream) {
+  FP8_REQUIRE(code_out != nullptr, FP8_ERR_INVALID_ARGUMENT, "code_out is NULL");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  FP8_CUDA_TRY(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+  int code = 0;
+  FP8_CUDA_TRY(cudaMemcpyFromSymbol(&code, g_fp8_device_error, sizeof(int)));
+  if (code != 0) {
+    const int zero = 0;
+    FP8_CUDA_TRY(cudaMemcpyToSymbol(g_fp8_device_error, &zero, sizeof(int)));
+  }
+  *code_out = code;
+  return ok();
+}
+
+int fp8_sm_count(int* out) {
+  FP8_REQUIRE(out != nullptr, FP8_ERR_INVALID_ARGUMENT, "out is NULL");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  *out = st->sm_count;
+  return ok();
+}
+
+size_t fp8_quantize_workspace_bytes(int64_t n) {
+  int dev = 0;
+  int sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  (void)cudaGetLastError();
+  return static_cast<size_t>(quant_partials(n, sms)) * sizeof(float);
+}
+
+int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, void* workspace,
+                         size_t workspace_bytes, int64_t n, fp8_stream_t stream) {
+  FP8_REQUIRE(n >= 0, FP8_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  FP8_REQUIRE(scale_out != nullptr && aligned(scale_out, 4), FP8_ERR_INVALID_ARGUMENT, "bad scale_out");
+  FP8_REQUIRE(n == 0 || (x_bf16 != nullptr && q_e4m3 != nullptr), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(x_bf16, 2), FP8_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const int parts = quant_partials(n, st->sm_count);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= parts * sizeof(float) && aligned(workspace, 4),
+              FP8_ERR_WORKSPACE, "quantize workspace too small: need %zu bytes", parts * sizeof(float));
+  float* partials = static_cast<float*>(workspace);
+  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
+  const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
+  uint8_t* q = static_cast<uint8_t*>(q_e4m3);
+  const int cast_blocks = quant_cast_blocks(n, st->sm_count);
+  if (vec) {
+    amax_partials_kernel<true><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
+    quantize_cast_kernel<kCurrent, true>
+        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
+  } else {
+    amax_partials_kernel<false><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
+    quantize_cast_kernel<kCurrent, false>
+        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
+  }
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_scale, float* scale_curr_out,
+                         void* workspace, size_t workspace_bytes, int64_t n, fp8_stream_t stream) {
+  FP8_REQUIRE(n >= 0, FP8_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  FP8_REQUIRE(prev_scale != nullptr && aligned(prev_scale, 4), FP8_ERR_INVALID_ARGUMENT, "bad prev_scale");
+  FP8_REQUIRE(scale_curr_out != nullptr && aligned(scale_curr_out, 4), FP8_ERR_INVALID_ARGUMENT,
+              "bad scale_curr_out");
+  FP8_REQUIRE(n == 0 || (x_bf16 != nullptr && q_e4m3 != nullptr), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(x_bf16, 2), FP8_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  // The cast pass writes one partial per CTA, so its grid is the partial count.
+  const int parts = quant_partials(n, st->sm_count);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= parts * sizeof(float) && aligned(workspace, 4),
+              FP8_ERR_WORKSPACE, "quantize workspace too small: need %zu bytes", parts * sizeof(float));
+  float* partials = static_cast<float*>(workspace);
+  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
+  const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
+  uint8_t* q = static_cast<uint8_t*>(q_e4m3);
+  if (vec)
+    quantize_cast_kernel<kDelayed, true>
+        <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
+  else
+    quantize_cast_kernel<kDelayed, false>
+        <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
+  finalize_scale_kernel<<<1, kQuantThreads, 0, cs>>>(partials, parts, scale_curr_out);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int fp8_transpose_2d(const void* src, void* dst, int64_t rows, int64_t cols, fp8_stream_t stream) {
+  FP8_REQUIRE(rows >= 0 && cols >= 0, FP8_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows == 0 || cols == 0) return ok();
+  FP8_REQUIRE(src != nullptr && dst != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  const int64_t gx = (rows + kTransTile - 1) / kTransTile, gy = (cols + kTransTile - 1) / kTransTile;
+  FP8_REQUIRE(gx < (1ll << 31) && gy <= 65535, FP8_ERR_UNSUPPORTED, "transpose too large");
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), 1);
+  transpose_u8_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, cols, cols, rows, 0, 0);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8_stream_t stream) {
+  FP8_REQUIRE(cout > 0 && cin > 0, FP8_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  FP8_REQUIRE(wq != nullptr && wq_t != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  // src [Cout][9][Cin]: per tap a Cout x Cin matrix with leading dim 9*Cin, batch stride Cin.
+  // dst [Cin][9][Cout]: per tap a Cin x Cout matrix with leading dim 9*Cout, batch stride Cout.
+  dim3 grid((cout + kTransTile - 1) / kTransTile, (cin + kTransTile - 1) / kTransTile, 9);
+  transpose_u8_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(wq), static_cast<uint8_t*>(wq_t), cout, cin, 9ll * cin, 9ll * cout, cin, cout);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, const float* sw, const void* bias,
+                    int epilogue, int batch, int height, int width, int cin, int cout, fp8_stream_t stream) {
+  ConvTile t;
+  if (int s = check_conv_args(batch, height, width, cin, cout, &t)) return s;
+  if (int s = check_scale_ptrs(sx, sw)) return s;
+  FP8_REQUIRE(xq && wq && y, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(xq, 16) && aligned(wq, 16) && aligned(y, 16), FP8_ERR_INVALID_ARGUMENT,
+              "conv tensors must be 16-byte aligned");
+  FP8_REQUIRE(epilogue >= FP8_EPILOGUE_NONE && epilogue <= FP8_EPILOGUE_BIAS_SILU, FP8_ERR_INVALID_ARGUMENT,
+              "unknown epilogue %d", epilogue);
+  FP8_REQUIRE(epilogue == FP8_EPILOGUE_NONE || (bias != nullptr && aligned(bias, 16)), FP8_ERR_INVALID_ARGUMENT,
+              "bias epilogue needs a 16-byte aligned bias");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  CUtensorMap ma, mb;
+  if (int s = make_map_conv(&ma, xq, batch, height, width, cin, t)) return s;
+  const int64_t M = static_cast<int64_t>(batch) * height * width;
+  const int k_blocks = 9 * (cin / 128);
+  int bm_sub, bn;
+  choose_kgemm_tile({M, cout, k_blocks}, st->sm_count, &bm_sub, &bn);
+  if (int s = make_map_2d(&mb, wq, cout, 9ll * cin, bn)) return s;
+  KGemmParams p{};
+  p.k_blocks = k_blocks;
+  p.M = static_cast<int>(M);
+  p.N = cout;
+  p.ldo = cout;
+  p.a_conv = 1;
+  p.HW = height * width;
+  p.W = width;
+  p.cchunks = cin / 128;
+  p.tap_sign = 1;
+  p.scale_a = sx;
+  p.scale_b = sw;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.epilogue = epilogue;
+  p.out = static_cast<__nv_bfloat16*>(y);
+  p.err = st->err_ptr;
+  if (int s = launch_kgemm(ma, mb, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream))) return s;
+  return ok();
+}
+
+int fp8_conv3x3_dgrad(const void* dyq, const void* wq_t, void* dx, const float* sdy, const float* sw, int batch,
+                      int height, int width, int cin, int cout, fp8_stream_t stream) {
+  ConvTile t;
+  if (int s = check_conv_args(batch, height, width, cin, cout, &t)) return s;
+  if (int s = check_scale_ptrs(sdy, sw)) return s;
+  FP8_REQUIRE(dyq && wq_t && dx, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(dyq, 16) && aligned(wq_t, 16) && aligned(dx, 16), FP8_ERR_INVALID_ARGUMENT,
+              "conv tensors must be 16-byte aligned");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  CUtensorMap ma, mb;
+  if (int s = make_map_conv(&ma, dyq, batch, height, width, cout, t)) return s;
+  const int64_t M = static_cast<int64_t>(batch) * height * width;
+  const int k_blocks = 9 * (cout / 128);
+  int bm_sub, bn;
+  choose_kgemm_tile({M, cin, k_blocks}, st->sm_count, &bm_sub, &bn);
+  if (int s = make_map_2d(&mb, wq_t, cin, 9ll * cout, bn)) return s;
+  KGemmParams p{};
+  p.k_blocks = k_blocks;
+  p.M = static_cast<int>(M);
+  p.N = cin;
+  p.ldo = cin;
+  p.a_conv = 1;
+  p.HW = height * width;
+  p.W = width;
+  p.cchunks = cout / 128;
+  p.tap_sign = -1;
+  p.scale_a = sdy;
+  p.scale_b = sw;
+  p.bias = nullptr;
+  p.epilogue = kEpiNone;
+  p.out = static_cast<__nv_bfloat16*>(dx);
+  p.err = st->err_ptr;
+  if (int s = launch_kgemm(ma, mb, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream))) return s;
+  return ok();
+}
+
+size_t fp8_conv3x3_wgrad_workspace_bytes(int batch, int height, int width, int cin, int cout, int split_k) {
+  ConvTile t;
+  if (batch <= 0 || cin % 128 != 0 || cout % 128 != 0 || cin <= 0 || cout <= 0 || !conv_tile(height, width, &t))
+    return 0;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  (void)cudaGetLastError();
+  const WGradPlan w = plan_wgrad(cout, 9ll * cin, static_cast<int64_t>(batch) * height * width, split_k, sms);
+  return static_cast<size_t>(w.splits) * cout * 9 * cin * sizeof(float);
+}
+
+int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx, const float* sdy, int batch,
+                      int height, int width, int cin, int cout, int split_k, void* workspace,
+                      size_t workspace_bytes, fp8_stream_t stream) {
+  ConvTile t;
+  if (int s = check_conv_args(batch, height, width, cin, cout, &t)) return s;
+  if (int s = check_scale_ptrs(sx, sdy)) return s;
+  FP8_REQUIRE(xq && dyq && dw, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(xq, 16) && aligned(dyq, 16) && aligned(dw, 16), FP8_ERR_INVALID_ARGUMENT,
+              "conv tensors must be 16-byte aligned");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  const int64_t pixels = static_cast<int64_t>(batch) * height * width;
+  const WGradPlan w = plan_wgrad(cout, 9ll * cin, pixels, split_k, st->sm_count);
+  const size_t need = static_cast<size_t>(w.splits) * cout * 9 * cin * sizeof(float);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
+              "wgrad workspace too small: need %zu bytes (splits=%d)", need, w.splits);
+  CUtensorMap mdy, mx;
+  if (int s = make_map_2d(&mdy, dyq, pixels, cout, 128)) return s;
+  if (int s = make_map_conv(&mx, xq, batch, height, width, cin, t)) return s;
+  WGradParams p{};
+  p.num_tiles = w.num_tiles;
+  p.num_groups = w.num_groups;
+  p.splits = w.splits;
+  p.k_blocks = w.k_blocks;
+  p.b_conv = 1;
+  p.HW = height * width;
+  p.W = width;
+  p.cchunks = cin / 128;
+  p.n_cols = 9 * cin;
+  p.m_rows = cout;
+  p.partials = static_cast<float*>(workspace);
+  p.err = st->err_ptr;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (int s = launch_wgrad(mdy, mx, p, w.group, cs)) return s;
+  if (int s = launch_wgrad_reduce(p.partials, w.splits, static_cast<int64_t>(cout) * 9 * cin, sx, sdy, dw,
+                                  st->sm_count, cs))
+    return s;
+  return ok();
+}
+
+int fp8_gemm(const void* a, const void* b, void* out, const float* sa, const float* sb, const void* bias,
+             int epilogue, int64_t m, int64_t n, int64_t k, fp8_stream_t stream) {
+  FP8_REQUIRE(m > 0 && n > 0 && k > 0, FP8_ERR_INVALID_ARGUMENT, "GEMM sizes must be positive");
+  FP8_REQUIRE(k % 16 == 0, FP8_ERR_UNSUPPORTED, "K must be a multiple of 16 (K=%lld)", (long long)k);
+  FP8_REQUIRE(n % 32 == 0, FP8_ERR_UNSUPPORTED, "N must be a multiple of 32 (N=%lld)", (long long)n);
+  FP8_REQUIRE(m < (1ll << 31) && n < (1ll << 31), FP8_ERR_UNSUPPORTED, "GEMM too large");
+  if (int s = check_scale_ptrs(sa, sb)) return s;
+  FP8_REQUIRE(a && b && out, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(a, 16) && aligned(b, 16) && aligned(out, 16), FP8_ERR_INVALID_ARGUMENT,
+              "GEMM tensors must be 16-byte aligned");
+  FP8_REQUIRE(epilogue >= FP8_EPILOGUE_NONE && epilogue <= FP8_EPILOGUE_BIAS_SILU, FP8_ERR_INVALID_ARGUMENT,
+              "unknown epilogue %d", epilogue);
+  FP8_REQUIRE(epilogue == FP8_EPILOGUE_NONE || (bias != nullptr && aligned(bias, 16)), FP8_ERR_INVALID_ARGUMENT,
+              "bias epilogue needs a 16-byte aligned bias");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  const int k_blocks = static_cast<int>((k + 127) / 128);
+  int bm_sub, bn;
+  choose_kgemm_tile({m, n, k_blocks}, st->sm_count, &bm_sub, &bn);
+  CUtensorMap ma, mb;
+  if (int s = make_map_2d(&ma, a, m, k, 128)) return s;
+  if (int s = make_map_2d(&mb, b, n, k, bn)) return s;
+  KGemmParams p{};
+  p.k_blocks = k_blocks;
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.ldo = static_cast<int>(n);
+  p.a_conv = 0;
+  p.scale_a = sa;
+  p.scale_b = sb;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.epilogue = epilogue;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.err = st->err_ptr;
+  if (int s = launch_kgemm(ma, mb, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream))) return s;
+  return ok();
+}
+
+size_t fp8_gemm_wgrad_workspace_bytes(int64_t m, int64_t n, int64_t k, int split_k) {
+  if (m <= 0 || n <= 0 || k <= 0 || n % 128 != 0 || k % 128 != 0) return 0;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  (void)cudaGetLastError();
+  const WGradPlan w = plan_wgrad(n, k, m, split_k, sms);
+  return static_cast<size_t>(w.splits) * n * k * sizeof(float);
+}
+
+int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, const float* sx, int64_t m,
+                   int64_t n, int64_t k, int split_k, void* workspace, size_t workspace_bytes,
+                   fp8_stream_t stream) {
+  FP8_REQUIRE(m > 0 && n > 0 && k > 0, FP8_ERR_INVALID_ARGUMENT, "GEMM sizes must be positive");
+  FP8_REQUIRE(n % 128 == 0 && k % 128 == 0, FP8_ERR_UNSUPPORTED,
+              "weight-gradient N and K must be multiples of 128 (N=%lld K=%lld)", (long long)n, (long long)k);
+  FP8_REQUIRE(m < (1ll << 31), FP8_ERR_UNSUPPORTED, "GEMM too large");
+  if (int s = check_scale_ptrs(sdy, sx)) return s;
+  FP8_REQUIRE(dy && x && dw, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(dy, 16) && aligned(x, 16) && aligned(dw, 16), FP8_ERR_INVALID_ARGUMENT,
+              "GEMM tensors must be 16-byte aligned");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  const WGradPlan w = plan_wgrad(n, k, m, split_k, st->sm_count);
+  const size_t need = static_cast<size_t>(w.splits) * n * k * sizeof(float);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
+              "wgrad workspace too small: need %zu bytes (splits=%d)", need, w.splits);
+  CUtensorMap mdy, mx;
+  if (int s = make_map_2d(&mdy, dy, m, n, 128)) return s;
+  if (int s = make_map_2d(&mx, x, m, k, 128)) return s;
+  WGradParams p{};
+  p.num_tiles = w.num_tiles;
+  p.num_groups = w.num_groups;
+  p.splits = w.splits;
+  p.k_blocks = w.k_blocks;
+  p.b_conv = 0;
+  p.n_cols = static_cast<int>(k);
+  p.m_rows = static_cast<int>(n);
+  p.partials = static_cast<float*>(workspace);
+  p.err = st->err_ptr;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (int s = launch_wgrad(mdy, mx, p, w.group, cs)) return s;
+  if (int s = launch_wgrad_reduce(p.partials, w.splits, n * k, sdy, sx, dw, st->sm_count, cs)) return s;
+  return ok();
+}
+
+int fp8_set_tile_override(int bm_sub, int bn, int wgrad_group) {
+  FP8_REQUIRE(bm_sub == 0 || bm_sub == 1 || bm_sub == 2, FP8_ERR_INVALID_ARGUMENT, "bm_sub must be 0, 1 or 2");
+  FP8_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 256, FP8_ERR_INVALID_ARGUMENT, "bn must be 0/64/128/256");
+  FP8_REQUIRE(wgrad_group >= 0 && wgrad_group <= 3, FP8_ERR_INVALID_ARGUMENT, "group must be 0..3");
+  g_override_bm_sub = bm_sub;
+  g_override_bn = bn;
+  g_override_group = wgrad_group;
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,278 @@
+// gemm_kmajor.cuh — persistent, warp-specialised tcgen05 FP8 GEMM with both
+// operands K-major:   OUT[m, n] = epi( (sum_k A[m, k] * B[n, k]) * sa * sb )
+//
+// One kernel serves three hot-path ops:
+//   * 3x3 conv forward  (reference conv2d_fwd_fp8_kernel, fp8_kernels.py:168-247):
+//       A = im2col(Xq) fetched tap by tap with 4-D TMA boxes over NHWC Xq; the
+//       zero padding comes from TMA out-of-bounds fill; B = Wq as [Cout][9*Cin].
+//   * 3x3 conv data-grad (reference conv2d_dx_fp8_kernel, fp8_kernels.py:250-318):
+//       A = dYq windows at the flipped taps (offset 1-kh, 1-kw); B = Wq re-laid
+//       out as [Cin][9*Cout].
+//   * FP8 linear (no reference kernel): A = Xq [M][K], B = Wq [N][K] (nn.Linear layout).
+//
+// Roles (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer (one lane) — fills a STAGES-deep smem ring
+//   warp 1      TMEM allocator + MMA issuer (one lane) — tcgen05.mma kind::f8f6f4,
+//               M=128 per sub-tile, N=BN, K=32 per instruction (4 per 128-byte K block)
+//   warps 2..5  epilogue — tcgen05.ld the fp32 accumulator, scale, optional
+//               bias + SiLU, round to bf16 and store; two accumulator buffers in
+//               TMEM let the epilogue of tile i overlap the MMAs of tile i+1.
+#pragma once
+
+#include "sm100_common.cuh"
+
+namespace fp8b {
+
+constexpr int kGemmThreads = 192;
+constexpr int kKBlockBytes = 128;          // one 128-byte swizzle row of K per stage
+constexpr int kSubTileRows = 128;          // UMMA M
+constexpr int kATileBytes = kSubTileRows * kKBlockBytes;  // 16 KB
+
+enum Epilogue : int { kEpiNone = 0, kEpiBias = 1, kEpiBiasSilu = 2 };
+
+struct KGemmParams {
+  int num_n_tiles;
+  int num_tiles;
+  int k_blocks;      // K / 128 (rounded up; TMA zero-fills the ragged end)
+  int M, N;          // logical output extent (rows beyond M / cols beyond N are not stored)
+  int ldo;           // output row stride in elements
+  // A operand source: 1 = 3x3 conv window over NHWC activations, 0 = plain [M][K]
+  int a_conv;
+  int HW, W;         // conv geometry (pixels per image, image width)
+  int cchunks;       // conv: 128-channel chunks per tap
+  int tap_sign;      // conv: +1 forward (input row = out row + kh - 1), -1 data-grad
+  const float* scale_a;
+  const float* scale_b;
+  const __nv_bfloat16* bias;  // [N], used by kEpiBias / kEpiBiasSilu
+  int epilogue;
+  __nv_bfloat16* out;
+  int* err;
+};
+
+template <int BM_SUB, int BN, int STAGES>
+struct KGemmConfig {
+  static_assert(BM_SUB == 1 || BM_SUB == 2, "BM_SUB");
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static constexpr int kBTileBytes = BN * kKBlockBytes;
+  static constexpr int kStageBytes = BM_SUB * kATileBytes + kBTileBytes;
+  static constexpr int kAccCols = BM_SUB * BN;            // TMEM columns per accumulator buffer
+  static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : 2 * kAccCols;  // power of two here
+  static constexpr int kBarBytes = 1024;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kBarBytes + 1024;  // +1024 alignment slack
+  static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
+  static_assert(kSmemBytes <= 232448, "smem");
+};
+
+template <int BM_SUB, int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    kgemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     const KGemmParams p) {
+  using Cfg = KGemmConfig<BM_SUB, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bar_area = smem + STAGES * Cfg::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4 * 32);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int mt = tile / p.num_n_tiles;
+        const int nt = tile - mt * p.num_n_tiles;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::kStageBytes;
+          uint8_t* sb = sa + BM_SUB * kATileBytes;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+          if (p.a_conv) {
+            const int tap = kb / p.cchunks;
+            const int chunk = kb - tap * p.cchunks;
+            const int kh = tap / 3, kw = tap - 3 * (tap / 3);
+            const int dh = p.tap_sign * (kh - 1), dw = p.tap_sign * (kw - 1);
+#pragma unroll
+            for (int sub = 0; sub < BM_SUB; ++sub) {
+              const int m0 = (mt * BM_SUB + sub) * kSubTileRows;
+              const int img = m0 / p.HW;
+              const int h0 = (m0 - img * p.HW) / p.W;
+              tma_load_4d(sa + sub * kATileBytes, &tmap_a, &full_bar[stage], chunk * kKBlockBytes, dw, h0 + dh,
+                          img);
+            }
+          } else {
+#pragma unroll
+            for (int sub = 0; sub < BM_SUB; ++sub) {
+              tma_load_2d(sa + sub * kATileBytes, &tmap_a, &full_bar[stage], kb * kKBlockBytes,
+                          (mt * BM_SUB + sub) * kSubTileRows);
+            }
+          }
+          tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * kKBlockBytes, nt * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the loads already in flight land before the CTA can exit.
+        const int64_t first = issued > STAGES ? issued - STAGES : 0;
+        volatile int never = 0;
+        for (int64_t i = first; i < issued; ++i)
+          mbar_wait(&full_bar[i % STAGES], uint32_t((i / STAGES) & 1), &never, p.err, kErrTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_e4m3(kSubTileRows, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+          const uint32_t sb = sa + BM_SUB * kATileBytes;
+#pragma unroll
+          for (int sub = 0; sub < BM_SUB; ++sub) {
+#pragma unroll
+            for (int k = 0; k < kKBlockBytes / 32; ++k) {
+              const uint64_t adesc = make_smem_desc(sa + sub * kATileBytes + k * 32, 16, 1024);
+              const uint64_t bdesc = make_smem_desc(sb + k * 32, 16, 1024);
+              umma_f8(d_tmem + sub * BN, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull_bar[acc]);
+      }
+      // Drain: wait until every MMA issued by this thread has retired.
+      umma_commit(drain_bar);
+      volatile int never = 0;
+      mbar_wait(drain_bar, 0, &never, p.err, kErrTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const float scale = __ldg(p.scale_a) * __ldg(p.scale_b);
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      const int mt = tile / p.num_n_tiles;
+      const int nt = tile - mt * p.num_n_tiles;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int sub = 0; sub < BM_SUB; ++sub) {
+        const int m = (mt * BM_SUB + sub) * kSubTileRows + row;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols + sub * BN + c, r);
+          tmem_ld_wait();
+          const int n0 = nt * BN + c;
+          if (m < p.M && n0 < p.N) {
+            uint32_t packed[16];
+            if (p.epilogue == kEpiNone) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                packed[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * scale, __uint_as_float(r[2 * i + 1]) * scale);
+            } else {
+              const uint4* bv = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const uint4 b8 = __ldg(bv + v);
+                const uint32_t bw[4] = {b8.x, b8.y, b8.z, b8.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  float lo = __uint_as_float(r[8 * v + 2 * j]) * scale + bf16_lo_f(bw[j]);
+                  float hi = __uint_as_float(r[8 * v + 2 * j + 1]) * scale + bf16_hi_f(bw[j]);
+                  if (p.epilogue == kEpiBiasSilu) {
+                    lo = silu_f32(lo);
+                    hi = silu_f32(hi);
+                  }
+                  packed[4 * v + j] = pack_bf16x2(lo, hi);
+                }
+              }
+            }
+            uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m) * p.ldo + n0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace fp8b

@@ -1,0 +1,251 @@
+// gemm_wgrad.cuh — tcgen05 FP8 weight-gradient GEMM with MN-major operands and
+// split-K over the pixel (token) dimension:
+//
+//   partial[s, co, j] = sum_{m in split s} dY[m, co] * B[m, j]
+//   dW[co, j]         = bf16( (sum_s partial[s, co, j]) * sx * sdy )
+//
+// 3x3 conv (reference conv2d_dw_fp8_kernel + conv2d_dw_reduce_fp8_kernel,
+// fp8_kernels.py:385-468): j = tap * Cin + ci and B[m, j] = Xq at pixel m shifted
+// by the tap (zero outside the image, from TMA out-of-bounds fill), so dW comes
+// out as [Cout][3][3][Cin], the channels_last layout of [Cout, Cin, 3, 3].
+// FP8 linear: B = Xq [M][K] and dW = [N][K], the nn.Linear weight layout.
+//
+// Both operands are read in their natural row-major layout: dY rows are
+// [pixels][Cout] (co contiguous) and X rows are [pixels][C] (channel contiguous),
+// i.e. MN-major for this contraction, so the transpose of dY that the reference
+// performs before its dW kernel (fp8_kernels.py:754-771) is not needed.
+//
+// Each CTA owns one output tile (128 rows of co x G*128 columns of j) and one
+// K split; it is not persistent.  Roles as in the K-major kernel: warp 0 TMA,
+// warp 1 TMEM + MMA, warps 2..5 write fp32 partials.
+#pragma once
+
+#include "gemm_kmajor.cuh"
+
+namespace fp8b {
+
+constexpr int kBoxBytes = 128 * 128;  // one 128 (K rows) x 128 (bytes of MN) TMA box
+
+struct WGradParams {
+  int num_tiles;       // co tiles x column groups
+  int num_groups;      // column groups (G boxes of 128 columns each)
+  int splits;
+  int k_blocks;        // ceil(pixels / 128)
+  int b_conv;          // 1: B is a 3x3 conv window over NHWC X, 0: plain [M][K]
+  int HW, W, cchunks;  // conv geometry
+  int n_cols;          // columns of the partial / dW rows (9*Cin or K)
+  int m_rows;          // rows of dW (Cout or N)
+  float* partials;     // [splits][m_rows][n_cols]
+  int* err;
+};
+
+template <int G>
+struct WGradConfig {
+  static constexpr int kStageBytes = (1 + G) * kBoxBytes;
+  static constexpr int kStages = (G == 1) ? 6 : (G == 2 ? 4 : 3);
+  static constexpr int kAccCols = G * 128;
+  static constexpr int kTmemCols = (kAccCols <= 128) ? 128 : (kAccCols <= 256 ? 256 : 512);
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 1024;
+  static_assert(kSmemBytes <= 232448, "smem");
+};
+
+template <int G>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    wgrad_fp8_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_b,
+                     const WGradParams p) {
+  using Cfg = WGradConfig<G>;
+  constexpr int STAGES = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bar_area = smem + STAGES * Cfg::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* drain_bar = tfull_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int tile = blockIdx.x % p.num_tiles;
+  const int split = blockIdx.x / p.num_tiles;
+  const int co_tile = tile / p.num_groups;
+  const int group = tile - co_tile * p.num_groups;
+  const int kb_begin = static_cast<int>((static_cast<int64_t>(split) * p.k_blocks) / p.splits);
+  const int kb_end = static_cast<int>((static_cast<int64_t>(split + 1) * p.k_blocks) / p.splits);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_dy);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + stage * Cfg::kStageBytes;
+        mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+        const int m0 = kb * 128;
+        tma_load_2d(sa, &tmap_dy, &full_bar[stage], co_tile * 128, m0);
+        if (p.b_conv) {
+          const int img = m0 / p.HW;
+          const int h0 = (m0 - img * p.HW) / p.W;
+#pragma unroll
+          for (int b = 0; b < G; ++b) {
+            const int gb = group * G + b;
+            const int tap = gb / p.cchunks;
+            const int chunk = gb - tap * p.cchunks;
+            const int kh = tap / 3, kw = tap - 3 * (tap / 3);
+            tma_load_4d(sa + (1 + b) * kBoxBytes, &tmap_b, &full_bar[stage], chunk * 128, kw - 1, h0 + kh - 1,
+                        img);
+          }
+        } else {
+#pragma unroll
+          for (int b = 0; b < G; ++b)
+            tma_load_2d(sa + (1 + b) * kBoxBytes, &tmap_b, &full_bar[stage], (group * G + b) * 128, m0);
+        }
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        const int64_t first = issued > STAGES ? issued - STAGES : 0;
+        volatile int never = 0;
+        for (int64_t i = first; i < issued; ++i)
+          mbar_wait(&full_bar[i % STAGES], uint32_t((i / STAGES) & 1), &never, p.err, kErrTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_pair = make_idesc_e4m3(128, 256, 1, 1);
+      constexpr uint32_t idesc_single = make_idesc_e4m3(128, 128, 1, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb_begin; kb < kb_end; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+        const uint32_t accumulate_base = (kb != kb_begin) ? 1u : 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // 4 x 32 K rows per 128-row block
+          // MN-major SW128: 8-row core groups 1024 B apart (SBO); 128-column blocks
+          // of the operand 16 KB apart (LBO).
+          const uint64_t adesc = make_smem_desc(sa + k * 4096, kBoxBytes, 1024);
+          const uint32_t acc = (accumulate_base | (k != 0 ? 1u : 0u));
+#pragma unroll
+          for (int b = 0; b + 1 < G + 1; b += 2) {
+            const uint64_t bdesc = make_smem_desc(sa + (1 + b) * kBoxBytes + k * 4096, kBoxBytes, 1024);
+            if (b + 1 < G)
+              umma_f8(tmem_base + b * 128, adesc, bdesc, idesc_pair, acc);
+            else
+              umma_f8(tmem_base + b * 128, adesc, bdesc, idesc_single, acc);
+          }
+        }
+        umma_commit(&empty_bar[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) umma_commit(tfull_bar);
+      umma_commit(drain_bar);
+      volatile int never = 0;
+      mbar_wait(drain_bar, 0, &never, p.err, kErrTimeoutDrain);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int co = co_tile * 128 + row;
+    const bool has_work = kb_end > kb_begin;
+    bool ok = true;
+    if (has_work) ok = mbar_wait(tfull_bar, 0, abort_flag, p.err, kErrTimeoutEpilogue);
+    if (ok) {
+      tc_fence_after();
+      float* dst_row = p.partials + (static_cast<int64_t>(split) * p.m_rows + co) * p.n_cols;
+#pragma unroll 1
+      for (int c = 0; c < G * 128; c += 32) {
+        const int j0 = group * G * 128 + c;
+        float4* dst = reinterpret_cast<float4*>(dst_row + j0);
+        if (has_work) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+        } else {
+#pragma unroll
+          for (int v = 0; v < 8; ++v) dst[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// dW[i] = bf16( (sum_s partials[s][i]) * sx * sdy ), i over rows*cols (multiple of 4).
+// Same order as the reference reduce (fp8_kernels.py:463-468): sum splits, then scale.
+__global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restrict__ partials, int splits,
+                                                           int64_t count, const float* __restrict__ sa,
+                                                           const float* __restrict__ sb,
+                                                           __nv_bfloat16* __restrict__ out) {
+  const float scale = __ldg(sa) * __ldg(sb);
+  const int64_t n4 = count >> 2;
+  const float4* p4 = reinterpret_cast<const float4*>(partials);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 acc = __ldg(p4 + i);
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = __ldg(p4 + static_cast<int64_t>(s) * n4 + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    uint2 o;
+    o.x = pack_bf16x2(acc.x * scale, acc.y * scale);
+    o.y = pack_bf16x2(acc.z * scale, acc.w * scale);
+    reinterpret_cast<uint2*>(out)[i] = o;
+  }
+}
+
+}  // namespace fp8b

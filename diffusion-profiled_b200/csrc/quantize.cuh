@@ -1,0 +1,205 @@
+// quantize.cuh — per-tensor e4m3 quantisation kernels (bandwidth bound).
+//
+// Semantics restated from the reference (diffusion/fp8_kernels.py):
+//   amax      = max |x|                                   (:54-64, partial_amax_kernel)
+//   scale     = amax > 0 ? amax / 448 : 1.0   (fp32)      (:90-102, finalize_amax_kernel)
+//   q         = e4m3(max(-448, min(x / scale, 448)))      (:105-120, quantize_fp8_kernel)
+// The clamp uses min-then-max with non-NaN-propagating fminf/fmaxf (the
+// reference's tl.minimum / tl.maximum defaults), so x/0 = NaN clamps to +448.
+// The division is IEEE round-to-nearest (__fdiv_rn) and the cast is
+// cvt.rn.satfinite.e4m3x2.f32, which makes the bytes reproducible on the CPU.
+//
+// Current scaling (quantize_fp8, :559-601) is two launches:
+//   amax_partials_kernel : grid-stride |x| max, one fp32 partial per CTA
+//   quantize_cast_kernel<kCurrent> : every CTA folds the partials into amax and
+//                          the scale (the reference's separate finalize launch
+//                          disappears), CTA 0 publishes the scale, then casts.
+// Delayed scaling (quantize_fp8_delayed, :518-556) is one pass plus a 1-CTA fold:
+//   quantize_cast_kernel<kDelayed> : cast with the previous scale and emit amax partials
+//   finalize_scale_kernel          : partials -> current scale
+#pragma once
+
+#include "sm100_common.cuh"
+
+namespace fp8b {
+
+constexpr int kQuantThreads = 256;
+constexpr float kE4M3Max = 448.0f;
+
+enum QuantMode : int { kCurrent = 0, kDelayed = 1 };
+
+// Two floats -> two e4m3 bytes; `lo` lands in the low byte.
+__device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float scale_and_clamp(float v, float s) {
+  float t = __fdiv_rn(v, s);
+  t = fminf(t, kE4M3Max);   // tl.minimum(scaled, FP8_MAX)
+  return fmaxf(-kE4M3Max, t);  // tl.maximum(-FP8_MAX, .)
+}
+
+__device__ __forceinline__ float absmax_word(float m, uint32_t w) {
+  return fmaxf(m, fmaxf(fabsf(bf16_lo_f(w)), fabsf(bf16_hi_f(w))));
+}
+
+// Block-wide max of a non-negative value; result valid in every thread.
+__device__ __forceinline__ float block_max(float v) {
+  __shared__ float red[kQuantThreads / 32];
+  __shared__ float result;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < (kQuantThreads / 32) ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
+    if (lane == 0) result = w;
+  }
+  __syncthreads();
+  return result;
+}
+
+__device__ __forceinline__ float scale_from_amax(float amax) {
+  return amax > 0.0f ? __fdiv_rn(amax, kE4M3Max) : 1.0f;
+}
+
+// Fold `count` partial maxima into the tensor scale (every CTA does this; the
+// partials are a few KB and L2 resident).
+__device__ __forceinline__ float fold_partials_to_scale(const float* __restrict__ partials, int count) {
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) m = fmaxf(m, partials[i]);
+  return scale_from_amax(block_max(m));
+}
+
+// Pass 1 of current scaling: |x| max per CTA.  VEC: x is 16-byte aligned.
+template <bool VEC>
+__global__ void __launch_bounds__(kQuantThreads) amax_partials_kernel(const uint16_t* __restrict__ x, int64_t n,
+                                                                      float* __restrict__ partials) {
+  float m = 0.0f;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (VEC) {
+    const int64_t nvec = n >> 3;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    int64_t i = tid;
+    for (; i + 3 * nthreads < nvec; i += 4 * nthreads) {
+      uint4 a = __ldg(xv + i), b = __ldg(xv + i + nthreads), c = __ldg(xv + i + 2 * nthreads),
+            d = __ldg(xv + i + 3 * nthreads);
+      m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
+      m = absmax_word(m, b.x); m = absmax_word(m, b.y); m = absmax_word(m, b.z); m = absmax_word(m, b.w);
+      m = absmax_word(m, c.x); m = absmax_word(m, c.y); m = absmax_word(m, c.z); m = absmax_word(m, c.w);
+      m = absmax_word(m, d.x); m = absmax_word(m, d.y); m = absmax_word(m, d.z); m = absmax_word(m, d.w);
+    }
+    for (; i < nvec; i += nthreads) {
+      uint4 a = __ldg(xv + i);
+      m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
+    }
+    done = nvec << 3;
+  }
+  for (int64_t i = done + tid; i < n; i += nthreads) m = fmaxf(m, fabsf(__uint_as_float(uint32_t(x[i]) << 16)));
+  m = block_max(m);
+  if (threadIdx.x == 0) partials[blockIdx.x] = m;
+}
+
+__device__ __forceinline__ uint32_t cast4(uint32_t w0, uint32_t w1, float s) {
+  const uint32_t lo = cvt_e4m3x2(scale_and_clamp(bf16_lo_f(w0), s), scale_and_clamp(bf16_hi_f(w0), s));
+  const uint32_t hi = cvt_e4m3x2(scale_and_clamp(bf16_lo_f(w1), s), scale_and_clamp(bf16_hi_f(w1), s));
+  return lo | (hi << 16);
+}
+
+// Cast pass.  kCurrent: scale = fold(partials_in); CTA 0 stores it to scale_out.
+//             kDelayed: scale = *prev_scale; each CTA also writes its |x| max
+//                       to partials_out[blockIdx.x].
+// VEC: x 16-byte aligned and q 8-byte aligned.
+template <int MODE, bool VEC>
+__global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
+    const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
+    int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
+    float* __restrict__ partials_out) {
+  float s;
+  if (MODE == kCurrent) {
+    s = fold_partials_to_scale(partials_in, n_partials);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
+  } else {
+    s = *prev_scale;
+  }
+  float m = 0.0f;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (VEC) {
+    const int64_t nvec = n >> 3;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    uint2* qv = reinterpret_cast<uint2*>(q);
+    int64_t i = tid;
+    for (; i + nthreads < nvec; i += 2 * nthreads) {
+      const uint4 a = __ldg(xv + i), b = __ldg(xv + i + nthreads);
+      if (MODE == kDelayed) {
+        m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
+        m = absmax_word(m, b.x); m = absmax_word(m, b.y); m = absmax_word(m, b.z); m = absmax_word(m, b.w);
+      }
+      qv[i] = make_uint2(cast4(a.x, a.y, s), cast4(a.z, a.w, s));
+      qv[i + nthreads] = make_uint2(cast4(b.x, b.y, s), cast4(b.z, b.w, s));
+    }
+    for (; i < nvec; i += nthreads) {
+      const uint4 a = __ldg(xv + i);
+      if (MODE == kDelayed) {
+        m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
+      }
+      qv[i] = make_uint2(cast4(a.x, a.y, s), cast4(a.z, a.w, s));
+    }
+    done = nvec << 3;
+  }
+  for (int64_t i = done + tid; i < n; i += nthreads) {
+    const float v = __uint_as_float(uint32_t(x[i]) << 16);
+    if (MODE == kDelayed) m = fmaxf(m, fabsf(v));
+    q[i] = static_cast<uint8_t>(cvt_e4m3x2(scale_and_clamp(v, s), 0.0f) & 0xFFu);
+  }
+  if (MODE == kDelayed) {
+    m = block_max(m);
+    if (threadIdx.x == 0) partials_out[blockIdx.x] = m;
+  }
+}
+
+__global__ void __launch_bounds__(kQuantThreads) finalize_scale_kernel(const float* __restrict__ partials,
+                                                                       int n_partials, float* __restrict__ scale_out) {
+  const float s = fold_partials_to_scale(partials, n_partials);
+  if (threadIdx.x == 0) *scale_out = s;
+}
+
+// ---------------------------------------------------------------- byte transposes
+// dst[b][c][r] = src[b][r][c] for a batch of R x C byte matrices with arbitrary
+// leading dimensions.  Used for the conv weight re-layout
+// [Cout][3][3][Cin] -> [Cin][3][3][Cout] (batch = the 9 taps) and for the plain
+// 2-D transpose the reference applies to dY (fp8_kernels.py:321-337).
+constexpr int kTransTile = 64;
+
+__global__ void __launch_bounds__(256) transpose_u8_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                           int64_t rows, int64_t cols, int64_t src_ld,
+                                                           int64_t dst_ld, int64_t src_bstride,
+                                                           int64_t dst_bstride) {
+  __shared__ uint8_t tile[kTransTile][kTransTile + 4];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kTransTile;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * kTransTile;
+  const uint8_t* s = src + static_cast<int64_t>(blockIdx.z) * src_bstride;
+  uint8_t* d = dst + static_cast<int64_t>(blockIdx.z) * dst_bstride;
+  for (int i = threadIdx.x; i < kTransTile * kTransTile; i += blockDim.x) {
+    const int rr = i / kTransTile, cc = i % kTransTile;
+    const int64_t r = r0 + rr, c = c0 + cc;
+    if (r < rows && c < cols) tile[rr][cc] = s[r * src_ld + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kTransTile * kTransTile; i += blockDim.x) {
+    const int cc = i / kTransTile, rr = i % kTransTile;
+    const int64_t r = r0 + rr, c = c0 + cc;
+    if (r < rows && c < cols) d[c * dst_ld + r] = tile[rr][cc];
+  }
+}
+
+}  // namespace fp8b

@@ -1,0 +1,358 @@
+"""Torch custom ops over the C ABI (``fp8_b200::*``).
+
+Each op allocates its outputs and workspaces with the torch caching allocator,
+launches the native kernels on torch's current stream and never synchronises,
+so the ops can be captured in CUDA graphs.  They are registered with
+``torch.library.custom_op`` plus fake (meta) implementations so that
+``torch.compile`` treats them as opaque nodes.
+
+Layouts: 4-D activations and conv weights are channels_last (physically NHWC /
+[Cout][3][3][Cin]); FP8 tensors are ``torch.float8_e4m3fn``; scales are fp32
+0-d device tensors holding the dequantisation scale ``amax / 448``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_void_p
+
+import torch
+
+from . import _lib
+
+FP8_DTYPE = torch.float8_e4m3fn
+
+EPILOGUE_NONE = _lib.EPILOGUE_NONE
+EPILOGUE_BIAS = _lib.EPILOGUE_BIAS
+EPILOGUE_BIAS_SILU = _lib.EPILOGUE_BIAS_SILU
+
+
+def _ptr(t: torch.Tensor | None) -> c_void_p:
+    return c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(device: torch.device) -> c_void_p:
+    return c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError("fp8_b200 ops run on CUDA tensors only (there is no CPU path)")
+        if t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {t.device} vs {dev}")
+    return dev
+
+
+def _nhwc_dims(t: torch.Tensor) -> tuple[int, int, int, int]:
+    b, c, h, w = t.shape
+    return b, c, h, w
+
+
+# ----------------------------------------------------------------------------- quantize
+@torch.library.custom_op("fp8_b200::quantize_current", mutates_args=())
+def quantize_current(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-tensor e4m3 quantisation with the tensor's own amax (fp8_kernels.py:559-601)."""
+    dev = _require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"quantize expects bfloat16, got {x.dtype}")
+    if not (x.is_contiguous() or x.is_contiguous(memory_format=torch.channels_last)):
+        raise RuntimeError("quantize expects a dense (contiguous or channels_last) tensor")
+    q = torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format)
+    scale = torch.empty((), device=dev, dtype=torch.float32)
+    n = x.numel()
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.fp8_quantize_workspace_bytes(n)
+        ws = torch.empty(max(ws_bytes // 4, 1), device=dev, dtype=torch.float32)
+        _lib.check(
+            lib.fp8_quantize_current(_ptr(x), _ptr(q), _ptr(scale), _ptr(ws), ws.numel() * 4, n, _stream(dev)),
+            "fp8_quantize_current",
+        )
+    return q, scale
+
+
+@quantize_current.register_fake
+def _(x):
+    return torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format), x.new_empty(
+        (), dtype=torch.float32
+    )
+
+
+@torch.library.custom_op("fp8_b200::quantize_delayed", mutates_args=())
+def quantize_delayed(x: torch.Tensor, prev_scale: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Cast with ``prev_scale``; also return the scale of x's own amax (fp8_kernels.py:518-556)."""
+    dev = _require_cuda(x, prev_scale)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"quantize expects bfloat16, got {x.dtype}")
+    if prev_scale.dtype != torch.float32 or prev_scale.numel() != 1:
+        raise RuntimeError("prev_scale must be a one-element float32 tensor")
+    if not (x.is_contiguous() or x.is_contiguous(memory_format=torch.channels_last)):
+        raise RuntimeError("quantize expects a dense (contiguous or channels_last) tensor")
+    q = torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format)
+    scale = torch.empty((), device=dev, dtype=torch.float32)
+    n = x.numel()
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.fp8_quantize_workspace_bytes(n)
+        ws = torch.empty(max(ws_bytes // 4, 1), device=dev, dtype=torch.float32)
+        _lib.check(
+            lib.fp8_quantize_delayed(
+                _ptr(x), _ptr(q), _ptr(prev_scale), _ptr(scale), _ptr(ws), ws.numel() * 4, n, _stream(dev)
+            ),
+            "fp8_quantize_delayed",
+        )
+    return q, scale
+
+
+@quantize_delayed.register_fake
+def _(x, prev_scale):
+    return torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format), x.new_empty(
+        (), dtype=torch.float32
+    )
+
+
+# ----------------------------------------------------------------------------- transposes
+@torch.library.custom_op("fp8_b200::transpose_2d", mutates_args=())
+def transpose_2d(src: torch.Tensor) -> torch.Tensor:
+    """[R, C] -> [C, R] byte transpose (fp8_kernels.py:321-337)."""
+    dev = _require_cuda(src)
+    if src.dim() != 2 or not src.is_contiguous() or src.element_size() != 1:
+        raise RuntimeError("transpose_2d expects a contiguous 2-D 1-byte tensor")
+    rows, cols = src.shape
+    dst = torch.empty((cols, rows), device=dev, dtype=src.dtype)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_transpose_2d", _ptr(src), _ptr(dst), rows, cols, _stream(dev))
+    return dst
+
+
+@transpose_2d.register_fake
+def _(src):
+    return src.new_empty((src.shape[1], src.shape[0]))
+
+
+def _conv_weight_t(wq: torch.Tensor) -> torch.Tensor:
+    """[Cout, Cin, 3, 3] channels_last e4m3 -> [Cin][3][3][Cout] bytes (as [Cin, 9*Cout])."""
+    cout, cin = wq.shape[0], wq.shape[1]
+    wt = torch.empty((cin, 9 * cout), device=wq.device, dtype=FP8_DTYPE)
+    _lib.call("fp8_conv_weight_transpose", _ptr(wq), _ptr(wt), cout, cin, _stream(wq.device))
+    return wt
+
+
+# ----------------------------------------------------------------------------- conv 3x3
+def _check_conv_operand(t: torch.Tensor, name: str) -> None:
+    if t.dim() != 4:
+        raise RuntimeError(f"{name} must be 4-D")
+    if t.dtype != FP8_DTYPE:
+        raise RuntimeError(f"{name} must be float8_e4m3fn, got {t.dtype}")
+    if not t.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError(f"{name} must be channels_last contiguous")
+
+
+def _check_scale(s: torch.Tensor, dev: torch.device, name: str) -> None:
+    if s.device != dev or s.dtype != torch.float32 or s.numel() != 1:
+        raise RuntimeError(f"{name} must be a one-element float32 tensor on {dev}")
+
+
+@torch.library.custom_op("fp8_b200::conv3x3_fwd", mutates_args=())
+def conv3x3_fwd(
+    xq: torch.Tensor,
+    wq: torch.Tensor,
+    sx: torch.Tensor,
+    sw: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    epilogue: int = EPILOGUE_NONE,
+) -> torch.Tensor:
+    """bf16 channels_last ``conv2d(xq*sx, wq*sw, padding=1)`` (+bias, +SiLU)."""
+    dev = _require_cuda(xq, wq)
+    _check_conv_operand(xq, "x")
+    _check_conv_operand(wq, "weight")
+    _check_scale(sx, dev, "x_scale")
+    _check_scale(sw, dev, "weight_scale")
+    b, cin, h, w = xq.shape
+    cout = wq.shape[0]
+    if tuple(wq.shape[1:]) != (cin, 3, 3):
+        raise RuntimeError(f"weight shape {tuple(wq.shape)} does not match Cin={cin} 3x3")
+    if epilogue != EPILOGUE_NONE:
+        if bias is None or bias.dtype != torch.bfloat16 or bias.numel() != cout or not bias.is_contiguous():
+            raise RuntimeError("bias epilogue needs a contiguous bf16 bias of Cout elements")
+    y = torch.empty((b, cout, h, w), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "fp8_conv3x3_fwd", _ptr(xq), _ptr(wq), _ptr(y), _ptr(sx), _ptr(sw), _ptr(bias), epilogue, b, h, w,
+            cin, cout, _stream(dev),
+        )
+    return y
+
+
+@conv3x3_fwd.register_fake
+def _(xq, wq, sx, sw, bias=None, epilogue=EPILOGUE_NONE):
+    b, _, h, w = xq.shape
+    return torch.empty(
+        (b, wq.shape[0], h, w), device=xq.device, dtype=torch.bfloat16, memory_format=torch.channels_last
+    )
+
+
+@torch.library.custom_op("fp8_b200::conv3x3_dgrad", mutates_args=())
+def conv3x3_dgrad(dyq: torch.Tensor, wq: torch.Tensor, sdy: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    """bf16 channels_last input gradient of the 3x3 conv (fp8_kernels.py:671-709)."""
+    dev = _require_cuda(dyq, wq)
+    _check_conv_operand(dyq, "dy")
+    _check_conv_operand(wq, "weight")
+    _check_scale(sdy, dev, "dy_scale")
+    _check_scale(sw, dev, "weight_scale")
+    b, cout, h, w = dyq.shape
+    cin = wq.shape[1]
+    if tuple(wq.shape) != (cout, cin, 3, 3):
+        raise RuntimeError(f"weight shape {tuple(wq.shape)} does not match Cout={cout} 3x3")
+    dx = torch.empty((b, cin, h, w), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        wt = _conv_weight_t(wq)
+        _lib.call(
+            "fp8_conv3x3_dgrad", _ptr(dyq), _ptr(wt), _ptr(dx), _ptr(sdy), _ptr(sw), b, h, w, cin, cout,
+            _stream(dev),
+        )
+    return dx
+
+
+@conv3x3_dgrad.register_fake
+def _(dyq, wq, sdy, sw):
+    b, _, h, w = dyq.shape
+    return torch.empty(
+        (b, wq.shape[1], h, w), device=dyq.device, dtype=torch.bfloat16, memory_format=torch.channels_last
+    )
+
+
+@torch.library.custom_op("fp8_b200::conv3x3_wgrad", mutates_args=())
+def conv3x3_wgrad(
+    xq: torch.Tensor, dyq: torch.Tensor, sx: torch.Tensor, sdy: torch.Tensor, split_k: int = 0
+) -> torch.Tensor:
+    """bf16 channels_last weight gradient [Cout, Cin, 3, 3] (fp8_kernels.py:723-808)."""
+    dev = _require_cuda(xq, dyq)
+    _check_conv_operand(xq, "x")
+    _check_conv_operand(dyq, "dy")
+    _check_scale(sx, dev, "x_scale")
+    _check_scale(sdy, dev, "dy_scale")
+    b, cin, h, w = xq.shape
+    cout = dyq.shape[1]
+    if (dyq.shape[0], dyq.shape[2], dyq.shape[3]) != (b, h, w):
+        raise RuntimeError("x and dy batch/spatial dims differ")
+    dw = torch.empty((cout, cin, 3, 3), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.fp8_conv3x3_wgrad_workspace_bytes(b, h, w, cin, cout, split_k)
+        ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
+        _lib.check(
+            lib.fp8_conv3x3_wgrad(
+                _ptr(xq), _ptr(dyq), _ptr(dw), _ptr(sx), _ptr(sdy), b, h, w, cin, cout, split_k, _ptr(ws),
+                ws.numel() * 4, _stream(dev),
+            ),
+            "fp8_conv3x3_wgrad",
+        )
+    return dw
+
+
+@conv3x3_wgrad.register_fake
+def _(xq, dyq, sx, sdy, split_k=0):
+    return torch.empty(
+        (dyq.shape[1], xq.shape[1], 3, 3), device=xq.device, dtype=torch.bfloat16, memory_format=torch.channels_last
+    )
+
+
+# ----------------------------------------------------------------------------- GEMM (linear)
+def _check_2d_fp8(t: torch.Tensor, name: str) -> None:
+    if t.dim() != 2 or t.dtype != FP8_DTYPE or not t.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous 2-D float8_e4m3fn tensor")
+
+
+@torch.library.custom_op("fp8_b200::gemm", mutates_args=())
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    sa: torch.Tensor,
+    sb: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    epilogue: int = EPILOGUE_NONE,
+) -> torch.Tensor:
+    """``out[M, N] = (a[M, K] @ b[N, K].T) * sa * sb`` (+bias, +SiLU), bf16."""
+    dev = _require_cuda(a, b)
+    _check_2d_fp8(a, "a")
+    _check_2d_fp8(b, "b")
+    _check_scale(sa, dev, "a_scale")
+    _check_scale(sb, dev, "b_scale")
+    m, k = a.shape
+    n = b.shape[0]
+    if b.shape[1] != k:
+        raise RuntimeError(f"inner dims differ: a {tuple(a.shape)} b {tuple(b.shape)}")
+    if epilogue != EPILOGUE_NONE:
+        if bias is None or bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous():
+            raise RuntimeError("bias epilogue needs a contiguous bf16 bias of N elements")
+    out = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "fp8_gemm", _ptr(a), _ptr(b), _ptr(out), _ptr(sa), _ptr(sb), _ptr(bias), epilogue, m, n, k,
+            _stream(dev),
+        )
+    return out
+
+
+@gemm.register_fake
+def _(a, b, sa, sb, bias=None, epilogue=EPILOGUE_NONE):
+    return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("fp8_b200::gemm_wgrad", mutates_args=())
+def gemm_wgrad(dy: torch.Tensor, x: torch.Tensor, sdy: torch.Tensor, sx: torch.Tensor, split_k: int = 0) -> torch.Tensor:
+    """``dw[N, K] = dy[M, N].T @ x[M, K] * sdy * sx`` in bf16."""
+    dev = _require_cuda(dy, x)
+    _check_2d_fp8(dy, "dy")
+    _check_2d_fp8(x, "x")
+    _check_scale(sdy, dev, "dy_scale")
+    _check_scale(sx, dev, "x_scale")
+    m, n = dy.shape
+    if x.shape[0] != m:
+        raise RuntimeError("dy and x row counts differ")
+    k = x.shape[1]
+    dw = torch.empty((n, k), device=dev, dtype=torch.bfloat16)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.fp8_gemm_wgrad_workspace_bytes(m, n, k, split_k)
+        ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
+        _lib.check(
+            lib.fp8_gemm_wgrad(
+                _ptr(dy), _ptr(x), _ptr(dw), _ptr(sdy), _ptr(sx), m, n, k, split_k, _ptr(ws), ws.numel() * 4,
+                _stream(dev),
+            ),
+            "fp8_gemm_wgrad",
+        )
+    return dw
+
+
+@gemm_wgrad.register_fake
+def _(dy, x, sdy, sx, split_k=0):
+    return dy.new_empty((dy.shape[1], x.shape[1]), dtype=torch.bfloat16)
+
+
+def device_error(device: torch.device | None = None) -> int:
+    """Read and clear the device error word (synchronises the current stream)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        return _lib.device_error(torch.cuda.current_stream(dev).cuda_stream)
+
+
+__all__ = [
+    "FP8_DTYPE",
+    "EPILOGUE_NONE",
+    "EPILOGUE_BIAS",
+    "EPILOGUE_BIAS_SILU",
+    "quantize_current",
+    "quantize_delayed",
+    "transpose_2d",
+    "conv3x3_fwd",
+    "conv3x3_dgrad",
+    "conv3x3_wgrad",
+    "gemm",
+    "gemm_wgrad",
+    "device_error",
+]

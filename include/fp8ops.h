@@ -1,0 +1,153 @@
+/*
+ * fp8ops.h — C ABI of the B200 (sm_100a) FP8 hot path.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream, enqueues
+ * its kernels on that stream and returns a status code.  None of them allocates
+ * device memory or synchronises: buffers (outputs and workspaces) are owned by
+ * the caller, so the calls can be captured in CUDA graphs.  Scales are fp32
+ * scalars in device memory (the reference keeps them as 0-d CUDA tensors and
+ * never reads them on the host).
+ *
+ * FP8 tensors are float8_e4m3fn bytes.  "scale" is the dequantisation scale
+ * s = amax / 448 of the reference (x ~= q * s).
+ *
+ * Reference interfaces (fattorib/diffusion-profiled, diffusion/fp8_kernels.py)
+ * that each entry point replaces are cited per function.  The reference is
+ * Python + Triton; its "FFI" is the Python call into the Triton launcher, so the
+ * binding a maintainer adds is the ctypes layer shown in INTEGRATION.md.
+ */
+#ifndef FP8OPS_H_
+#define FP8OPS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ABI-compatible with cudaStream_t / CUstream. NULL = legacy default stream. */
+typedef struct CUstream_st* fp8_stream_t;
+
+/* Status codes. */
+#define FP8_OK 0
+#define FP8_ERR_INVALID_ARGUMENT 1 /* bad pointer, size, alignment or shape      */
+#define FP8_ERR_UNSUPPORTED 2      /* shape outside what the kernels implement    */
+#define FP8_ERR_CUDA 3             /* a CUDA runtime / driver call failed          */
+#define FP8_ERR_WORKSPACE 4        /* workspace too small                          */
+
+/* Epilogues of the forward GEMM / conv. */
+#define FP8_EPILOGUE_NONE 0      /* y = acc * sa * sb                              */
+#define FP8_EPILOGUE_BIAS 1      /* y = acc * sa * sb + bias[n]                    */
+#define FP8_EPILOGUE_BIAS_SILU 2 /* y = silu(acc * sa * sb + bias[n])              */
+
+/* Version of this ABI (incremented on any signature change). */
+int fp8_abi_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated to
+ * len) into buf and returns the status code of that error (FP8_OK if none). */
+int fp8_last_error(char* buf, size_t len);
+
+/* Reads and clears the device-side error word of the current device (kernels
+ * record a code there when a bounded wait inside them times out).  Synchronises
+ * `stream`.  *code_out = 0 means no device error was recorded. */
+int fp8_device_error(int* code_out, fp8_stream_t stream);
+
+/* Number of streaming multiprocessors of the current device (launch sizing). */
+int fp8_sm_count(int* out);
+
+/* ------------------------------------------------------------------ quantize */
+
+/* Bytes of fp32 workspace the quantize calls need for n elements. */
+size_t fp8_quantize_workspace_bytes(int64_t n);
+
+/* Current (just-in-time) per-tensor scaling of n bf16 values:
+ *   *scale_out = amax>0 ? amax/448 : 1;  q = e4m3(clamp(x / *scale_out, +-448)).
+ * Replaces quantize_fp8 (fp8_kernels.py:559-601) and its kernels
+ * partial_amax_kernel (:54-64), finalize_amax_kernel (:90-102) and
+ * quantize_fp8_kernel (:105-120).  The element order of x is irrelevant (the
+ * reference also treats the tensor as flat memory); q has the same order. */
+int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, void* workspace,
+                         size_t workspace_bytes, int64_t n, fp8_stream_t stream);
+
+/* Delayed scaling: q = e4m3(clamp(x / *prev_scale, +-448)) and
+ * *scale_curr_out = scale of x's own amax.
+ * Replaces quantize_fp8_delayed (fp8_kernels.py:518-556) and
+ * partial_amax_kernel_delayed (:69-87) + finalize_amax_kernel (:90-102). */
+int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_scale, float* scale_curr_out,
+                         void* workspace, size_t workspace_bytes, int64_t n, fp8_stream_t stream);
+
+/* --------------------------------------------------------------- transposes */
+
+/* dst[c][r] = src[r][c] for a rows x cols byte matrix.
+ * Replaces transpose_fp8_2d_kernel (fp8_kernels.py:321-337). */
+int fp8_transpose_2d(const void* src, void* dst, int64_t rows, int64_t cols, fp8_stream_t stream);
+
+/* Conv weight re-layout for the data-grad: wq [Cout][3][3][Cin] (channels_last
+ * [Cout,Cin,3,3]) -> wq_t [Cin][3][3][Cout].  No reference counterpart: the
+ * reference's dX kernel gathers W with strided loads (fp8_kernels.py:306-309). */
+int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8_stream_t stream);
+
+/* ------------------------------------------------------------ 3x3 conv (pad 1) */
+
+/* y[n,h,w,co] = epi( sum_{kh,kw,ci} xq[n,h+kh-1,w+kw-1,ci] * wq[co,kh,kw,ci] * sx * sw )
+ * xq: NHWC e4m3 [B][H][W][Cin]; wq: [Cout][3][3][Cin]; y: NHWC bf16 [B][H][W][Cout];
+ * bias: bf16 [Cout] (only read by the bias epilogues, else may be NULL).
+ * Replaces conv2d_fwd_fp8_prequantized + conv2d_fwd_fp8_kernel
+ * (fp8_kernels.py:604-639, :168-247).  Cin, Cout: multiples of 128; the width
+ * must divide 128 and a 128-pixel tile must cover whole rows of one image or
+ * whole images (true for every shape in SUPPORTED_UNET_SHAPES). */
+int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, const float* sw, const void* bias,
+                    int epilogue, int batch, int height, int width, int cin, int cout, fp8_stream_t stream);
+
+/* dx[n,h,w,ci] = sum_{kh,kw,co} dyq[n,h+1-kh,w+1-kw,co] * wq[co,kh,kw,ci] * sdy * sw
+ * dyq: NHWC e4m3 [B][H][W][Cout]; wq_t: [Cin][3][3][Cout] (fp8_conv_weight_transpose);
+ * dx: NHWC bf16 [B][H][W][Cin].
+ * Replaces conv2d_bwd_input_fp8_prequantized + conv2d_dx_fp8_kernel
+ * (fp8_kernels.py:671-709, :250-318). */
+int fp8_conv3x3_dgrad(const void* dyq, const void* wq_t, void* dx, const float* sdy, const float* sw, int batch,
+                      int height, int width, int cin, int cout, fp8_stream_t stream);
+
+/* Workspace bytes of fp8_conv3x3_wgrad for a split count (split_k <= 0: the
+ * library's choice, the same one fp8_conv3x3_wgrad makes for split_k <= 0). */
+size_t fp8_conv3x3_wgrad_workspace_bytes(int batch, int height, int width, int cin, int cout, int split_k);
+
+/* dw[co,kh,kw,ci] = sum_{n,h,w} dyq[n,h,w,co] * xq[n,h+kh-1,w+kw-1,ci] * sx * sdy
+ * xq: NHWC e4m3 [B][H][W][Cin]; dyq: NHWC e4m3 [B][H][W][Cout]; dw: bf16
+ * [Cout][3][3][Cin] (channels_last [Cout,Cin,3,3]).  Split-K over pixels with
+ * fp32 partials in the workspace.
+ * Replaces conv2d_bwd_weight_fp8_prequantized (fp8_kernels.py:723-808) with
+ * its transpose_fp8_2d_kernel, conv2d_dw_fp8_kernel and
+ * conv2d_dw_reduce_fp8_kernel (:321-337, :385-468). */
+int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx, const float* sdy, int batch,
+                      int height, int width, int cin, int cout, int split_k, void* workspace,
+                      size_t workspace_bytes, fp8_stream_t stream);
+
+/* --------------------------------------------------------------- FP8 linear */
+
+/* out[m,n] = epi( sum_k a[m,k] * b[n,k] * sa * sb ), a: [M][K] e4m3, b: [N][K]
+ * e4m3 (the nn.Linear weight layout), out: [M][N] bf16, bias: bf16 [N].
+ * No reference kernel: the reference runs these linears (unet.py:101, 171-172,
+ * 331-336) in bf16; this is the new scaled FP8 GEMM.  K % 16 == 0, N % 32 == 0. */
+int fp8_gemm(const void* a, const void* b, void* out, const float* sa, const float* sb, const void* bias,
+             int epilogue, int64_t m, int64_t n, int64_t k, fp8_stream_t stream);
+
+/* Workspace bytes of fp8_gemm_wgrad. */
+size_t fp8_gemm_wgrad_workspace_bytes(int64_t m, int64_t n, int64_t k, int split_k);
+
+/* dw[n,k] = sum_m dy[m,n] * x[m,k] * sdy * sx; dy: [M][N] e4m3, x: [M][K] e4m3,
+ * dw: [N][K] bf16.  N, K multiples of 128.  No reference counterpart. */
+int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, const float* sx, int64_t m,
+                   int64_t n, int64_t k, int split_k, void* workspace, size_t workspace_bytes,
+                   fp8_stream_t stream);
+
+/* Tuning override for the K-major GEMM tile (bm_sub in {1,2}, bn in {64,128,256})
+ * and the weight-gradient column group (g in {1,2,3}); 0 restores the built-in
+ * choice.  Process-wide; meant for benchmarks and tests. */
+int fp8_set_tile_override(int bm_sub, int bn, int wgrad_group);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP8OPS_H_ */

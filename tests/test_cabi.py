@@ -1,0 +1,148 @@
+"""CPU tests of the C ABI: the library loads, exports every declared symbol, and
+validates arguments on the host (no CUDA call is reached for invalid sizes)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from ctypes import c_void_p
+from pathlib import Path
+
+import pytest
+
+from fp8_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "fp8ops.h"
+
+
+def _declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int|size_t)\s+(fp8_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_functions():
+    names = _declared_functions()
+    assert "fp8_conv3x3_fwd" in names and "fp8_quantize_current" in names and len(names) >= 15
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    missing = [n for n in _declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol():
+    assert sorted(_lib.exported_symbols()) == _declared_functions()
+
+
+def test_abi_version():
+    assert _lib.load().fp8_abi_version() == 1
+
+
+def _status_and_message(fn, *args):
+    status = fn(*args)
+    code, msg = _lib.last_error()
+    return status, code, msg
+
+
+def test_conv_rejects_unsupported_channels_without_touching_cuda():
+    lib = _lib.load()
+    null = c_void_p(0)
+    status, code, msg = _status_and_message(
+        lib.fp8_conv3x3_fwd, null, null, null, null, null, null, 0, 2, 8, 8, 100, 128, null
+    )
+    assert status == _lib.FP8_ERR_UNSUPPORTED and code == status and "multiples of 128" in msg
+
+
+def test_conv_rejects_untileable_spatial():
+    lib = _lib.load()
+    null = c_void_p(0)
+    status, _, msg = _status_and_message(lib.fp8_conv3x3_dgrad, null, null, null, null, null, 2, 7, 7, 128, 128,
+                                         null)
+    assert status == _lib.FP8_ERR_UNSUPPORTED and "tileable" in msg
+
+
+def test_conv_rejects_nonpositive_sizes():
+    lib = _lib.load()
+    null = c_void_p(0)
+    status, _, _ = _status_and_message(lib.fp8_conv3x3_wgrad, null, null, null, null, null, 0, 8, 8, 128, 128, 0,
+                                       null, 0, null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT
+
+
+def test_gemm_rejects_bad_k_and_n():
+    lib = _lib.load()
+    null = c_void_p(0)
+    assert lib.fp8_gemm(null, null, null, null, null, null, 0, 16, 64, 10, null) == _lib.FP8_ERR_UNSUPPORTED
+    assert lib.fp8_gemm(null, null, null, null, null, null, 0, 16, 40, 64, null) == _lib.FP8_ERR_UNSUPPORTED
+    assert lib.fp8_gemm_wgrad(null, null, null, null, null, 16, 64, 128, 0, null, 0, null) == \
+        _lib.FP8_ERR_UNSUPPORTED
+
+
+def test_quantize_rejects_negative_n_and_null_scale():
+    lib = _lib.load()
+    null = c_void_p(0)
+    assert lib.fp8_quantize_current(null, null, null, null, 0, -1, null) == _lib.FP8_ERR_INVALID_ARGUMENT
+    status, _, msg = _status_and_message(lib.fp8_quantize_delayed, null, null, null, null, null, 0, 4, null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "prev_scale" in msg
+
+
+def test_tile_override_validation():
+    lib = _lib.load()
+    assert lib.fp8_set_tile_override(3, 0, 0) == _lib.FP8_ERR_INVALID_ARGUMENT
+    assert lib.fp8_set_tile_override(0, 96, 0) == _lib.FP8_ERR_INVALID_ARGUMENT
+    assert lib.fp8_set_tile_override(0, 0, 0) == _lib.FP8_OK
+    assert _lib.last_error() == (0, "")
+
+
+def test_check_raises_with_library_message():
+    lib = _lib.load()
+    with pytest.raises(RuntimeError, match="bm_sub"):
+        _lib.check(lib.fp8_set_tile_override(5, 0, 0), "fp8_set_tile_override")
+
+
+def test_workspace_queries_are_host_only():
+    lib = _lib.load()
+    # unsupported geometry -> 0 bytes, no CUDA needed
+    assert lib.fp8_conv3x3_wgrad_workspace_bytes(2, 7, 7, 128, 128, 0) == 0
+    assert lib.fp8_gemm_wgrad_workspace_bytes(16, 100, 128, 0) == 0
+    # explicit split count: splits * Cout * 9 * Cin * 4 bytes
+    assert lib.fp8_conv3x3_wgrad_workspace_bytes(2, 8, 8, 128, 128, 1) == 128 * 9 * 128 * 4
+
+
+def test_python_ops_have_no_cpu_path():
+    import torch
+
+    from fp8_b200 import fp8_kernels, ops
+
+    x = torch.zeros(1, 128, 8, 8, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.quantize_current(x)
+    with pytest.raises(AssertionError):  # the reference API asserts is_cuda (fp8_kernels.py:560-562)
+        fp8_kernels.quantize_fp8(x)
+
+
+def test_reference_api_names_present():
+    from fp8_b200 import fp8_kernels
+
+    for name in [
+        "FP8_DTYPE", "FP8_MAX_E4M3", "SUPPORTED_UNET_SHAPES", "quantize_fp8", "quantize_fp8_delayed",
+        "conv2d_fwd_fp8", "conv2d_fwd_fp8_prequantized", "conv2d_fwd_fp8_delayed", "conv2d_bwd_input_fp8",
+        "conv2d_bwd_input_fp8_prequantized", "conv2d_bwd_weight_fp8", "conv2d_bwd_weight_fp8_prequantized",
+        "Conv2dFP8Specialized", "triton_conv2d_fp8", "torch_checks_conv", "fwd_shapes", "xgrad_shapes",
+        "wgrad_shapes", "torch_checks_scale",
+    ]:
+        assert hasattr(fp8_kernels, name), name
+    assert fp8_kernels.FP8_MAX_E4M3 == 448.0
+    assert len(fp8_kernels.SUPPORTED_UNET_SHAPES) == 9
+
+
+def test_ctypes_signatures_match_header_arity():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for name, (_, args) in _lib._SIGNATURES.items():
+        m = re.search(rf"\b{name}\s*\((.*?)\)\s*;", text, flags=re.S)
+        assert m, name
+        params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(args), (name, len(params), len(args))
+    assert ctypes.sizeof(ctypes.c_size_t) == 8

@@ -1,0 +1,176 @@
+"""GPU parity: the tcgen05 3x3 conv (fwd, dX, dW) against the CPU oracle and the reference golden outputs.
+
+Tolerance (the parity contract): max|y - ref| / max|ref| <= 1e-2, where the
+reference is fp32 accumulation of the same e4m3 operands times the scales, in bf16.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import fp8_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+SUPPORTED = [
+    (128, 128, 32, 32),
+    (128, 256, 32, 32),
+    (256, 256, 16, 16),
+    (512, 256, 16, 16),
+    (256, 256, 8, 8),
+    (512, 256, 8, 8),
+    (512, 128, 32, 32),
+    (256, 256, 32, 32),
+    (256, 256, 4, 4),
+]
+
+
+def _rand_q(shape, seed, device, scale=1.0):
+    """Random channels_last bf16 tensor quantised by the oracle -> (fp8 on device, scale on device)."""
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    q, s = oracle.quantize_tensor(x)
+    return q.to(device), s.to(device)
+
+
+def _golden_case(golden, tag, device):
+    b, cin, cout, h, w = (int(v) for v in golden[f"{tag}_dims"])
+
+    def fp8(arr, shape):
+        return torch.from_numpy(arr.reshape(shape)).view(torch.float8_e4m3fn).permute(0, 3, 1, 2).to(device)
+
+    def bf16(arr, shape):
+        return torch.from_numpy(arr.reshape(shape).view(np.int16)).view(torch.bfloat16).permute(0, 3, 1, 2)
+
+    sx, sw, sdy = (torch.tensor(float(v), device=device) for v in golden[f"{tag}_scales"])
+    return dict(
+        xq=fp8(golden[f"{tag}_xq"], (b, h, w, cin)),
+        wq=fp8(golden[f"{tag}_wq"], (cout, 3, 3, cin)),
+        dyq=fp8(golden[f"{tag}_dyq"], (b, h, w, cout)),
+        sx=sx, sw=sw, sdy=sdy,
+        y=bf16(golden[f"{tag}_y"], (b, h, w, cout)),
+        dx=bf16(golden[f"{tag}_dx"], (b, h, w, cin)),
+        dw=bf16(golden[f"{tag}_dw"], (cout, 3, 3, cin)),
+    )
+
+
+@pytest.mark.parametrize("tag", ["c128x8", "c256x4", "c128to256x16"])
+def test_conv_matches_reference_kernel_outputs(cuda, golden, tag):
+    from fp8_b200 import ops
+
+    c = _golden_case(golden, tag, cuda)
+    y = ops.conv3x3_fwd(c["xq"], c["wq"], c["sx"], c["sw"])
+    dx = ops.conv3x3_dgrad(c["dyq"], c["wq"], c["sdy"], c["sw"])
+    dw = ops.conv3x3_wgrad(c["xq"], c["dyq"], c["sx"], c["sdy"])
+    assert y.is_contiguous(memory_format=torch.channels_last)
+    assert oracle.max_rel_err(y, c["y"]) <= TOL
+    assert oracle.max_rel_err(dx, c["dx"]) <= TOL
+    assert oracle.max_rel_err(dw, c["dw"]) <= TOL
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("cin,cout,h,w", SUPPORTED)
+def test_conv_fwd_all_unet_shapes(cuda, cin, cout, h, w):
+    from fp8_b200 import ops
+
+    b = max(2, 256 // (h * w))
+    xq, sx = _rand_q((b, cin, h, w), seed=cin + cout + h, device=cuda)
+    wq, sw = _rand_q((cout, cin, 3, 3), seed=7 + cin, device=cuda, scale=0.05)
+    y = ops.conv3x3_fwd(xq, wq, sx, sw)
+    ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())
+    assert oracle.max_rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("cin,cout,h,w", SUPPORTED)
+def test_conv_dgrad_all_unet_shapes(cuda, cin, cout, h, w):
+    from fp8_b200 import ops
+
+    b = max(2, 256 // (h * w))
+    dyq, sdy = _rand_q((b, cout, h, w), seed=cin * 3 + cout + h, device=cuda, scale=1e-2)
+    wq, sw = _rand_q((cout, cin, 3, 3), seed=9 + cin, device=cuda, scale=0.05)
+    dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
+    ref = oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())
+    assert oracle.max_rel_err(dx, ref) <= TOL
+
+
+@pytest.mark.parametrize("cin,cout,h,w", SUPPORTED)
+def test_conv_wgrad_all_unet_shapes(cuda, cin, cout, h, w):
+    from fp8_b200 import ops
+
+    b = max(2, 512 // (h * w))
+    xq, sx = _rand_q((b, cin, h, w), seed=cin + 5 * cout + h, device=cuda)
+    dyq, sdy = _rand_q((b, cout, h, w), seed=cin + 7 * cout + w, device=cuda, scale=1e-2)
+    dw = ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+    ref = oracle.conv_dw(xq.cpu(), dyq.cpu(), sx.item(), sdy.item())
+    assert dw.shape == (cout, cin, 3, 3) and dw.is_contiguous(memory_format=torch.channels_last)
+    assert oracle.max_rel_err(dw, ref) <= TOL
+
+
+@pytest.mark.parametrize("split_k", [1, 3, 7])
+def test_conv_wgrad_split_counts(cuda, split_k):
+    from fp8_b200 import ops
+
+    xq, sx = _rand_q((8, 128, 16, 16), seed=21, device=cuda)
+    dyq, sdy = _rand_q((8, 128, 16, 16), seed=22, device=cuda, scale=1e-2)
+    dw = ops.conv3x3_wgrad(xq, dyq, sx, sdy, split_k)
+    ref = oracle.conv_dw(xq.cpu(), dyq.cpu(), sx.item(), sdy.item())
+    assert oracle.max_rel_err(dw, ref) <= TOL
+
+
+@pytest.mark.parametrize("epilogue", [1, 2])
+def test_conv_fwd_bias_silu_epilogue(cuda, epilogue):
+    from fp8_b200 import ops
+
+    xq, sx = _rand_q((4, 128, 32, 32), seed=31, device=cuda)
+    wq, sw = _rand_q((128, 128, 3, 3), seed=32, device=cuda, scale=0.05)
+    g = torch.Generator().manual_seed(33)
+    bias = (torch.randn(128, generator=g) * 0.1).to(torch.bfloat16)
+    y = ops.conv3x3_fwd(xq, wq, sx, sw, bias.to(cuda), epilogue)
+    ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item(), bias=bias, silu=(epilogue == 2))
+    assert oracle.max_rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("bm_sub,bn", [(2, 128), (1, 64), (1, 128)])
+def test_conv_fwd_tile_variants(cuda, bm_sub, bn):
+    from fp8_b200 import _lib, ops
+
+    xq, sx = _rand_q((8, 128, 32, 32), seed=41, device=cuda)
+    wq, sw = _rand_q((128, 128, 3, 3), seed=42, device=cuda, scale=0.05)
+    ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())
+    try:
+        _lib.set_tile_override(bm_sub, bn, 0)
+        y = ops.conv3x3_fwd(xq, wq, sx, sw)
+    finally:
+        _lib.set_tile_override(0, 0, 0)
+    assert oracle.max_rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("group", [1, 3])
+def test_conv_wgrad_group_variants(cuda, group):
+    from fp8_b200 import _lib, ops
+
+    xq, sx = _rand_q((4, 128, 32, 32), seed=51, device=cuda)
+    dyq, sdy = _rand_q((4, 128, 32, 32), seed=52, device=cuda, scale=1e-2)
+    ref = oracle.conv_dw(xq.cpu(), dyq.cpu(), sx.item(), sdy.item())
+    try:
+        _lib.set_tile_override(0, 0, group)
+        dw = ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+    finally:
+        _lib.set_tile_override(0, 0, 0)
+    assert oracle.max_rel_err(dw, ref) <= TOL
+
+
+def test_conv_config2_full_size(cuda):
+    """BASELINE config 2 at full size: B=128, 128->128, 32x32 (M=131072, N=128, K=1152)."""
+    from fp8_b200 import ops
+
+    xq, sx = _rand_q((128, 128, 32, 32), seed=0, device=cuda)
+    wq, sw = _rand_q((128, 128, 3, 3), seed=1, device=cuda, scale=0.05)
+    y = ops.conv3x3_fwd(xq, wq, sx, sw)
+    ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())
+    assert oracle.max_rel_err(y, ref) <= TOL
+    assert ops.device_error() == 0

@@ -1,0 +1,134 @@
+"""GPU parity: quantize kernels are bit-exact (bytes and scales) against the CPU oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import fp8_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _bytes(t: torch.Tensor) -> np.ndarray:
+    """float8 tensor -> bytes in memory order."""
+    t = t.detach()
+    flat = t.as_strided((t.numel(),), (1,)) if t.is_contiguous() or t.is_contiguous(
+        memory_format=torch.channels_last) else t.reshape(-1)
+    return flat.view(torch.uint8).cpu().numpy()
+
+
+def _check_current(x: torch.Tensor):
+    from fp8_b200 import ops
+
+    q, s = ops.quantize_current(x)
+    q_ref, s_ref = oracle.quantize_current(x.cpu())
+    assert q.dtype == torch.float8_e4m3fn and q.stride() == x.stride()
+    assert np.float32(s.item()).tobytes() == s_ref.tobytes(), (s.item(), s_ref)
+    got = _bytes(q)
+    if not np.array_equal(got, q_ref):
+        bad = np.nonzero(got != q_ref)[0]
+        raise AssertionError(f"{bad.size} byte mismatches, first at {bad[:5]}: {got[bad[:5]]} vs {q_ref[bad[:5]]}")
+
+
+def _gen(shape, seed, scale=1.0, device="cuda"):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).to(device)
+
+
+@pytest.mark.parametrize(
+    "shape,scale",
+    [
+        ((2, 3, 4, 5), 1.0),
+        ((1, 1, 1, 1), 3.0),
+        ((3, 5, 7, 11), 1.0),  # n % 8 != 0: scalar tail
+        ((1, 1, 1, 8192 + 13), 37.0),
+        ((128, 128, 32, 32), 1.0),  # config-2 activation, 16.7M elements
+        ((4, 256, 16, 16), 1e-3),  # small magnitudes: subnormal e4m3 outputs
+        ((2, 64, 8, 8), 5e4),  # large magnitudes
+    ],
+)
+def test_quantize_current_bit_exact(cuda, shape, scale):
+    _check_current(_gen(shape, seed=hash(shape) & 0xFFFF, scale=scale))
+
+
+def test_quantize_current_channels_last_keeps_layout(cuda):
+    x = _gen((8, 128, 16, 16), seed=3).contiguous(memory_format=torch.channels_last)
+    _check_current(x)
+
+
+def test_quantize_zero_tensor_scale_one(cuda):
+    from fp8_b200 import ops
+
+    q, s = ops.quantize_current(torch.zeros(2, 3, 4, 5, dtype=torch.bfloat16, device=cuda))
+    assert s.item() == 1.0 and not _bytes(q).any()
+
+
+def test_quantize_power_of_two_amax_and_ties(cuda):
+    # amax exactly 448 * 2**-3 -> scale 2**-3 exactly; values on e4m3 midpoints tie to even
+    vals = torch.from_numpy(np.arange(256, dtype=np.uint8)).view(torch.float8_e4m3fn).float()
+    fin = torch.unique(vals[torch.isfinite(vals)])
+    mids = (fin[1:] + fin[:-1]) / 2 / 8.0  # scaled by the scale 2**-3
+    x = torch.cat([mids, fin / 8.0, torch.tensor([56.0])]).to(torch.bfloat16)  # 448/8 = 56 sets amax
+    _check_current(x.reshape(1, 1, 1, -1).to(cuda))
+
+
+def test_quantize_unaligned_view_scalar_path(cuda):
+    base = _gen((1, 1, 1, 4099), seed=11)
+    x = base[..., 1:]  # 2-byte offset: not 16-byte aligned
+    assert x.data_ptr() % 16 != 0
+    _check_current(x.contiguous() if not x.is_contiguous() else x)
+
+
+@pytest.mark.parametrize("prev", [0.05, 1.0, 1e-4, 0.0])
+def test_quantize_delayed_bit_exact(cuda, prev):
+    from fp8_b200 import ops
+
+    x = _gen((16, 128, 8, 8), seed=5)
+    prev_t = torch.tensor(prev, dtype=torch.float32, device=cuda)
+    q, s_curr = ops.quantize_delayed(x, prev_t)
+    q_ref, s_ref = oracle.quantize_delayed(x.cpu(), prev)
+    assert np.float32(s_curr.item()).tobytes() == s_ref.tobytes()
+    assert np.array_equal(_bytes(q), q_ref)
+
+
+def test_quantize_delayed_ragged(cuda):
+    from fp8_b200 import ops
+
+    x = _gen((1, 3, 7, 13), seed=9, scale=20.0)
+    prev_t = torch.tensor(0.01, dtype=torch.float32, device=cuda)
+    q, s_curr = ops.quantize_delayed(x, prev_t)
+    q_ref, s_ref = oracle.quantize_delayed(x.cpu(), 0.01)
+    assert np.float32(s_curr.item()).tobytes() == s_ref.tobytes()
+    assert np.array_equal(_bytes(q), q_ref)
+
+
+@pytest.mark.parametrize("name", ["randn", "zeros", "pow2", "ragged", "tiny"])
+def test_quantize_matches_golden_scales(cuda, golden, name):
+    from fp8_b200 import ops
+
+    bits = golden[f"q_{name}_x"]
+    shape = tuple(int(v) for v in golden[f"q_{name}_shape"])
+    x = torch.from_numpy(bits.view(np.int16).reshape(shape)).view(torch.bfloat16).to(cuda)
+    _, s = ops.quantize_current(x)
+    assert np.float32(s.item()).tobytes() == golden[f"q_{name}_scale"].tobytes()
+    prev = torch.tensor(float(golden[f"q_{name}_delayed_prev"][0]), device=cuda)
+    _, s_curr = ops.quantize_delayed(x, prev)
+    assert np.float32(s_curr.item()).tobytes() == golden[f"q_{name}_delayed_scale"].tobytes()
+
+
+def test_transpose_2d_matches_reference_fixture(cuda, golden):
+    from fp8_b200 import ops
+
+    for tag in ("c128x8", "c256x4", "c128to256x16"):
+        b, cin, cout, h, w = (int(v) for v in golden[f"{tag}_dims"])
+        dyq = torch.from_numpy(golden[f"{tag}_dyq"].reshape(b * h * w, cout)).view(torch.float8_e4m3fn).to(cuda)
+        t = ops.transpose_2d(dyq)
+        assert np.array_equal(t.view(torch.uint8).cpu().numpy(), golden[f"{tag}_dyt"])
+
+
+def test_no_device_error_recorded(cuda):
+    from fp8_b200 import ops
+
+    assert ops.device_error() == 0
