@@ -6,6 +6,7 @@
 // launches on the caller's stream.  It allocates nothing.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -24,6 +25,10 @@ __device__ int g_fp8_device_error = 0;
 namespace {
 
 constexpr int kMaxDevices = 64;
+
+// Kernels launched through this library since load (graph replays not included).
+std::atomic<unsigned long long> g_launches{0};
+inline void count_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 thread_local int t_last_status = FP8_OK;
 thread_local char t_last_msg[512] = {0};
@@ -177,6 +182,7 @@ int launch_kgemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb, KGemmParams p
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   const int grid = p.num_tiles < sm_count ? p.num_tiles : sm_count;
   kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mb, p);
+  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
@@ -243,6 +249,7 @@ int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams 
   auto kern = wgrad_fp8_kernel<G>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   kern<<<p.num_tiles * p.splits, kGemmThreads, Cfg::kSmemBytes, stream>>>(mdy, mb, p);
+  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
@@ -288,6 +295,7 @@ int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const 
   if (blocks < 1) blocks = 1;
   wgrad_reduce_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(partials, splits, count, sa, sb,
                                                                     static_cast<__nv_bfloat16*>(out));
+  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
@@ -340,6 +348,12 @@ int fp8_device_error(int* code_out, fp8_stream_t stream) {
   return ok();
 }
 
+int fp8_kernel_launch_count(unsigned long long* out) {
+  FP8_REQUIRE(out != nullptr, FP8_ERR_INVALID_ARGUMENT, "out is NULL");
+  *out = g_launches.load(std::memory_order_relaxed);
+  return ok();
+}
+
 int fp8_sm_count(int* out) {
   FP8_REQUIRE(out != nullptr, FP8_ERR_INVALID_ARGUMENT, "out is NULL");
   DeviceState* st;
@@ -383,6 +397,7 @@ int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, voi
     quantize_cast_kernel<kCurrent, false>
         <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
   }
+  count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }
@@ -413,6 +428,7 @@ int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_sca
     quantize_cast_kernel<kDelayed, false>
         <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
   finalize_scale_kernel<<<1, kQuantThreads, 0, cs>>>(partials, parts, scale_curr_out);
+  count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }
@@ -426,6 +442,7 @@ int fp8_transpose_2d(const void* src, void* dst, int64_t rows, int64_t cols, fp8
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), 1);
   transpose_u8_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, cols, cols, rows, 0, 0);
+  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }
@@ -438,6 +455,7 @@ int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8
   dim3 grid((cout + kTransTile - 1) / kTransTile, (cin + kTransTile - 1) / kTransTile, 9);
   transpose_u8_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(wq), static_cast<uint8_t*>(wq_t), cout, cin, 9ll * cin, 9ll * cout, cin, cout);
+  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }

@@ -30,6 +30,7 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_last_error": (c_int, [c_char_p, c_size_t]),
     "fp8_device_error": (c_int, [POINTER(c_int), c_void_p]),
     "fp8_sm_count": (c_int, [POINTER(c_int)]),
+    "fp8_kernel_launch_count": (c_int, [POINTER(ctypes.c_ulonglong)]),
     "fp8_quantize_workspace_bytes": (c_size_t, [c_int64]),
     "fp8_quantize_current": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int64, c_void_p]),
     "fp8_quantize_delayed": (
@@ -120,6 +121,12 @@ def device_error(stream: int = 0) -> int:
 def sm_count() -> int:
     out = c_int(0)
     check(load().fp8_sm_count(ctypes.byref(out)), "fp8_sm_count")
+    return out.value
+
+
+def kernel_launch_count() -> int:
+    out = ctypes.c_ulonglong(0)
+    check(load().fp8_kernel_launch_count(ctypes.byref(out)), "fp8_kernel_launch_count")
     return out.value
 
 

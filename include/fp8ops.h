@@ -56,6 +56,10 @@ int fp8_device_error(int* code_out, fp8_stream_t stream);
 /* Number of streaming multiprocessors of the current device (launch sizing). */
 int fp8_sm_count(int* out);
 
+/* Number of kernels this library has launched in this process (host-side
+ * launches; replays of a captured CUDA graph are not counted). */
+int fp8_kernel_launch_count(unsigned long long* out);
+
 /* ------------------------------------------------------------------ quantize */
 
 /* Bytes of fp32 workspace the quantize calls need for n elements. */
