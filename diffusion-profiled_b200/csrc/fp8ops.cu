@@ -125,6 +125,28 @@ int make_map_2d(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, i
   return FP8_OK;
 }
 
+// 2-D matrix [rows][cols] of `elem_bytes`-wide elements with row stride `ld`
+// elements; box = box_cols x box_rows, 128B swizzle (box_cols * elem_bytes == 128).
+// Used for the epilogue TMA stores (bf16 outputs, fp32 split-K partials).
+int make_map_2d_store(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, int64_t rows,
+                      int64_t cols, int64_t ld, int box_cols, int box_rows) {
+  EncodeTiledFn enc;
+  if (int s = get_encode_fn(&enc)) return s;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * elem_bytes};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FP8_REQUIRE(r == CUDA_SUCCESS, FP8_ERR_CUDA, "cuTensorMapEncodeTiled(store %lldx%lld) failed: %d",
+              (long long)rows, (long long)cols, (int)r);
+  return FP8_OK;
+}
+
+int make_map_out_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols) {
+  return make_map_2d_store(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, cols, 64, 32);
+}
+
 // Conv geometry: 128-pixel tiles that cover whole image rows (or whole images).
 struct ConvTile {
   int rows;  // image rows per 128-pixel tile
@@ -175,13 +197,13 @@ int g_override_group = 0;
 
 // ------------------------------------------------------------------ K-major GEMM launch
 template <int BM_SUB, int BN, int STAGES>
-int launch_kgemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb, KGemmParams p, int sm_count,
-                     cudaStream_t stream) {
+int launch_kgemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, KGemmParams p,
+                     int sm_count, cudaStream_t stream) {
   using Cfg = KGemmConfig<BM_SUB, BN, STAGES>;
   auto kern = kgemm_fp8_kernel<BM_SUB, BN, STAGES>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   const int grid = p.num_tiles < sm_count ? p.num_tiles : sm_count;
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mb, p);
+  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
   count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
@@ -210,17 +232,17 @@ void choose_kgemm_tile(const KGemmShape& s, int sm_count, int* bm_sub, int* bn) 
   }
 }
 
-int launch_kgemm(const CUtensorMap& ma, const CUtensorMap& mb, KGemmParams p, int bm_sub, int bn, int sm_count,
-                 cudaStream_t stream) {
+int launch_kgemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, KGemmParams p, int bm_sub,
+                 int bn, int sm_count, cudaStream_t stream) {
   const int64_t m_tiles = (static_cast<int64_t>(p.M) + 128 * bm_sub - 1) / (128 * bm_sub);
   p.num_n_tiles = (p.N + bn - 1) / bn;
   const int64_t tiles = m_tiles * p.num_n_tiles;
   FP8_REQUIRE(tiles < (1ll << 31), FP8_ERR_UNSUPPORTED, "too many tiles");
   p.num_tiles = static_cast<int>(tiles);
-  if (bm_sub == 1 && bn == 64) return launch_kgemm_cfg<1, 64, 8>(ma, mb, p, sm_count, stream);
-  if (bm_sub == 1 && bn == 128) return launch_kgemm_cfg<1, 128, 6>(ma, mb, p, sm_count, stream);
-  if (bm_sub == 1 && bn == 256) return launch_kgemm_cfg<1, 256, 4>(ma, mb, p, sm_count, stream);
-  if (bm_sub == 2 && bn == 128) return launch_kgemm_cfg<2, 128, 4>(ma, mb, p, sm_count, stream);
+  if (bm_sub == 1 && bn == 64) return launch_kgemm_cfg<1, 64, 8>(ma, mb, mo, p, sm_count, stream);
+  if (bm_sub == 1 && bn == 128) return launch_kgemm_cfg<1, 128, 6>(ma, mb, mo, p, sm_count, stream);
+  if (bm_sub == 1 && bn == 256) return launch_kgemm_cfg<1, 256, 4>(ma, mb, mo, p, sm_count, stream);
+  if (bm_sub == 2 && bn == 128) return launch_kgemm_cfg<2, 128, 4>(ma, mb, mo, p, sm_count, stream);
   return set_error(FP8_ERR_UNSUPPORTED, "no K-major GEMM instance for bm_sub=%d bn=%d", bm_sub, bn);
 }
 
@@ -244,11 +266,12 @@ int check_conv_args(int batch, int height, int width, int cin, int cout, ConvTil
 
 // ------------------------------------------------------------------ weight-gradient launch
 template <int G>
-int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, cudaStream_t stream) {
+int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, const CUtensorMap& mp, WGradParams p,
+                     cudaStream_t stream) {
   using Cfg = WGradConfig<G>;
   auto kern = wgrad_fp8_kernel<G>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-  kern<<<p.num_tiles * p.splits, kGemmThreads, Cfg::kSmemBytes, stream>>>(mdy, mb, p);
+  kern<<<p.num_tiles * p.splits, kGemmThreads, Cfg::kSmemBytes, stream>>>(mdy, mb, mp, p);
   count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
@@ -281,9 +304,13 @@ WGradPlan plan_wgrad(int64_t m_rows, int64_t n_cols, int64_t pixels, int split_k
 }
 
 int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, int group, cudaStream_t stream) {
-  if (group == 1) return launch_wgrad_cfg<1>(mdy, mb, p, stream);
-  if (group == 2) return launch_wgrad_cfg<2>(mdy, mb, p, stream);
-  if (group == 3) return launch_wgrad_cfg<3>(mdy, mb, p, stream);
+  CUtensorMap mp;
+  if (int s = make_map_2d_store(&mp, p.partials, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                                static_cast<int64_t>(p.splits) * p.m_rows, p.n_cols, p.n_cols, 32, 32))
+    return s;
+  if (group == 1) return launch_wgrad_cfg<1>(mdy, mb, mp, p, stream);
+  if (group == 2) return launch_wgrad_cfg<2>(mdy, mb, mp, p, stream);
+  if (group == 3) return launch_wgrad_cfg<3>(mdy, mb, mp, p, stream);
   return set_error(FP8_ERR_UNSUPPORTED, "no weight-gradient instance for group=%d", group);
 }
 
@@ -301,21 +328,24 @@ int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const 
 }
 
 // ------------------------------------------------------------------ quantize launch helpers
-int quant_partials(int64_t n, int sm_count) {
-  const int64_t vec_threads = (n / 8 + 3) / 4;  // ~4 vectors per thread in the amax pass
-  int64_t blocks = (vec_threads + kQuantThreads - 1) / kQuantThreads;
-  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+constexpr int kAmaxVec = 8;          // 16-byte loads in flight per thread, amax pass
+constexpr int kCastVec = 2;          // 16-byte loads in flight per thread, cast pass
+constexpr int kMaxQuantBlocksPerSm = 8;
+int g_quant_amax_bps = 4;            // CTAs per SM (grid cap) of the amax pass
+int g_quant_cast_bps = 4;            // CTAs per SM (grid cap) of the cast pass
+
+int quant_grid(int64_t n, int vec, int blocks_per_sm, int sm_count) {
+  const int64_t per_block = static_cast<int64_t>(kQuantThreads) * vec * 8;  // elements per CTA iteration
+  int64_t blocks = (n + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count) * blocks_per_sm;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   return static_cast<int>(blocks);
 }
 
-int quant_cast_blocks(int64_t n, int sm_count) {
-  int64_t blocks = (n / 8 + 2 * kQuantThreads - 1) / (2 * kQuantThreads);
-  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
-  if (blocks > cap) blocks = cap;
-  if (blocks < 1) blocks = 1;
-  return static_cast<int>(blocks);
+// Partials never exceed kMaxQuantBlocksPerSm per SM, whatever the tuning.
+size_t quant_workspace_bytes(int sm_count) {
+  return static_cast<size_t>(sm_count) * kMaxQuantBlocksPerSm * sizeof(float);
 }
 
 }  // namespace
@@ -368,7 +398,8 @@ size_t fp8_quantize_workspace_bytes(int64_t n) {
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (sms <= 0) sms = 148;
   (void)cudaGetLastError();
-  return static_cast<size_t>(quant_partials(n, sms)) * sizeof(float);
+  (void)n;
+  return quant_workspace_bytes(sms);
 }
 
 int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, void* workspace,
@@ -380,21 +411,21 @@ int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, voi
   DeviceState* st;
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  const int parts = quant_partials(n, st->sm_count);
+  const int parts = quant_grid(n, kAmaxVec, g_quant_amax_bps, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= parts * sizeof(float) && aligned(workspace, 4),
               FP8_ERR_WORKSPACE, "quantize workspace too small: need %zu bytes", parts * sizeof(float));
   float* partials = static_cast<float*>(workspace);
   const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
   const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
   uint8_t* q = static_cast<uint8_t*>(q_e4m3);
-  const int cast_blocks = quant_cast_blocks(n, st->sm_count);
+  const int cast_blocks = quant_grid(n, kCastVec, g_quant_cast_bps, st->sm_count);
   if (vec) {
-    amax_partials_kernel<true><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
-    quantize_cast_kernel<kCurrent, true>
+    amax_partials_kernel<true, kAmaxVec><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
+    quantize_cast_kernel<kCurrent, true, kCastVec>
         <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
   } else {
-    amax_partials_kernel<false><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
-    quantize_cast_kernel<kCurrent, false>
+    amax_partials_kernel<false, 1><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
+    quantize_cast_kernel<kCurrent, false, 1>
         <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
   }
   count_launches(2);
@@ -414,7 +445,7 @@ int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_sca
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   // The cast pass writes one partial per CTA, so its grid is the partial count.
-  const int parts = quant_partials(n, st->sm_count);
+  const int parts = quant_grid(n, kCastVec, g_quant_cast_bps, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= parts * sizeof(float) && aligned(workspace, 4),
               FP8_ERR_WORKSPACE, "quantize workspace too small: need %zu bytes", parts * sizeof(float));
   float* partials = static_cast<float*>(workspace);
@@ -422,10 +453,10 @@ int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_sca
   const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
   uint8_t* q = static_cast<uint8_t*>(q_e4m3);
   if (vec)
-    quantize_cast_kernel<kDelayed, true>
+    quantize_cast_kernel<kDelayed, true, kCastVec>
         <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
   else
-    quantize_cast_kernel<kDelayed, false>
+    quantize_cast_kernel<kDelayed, false, 1>
         <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
   finalize_scale_kernel<<<1, kQuantThreads, 0, cs>>>(partials, parts, scale_curr_out);
   count_launches(2);
@@ -481,11 +512,12 @@ int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, co
   int bm_sub, bn;
   choose_kgemm_tile({M, cout, k_blocks}, st->sm_count, &bm_sub, &bn);
   if (int s = make_map_2d(&mb, wq, cout, 9ll * cin, bn)) return s;
+  CUtensorMap mo;
+  if (int s = make_map_out_bf16(&mo, y, M, cout)) return s;
   KGemmParams p{};
   p.k_blocks = k_blocks;
   p.M = static_cast<int>(M);
   p.N = cout;
-  p.ldo = cout;
   p.a_conv = 1;
   p.HW = height * width;
   p.W = width;
@@ -495,9 +527,9 @@ int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, co
   p.scale_b = sw;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.epilogue = epilogue;
-  p.out = static_cast<__nv_bfloat16*>(y);
   p.err = st->err_ptr;
-  if (int s = launch_kgemm(ma, mb, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream))) return s;
+  if (int s = launch_kgemm(ma, mb, mo, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+    return s;
   return ok();
 }
 
@@ -518,11 +550,12 @@ int fp8_conv3x3_dgrad(const void* dyq, const void* wq_t, void* dx, const float* 
   int bm_sub, bn;
   choose_kgemm_tile({M, cin, k_blocks}, st->sm_count, &bm_sub, &bn);
   if (int s = make_map_2d(&mb, wq_t, cin, 9ll * cout, bn)) return s;
+  CUtensorMap mo;
+  if (int s = make_map_out_bf16(&mo, dx, M, cin)) return s;
   KGemmParams p{};
   p.k_blocks = k_blocks;
   p.M = static_cast<int>(M);
   p.N = cin;
-  p.ldo = cin;
   p.a_conv = 1;
   p.HW = height * width;
   p.W = width;
@@ -532,9 +565,9 @@ int fp8_conv3x3_dgrad(const void* dyq, const void* wq_t, void* dx, const float* 
   p.scale_b = sw;
   p.bias = nullptr;
   p.epilogue = kEpiNone;
-  p.out = static_cast<__nv_bfloat16*>(dx);
   p.err = st->err_ptr;
-  if (int s = launch_kgemm(ma, mb, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream))) return s;
+  if (int s = launch_kgemm(ma, mb, mo, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+    return s;
   return ok();
 }
 
@@ -612,19 +645,20 @@ int fp8_gemm(const void* a, const void* b, void* out, const float* sa, const flo
   CUtensorMap ma, mb;
   if (int s = make_map_2d(&ma, a, m, k, 128)) return s;
   if (int s = make_map_2d(&mb, b, n, k, bn)) return s;
+  CUtensorMap mo;
+  if (int s = make_map_out_bf16(&mo, out, m, n)) return s;
   KGemmParams p{};
   p.k_blocks = k_blocks;
   p.M = static_cast<int>(m);
   p.N = static_cast<int>(n);
-  p.ldo = static_cast<int>(n);
   p.a_conv = 0;
   p.scale_a = sa;
   p.scale_b = sb;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.epilogue = epilogue;
-  p.out = static_cast<__nv_bfloat16*>(out);
   p.err = st->err_ptr;
-  if (int s = launch_kgemm(ma, mb, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream))) return s;
+  if (int s = launch_kgemm(ma, mb, mo, p, bm_sub, bn, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+    return s;
   return ok();
 }
 
@@ -671,6 +705,15 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   if (int s = launch_wgrad(mdy, mx, p, w.group, cs)) return s;
   if (int s = launch_wgrad_reduce(p.partials, w.splits, n * k, sdy, sx, dw, st->sm_count, cs)) return s;
+  return ok();
+}
+
+int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
+  FP8_REQUIRE(amax_blocks_per_sm >= 0 && amax_blocks_per_sm <= kMaxQuantBlocksPerSm && cast_blocks_per_sm >= 0 &&
+                  cast_blocks_per_sm <= kMaxQuantBlocksPerSm,
+              FP8_ERR_INVALID_ARGUMENT, "blocks per SM must be in 0..%d", kMaxQuantBlocksPerSm);
+  g_quant_amax_bps = amax_blocks_per_sm > 0 ? amax_blocks_per_sm : 4;
+  g_quant_cast_bps = cast_blocks_per_sm > 0 ? cast_blocks_per_sm : 4;
   return ok();
 }
 

@@ -14,9 +14,13 @@
 //   warp 0      TMA producer (one lane) — fills a STAGES-deep smem ring
 //   warp 1      TMEM allocator + MMA issuer (one lane) — tcgen05.mma kind::f8f6f4,
 //               M=128 per sub-tile, N=BN, K=32 per instruction (4 per 128-byte K block)
-//   warps 2..5  epilogue — tcgen05.ld the fp32 accumulator, scale, optional
-//               bias + SiLU, round to bf16 and store; two accumulator buffers in
-//               TMEM let the epilogue of tile i overlap the MMAs of tile i+1.
+//   warps 2..5  epilogue — each owns one 32-lane quarter of TMEM: tcgen05.ld the
+//               fp32 accumulator 64 columns at a time, scale (+ bias, + SiLU),
+//               round to bf16, write a 32x64 tile into a 128B-swizzled staging
+//               buffer and TMA-store it (coalesced; rows past M and columns past
+//               N are clipped by TMA).  Two accumulator buffers in TMEM let the
+//               epilogue of tile i overlap the MMAs of tile i+1; the accumulator
+//               is released as soon as its last TMEM load has landed.
 #pragma once
 
 #include "sm100_common.cuh"
@@ -27,6 +31,9 @@ constexpr int kGemmThreads = 192;
 constexpr int kKBlockBytes = 128;          // one 128-byte swizzle row of K per stage
 constexpr int kSubTileRows = 128;          // UMMA M
 constexpr int kATileBytes = kSubTileRows * kKBlockBytes;  // 16 KB
+constexpr int kEpiWarps = 4;
+constexpr int kEpiBufBytes = 32 * 128;     // 32 rows x 128 bytes (64 bf16 or 32 fp32 columns)
+constexpr int kEpiSmemBytes = kEpiWarps * 2 * kEpiBufBytes;  // double buffered per warp
 
 enum Epilogue : int { kEpiNone = 0, kEpiBias = 1, kEpiBiasSilu = 2 };
 
@@ -34,8 +41,7 @@ struct KGemmParams {
   int num_n_tiles;
   int num_tiles;
   int k_blocks;      // K / 128 (rounded up; TMA zero-fills the ragged end)
-  int M, N;          // logical output extent (rows beyond M / cols beyond N are not stored)
-  int ldo;           // output row stride in elements
+  int M, N;          // logical output extent
   // A operand source: 1 = 3x3 conv window over NHWC activations, 0 = plain [M][K]
   int a_conv;
   int HW, W;         // conv geometry (pixels per image, image width)
@@ -45,7 +51,6 @@ struct KGemmParams {
   const float* scale_b;
   const __nv_bfloat16* bias;  // [N], used by kEpiBias / kEpiBiasSilu
   int epilogue;
-  __nv_bfloat16* out;
   int* err;
 };
 
@@ -58,19 +63,42 @@ struct KGemmConfig {
   static constexpr int kAccCols = BM_SUB * BN;            // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : 2 * kAccCols;  // power of two here
   static constexpr int kBarBytes = 1024;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + kBarBytes + 1024;  // +1024 alignment slack
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiSmemBytes + kBarBytes + 1024;  // +1024 alignment
   static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
   static_assert(kSmemBytes <= 232448, "smem");
 };
 
+// 8 consecutive output columns of one row: scale, optional bias / SiLU, bf16x8.
+__device__ __forceinline__ uint4 epilogue8(const uint32_t* acc, float scale, int epi, const __nv_bfloat16* bias8) {
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(acc[i]) * scale;
+  if (epi != kEpiNone) {
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(bias8));
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] += bf16_lo_f(bw[j]);
+      v[2 * j + 1] += bf16_hi_f(bw[j]);
+    }
+    if (epi == kEpiBiasSilu) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = silu_f32(v[i]);
+    }
+  }
+  return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                    pack_bf16x2(v[6], v[7]));
+}
+
 template <int BM_SUB, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     kgemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     const KGemmParams p) {
+                     const __grid_constant__ CUtensorMap tmap_out, const KGemmParams p) {
   using Cfg = KGemmConfig<BM_SUB, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bar_area = smem + STAGES * Cfg::kStageBytes;
+  uint8_t* epi_smem = smem + STAGES * Cfg::kStageBytes;
+  uint8_t* bar_area = epi_smem + kEpiSmemBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
@@ -89,7 +117,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4 * 32);
+      mbar_init(&tempty_bar[a], kEpiWarps * 32);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -98,6 +126,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -212,9 +241,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;
+    uint8_t* stage_buf = epi_smem + (warp - 2) * 2 * kEpiBufBytes;
     const float scale = __ldg(p.scale_a) * __ldg(p.scale_b);
     int local = 0;
+    int buf = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int mt = tile / p.num_n_tiles;
       const int nt = tile - mt * p.num_n_tiles;
@@ -224,47 +254,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
 #pragma unroll 1
       for (int sub = 0; sub < BM_SUB; ++sub) {
-        const int m = (mt * BM_SUB + sub) * kSubTileRows + row;
+        const int m0 = (mt * BM_SUB + sub) * kSubTileRows + quarter * 32;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols + sub * BN + c, r);
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t r[64];
+          const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols + sub * BN + c;
+          tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
           tmem_ld_wait();
-          const int n0 = nt * BN + c;
-          if (m < p.M && n0 < p.N) {
-            uint32_t packed[16];
-            if (p.epilogue == kEpiNone) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                packed[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * scale, __uint_as_float(r[2 * i + 1]) * scale);
-            } else {
-              const uint4* bv = reinterpret_cast<const uint4*>(p.bias + n0);
-#pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                const uint4 b8 = __ldg(bv + v);
-                const uint32_t bw[4] = {b8.x, b8.y, b8.z, b8.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  float lo = __uint_as_float(r[8 * v + 2 * j]) * scale + bf16_lo_f(bw[j]);
-                  float hi = __uint_as_float(r[8 * v + 2 * j + 1]) * scale + bf16_hi_f(bw[j]);
-                  if (p.epilogue == kEpiBiasSilu) {
-                    lo = silu_f32(lo);
-                    hi = silu_f32(hi);
-                  }
-                  packed[4 * v + j] = pack_bf16x2(lo, hi);
-                }
-              }
-            }
-            uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m) * p.ldo + n0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          if (sub == BM_SUB - 1 && c + 64 >= BN) {
+            // last read of this accumulator: hand it back to the MMA warp
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[acc]);
           }
+          const int n0 = nt * BN + c;
+          if (n0 >= p.N) continue;
+          uint8_t* sbuf = stage_buf + buf * kEpiBufBytes;
+          if (lane == 0) bulk_wait_group_read<1>();  // this buffer's previous store has read smem
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue, p.bias + n0 + 8 * j);
+            st_shared_v4(sbuf + swizzle128_offset(lane, j), o.x, o.y, o.z, o.w);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, sbuf, n0, m0);
+            bulk_commit_group();
+          }
+          buf ^= 1;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
     }
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();

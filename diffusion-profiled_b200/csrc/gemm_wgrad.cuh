@@ -45,19 +45,20 @@ struct WGradConfig {
   static constexpr int kStages = (G == 1) ? 6 : (G == 2 ? 4 : 3);
   static constexpr int kAccCols = G * 128;
   static constexpr int kTmemCols = (kAccCols <= 128) ? 128 : (kAccCols <= 256 ? 256 : 512);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiSmemBytes + 1024 + 1024;
   static_assert(kSmemBytes <= 232448, "smem");
 };
 
 template <int G>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     wgrad_fp8_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_b,
-                     const WGradParams p) {
+                     const __grid_constant__ CUtensorMap tmap_part, const WGradParams p) {
   using Cfg = WGradConfig<G>;
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bar_area = smem + STAGES * Cfg::kStageBytes;
+  uint8_t* epi_smem = smem + STAGES * Cfg::kStageBytes;
+  uint8_t* bar_area = epi_smem + kEpiSmemBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
@@ -88,6 +89,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_dy);
     tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_part);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -185,32 +187,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait(drain_bar, 0, &never, p.err, kErrTimeoutDrain);
     }
   } else {
+    // Epilogue: fp32 partial rows of this split, 32 columns (128 B) at a time,
+    // staged 128B-swizzled in shared memory and written with TMA stores.
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int co = co_tile * 128 + row;
+    uint8_t* stage_buf = epi_smem + (warp - 2) * 2 * kEpiBufBytes;
+    const int row0 = split * p.m_rows + co_tile * 128 + quarter * 32;  // partial row of lane 0
     const bool has_work = kb_end > kb_begin;
     bool ok = true;
     if (has_work) ok = mbar_wait(tfull_bar, 0, abort_flag, p.err, kErrTimeoutEpilogue);
     if (ok) {
       tc_fence_after();
-      float* dst_row = p.partials + (static_cast<int64_t>(split) * p.m_rows + co) * p.n_cols;
+      int buf = 0;
 #pragma unroll 1
       for (int c = 0; c < G * 128; c += 32) {
-        const int j0 = group * G * 128 + c;
-        float4* dst = reinterpret_cast<float4*>(dst_row + j0);
+        uint32_t r[32];
         if (has_work) {
-          uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + c, r);
           tmem_ld_wait();
-#pragma unroll
-          for (int v = 0; v < 8; ++v)
-            dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
         } else {
 #pragma unroll
-          for (int v = 0; v < 8; ++v) dst[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
         }
+        uint8_t* sbuf = stage_buf + buf * kEpiBufBytes;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(sbuf + swizzle128_offset(lane, j), r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_part, sbuf, group * G * 128 + c, row0);
+          bulk_commit_group();
+        }
+        buf ^= 1;
       }
+      if (lane == 0) bulk_wait_group<0>();
     }
   }
 

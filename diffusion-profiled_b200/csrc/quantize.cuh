@@ -76,8 +76,18 @@ __device__ __forceinline__ float fold_partials_to_scale(const float* __restrict_
   return scale_from_amax(block_max(m));
 }
 
-// Pass 1 of current scaling: |x| max per CTA.  VEC: x is 16-byte aligned.
-template <bool VEC>
+__device__ __forceinline__ float absmax_pair(uint32_t w) { return fmaxf(fabsf(bf16_lo_f(w)), fabsf(bf16_hi_f(w))); }
+
+// max |.| of the 8 bf16 of a 16-byte vector folded into m (a depth-3 tree, so
+// consecutive vectors do not serialise on one accumulator).
+__device__ __forceinline__ float absmax_vec(float m, const uint4& a) {
+  return fmaxf(m, fmaxf(fmaxf(absmax_pair(a.x), absmax_pair(a.y)), fmaxf(absmax_pair(a.z), absmax_pair(a.w))));
+}
+
+// Pass 1 of current scaling: |x| max per CTA.  Each thread keeps V 16-byte
+// loads in flight per iteration (coalesced: vector i + v*T).  VEC: x is
+// 16-byte aligned.
+template <bool VEC, int V>
 __global__ void __launch_bounds__(kQuantThreads) amax_partials_kernel(const uint16_t* __restrict__ x, int64_t n,
                                                                       float* __restrict__ partials) {
   float m = 0.0f;
@@ -88,18 +98,21 @@ __global__ void __launch_bounds__(kQuantThreads) amax_partials_kernel(const uint
     const int64_t nvec = n >> 3;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
     int64_t i = tid;
-    for (; i + 3 * nthreads < nvec; i += 4 * nthreads) {
-      uint4 a = __ldg(xv + i), b = __ldg(xv + i + nthreads), c = __ldg(xv + i + 2 * nthreads),
-            d = __ldg(xv + i + 3 * nthreads);
-      m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
-      m = absmax_word(m, b.x); m = absmax_word(m, b.y); m = absmax_word(m, b.z); m = absmax_word(m, b.w);
-      m = absmax_word(m, c.x); m = absmax_word(m, c.y); m = absmax_word(m, c.z); m = absmax_word(m, c.w);
-      m = absmax_word(m, d.x); m = absmax_word(m, d.y); m = absmax_word(m, d.z); m = absmax_word(m, d.w);
+    for (; i + (V - 1) * nthreads < nvec; i += V * nthreads) {
+      uint4 a[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) a[v] = __ldg(xv + i + v * nthreads);
+      float mv[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) mv[v] = absmax_vec(0.0f, a[v]);
+#pragma unroll
+      for (int w = 1; w < V; w *= 2) {
+#pragma unroll
+        for (int v = 0; v + w < V; v += 2 * w) mv[v] = fmaxf(mv[v], mv[v + w]);
+      }
+      m = fmaxf(m, mv[0]);
     }
-    for (; i < nvec; i += nthreads) {
-      uint4 a = __ldg(xv + i);
-      m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
-    }
+    for (; i < nvec; i += nthreads) m = absmax_vec(m, __ldg(xv + i));
     done = nvec << 3;
   }
   for (int64_t i = done + tid; i < n; i += nthreads) m = fmaxf(m, fabsf(__uint_as_float(uint32_t(x[i]) << 16)));
@@ -113,11 +126,18 @@ __device__ __forceinline__ uint32_t cast4(uint32_t w0, uint32_t w1, float s) {
   return lo | (hi << 16);
 }
 
+__device__ __forceinline__ uint2 cast_vec(const uint4& a, float s) {
+  return make_uint2(cast4(a.x, a.y, s), cast4(a.z, a.w, s));
+}
+
 // Cast pass.  kCurrent: scale = fold(partials_in); CTA 0 stores it to scale_out.
 //             kDelayed: scale = *prev_scale; each CTA also writes its |x| max
 //                       to partials_out[blockIdx.x].
+// V 16-byte loads in flight per thread and iteration.  In current mode x was
+// just read by the amax pass, so the loads here are its last use (streaming
+// hint); the e4m3 output is stored normally (its consumer follows).
 // VEC: x 16-byte aligned and q 8-byte aligned.
-template <int MODE, bool VEC>
+template <int MODE, bool VEC, int V>
 __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
     int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
@@ -138,21 +158,21 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
     const uint4* xv = reinterpret_cast<const uint4*>(x);
     uint2* qv = reinterpret_cast<uint2*>(q);
     int64_t i = tid;
-    for (; i + nthreads < nvec; i += 2 * nthreads) {
-      const uint4 a = __ldg(xv + i), b = __ldg(xv + i + nthreads);
+    for (; i + (V - 1) * nthreads < nvec; i += V * nthreads) {
+      uint4 a[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) a[v] = MODE == kCurrent ? __ldcs(xv + i + v * nthreads) : __ldg(xv + i + v * nthreads);
       if (MODE == kDelayed) {
-        m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
-        m = absmax_word(m, b.x); m = absmax_word(m, b.y); m = absmax_word(m, b.z); m = absmax_word(m, b.w);
+#pragma unroll
+        for (int v = 0; v < V; ++v) m = absmax_vec(m, a[v]);
       }
-      qv[i] = make_uint2(cast4(a.x, a.y, s), cast4(a.z, a.w, s));
-      qv[i + nthreads] = make_uint2(cast4(b.x, b.y, s), cast4(b.z, b.w, s));
+#pragma unroll
+      for (int v = 0; v < V; ++v) qv[i + v * nthreads] = cast_vec(a[v], s);
     }
     for (; i < nvec; i += nthreads) {
       const uint4 a = __ldg(xv + i);
-      if (MODE == kDelayed) {
-        m = absmax_word(m, a.x); m = absmax_word(m, a.y); m = absmax_word(m, a.z); m = absmax_word(m, a.w);
-      }
-      qv[i] = make_uint2(cast4(a.x, a.y, s), cast4(a.z, a.w, s));
+      if (MODE == kDelayed) m = absmax_vec(m, a);
+      qv[i] = cast_vec(a, s);
     }
     done = nvec << 3;
   }

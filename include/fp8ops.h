@@ -150,6 +150,10 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
  * choice.  Process-wide; meant for benchmarks and tests. */
 int fp8_set_tile_override(int bm_sub, int bn, int wgrad_group);
 
+/* Tuning override for the quantize grids: CTAs per SM of the amax pass and of
+ * the cast pass (1..8; 0 restores the built-in choice).  Process-wide. */
+int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);
+
 #ifdef __cplusplus
 }
 #endif
