@@ -433,6 +433,79 @@ int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, voi
   return ok();
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free quantize
+// Scratch of fp8_quantize_current_noalloc: the per-CTA |x| maxima of the amax
+// pass.  It is a fixed array in this library's own device memory, so callers
+// that cannot allocate device memory (see include/fp8ops.h) still get the
+// current-scaling quantize.  Every device that loads the library holds one copy
+// (8 KB) until the process exits.
+constexpr int kNoAllocPartials = 2048;
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
+
+namespace {
+float* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_partials for the current device.  The host-side
+// name of the array is only a stand-in; the address must come from the
+// runtime, once per device, with that device current.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  FP8_CUDA_TRY(cudaGetDevice(&dev));
+  FP8_REQUIRE(dev >= 0 && dev < kMaxDevices, FP8_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      FP8_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_partials));
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+  }
+  *out = g_noalloc_ptr[dev];
+  return FP8_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int fp8_quantize_current_noalloc(const void* x_bf16, void* q_e4m3, float* scale_out, int64_t n,
+                                 fp8_stream_t stream) {
+  FP8_REQUIRE(n >= 0, FP8_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  FP8_REQUIRE(scale_out != nullptr && aligned(scale_out, 4), FP8_ERR_INVALID_ARGUMENT, "bad scale_out");
+  FP8_REQUIRE(n == 0 || (x_bf16 != nullptr && q_e4m3 != nullptr), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(x_bf16, 2), FP8_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  float* partials = nullptr;
+  if (int s = noalloc_scratch(&partials)) return s;
+  const int parts = quant_grid(n, kAmaxVec, g_quant_amax_bps, st->sm_count);
+  FP8_REQUIRE(parts <= kNoAllocPartials, FP8_ERR_UNSUPPORTED,
+              "allocation-free quantize needs %d partial slots but its static scratch holds %d "
+              "(device has too many SMs for it); use fp8_quantize_current with a workspace",
+              parts, kNoAllocPartials);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
+  const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
+  uint8_t* q = static_cast<uint8_t*>(q_e4m3);
+  const int cast_blocks = quant_grid(n, kCastVec, g_quant_cast_bps, st->sm_count);
+  // Every CTA of the amax pass overwrites its own slot before the cast pass
+  // reads slots [0, parts), so nothing has to be cleared between calls.
+  if (vec) {
+    amax_partials_kernel<true, kAmaxVec><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
+    quantize_cast_kernel<kCurrent, true, kCastVec>
+        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
+  } else {
+    amax_partials_kernel<false, 1><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
+    quantize_cast_kernel<kCurrent, false, 1>
+        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
+  }
+  count_launches(2);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
 int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_scale, float* scale_curr_out,
                          void* workspace, size_t workspace_bytes, int64_t n, fp8_stream_t stream) {
   FP8_REQUIRE(n >= 0, FP8_ERR_INVALID_ARGUMENT, "n must be >= 0");

@@ -33,6 +33,7 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_kernel_launch_count": (c_int, [POINTER(ctypes.c_ulonglong)]),
     "fp8_quantize_workspace_bytes": (c_size_t, [c_int64]),
     "fp8_quantize_current": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int64, c_void_p]),
+    "fp8_quantize_current_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "fp8_quantize_delayed": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int64, c_void_p],

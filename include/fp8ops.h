@@ -74,6 +74,22 @@ size_t fp8_quantize_workspace_bytes(int64_t n);
 int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, void* workspace,
                          size_t workspace_bytes, int64_t n, fp8_stream_t stream);
 
+/* Allocation-free variant of fp8_quantize_current (same results, bit for bit).
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory, e.g. code that runs while a CUDA graph is being captured (where
+ * cudaMalloc is not allowed), runtimes whose device memory is entirely owned by
+ * another allocator, or a foreign-language host with no device allocator of its
+ * own.  It takes no workspace: its scratch (the per-CTA amax partials) is a
+ * static 8 KB array inside this library, one per device, held until the process
+ * exits.  Limit: that array has 2048 slots; a call whose amax pass would need
+ * more (a device with more than 256 SMs) is rejected with FP8_ERR_UNSUPPORTED.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  All calls share the one array: calls
+ * that overlap on the GPU (different streams, no ordering between them) race
+ * and may produce wrong scales; serialise them. */
+int fp8_quantize_current_noalloc(const void* x_bf16, void* q_e4m3, float* scale_out, int64_t n,
+                                 fp8_stream_t stream);
+
 /* Delayed scaling: q = e4m3(clamp(x / *prev_scale, +-448)) and
  * *scale_curr_out = scale of x's own amax.
  * Replaces quantize_fp8_delayed (fp8_kernels.py:518-556) and
