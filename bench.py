@@ -142,7 +142,8 @@ def measured_peaks() -> dict:
 
 
 def ncu_traffic() -> dict:
-    path = ROOT / "profiles" / "ncu_traffic.json"
+    # JSON text: op name -> DRAM bytes (read + write) per launch from one ncu capture
+    path = ROOT / "profiles" / "ncu_traffic_per_launch.txt"
     return json.loads(path.read_text()) if path.exists() else {}
 
 
@@ -363,7 +364,7 @@ def time_kernels(args, dev, w, sets) -> dict:
         xq, sx = ops.quantize_current(x)
         wq, sw = ops.quantize_current(w)
         dyq, sdy = ops.quantize_current(dy)
-        wt = torch.empty((cin, 9 * cout), device=dev, dtype=torch.float8_e4m3fn)
+        wt = torch.empty((cin, 9 * cout), device=dev, dtype=torch.float8_e4m3fn)  # dgrad's K-major weights
         _lib.call("fp8_conv_weight_transpose", p(wq), p(wt), cout, cin, stream())
         y = torch.empty((b, cout, h, wd), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
         dx = torch.empty((b, cin, h, wd), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
@@ -386,7 +387,7 @@ def time_kernels(args, dev, w, sets) -> dict:
             stream()), "fwd"),
         "conv3x3_dgrad (kgemm_fp8_kernel)": lambda o: _lib.check(lib.fp8_conv3x3_dgrad(
             p(o["dyq"]), p(o["wt"]), p(o["dx"]), p(o["sdy"]), p(o["sw"]), b, h, wd, cin, cout, stream()), "dgrad"),
-        "conv3x3_wgrad (wgrad_fp8_kernel + reduce, 2 launches)": lambda o: _lib.check(lib.fp8_conv3x3_wgrad(
+        "conv3x3_wgrad (memset + wgrad_fp8_kernel + convert)": lambda o: _lib.check(lib.fp8_conv3x3_wgrad(
             p(o["xq"]), p(o["dyq"]), p(o["dw"]), p(o["sx"]), p(o["sdy"]), b, h, wd, cin, cout, 0, p(o["ws"]),
             o["ws"].numel() * 4, stream()), "wgrad"),
     }
@@ -423,7 +424,7 @@ def roofline(kernels: dict, peaks: dict, batch: int) -> dict | None:
         "quantize_current (amax + cast, 2 launches)": ("hbm", pix * cin * 3.0),  # read bf16 once + write e4m3
         "conv3x3_fwd (kgemm_fp8_kernel)": ("tensor", flops),
         "conv3x3_dgrad (kgemm_fp8_kernel)": ("tensor", flops),
-        "conv3x3_wgrad (wgrad_fp8_kernel + reduce, 2 launches)": ("tensor", flops),
+        "conv3x3_wgrad (memset + wgrad_fp8_kernel + convert)": ("tensor", flops),
     }
     name = max(kernels, key=lambda k: kernels[k]["ms"])
     bound, work = algo[name]
@@ -449,32 +450,35 @@ def time_e2e(args, dev, world, conv_api, step_flops) -> dict:
     b = args.batch
     cin, cout, h, w = SHAPE["cin"], SHAPE["cout"], SHAPE["h"], SHAPE["w"]
 
-    def pinned_nchw_cl(c):
-        return torch.empty((b, h, w, c), dtype=torch.bfloat16, pin_memory=True).permute(0, 3, 1, 2)
+    # Host buffers are contiguous NHWC ([Cout][3][3][Cin] for weights), i.e. the
+    # channels_last memory order, so every transfer is one contiguous DMA; the
+    # logical NCHW views the API takes are permutations of them.
+    def pinned(*shape):
+        return torch.empty(shape, dtype=torch.bfloat16, pin_memory=True)
 
-    x_h = pinned_nchw_cl(cin)
-    dy_h = pinned_nchw_cl(cout)
+    nhwc = (0, 2, 3, 1)
+    nchw = (0, 3, 1, 2)
+    x_h, dy_h = pinned(b, h, w, cin), pinned(b, h, w, cout)
     x0, dy0 = make_inputs(b, "cpu", seed=4242)
-    x_h.copy_(x0)
-    dy_h.copy_(dy0)
-    w_h = torch.empty((cout, 3, 3, cin), dtype=torch.bfloat16, pin_memory=True).permute(0, 3, 1, 2)
-    w_h.copy_(make_weight("cpu"))
-    y_h = pinned_nchw_cl(cout)
-    dx_h = pinned_nchw_cl(cin)
-    dw_h = torch.empty((cout, 3, 3, cin), dtype=torch.bfloat16, pin_memory=True).permute(0, 3, 1, 2)
+    x_h.copy_(x0.permute(*nhwc))
+    dy_h.copy_(dy0.permute(*nhwc))
+    w_h = pinned(cout, 3, 3, cin)
+    w_h.copy_(make_weight("cpu").permute(*nhwc))
+    y_h, dx_h, dw_h = pinned(b, h, w, cout), pinned(b, h, w, cin), pinned(cout, 3, 3, cin)
     h2d = x_h.numel() * 2 + w_h.numel() * 2 + (dy_h.numel() * 2 if args.workload == "layer" else 0)
     d2h = y_h.numel() * 2 + ((dx_h.numel() + dw_h.numel()) * 2 if args.workload == "layer" else 0)
+    train = args.workload == "layer"
 
     def one():
-        x = x_h.to(dev, non_blocking=True).requires_grad_(args.workload == "layer")
-        wt = w_h.to(dev, non_blocking=True).requires_grad_(args.workload == "layer")
+        x = x_h.to(dev, non_blocking=True).permute(*nchw).requires_grad_(train)
+        wt = w_h.to(dev, non_blocking=True).permute(*nchw).requires_grad_(train)
         y = conv_api(x, wt)
-        y_h.copy_(y, non_blocking=True)
-        if args.workload == "layer":
-            dy = dy_h.to(dev, non_blocking=True)
+        y_h.copy_(y.permute(*nhwc), non_blocking=True)
+        if train:
+            dy = dy_h.to(dev, non_blocking=True).permute(*nchw)
             gx, gw = torch.autograd.grad(y, (x, wt), dy)
-            dx_h.copy_(gx, non_blocking=True)
-            dw_h.copy_(gw, non_blocking=True)
+            dx_h.copy_(gx.permute(*nhwc), non_blocking=True)
+            dw_h.copy_(gw.permute(*nhwc), non_blocking=True)
 
     for _ in range(3):
         one()

@@ -190,6 +190,27 @@ int make_map_conv(CUtensorMap* map, const void* ptr, int batch, int height, int 
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Batched byte transpose dst[b][c][r] = src[b][r][c]; whole 16-byte-aligned
+// 64x64 tiles take the vectorised kernel.
+int launch_transpose(const void* src, void* dst, int64_t rows, int64_t cols, int64_t src_ld, int64_t dst_ld,
+                     int64_t src_bstride, int64_t dst_bstride, int batch, cudaStream_t stream) {
+  const int64_t gx = (rows + kTransTile - 1) / kTransTile, gy = (cols + kTransTile - 1) / kTransTile;
+  FP8_REQUIRE(gx < (1ll << 31) && gy <= 65535 && batch <= 65535, FP8_ERR_UNSUPPORTED, "transpose too large");
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(batch));
+  const bool tiles16 = rows % kTransTile == 0 && cols % kTransTile == 0 && src_ld % 16 == 0 && dst_ld % 16 == 0 &&
+                       src_bstride % 16 == 0 && dst_bstride % 16 == 0 && aligned(src, 16) && aligned(dst, 16);
+  if (tiles16)
+    transpose_u8_tiles16_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(src),
+                                                           static_cast<uint8_t*>(dst), src_ld, dst_ld, src_bstride,
+                                                           dst_bstride);
+  else
+    transpose_u8_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst),
+                                                  rows, cols, src_ld, dst_ld, src_bstride, dst_bstride);
+  count_launches(1);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
+}
+
 // ------------------------------------------------------------------ tuning overrides
 int g_override_bm_sub = 0;
 int g_override_bn = 0;
@@ -288,7 +309,9 @@ struct WGradPlan {
 WGradPlan plan_wgrad(int64_t m_rows, int64_t n_cols, int64_t pixels, int split_k, int sm_count) {
   WGradPlan w{};
   const int boxes = static_cast<int>(n_cols / 128);
-  w.group = 1;
+  // Wider column groups share each dY box among more MMAs (less L2->SMEM traffic
+  // per FLOP): 3 boxes (384 TMEM columns) when the column count allows it.
+  w.group = boxes % 3 == 0 ? 3 : (boxes % 2 == 0 ? 2 : 1);
   if (g_override_group > 0 && boxes % g_override_group == 0) w.group = g_override_group;
   w.num_groups = boxes / w.group;
   w.num_tiles = static_cast<int>(m_rows / 128) * w.num_groups;
@@ -305,9 +328,10 @@ WGradPlan plan_wgrad(int64_t m_rows, int64_t n_cols, int64_t pixels, int split_k
 
 int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, int group, cudaStream_t stream) {
   CUtensorMap mp;
-  if (int s = make_map_2d_store(&mp, p.partials, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
-                                static_cast<int64_t>(p.splits) * p.m_rows, p.n_cols, p.n_cols, 32, 32))
+  if (int s = make_map_2d_store(&mp, p.acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.m_rows, p.n_cols, p.n_cols, 32,
+                                32))
     return s;
+  FP8_CUDA_TRY(cudaMemsetAsync(p.acc, 0, static_cast<size_t>(p.m_rows) * p.n_cols * sizeof(float), stream));
   if (group == 1) return launch_wgrad_cfg<1>(mdy, mb, mp, p, stream);
   if (group == 2) return launch_wgrad_cfg<2>(mdy, mb, mp, p, stream);
   if (group == 3) return launch_wgrad_cfg<3>(mdy, mb, mp, p, stream);
@@ -353,7 +377,7 @@ size_t quant_workspace_bytes(int sm_count) {
 // ======================================================================== C ABI
 extern "C" {
 
-int fp8_abi_version(void) { return 1; }
+int fp8_abi_version(void) { return 2; }
 
 int fp8_last_error(char* buf, size_t len) {
   if (buf != nullptr && len > 0) {
@@ -541,13 +565,8 @@ int fp8_transpose_2d(const void* src, void* dst, int64_t rows, int64_t cols, fp8
   FP8_REQUIRE(rows >= 0 && cols >= 0, FP8_ERR_INVALID_ARGUMENT, "negative size");
   if (rows == 0 || cols == 0) return ok();
   FP8_REQUIRE(src != nullptr && dst != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
-  const int64_t gx = (rows + kTransTile - 1) / kTransTile, gy = (cols + kTransTile - 1) / kTransTile;
-  FP8_REQUIRE(gx < (1ll << 31) && gy <= 65535, FP8_ERR_UNSUPPORTED, "transpose too large");
-  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), 1);
-  transpose_u8_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, cols, cols, rows, 0, 0);
-  count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
+  if (int s = launch_transpose(src, dst, rows, cols, cols, rows, 0, 0, 1, reinterpret_cast<cudaStream_t>(stream)))
+    return s;
   return ok();
 }
 
@@ -556,11 +575,9 @@ int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8
   FP8_REQUIRE(wq != nullptr && wq_t != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   // src [Cout][9][Cin]: per tap a Cout x Cin matrix with leading dim 9*Cin, batch stride Cin.
   // dst [Cin][9][Cout]: per tap a Cin x Cout matrix with leading dim 9*Cout, batch stride Cout.
-  dim3 grid((cout + kTransTile - 1) / kTransTile, (cin + kTransTile - 1) / kTransTile, 9);
-  transpose_u8_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(wq), static_cast<uint8_t*>(wq_t), cout, cin, 9ll * cin, 9ll * cout, cin, cout);
-  count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
+  if (int s = launch_transpose(wq, wq_t, cout, cin, 9ll * cin, 9ll * cout, cin, cout, 9,
+                               reinterpret_cast<cudaStream_t>(stream)))
+    return s;
   return ok();
 }
 
@@ -652,8 +669,9 @@ size_t fp8_conv3x3_wgrad_workspace_bytes(int batch, int height, int width, int c
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (sms <= 0) sms = 148;
   (void)cudaGetLastError();
-  const WGradPlan w = plan_wgrad(cout, 9ll * cin, static_cast<int64_t>(batch) * height * width, split_k, sms);
-  return static_cast<size_t>(w.splits) * cout * 9 * cin * sizeof(float);
+  (void)sms;
+  (void)split_k;
+  return static_cast<size_t>(cout) * 9 * cin * sizeof(float);
 }
 
 int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx, const float* sdy, int batch,
@@ -669,9 +687,9 @@ int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx
   if (int s = device_state(&st)) return s;
   const int64_t pixels = static_cast<int64_t>(batch) * height * width;
   const WGradPlan w = plan_wgrad(cout, 9ll * cin, pixels, split_k, st->sm_count);
-  const size_t need = static_cast<size_t>(w.splits) * cout * 9 * cin * sizeof(float);
+  const size_t need = static_cast<size_t>(cout) * 9 * cin * sizeof(float);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
-              "wgrad workspace too small: need %zu bytes (splits=%d)", need, w.splits);
+              "wgrad workspace too small: need %zu bytes", need);
   CUtensorMap mdy, mx;
   if (int s = make_map_2d(&mdy, dyq, pixels, cout, 128)) return s;
   if (int s = make_map_conv(&mx, xq, batch, height, width, cin, t)) return s;
@@ -686,12 +704,11 @@ int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx
   p.cchunks = cin / 128;
   p.n_cols = 9 * cin;
   p.m_rows = cout;
-  p.partials = static_cast<float*>(workspace);
+  p.acc = static_cast<float*>(workspace);
   p.err = st->err_ptr;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   if (int s = launch_wgrad(mdy, mx, p, w.group, cs)) return s;
-  if (int s = launch_wgrad_reduce(p.partials, w.splits, static_cast<int64_t>(cout) * 9 * cin, sx, sdy, dw,
-                                  st->sm_count, cs))
+  if (int s = launch_wgrad_reduce(p.acc, 1, static_cast<int64_t>(cout) * 9 * cin, sx, sdy, dw, st->sm_count, cs))
     return s;
   return ok();
 }
@@ -741,8 +758,9 @@ size_t fp8_gemm_wgrad_workspace_bytes(int64_t m, int64_t n, int64_t k, int split
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (sms <= 0) sms = 148;
   (void)cudaGetLastError();
-  const WGradPlan w = plan_wgrad(n, k, m, split_k, sms);
-  return static_cast<size_t>(w.splits) * n * k * sizeof(float);
+  (void)sms;
+  (void)split_k;
+  return static_cast<size_t>(n) * k * sizeof(float);
 }
 
 int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, const float* sx, int64_t m,
@@ -759,9 +777,9 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
   DeviceState* st;
   if (int s = device_state(&st)) return s;
   const WGradPlan w = plan_wgrad(n, k, m, split_k, st->sm_count);
-  const size_t need = static_cast<size_t>(w.splits) * n * k * sizeof(float);
+  const size_t need = static_cast<size_t>(n) * k * sizeof(float);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
-              "wgrad workspace too small: need %zu bytes (splits=%d)", need, w.splits);
+              "wgrad workspace too small: need %zu bytes", need);
   CUtensorMap mdy, mx;
   if (int s = make_map_2d(&mdy, dy, m, n, 128)) return s;
   if (int s = make_map_2d(&mx, x, m, k, 128)) return s;
@@ -773,11 +791,11 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
   p.b_conv = 0;
   p.n_cols = static_cast<int>(k);
   p.m_rows = static_cast<int>(n);
-  p.partials = static_cast<float*>(workspace);
+  p.acc = static_cast<float*>(workspace);
   p.err = st->err_ptr;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   if (int s = launch_wgrad(mdy, mx, p, w.group, cs)) return s;
-  if (int s = launch_wgrad_reduce(p.partials, w.splits, n * k, sdy, sx, dw, st->sm_count, cs)) return s;
+  if (int s = launch_wgrad_reduce(p.acc, 1, n * k, sdy, sx, dw, st->sm_count, cs)) return s;
   return ok();
 }
 

@@ -1,8 +1,8 @@
 // gemm_wgrad.cuh — tcgen05 FP8 weight-gradient GEMM with MN-major operands and
 // split-K over the pixel (token) dimension:
 //
-//   partial[s, co, j] = sum_{m in split s} dY[m, co] * B[m, j]
-//   dW[co, j]         = bf16( (sum_s partial[s, co, j]) * sx * sdy )
+//   acc[co, j] += sum_{m in split s} dY[m, co] * B[m, j]      (every split s, in L2)
+//   dW[co, j]   = bf16( acc[co, j] * sx * sdy )
 //
 // 3x3 conv (reference conv2d_dw_fp8_kernel + conv2d_dw_reduce_fp8_kernel,
 // fp8_kernels.py:385-468): j = tap * Cin + ci and B[m, j] = Xq at pixel m shifted
@@ -17,7 +17,11 @@
 //
 // Each CTA owns one output tile (128 rows of co x G*128 columns of j) and one
 // K split; it is not persistent.  Roles as in the K-major kernel: warp 0 TMA,
-// warp 1 TMEM + MMA, warps 2..5 write fp32 partials.
+// warp 1 TMEM + MMA, warps 2..5 move the fp32 tile out.  Split results are
+// summed by TMA reduce-add (cp.reduce.async.bulk.tensor .add) into one fp32
+// accumulator that the host zeroes first, instead of materialising one partial
+// matrix per split and reading them all back (the reference's reduce kernel);
+// the order of those fp32 additions is not fixed.
 #pragma once
 
 #include "gemm_kmajor.cuh"
@@ -35,7 +39,7 @@ struct WGradParams {
   int HW, W, cchunks;  // conv geometry
   int n_cols;          // columns of the partial / dW rows (9*Cin or K)
   int m_rows;          // rows of dW (Cout or N)
-  float* partials;     // [splits][m_rows][n_cols]
+  float* acc;          // [m_rows][n_cols] fp32, zeroed before the launch
   int* err;
 };
 
@@ -52,7 +56,7 @@ struct WGradConfig {
 template <int G>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     wgrad_fp8_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_b,
-                     const __grid_constant__ CUtensorMap tmap_part, const WGradParams p) {
+                     const __grid_constant__ CUtensorMap tmap_acc, const WGradParams p) {
   using Cfg = WGradConfig<G>;
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -89,7 +93,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_dy);
     tma_prefetch_desc(&tmap_b);
-    tma_prefetch_desc(&tmap_part);
+    tma_prefetch_desc(&tmap_acc);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -187,27 +191,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait(drain_bar, 0, &never, p.err, kErrTimeoutDrain);
     }
   } else {
-    // Epilogue: fp32 partial rows of this split, 32 columns (128 B) at a time,
-    // staged 128B-swizzled in shared memory and written with TMA stores.
+    // Epilogue: this split's fp32 rows, 32 columns (128 B) at a time, staged
+    // 128B-swizzled in shared memory and added into the accumulator by TMA.
     const int quarter = warp & 3;
     uint8_t* stage_buf = epi_smem + (warp - 2) * 2 * kEpiBufBytes;
-    const int row0 = split * p.m_rows + co_tile * 128 + quarter * 32;  // partial row of lane 0
+    const int row0 = co_tile * 128 + quarter * 32;
     const bool has_work = kb_end > kb_begin;
-    bool ok = true;
-    if (has_work) ok = mbar_wait(tfull_bar, 0, abort_flag, p.err, kErrTimeoutEpilogue);
-    if (ok) {
+    if (has_work && mbar_wait(tfull_bar, 0, abort_flag, p.err, kErrTimeoutEpilogue)) {
       tc_fence_after();
       int buf = 0;
 #pragma unroll 1
       for (int c = 0; c < G * 128; c += 32) {
         uint32_t r[32];
-        if (has_work) {
-          tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + c, r);
-          tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
-        }
+        tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + c, r);
+        tmem_ld_wait();
         uint8_t* sbuf = stage_buf + buf * kEpiBufBytes;
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
@@ -217,7 +214,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmap_part, sbuf, group * G * 128 + c, row0);
+          tma_reduce_add_2d(&tmap_acc, sbuf, group * G * 128 + c, row0);
           bulk_commit_group();
         }
         buf ^= 1;
@@ -234,8 +231,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// dW[i] = bf16( (sum_s partials[s][i]) * sx * sdy ), i over rows*cols (multiple of 4).
-// Same order as the reference reduce (fp8_kernels.py:463-468): sum splits, then scale.
+// dW[i] = bf16( (sum_s partials[s][i]) * sx * sdy ), i over rows*cols (multiple of 4):
+// the reference's reduce (fp8_kernels.py:463-468) — sum the splits, then scale.
+// With the in-L2 split reduction there is one "split" (the accumulator).
 __global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restrict__ partials, int splits,
                                                            int64_t count, const float* __restrict__ sa,
                                                            const float* __restrict__ sb,

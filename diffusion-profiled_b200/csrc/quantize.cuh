@@ -222,4 +222,29 @@ __global__ void __launch_bounds__(256) transpose_u8_kernel(const uint8_t* __rest
   }
 }
 
+// Same transpose for whole 64x64 tiles with 16-byte aligned rows: one 16-byte
+// load and one 16-byte store per thread (the weight re-layout of the
+// data-grad runs on every backward pass, so it should cost a launch, not more).
+__global__ void __launch_bounds__(256) transpose_u8_tiles16_kernel(const uint8_t* __restrict__ src,
+                                                                   uint8_t* __restrict__ dst, int64_t src_ld,
+                                                                   int64_t dst_ld, int64_t src_bstride,
+                                                                   int64_t dst_bstride) {
+  __shared__ __align__(16) uint8_t tile[kTransTile][kTransTile + 4];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kTransTile;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * kTransTile;
+  const uint8_t* s = src + static_cast<int64_t>(blockIdx.z) * src_bstride;
+  uint8_t* d = dst + static_cast<int64_t>(blockIdx.z) * dst_bstride;
+  const int row = threadIdx.x >> 2, seg = (threadIdx.x & 3) * 16;
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(s + (r0 + row) * src_ld + c0 + seg));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) tile[row][seg + i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+  __syncthreads();
+  // output row = input column `row`, output bytes = input rows seg .. seg+15
+  uint32_t o[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i >> 2] |= static_cast<uint32_t>(tile[seg + i][row]) << (8 * (i & 3));
+  *reinterpret_cast<uint4*>(d + (c0 + row) * dst_ld + r0 + seg) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 }  // namespace fp8b

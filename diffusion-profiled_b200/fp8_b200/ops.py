@@ -132,14 +132,6 @@ def _(src):
     return src.new_empty((src.shape[1], src.shape[0]))
 
 
-def _conv_weight_t(wq: torch.Tensor) -> torch.Tensor:
-    """[Cout, Cin, 3, 3] channels_last e4m3 -> [Cin][3][3][Cout] bytes (as [Cin, 9*Cout])."""
-    cout, cin = wq.shape[0], wq.shape[1]
-    wt = torch.empty((cin, 9 * cout), device=wq.device, dtype=FP8_DTYPE)
-    _lib.call("fp8_conv_weight_transpose", _ptr(wq), _ptr(wt), cout, cin, _stream(wq.device))
-    return wt
-
-
 # ----------------------------------------------------------------------------- conv 3x3
 def _check_conv_operand(t: torch.Tensor, name: str) -> None:
     if t.dim() != 4:
@@ -208,7 +200,8 @@ def conv3x3_dgrad(dyq: torch.Tensor, wq: torch.Tensor, sdy: torch.Tensor, sw: to
         raise RuntimeError(f"weight shape {tuple(wq.shape)} does not match Cout={cout} 3x3")
     dx = torch.empty((b, cin, h, w), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
     with torch.cuda.device(dev):
-        wt = _conv_weight_t(wq)
+        wt = torch.empty((cin, 9 * cout), device=dev, dtype=FP8_DTYPE)  # [Cin][3][3][Cout]
+        _lib.call("fp8_conv_weight_transpose", _ptr(wq), _ptr(wt), cout, cin, _stream(dev))
         _lib.call(
             "fp8_conv3x3_dgrad", _ptr(dyq), _ptr(wt), _ptr(dx), _ptr(sdy), _ptr(sw), b, h, w, cin, cout,
             _stream(dev),

@@ -104,8 +104,9 @@ int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_sca
 int fp8_transpose_2d(const void* src, void* dst, int64_t rows, int64_t cols, fp8_stream_t stream);
 
 /* Conv weight re-layout for the data-grad: wq [Cout][3][3][Cin] (channels_last
- * [Cout,Cin,3,3]) -> wq_t [Cin][3][3][Cout].  No reference counterpart: the
- * reference's dX kernel gathers W with strided loads (fp8_kernels.py:306-309). */
+ * [Cout,Cin,3,3]) -> wq_t [Cin][3][3][Cout], so that fp8_conv3x3_dgrad reads a
+ * K-major B operand.  No reference counterpart: the reference's dX kernel
+ * gathers W with strided loads (fp8_kernels.py:306-309). */
 int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8_stream_t stream);
 
 /* ------------------------------------------------------------ 3x3 conv (pad 1) */
@@ -121,21 +122,23 @@ int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, co
                     int epilogue, int batch, int height, int width, int cin, int cout, fp8_stream_t stream);
 
 /* dx[n,h,w,ci] = sum_{kh,kw,co} dyq[n,h+1-kh,w+1-kw,co] * wq[co,kh,kw,ci] * sdy * sw
- * dyq: NHWC e4m3 [B][H][W][Cout]; wq_t: [Cin][3][3][Cout] (fp8_conv_weight_transpose);
- * dx: NHWC bf16 [B][H][W][Cin].
+ * dyq: NHWC e4m3 [B][H][W][Cout]; wq_t: [Cin][3][3][Cout] (fp8_conv_weight_transpose
+ * of the forward's wq); dx: NHWC bf16 [B][H][W][Cin].
  * Replaces conv2d_bwd_input_fp8_prequantized + conv2d_dx_fp8_kernel
  * (fp8_kernels.py:671-709, :250-318). */
 int fp8_conv3x3_dgrad(const void* dyq, const void* wq_t, void* dx, const float* sdy, const float* sw, int batch,
                       int height, int width, int cin, int cout, fp8_stream_t stream);
 
-/* Workspace bytes of fp8_conv3x3_wgrad for a split count (split_k <= 0: the
- * library's choice, the same one fp8_conv3x3_wgrad makes for split_k <= 0). */
+/* Workspace bytes of fp8_conv3x3_wgrad: one fp32 accumulator of Cout*9*Cin
+ * elements (split_k does not change it; 0 for unsupported geometry). */
 size_t fp8_conv3x3_wgrad_workspace_bytes(int batch, int height, int width, int cin, int cout, int split_k);
 
 /* dw[co,kh,kw,ci] = sum_{n,h,w} dyq[n,h,w,co] * xq[n,h+kh-1,w+kw-1,ci] * sx * sdy
  * xq: NHWC e4m3 [B][H][W][Cin]; dyq: NHWC e4m3 [B][H][W][Cout]; dw: bf16
- * [Cout][3][3][Cin] (channels_last [Cout,Cin,3,3]).  Split-K over pixels with
- * fp32 partials in the workspace.
+ * [Cout][3][3][Cin] (channels_last [Cout,Cin,3,3]).  Split-K over pixels
+ * (split_k <= 0: the library's choice); the splits' fp32 sums are added in L2
+ * into the workspace accumulator (zeroed by this call), so their order of
+ * addition is not fixed.
  * Replaces conv2d_bwd_weight_fp8_prequantized (fp8_kernels.py:723-808) with
  * its transpose_fp8_2d_kernel, conv2d_dw_fp8_kernel and
  * conv2d_dw_reduce_fp8_kernel (:321-337, :385-468). */
@@ -152,7 +155,7 @@ int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx
 int fp8_gemm(const void* a, const void* b, void* out, const float* sa, const float* sb, const void* bias,
              int epilogue, int64_t m, int64_t n, int64_t k, fp8_stream_t stream);
 
-/* Workspace bytes of fp8_gemm_wgrad. */
+/* Workspace bytes of fp8_gemm_wgrad: one fp32 accumulator of N*K elements. */
 size_t fp8_gemm_wgrad_workspace_bytes(int64_t m, int64_t n, int64_t k, int split_k);
 
 /* dw[n,k] = sum_m dy[m,n] * x[m,k] * sdy * sx; dy: [M][N] e4m3, x: [M][K] e4m3,

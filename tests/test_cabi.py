@@ -37,7 +37,7 @@ def test_binding_covers_every_declared_symbol():
 
 
 def test_abi_version():
-    assert _lib.load().fp8_abi_version() == 1
+    assert _lib.load().fp8_abi_version() == 2
 
 
 def _status_and_message(fn, *args):
@@ -107,8 +107,10 @@ def test_workspace_queries_are_host_only():
     # unsupported geometry -> 0 bytes, no CUDA needed
     assert lib.fp8_conv3x3_wgrad_workspace_bytes(2, 7, 7, 128, 128, 0) == 0
     assert lib.fp8_gemm_wgrad_workspace_bytes(16, 100, 128, 0) == 0
-    # explicit split count: splits * Cout * 9 * Cin * 4 bytes
+    # one fp32 accumulator of Cout * 9 * Cin, whatever the split count
     assert lib.fp8_conv3x3_wgrad_workspace_bytes(2, 8, 8, 128, 128, 1) == 128 * 9 * 128 * 4
+    assert lib.fp8_conv3x3_wgrad_workspace_bytes(2, 8, 8, 128, 256, 7) == 256 * 9 * 128 * 4
+    assert lib.fp8_gemm_wgrad_workspace_bytes(300, 256, 128, 0) == 256 * 128 * 4
 
 
 def test_python_ops_have_no_cpu_path():
