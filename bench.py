@@ -63,6 +63,8 @@ def parse_args():
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
+    ap.add_argument("--no-unet", action="store_true", help="skip the UNet training-step measurement")
+    ap.add_argument("--unet-steps", type=int, default=30, help="timed UNet training steps")
     return ap.parse_args()
 
 
@@ -279,6 +281,13 @@ def run_b200(args) -> None:
     del graphs
     torch.cuda.synchronize()
 
+    unet = None
+    if not args.no_unet:
+        unet = {"fp8_convs": time_unet(args, dev, world, fp8=True)}
+        if world == 1:
+            unet["bf16"] = time_unet(args, dev, world, fp8=False)
+            unet["fp8_speedup_vs_bf16"] = round(unet["fp8_convs"]["value"] / unet["bf16"]["value"], 3)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_oracle_baseline(args, seconds=args.cpu_seconds)
@@ -322,6 +331,7 @@ def run_b200(args) -> None:
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "unet_train": unet,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -441,6 +451,53 @@ def roofline(kernels: dict, peaks: dict, batch: int) -> dict | None:
             "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
             "peak_note": f"{peaks['source']} HBM copy bandwidth",
             "algorithmic": f"3 B/elem = {work:.4g} B per call"}
+
+
+def time_unet(args, dev, world, fp8: bool) -> dict:
+    """BASELINE configs 4/5: the CUDA-graph UNet training step (B images per GPU,
+    data parallel with the bucketed bf16 all-reduce when world > 1)."""
+    import torch.distributed as dist
+
+    from fp8_b200.train import GraphedTrainStep, TrainConfig, build_model, images_per_second
+
+    rank = int(os.environ.get("RANK", "0"))
+    model = build_model(fp8=fp8, scaling="delayed", device=dev, seed=0)
+    step = GraphedTrainStep(model, TrainConfig(batch_size=args.batch), dev)
+    torch.manual_seed(100 + rank)
+    step.prepare()
+    g = torch.Generator().manual_seed(200 + rank)
+    images = [(torch.rand(args.batch, 3, 32, 32, generator=g) * 2 - 1).to(memory_format=torch.channels_last)
+              .to(dev) for _ in range(2)]
+    for i in range(3):
+        step.step(images[i % 2])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.unet_steps):
+        step.step(images[i % 2])
+    ev1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.unet_steps
+    loss = step.loss_acc.item() / (args.unet_steps + 3)
+    n_fp8 = sum(1 for m in model.modules() if hasattr(m, "uses_fp8"))
+    allreduce = step.dp.bytes_per_step() if step.dp is not None else 0
+    step.release()
+    del step, model
+    torch.cuda.synchronize()
+    return {"metric": "UNet train imgs/s", "value": round(images_per_second(args.batch, world, ms), 1),
+            "unit": "imgs/s", "ms_per_step": round(ms, 4), "steps": args.unet_steps, "batch_per_gpu": args.batch,
+            "global_batch": args.batch * world, "n_gpus": world, "mean_loss": round(loss, 4),
+            "fp8": ("whitelisted 3x3 convs, delayed scaling" if fp8 else "off (bf16 autocast)"),
+            "conv_modules": n_fp8, "allreduce_bf16_bytes_per_step": allreduce,
+            "step": "noise + UNet fwd/bwd (bf16 autocast) + grad all-reduce + clip 1.0 + fused AdamW 2e-4 + EMA, "
+                    "one CUDA graph replay"}
 
 
 def time_e2e(args, dev, world, conv_api, step_flops) -> dict:

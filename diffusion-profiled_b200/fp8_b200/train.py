@@ -1,0 +1,243 @@
+"""DDPM UNet training step on B200: CUDA-graph captured, data parallel over NCCL.
+
+What one step does (the reference's captured step, train.py:104-149 with the
+loss of ddpm.py:174-215):
+
+    x_t = sqrt(abar_t) x + sqrt(1 - abar_t) eps     t ~ U{0..T-1}, eps ~ N(0, 1)
+    loss = mse(UNet(x_t, t), eps)                    bf16 autocast, FP8 convs
+    backward -> (data parallel) bf16 gradient all-reduce -> clip_grad_norm(1.0)
+    -> fused AdamW -> EMA of the weights (beta 0.9999)
+
+Data parallelism: every rank holds a full replica and its own batch.  The
+gradients are averaged with NCCL all-reduces of bf16 buckets (~25 MB), each
+launched on a side stream as soon as backward has produced every gradient of
+the bucket (post-accumulate-grad hooks), so the exchange overlaps the rest of
+backward; the step joins the side stream before clipping.  FP8 scales and the
+delayed-scaling windows stay rank-local (the reference has no distributed code;
+this is the data-parallel step of BASELINE config 5).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .unet import UNet, UNetConfig
+
+
+# ----------------------------------------------------------------------------- diffusion
+class LinearSchedule:
+    """Linear beta schedule of ddpm.py:122-131 (betas 1e-4 .. 0.02 over T steps, computed in fp64)."""
+
+    def __init__(self, max_t: int = 1000, device: torch.device | str = "cuda"):
+        scale = max_t / 1000
+        betas = torch.linspace(1e-4 / scale, 0.02 / scale, max_t, dtype=torch.float64)
+        self.alpha_bars = torch.cumprod(1.0 - betas, dim=0).float().to(device)
+        self.max_t = max_t
+
+    def noise(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(x_t, eps, t) for a batch (ddpm.py:190-206)."""
+        t = torch.randint(0, self.max_t, (x.shape[0],), device=x.device)
+        eps = torch.randn_like(x)
+        ab = self.alpha_bars[t][:, None, None, None]
+        return ab.sqrt() * x + (1.0 - ab).sqrt() * eps, eps, t
+
+
+def diffusion_loss(model: torch.nn.Module, x: torch.Tensor, sched: LinearSchedule) -> torch.Tensor:
+    x_t, eps, t = sched.noise(x)
+    return F.mse_loss(model(x_t, t), eps)
+
+
+# ----------------------------------------------------------------------------- gradient all-reduce
+class BucketedAllReduce:
+    """Average gradients across ranks in bf16 buckets, overlapped with backward.
+
+    Buckets are filled in reverse parameter order (roughly the order backward
+    produces gradients).  For each bucket a hook counts the gradients that have
+    been accumulated; the last one launches, on ``comm_stream``, the pack to a
+    flat bf16 buffer, ``all_reduce(SUM)``, and the unpack ``grad = flat / world``.
+    ``finish()`` makes the current stream wait for the side stream.
+    """
+
+    def __init__(self, params: list[torch.nn.Parameter], group=None, bucket_bytes: int = 25 << 20):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.params = [p for p in params if p.requires_grad]
+        # CPU tensors (gloo, host-side tests) reduce synchronously, without a side stream.
+        self.comm_stream = torch.cuda.Stream(self.params[0].device) if self.params[0].is_cuda else None
+        self.buckets: list[list[torch.nn.Parameter]] = []
+        cur, size = [], 0
+        for p in reversed(self.params):
+            cur.append(p)
+            size += p.numel() * 2
+            if size >= bucket_bytes:
+                self.buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.buckets.append(cur)
+        self.flat = [torch.empty(sum(p.numel() for p in b), device=b[0].device, dtype=torch.bfloat16)
+                     for b in self.buckets]
+        self.pending = [0] * len(self.buckets)
+        self.bucket_of = {}
+        for i, b in enumerate(self.buckets):
+            for p in b:
+                self.bucket_of[p] = i
+        self.handles = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
+        self.launched = 0
+
+    def bytes_per_step(self) -> int:
+        return sum(f.numel() * 2 for f in self.flat)
+
+    def start(self) -> None:
+        self.pending = [len(b) for b in self.buckets]
+        self.launched = 0
+
+    def _on_grad(self, p: torch.nn.Parameter) -> None:
+        i = self.bucket_of[p]
+        self.pending[i] -= 1
+        if self.pending[i] == 0:
+            self._launch(i)
+
+    def _reduce(self, i: int) -> None:
+        bucket, flat = self.buckets[i], self.flat[i]
+        torch.cat([p.grad.reshape(-1) for p in bucket], out=flat)  # fp32 -> bf16 pack
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+        off = 0
+        for p in bucket:
+            n = p.numel()
+            p.grad.copy_(flat[off:off + n].view_as(p.grad)).div_(self.world)
+            off += n
+
+    def _launch(self, i: int) -> None:
+        if self.comm_stream is None:
+            self._reduce(i)
+        else:
+            self.comm_stream.wait_stream(torch.cuda.current_stream(self.flat[i].device))
+            with torch.cuda.stream(self.comm_stream):
+                self._reduce(i)
+        self.launched += 1
+
+    def finish(self) -> None:
+        if self.launched != len(self.buckets):
+            raise RuntimeError(f"only {self.launched} of {len(self.buckets)} gradient buckets were reduced")
+        if self.comm_stream is not None:
+            torch.cuda.current_stream(self.flat[0].device).wait_stream(self.comm_stream)
+
+    def remove(self) -> None:
+        for h in self.handles:
+            h.remove()
+
+
+# ----------------------------------------------------------------------------- the step
+@dataclass
+class TrainConfig:
+    batch_size: int = 128
+    lr: float = 2e-4
+    max_t: int = 1000
+    ema_beta: float = 0.9999
+    grad_clip: float = 1.0
+    warmup_iters: int = 3
+
+
+class EMA:
+    """Exponential moving average of the floating-point state (ddpm.py:10-25)."""
+
+    def __init__(self, model: torch.nn.Module, beta: float):
+        self.beta = beta
+        self.src = [v for v in model.state_dict().values() if v.is_floating_point()]
+        self.avg = [v.detach().clone() for v in self.src]
+
+    @torch.no_grad()
+    def update(self) -> None:
+        torch._foreach_mul_(self.avg, self.beta)
+        torch._foreach_add_(self.avg, self.src, alpha=1.0 - self.beta)
+
+
+class GraphedTrainStep:
+    """The captured training step; ``step(images)`` copies the batch in and replays."""
+
+    def __init__(self, model: UNet, cfg: TrainConfig, device: torch.device, dp_group=None, use_graph: bool = True):
+        self.model = model
+        self.cfg = cfg
+        self.device = device
+        self.sched = LinearSchedule(cfg.max_t, device)
+        self.params = [p for p in model.parameters() if p.requires_grad]
+        self.opt = torch.optim.AdamW(self.params, lr=cfg.lr, fused=True, capturable=True)
+        self.ema = EMA(model, cfg.ema_beta)
+        self.dp = BucketedAllReduce(self.params, dp_group) if dist.is_initialized() and \
+            dist.get_world_size(dp_group) > 1 else None
+        cin, res = model.config.in_channels, model.config.in_resolution
+        self.static_batch = torch.zeros(cfg.batch_size, cin, res, res, device=device).to(
+            memory_format=torch.channels_last)
+        self.loss_acc = torch.zeros((), device=device)
+        self.graph = None
+        self.use_graph = use_graph
+
+    def _body(self) -> torch.Tensor:
+        self.opt.zero_grad(set_to_none=False)
+        if self.dp is not None:
+            self.dp.start()
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            loss = diffusion_loss(self.model, self.static_batch, self.sched)
+        self.loss_acc.add_(loss.detach())
+        loss.backward()
+        if self.dp is not None:
+            self.dp.finish()
+        torch.nn.utils.clip_grad_norm_(self.params, max_norm=self.cfg.grad_clip)
+        self.opt.step()
+        self.ema.update()
+        return loss
+
+    def prepare(self) -> None:
+        """Eager warm-up iterations on a side stream (they also fill the delayed-scaling
+        windows, train.py:114-128), then capture."""
+        self.model.train()
+        for p in self.params:  # grads must exist before capture (zero_grad keeps them)
+            p.grad = torch.zeros_like(p)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(self.cfg.warmup_iters):
+                self._body()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        if self.use_graph:
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._body()
+        self.loss_acc.zero_()
+
+    def step(self, images: torch.Tensor | None = None) -> None:
+        if images is not None:
+            self.static_batch.copy_(images, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._body()
+
+    def release(self) -> None:
+        """Drop the graph (before tearing the process group down) and the hooks."""
+        self.graph = None
+        if self.dp is not None:
+            self.dp.remove()
+
+
+def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16,), p_drop: float = 0.1,
+                device: torch.device | str = "cuda", seed: int = 0) -> UNet:
+    torch.manual_seed(seed)
+    cfg = UNetConfig(fp8_convs_enabled=fp8, fp8_scaling_type=scaling, attn_resolutions=list(attn_resolutions),
+                     p_drop=p_drop)
+    model = UNet(cfg).to(memory_format=torch.channels_last)
+    return model.to(device)
+
+
+def images_per_second(batch: int, world: int, ms_per_step: float) -> float:
+    return batch * world / (ms_per_step * 1e-3)
+
+
+__all__ = ["LinearSchedule", "diffusion_loss", "BucketedAllReduce", "TrainConfig", "EMA", "GraphedTrainStep",
+           "build_model", "images_per_second", "math"]

@@ -1,0 +1,233 @@
+"""DDPM UNet with the reference's architecture, calling the B200 FP8 conv op.
+
+This is the caller of the FP8 path (the reference's ``diffusion/unet.py``),
+rebuilt here so that the training step can run on a machine without the
+reference checkout.  Module and buffer names follow the reference one for one,
+so ``state_dict``s are interchangeable:
+
+* ``Conv2dFP8`` (unet.py:32-94): an ``nn.Conv2d`` 3x3 (``.conv``) plus, for
+  delayed scaling, the windows ``amax_window_{weights,acts,dy}`` (they hold
+  scales, amax/448) and ``window_pos``; shapes in ``SUPPORTED_UNET_SHAPES`` go to
+  ``triton_conv2d_fp8``, everything else to the bf16 conv.
+* ``ResidualBlock`` (unet.py:107-161), ``CHWAttention`` (:164-203), ``Stage``
+  (:206-242), ``UNet`` (:245-388) with ``UNetConfig`` (:13-28).
+
+Architecture (reference defaults used by BASELINE config 4: base 128, channel
+multipliers (1, 2, 2, 2), 2 residual blocks per level, GroupNorm(32), SiLU,
+dropout, attention at the listed resolutions plus the 4x4 middle stage, a
+512-wide time-embedding MLP on a 128-wide sinusoidal embedding).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, field
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
+
+
+@dataclass
+class UNetConfig:
+    in_channels: int = 3
+    base_hidden: int = 128
+    scales: list[int] = field(default_factory=lambda: [1, 2, 2, 2])
+    n_heads: int = 4
+    p_drop: float = 0.1
+    attn_resolutions: list[int] = field(default_factory=lambda: [16])
+    in_resolution: int = 32
+    n_resblocks: int = 2
+    fp8_convs_enabled: bool = False
+    fp8_scaling_type: str = "current"
+    fp8_amax_history: int = 1024
+
+    def as_dict(self):
+        return asdict(self)
+
+
+class Conv2dFP8(nn.Module):
+    """3x3 / pad 1 conv; FP8 for whitelisted shapes, bf16 ``nn.Conv2d`` otherwise."""
+
+    def __init__(self, in_channels: int, out_channels: int, fp8_convs_enabled: bool, scaling_type: str = "current",
+                 amax_history: int | None = None):
+        super().__init__()
+        if scaling_type not in ("current", "delayed"):
+            raise ValueError(f"unknown FP8 scaling type {scaling_type!r}")
+        self.conv = nn.Conv2d(in_channels, out_channels, (3, 3), stride=1, padding=1, bias=False)
+        self.scaling_type = scaling_type
+        self.fp8_convs_enabled = fp8_convs_enabled
+        if scaling_type == "delayed":
+            if amax_history is None:
+                raise ValueError("delayed scaling needs amax_history")
+            self.amax_history = amax_history
+            # scale history (amax / 448) of the weights, inputs and output gradients
+            self.register_buffer("amax_window_weights", torch.zeros(amax_history))
+            self.register_buffer("amax_window_acts", torch.zeros(amax_history))
+            self.register_buffer("amax_window_dy", torch.zeros(amax_history))
+            self.register_buffer("window_pos", torch.zeros((), dtype=torch.long))
+
+    def uses_fp8(self, x: torch.Tensor) -> bool:
+        key = (x.shape[1], self.conv.weight.shape[0], x.shape[2], x.shape[3])
+        return self.fp8_convs_enabled and key in SUPPORTED_UNET_SHAPES
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not self.uses_fp8(x):
+            return self.conv(x)
+        x = x.contiguous(memory_format=torch.channels_last)
+        if self.scaling_type == "current":
+            return triton_conv2d_fp8(x, self.conv.weight)
+        with torch.no_grad():
+            x_hist = torch.max(self.amax_window_acts)
+            w_hist = torch.max(self.amax_window_weights)
+        out, x_scale, w_scale = triton_conv2d_fp8(
+            x, self.conv.weight, (x_hist, w_hist), (self.amax_window_dy, self.window_pos), do_delayed=True
+        )
+        with torch.no_grad():
+            idx = self.window_pos.unsqueeze(0)
+            self.amax_window_weights.scatter_(0, idx, w_scale.detach().unsqueeze(0))
+            self.amax_window_acts.scatter_(0, idx, x_scale.detach().unsqueeze(0))
+            self.window_pos.add_(1).remainder_(self.amax_history)
+        return out
+
+
+class TimeEmbed(nn.Module):
+    """Per-block projection of the time embedding to a (scale, shift) pair."""
+
+    def __init__(self, embed_channels: int, channels: int):
+        super().__init__()
+        self.mlp = nn.Linear(embed_channels, channels, bias=False)
+
+    def forward(self, t: torch.Tensor) -> torch.Tensor:
+        return self.mlp(t)[:, :, None, None]
+
+
+class ResidualBlock(nn.Module):
+    def __init__(self, config: UNetConfig, in_chann: int, out_chann: int, p_drop: float = 0.0):
+        super().__init__()
+        conv = dict(fp8_convs_enabled=config.fp8_convs_enabled, scaling_type=config.fp8_scaling_type,
+                    amax_history=config.fp8_amax_history)
+        self.conv_1 = Conv2dFP8(in_chann, out_chann, **conv)
+        self.conv_2 = Conv2dFP8(out_chann, out_chann, **conv)
+        self.norm1 = nn.GroupNorm(32, in_chann)
+        self.norm2 = nn.GroupNorm(32, out_chann)
+        self.t_embed_wb = TimeEmbed(4 * config.base_hidden, 2 * out_chann)
+        self.skip_connection: nn.Module = (
+            nn.Identity() if in_chann == out_chann else nn.Conv2d(in_chann, out_chann, (1, 1), bias=False)
+        )
+        self.dropout = nn.Dropout(p_drop)
+        nn.init.zeros_(self.conv_2.conv.weight)
+
+    def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        h = self.conv_1(F.silu(self.norm1(x)))
+        scale, shift = torch.chunk(self.t_embed_wb(t), chunks=2, dim=1)
+        h = (scale + 1) * self.norm2(h) + shift
+        h = self.conv_2(self.dropout(F.silu(h)))
+        return (self.skip_connection(x) + h) / math.sqrt(2.0)
+
+
+class CHWAttention(nn.Module):
+    """Multi-head self-attention over the pixels of a [B, C, H, W] feature map."""
+
+    def __init__(self, config: UNetConfig, hidden_size: int):
+        super().__init__()
+        self.nh = config.n_heads
+        self.qkv = nn.Linear(hidden_size, 3 * hidden_size, bias=False)
+        self.out = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.norm = nn.LayerNorm(hidden_size)
+        nn.init.zeros_(self.out.weight)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        b, c, h, w = x.shape
+        tokens = self.norm(x.flatten(2).transpose(1, 2))  # [B, HW, C]
+        q, k, v = self.qkv(tokens).chunk(3, dim=-1)
+        heads = lambda z: z.unflatten(-1, (self.nh, c // self.nh)).transpose(1, 2)  # noqa: E731
+        o = F.scaled_dot_product_attention(heads(q), heads(k), heads(v))
+        o = self.out(o.transpose(1, 2).flatten(2))  # [B, HW, C]
+        return (o.transpose(1, 2).reshape(b, c, h, w) + x) / math.sqrt(2.0)
+
+
+class Stage(nn.Module):
+    def __init__(self, config: UNetConfig, in_channels: int, hidden_channels: int, out_channels: int,
+                 attention: bool = False, num_blocks: int = 2):
+        super().__init__()
+        self.num_blocks = num_blocks
+        widths = [in_channels] + [hidden_channels] * (num_blocks - 1) + [out_channels]
+        self.blocks = nn.ModuleList(
+            ResidualBlock(config, widths[i], widths[i + 1], p_drop=config.p_drop) for i in range(num_blocks)
+        )
+        self.attns = nn.ModuleList(
+            CHWAttention(config, widths[i + 1]) if attention else nn.Identity() for i in range(num_blocks)
+        )
+
+    def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        for block, attn in zip(self.blocks, self.attns):
+            x = attn(block(x, t))
+        return x
+
+
+class UNet(nn.Module):
+    def __init__(self, config: UNetConfig):
+        super().__init__()
+        self.config = config
+        self.base_channs = base = config.base_hidden
+        chans = [s * base for s in config.scales]
+        self.conv_in = nn.Conv2d(config.in_channels, chans[0], (3, 3), padding=1, bias=False)
+
+        down, up = [], []
+        res = config.in_resolution
+        for cur, nxt in zip(chans[:-1], chans[1:]):
+            attn = res in config.attn_resolutions
+            down.append(Stage(config, cur, cur, nxt, attention=attn, num_blocks=config.n_resblocks))
+            up.insert(0, Stage(config, 2 * nxt, cur, cur, attention=attn, num_blocks=config.n_resblocks + 1))
+            res //= 2
+        mid = chans[-1]
+        down.append(Stage(config, mid, mid, mid, num_blocks=config.n_resblocks))
+        up.insert(0, Stage(config, 2 * mid, mid, mid, num_blocks=config.n_resblocks + 1))
+        # the reference always gives the middle stage attention (unet.py:311-318)
+        self.mid = Stage(config, mid, mid, mid, attention=True, num_blocks=config.n_resblocks)
+        self.down_stages = nn.ModuleList(down)
+        self.up_stages = nn.ModuleList(up)
+
+        self.out = nn.Sequential(
+            nn.GroupNorm(32, chans[0]), nn.SiLU(),
+            nn.Conv2d(chans[0], config.in_channels, (3, 3), padding=1, bias=False),
+        )
+        self.time_embed = nn.Sequential(
+            nn.Linear(base, 4 * base, bias=False), nn.SiLU(), nn.Linear(4 * base, 4 * base, bias=False), nn.SiLU(),
+        )
+        nn.init.zeros_(self.out[-1].weight)
+        half = base // 2
+        freqs = torch.exp(-torch.arange(half, dtype=torch.float32) * (math.log(10000.0) / half))
+        self.register_buffer("freqs", freqs, persistent=False)
+
+    def _timestep(self, t: torch.Tensor) -> torch.Tensor:
+        emb = t[:, None].float() * self.freqs[None]
+        emb = torch.cat([emb.sin(), emb.cos()], dim=1)
+        if self.base_channs % 2 == 1:
+            emb = F.pad(emb, (0, 1))
+        return emb
+
+    def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        t_emb = self.time_embed(self._timestep(t))
+        act = self.conv_in(x)
+        skips = []
+        for i, stage in enumerate(self.down_stages):
+            act = stage(F.interpolate(act, scale_factor=0.5, mode="nearest") if i > 0 else act, t_emb)
+            skips.append(act)
+        act = self.mid(act, t_emb)
+        for i, stage in enumerate(self.up_stages):
+            h = skips.pop()
+            up = F.interpolate(act, scale_factor=2.0, mode="nearest") if i > 0 else act
+            act = stage(torch.cat([up, h], dim=1), t_emb)
+        return self.out(act)
+
+
+def fp8_conv_modules(model: nn.Module) -> list[Conv2dFP8]:
+    return [m for m in model.modules() if isinstance(m, Conv2dFP8)]
+
+
+__all__ = ["UNetConfig", "UNet", "Conv2dFP8", "ResidualBlock", "CHWAttention", "Stage", "TimeEmbed",
+           "fp8_conv_modules"]
