@@ -6,6 +6,7 @@
 // launches on the caller's stream.  It allocates nothing.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -16,6 +17,7 @@
 #include "gemm_kmajor.cuh"
 #include "gemm_wgrad.cuh"
 #include "quantize.cuh"
+#include "conv_halo.cuh"
 
 using namespace fp8b;
 
@@ -215,6 +217,92 @@ int launch_transpose(const void* src, void* dst, int64_t rows, int64_t cols, int
 int g_override_bm_sub = 0;
 int g_override_bn = 0;
 int g_override_group = 0;
+int g_conv_algo = 0;  // 0 auto, 1 tap-by-tap K-major GEMM, 2 halo kernel (where it applies)
+
+// ------------------------------------------------------------------ halo conv launch
+// NHWC map whose box is (128 channels, W, R+2 rows, 1 image): the rows of one
+// 128-pixel tile plus one halo row on each side.
+int make_map_conv_halo(CUtensorMap* map, const void* ptr, int batch, int height, int width, int channels,
+                       int rows_per_tile) {
+  EncodeTiledFn enc;
+  if (int s = get_encode_fn(&enc)) return s;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(width),
+                        static_cast<cuuint64_t>(height), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(width) * channels,
+                           static_cast<cuuint64_t>(height) * width * channels};
+  cuuint32_t box[4] = {128u, static_cast<cuuint32_t>(width), static_cast<cuuint32_t>(rows_per_tile + 2), 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FP8_REQUIRE(r == CUDA_SUCCESS, FP8_ERR_CUDA, "cuTensorMapEncodeTiled(conv halo %dx%dx%dx%d) failed: %d", batch,
+              height, width, channels, (int)r);
+  return FP8_OK;
+}
+
+// The halo kernel needs 128-pixel tiles inside one image with 1024-byte aligned
+// row shifts: W in {16, 32} (every 32x32 and 16x16 shape of the UNet).
+bool halo_applies(int height, int width) {
+  return (width == 32 || width == 16) && (height * width) % 128 == 0 && height % (128 / width) == 0;
+}
+
+template <int BN, bool RES, int W>
+int launch_halo_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const HaloParams& p,
+                    int sm_count, cudaStream_t stream) {
+  using Cfg = HaloConfig<BN, RES, W>;
+  auto kern = conv_halo_fp8_kernel<BN, RES, W>;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  int grid;
+  if (RES) {
+    // every CTA owns one column tile (its weights stay in smem)
+    const int per_n = std::max(1, std::min(sm_count / p.num_n_tiles, p.num_m_tiles));
+    grid = per_n * p.num_n_tiles;
+  } else {
+    grid = std::min(sm_count, p.num_m_tiles * p.num_n_tiles);
+  }
+  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
+  count_launches(1);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
+}
+
+// Conv fwd / data-grad with the halo kernel.  act: NHWC e4m3 input of the GEMM
+// (X for fwd, dY for data-grad) with `c_red` channels; wmat: K-major weights
+// [n_out][9*c_red]; out: NHWC bf16 [B*H*W][n_out].
+int launch_conv_halo(const void* act, const void* wmat, void* out, const float* sa, const float* sb,
+                     const void* bias, int epilogue, int batch, int height, int width, int c_red, int n_out,
+                     bool fwd, int* err, int sm_count, cudaStream_t stream) {
+  const int rows = 128 / width;
+  const bool resident = (c_red == 128);
+  const int bn = resident ? 128 : (n_out % 256 == 0 ? 256 : 128);
+  CUtensorMap ma, mb, mo;
+  if (int s = make_map_conv_halo(&ma, act, batch, height, width, c_red, rows)) return s;
+  if (int s = make_map_2d(&mb, wmat, n_out, 9ll * c_red, bn)) return s;
+  const int64_t M = static_cast<int64_t>(batch) * height * width;
+  if (int s = make_map_out_bf16(&mo, out, M, n_out)) return s;
+  HaloParams p{};
+  p.num_n_tiles = n_out / bn;
+  p.num_m_tiles = static_cast<int>(M / 128);
+  p.cchunks = c_red / 128;
+  p.HW = height * width;
+  p.W = width;
+  p.R = rows;
+  p.fwd = fwd ? 1 : 0;
+  p.N = n_out;
+  p.scale_a = sa;
+  p.scale_b = sb;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.epilogue = epilogue;
+  p.err = err;
+  if (width == 32) {
+    if (resident) return launch_halo_cfg<128, true, 32>(ma, mb, mo, p, sm_count, stream);
+    if (bn == 256) return launch_halo_cfg<256, false, 32>(ma, mb, mo, p, sm_count, stream);
+    return launch_halo_cfg<128, false, 32>(ma, mb, mo, p, sm_count, stream);
+  }
+  if (resident) return launch_halo_cfg<128, true, 16>(ma, mb, mo, p, sm_count, stream);
+  if (bn == 256) return launch_halo_cfg<256, false, 16>(ma, mb, mo, p, sm_count, stream);
+  return launch_halo_cfg<128, false, 16>(ma, mb, mo, p, sm_count, stream);
+}
 
 // ------------------------------------------------------------------ K-major GEMM launch
 template <int BM_SUB, int BN, int STAGES>
@@ -595,6 +683,12 @@ int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, co
               "bias epilogue needs a 16-byte aligned bias");
   DeviceState* st;
   if (int s = device_state(&st)) return s;
+  if (g_conv_algo != 1 && halo_applies(height, width)) {
+    if (int s = launch_conv_halo(xq, wq, y, sx, sw, bias, epilogue, batch, height, width, cin, cout, true,
+                                 st->err_ptr, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+      return s;
+    return ok();
+  }
   CUtensorMap ma, mb;
   if (int s = make_map_conv(&ma, xq, batch, height, width, cin, t)) return s;
   const int64_t M = static_cast<int64_t>(batch) * height * width;
@@ -633,6 +727,12 @@ int fp8_conv3x3_dgrad(const void* dyq, const void* wq_t, void* dx, const float* 
               "conv tensors must be 16-byte aligned");
   DeviceState* st;
   if (int s = device_state(&st)) return s;
+  if (g_conv_algo != 1 && halo_applies(height, width)) {
+    if (int s = launch_conv_halo(dyq, wq_t, dx, sdy, sw, nullptr, kEpiNone, batch, height, width, cout, cin, false,
+                                 st->err_ptr, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+      return s;
+    return ok();
+  }
   CUtensorMap ma, mb;
   if (int s = make_map_conv(&ma, dyq, batch, height, width, cout, t)) return s;
   const int64_t M = static_cast<int64_t>(batch) * height * width;
@@ -805,6 +905,12 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
               FP8_ERR_INVALID_ARGUMENT, "blocks per SM must be in 0..%d", kMaxQuantBlocksPerSm);
   g_quant_amax_bps = amax_blocks_per_sm > 0 ? amax_blocks_per_sm : 4;
   g_quant_cast_bps = cast_blocks_per_sm > 0 ? cast_blocks_per_sm : 4;
+  return ok();
+}
+
+int fp8_set_conv_algo(int algo) {
+  FP8_REQUIRE(algo >= 0 && algo <= 2, FP8_ERR_INVALID_ARGUMENT, "conv algo must be 0 (auto), 1 or 2");
+  g_conv_algo = algo;
   return ok();
 }
 

@@ -67,6 +67,7 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "fp8_set_tile_override": (c_int, [c_int, c_int, c_int]),
     "fp8_set_quantize_override": (c_int, [c_int, c_int]),
+    "fp8_set_conv_algo": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()
@@ -134,6 +135,10 @@ def kernel_launch_count() -> int:
 
 def set_tile_override(bm_sub: int = 0, bn: int = 0, wgrad_group: int = 0) -> None:
     check(load().fp8_set_tile_override(bm_sub, bn, wgrad_group), "fp8_set_tile_override")
+
+
+def set_conv_algo(algo: int = 0) -> None:
+    check(load().fp8_set_conv_algo(algo), "fp8_set_conv_algo")
 
 
 def set_quantize_override(amax_blocks_per_sm: int = 0, cast_blocks_per_sm: int = 0) -> None:

@@ -169,6 +169,12 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
  * choice.  Process-wide; meant for benchmarks and tests. */
 int fp8_set_tile_override(int bm_sub, int bn, int wgrad_group);
 
+/* Algorithm of fp8_conv3x3_fwd / fp8_conv3x3_dgrad: 0 = the library's choice
+ * (the halo kernel for 32x32 and 16x16 images, the tap-by-tap GEMM otherwise),
+ * 1 = always tap-by-tap, 2 = halo wherever it applies.  Process-wide; meant for
+ * benchmarks and tests. */
+int fp8_set_conv_algo(int algo);
+
 /* Tuning override for the quantize grids: CTAs per SM of the amax pass and of
  * the cast pass (1..8; 0 restores the built-in choice).  Process-wide. */
 int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);

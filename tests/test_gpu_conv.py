@@ -174,3 +174,41 @@ def test_conv_config2_full_size(cuda):
     ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())
     assert oracle.max_rel_err(y, ref) <= TOL
     assert ops.device_error() == 0
+
+
+HALO_SHAPES = [s for s in SUPPORTED if s[3] in (16, 32)]
+
+
+@pytest.mark.parametrize("algo", [1, 2])
+@pytest.mark.parametrize("cin,cout,h,w", HALO_SHAPES)
+def test_conv_fwd_and_dgrad_both_algorithms(cuda, algo, cin, cout, h, w):
+    """Tap-by-tap GEMM (algo 1) and the halo kernel (algo 2) against the oracle."""
+    from fp8_b200 import _lib, ops
+
+    b = 2 if h == 32 else 4
+    xq, sx = _rand_q((b, cin, h, w), seed=3 * cin + cout + w, device=cuda)
+    dyq, sdy = _rand_q((b, cout, h, w), seed=5 * cin + cout + h, device=cuda, scale=1e-2)
+    wq, sw = _rand_q((cout, cin, 3, 3), seed=11 + cout, device=cuda, scale=0.05)
+    y_ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())
+    dx_ref = oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())
+    try:
+        _lib.set_conv_algo(algo)
+        y = ops.conv3x3_fwd(xq, wq, sx, sw)
+        dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
+    finally:
+        _lib.set_conv_algo(0)
+    assert oracle.max_rel_err(y, y_ref) <= TOL
+    assert oracle.max_rel_err(dx, dx_ref) <= TOL
+    assert ops.device_error() == 0
+
+
+def test_conv_halo_bias_silu_epilogue(cuda):
+    from fp8_b200 import ops
+
+    xq, sx = _rand_q((2, 128, 16, 16), seed=61, device=cuda)
+    wq, sw = _rand_q((256, 128, 3, 3), seed=62, device=cuda, scale=0.05)
+    g = torch.Generator().manual_seed(63)
+    bias = (torch.randn(256, generator=g) * 0.1).to(torch.bfloat16)
+    y = ops.conv3x3_fwd(xq, wq, sx, sw, bias.to(cuda), 2)
+    ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item(), bias=bias, silu=True)
+    assert oracle.max_rel_err(y, ref) <= TOL
