@@ -440,19 +440,56 @@ int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const 
 }
 
 // ------------------------------------------------------------------ quantize launch helpers
-constexpr int kAmaxVec = 8;          // 16-byte loads in flight per thread, amax pass
-constexpr int kCastVec = 2;          // 16-byte loads in flight per thread, cast pass
+// 16-byte aligned x with 8-byte aligned q takes the streaming kernels
+// (quant_stream_kernel); anything else takes the grid-stride scalar kernels.
 constexpr int kMaxQuantBlocksPerSm = 8;
-int g_quant_amax_bps = 4;            // CTAs per SM (grid cap) of the amax pass
-int g_quant_cast_bps = 4;            // CTAs per SM (grid cap) of the cast pass
+constexpr int kMaxStreamBlocksPerSm = 3;  // 3 x kStreamSmemBytes fit in one SM's shared memory
+int g_quant_amax_bps = 2;                 // CTAs per SM (grid cap) of the amax pass
+int g_quant_cast_bps = 2;                 // CTAs per SM (grid cap) of the cast pass
 
-int quant_grid(int64_t n, int vec, int blocks_per_sm, int sm_count) {
-  const int64_t per_block = static_cast<int64_t>(kQuantThreads) * vec * 8;  // elements per CTA iteration
-  int64_t blocks = (n + per_block - 1) / per_block;
+int quant_grid(int64_t n, bool vec, int blocks_per_sm, int sm_count) {
+  int64_t blocks;
+  if (vec) {
+    blocks = ((n & ~int64_t(7)) * 2 + kStreamChunkBytes - 1) / kStreamChunkBytes;
+    if (blocks_per_sm > kMaxStreamBlocksPerSm) blocks_per_sm = kMaxStreamBlocksPerSm;
+  } else {
+    blocks = (n + kQuantThreads - 1) / kQuantThreads;
+  }
   const int64_t cap = static_cast<int64_t>(sm_count) * blocks_per_sm;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   return static_cast<int>(blocks);
+}
+
+template <int KIND>
+int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const float* partials_in, int n_partials,
+                  const float* prev_scale, float* scale_out, float* partials_out, int* err, cudaStream_t cs) {
+  FP8_CUDA_TRY(cudaFuncSetAttribute(quant_stream_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kStreamSmemBytes)));
+  quant_stream_kernel<KIND><<<grid, kStreamThreads, kStreamSmemBytes, cs>>>(x, q, n, partials_in, n_partials,
+                                                                             prev_scale, scale_out, partials_out, err);
+  return FP8_OK;
+}
+
+// Current scaling: amax pass (parts CTAs, one partial each), then the cast pass.
+int launch_quantize_current(const uint16_t* x, uint8_t* q, float* scale_out, float* partials, int parts, int64_t n,
+                            bool vec, const DeviceState* st, cudaStream_t cs) {
+  const int cast_blocks = quant_grid(n, vec, g_quant_cast_bps, st->sm_count);
+  if (vec) {
+    if (int s = launch_stream<kStreamAmax>(parts, x, nullptr, n, nullptr, 0, nullptr, nullptr, partials,
+                                           st->err_ptr, cs))
+      return s;
+    if (int s = launch_stream<kStreamCastCurrent>(cast_blocks, x, q, n, partials, parts, nullptr, scale_out, nullptr,
+                                                  st->err_ptr, cs))
+      return s;
+  } else {
+    amax_partials_kernel<<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
+    quantize_cast_kernel<kCurrent>
+        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
+  }
+  count_launches(2);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
 }
 
 // Partials never exceed kMaxQuantBlocksPerSm per SM, whatever the tuning.
@@ -523,25 +560,13 @@ int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, voi
   DeviceState* st;
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  const int parts = quant_grid(n, kAmaxVec, g_quant_amax_bps, st->sm_count);
+  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
+  const int parts = quant_grid(n, vec, g_quant_amax_bps, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= parts * sizeof(float) && aligned(workspace, 4),
               FP8_ERR_WORKSPACE, "quantize workspace too small: need %zu bytes", parts * sizeof(float));
-  float* partials = static_cast<float*>(workspace);
-  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
-  const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
-  uint8_t* q = static_cast<uint8_t*>(q_e4m3);
-  const int cast_blocks = quant_grid(n, kCastVec, g_quant_cast_bps, st->sm_count);
-  if (vec) {
-    amax_partials_kernel<true, kAmaxVec><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
-    quantize_cast_kernel<kCurrent, true, kCastVec>
-        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
-  } else {
-    amax_partials_kernel<false, 1><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
-    quantize_cast_kernel<kCurrent, false, 1>
-        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
-  }
-  count_launches(2);
-  FP8_CUDA_TRY(cudaGetLastError());
+  if (int s = launch_quantize_current(static_cast<const uint16_t*>(x_bf16), static_cast<uint8_t*>(q_e4m3), scale_out,
+                                      static_cast<float*>(workspace), parts, n, vec, st, cs))
+    return s;
   return ok();
 }
 
@@ -592,29 +617,17 @@ int fp8_quantize_current_noalloc(const void* x_bf16, void* q_e4m3, float* scale_
   if (int s = device_state(&st)) return s;
   float* partials = nullptr;
   if (int s = noalloc_scratch(&partials)) return s;
-  const int parts = quant_grid(n, kAmaxVec, g_quant_amax_bps, st->sm_count);
+  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
+  const int parts = quant_grid(n, vec, g_quant_amax_bps, st->sm_count);
   FP8_REQUIRE(parts <= kNoAllocPartials, FP8_ERR_UNSUPPORTED,
               "allocation-free quantize needs %d partial slots but its static scratch holds %d "
               "(device has too many SMs for it); use fp8_quantize_current with a workspace",
               parts, kNoAllocPartials);
-  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
-  const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
-  uint8_t* q = static_cast<uint8_t*>(q_e4m3);
-  const int cast_blocks = quant_grid(n, kCastVec, g_quant_cast_bps, st->sm_count);
   // Every CTA of the amax pass overwrites its own slot before the cast pass
   // reads slots [0, parts), so nothing has to be cleared between calls.
-  if (vec) {
-    amax_partials_kernel<true, kAmaxVec><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
-    quantize_cast_kernel<kCurrent, true, kCastVec>
-        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
-  } else {
-    amax_partials_kernel<false, 1><<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
-    quantize_cast_kernel<kCurrent, false, 1>
-        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
-  }
-  count_launches(2);
-  FP8_CUDA_TRY(cudaGetLastError());
+  if (int s = launch_quantize_current(static_cast<const uint16_t*>(x_bf16), static_cast<uint8_t*>(q_e4m3), scale_out,
+                                      partials, parts, n, vec, st, reinterpret_cast<cudaStream_t>(stream)))
+    return s;
   return ok();
 }
 
@@ -630,19 +643,21 @@ int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_sca
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   // The cast pass writes one partial per CTA, so its grid is the partial count.
-  const int parts = quant_grid(n, kCastVec, g_quant_cast_bps, st->sm_count);
+  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
+  const int parts = quant_grid(n, vec, g_quant_cast_bps, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= parts * sizeof(float) && aligned(workspace, 4),
               FP8_ERR_WORKSPACE, "quantize workspace too small: need %zu bytes", parts * sizeof(float));
   float* partials = static_cast<float*>(workspace);
-  const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
   const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
   uint8_t* q = static_cast<uint8_t*>(q_e4m3);
-  if (vec)
-    quantize_cast_kernel<kDelayed, true, kCastVec>
+  if (vec) {
+    if (int s = launch_stream<kStreamCastDelayed>(parts, x, q, n, nullptr, 0, prev_scale, nullptr, partials,
+                                                  st->err_ptr, cs))
+      return s;
+  } else {
+    quantize_cast_kernel<kDelayed>
         <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
-  else
-    quantize_cast_kernel<kDelayed, false, 1>
-        <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
+  }
   finalize_scale_kernel<<<1, kQuantThreads, 0, cs>>>(partials, parts, scale_curr_out);
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
@@ -903,8 +918,8 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
   FP8_REQUIRE(amax_blocks_per_sm >= 0 && amax_blocks_per_sm <= kMaxQuantBlocksPerSm && cast_blocks_per_sm >= 0 &&
                   cast_blocks_per_sm <= kMaxQuantBlocksPerSm,
               FP8_ERR_INVALID_ARGUMENT, "blocks per SM must be in 0..%d", kMaxQuantBlocksPerSm);
-  g_quant_amax_bps = amax_blocks_per_sm > 0 ? amax_blocks_per_sm : 4;
-  g_quant_cast_bps = cast_blocks_per_sm > 0 ? cast_blocks_per_sm : 4;
+  g_quant_amax_bps = amax_blocks_per_sm > 0 ? amax_blocks_per_sm : 2;
+  g_quant_cast_bps = cast_blocks_per_sm > 0 ? cast_blocks_per_sm : 2;
   return ok();
 }
 

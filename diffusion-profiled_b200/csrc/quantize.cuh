@@ -6,17 +6,21 @@
 //   q         = e4m3(max(-448, min(x / scale, 448)))      (:105-120, quantize_fp8_kernel)
 // The clamp uses min-then-max with non-NaN-propagating fminf/fmaxf (the
 // reference's tl.minimum / tl.maximum defaults), so x/0 = NaN clamps to +448.
-// The division is IEEE round-to-nearest (__fdiv_rn) and the cast is
+// x / scale is the IEEE round-to-nearest fp32 quotient (computed exactly
+// without a divide per element, see CastMarkstein and DivF64) and the cast is
 // cvt.rn.satfinite.e4m3x2.f32, which makes the bytes reproducible on the CPU.
 //
 // Current scaling (quantize_fp8, :559-601) is two launches:
-//   amax_partials_kernel : grid-stride |x| max, one fp32 partial per CTA
-//   quantize_cast_kernel<kCurrent> : every CTA folds the partials into amax and
-//                          the scale (the reference's separate finalize launch
-//                          disappears), CTA 0 publishes the scale, then casts.
+//   amax pass : |x| max, one fp32 partial per CTA
+//   cast pass : every CTA folds the partials into amax and the scale (the
+//               reference's separate finalize launch disappears), CTA 0
+//               publishes the scale, then casts.
 // Delayed scaling (quantize_fp8_delayed, :518-556) is one pass plus a 1-CTA fold:
-//   quantize_cast_kernel<kDelayed> : cast with the previous scale and emit amax partials
-//   finalize_scale_kernel          : partials -> current scale
+//   cast pass             : cast with the previous scale and emit amax partials
+//   finalize_scale_kernel : partials -> current scale
+// Each pass exists twice: quant_stream_kernel (bulk copies through shared
+// memory; 16-byte aligned x, 8-byte aligned q) and the scalar grid-stride
+// amax_partials_kernel / quantize_cast_kernel for any other alignment.
 #pragma once
 
 #include "sm100_common.cuh"
@@ -35,19 +39,106 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
   return r;
 }
 
-__device__ __forceinline__ float scale_and_clamp(float v, float s) {
-  float t = __fdiv_rn(v, s);
-  t = fminf(t, kE4M3Max);   // tl.minimum(scaled, FP8_MAX)
+// Two ways to get the e4m3 byte of x / s without an fp32 divide per element.
+// Both give the byte of the IEEE round-to-nearest fp32 quotient for every bf16
+// x; the kernel picks one per launch from s alone.
+//
+// DivF64 (any s).  With r = RN64(1/s) the double product RN64(x * r) is within
+// about 2^-52 (relative) of the exact quotient.  x is a bf16 value (integer
+// significand A < 2^8) and s an fp32 value (integer significand B < 2^24), so
+// the exact quotient is either an fp32 number or stays away from every fp32
+// rounding midpoint M = odd * 2^-p of its binade: |A/B - M| = |A*2^p - odd*B| /
+// (B*2^p) has a non-zero integer numerator, so it is at least 1/(B*2^p), which
+// is at least 2^-25/B > 2^-49 of M.  A double within 2^-52 of the quotient is
+// thus on the same side of every midpoint and rounds to the same fp32 value:
+// __double2float_rn(x * r) == IEEE x / s.  (Below 2^-126 the fp32 grid is
+// coarser; such quotients become e4m3 zero either way.)  Scales of 0, inf and
+// NaN behave as IEEE division does (r = inf, 0, NaN).  Costs two fp64
+// conversions per element, which bound the cast kernel's throughput.
+struct DivF64 {
+  double r;
+  __device__ __forceinline__ explicit DivF64(float s) : r(1.0 / static_cast<double>(s)) {}
+  __device__ __forceinline__ float operator()(float x) const {
+    return __double2float_rn(static_cast<double>(x) * r);
+  }
+  __device__ __forceinline__ uint32_t word(uint32_t w) const;
+};
+
+// Packed helpers: two bf16 in a 32-bit word (min/max return the other operand
+// when one is NaN), two fp32 in one instruction (sm_100 f32x2 arithmetic).
+__device__ __forceinline__ uint32_t bf16x2_min(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ float2 f32x2_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 f32x2_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// CastMarkstein (2^-60 <= s <= 2^100, i.e. every scale amax / 448 of a tensor
+// whose amax lies in [2^-51, 2^108]).  Per pair of bf16:
+//  1. clamp x to [-L, L] with bf16 min then max, where L is s * 1024 rounded up
+//     to bf16.  Values beyond L have |x / s| > 1024 and saturate either way,
+//     and a NaN x becomes L, so +448, as min(NaN / s, 448) does.  After this
+//     the quotient is finite and below 2^11.
+//  2. Markstein's correction step (P. Markstein, IBM J. Res. Dev. 34(1), 1990):
+//     with r = RN32(1/s), q0 = RN32(x * r), e = fma(q0, -s, x) (exact),
+//     q1 = RN32(q0 + e * r) is the correctly rounded quotient while
+//     |q0| >= 2^-11, where e stays normal.
+//  3. |q1| takes the sign of x: below 2^-11 the quotient becomes an e4m3 zero
+//     whose sign is that of x (q1 alone can lose it: -0 / s gives q1 = +0).
+//  4. cvt.rn.satfinite saturates |q1| >= 448 to +-448, as the clamp does.
+// The sequence is checked against IEEE division and the reference clamp on the
+// CPU: every (bf16 significand, fp32 significand) pair, exponents at the edges
+// of the scale range, and all 65,536 bf16 bit patterns against sampled scales.
+struct CastMarkstein {
+  float2 r2, ns2;      // (r, r), (-s, -s)
+  uint32_t lb2, nlb2;  // (L, L), (-L, -L) as bf16x2
+  // Two bf16 -> two e4m3 bytes in the low 16 bits.
+  __device__ __forceinline__ uint32_t word(uint32_t w) const {
+    const uint32_t c = bf16x2_max(bf16x2_min(w, lb2), nlb2);
+    const uint32_t lo = c << 16, hi = c & 0xFFFF0000u;
+    const float2 x = make_float2(__uint_as_float(lo), __uint_as_float(hi));
+    const float2 q0 = f32x2_mul(x, r2);
+    const float2 e = f32x2_fma(q0, ns2, x);
+    const float2 q1 = f32x2_fma(e, r2, q0);
+    const float t0 = __uint_as_float((__float_as_uint(q1.x) & 0x7FFFFFFFu) | (lo & 0x80000000u));
+    const float t1 = __uint_as_float((__float_as_uint(q1.y) & 0x7FFFFFFFu) | (hi & 0x80000000u));
+    return cvt_e4m3x2(t0, t1);
+  }
+};
+
+__device__ __forceinline__ bool markstein_applies(float s) { return s >= 0x1p-60f && s <= 0x1p100f; }
+__device__ __forceinline__ CastMarkstein make_markstein(float s) {
+  CastMarkstein c;
+  const float r = __fdiv_rn(1.0f, s);
+  c.r2 = make_float2(r, r);
+  c.ns2 = make_float2(-s, -s);
+  const uint32_t lb = ((__float_as_uint(s * 1024.0f) + 0xFFFFu) >> 16) & 0xFFFFu;  // round up to bf16
+  c.lb2 = lb | (lb << 16);
+  c.nlb2 = c.lb2 | 0x80008000u;
+  return c;
+}
+
+__device__ __forceinline__ float scale_and_clamp(float v, const DivF64& div) {
+  float t = div(v);
+  t = fminf(t, kE4M3Max);      // tl.minimum(scaled, FP8_MAX)
   return fmaxf(-kE4M3Max, t);  // tl.maximum(-FP8_MAX, .)
 }
 
-__device__ __forceinline__ float absmax_word(float m, uint32_t w) {
-  return fmaxf(m, fmaxf(fabsf(bf16_lo_f(w)), fabsf(bf16_hi_f(w))));
+__device__ __forceinline__ uint32_t DivF64::word(uint32_t w) const {
+  return cvt_e4m3x2(scale_and_clamp(bf16_lo_f(w), *this), scale_and_clamp(bf16_hi_f(w), *this));
 }
 
-// Block-wide max of a non-negative value; result valid in every thread.
+// Block-wide max of a non-negative value over NT threads; result valid in every thread.
+template <int NT = kQuantThreads>
 __device__ __forceinline__ float block_max(float v) {
-  __shared__ float red[kQuantThreads / 32];
+  static_assert(NT % 32 == 0 && NT <= 1024, "block size");
+  __shared__ float red[NT / 32];
   __shared__ float result;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -55,7 +146,7 @@ __device__ __forceinline__ float block_max(float v) {
   if (lane == 0) red[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    float w = lane < (kQuantThreads / 32) ? red[lane] : 0.0f;
+    float w = lane < (NT / 32) ? red[lane] : 0.0f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
     if (lane == 0) result = w;
@@ -70,74 +161,69 @@ __device__ __forceinline__ float scale_from_amax(float amax) {
 
 // Fold `count` partial maxima into the tensor scale (every CTA does this; the
 // partials are a few KB and L2 resident).
+template <int NT = kQuantThreads>
 __device__ __forceinline__ float fold_partials_to_scale(const float* __restrict__ partials, int count) {
   float m = 0.0f;
-  for (int i = threadIdx.x; i < count; i += blockDim.x) m = fmaxf(m, partials[i]);
-  return scale_from_amax(block_max(m));
+  for (int i = threadIdx.x; i < count; i += NT) m = fmaxf(m, partials[i]);
+  return scale_from_amax(block_max<NT>(m));
 }
 
-__device__ __forceinline__ float absmax_pair(uint32_t w) { return fmaxf(fabsf(bf16_lo_f(w)), fabsf(bf16_hi_f(w))); }
+// |x| maxima kept packed: two running bf16 maxima per 32-bit word (clearing
+// the sign bits is |.|; bf16x2 max skips NaN like fmaxf).  Exact: a max of
+// bf16 values is one of them.
+constexpr uint32_t kAbsMask2 = 0x7FFF7FFFu;
 
-// max |.| of the 8 bf16 of a 16-byte vector folded into m (a depth-3 tree, so
-// consecutive vectors do not serialise on one accumulator).
-__device__ __forceinline__ float absmax_vec(float m, const uint4& a) {
-  return fmaxf(m, fmaxf(fmaxf(absmax_pair(a.x), absmax_pair(a.y)), fmaxf(absmax_pair(a.z), absmax_pair(a.w))));
+// max |.| of the 8 bf16 of a 16-byte vector (a depth-2 tree).
+__device__ __forceinline__ uint32_t absmax_vec2(const uint4& a) {
+  return bf16x2_max(bf16x2_max(a.x & kAbsMask2, a.y & kAbsMask2), bf16x2_max(a.z & kAbsMask2, a.w & kAbsMask2));
 }
 
-// Pass 1 of current scaling: |x| max per CTA.  Each thread keeps V 16-byte
-// loads in flight per iteration (coalesced: vector i + v*T).  VEC: x is
-// 16-byte aligned.
-template <bool VEC, int V>
+__device__ __forceinline__ float unpack_max2(uint32_t m2) { return fmaxf(bf16_lo_f(m2), bf16_hi_f(m2)); }
+
+template <class Div>
+__device__ __forceinline__ uint32_t cast4(uint32_t w0, uint32_t w1, const Div& d) {
+  return d.word(w0) | (d.word(w1) << 16);
+}
+
+template <class Div>
+__device__ __forceinline__ uint2 cast_vec(const uint4& a, const Div& d) {
+  return make_uint2(cast4(a.x, a.y, d), cast4(a.z, a.w, d));
+}
+
+// ---------------------------------------------------------------- scalar passes
+// Grid-stride, one element per thread and step: the path for x that is not
+// 16-byte aligned or q that is not 8-byte aligned (views with an odd offset).
+// Aligned tensors take the streaming passes below.
+
+// Pass 1 of current scaling: |x| max per CTA.
 __global__ void __launch_bounds__(kQuantThreads) amax_partials_kernel(const uint16_t* __restrict__ x, int64_t n,
                                                                       float* __restrict__ partials) {
-  float m = 0.0f;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t done = 0;
-  if (VEC) {
-    const int64_t nvec = n >> 3;
-    const uint4* xv = reinterpret_cast<const uint4*>(x);
-    int64_t i = tid;
-    for (; i + (V - 1) * nthreads < nvec; i += V * nthreads) {
-      uint4 a[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) a[v] = __ldg(xv + i + v * nthreads);
-      float mv[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) mv[v] = absmax_vec(0.0f, a[v]);
-#pragma unroll
-      for (int w = 1; w < V; w *= 2) {
-#pragma unroll
-        for (int v = 0; v + w < V; v += 2 * w) mv[v] = fmaxf(mv[v], mv[v + w]);
-      }
-      m = fmaxf(m, mv[0]);
-    }
-    for (; i < nvec; i += nthreads) m = absmax_vec(m, __ldg(xv + i));
-    done = nvec << 3;
-  }
-  for (int64_t i = done + tid; i < n; i += nthreads) m = fmaxf(m, fabsf(__uint_as_float(uint32_t(x[i]) << 16)));
+  float m = 0.0f;
+  for (int64_t i = tid; i < n; i += nthreads) m = fmaxf(m, fabsf(__uint_as_float(uint32_t(x[i]) << 16)));
   m = block_max(m);
   if (threadIdx.x == 0) partials[blockIdx.x] = m;
 }
 
-__device__ __forceinline__ uint32_t cast4(uint32_t w0, uint32_t w1, float s) {
-  const uint32_t lo = cvt_e4m3x2(scale_and_clamp(bf16_lo_f(w0), s), scale_and_clamp(bf16_hi_f(w0), s));
-  const uint32_t hi = cvt_e4m3x2(scale_and_clamp(bf16_lo_f(w1), s), scale_and_clamp(bf16_hi_f(w1), s));
-  return lo | (hi << 16);
-}
-
-__device__ __forceinline__ uint2 cast_vec(const uint4& a, float s) {
-  return make_uint2(cast4(a.x, a.y, s), cast4(a.z, a.w, s));
+template <int MODE, class Div>
+__device__ __forceinline__ float cast_loop(const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n,
+                                           const Div& div) {
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  float m = 0.0f;
+  for (int64_t i = tid; i < n; i += nthreads) {
+    const uint32_t w = x[i];
+    if (MODE == kDelayed) m = fmaxf(m, fabsf(__uint_as_float(w << 16)));
+    q[i] = static_cast<uint8_t>(div.word(w) & 0xFFu);
+  }
+  return m;
 }
 
 // Cast pass.  kCurrent: scale = fold(partials_in); CTA 0 stores it to scale_out.
 //             kDelayed: scale = *prev_scale; each CTA also writes its |x| max
 //                       to partials_out[blockIdx.x].
-// V 16-byte loads in flight per thread and iteration.  In current mode x was
-// just read by the amax pass, so the loads here are its last use (streaming
-// hint); the e4m3 output is stored normally (its consumer follows).
-// VEC: x 16-byte aligned and q 8-byte aligned.
-template <int MODE, bool VEC, int V>
+template <int MODE>
 __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
     int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
@@ -149,41 +235,12 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
   } else {
     s = *prev_scale;
   }
-  float m = 0.0f;
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t done = 0;
-  if (VEC) {
-    const int64_t nvec = n >> 3;
-    const uint4* xv = reinterpret_cast<const uint4*>(x);
-    uint2* qv = reinterpret_cast<uint2*>(q);
-    int64_t i = tid;
-    for (; i + (V - 1) * nthreads < nvec; i += V * nthreads) {
-      uint4 a[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) a[v] = MODE == kCurrent ? __ldcs(xv + i + v * nthreads) : __ldg(xv + i + v * nthreads);
-      if (MODE == kDelayed) {
-#pragma unroll
-        for (int v = 0; v < V; ++v) m = absmax_vec(m, a[v]);
-      }
-#pragma unroll
-      for (int v = 0; v < V; ++v) qv[i + v * nthreads] = cast_vec(a[v], s);
-    }
-    for (; i < nvec; i += nthreads) {
-      const uint4 a = __ldg(xv + i);
-      if (MODE == kDelayed) m = absmax_vec(m, a);
-      qv[i] = cast_vec(a, s);
-    }
-    done = nvec << 3;
-  }
-  for (int64_t i = done + tid; i < n; i += nthreads) {
-    const float v = __uint_as_float(uint32_t(x[i]) << 16);
-    if (MODE == kDelayed) m = fmaxf(m, fabsf(v));
-    q[i] = static_cast<uint8_t>(cvt_e4m3x2(scale_and_clamp(v, s), 0.0f) & 0xFFu);
-  }
+  // s is uniform over the grid, so the branch never diverges.
+  const float m = markstein_applies(s) ? cast_loop<MODE>(x, q, n, make_markstein(s))
+                                       : cast_loop<MODE>(x, q, n, DivF64(s));
   if (MODE == kDelayed) {
-    m = block_max(m);
-    if (threadIdx.x == 0) partials_out[blockIdx.x] = m;
+    const float bm = block_max(m);
+    if (threadIdx.x == 0) partials_out[blockIdx.x] = bm;
   }
 }
 
@@ -191,6 +248,180 @@ __global__ void __launch_bounds__(kQuantThreads) finalize_scale_kernel(const flo
                                                                        int n_partials, float* __restrict__ scale_out) {
   const float s = fold_partials_to_scale(partials, n_partials);
   if (threadIdx.x == 0) *scale_out = s;
+}
+
+// ---------------------------------------------------------------- streaming passes
+// The 16-byte aligned bulk of x (all but the last n % 8 elements) moves through
+// shared memory in chunks of kStreamChunkBytes: one producer thread keeps
+// kStreamStages untiled bulk copies (cp.async.bulk, no multicast) in flight per
+// CTA, paced by full/empty mbarriers, and eight consumer warps read each chunk
+// from shared memory.  The copy engine keeps the loads in flight, so the
+// threads only spend instructions on the bytes themselves.  CTA c takes chunks
+// c, c + grid, ...; the last chunk may be short (a multiple of 16 bytes) and
+// CTA 0 also handles the n % 8 tail elements with plain loads.
+//   kStreamAmax        : |x| max per CTA                         -> partials_out
+//   kStreamCastCurrent : scale = fold(partials_in), cast; CTA 0 -> scale_out
+//   kStreamCastDelayed : cast with *prev_scale, |x| max per CTA  -> partials_out
+enum StreamKind : int { kStreamAmax = 0, kStreamCastCurrent = 1, kStreamCastDelayed = 2 };
+
+#ifndef FP8_STREAM_CHUNK_BYTES
+#define FP8_STREAM_CHUNK_BYTES 16384
+#endif
+#ifndef FP8_STREAM_STAGES
+#define FP8_STREAM_STAGES 4
+#endif
+#ifndef FP8_STREAM_CONSUMER_WARPS
+#define FP8_STREAM_CONSUMER_WARPS 8
+#endif
+constexpr int kStreamChunkBytes = FP8_STREAM_CHUNK_BYTES;
+constexpr int kStreamStages = FP8_STREAM_STAGES;
+constexpr int kStreamConsumerWarps = FP8_STREAM_CONSUMER_WARPS;
+constexpr int kStreamConsumers = kStreamConsumerWarps * 32;
+constexpr int kStreamThreads = kStreamConsumers + 32;  // + the producer warp
+constexpr int kStreamVecPerThread = kStreamChunkBytes / 16 / kStreamConsumers;
+constexpr size_t kStreamSmemBytes = static_cast<size_t>(kStreamStages) * kStreamChunkBytes + 2 * kStreamStages * 8;
+static_assert(kStreamChunkBytes % (16 * kStreamConsumers) == 0, "chunk must split evenly over the consumers");
+
+struct StreamShape {
+  int64_t main_bytes;  // bytes of x moved by bulk copies (a multiple of 16)
+  int64_t nchunks;
+};
+
+__device__ __forceinline__ StreamShape stream_shape(int64_t n) {
+  StreamShape sh;
+  sh.main_bytes = (n & ~int64_t(7)) * 2;
+  sh.nchunks = (sh.main_bytes + kStreamChunkBytes - 1) / kStreamChunkBytes;
+  return sh;
+}
+
+__device__ __forceinline__ void stream_produce(const uint16_t* __restrict__ x, uint8_t* bufs, uint64_t* full,
+                                               uint64_t* empty, const StreamShape& sh, volatile int* abort_flag,
+                                               int* err) {
+  int64_t issued = 0;
+  for (int64_t c = blockIdx.x; c < sh.nchunks; c += gridDim.x, ++issued) {
+    const int stage = static_cast<int>(issued % kStreamStages);
+    if (issued >= kStreamStages &&
+        !mbar_wait(&empty[stage], static_cast<uint32_t>((issued / kStreamStages - 1) & 1), abort_flag, err,
+                   kErrTimeoutQuant))
+      break;
+    const int64_t off = c * kStreamChunkBytes;
+    const int64_t left = sh.main_bytes - off;
+    const uint32_t bytes = static_cast<uint32_t>(left < kStreamChunkBytes ? left : kStreamChunkBytes);
+    mbar_arrive_expect_tx(&full[stage], bytes);
+    bulk_load_1d(bufs + stage * kStreamChunkBytes, reinterpret_cast<const uint8_t*>(x) + off, bytes, &full[stage]);
+  }
+  if (*abort_flag) {
+    // Consumers gave up: let the copies still in flight land before the CTA exits.
+    volatile int never = 0;
+    const int64_t first = issued > kStreamStages ? issued - kStreamStages : 0;
+    for (int64_t i = first; i < issued; ++i)
+      mbar_wait(&full[i % kStreamStages], static_cast<uint32_t>((i / kStreamStages) & 1), &never, err,
+                kErrTimeoutDrain);
+  }
+}
+
+// Consumer side; returns this thread's packed |x| maxima (amax kinds).
+template <int KIND, class Div>
+__device__ __forceinline__ uint32_t stream_consume(const uint8_t* bufs, uint64_t* full, uint64_t* empty,
+                                                   uint8_t* __restrict__ q, const StreamShape& sh, const Div& div,
+                                                   volatile int* abort_flag, int* err) {
+  uint32_t m2 = 0u;
+  const int t = threadIdx.x;
+  int64_t i = 0;
+  for (int64_t c = blockIdx.x; c < sh.nchunks; c += gridDim.x, ++i) {
+    const int stage = static_cast<int>(i % kStreamStages);
+    // Every lane waits (each needs the copy's bytes visible); the vote keeps the
+    // warp together if the wait gives up.
+    const bool ok = mbar_wait(&full[stage], static_cast<uint32_t>((i / kStreamStages) & 1), abort_flag, err,
+                              kErrTimeoutQuant);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const int64_t off = c * kStreamChunkBytes;
+    const int64_t left = sh.main_bytes - off;
+    const int nv = static_cast<int>((left < kStreamChunkBytes ? left : kStreamChunkBytes) >> 4);
+    const uint8_t* buf = bufs + stage * kStreamChunkBytes;
+    uint4 a[kStreamVecPerThread];
+#pragma unroll
+    for (int j = 0; j < kStreamVecPerThread; ++j) {
+      const int v = t + j * kStreamConsumers;
+      a[j] = v < nv ? ld_shared_v4(buf + v * 16) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    // The chunk is in registers: hand the stage back to the producer.
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&empty[stage]);
+    if (KIND != kStreamAmax) {
+      uint2* qv = reinterpret_cast<uint2*>(q + (off >> 1));
+#pragma unroll
+      for (int j = 0; j < kStreamVecPerThread; ++j) {
+        const int v = t + j * kStreamConsumers;
+        if (v < nv) qv[v] = cast_vec(a[j], div);
+      }
+    }
+    if (KIND != kStreamCastCurrent) {
+#pragma unroll
+      for (int j = 0; j < kStreamVecPerThread; ++j) m2 = bf16x2_max(m2, absmax_vec2(a[j]));
+    }
+  }
+  return m2;
+}
+
+// Both roles plus the tail; returns this thread's |x| max (amax kinds).
+template <int KIND, class Div>
+__device__ __forceinline__ float stream_body(const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n,
+                                             uint8_t* bufs, uint64_t* full, uint64_t* empty, const Div& div,
+                                             volatile int* abort_flag, int* err) {
+  const StreamShape sh = stream_shape(n);
+  float m = 0.0f;
+  if (threadIdx.x >= kStreamConsumers) {
+    if (threadIdx.x == kStreamConsumers) stream_produce(x, bufs, full, empty, sh, abort_flag, err);
+  } else {
+    m = unpack_max2(stream_consume<KIND>(bufs, full, empty, q, sh, div, abort_flag, err));
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t i = (sh.main_bytes >> 1) + threadIdx.x; i < n; i += kStreamThreads) {
+      const uint32_t w = x[i];
+      if (KIND != kStreamCastCurrent) m = fmaxf(m, fabsf(__uint_as_float(w << 16)));
+      if (KIND != kStreamAmax) q[i] = static_cast<uint8_t>(div.word(w) & 0xFFu);
+    }
+  }
+  return m;
+}
+
+// x 16-byte aligned, q 8-byte aligned.  Dynamic shared memory: kStreamSmemBytes.
+template <int KIND>
+__global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
+    const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
+    int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
+    float* __restrict__ partials_out, int* err) {
+  extern __shared__ __align__(128) uint8_t stream_smem[];
+  uint8_t* bufs = stream_smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stream_smem + kStreamStages * kStreamChunkBytes);
+  uint64_t* empty = full + kStreamStages;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStreamStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kStreamConsumerWarps);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  float s = 1.0f;
+  if (KIND == kStreamCastCurrent) {
+    s = fold_partials_to_scale<kStreamThreads>(partials_in, n_partials);  // contains __syncthreads
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
+  } else {
+    if (KIND == kStreamCastDelayed) s = *prev_scale;
+    __syncthreads();
+  }
+  float m;
+  if (KIND == kStreamAmax || !markstein_applies(s))  // s is uniform over the grid: no divergence
+    m = stream_body<KIND>(x, q, n, bufs, full, empty, DivF64(s), &abort_flag, err);
+  else
+    m = stream_body<KIND>(x, q, n, bufs, full, empty, make_markstein(s), &abort_flag, err);
+  if (KIND != kStreamCastCurrent) {
+    const float bm = block_max<kStreamThreads>(m);
+    if (threadIdx.x == 0) partials_out[blockIdx.x] = bm;
+  }
 }
 
 // ---------------------------------------------------------------- byte transposes

@@ -36,6 +36,7 @@ enum DeviceError : int {
   kErrTimeoutMma = 102,       // MMA issuer gave up waiting for a full stage / free accumulator
   kErrTimeoutEpilogue = 103,  // epilogue gave up waiting for a finished accumulator
   kErrTimeoutDrain = 104,     // teardown gave up waiting for in-flight async work
+  kErrTimeoutQuant = 105,     // streaming quantize pass gave up waiting for a bulk copy / free stage
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -163,6 +164,25 @@ __device__ __forceinline__ void bulk_wait_group_read() {
 template <int N>
 __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Untiled bulk copy global -> shared (no multicast), completing on `bar` with
+// `bytes` of transaction count.  Both addresses 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p))
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void st_shared_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

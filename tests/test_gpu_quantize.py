@@ -93,6 +93,33 @@ def test_quantize_delayed_bit_exact(cuda, prev):
     assert np.array_equal(_bytes(q), q_ref)
 
 
+@pytest.mark.parametrize(
+    "scale",
+    [1.0, 0.125, 0.1, 1.0 / 3.0, 0.7071068, 3.0, 7.3e-5, 1.2345678e-2, 2.9e5, 1e30,
+     2.0**-60, 2.0**100,  # edges of the fp32 correction-step window
+     1e-30, 2.0**-61, 3e30, 1e-40],  # outside it: the double-reciprocal path
+)
+@pytest.mark.parametrize("offset", [0, 1])  # 1: a view 2 bytes off 16-byte alignment (scalar kernels)
+def test_quantize_cast_every_bf16_value(cuda, scale, offset):
+    """Every one of the 65,536 bf16 bit patterns (NaN, inf, subnormals included), cast
+    with a fixed scale, gives the oracle's byte: both of the GPU's divide-free
+    quotients must equal IEEE fp32 division for every input, in the streaming and
+    in the scalar kernels."""
+    from fp8_b200 import ops
+
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.int16)
+    buf = torch.zeros(65536 + offset, dtype=torch.int16)
+    buf[offset:] = torch.from_numpy(bits.copy())
+    x = buf.to(cuda).view(torch.bfloat16)[offset:]
+    assert (x.data_ptr() % 16 == 0) == (offset == 0)
+    s32 = np.float32(scale)
+    q, _ = ops.quantize_delayed(x, torch.tensor(float(s32), dtype=torch.float32, device=cuda))
+    q_ref = oracle.cast_with_scale(oracle.bf16_bits_to_f32(bits.view(np.uint16)), s32)
+    got = _bytes(q)
+    bad = np.nonzero(got != q_ref)[0]
+    assert bad.size == 0, f"{bad.size} mismatches, first bf16 bits {bits.view(np.uint16)[bad[:5]]}"
+
+
 def test_quantize_delayed_ragged(cuda):
     from fp8_b200 import ops
 

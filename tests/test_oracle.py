@@ -23,6 +23,23 @@ def test_encoder_matches_torch_on_every_bf16_value():
         assert np.array_equal(oracle.e4m3_encode(t), _torch_e4m3(t)), s
 
 
+def test_double_reciprocal_multiply_equals_fp32_division():
+    """The GPU cast computes x / s as RN32(RN64(x * RN64(1 / s))).  Check that this
+    equals IEEE fp32 division for every finite bf16 x and many fp32 scales with full
+    24-bit significands (the CPU restatement of the argument in quantize.cuh)."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    v = oracle.bf16_bits_to_f32(bits)
+    v = v[np.isfinite(v)]
+    rng = np.random.default_rng(1234)
+    scales = (rng.random(300) * 2.0 ** rng.integers(-40, 40, 300)).astype(np.float32)
+    scales = np.concatenate([scales, np.float32([1.0, 0.1, 1 / 3, 448.0, 1 / 448, 2.0**-126, 3.4e38])])
+    v64 = v.astype(np.float64)
+    with np.errstate(over="ignore", under="ignore"):
+        for s in scales:
+            r = np.float64(1.0) / np.float64(s)
+            assert np.array_equal((v64 * r).astype(np.float32), v / s), s
+
+
 def test_encoder_ties_round_to_even():
     allb = np.arange(256, dtype=np.uint8)
     vals = torch.from_numpy(allb).view(torch.float8_e4m3fn).float().numpy()
