@@ -217,7 +217,7 @@ int launch_transpose(const void* src, void* dst, int64_t rows, int64_t cols, int
 int g_override_bm_sub = 0;
 int g_override_bn = 0;
 int g_override_group = 0;
-int g_conv_algo = 0;  // 0 auto, 1 tap-by-tap K-major GEMM, 2 halo kernel (where it applies)
+int g_conv_algo = 0;  // 0 auto, 1 tap-by-tap K-major GEMM, 2 halo kernel, 3 CTA-pair halo (where they apply)
 
 // ------------------------------------------------------------------ halo conv launch
 // NHWC map whose box is (128 channels, W, R+2 rows, 1 image): the rows of one
@@ -266,6 +266,44 @@ int launch_halo_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensor
   return FP8_OK;
 }
 
+// Clusters of two CTAs that can be resident at once (cached per device).
+int g_pair_clusters[kMaxDevices] = {};
+
+template <int W>
+int launch_halo_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const HaloParams& p,
+                     int sm_count, cudaStream_t stream) {
+  using Cfg = HaloPairConfig<W>;
+  auto kern = conv_halo_pair_fp8_kernel<W>;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int dev = 0;
+  FP8_CUDA_TRY(cudaGetDevice(&dev));
+  int max_pairs = (dev >= 0 && dev < kMaxDevices) ? g_pair_clusters[dev] : 0;
+  if (max_pairs <= 0) {
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count & ~1), 1, 1);
+    FP8_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg));
+    if (max_pairs <= 0) max_pairs = sm_count / 2;
+    if (dev >= 0 && dev < kMaxDevices) g_pair_clusters[dev] = max_pairs;
+  }
+  // Every pair keeps one column tile's weights resident: a whole number of pairs per column tile.
+  const int pair_tiles = p.num_m_tiles / 2;
+  const int per_n = std::max(1, std::min(max_pairs / p.num_n_tiles, pair_tiles));
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * per_n * p.num_n_tiles), 1, 1);
+  FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, p));
+  count_launches(1);
+  return FP8_OK;
+}
+
 // Conv fwd / data-grad with the halo kernel.  act: NHWC e4m3 input of the GEMM
 // (X for fwd, dY for data-grad) with `c_red` channels; wmat: K-major weights
 // [n_out][9*c_red]; out: NHWC bf16 [B*H*W][n_out].
@@ -274,10 +312,14 @@ int launch_conv_halo(const void* act, const void* wmat, void* out, const float* 
                      bool fwd, int* err, int sm_count, cudaStream_t stream) {
   const int rows = 128 / width;
   const bool resident = (c_red == 128);
+  // CTA pairs (only on request: measured slower than the single-CTA kernel on
+  // config 2): 128 reduced channels, whole 128-column tiles, 256-pixel tiles
+  // inside one image.
+  const bool pair = resident && g_conv_algo == 3 && n_out % 128 == 0 && (height * width) % 256 == 0;
   const int bn = resident ? 128 : (n_out % 256 == 0 ? 256 : 128);
   CUtensorMap ma, mb, mo;
   if (int s = make_map_conv_halo(&ma, act, batch, height, width, c_red, rows)) return s;
-  if (int s = make_map_2d(&mb, wmat, n_out, 9ll * c_red, bn)) return s;
+  if (int s = make_map_2d(&mb, wmat, n_out, 9ll * c_red, pair ? 64 : bn)) return s;
   const int64_t M = static_cast<int64_t>(batch) * height * width;
   if (int s = make_map_out_bf16(&mo, out, M, n_out)) return s;
   HaloParams p{};
@@ -294,6 +336,10 @@ int launch_conv_halo(const void* act, const void* wmat, void* out, const float* 
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.epilogue = epilogue;
   p.err = err;
+  if (pair) {
+    if (width == 32) return launch_halo_pair<32>(ma, mb, mo, p, sm_count, stream);
+    return launch_halo_pair<16>(ma, mb, mo, p, sm_count, stream);
+  }
   if (width == 32) {
     if (resident) return launch_halo_cfg<128, true, 32>(ma, mb, mo, p, sm_count, stream);
     if (bn == 256) return launch_halo_cfg<256, false, 32>(ma, mb, mo, p, sm_count, stream);
@@ -924,7 +970,7 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
 }
 
 int fp8_set_conv_algo(int algo) {
-  FP8_REQUIRE(algo >= 0 && algo <= 2, FP8_ERR_INVALID_ARGUMENT, "conv algo must be 0 (auto), 1 or 2");
+  FP8_REQUIRE(algo >= 0 && algo <= 3, FP8_ERR_INVALID_ARGUMENT, "conv algo must be 0 (auto), 1, 2 or 3");
   g_conv_algo = algo;
   return ok();
 }

@@ -179,10 +179,12 @@ def test_conv_config2_full_size(cuda):
 HALO_SHAPES = [s for s in SUPPORTED if s[3] in (16, 32)]
 
 
-@pytest.mark.parametrize("algo", [1, 2])
+@pytest.mark.parametrize("algo", [1, 2, 3])
 @pytest.mark.parametrize("cin,cout,h,w", HALO_SHAPES)
-def test_conv_fwd_and_dgrad_both_algorithms(cuda, algo, cin, cout, h, w):
-    """Tap-by-tap GEMM (algo 1) and the halo kernel (algo 2) against the oracle."""
+def test_conv_fwd_and_dgrad_every_algorithm(cuda, algo, cin, cout, h, w):
+    """Tap-by-tap GEMM (algo 1), the single-CTA halo kernel (algo 2) and the
+    CTA-pair halo kernel (algo 3, where the reduced dimension is 128 channels)
+    against the oracle."""
     from fp8_b200 import _lib, ops
 
     b = 2 if h == 32 else 4
@@ -212,3 +214,22 @@ def test_conv_halo_bias_silu_epilogue(cuda):
     y = ops.conv3x3_fwd(xq, wq, sx, sw, bias.to(cuda), 2)
     ref = oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item(), bias=bias, silu=True)
     assert oracle.max_rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("algo", [2, 3])
+def test_conv_config2_halo_variants_full_size(cuda, algo):
+    """Config 2 at full size through both halo kernels, fwd and data-grad."""
+    from fp8_b200 import _lib, ops
+
+    xq, sx = _rand_q((128, 128, 32, 32), seed=70, device=cuda)
+    dyq, sdy = _rand_q((128, 128, 32, 32), seed=71, device=cuda, scale=1e-2)
+    wq, sw = _rand_q((128, 128, 3, 3), seed=72, device=cuda, scale=0.05)
+    try:
+        _lib.set_conv_algo(algo)
+        y = ops.conv3x3_fwd(xq, wq, sx, sw)
+        dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
+    finally:
+        _lib.set_conv_algo(0)
+    assert oracle.max_rel_err(y, oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())) <= TOL
+    assert oracle.max_rel_err(dx, oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())) <= TOL
+    assert ops.device_error() == 0
