@@ -18,6 +18,7 @@
 #include "gemm_wgrad.cuh"
 #include "quantize.cuh"
 #include "conv_halo.cuh"
+#include "conv_halo_t.cuh"
 
 using namespace fp8b;
 
@@ -217,7 +218,8 @@ int launch_transpose(const void* src, void* dst, int64_t rows, int64_t cols, int
 int g_override_bm_sub = 0;
 int g_override_bn = 0;
 int g_override_group = 0;
-int g_conv_algo = 0;  // 0 auto, 1 tap-by-tap K-major GEMM, 2 halo kernel, 3 CTA-pair halo (where they apply)
+// 0 auto, 1 tap-by-tap K-major GEMM, 2 halo kernel, 3 CTA-pair halo, 4 transposed halo (where they apply)
+int g_conv_algo = 0;
 
 // ------------------------------------------------------------------ halo conv launch
 // NHWC map whose box is (128 channels, W, R+2 rows, 1 image): the rows of one
@@ -304,6 +306,27 @@ int launch_halo_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   return FP8_OK;
 }
 
+template <int W>
+int launch_halo_t(const CUtensorMap& ma, const CUtensorMap& mw, HaloTParams p, int sm_count, cudaStream_t stream) {
+  using Cfg = HaloTConfig<W>;
+  auto kern = conv_halo_t_fp8_kernel<W>;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  // Every CTA keeps one column tile's weights resident: a whole number of CTAs per column tile.
+  const int per_n = std::max(1, std::min(sm_count / p.num_n_tiles, p.full_tiles));
+  p.whole_tiles = (p.full_tiles / per_n) * per_n;
+  kern<<<per_n * p.num_n_tiles, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mw, p);
+  count_launches(1);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
+}
+
+// The transposed halo kernel: 128 reduced channels, whole 128-channel output
+// tiles, 256-pixel tiles inside one image, 4-byte aligned output rows.
+bool halo_t_applies(int height, int width, int c_red, int n_out, const void* out) {
+  return (width == 32 || width == 16) && c_red == 128 && n_out % 128 == 0 && (height * width) % 256 == 0 &&
+         aligned(out, 4);
+}
+
 // Conv fwd / data-grad with the halo kernel.  act: NHWC e4m3 input of the GEMM
 // (X for fwd, dY for data-grad) with `c_red` channels; wmat: K-major weights
 // [n_out][9*c_red]; out: NHWC bf16 [B*H*W][n_out].
@@ -311,6 +334,27 @@ int launch_conv_halo(const void* act, const void* wmat, void* out, const float* 
                      const void* bias, int epilogue, int batch, int height, int width, int c_red, int n_out,
                      bool fwd, int* err, int sm_count, cudaStream_t stream) {
   const int rows = 128 / width;
+  const int64_t M = static_cast<int64_t>(batch) * height * width;
+  if ((g_conv_algo == 0 || g_conv_algo == 4) && halo_t_applies(height, width, c_red, n_out, out)) {
+    CUtensorMap ma, mw;
+    if (int s = make_map_conv_halo(&ma, act, batch, height, width, c_red, 2 * rows)) return s;
+    if (int s = make_map_2d(&mw, wmat, n_out, 9ll * c_red, 128)) return s;
+    HaloTParams t{};
+    t.num_n_tiles = n_out / 128;
+    t.full_tiles = static_cast<int>(M / 256);
+    t.HW = height * width;
+    t.W = width;
+    t.fwd = fwd ? 1 : 0;
+    t.N = n_out;
+    t.scale_a = sa;
+    t.scale_b = sb;
+    t.bias = static_cast<const __nv_bfloat16*>(bias);
+    t.out = static_cast<__nv_bfloat16*>(out);
+    t.epilogue = epilogue;
+    t.err = err;
+    if (width == 32) return launch_halo_t<32>(ma, mw, t, sm_count, stream);
+    return launch_halo_t<16>(ma, mw, t, sm_count, stream);
+  }
   const bool resident = (c_red == 128);
   // CTA pairs (only on request: measured slower than the single-CTA kernel on
   // config 2): 128 reduced channels, whole 128-column tiles, 256-pixel tiles
@@ -320,7 +364,6 @@ int launch_conv_halo(const void* act, const void* wmat, void* out, const float* 
   CUtensorMap ma, mb, mo;
   if (int s = make_map_conv_halo(&ma, act, batch, height, width, c_red, rows)) return s;
   if (int s = make_map_2d(&mb, wmat, n_out, 9ll * c_red, pair ? 64 : bn)) return s;
-  const int64_t M = static_cast<int64_t>(batch) * height * width;
   if (int s = make_map_out_bf16(&mo, out, M, n_out)) return s;
   HaloParams p{};
   p.num_n_tiles = n_out / bn;
@@ -970,7 +1013,7 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
 }
 
 int fp8_set_conv_algo(int algo) {
-  FP8_REQUIRE(algo >= 0 && algo <= 3, FP8_ERR_INVALID_ARGUMENT, "conv algo must be 0 (auto), 1, 2 or 3");
+  FP8_REQUIRE(algo >= 0 && algo <= 4, FP8_ERR_INVALID_ARGUMENT, "conv algo must be 0 (auto), 1, 2, 3 or 4");
   g_conv_algo = algo;
   return ok();
 }

@@ -170,9 +170,11 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
 int fp8_set_tile_override(int bm_sub, int bn, int wgrad_group);
 
 /* Algorithm of fp8_conv3x3_fwd / fp8_conv3x3_dgrad: 0 = the library's choice
- * (the single-CTA halo kernel for 32x32 and 16x16 images, the tap-by-tap GEMM
- * otherwise), 1 = always tap-by-tap, 2 = single-CTA halo wherever it applies,
- * 3 = CTA-pair halo where the reduced dimension is 128 channels (else as 2).
+ * (for 32x32 and 16x16 images the transposed halo kernel when the reduced
+ * dimension is 128 channels, else the single-CTA halo kernel; the tap-by-tap
+ * GEMM for other sizes), 1 = always tap-by-tap, 2 = single-CTA halo wherever
+ * it applies, 3 = CTA-pair halo where the reduced dimension is 128 channels
+ * (else as 2), 4 = transposed halo where it applies (else as 2).
  * Process-wide; meant for benchmarks and tests. */
 int fp8_set_conv_algo(int algo);
 

@@ -179,12 +179,12 @@ def test_conv_config2_full_size(cuda):
 HALO_SHAPES = [s for s in SUPPORTED if s[3] in (16, 32)]
 
 
-@pytest.mark.parametrize("algo", [1, 2, 3])
+@pytest.mark.parametrize("algo", [1, 2, 3, 4])
 @pytest.mark.parametrize("cin,cout,h,w", HALO_SHAPES)
 def test_conv_fwd_and_dgrad_every_algorithm(cuda, algo, cin, cout, h, w):
-    """Tap-by-tap GEMM (algo 1), the single-CTA halo kernel (algo 2) and the
-    CTA-pair halo kernel (algo 3, where the reduced dimension is 128 channels)
-    against the oracle."""
+    """Tap-by-tap GEMM (algo 1), the single-CTA halo kernel (algo 2), the
+    CTA-pair halo kernel (algo 3) and the transposed halo kernel (algo 4; both
+    where the reduced dimension is 128 channels) against the oracle."""
     from fp8_b200 import _lib, ops
 
     b = 2 if h == 32 else 4
@@ -216,7 +216,7 @@ def test_conv_halo_bias_silu_epilogue(cuda):
     assert oracle.max_rel_err(y, ref) <= TOL
 
 
-@pytest.mark.parametrize("algo", [2, 3])
+@pytest.mark.parametrize("algo", [2, 3, 4])
 def test_conv_config2_halo_variants_full_size(cuda, algo):
     """Config 2 at full size through both halo kernels, fwd and data-grad."""
     from fp8_b200 import _lib, ops
@@ -230,6 +230,22 @@ def test_conv_config2_halo_variants_full_size(cuda, algo):
         dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
     finally:
         _lib.set_conv_algo(0)
+    assert oracle.max_rel_err(y, oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())) <= TOL
+    assert oracle.max_rel_err(dx, oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())) <= TOL
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("cin,cout", [(128, 128), (128, 256), (512, 128)])
+def test_conv_transposed_halo_tail_half_tiles(cuda, cin, cout):
+    """B = 40 at 32x32: 160 tiles of 256 pixels per column tile, more than one
+    round of the persistent grid, so the last tiles run as 128-pixel halves."""
+    from fp8_b200 import ops
+
+    xq, sx = _rand_q((40, cin, 32, 32), seed=81 + cout, device=cuda)
+    dyq, sdy = _rand_q((40, cout, 32, 32), seed=82 + cin, device=cuda, scale=1e-2)
+    wq, sw = _rand_q((cout, cin, 3, 3), seed=83, device=cuda, scale=0.05)
+    y = ops.conv3x3_fwd(xq, wq, sx, sw)
+    dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
     assert oracle.max_rel_err(y, oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())) <= TOL
     assert oracle.max_rel_err(dx, oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())) <= TOL
     assert ops.device_error() == 0

@@ -159,3 +159,38 @@ def test_no_device_error_recorded(cuda):
     from fp8_b200 import ops
 
     assert ops.device_error() == 0
+
+
+def test_quantize_current_large_tensor(cuda):
+    """67 MB of bf16 (the largest UNet activation): about 14 chunks per CTA in each pass."""
+    _check_current(_gen((128, 256, 32, 32), seed=21, scale=2.0).contiguous(memory_format=torch.channels_last))
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 32, 32), (3, 5, 7, 11), (1, 1, 1, 8192 + 13)])
+def test_quantize_current_grid_override(cuda, shape):
+    """Other grid sizes of the two passes, selected through the tuning override."""
+    from fp8_b200 import _lib
+
+    try:
+        _lib.set_quantize_override(1, 3)
+        _check_current(_gen(shape, seed=sum(shape), scale=3.0))
+    finally:
+        _lib.set_quantize_override(0, 0)
+
+
+def test_quantize_current_captured_in_cuda_graph(cuda):
+    """Captured in a CUDA graph and replayed on new data: same bytes as the oracle."""
+    from fp8_b200 import ops
+
+    x = _gen((16, 128, 32, 32), seed=31)
+    ops.quantize_current(x)  # warm-up outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        q, s = ops.quantize_current(x)
+    x.copy_(_gen((16, 128, 32, 32), seed=32, scale=7.0))
+    g.replay()
+    torch.cuda.synchronize()
+    q_ref, s_ref = oracle.quantize_current(x.cpu())
+    assert np.float32(s.item()).tobytes() == s_ref.tobytes()
+    assert np.array_equal(_bytes(q), q_ref)
