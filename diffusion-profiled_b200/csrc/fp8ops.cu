@@ -463,11 +463,11 @@ int check_conv_args(int batch, int height, int width, int cin, int cout, ConvTil
 }
 
 // ------------------------------------------------------------------ weight-gradient launch
-template <int G>
+template <int G, bool HALO = false>
 int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, const CUtensorMap& mp, WGradParams p,
                      cudaStream_t stream) {
-  using Cfg = WGradConfig<G>;
-  auto kern = wgrad_fp8_kernel<G>;
+  using Cfg = WGradConfig<G, HALO>;
+  auto kern = wgrad_fp8_kernel<G, HALO>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   kern<<<p.num_tiles * p.splits, kGemmThreads, Cfg::kSmemBytes, stream>>>(mdy, mb, mp, p);
   count_launches(1);
@@ -503,12 +503,18 @@ WGradPlan plan_wgrad(int64_t m_rows, int64_t n_cols, int64_t pixels, int split_k
   return w;
 }
 
-int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, int group, cudaStream_t stream) {
+// halo: mb is a halo map (make_map_conv_halo) and group == 3.
+int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, int group, cudaStream_t stream,
+                 bool halo = false) {
   CUtensorMap mp;
   if (int s = make_map_2d_store(&mp, p.acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.m_rows, p.n_cols, p.n_cols, 32,
                                 32))
     return s;
   FP8_CUDA_TRY(cudaMemsetAsync(p.acc, 0, static_cast<size_t>(p.m_rows) * p.n_cols * sizeof(float), stream));
+  if (halo) {
+    FP8_REQUIRE(group == 3, FP8_ERR_UNSUPPORTED, "halo weight-gradient needs group 3, got %d", group);
+    return launch_wgrad_cfg<3, true>(mdy, mb, mp, p, stream);
+  }
   if (group == 1) return launch_wgrad_cfg<1>(mdy, mb, mp, p, stream);
   if (group == 2) return launch_wgrad_cfg<2>(mdy, mb, mp, p, stream);
   if (group == 3) return launch_wgrad_cfg<3>(mdy, mb, mp, p, stream);
@@ -894,9 +900,15 @@ int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx
   const size_t need = static_cast<size_t>(cout) * 9 * cin * sizeof(float);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
               "wgrad workspace too small: need %zu bytes", need);
+  // Halo mode: 128-pixel K blocks of whole image rows of one image, 3-box groups.
+  const bool halo = g_conv_algo != 1 && w.group == 3 && halo_applies(height, width);
   CUtensorMap mdy, mx;
   if (int s = make_map_2d(&mdy, dyq, pixels, cout, 128)) return s;
-  if (int s = make_map_conv(&mx, xq, batch, height, width, cin, t)) return s;
+  if (halo) {
+    if (int s = make_map_conv_halo(&mx, xq, batch, height, width, cin, 128 / width)) return s;
+  } else {
+    if (int s = make_map_conv(&mx, xq, batch, height, width, cin, t)) return s;
+  }
   WGradParams p{};
   p.num_tiles = w.num_tiles;
   p.num_groups = w.num_groups;
@@ -906,12 +918,13 @@ int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx
   p.HW = height * width;
   p.W = width;
   p.cchunks = cin / 128;
+  p.halo_box_bytes = (128 / width + 2) * width * 128;
   p.n_cols = 9 * cin;
   p.m_rows = cout;
   p.acc = static_cast<float*>(workspace);
   p.err = st->err_ptr;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  if (int s = launch_wgrad(mdy, mx, p, w.group, cs)) return s;
+  if (int s = launch_wgrad(mdy, mx, p, w.group, cs, halo)) return s;
   if (int s = launch_wgrad_reduce(p.acc, 1, static_cast<int64_t>(cout) * 9 * cin, sx, sdy, dw, st->sm_count, cs))
     return s;
   return ok();

@@ -15,6 +15,16 @@
 // i.e. MN-major for this contraction, so the transpose of dY that the reference
 // performs before its dW kernel (fp8_kernels.py:754-771) is not needed.
 //
+// Halo mode (3x3 conv with W in {16, 32}, G = 3): a column group is one column
+// tap kw and one 128-channel chunk, and its three boxes are the row taps
+// kh = 0, 1, 2.  X is MN-major here (pixels are K), so one 4-D TMA box of R+2
+// image rows (R = 128 / W rows per 128-pixel K block, one halo row above and
+// below) holds all three: row tap kh starts kh*W rows into the box, a whole
+// number of 1024-byte swizzle atoms.  kh = 0 and 1 are one N = 256 MMA whose
+// two 128-column blocks are W*128 bytes apart (the descriptor's leading byte
+// offset), kh = 2 an N = 128 MMA.  Per K block the CTA loads 16 KB of dY and
+// (R+2)*W*128 bytes of X instead of 16 KB + 3 x 16 KB.
+//
 // Each CTA owns one output tile (128 rows of co x G*128 columns of j) and one
 // K split; it is not persistent.  Roles as in the K-major kernel: warp 0 TMA,
 // warp 1 TMEM + MMA, warps 2..5 move the fp32 tile out.  Split results are
@@ -37,27 +47,31 @@ struct WGradParams {
   int k_blocks;        // ceil(pixels / 128)
   int b_conv;          // 1: B is a 3x3 conv window over NHWC X, 0: plain [M][K]
   int HW, W, cchunks;  // conv geometry
+  int halo_box_bytes;  // halo mode: bytes of one X box ((128 / W + 2) * W * 128)
   int n_cols;          // columns of the partial / dW rows (9*Cin or K)
   int m_rows;          // rows of dW (Cout or N)
   float* acc;          // [m_rows][n_cols] fp32, zeroed before the launch
   int* err;
 };
 
-template <int G>
+constexpr int kMaxHaloBoxBytes = (128 / 32 + 2) * 32 * 128;  // W = 32 (W = 16 needs 20 KB)
+
+template <int G, bool HALO = false>
 struct WGradConfig {
-  static constexpr int kStageBytes = (1 + G) * kBoxBytes;
-  static constexpr int kStages = (G == 1) ? 6 : (G == 2 ? 4 : 3);
+  static_assert(!HALO || G == 3, "halo mode groups the three row taps");
+  static constexpr int kStageBytes = HALO ? kBoxBytes + kMaxHaloBoxBytes : (1 + G) * kBoxBytes;
+  static constexpr int kStages = HALO ? 4 : ((G == 1) ? 6 : (G == 2 ? 4 : 3));
   static constexpr int kAccCols = G * 128;
   static constexpr int kTmemCols = (kAccCols <= 128) ? 128 : (kAccCols <= 256 ? 256 : 512);
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiSmemBytes + 1024 + 1024;
   static_assert(kSmemBytes <= 232448, "smem");
 };
 
-template <int G>
+template <int G, bool HALO = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     wgrad_fp8_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_acc, const WGradParams p) {
-  using Cfg = WGradConfig<G>;
+  using Cfg = WGradConfig<G, HALO>;
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -116,10 +130,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         uint8_t* sa = smem + stage * Cfg::kStageBytes;
-        mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+        mbar_arrive_expect_tx(&full_bar[stage], HALO ? kBoxBytes + p.halo_box_bytes : Cfg::kStageBytes);
         const int m0 = kb * 128;
         tma_load_2d(sa, &tmap_dy, &full_bar[stage], co_tile * 128, m0);
-        if (p.b_conv) {
+        if (HALO) {
+          const int img = m0 / p.HW;
+          const int h0 = (m0 - img * p.HW) / p.W;
+          const int kw = group % 3, chunk = group / 3;
+          tma_load_4d(sa + kBoxBytes, &tmap_b, &full_bar[stage], chunk * 128, kw - 1, h0 - 1, img);
+        } else if (p.b_conv) {
           const int img = m0 / p.HW;
           const int h0 = (m0 - img * p.HW) / p.W;
 #pragma unroll
@@ -170,13 +189,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // of the operand 16 KB apart (LBO).
           const uint64_t adesc = make_smem_desc(sa + k * 4096, kBoxBytes, 1024);
           const uint32_t acc = (accumulate_base | (k != 0 ? 1u : 0u));
+          if (HALO) {
+            // row taps 0 and 1: two 128-column blocks W*128 bytes apart; row tap 2 alone
+            const uint32_t sb = sa + kBoxBytes + k * 4096;
+            const uint32_t row = static_cast<uint32_t>(p.W) * 128u;
+            umma_f8(tmem_base, adesc, make_smem_desc(sb, row, 1024), idesc_pair, acc);
+            umma_f8(tmem_base + 256, adesc, make_smem_desc(sb + 2 * row, kBoxBytes, 1024), idesc_single, acc);
+          } else {
 #pragma unroll
-          for (int b = 0; b + 1 < G + 1; b += 2) {
-            const uint64_t bdesc = make_smem_desc(sa + (1 + b) * kBoxBytes + k * 4096, kBoxBytes, 1024);
-            if (b + 1 < G)
-              umma_f8(tmem_base + b * 128, adesc, bdesc, idesc_pair, acc);
-            else
-              umma_f8(tmem_base + b * 128, adesc, bdesc, idesc_single, acc);
+            for (int b = 0; b + 1 < G + 1; b += 2) {
+              const uint64_t bdesc = make_smem_desc(sa + (1 + b) * kBoxBytes + k * 4096, kBoxBytes, 1024);
+              if (b + 1 < G)
+                umma_f8(tmem_base + b * 128, adesc, bdesc, idesc_pair, acc);
+              else
+                umma_f8(tmem_base + b * 128, adesc, bdesc, idesc_single, acc);
+            }
           }
         }
         umma_commit(&empty_bar[stage]);
@@ -214,7 +241,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_reduce_add_2d(&tmap_acc, sbuf, group * G * 128 + c, row0);
+          // Halo mode: TMEM block b is row tap kh = b of column tap kw, chunk.
+          const int col = HALO ? ((c >> 7) * 3 + group % 3) * p.cchunks * 128 + (group / 3) * 128 + (c & 127)
+                               : group * G * 128 + c;
+          tma_reduce_add_2d(&tmap_acc, sbuf, col, row0);
           bulk_commit_group();
         }
         buf ^= 1;

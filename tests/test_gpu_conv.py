@@ -249,3 +249,23 @@ def test_conv_transposed_halo_tail_half_tiles(cuda, cin, cout):
     assert oracle.max_rel_err(y, oracle.conv_fwd(xq.cpu(), wq.cpu(), sx.item(), sw.item())) <= TOL
     assert oracle.max_rel_err(dx, oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())) <= TOL
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("algo", [1, 0])
+@pytest.mark.parametrize("cin,cout,h,w", HALO_SHAPES)
+def test_conv_wgrad_tap_and_halo_paths(cuda, algo, cin, cout, h, w):
+    """Weight gradient with per-tap X windows (algo 1) and with one halo box per
+    column tap (the default for 32x32 and 16x16 images) against the oracle."""
+    from fp8_b200 import _lib, ops
+
+    b = 2 if h == 32 else 4
+    xq, sx = _rand_q((b, cin, h, w), seed=7 * cin + cout + h, device=cuda)
+    dyq, sdy = _rand_q((b, cout, h, w), seed=9 * cin + cout + w, device=cuda, scale=1e-2)
+    ref = oracle.conv_dw(xq.cpu(), dyq.cpu(), sx.item(), sdy.item())
+    try:
+        _lib.set_conv_algo(algo)
+        dw = ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+    finally:
+        _lib.set_conv_algo(0)
+    assert oracle.max_rel_err(dw, ref) <= TOL
+    assert ops.device_error() == 0
