@@ -19,6 +19,7 @@
 #include "quantize.cuh"
 #include "conv_halo.cuh"
 #include "conv_halo_t.cuh"
+#include "groupnorm.cuh"
 
 using namespace fp8b;
 
@@ -534,6 +535,33 @@ int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const 
   return FP8_OK;
 }
 
+// ------------------------------------------------------------------ group norm helpers
+// CTAs per sample: about three per SM over the batch, each with at least one
+// row step of pixels.
+int gn_slices(int n, int hw, int c, int sm_count) {
+  const int rows = kGnThreads / (c / 8);
+  int s = (3 * sm_count + n - 1) / std::max(n, 1);
+  s = std::min(s, std::max(1, hw / rows));
+  return std::max(s, 1);
+}
+
+size_t gn_workspace(int n, int hw, int c, int sm_count) {
+  return static_cast<size_t>(n) * gn_slices(n, hw, c, sm_count) * 3 * c * sizeof(float);
+}
+
+int check_gn_args(const void* x, const void* out, const float* gamma, const float* beta, int n, int hw, int c,
+                  int groups, int film_ld, const void* film, float p, float eps) {
+  FP8_REQUIRE(n > 0 && hw > 0 && c > 0 && groups > 0, FP8_ERR_INVALID_ARGUMENT, "bad group-norm sizes");
+  FP8_REQUIRE(c % 8 == 0 && c <= 512 && c % groups == 0, FP8_ERR_UNSUPPORTED,
+              "group norm needs c %% 8 == 0, c <= 512, c %% groups == 0 (c=%d, groups=%d)", c, groups);
+  FP8_REQUIRE(x && out && gamma && beta, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(x, 16) && aligned(out, 16), FP8_ERR_INVALID_ARGUMENT, "activations must be 16-byte aligned");
+  FP8_REQUIRE(film == nullptr || film_ld >= 2 * c, FP8_ERR_INVALID_ARGUMENT, "film_ld must be >= 2c");
+  FP8_REQUIRE(p >= 0.0f && p < 1.0f, FP8_ERR_INVALID_ARGUMENT, "dropout p must be in [0, 1)");
+  FP8_REQUIRE(eps > 0.0f, FP8_ERR_INVALID_ARGUMENT, "eps must be > 0");
+  return FP8_OK;
+}
+
 // ------------------------------------------------------------------ quantize launch helpers
 // 16-byte aligned x with 8-byte aligned q takes the streaming kernels
 // (quant_stream_kernel); anything else takes the grid-stride scalar kernels.
@@ -597,7 +625,7 @@ size_t quant_workspace_bytes(int sm_count) {
 // ======================================================================== C ABI
 extern "C" {
 
-int fp8_abi_version(void) { return 2; }
+int fp8_abi_version(void) { return 3; }
 
 int fp8_last_error(char* buf, size_t len) {
   if (buf != nullptr && len > 0) {
@@ -1038,6 +1066,77 @@ int fp8_set_tile_override(int bm_sub, int bn, int wgrad_group) {
   g_override_bm_sub = bm_sub;
   g_override_bn = bn;
   g_override_group = wgrad_group;
+  return ok();
+}
+
+}  // extern "C"
+
+// ======================================================================== group norm + activation
+extern "C" {
+
+size_t fp8_gn_workspace_bytes(int n, int hw, int c) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  (void)cudaGetLastError();
+  if (n <= 0 || hw <= 0 || c < 8) return 0;
+  return gn_workspace(n, hw, c, sms > 0 ? sms : 148);
+}
+
+int fp8_gn_act_fwd(const void* x, const float* gamma, const float* beta, const void* film, int film_ld,
+                   const int64_t* seed, float p, float eps, float* stats, void* out, int n, int hw, int c,
+                   int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+  if (int s = check_gn_args(x, out, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
+  FP8_REQUIRE(stats != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  const size_t need = gn_workspace(n, hw, c, st->sm_count);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
+              "group-norm workspace too small: need %zu bytes", need);
+  GnShape sh{n, hw, c, groups, gn_slices(n, hw, c, st->sm_count)};
+  GnActParams q{gamma, beta, static_cast<const uint16_t*>(film), film_ld, seed, p, eps};
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s1)));
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s2)));
+  gn_stats_kernel<<<n * sh.slices, kGnThreads, s1, cs>>>(static_cast<const uint16_t*>(x), sh, part);
+  gn_act_fwd_kernel<<<n * sh.slices, kGnThreads, s2, cs>>>(static_cast<const uint16_t*>(x), sh, part, q, stats,
+                                                            static_cast<uint16_t*>(out));
+  count_launches(2);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int fp8_gn_act_bwd(const void* x, const void* dy, const float* gamma, const float* beta, const void* film,
+                   int film_ld, const int64_t* seed, float p, float eps, const float* stats, float* totals,
+                   void* dx, int n, int hw, int c, int groups, void* workspace, size_t workspace_bytes,
+                   fp8_stream_t stream) {
+  if (int s = check_gn_args(x, dx, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
+  FP8_REQUIRE(dy != nullptr && aligned(dy, 16), FP8_ERR_INVALID_ARGUMENT, "dy must be 16-byte aligned");
+  FP8_REQUIRE(stats != nullptr && totals != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats / totals");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  const size_t need = gn_workspace(n, hw, c, st->sm_count);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
+              "group-norm workspace too small: need %zu bytes", need);
+  GnShape sh{n, hw, c, groups, gn_slices(n, hw, c, st->sm_count)};
+  GnActParams q{gamma, beta, static_cast<const uint16_t*>(film), film_ld, seed, p, eps};
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  const size_t s1 = gn_bwd_reduce_smem(c, groups), s2 = gn_bwd_apply_smem(c, groups);
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_reduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s1)));
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s2)));
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  const uint16_t* ds = static_cast<const uint16_t*>(dy);
+  gn_act_bwd_reduce_kernel<<<n * sh.slices, kGnThreads, s1, cs>>>(xs, ds, sh, stats, q, part);
+  gn_act_bwd_apply_kernel<<<n * sh.slices, kGnThreads, s2, cs>>>(xs, ds, sh, stats, q, part, totals,
+                                                                  static_cast<uint16_t*>(dx));
+  count_launches(2);
+  FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }
 

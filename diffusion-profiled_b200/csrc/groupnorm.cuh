@@ -1,0 +1,485 @@
+// groupnorm.cuh — GroupNorm + optional FiLM + SiLU + optional dropout, forward and
+// backward, on NHWC bf16 activations (the UNet's norm -> activation chains that
+// feed its 3x3 convs, reference unet.py:151 and :157-159).
+//
+// Forward, per sample n, channel c (group g = c / Cg, m = HW * Cg elements per group):
+//   z = (x - mean_g) * rstd_g * gamma_c + beta_c          (nn.GroupNorm, eps inside rstd)
+//   f = (s_nc + 1) * z + t_nc                             (FiLM, optional: s, t from the time embedding)
+//   a = silu(f) * keep / (1 - p)                          (dropout, optional)
+// which is one affine map per (n, c): f = A_nc * x + B_nc.
+//
+// Kernels (grid = samples x slices; a CTA owns a contiguous pixel range of one
+// sample; thread (v, r) handles channel vector v (8 channels, 16 bytes) of
+// pixels r, r + R, ...; C <= 512):
+//   gn_stats_kernel     : per-channel sums of (x - x[n, 0, c]) and its square per slice
+//   gn_act_fwd_kernel   : merges the slices' sums into per-group mean / rstd (Chan's
+//                         pairwise update, so channels with different shifts combine
+//                         without cancellation), writes them (slice 0) and applies the map
+//   gn_act_bwd_reduce_kernel : recomputes f from x and the saved statistics; per-channel
+//                         sums of df, df * z and df * xhat per slice (df = dL/df)
+//   gn_act_bwd_apply_kernel  : dx = rstd * (gamma (s+1) df - mean_g[gamma (s+1) df]
+//                              - xhat * mean_g[gamma (s+1) df xhat]),
+//                         and the per-(n, c) totals the host turns into the parameter,
+//                         scale and shift gradients.
+// Dropout keeps element e when a 16-bit slice of splitmix64(seed, e / 4) is >= p * 65536
+// (splitmix64: Steele, Lea and Flood, "Fast splittable pseudorandom number
+// generators", OOPSLA 2014); the seed is read from device memory so a captured
+// graph draws a new mask each replay when the caller advances it.
+#pragma once
+
+#include "sm100_common.cuh"
+
+namespace fp8b {
+
+constexpr int kGnThreads = 512;
+
+struct GnShape {
+  int n, hw, c, groups;
+  int slices;  // CTAs per sample
+};
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Keep mask bits for the 8 elements starting at linear NHWC index e0 (e0 % 8 == 0).
+__device__ __forceinline__ uint32_t dropout_keep8(uint64_t seed, int64_t e0, uint32_t thresh16) {
+  uint32_t keep = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint64_t r = splitmix64(seed ^ (static_cast<uint64_t>(e0 / 4 + h) * 0xD1B54A32D192ED03ull));
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (static_cast<uint32_t>((r >> (16 * k)) & 0xFFFFu) >= thresh16) keep |= 1u << (h * 4 + k);
+  }
+  return keep;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = bf16_lo_f(w[i]);
+    f[2 * i + 1] = bf16_hi_f(w[i]);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+
+// Thread layout shared by all four kernels.
+struct GnThread {
+  int vecs;   // C / 8 channel vectors per pixel
+  int rows;   // pixel rows per CTA step (kGnThreads / vecs)
+  int v, r;   // this thread's channel vector and row (r >= rows: idle in the streaming loops)
+  int p0, p1; // pixel range of this CTA
+  int n;      // sample
+};
+
+__device__ __forceinline__ GnThread gn_thread(const GnShape& s) {
+  GnThread t;
+  t.vecs = s.c / 8;
+  t.rows = kGnThreads / t.vecs;
+  t.v = threadIdx.x % t.vecs;
+  t.r = threadIdx.x / t.vecs;
+  t.n = blockIdx.x / s.slices;
+  const int slice = blockIdx.x % s.slices;
+  const int per = (s.hw + s.slices - 1) / s.slices;
+  t.p0 = min(s.hw, slice * per);
+  t.p1 = min(s.hw, t.p0 + per);
+  return t;
+}
+
+// Sum `vals[j]` (j < NV) of every thread with the same channel vector into
+// red[j * C + c], in a fixed order (deterministic).  buf: smem float[rows][NV][C];
+// red: smem float[NV][C].  Ends with a __syncthreads.
+template <int NV>
+__device__ __forceinline__ void gn_reduce_rows(const GnThread& t, const GnShape& s, const float (*vals)[8],
+                                               float* buf, float* red) {
+  if (t.r < t.rows) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) buf[(t.r * NV + j) * s.c + t.v * 8 + k] = vals[j][k];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NV * s.c; i += blockDim.x) {
+    float v = 0.0f;
+    for (int r = 0; r < t.rows; ++r) v += buf[r * NV * s.c + i];
+    red[i] = v;
+  }
+  __syncthreads();
+}
+
+// Dynamic shared memory (bytes) of each kernel for C channels and G groups.
+__host__ __device__ constexpr size_t gn_reduce_smem(int c, int nv) {
+  return static_cast<size_t>(kGnThreads / (c / 8)) * nv * c * 4 + static_cast<size_t>(nv) * c * 4;
+}
+__host__ __device__ constexpr size_t gn_stats_smem(int c) { return gn_reduce_smem(c, 2); }
+__host__ __device__ constexpr size_t gn_fwd_smem(int c, int g) { return (2 * static_cast<size_t>(g) + 4 * c) * 4; }
+__host__ __device__ constexpr size_t gn_bwd_reduce_smem(int c, int g) {
+  return (4 * static_cast<size_t>(c) + 2 * g) * 4 + gn_reduce_smem(c, 3);
+}
+__host__ __device__ constexpr size_t gn_bwd_apply_smem(int c, int g) {
+  return (8 * static_cast<size_t>(c) + 4 * g) * 4;
+}
+
+// ------------------------------------------------------------------ statistics
+// part[(n * slices + slice) * 2C + {0, C} + c] = sum (x - shift_c), sum (x - shift_c)^2
+__global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const uint16_t* __restrict__ x, GnShape s,
+                                                              float* __restrict__ part) {
+  extern __shared__ float gn_smem[];
+  const GnThread t = gn_thread(s);
+  float acc[2][8] = {};
+  if (t.r < t.rows) {
+    const uint4* xs = reinterpret_cast<const uint4*>(x) + static_cast<int64_t>(t.n) * s.hw * t.vecs;
+    float sh[8];
+    unpack8(__ldg(xs + t.v), sh);
+    // Four pixel rows per step: their loads are in flight together.
+    for (int p = t.p0 + t.r; p < t.p1; p += 4 * t.rows) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int pu = p + u * t.rows;
+        v[u] = pu < t.p1 ? __ldg(xs + static_cast<int64_t>(pu) * t.vecs + t.v) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (p + u * t.rows >= t.p1) break;
+        float f[8];
+        unpack8(v[u], f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float d = f[k] - sh[k];
+          acc[0][k] += d;
+          acc[1][k] = fmaf(d, d, acc[1][k]);
+        }
+      }
+    }
+  }
+  float* red = gn_smem + static_cast<size_t>(t.rows) * 2 * s.c;
+  gn_reduce_rows<2>(t, s, acc, gn_smem, red);
+  float* out = part + static_cast<int64_t>(blockIdx.x) * 2 * s.c;
+  for (int i = threadIdx.x; i < 2 * s.c; i += blockDim.x) out[i] = red[i];
+}
+
+// Per-group mean / rstd of sample n from the slices' partial sums (all threads call;
+// result in smem mean_g[G], rstd_g[G]).  shift_c = x[n, 0, c].
+__device__ __forceinline__ void gn_group_stats(const uint16_t* __restrict__ x, const float* __restrict__ part,
+                                               const GnShape& s, int n, float eps, float* mean_g, float* rstd_g,
+                                               float* ch_mean, float* ch_m2) {
+  const float cnt = static_cast<float>(s.hw);
+  for (int c = threadIdx.x; c < s.c; c += blockDim.x) {
+    float s1 = 0.0f, s2 = 0.0f;
+    for (int k = 0; k < s.slices; ++k) {
+      const float* pp = part + (static_cast<int64_t>(n) * s.slices + k) * 2 * s.c;
+      s1 += pp[c];
+      s2 += pp[s.c + c];
+    }
+    const float shift = __uint_as_float(static_cast<uint32_t>(x[static_cast<int64_t>(n) * s.hw * s.c + c]) << 16);
+    ch_mean[c] = shift + s1 / cnt;
+    ch_m2[c] = fmaxf(s2 - s1 * s1 / cnt, 0.0f);
+  }
+  __syncthreads();
+  const int cg = s.c / s.groups;
+  for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
+    float mean = 0.0f;
+    for (int j = 0; j < cg; ++j) mean += ch_mean[g * cg + j];
+    mean /= static_cast<float>(cg);
+    float m2 = 0.0f;
+    for (int j = 0; j < cg; ++j) {
+      const float d = ch_mean[g * cg + j] - mean;
+      m2 += ch_m2[g * cg + j] + cnt * d * d;
+    }
+    mean_g[g] = mean;
+    rstd_g[g] = rsqrtf(m2 / (cnt * static_cast<float>(cg)) + eps);
+  }
+  __syncthreads();
+}
+
+struct GnActParams {
+  const float* gamma;   // [C]
+  const float* beta;    // [C]
+  const uint16_t* film; // bf16 [N][film_ld]: scale at +0, shift at +C (nullptr: no FiLM)
+  int film_ld;
+  const int64_t* seed;  // device seed (nullptr: no dropout)
+  float p;              // dropout probability
+  float eps;
+};
+
+// Per-(n, c) affine map f = A x + B into smem A[C], B[C] (also z = a x + b for backward).
+__device__ __forceinline__ void gn_coeffs(const GnShape& s, const GnActParams& q, int n, const float* mean_g,
+                                          const float* rstd_g, float* A, float* B, float* a_z, float* b_z) {
+  const int cg = s.c / s.groups;
+  for (int c = threadIdx.x; c < s.c; c += blockDim.x) {
+    const int g = c / cg;
+    const float a = q.gamma[c] * rstd_g[g];
+    const float b = q.beta[c] - mean_g[g] * a;
+    float sc = 1.0f, sh = 0.0f;
+    if (q.film != nullptr) {
+      const uint16_t* fr = q.film + static_cast<int64_t>(n) * q.film_ld;
+      sc += __uint_as_float(static_cast<uint32_t>(fr[c]) << 16);
+      sh = __uint_as_float(static_cast<uint32_t>(fr[s.c + c]) << 16);
+    }
+    A[c] = sc * a;
+    B[c] = fmaf(sc, b, sh);
+    if (a_z != nullptr) {
+      a_z[c] = a;
+      b_z[c] = b;
+    }
+  }
+  __syncthreads();
+}
+
+// stats[n * 2G + {0, G} + g] = mean, rstd (written by slice 0 of each sample).
+__global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const uint16_t* __restrict__ x, GnShape s,
+                                                                const float* __restrict__ part, GnActParams q,
+                                                                float* __restrict__ stats,
+                                                                uint16_t* __restrict__ out) {
+  extern __shared__ float gn_smem[];
+  float* mean_g = gn_smem;
+  float* rstd_g = mean_g + s.groups;
+  float* A = rstd_g + s.groups;
+  float* B = A + s.c;
+  float* ch_mean = B + s.c;
+  float* ch_m2 = ch_mean + s.c;
+  const GnThread t = gn_thread(s);
+  gn_group_stats(x, part, s, t.n, q.eps, mean_g, rstd_g, ch_mean, ch_m2);
+  if (blockIdx.x % s.slices == 0)
+    for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
+      stats[static_cast<int64_t>(t.n) * 2 * s.groups + g] = mean_g[g];
+      stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g] = rstd_g[g];
+    }
+  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, nullptr, nullptr);
+  if (t.r >= t.rows) return;
+  float a[8], b[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    a[k] = A[t.v * 8 + k];
+    b[k] = B[t.v * 8 + k];
+  }
+  const bool drop = q.seed != nullptr && q.p > 0.0f;
+  const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
+  const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
+  const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
+  const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
+  const uint4* xs = reinterpret_cast<const uint4*>(x) + base;
+  uint4* os = reinterpret_cast<uint4*>(out) + base;
+  for (int p = t.p0 + t.r; p < t.p1; p += 4 * t.rows) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int pu = p + u * t.rows;
+      v[u] = pu < t.p1 ? __ldg(xs + static_cast<int64_t>(pu) * t.vecs + t.v) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int pu = p + u * t.rows;
+      if (pu >= t.p1) break;
+      const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
+      float f[8];
+      unpack8(v[u], f);
+      const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float z = fmaf(a[k], f[k], b[k]);
+        const float act = silu_f32(z) * keep_scale;
+        f[k] = (keep >> k) & 1u ? act : 0.0f;
+      }
+      os[vi] = pack8(f);
+    }
+  }
+}
+
+// Recompute, per element of one 8-channel vector: z, f, and df = dL/df.
+struct GnBwdElem {
+  float z, df, xhat;
+};
+
+// part[(n * slices + slice) * 3C + {0, C, 2C} + c] = sum df, sum df * z, sum df * xhat
+__global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
+    GnActParams q, float* __restrict__ part) {
+  extern __shared__ float gn_smem[];
+  float* A = gn_smem;
+  float* B = A + s.c;
+  float* az = B + s.c;
+  float* bz = az + s.c;
+  float* mean_g = bz + s.c;
+  float* rstd_g = mean_g + s.groups;
+  float* buf = rstd_g + s.groups;
+  const GnThread t = gn_thread(s);
+  float* red = buf + static_cast<size_t>(t.rows) * 3 * s.c;
+  for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
+    mean_g[g] = stats[static_cast<int64_t>(t.n) * 2 * s.groups + g];
+    rstd_g[g] = stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g];
+  }
+  __syncthreads();
+  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, az, bz);
+  float acc[3][8] = {};
+  if (t.r < t.rows) {
+    const int cg = s.c / s.groups;
+    float a[8], b[8], za[8], zb[8], mu[8], rs[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = t.v * 8 + k;
+      a[k] = A[c];
+      b[k] = B[c];
+      za[k] = az[c];
+      zb[k] = bz[c];
+      mu[k] = mean_g[c / cg];
+      rs[k] = rstd_g[c / cg];
+    }
+    const bool drop = q.seed != nullptr && q.p > 0.0f;
+    const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
+    const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
+    const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
+    const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
+    const uint4* xs = reinterpret_cast<const uint4*>(x) + base;
+    const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
+    for (int p = t.p0 + t.r; p < t.p1; p += 2 * t.rows) {
+      uint4 vx[2], vd[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int pu = p + u * t.rows;
+        const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
+        vx[u] = pu < t.p1 ? __ldg(xs + vi) : make_uint4(0u, 0u, 0u, 0u);
+        vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int pu = p + u * t.rows;
+        if (pu >= t.p1) break;
+        const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
+        float xf[8], gf[8];
+        unpack8(vx[u], xf);
+        unpack8(vd[u], gf);
+        const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float f = fmaf(a[k], xf[k], b[k]);
+          const float sg = 1.0f / (1.0f + __expf(-f));
+          const float du = (keep >> k) & 1u ? gf[k] * keep_scale : 0.0f;
+          const float df = du * sg * fmaf(f, 1.0f - sg, 1.0f);
+          acc[0][k] += df;
+          acc[1][k] = fmaf(df, fmaf(za[k], xf[k], zb[k]), acc[1][k]);
+          acc[2][k] = fmaf(df, (xf[k] - mu[k]) * rs[k], acc[2][k]);
+        }
+      }
+    }
+  }
+  gn_reduce_rows<3>(t, s, acc, buf, red);
+  float* out = part + static_cast<int64_t>(blockIdx.x) * 3 * s.c;
+  for (int i = threadIdx.x; i < 3 * s.c; i += blockDim.x) out[i] = red[i];
+}
+
+// totals[n * 3C + {0, C, 2C} + c] = sum df, sum df z, sum df xhat over the sample
+// (written by slice 0); dx as above.
+__global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
+    GnActParams q, const float* __restrict__ part, float* __restrict__ totals, uint16_t* __restrict__ dx) {
+  extern __shared__ float gn_smem[];
+  float* A = gn_smem;
+  float* B = A + s.c;
+  float* az = B + s.c;
+  float* bz = az + s.c;
+  float* mean_g = bz + s.c;
+  float* rstd_g = mean_g + s.groups;
+  float* tot = rstd_g + s.groups;  // [3][C]
+  float* g1 = tot + 3 * s.c;       // [G] mean over the group of gamma (s+1) df
+  float* g2 = g1 + s.groups;       // [G] mean over the group of gamma (s+1) df xhat
+  float* gs = g2 + s.groups;       // [C] gamma_c (s_nc + 1)
+  const GnThread t = gn_thread(s);
+  for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
+    mean_g[g] = stats[static_cast<int64_t>(t.n) * 2 * s.groups + g];
+    rstd_g[g] = stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g];
+  }
+  __syncthreads();
+  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, az, bz);
+  const bool first = blockIdx.x % s.slices == 0;
+  for (int i = threadIdx.x; i < 3 * s.c; i += blockDim.x) {
+    float v = 0.0f;
+    for (int k = 0; k < s.slices; ++k) v += part[(static_cast<int64_t>(t.n) * s.slices + k) * 3 * s.c + i];
+    tot[i] = v;
+    if (first) totals[static_cast<int64_t>(t.n) * 3 * s.c + i] = v;
+  }
+  for (int c = threadIdx.x; c < s.c; c += blockDim.x) {
+    float sc = 1.0f;
+    if (q.film != nullptr)
+      sc += __uint_as_float(static_cast<uint32_t>(q.film[static_cast<int64_t>(t.n) * q.film_ld + c]) << 16);
+    gs[c] = q.gamma[c] * sc;
+  }
+  __syncthreads();
+  const int cg = s.c / s.groups;
+  const float inv_m = 1.0f / (static_cast<float>(s.hw) * static_cast<float>(cg));
+  for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
+    float s1 = 0.0f, s3 = 0.0f;
+    for (int j = 0; j < cg; ++j) {
+      const int c = g * cg + j;
+      s1 = fmaf(gs[c], tot[c], s1);
+      s3 = fmaf(gs[c], tot[2 * s.c + c], s3);
+    }
+    g1[g] = s1 * inv_m;
+    g2[g] = s3 * inv_m;
+  }
+  __syncthreads();
+  if (t.r >= t.rows) return;
+  float a[8], b[8], mu[8], rs[8], gk[8], m1[8], m2[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int c = t.v * 8 + k;
+    const int g = c / cg;
+    a[k] = A[c];
+    b[k] = B[c];
+    mu[k] = mean_g[g];
+    rs[k] = rstd_g[g];
+    gk[k] = gs[c];
+    m1[k] = g1[g];
+    m2[k] = g2[g];
+  }
+  const bool drop = q.seed != nullptr && q.p > 0.0f;
+  const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
+  const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
+  const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
+  const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
+  const uint4* xs = reinterpret_cast<const uint4*>(x) + base;
+  const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
+  uint4* os = reinterpret_cast<uint4*>(dx) + base;
+  for (int p = t.p0 + t.r; p < t.p1; p += 2 * t.rows) {
+    uint4 vx[2], vd[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int pu = p + u * t.rows;
+      const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
+      vx[u] = pu < t.p1 ? __ldg(xs + vi) : make_uint4(0u, 0u, 0u, 0u);
+      vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int pu = p + u * t.rows;
+      if (pu >= t.p1) break;
+      const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
+      float xf[8], gf[8], o[8];
+      unpack8(vx[u], xf);
+      unpack8(vd[u], gf);
+      const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float f = fmaf(a[k], xf[k], b[k]);
+        const float sg = 1.0f / (1.0f + __expf(-f));
+        const float du = (keep >> k) & 1u ? gf[k] * keep_scale : 0.0f;
+        const float df = du * sg * fmaf(f, 1.0f - sg, 1.0f);
+        const float xhat = (xf[k] - mu[k]) * rs[k];
+        o[k] = rs[k] * (gk[k] * df - m1[k] - xhat * m2[k]);
+      }
+      os[vi] = pack8(o);
+    }
+  }
+}
+
+}  // namespace fp8b

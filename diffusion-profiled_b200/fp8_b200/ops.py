@@ -349,3 +349,71 @@ __all__ = [
     "gemm_wgrad",
     "device_error",
 ]
+
+
+# ----------------------------------------------------------------------------- group norm + activation
+def _gn_check(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
+              groups: int) -> tuple[int, int, int]:
+    if x.dtype != torch.bfloat16 or x.dim() != 4 or not x.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError("group norm expects a channels_last bfloat16 [N, C, H, W] tensor")
+    n, c, h, w = x.shape
+    if gamma.dtype != torch.float32 or beta.dtype != torch.float32 or gamma.numel() != c or beta.numel() != c:
+        raise RuntimeError("gamma / beta must be float32 [C]")
+    if film is not None and (film.dtype != torch.bfloat16 or film.shape[0] != n or film.numel() != n * 2 * c
+                             or not film.is_contiguous()):
+        raise RuntimeError("film must be a contiguous bfloat16 [N, 2C] (scale, shift) tensor")
+    return n, c, h * w
+
+
+@torch.library.custom_op("fp8_b200::gn_act_fwd", mutates_args=())
+def gn_act_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
+               seed: torch.Tensor | None, p: float, eps: float, groups: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """a = dropout(silu((film_scale + 1) * GroupNorm(x) + film_shift)) -> (a bf16 channels_last, stats [N, 2, G]).
+
+    No reference kernel: replaces the torch chain of the reference ResBlock
+    (unet.py:151, :157-159).  `seed` (int64 device scalar) selects the dropout mask."""
+    dev = _require_cuda(x, gamma, beta)
+    n, c, hw = _gn_check(x, gamma, beta, film, groups)
+    out = torch.empty_like(x, memory_format=torch.channels_last)
+    stats = torch.empty((n, 2, groups), device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_gn_workspace_bytes(n, hw, c) // 4, 4), device=dev, dtype=torch.float32)
+        _lib.check(lib.fp8_gn_act_fwd(
+            _ptr(x), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps), _ptr(stats),
+            _ptr(out), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)), "fp8_gn_act_fwd")
+    return out, stats
+
+
+@gn_act_fwd.register_fake
+def _(x, gamma, beta, film, seed, p, eps, groups):
+    return (torch.empty_like(x, memory_format=torch.channels_last),
+            x.new_empty((x.shape[0], 2, groups), dtype=torch.float32))
+
+
+@torch.library.custom_op("fp8_b200::gn_act_bwd", mutates_args=())
+def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+               film: torch.Tensor | None, seed: torch.Tensor | None, stats: torch.Tensor, p: float, eps: float,
+               groups: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Backward of gn_act_fwd -> (dx bf16 channels_last, totals [N, 3, C]: sums of df, df*z, df*xhat)."""
+    dev = _require_cuda(x, dy, gamma, beta, stats)
+    n, c, hw = _gn_check(x, gamma, beta, film, groups)
+    dy = dy.contiguous(memory_format=torch.channels_last)
+    if dy.dtype != torch.bfloat16 or dy.shape != x.shape:
+        raise RuntimeError("dy must be a bfloat16 tensor shaped like x")
+    dx = torch.empty_like(x, memory_format=torch.channels_last)
+    totals = torch.empty((n, 3, c), device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_gn_workspace_bytes(n, hw, c) // 4, 4), device=dev, dtype=torch.float32)
+        _lib.check(lib.fp8_gn_act_bwd(
+            _ptr(x), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps),
+            _ptr(stats), _ptr(totals), _ptr(dx), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)),
+            "fp8_gn_act_bwd")
+    return dx, totals
+
+
+@gn_act_bwd.register_fake
+def _(x, dy, gamma, beta, film, seed, stats, p, eps, groups):
+    return (torch.empty_like(x, memory_format=torch.channels_last),
+            x.new_empty((x.shape[0], 3, x.shape[1]), dtype=torch.float32))

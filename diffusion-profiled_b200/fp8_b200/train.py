@@ -227,10 +227,10 @@ class GraphedTrainStep:
 
 
 def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16,), p_drop: float = 0.1,
-                device: torch.device | str = "cuda", seed: int = 0) -> UNet:
+                device: torch.device | str = "cuda", seed: int = 0, fused_norm: bool = True) -> UNet:
     torch.manual_seed(seed)
     cfg = UNetConfig(fp8_convs_enabled=fp8, fp8_scaling_type=scaling, attn_resolutions=list(attn_resolutions),
-                     p_drop=p_drop)
+                     p_drop=p_drop, fused_norm=fused_norm)
     model = UNet(cfg).to(memory_format=torch.channels_last)
     return model.to(device)
 

@@ -28,6 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
+from .norm import fused_norm_supported, group_norm_act
 
 
 @dataclass
@@ -43,6 +44,10 @@ class UNetConfig:
     fp8_convs_enabled: bool = False
     fp8_scaling_type: str = "current"
     fp8_amax_history: int = 1024
+    # GroupNorm -> (FiLM) -> SiLU -> (dropout) chains as one fused CUDA op
+    # (fp8_b200.norm) where the activation is a bf16 CUDA tensor; the reference's
+    # separate torch ops otherwise.  No parameters or buffers depend on it.
+    fused_norm: bool = True
 
     def as_dict(self):
         return asdict(self)
@@ -119,10 +124,27 @@ class ResidualBlock(nn.Module):
         )
         self.dropout = nn.Dropout(p_drop)
         nn.init.zeros_(self.conv_2.conv.weight)
+        self.fused_norm = config.fused_norm
+        # dropout mask seed of the fused path (device scalar, advanced every
+        # training forward so a captured graph draws a new mask each replay)
+        self.register_buffer("dropout_seed", torch.randint(0, 2**62, (), dtype=torch.int64), persistent=False)
+
+    def _next_seed(self) -> torch.Tensor:
+        seed = self.dropout_seed.clone()
+        self.dropout_seed.add_(1)
+        return seed
 
     def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
-        h = self.conv_1(F.silu(self.norm1(x)))
-        scale, shift = torch.chunk(self.t_embed_wb(t), chunks=2, dim=1)
+        emb = self.t_embed_wb(t)
+        if self.fused_norm and fused_norm_supported(x, self.norm1):
+            h = self.conv_1(group_norm_act(x, self.norm1))
+            if fused_norm_supported(h, self.norm2) and emb.dtype == torch.bfloat16:
+                p = self.dropout.p if self.training else 0.0
+                h = self.conv_2(group_norm_act(h, self.norm2, emb, p, self._next_seed() if p > 0.0 else None))
+                return (self.skip_connection(x) + h) / math.sqrt(2.0)
+        else:
+            h = self.conv_1(F.silu(self.norm1(x)))
+        scale, shift = torch.chunk(emb, chunks=2, dim=1)
         h = (scale + 1) * self.norm2(h) + shift
         h = self.conv_2(self.dropout(F.silu(h)))
         return (self.skip_connection(x) + h) / math.sqrt(2.0)
@@ -222,6 +244,8 @@ class UNet(nn.Module):
             h = skips.pop()
             up = F.interpolate(act, scale_factor=2.0, mode="nearest") if i > 0 else act
             act = stage(torch.cat([up, h], dim=1), t_emb)
+        if self.config.fused_norm and fused_norm_supported(act, self.out[0]):
+            return self.out[2](group_norm_act(act, self.out[0]))
         return self.out(act)
 
 

@@ -182,6 +182,32 @@ int fp8_set_conv_algo(int algo);
  * the cast pass (1..8; 0 restores the built-in choice).  Process-wide. */
 int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);
 
+/* ---- GroupNorm + FiLM + SiLU + dropout (the activations that feed the FP8 convs).
+ * No reference kernel: these replace the torch ops of the reference ResBlock,
+ * norm1 -> silu (unet.py:151) and norm2 -> (scale + 1) * h + shift -> silu ->
+ * dropout (unet.py:157-159), with one statistics pass and one apply pass.
+ * x, dy, out, dx: NHWC bf16 [n][hw][c] (channels_last), 16-byte aligned, c a
+ * multiple of 8, c <= 512, c % groups == 0.  gamma, beta: fp32 [c].
+ * film: nullable bf16 [n][film_ld], FiLM scale at film[i*film_ld + ch] and shift
+ * at film[i*film_ld + c + ch] (the chunk of the time-embedding projection).
+ * seed: nullable device int64 (dropout off when null or p == 0); element e is
+ * kept when a 16-bit slice of splitmix64 of (seed, e / 4) is >= p * 65536.
+ * stats: fp32 [n][2][groups] (mean, rstd), written by the forward and read by
+ * the backward.  totals (backward): fp32 [n][3][c] = per sample and channel the
+ * sums over pixels of df, df * z and df * xhat, where f = (scale + 1) * z + shift
+ * and z = gamma * xhat + beta; the caller forms d gamma = sum_n (scale+1) * totals[2],
+ * d beta = sum_n (scale+1) * totals[0], d scale = totals[1], d shift = totals[0]. */
+size_t fp8_gn_workspace_bytes(int n, int hw, int c);
+
+int fp8_gn_act_fwd(const void* x, const float* gamma, const float* beta, const void* film, int film_ld,
+                   const int64_t* seed, float p, float eps, float* stats, void* out, int n, int hw, int c,
+                   int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
+
+int fp8_gn_act_bwd(const void* x, const void* dy, const float* gamma, const float* beta, const void* film,
+                   int film_ld, const int64_t* seed, float p, float eps, const float* stats, float* totals,
+                   void* dx, int n, int hw, int c, int groups, void* workspace, size_t workspace_bytes,
+                   fp8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,7 +37,7 @@ def test_binding_covers_every_declared_symbol():
 
 
 def test_abi_version():
-    assert _lib.load().fp8_abi_version() == 2
+    assert _lib.load().fp8_abi_version() == 3
 
 
 def _status_and_message(fn, *args):
