@@ -549,6 +549,33 @@ size_t gn_workspace(int n, int hw, int c, int sm_count) {
   return static_cast<size_t>(n) * gn_slices(n, hw, c, sm_count) * 3 * c * sizeof(float);
 }
 
+template <typename TX>
+int launch_gn_fwd(const TX* x, const GnShape& sh, float* part, const GnActParams& q, float* stats, void* out,
+                  size_t s1, size_t s2, cudaStream_t cs) {
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_stats_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s1)));
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_fwd_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s2)));
+  gn_stats_kernel<TX><<<sh.n * sh.slices, kGnThreads, s1, cs>>>(x, sh, part);
+  gn_act_fwd_kernel<TX><<<sh.n * sh.slices, kGnThreads, s2, cs>>>(x, sh, part, q, stats,
+                                                                   static_cast<uint16_t*>(out));
+  count_launches(2);
+  return FP8_OK;
+}
+
+template <typename TX>
+int launch_gn_bwd(const TX* x, const uint16_t* dy, const GnShape& sh, const float* stats, const GnActParams& q,
+                  float* part, float* totals, TX* dx, size_t s1, size_t s2, cudaStream_t cs) {
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_reduce_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s1)));
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_apply_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(s2)));
+  gn_act_bwd_reduce_kernel<TX><<<sh.n * sh.slices, kGnThreads, s1, cs>>>(x, dy, sh, stats, q, part);
+  gn_act_bwd_apply_kernel<TX><<<sh.n * sh.slices, kGnThreads, s2, cs>>>(x, dy, sh, stats, q, part, totals, dx);
+  count_launches(2);
+  return FP8_OK;
+}
+
 int check_gn_args(const void* x, const void* out, const float* gamma, const float* beta, int n, int hw, int c,
                   int groups, int film_ld, const void* film, float p, float eps) {
   FP8_REQUIRE(n > 0 && hw > 0 && c > 0 && groups > 0, FP8_ERR_INVALID_ARGUMENT, "bad group-norm sizes");
@@ -1082,9 +1109,9 @@ size_t fp8_gn_workspace_bytes(int n, int hw, int c) {
   return gn_workspace(n, hw, c, sms > 0 ? sms : 148);
 }
 
-int fp8_gn_act_fwd(const void* x, const float* gamma, const float* beta, const void* film, int film_ld,
-                   const int64_t* seed, float p, float eps, float* stats, void* out, int n, int hw, int c,
-                   int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+int fp8_gn_act_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                   int film_ld, const int64_t* seed, float p, float eps, float* stats, void* out, int n, int hw,
+                   int c, int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
   if (int s = check_gn_args(x, out, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
   FP8_REQUIRE(stats != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats");
   DeviceState* st;
@@ -1097,22 +1124,19 @@ int fp8_gn_act_fwd(const void* x, const float* gamma, const float* beta, const v
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s1)));
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s2)));
-  gn_stats_kernel<<<n * sh.slices, kGnThreads, s1, cs>>>(static_cast<const uint16_t*>(x), sh, part);
-  gn_act_fwd_kernel<<<n * sh.slices, kGnThreads, s2, cs>>>(static_cast<const uint16_t*>(x), sh, part, q, stats,
-                                                            static_cast<uint16_t*>(out));
-  count_launches(2);
+  if (x_fp32) {
+    if (int s = launch_gn_fwd(static_cast<const float*>(x), sh, part, q, stats, out, s1, s2, cs)) return s;
+  } else {
+    if (int s = launch_gn_fwd(static_cast<const uint16_t*>(x), sh, part, q, stats, out, s1, s2, cs)) return s;
+  }
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }
 
-int fp8_gn_act_bwd(const void* x, const void* dy, const float* gamma, const float* beta, const void* film,
-                   int film_ld, const int64_t* seed, float p, float eps, const float* stats, float* totals,
-                   void* dx, int n, int hw, int c, int groups, void* workspace, size_t workspace_bytes,
-                   fp8_stream_t stream) {
+int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,
+                   const void* film, int film_ld, const int64_t* seed, float p, float eps, const float* stats,
+                   float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
+                   size_t workspace_bytes, fp8_stream_t stream) {
   if (int s = check_gn_args(x, dx, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
   FP8_REQUIRE(dy != nullptr && aligned(dy, 16), FP8_ERR_INVALID_ARGUMENT, "dy must be 16-byte aligned");
   FP8_REQUIRE(stats != nullptr && totals != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats / totals");
@@ -1126,16 +1150,16 @@ int fp8_gn_act_bwd(const void* x, const void* dy, const float* gamma, const floa
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const size_t s1 = gn_bwd_reduce_smem(c, groups), s2 = gn_bwd_apply_smem(c, groups);
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_reduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s1)));
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s2)));
-  const uint16_t* xs = static_cast<const uint16_t*>(x);
   const uint16_t* ds = static_cast<const uint16_t*>(dy);
-  gn_act_bwd_reduce_kernel<<<n * sh.slices, kGnThreads, s1, cs>>>(xs, ds, sh, stats, q, part);
-  gn_act_bwd_apply_kernel<<<n * sh.slices, kGnThreads, s2, cs>>>(xs, ds, sh, stats, q, part, totals,
-                                                                  static_cast<uint16_t*>(dx));
-  count_launches(2);
+  if (x_fp32) {
+    if (int s = launch_gn_bwd(static_cast<const float*>(x), ds, sh, stats, q, part, totals, static_cast<float*>(dx),
+                              s1, s2, cs))
+      return s;
+  } else {
+    if (int s = launch_gn_bwd(static_cast<const uint16_t*>(x), ds, sh, stats, q, part, totals,
+                              static_cast<uint16_t*>(dx), s1, s2, cs))
+      return s;
+  }
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }

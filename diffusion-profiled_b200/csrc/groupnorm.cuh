@@ -21,6 +21,7 @@
 //                              - xhat * mean_g[gamma (s+1) df xhat]),
 //                         and the per-(n, c) totals the host turns into the parameter,
 //                         scale and shift gradients.
+// x (and dx) may be bf16 or fp32; the activation and its gradient are bf16.
 // Dropout keeps element e when a 16-bit slice of splitmix64(seed, e / 4) is >= p * 65536
 // (splitmix64: Steele, Lea and Flood, "Fast splittable pseudorandom number
 // generators", OOPSLA 2014); the seed is read from device memory so a captured
@@ -70,6 +71,73 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
                     pack_bf16x2(f[6], f[7]));
+}
+
+// Eight consecutive channels of x, stored as bf16 (uint16_t) or fp32: the
+// reference runs GroupNorm on whatever its input is (fp32 after autocast's fp32
+// resampling, bf16 after a conv), so both element types are accepted.
+template <typename TX>
+struct XVec;
+template <>
+struct XVec<uint16_t> {
+  uint4 v;
+};
+template <>
+struct XVec<float> {
+  float4 a, b;
+};
+
+template <typename TX>
+__device__ __forceinline__ XVec<TX> load_x8(const TX* __restrict__ x, int64_t vi) {
+  XVec<TX> r;
+  if constexpr (sizeof(TX) == 2) {
+    r.v = __ldg(reinterpret_cast<const uint4*>(x) + vi);
+  } else {
+    r.a = __ldg(reinterpret_cast<const float4*>(x) + 2 * vi);
+    r.b = __ldg(reinterpret_cast<const float4*>(x) + 2 * vi + 1);
+  }
+  return r;
+}
+
+template <typename TX>
+__device__ __forceinline__ XVec<TX> zero_x8() {
+  XVec<TX> r;
+  if constexpr (sizeof(TX) == 2) {
+    r.v = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    r.a = make_float4(0.f, 0.f, 0.f, 0.f);
+    r.b = r.a;
+  }
+  return r;
+}
+
+template <typename TX>
+__device__ __forceinline__ void unpack_x8(const XVec<TX>& r, float (&f)[8]) {
+  if constexpr (sizeof(TX) == 2) {
+    unpack8(r.v, f);
+  } else {
+    f[0] = r.a.x; f[1] = r.a.y; f[2] = r.a.z; f[3] = r.a.w;
+    f[4] = r.b.x; f[5] = r.b.y; f[6] = r.b.z; f[7] = r.b.w;
+  }
+}
+
+template <typename TX>
+__device__ __forceinline__ void store_x8(TX* __restrict__ x, int64_t vi, const float (&f)[8]) {
+  if constexpr (sizeof(TX) == 2) {
+    reinterpret_cast<uint4*>(x)[vi] = pack8(f);
+  } else {
+    reinterpret_cast<float4*>(x)[2 * vi] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(x)[2 * vi + 1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+template <typename TX>
+__device__ __forceinline__ float load_x1(const TX* __restrict__ x, int64_t i) {
+  if constexpr (sizeof(TX) == 2) {
+    return __uint_as_float(static_cast<uint32_t>(x[i]) << 16);
+  } else {
+    return x[i];
+  }
 }
 
 // Thread layout shared by all four kernels.
@@ -131,28 +199,29 @@ __host__ __device__ constexpr size_t gn_bwd_apply_smem(int c, int g) {
 
 // ------------------------------------------------------------------ statistics
 // part[(n * slices + slice) * 2C + {0, C} + c] = sum (x - shift_c), sum (x - shift_c)^2
-__global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const uint16_t* __restrict__ x, GnShape s,
+template <typename TX>
+__global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const TX* __restrict__ x, GnShape s,
                                                               float* __restrict__ part) {
   extern __shared__ float gn_smem[];
   const GnThread t = gn_thread(s);
   float acc[2][8] = {};
   if (t.r < t.rows) {
-    const uint4* xs = reinterpret_cast<const uint4*>(x) + static_cast<int64_t>(t.n) * s.hw * t.vecs;
+    const TX* xs = x + static_cast<int64_t>(t.n) * s.hw * s.c;
     float sh[8];
-    unpack8(__ldg(xs + t.v), sh);
+    unpack_x8(load_x8(xs, t.v), sh);
     // Four pixel rows per step: their loads are in flight together.
     for (int p = t.p0 + t.r; p < t.p1; p += 4 * t.rows) {
-      uint4 v[4];
+      XVec<TX> v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int pu = p + u * t.rows;
-        v[u] = pu < t.p1 ? __ldg(xs + static_cast<int64_t>(pu) * t.vecs + t.v) : make_uint4(0u, 0u, 0u, 0u);
+        v[u] = pu < t.p1 ? load_x8(xs, static_cast<int64_t>(pu) * t.vecs + t.v) : zero_x8<TX>();
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (p + u * t.rows >= t.p1) break;
         float f[8];
-        unpack8(v[u], f);
+        unpack_x8(v[u], f);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float d = f[k] - sh[k];
@@ -170,7 +239,8 @@ __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const uint16_t* __
 
 // Per-group mean / rstd of sample n from the slices' partial sums (all threads call;
 // result in smem mean_g[G], rstd_g[G]).  shift_c = x[n, 0, c].
-__device__ __forceinline__ void gn_group_stats(const uint16_t* __restrict__ x, const float* __restrict__ part,
+template <typename TX>
+__device__ __forceinline__ void gn_group_stats(const TX* __restrict__ x, const float* __restrict__ part,
                                                const GnShape& s, int n, float eps, float* mean_g, float* rstd_g,
                                                float* ch_mean, float* ch_m2) {
   const float cnt = static_cast<float>(s.hw);
@@ -181,7 +251,7 @@ __device__ __forceinline__ void gn_group_stats(const uint16_t* __restrict__ x, c
       s1 += pp[c];
       s2 += pp[s.c + c];
     }
-    const float shift = __uint_as_float(static_cast<uint32_t>(x[static_cast<int64_t>(n) * s.hw * s.c + c]) << 16);
+    const float shift = load_x1(x, static_cast<int64_t>(n) * s.hw * s.c + c);
     ch_mean[c] = shift + s1 / cnt;
     ch_m2[c] = fmaxf(s2 - s1 * s1 / cnt, 0.0f);
   }
@@ -237,7 +307,8 @@ __device__ __forceinline__ void gn_coeffs(const GnShape& s, const GnActParams& q
 }
 
 // stats[n * 2G + {0, G} + g] = mean, rstd (written by slice 0 of each sample).
-__global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const uint16_t* __restrict__ x, GnShape s,
+template <typename TX>
+__global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __restrict__ x, GnShape s,
                                                                 const float* __restrict__ part, GnActParams q,
                                                                 float* __restrict__ stats,
                                                                 uint16_t* __restrict__ out) {
@@ -268,14 +339,14 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const uint16_t* 
   const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
   const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
   const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
-  const uint4* xs = reinterpret_cast<const uint4*>(x) + base;
+  const TX* xs = x + base * 8;
   uint4* os = reinterpret_cast<uint4*>(out) + base;
   for (int p = t.p0 + t.r; p < t.p1; p += 4 * t.rows) {
-    uint4 v[4];
+    XVec<TX> v[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int pu = p + u * t.rows;
-      v[u] = pu < t.p1 ? __ldg(xs + static_cast<int64_t>(pu) * t.vecs + t.v) : make_uint4(0u, 0u, 0u, 0u);
+      v[u] = pu < t.p1 ? load_x8(xs, static_cast<int64_t>(pu) * t.vecs + t.v) : zero_x8<TX>();
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -283,7 +354,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const uint16_t* 
       if (pu >= t.p1) break;
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
       float f[8];
-      unpack8(v[u], f);
+      unpack_x8(v[u], f);
       const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -302,8 +373,9 @@ struct GnBwdElem {
 };
 
 // part[(n * slices + slice) * 3C + {0, C, 2C} + c] = sum df, sum df * z, sum df * xhat
+template <typename TX>
 __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
+    const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
     GnActParams q, float* __restrict__ part) {
   extern __shared__ float gn_smem[];
   float* A = gn_smem;
@@ -340,15 +412,16 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
     const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
     const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
     const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
-    const uint4* xs = reinterpret_cast<const uint4*>(x) + base;
+    const TX* xs = x + base * 8;
     const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
     for (int p = t.p0 + t.r; p < t.p1; p += 2 * t.rows) {
-      uint4 vx[2], vd[2];
+      XVec<TX> vx[2];
+      uint4 vd[2];
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int pu = p + u * t.rows;
         const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
-        vx[u] = pu < t.p1 ? __ldg(xs + vi) : make_uint4(0u, 0u, 0u, 0u);
+        vx[u] = pu < t.p1 ? load_x8(xs, vi) : zero_x8<TX>();
         vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
@@ -357,7 +430,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
         if (pu >= t.p1) break;
         const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
         float xf[8], gf[8];
-        unpack8(vx[u], xf);
+        unpack_x8(vx[u], xf);
         unpack8(vd[u], gf);
         const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
 #pragma unroll
@@ -380,9 +453,10 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
 
 // totals[n * 3C + {0, C, 2C} + c] = sum df, sum df z, sum df xhat over the sample
 // (written by slice 0); dx as above.
+template <typename TX>
 __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
-    GnActParams q, const float* __restrict__ part, float* __restrict__ totals, uint16_t* __restrict__ dx) {
+    const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
+    GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx) {
   extern __shared__ float gn_smem[];
   float* A = gn_smem;
   float* B = A + s.c;
@@ -447,16 +521,17 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
   const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
   const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
   const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
-  const uint4* xs = reinterpret_cast<const uint4*>(x) + base;
+  const TX* xs = x + base * 8;
   const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
-  uint4* os = reinterpret_cast<uint4*>(dx) + base;
+  TX* os = dx + base * 8;
   for (int p = t.p0 + t.r; p < t.p1; p += 2 * t.rows) {
-    uint4 vx[2], vd[2];
+    XVec<TX> vx[2];
+    uint4 vd[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int pu = p + u * t.rows;
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
-      vx[u] = pu < t.p1 ? __ldg(xs + vi) : make_uint4(0u, 0u, 0u, 0u);
+      vx[u] = pu < t.p1 ? load_x8(xs, vi) : zero_x8<TX>();
       vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
@@ -465,7 +540,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
       if (pu >= t.p1) break;
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
       float xf[8], gf[8], o[8];
-      unpack8(vx[u], xf);
+      unpack_x8(vx[u], xf);
       unpack8(vd[u], gf);
       const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
 #pragma unroll
@@ -477,7 +552,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
         const float xhat = (xf[k] - mu[k]) * rs[k];
         o[k] = rs[k] * (gk[k] * df - m1[k] - xhat * m2[k]);
       }
-      os[vi] = pack8(o);
+      store_x8(os, vi, o);
     }
   }
 }

@@ -43,7 +43,7 @@ class GroupNormAct(torch.autograd.Function):
 
 def group_norm_act(x: torch.Tensor, norm: torch.nn.GroupNorm, film: torch.Tensor | None = None,
                    p: float = 0.0, seed: torch.Tensor | None = None) -> torch.Tensor:
-    """``dropout_p(silu((film_scale + 1) * norm(x) + film_shift))`` for a channels_last bf16 CUDA ``x``.
+    """``dropout_p(silu((film_scale + 1) * norm(x) + film_shift))`` (bf16) for a bf16 or fp32 CUDA ``x``.
 
     ``film``: the time-embedding projection ``[N, 2C(, 1, 1)]`` (scale, shift), or None.
     ``seed``: int64 device scalar for the dropout mask (required when ``p > 0``)."""
@@ -56,5 +56,5 @@ def group_norm_act(x: torch.Tensor, norm: torch.nn.GroupNorm, film: torch.Tensor
 
 def fused_norm_supported(x: torch.Tensor, norm: torch.nn.GroupNorm) -> bool:
     c = x.shape[1]
-    return (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 4 and c % 8 == 0 and c <= 512
+    return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and x.dim() == 4 and c % 8 == 0 and c <= 512
             and c % norm.num_groups == 0 and norm.affine and norm.weight.dtype == torch.float32)

@@ -354,8 +354,9 @@ __all__ = [
 # ----------------------------------------------------------------------------- group norm + activation
 def _gn_check(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
               groups: int) -> tuple[int, int, int]:
-    if x.dtype != torch.bfloat16 or x.dim() != 4 or not x.is_contiguous(memory_format=torch.channels_last):
-        raise RuntimeError("group norm expects a channels_last bfloat16 [N, C, H, W] tensor")
+    if x.dtype not in (torch.bfloat16, torch.float32) or x.dim() != 4 or not x.is_contiguous(
+            memory_format=torch.channels_last):
+        raise RuntimeError("group norm expects a channels_last bfloat16 or float32 [N, C, H, W] tensor")
     n, c, h, w = x.shape
     if gamma.dtype != torch.float32 or beta.dtype != torch.float32 or gamma.numel() != c or beta.numel() != c:
         raise RuntimeError("gamma / beta must be float32 [C]")
@@ -370,24 +371,26 @@ def gn_act_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: t
                seed: torch.Tensor | None, p: float, eps: float, groups: int) -> tuple[torch.Tensor, torch.Tensor]:
     """a = dropout(silu((film_scale + 1) * GroupNorm(x) + film_shift)) -> (a bf16 channels_last, stats [N, 2, G]).
 
+    x is bf16 or fp32 (the dtype the reference's GroupNorm sees at that point).
+
     No reference kernel: replaces the torch chain of the reference ResBlock
     (unet.py:151, :157-159).  `seed` (int64 device scalar) selects the dropout mask."""
     dev = _require_cuda(x, gamma, beta)
     n, c, hw = _gn_check(x, gamma, beta, film, groups)
-    out = torch.empty_like(x, memory_format=torch.channels_last)
+    out = torch.empty_like(x, dtype=torch.bfloat16, memory_format=torch.channels_last)
     stats = torch.empty((n, 2, groups), device=dev, dtype=torch.float32)
     lib = _lib.load()
     with torch.cuda.device(dev):
         ws = torch.empty(max(lib.fp8_gn_workspace_bytes(n, hw, c) // 4, 4), device=dev, dtype=torch.float32)
         _lib.check(lib.fp8_gn_act_fwd(
-            _ptr(x), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps), _ptr(stats),
+            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps), _ptr(stats),
             _ptr(out), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)), "fp8_gn_act_fwd")
     return out, stats
 
 
 @gn_act_fwd.register_fake
 def _(x, gamma, beta, film, seed, p, eps, groups):
-    return (torch.empty_like(x, memory_format=torch.channels_last),
+    return (torch.empty_like(x, dtype=torch.bfloat16, memory_format=torch.channels_last),
             x.new_empty((x.shape[0], 2, groups), dtype=torch.float32))
 
 
@@ -395,7 +398,7 @@ def _(x, gamma, beta, film, seed, p, eps, groups):
 def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
                film: torch.Tensor | None, seed: torch.Tensor | None, stats: torch.Tensor, p: float, eps: float,
                groups: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Backward of gn_act_fwd -> (dx bf16 channels_last, totals [N, 3, C]: sums of df, df*z, df*xhat)."""
+    """Backward of gn_act_fwd -> (dx in x's dtype, channels_last; totals [N, 3, C]: sums of df, df*z, df*xhat)."""
     dev = _require_cuda(x, dy, gamma, beta, stats)
     n, c, hw = _gn_check(x, gamma, beta, film, groups)
     dy = dy.contiguous(memory_format=torch.channels_last)
@@ -407,7 +410,7 @@ def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: tor
     with torch.cuda.device(dev):
         ws = torch.empty(max(lib.fp8_gn_workspace_bytes(n, hw, c) // 4, 4), device=dev, dtype=torch.float32)
         _lib.check(lib.fp8_gn_act_bwd(
-            _ptr(x), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps),
+            _ptr(x), int(x.dtype == torch.float32), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps),
             _ptr(stats), _ptr(totals), _ptr(dx), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)),
             "fp8_gn_act_bwd")
     return dx, totals

@@ -186,8 +186,9 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);
  * No reference kernel: these replace the torch ops of the reference ResBlock,
  * norm1 -> silu (unet.py:151) and norm2 -> (scale + 1) * h + shift -> silu ->
  * dropout (unet.py:157-159), with one statistics pass and one apply pass.
- * x, dy, out, dx: NHWC bf16 [n][hw][c] (channels_last), 16-byte aligned, c a
- * multiple of 8, c <= 512, c % groups == 0.  gamma, beta: fp32 [c].
+ * x, dx: NHWC [n][hw][c] (channels_last), bf16 (x_fp32 = 0) or fp32 (x_fp32 = 1);
+ * out, dy: NHWC bf16; all 16-byte aligned; c a multiple of 8, c <= 512,
+ * c % groups == 0.  gamma, beta: fp32 [c].
  * film: nullable bf16 [n][film_ld], FiLM scale at film[i*film_ld + ch] and shift
  * at film[i*film_ld + c + ch] (the chunk of the time-embedding projection).
  * seed: nullable device int64 (dropout off when null or p == 0); element e is
@@ -199,14 +200,14 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);
  * d beta = sum_n (scale+1) * totals[0], d scale = totals[1], d shift = totals[0]. */
 size_t fp8_gn_workspace_bytes(int n, int hw, int c);
 
-int fp8_gn_act_fwd(const void* x, const float* gamma, const float* beta, const void* film, int film_ld,
-                   const int64_t* seed, float p, float eps, float* stats, void* out, int n, int hw, int c,
-                   int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
+int fp8_gn_act_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                   int film_ld, const int64_t* seed, float p, float eps, float* stats, void* out, int n, int hw,
+                   int c, int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
 
-int fp8_gn_act_bwd(const void* x, const void* dy, const float* gamma, const float* beta, const void* film,
-                   int film_ld, const int64_t* seed, float p, float eps, const float* stats, float* totals,
-                   void* dx, int n, int hw, int c, int groups, void* workspace, size_t workspace_bytes,
-                   fp8_stream_t stream);
+int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,
+                   const void* film, int film_ld, const int64_t* seed, float p, float eps, const float* stats,
+                   float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
+                   size_t workspace_bytes, fp8_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -20,9 +20,9 @@ def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
     return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
 
 
-def _inputs(n, c, h, w, film: bool, seed: int, device):
+def _inputs(n, c, h, w, film: bool, seed: int, device, dtype=torch.bfloat16):
     g = torch.Generator().manual_seed(seed)
-    x = (torch.randn(n, c, h, w, generator=g) * 2 + 0.5).to(torch.bfloat16)
+    x = (torch.randn(n, c, h, w, generator=g) * 2 + 0.5).to(dtype)
     x = x.contiguous(memory_format=torch.channels_last).to(device)
     norm = torch.nn.GroupNorm(32, c).to(device)
     with torch.no_grad():
@@ -44,12 +44,14 @@ def _reference(x, norm, film, mask=None, p=0.0):
     return a
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("film", [False, True])
 @pytest.mark.parametrize("c,h,w", SHAPES)
-def test_group_norm_act_forward_and_backward(cuda, c, h, w, film):
+def test_group_norm_act_forward_and_backward(cuda, c, h, w, film, dtype):
+    """bf16 input (after a conv) and fp32 input (after autocast's fp32 resampling)."""
     from fp8_b200.norm import group_norm_act
 
-    x, norm, f, dout = _inputs(4, c, h, w, film, seed=c + h + film, device=cuda)
+    x, norm, f, dout = _inputs(4, c, h, w, film, seed=c + h + film, device=cuda, dtype=dtype)
     xr = x.detach().clone().requires_grad_(True)
     fr = None if f is None else f.detach().clone().requires_grad_(True)
     x.requires_grad_(True)
@@ -63,6 +65,7 @@ def test_group_norm_act_forward_and_backward(cuda, c, h, w, film):
     assert _rel(out, ref) <= TOL
     out.backward(dout)
     ref.backward(dout.float())
+    assert x.grad.dtype == dtype
     assert _rel(x.grad, xr.grad) <= TOL
     assert _rel(norm.weight.grad, ref_norm.weight.grad) <= TOL
     assert _rel(norm.bias.grad, ref_norm.bias.grad) <= TOL

@@ -123,11 +123,16 @@ def _loss_curve(cuda, fp8: bool, steps: int, batch: int, scaling: str = "current
 def test_fp8_loss_curve_within_2pct_of_bf16(cuda):
     """200 training steps (BASELINE config 4 architecture, synthetic uniform images):
     the B200 path (FP8 convs, current scaling as the reference's default unet.py:24,
-    fused norm/activation ops) against the reference's bf16 model (torch ops)."""
+    fused norm/activation ops) against the reference's bf16 model (torch ops).
+
+    The curve is compared on its final 50 steps, where it has flattened: over
+    steps 100-200 the bf16 model alone spread 2.4 % across three seeds (mean
+    loss 0.1866-0.1911), over steps 150-200 0.3 % (0.1896-0.1901), with the
+    FP8 + fused path at 0.1882-0.1892 on two seeds."""
     fp8 = _loss_curve(cuda, True, 200, 128, scaling="current")
     bf16 = _loss_curve(cuda, False, 200, 128, fused_norm=False)
     assert np.isfinite(fp8).all() and np.isfinite(bf16).all()
-    tail_fp8, tail_bf16 = fp8[-100:].mean(), bf16[-100:].mean()
+    tail_fp8, tail_bf16 = fp8[-50:].mean(), bf16[-50:].mean()
     assert tail_bf16 < bf16[:10].mean()  # it trains
     rel = abs(tail_fp8 - tail_bf16) / tail_bf16
     assert rel <= 0.02, (tail_fp8, tail_bf16, rel)
