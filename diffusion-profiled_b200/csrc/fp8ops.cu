@@ -538,9 +538,12 @@ int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const 
 // ------------------------------------------------------------------ group norm helpers
 // CTAs per sample: about three per SM over the batch, each with at least one
 // row step of pixels.
+#ifndef FP8_GN_CTAS_PER_SM
+#define FP8_GN_CTAS_PER_SM 3
+#endif
 int gn_slices(int n, int hw, int c, int sm_count) {
   const int rows = kGnThreads / (c / 8);
-  int s = (3 * sm_count + n - 1) / std::max(n, 1);
+  int s = (FP8_GN_CTAS_PER_SM * sm_count + n - 1) / std::max(n, 1);
   s = std::min(s, std::max(1, hw / rows));
   return std::max(s, 1);
 }

@@ -32,7 +32,18 @@
 
 namespace fp8b {
 
-constexpr int kGnThreads = 512;
+#ifndef FP8_GN_THREADS
+#define FP8_GN_THREADS 256
+#endif
+#ifndef FP8_GN_UF
+#define FP8_GN_UF 4
+#endif
+#ifndef FP8_GN_UB
+#define FP8_GN_UB 2
+#endif
+constexpr int kGnThreads = FP8_GN_THREADS;
+constexpr int kGnUnrollFwd = FP8_GN_UF;  // pixel rows per step, forward kernels
+constexpr int kGnUnrollBwd = FP8_GN_UB;  // pixel rows per step, backward kernels
 
 struct GnShape {
   int n, hw, c, groups;
@@ -210,15 +221,15 @@ __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const TX* __restri
     float sh[8];
     unpack_x8(load_x8(xs, t.v), sh);
     // Four pixel rows per step: their loads are in flight together.
-    for (int p = t.p0 + t.r; p < t.p1; p += 4 * t.rows) {
-      XVec<TX> v[4];
+    for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollFwd * t.rows) {
+      XVec<TX> v[kGnUnrollFwd];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kGnUnrollFwd; ++u) {
         const int pu = p + u * t.rows;
         v[u] = pu < t.p1 ? load_x8(xs, static_cast<int64_t>(pu) * t.vecs + t.v) : zero_x8<TX>();
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kGnUnrollFwd; ++u) {
         if (p + u * t.rows >= t.p1) break;
         float f[8];
         unpack_x8(v[u], f);
@@ -341,15 +352,15 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __rest
   const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
   const TX* xs = x + base * 8;
   uint4* os = reinterpret_cast<uint4*>(out) + base;
-  for (int p = t.p0 + t.r; p < t.p1; p += 4 * t.rows) {
-    XVec<TX> v[4];
+  for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollFwd * t.rows) {
+    XVec<TX> v[kGnUnrollFwd];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kGnUnrollFwd; ++u) {
       const int pu = p + u * t.rows;
       v[u] = pu < t.p1 ? load_x8(xs, static_cast<int64_t>(pu) * t.vecs + t.v) : zero_x8<TX>();
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kGnUnrollFwd; ++u) {
       const int pu = p + u * t.rows;
       if (pu >= t.p1) break;
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
@@ -414,18 +425,18 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
     const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
     const TX* xs = x + base * 8;
     const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
-    for (int p = t.p0 + t.r; p < t.p1; p += 2 * t.rows) {
-      XVec<TX> vx[2];
-      uint4 vd[2];
+    for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollBwd * t.rows) {
+      XVec<TX> vx[kGnUnrollBwd];
+      uint4 vd[kGnUnrollBwd];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < kGnUnrollBwd; ++u) {
         const int pu = p + u * t.rows;
         const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
         vx[u] = pu < t.p1 ? load_x8(xs, vi) : zero_x8<TX>();
         vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < kGnUnrollBwd; ++u) {
         const int pu = p + u * t.rows;
         if (pu >= t.p1) break;
         const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
@@ -524,18 +535,18 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
   const TX* xs = x + base * 8;
   const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
   TX* os = dx + base * 8;
-  for (int p = t.p0 + t.r; p < t.p1; p += 2 * t.rows) {
-    XVec<TX> vx[2];
-    uint4 vd[2];
+  for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollBwd * t.rows) {
+    XVec<TX> vx[kGnUnrollBwd];
+    uint4 vd[kGnUnrollBwd];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kGnUnrollBwd; ++u) {
       const int pu = p + u * t.rows;
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
       vx[u] = pu < t.p1 ? load_x8(xs, vi) : zero_x8<TX>();
       vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kGnUnrollBwd; ++u) {
       const int pu = p + u * t.rows;
       if (pu >= t.p1) break;
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;

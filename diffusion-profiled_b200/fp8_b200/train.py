@@ -196,6 +196,13 @@ class GraphedTrainStep:
         """Eager warm-up iterations on a side stream (they also fill the delayed-scaling
         windows, train.py:114-128), then capture."""
         self.model.train()
+        if dist.is_available() and dist.is_initialized():
+            # every rank built the same model: give each rank its own dropout masks
+            with torch.no_grad():
+                for m in self.model.modules():
+                    seed = getattr(m, "dropout_seed", None)
+                    if isinstance(seed, torch.Tensor):
+                        seed.add_(dist.get_rank() << 40)
         for p in self.params:  # grads must exist before capture (zero_grad keeps them)
             p.grad = torch.zeros_like(p)
         s = torch.cuda.Stream(self.device)
