@@ -191,8 +191,7 @@ def run_b200(args) -> None:
     sets = [make_inputs(batch, dev, seed=1000 * rank + i) for i in range(max(1, args.rotate))]
 
     def step(x, dy):
-        xq, sx = ops.quantize_current(x)
-        wq, sw = ops.quantize_current(w)
+        xq, sx, wq, sw = ops.quantize_current_pair(x, w)  # the forward's input and weight together
         y = ops.conv3x3_fwd(xq, wq, sx, sw)
         if args.workload == "fwd":
             return (y,)

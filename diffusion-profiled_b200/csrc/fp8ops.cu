@@ -1168,3 +1168,75 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
 }
 
 }  // extern "C"
+
+// ======================================================================== multi-tensor quantize
+extern "C" {
+
+size_t fp8_quantize_multi_workspace_bytes(int count) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  (void)cudaGetLastError();
+  if (count < 1 || count > kMaxMultiTensors) return 0;
+  return static_cast<size_t>(count) * quant_workspace_bytes(sms > 0 ? sms : 148);
+}
+
+int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const* q_e4m3, float* const* scale_out,
+                               const int64_t* n, void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+  FP8_REQUIRE(count >= 1 && count <= kMaxMultiTensors, FP8_ERR_INVALID_ARGUMENT, "count must be 1..%d",
+              kMaxMultiTensors);
+  FP8_REQUIRE(x_bf16 && q_e4m3 && scale_out && n, FP8_ERR_INVALID_ARGUMENT, "NULL argument array");
+  bool vec = true;
+  for (int t = 0; t < count; ++t) {
+    FP8_REQUIRE(n[t] >= 0, FP8_ERR_INVALID_ARGUMENT, "n[%d] must be >= 0", t);
+    FP8_REQUIRE(scale_out[t] != nullptr && aligned(scale_out[t], 4), FP8_ERR_INVALID_ARGUMENT, "bad scale_out[%d]",
+                t);
+    FP8_REQUIRE(n[t] == 0 || (x_bf16[t] != nullptr && q_e4m3[t] != nullptr), FP8_ERR_INVALID_ARGUMENT,
+                "NULL tensor %d", t);
+    FP8_REQUIRE(aligned(x_bf16[t], 2), FP8_ERR_INVALID_ARGUMENT, "x[%d] must be 2-byte aligned", t);
+    vec = vec && aligned(x_bf16[t], 16) && aligned(q_e4m3[t], 8);
+  }
+  if (!vec) {  // odd views: one call per tensor (each uses the first slots of the workspace)
+    for (int t = 0; t < count; ++t)
+      if (int s = fp8_quantize_current(x_bf16[t], q_e4m3[t], scale_out[t], workspace, workspace_bytes, n[t], stream))
+        return s;
+    return ok();
+  }
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  MultiQuant m{};
+  m.count = count;
+  m.chunk_begin[0] = 0;
+  for (int t = 0; t < count; ++t) {
+    m.x[t] = static_cast<const uint16_t*>(x_bf16[t]);
+    m.q[t] = static_cast<uint8_t*>(q_e4m3[t]);
+    m.scale_out[t] = scale_out[t];
+    m.n[t] = n[t];
+    m.main_bytes[t] = (n[t] & ~int64_t(7)) * 2;
+    m.chunk_begin[t + 1] = m.chunk_begin[t] + (m.main_bytes[t] + kStreamChunkBytes - 1) / kStreamChunkBytes;
+  }
+  auto grid_for = [&](int bps) {
+    int64_t g = m.chunk_begin[count];
+    const int64_t cap = static_cast<int64_t>(st->sm_count) * std::min(bps, kMaxStreamBlocksPerSm);
+    if (g > cap) g = cap;
+    return static_cast<int>(g < 1 ? 1 : g);
+  };
+  const int parts = grid_for(g_quant_amax_bps);
+  const int cast_blocks = grid_for(g_quant_cast_bps);
+  FP8_REQUIRE(workspace != nullptr && aligned(workspace, 4) &&
+                  workspace_bytes >= static_cast<size_t>(count) * parts * sizeof(float),
+              FP8_ERR_WORKSPACE, "quantize workspace too small: need %zu bytes",
+              static_cast<size_t>(count) * parts * sizeof(float));
+  float* partials = static_cast<float*>(workspace);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  FP8_CUDA_TRY(cudaFuncSetAttribute(quant_multi_amax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kStreamSmemBytes)));
+  FP8_CUDA_TRY(cudaFuncSetAttribute(quant_multi_cast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kStreamSmemBytes)));
+  quant_multi_amax_kernel<<<parts, kStreamThreads, kStreamSmemBytes, cs>>>(m, partials, st->err_ptr);
+  quant_multi_cast_kernel<<<cast_blocks, kStreamThreads, kStreamSmemBytes, cs>>>(m, partials, parts, st->err_ptr);
+  count_launches(2);
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+}  // extern "C"

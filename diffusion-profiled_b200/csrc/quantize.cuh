@@ -424,6 +424,197 @@ __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
   }
 }
 
+// ---------------------------------------------------------------- several tensors per launch
+// Current scaling of up to kMaxMultiTensors tensors in one amax launch and one
+// cast launch (a layer's input and weight are quantized together): the chunks of
+// all tensors form one index space (chunk_begin holds the prefix sums), every CTA
+// keeps one |x| maximum per tensor, and every tensor gets its own scale.  Each
+// tensor's bytes are those fp8_quantize_current would produce.
+constexpr int kMaxMultiTensors = 4;
+
+struct MultiQuant {
+  const uint16_t* x[kMaxMultiTensors];
+  uint8_t* q[kMaxMultiTensors];
+  float* scale_out[kMaxMultiTensors];
+  int64_t n[kMaxMultiTensors];
+  int64_t main_bytes[kMaxMultiTensors];
+  int64_t chunk_begin[kMaxMultiTensors + 1];
+  int count;
+};
+
+__device__ __forceinline__ int multi_tensor_of(const MultiQuant& m, int64_t k) {
+  int t = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxMultiTensors; ++i)
+    if (i < m.count && k >= m.chunk_begin[i]) t = i;
+  return t;
+}
+
+// Producer side for the multi-tensor passes (same pacing as stream_produce).
+__device__ __forceinline__ void multi_produce(const MultiQuant& m, uint8_t* bufs, uint64_t* full, uint64_t* empty,
+                                              volatile int* abort_flag, int* err) {
+  int64_t issued = 0;
+  for (int64_t k = blockIdx.x; k < m.chunk_begin[m.count]; k += gridDim.x, ++issued) {
+    const int stage = static_cast<int>(issued % kStreamStages);
+    if (issued >= kStreamStages &&
+        !mbar_wait(&empty[stage], static_cast<uint32_t>((issued / kStreamStages - 1) & 1), abort_flag, err,
+                   kErrTimeoutQuant))
+      break;
+    const int t = multi_tensor_of(m, k);
+    const int64_t off = (k - m.chunk_begin[t]) * kStreamChunkBytes;
+    const int64_t left = m.main_bytes[t] - off;
+    const uint32_t bytes = static_cast<uint32_t>(left < kStreamChunkBytes ? left : kStreamChunkBytes);
+    mbar_arrive_expect_tx(&full[stage], bytes);
+    bulk_load_1d(bufs + stage * kStreamChunkBytes, reinterpret_cast<const uint8_t*>(m.x[t]) + off, bytes,
+                 &full[stage]);
+  }
+  if (*abort_flag) {
+    volatile int never = 0;
+    const int64_t first = issued > kStreamStages ? issued - kStreamStages : 0;
+    for (int64_t i = first; i < issued; ++i)
+      mbar_wait(&full[i % kStreamStages], static_cast<uint32_t>((i / kStreamStages) & 1), &never, err,
+                kErrTimeoutDrain);
+  }
+}
+
+__device__ __forceinline__ void multi_init(uint64_t* full, uint64_t* empty, int* abort_flag) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStreamStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kStreamConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+}
+
+// partials[t * gridDim.x + cta] = max |x_t| over the chunks of tensor t this CTA streamed.
+__global__ void __launch_bounds__(kStreamThreads) quant_multi_amax_kernel(MultiQuant m, float* __restrict__ partials,
+                                                                          int* err) {
+  extern __shared__ __align__(128) uint8_t stream_smem[];
+  uint8_t* bufs = stream_smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stream_smem + kStreamStages * kStreamChunkBytes);
+  uint64_t* empty = full + kStreamStages;
+  __shared__ int abort_flag;
+  multi_init(full, empty, &abort_flag);
+  uint32_t m2[kMaxMultiTensors] = {0u, 0u, 0u, 0u};
+  if (threadIdx.x == kStreamConsumers) {
+    multi_produce(m, bufs, full, empty, &abort_flag, err);
+  } else if (threadIdx.x < kStreamConsumers) {
+    const int t0 = threadIdx.x;
+    int64_t i = 0;
+    for (int64_t k = blockIdx.x; k < m.chunk_begin[m.count]; k += gridDim.x, ++i) {
+      const int stage = static_cast<int>(i % kStreamStages);
+      const bool ok = mbar_wait(&full[stage], static_cast<uint32_t>((i / kStreamStages) & 1), &abort_flag, err,
+                                kErrTimeoutQuant);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int t = multi_tensor_of(m, k);
+      const int64_t off = (k - m.chunk_begin[t]) * kStreamChunkBytes;
+      const int64_t left = m.main_bytes[t] - off;
+      const int nv = static_cast<int>((left < kStreamChunkBytes ? left : kStreamChunkBytes) >> 4);
+      const uint8_t* buf = bufs + stage * kStreamChunkBytes;
+      uint32_t mv = 0u;
+#pragma unroll
+      for (int j = 0; j < kStreamVecPerThread; ++j) {
+        const int v = t0 + j * kStreamConsumers;
+        if (v < nv) mv = bf16x2_max(mv, absmax_vec2(ld_shared_v4(buf + v * 16)));
+      }
+      __syncwarp();
+      if ((t0 & 31) == 0) mbar_arrive(&empty[stage]);
+#pragma unroll
+      for (int u = 0; u < kMaxMultiTensors; ++u)
+        if (u == t) m2[u] = bf16x2_max(m2[u], mv);
+    }
+  }
+  for (int u = 0; u < m.count; ++u) {
+    float mu = unpack_max2(m2[u]);
+    if (blockIdx.x == 0)
+      for (int64_t e = (m.main_bytes[u] >> 1) + threadIdx.x; e < m.n[u]; e += kStreamThreads)
+        mu = fmaxf(mu, fabsf(__uint_as_float(uint32_t(m.x[u][e]) << 16)));
+    mu = block_max<kStreamThreads>(mu);
+    if (threadIdx.x == 0) partials[u * gridDim.x + blockIdx.x] = mu;
+  }
+}
+
+// Cast pass: scale_t = fold(partials[t * n_partials .. +n_partials]); CTA 0 publishes them.
+__global__ void __launch_bounds__(kStreamThreads) quant_multi_cast_kernel(MultiQuant m,
+                                                                          const float* __restrict__ partials,
+                                                                          int n_partials, int* err) {
+  extern __shared__ __align__(128) uint8_t stream_smem[];
+  uint8_t* bufs = stream_smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stream_smem + kStreamStages * kStreamChunkBytes);
+  uint64_t* empty = full + kStreamStages;
+  __shared__ int abort_flag;
+  float sc[kMaxMultiTensors] = {1.0f, 1.0f, 1.0f, 1.0f};
+  for (int u = 0; u < m.count; ++u) {
+    const float su = fold_partials_to_scale<kStreamThreads>(partials + u * n_partials, n_partials);
+#pragma unroll
+    for (int w = 0; w < kMaxMultiTensors; ++w)
+      if (w == u) sc[w] = su;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *m.scale_out[u] = su;
+  }
+  multi_init(full, empty, &abort_flag);
+  if (threadIdx.x == kStreamConsumers) {
+    multi_produce(m, bufs, full, empty, &abort_flag, err);
+  } else if (threadIdx.x < kStreamConsumers) {
+    const int t0 = threadIdx.x;
+    int64_t i = 0;
+    for (int64_t k = blockIdx.x; k < m.chunk_begin[m.count]; k += gridDim.x, ++i) {
+      const int stage = static_cast<int>(i % kStreamStages);
+      const bool ok = mbar_wait(&full[stage], static_cast<uint32_t>((i / kStreamStages) & 1), &abort_flag, err,
+                                kErrTimeoutQuant);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int t = multi_tensor_of(m, k);
+      const int64_t off = (k - m.chunk_begin[t]) * kStreamChunkBytes;
+      const int64_t left = m.main_bytes[t] - off;
+      const int nv = static_cast<int>((left < kStreamChunkBytes ? left : kStreamChunkBytes) >> 4);
+      const uint8_t* buf = bufs + stage * kStreamChunkBytes;
+      uint4 a[kStreamVecPerThread];
+#pragma unroll
+      for (int j = 0; j < kStreamVecPerThread; ++j) {
+        const int v = t0 + j * kStreamConsumers;
+        a[j] = v < nv ? ld_shared_v4(buf + v * 16) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+      if ((t0 & 31) == 0) mbar_arrive(&empty[stage]);
+      float s = sc[0];
+#pragma unroll
+      for (int w = 1; w < kMaxMultiTensors; ++w)
+        if (w == t) s = sc[w];
+      uint2* qv = reinterpret_cast<uint2*>(m.q[t] + (off >> 1));
+      if (markstein_applies(s)) {  // uniform over the chunk: no divergence
+        const CastMarkstein d = make_markstein(s);
+#pragma unroll
+        for (int j = 0; j < kStreamVecPerThread; ++j) {
+          const int v = t0 + j * kStreamConsumers;
+          if (v < nv) qv[v] = cast_vec(a[j], d);
+        }
+      } else {
+        const DivF64 d(s);
+#pragma unroll
+        for (int j = 0; j < kStreamVecPerThread; ++j) {
+          const int v = t0 + j * kStreamConsumers;
+          if (v < nv) qv[v] = cast_vec(a[j], d);
+        }
+      }
+    }
+  }
+  if (blockIdx.x == 0) {
+    for (int u = 0; u < m.count; ++u) {
+      float s = sc[0];
+#pragma unroll
+      for (int w = 1; w < kMaxMultiTensors; ++w)
+        if (w == u) s = sc[w];
+      for (int64_t e = (m.main_bytes[u] >> 1) + threadIdx.x; e < m.n[u]; e += kStreamThreads) {
+        const uint32_t wv = m.x[u][e];
+        m.q[u][e] = static_cast<uint8_t>((markstein_applies(s) ? make_markstein(s).word(wv) : DivF64(s).word(wv)) &
+                                         0xFFu);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- byte transposes
 // dst[b][c][r] = src[b][r][c] for a batch of R x C byte matrices with arbitrary
 // leading dimensions.  Used for the conv weight re-layout

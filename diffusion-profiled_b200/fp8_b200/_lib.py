@@ -67,6 +67,9 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "fp8_set_tile_override": (c_int, [c_int, c_int, c_int]),
     "fp8_set_quantize_override": (c_int, [c_int, c_int]),
+    "fp8_quantize_multi_workspace_bytes": (c_size_t, [c_int]),
+    "fp8_quantize_current_multi": (c_int, [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
+                                           POINTER(c_int64), c_void_p, c_size_t, c_void_p]),
     "fp8_gn_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_fwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_float,
                                c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),

@@ -117,10 +117,16 @@ def conv2d_fwd_fp8_prequantized(
     return ops.conv3x3_fwd(_cl(x), _cl(weight), x_scale, weight_scale)
 
 
+def _quantize_fp8_pair(x: torch.Tensor, weight: torch.Tensor):
+    """quantize_fp8(x), quantize_fp8(weight) (same asserts, same bytes) in one pair of launches."""
+    for t in (x, weight):
+        assert t.dtype == torch.bfloat16 and t.is_cuda and t.ndim == 4, f"{t.dtype} {t.is_cuda} {t.ndim}"
+    return ops.quantize_current_pair(x, weight)
+
+
 def conv2d_fwd_fp8(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """fp8_kernels.py:642-650."""
-    x_fp8, x_scale = quantize_fp8(x)
-    weight_fp8, weight_scale = quantize_fp8(weight)
+    x_fp8, x_scale, weight_fp8, weight_scale = _quantize_fp8_pair(x, weight)
     return conv2d_fwd_fp8_prequantized(x_fp8, weight_fp8, x_scale, weight_scale)
 
 
@@ -218,8 +224,7 @@ class Conv2dFP8Specialized(torch.autograd.Function):
             ctx.window_pos = window_pos
             ctx.save_for_backward(x_fp8, weight_fp8, x_scale, weight_scale, dy_scale_hist)
         else:
-            x_fp8, x_scale = quantize_fp8(x)
-            weight_fp8, weight_scale = quantize_fp8(_cl(weight))
+            x_fp8, x_scale, weight_fp8, weight_scale = _quantize_fp8_pair(x, _cl(weight))
             ctx.save_for_backward(x_fp8, weight_fp8, x_scale, weight_scale)
 
         out = conv2d_fwd_fp8_prequantized(x_fp8, weight_fp8, x_scale, weight_scale)

@@ -30,8 +30,7 @@ class _FP8LinearFn(torch.autograd.Function):
     def forward(ctx: Any, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, silu: bool):
         x2 = x.to(torch.bfloat16).reshape(-1, x.shape[-1]).contiguous()
         w = weight.to(torch.bfloat16).contiguous()
-        xq, sx = ops.quantize_current(x2)
-        wq, sw = ops.quantize_current(w)
+        xq, sx, wq, sw = ops.quantize_current_pair(x2, w)
         b = None if bias is None else bias.to(torch.bfloat16).contiguous()
         if silu and b is None:
             raise RuntimeError("the fused SiLU epilogue needs a bias")

@@ -80,6 +80,37 @@ def _(x):
     )
 
 
+@torch.library.custom_op("fp8_b200::quantize_current_pair", mutates_args=())
+def quantize_current_pair(x: torch.Tensor, w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                                                     torch.Tensor]:
+    """quantize_current of two tensors (a layer's input and weight) in one amax and one
+    cast launch -> (xq, sx, wq, sw); bytes and scales as two quantize_current calls."""
+    dev = _require_cuda(x, w)
+    for t in (x, w):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"quantize expects bfloat16, got {t.dtype}")
+        if not (t.is_contiguous() or t.is_contiguous(memory_format=torch.channels_last)):
+            raise RuntimeError("quantize expects a dense (contiguous or channels_last) tensor")
+    qs = [torch.empty_like(t, dtype=FP8_DTYPE, memory_format=torch.preserve_format) for t in (x, w)]
+    scales = [torch.empty((), device=dev, dtype=torch.float32) for _ in range(2)]
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_quantize_multi_workspace_bytes(2) // 4, 1), device=dev, dtype=torch.float32)
+        xs = (c_void_p * 2)(x.data_ptr(), w.data_ptr())
+        qp = (c_void_p * 2)(qs[0].data_ptr(), qs[1].data_ptr())
+        sp = (c_void_p * 2)(scales[0].data_ptr(), scales[1].data_ptr())
+        ns = (ctypes.c_int64 * 2)(x.numel(), w.numel())
+        _lib.check(lib.fp8_quantize_current_multi(2, xs, qp, sp, ns, _ptr(ws), ws.numel() * 4, _stream(dev)),
+                   "fp8_quantize_current_multi")
+    return qs[0], scales[0], qs[1], scales[1]
+
+
+@quantize_current_pair.register_fake
+def _(x, w):
+    return (torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format), x.new_empty((), dtype=torch.float32),
+            torch.empty_like(w, dtype=FP8_DTYPE, memory_format=torch.preserve_format), w.new_empty((), dtype=torch.float32))
+
+
 @torch.library.custom_op("fp8_b200::quantize_delayed", mutates_args=())
 def quantize_delayed(x: torch.Tensor, prev_scale: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Cast with ``prev_scale``; also return the scale of x's own amax (fp8_kernels.py:518-556)."""

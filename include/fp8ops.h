@@ -94,6 +94,18 @@ int fp8_quantize_current_noalloc(const void* x_bf16, void* q_e4m3, float* scale_
  * *scale_curr_out = scale of x's own amax.
  * Replaces quantize_fp8_delayed (fp8_kernels.py:518-556) and
  * partial_amax_kernel_delayed (:69-87) + finalize_amax_kernel (:90-102). */
+/* Workspace bytes of fp8_quantize_current_multi for `count` tensors. */
+size_t fp8_quantize_multi_workspace_bytes(int count);
+
+/* fp8_quantize_current on `count` (1..4) tensors at once: one amax launch and one
+ * cast launch stream all of them, each tensor keeps its own amax and scale and
+ * gets exactly the bytes fp8_quantize_current would write.  The reference
+ * quantizes a conv's input and weight back to back (fp8_kernels.py:642-650 ->
+ * quantize_fp8 :559-601, twice); this is that pair in two launches instead of
+ * four.  x[i], q[i], scale_out[i], n[i] as for fp8_quantize_current. */
+int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const* q_e4m3, float* const* scale_out,
+                               const int64_t* n, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
+
 int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_scale, float* scale_curr_out,
                          void* workspace, size_t workspace_bytes, int64_t n, fp8_stream_t stream);
 

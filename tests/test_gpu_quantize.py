@@ -194,3 +194,33 @@ def test_quantize_current_captured_in_cuda_graph(cuda):
     q_ref, s_ref = oracle.quantize_current(x.cpu())
     assert np.float32(s.item()).tobytes() == s_ref.tobytes()
     assert np.array_equal(_bytes(q), q_ref)
+
+
+@pytest.mark.parametrize("shapes", [
+    ((128, 128, 32, 32), (128, 128, 3, 3)),   # config 2 input and weight
+    ((2, 3, 4, 5), (7, 11)),                  # ragged tails in both
+    ((1, 1, 1, 8192 * 3 + 5), (0,)),          # an empty tensor
+])
+def test_quantize_current_pair_matches_two_calls(cuda, shapes):
+    from fp8_b200 import ops
+
+    x = _gen(shapes[0], seed=41, scale=3.0)
+    w = _gen(shapes[1], seed=42, scale=0.05) if shapes[1] != (0,) else torch.empty(0, dtype=torch.bfloat16, device=cuda)
+    xq, sx, wq, sw = ops.quantize_current_pair(x, w)
+    for q, s, t in ((xq, sx, x), (wq, sw, w)):
+        q_ref, s_ref = oracle.quantize_current(t.cpu())
+        assert np.float32(s.item()).tobytes() == s_ref.tobytes()
+        assert np.array_equal(_bytes(q), q_ref)
+
+
+def test_quantize_current_pair_unaligned_falls_back(cuda):
+    from fp8_b200 import ops
+
+    base = _gen((1, 1, 1, 4099), seed=43)
+    x = base[..., 1:]
+    w = _gen((64, 64, 3, 3), seed=44, scale=0.05)
+    xq, sx, wq, sw = ops.quantize_current_pair(x, w)
+    for q, s, t in ((xq, sx, x), (wq, sw, w)):
+        q_ref, s_ref = oracle.quantize_current(t.cpu())
+        assert np.float32(s.item()).tobytes() == s_ref.tobytes()
+        assert np.array_equal(_bytes(q), q_ref)
