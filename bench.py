@@ -163,10 +163,21 @@ def make_weight(device, seed: int = 1234):
     return conv.weight.detach().to(torch.bfloat16).contiguous(memory_format=torch.channels_last).to(device)
 
 
+def json_stdout():
+    """A file on the process's original stdout, for the one JSON line.  File
+    descriptor 1 itself is pointed at stderr, so text that native libraries print
+    to stdout (NCCL's version banner, for one) cannot mix with that line."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 # ============================================================================ B200 arm
 def run_b200(args) -> None:
     import torch.distributed as dist
 
+    result_out = json_stdout()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -333,7 +344,7 @@ def run_b200(args) -> None:
             "cpu_baseline": cpu,
             "unet_train": unet,
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=result_out, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -59,8 +59,10 @@ class BucketedAllReduce:
     Buckets are filled in reverse parameter order (roughly the order backward
     produces gradients).  For each bucket a hook counts the gradients that have
     been accumulated; the last one launches, on ``comm_stream``, the pack to a
-    flat bf16 buffer, ``all_reduce(SUM)``, and the unpack ``grad = flat / world``.
-    ``finish()`` makes the current stream wait for the side stream.
+    flat bf16 buffer (one cat), the all-reduce (NCCL averages in the collective;
+    other backends sum, then scale), and the unpack into the fp32 gradients (one
+    multi-tensor copy).  ``finish()`` makes the current stream wait for the side
+    stream.
     """
 
     def __init__(self, params: list[torch.nn.Parameter], group=None, bucket_bytes: int = 25 << 20):
@@ -86,6 +88,15 @@ class BucketedAllReduce:
         for i, b in enumerate(self.buckets):
             for p in b:
                 self.bucket_of[p] = i
+        # per-bucket views of the flat buffer, one per gradient (for the multi-tensor unpack)
+        self.views = []
+        for b, flat in zip(self.buckets, self.flat):
+            off, vs = 0, []
+            for p in b:
+                vs.append(flat[off:off + p.numel()].view(p.shape))
+                off += p.numel()
+            self.views.append(vs)
+        self.avg_in_collective = dist.get_backend(group) == "nccl"
         self.handles = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
         self.launched = 0
 
@@ -105,12 +116,12 @@ class BucketedAllReduce:
     def _reduce(self, i: int) -> None:
         bucket, flat = self.buckets[i], self.flat[i]
         torch.cat([p.grad.reshape(-1) for p in bucket], out=flat)  # fp32 -> bf16 pack
-        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
-        off = 0
-        for p in bucket:
-            n = p.numel()
-            p.grad.copy_(flat[off:off + n].view_as(p.grad)).div_(self.world)
-            off += n
+        if self.avg_in_collective:
+            dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=self.group)
+        else:
+            dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+            flat.div_(self.world)
+        torch._foreach_copy_([p.grad for p in bucket], self.views[i])  # bf16 -> fp32 unpack
 
     def _launch(self, i: int) -> None:
         if self.comm_stream is None:
