@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-unet", action="store_true", help="skip the UNet training-step measurement")
+    ap.add_argument("--bucket-mb", type=float, default=None,
+                    help="gradient all-reduce bucket size of the data-parallel UNet step (MB of bf16)")
     ap.add_argument("--unet-steps", type=int, default=30, help="timed UNet training steps")
     return ap.parse_args()
 
@@ -478,7 +480,10 @@ def time_unet(args, dev, world, fp8: bool) -> dict:
     # the B200 path: FP8 convs + fused norm/activation ops; the comparison: the
     # reference's bf16 model with its torch ops
     model = build_model(fp8=fp8, scaling="delayed", device=dev, seed=0, fused_norm=fp8)
-    step = GraphedTrainStep(model, TrainConfig(batch_size=args.batch), dev)
+    cfg = TrainConfig(batch_size=args.batch)
+    if args.bucket_mb:
+        cfg.allreduce_bucket_mb = args.bucket_mb
+    step = GraphedTrainStep(model, cfg, dev)
     torch.manual_seed(100 + rank)
     step.prepare()
     g = torch.Generator().manual_seed(200 + rank)

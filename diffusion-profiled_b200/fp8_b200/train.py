@@ -9,7 +9,7 @@ loss of ddpm.py:174-215):
     -> fused AdamW -> EMA of the weights (beta 0.9999)
 
 Data parallelism: every rank holds a full replica and its own batch.  The
-gradients are averaged with NCCL all-reduces of bf16 buckets (~25 MB), each
+gradients are averaged with NCCL all-reduces of bf16 buckets (4 MB), each
 launched on a side stream as soon as backward has produced every gradient of
 the bucket (post-accumulate-grad hooks), so the exchange overlaps the rest of
 backward; the step joins the side stream before clipping.  FP8 scales and the
@@ -152,6 +152,7 @@ class TrainConfig:
     ema_beta: float = 0.9999
     grad_clip: float = 1.0
     warmup_iters: int = 3
+    allreduce_bucket_mb: float = 4.0  # bf16 gradient bucket size of the data-parallel all-reduce (4 MB: 18.25 ms vs 18.47 ms at 25 MB, 2 x B200)
 
 
 class EMA:
@@ -179,7 +180,8 @@ class GraphedTrainStep:
         self.params = [p for p in model.parameters() if p.requires_grad]
         self.opt = torch.optim.AdamW(self.params, lr=cfg.lr, fused=True, capturable=True)
         self.ema = EMA(model, cfg.ema_beta)
-        self.dp = BucketedAllReduce(self.params, dp_group) if dist.is_initialized() and \
+        self.dp = BucketedAllReduce(self.params, dp_group, int(cfg.allreduce_bucket_mb * (1 << 20))) \
+            if dist.is_initialized() and \
             dist.get_world_size(dp_group) > 1 else None
         cin, res = model.config.in_channels, model.config.in_resolution
         self.static_batch = torch.zeros(cfg.batch_size, cin, res, res, device=device).to(
