@@ -387,8 +387,6 @@ def time_kernels(args, dev, w, sets) -> dict:
         xq, sx = ops.quantize_current(x)
         wq, sw = ops.quantize_current(w)
         dyq, sdy = ops.quantize_current(dy)
-        wt = torch.empty((cin, 9 * cout), device=dev, dtype=torch.float8_e4m3fn)  # dgrad's K-major weights
-        _lib.call("fp8_conv_weight_transpose", p(wq), p(wt), cout, cin, stream())
         y = torch.empty((b, cout, h, wd), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
         dx = torch.empty((b, cin, h, wd), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
         dw = torch.empty((cout, cin, 3, 3), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
@@ -397,7 +395,7 @@ def time_kernels(args, dev, w, sets) -> dict:
         q_out = torch.empty_like(x, dtype=torch.float8_e4m3fn)
         s_out = torch.empty((), device=dev, dtype=torch.float32)
         qws = torch.empty(lib.fp8_quantize_workspace_bytes(x.numel()) // 4 + 1, device=dev, dtype=torch.float32)
-        ops_in.append(dict(x=x, xq=xq, sx=sx, wq=wq, sw=sw, dyq=dyq, sdy=sdy, wt=wt, y=y, dx=dx, dw=dw, ws=ws,
+        ops_in.append(dict(x=x, xq=xq, sx=sx, wq=wq, sw=sw, dyq=dyq, sdy=sdy, y=y, dx=dx, dw=dw, ws=ws,
                            q_out=q_out, s_out=s_out, qws=qws))
     torch.cuda.synchronize()
 
@@ -408,8 +406,9 @@ def time_kernels(args, dev, w, sets) -> dict:
         "conv3x3_fwd (conv_halo_t_fp8_kernel)": lambda o: _lib.check(lib.fp8_conv3x3_fwd(
             p(o["xq"]), p(o["wq"]), p(o["y"]), p(o["sx"]), p(o["sw"]), c_void_p(0), 0, b, h, wd, cin, cout,
             stream()), "fwd"),
-        "conv3x3_dgrad (conv_halo_t_fp8_kernel)": lambda o: _lib.check(lib.fp8_conv3x3_dgrad(
-            p(o["dyq"]), p(o["wt"]), p(o["dx"]), p(o["sdy"]), p(o["sw"]), b, h, wd, cin, cout, stream()), "dgrad"),
+        "conv3x3_dgrad (conv_halo_t_fp8_kernel, weights read in place)": lambda o: _lib.check(
+            lib.fp8_conv3x3_dgrad_w(p(o["dyq"]), p(o["wq"]), p(o["dx"]), p(o["sdy"]), p(o["sw"]), b, h, wd, cin,
+                                    cout, c_void_p(0), 0, stream()), "dgrad"),
         "conv3x3_wgrad (memset + wgrad_fp8_kernel halo + convert)": lambda o: _lib.check(lib.fp8_conv3x3_wgrad(
             p(o["xq"]), p(o["dyq"]), p(o["dw"]), p(o["sx"]), p(o["sdy"]), b, h, wd, cin, cout, 0, p(o["ws"]),
             o["ws"].numel() * 4, stream()), "wgrad"),
@@ -449,7 +448,7 @@ def roofline(kernels: dict, peaks: dict, batch: int) -> dict | None:
     algo = {
         "quantize_current (quant_stream_kernel amax + cast, 2 launches)": ("hbm", pix * cin * 3.0),  # read bf16 once + write e4m3
         "conv3x3_fwd (conv_halo_t_fp8_kernel)": ("tensor", flops),
-        "conv3x3_dgrad (conv_halo_t_fp8_kernel)": ("tensor", flops),
+        "conv3x3_dgrad (conv_halo_t_fp8_kernel, weights read in place)": ("tensor", flops),
         "conv3x3_wgrad (memset + wgrad_fp8_kernel halo + convert)": ("tensor", flops),
     }
     name = max(kernels, key=lambda k: kernels[k]["ms"])

@@ -21,6 +21,9 @@
 //   * The epilogue holds one output channel per thread and 32 pixels per
 //     tcgen05.ld; lane pairs swap halves so that every store is a 4-byte pair
 //     of channels, written straight to the NHWC bf16 output.
+//   * A_MN: the data-grad can take the forward's weights [Cout][3][3][Cin] as they
+//     are: per tap a 128 (Cout = K) x 128 (Cin = M) box is an MN-major UMMA A
+//     operand (M contiguous), so no transposed copy of the weights is needed.
 //   * Tiles are split across the persistent grid in whole rounds; the tiles
 //     left over after the last whole round are cut into 128-pixel halves
 //     (N = 128 MMAs), so no CTA ends a full tile behind the others.
@@ -58,7 +61,7 @@ struct HaloTConfig {
   static_assert((W * 128) % 1024 == 0 && kBoxBytes % 1024 == 0, "swizzle-atom alignment");
 };
 
-template <int W>
+template <int W, bool A_MN = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     conv_halo_t_fp8_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
                            const HaloTParams p) {
@@ -138,7 +141,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_arrive_expect_tx(&w_full[kw], 3 * Cfg::kWTapBytes);
         for (int kh = 0; kh < 3; ++kh) {
           const int tap = kh * 3 + kw;
-          tma_load_2d(w_smem + tap * Cfg::kWTapBytes, &tmap_w, &w_full[kw], tap * kKBlockBytes, nt * 128);
+          if (A_MN)  // 3-D map over [Cout][tap][Cin]: box (128 Cin, 1 tap, 128 Cout)
+            tma_load_3d(w_smem + tap * Cfg::kWTapBytes, &tmap_w, &w_full[kw], nt * 128, tap, 0);
+          else
+            tma_load_2d(w_smem + tap * Cfg::kWTapBytes, &tmap_w, &w_full[kw], tap * kKBlockBytes, nt * 128);
         }
       }
       int s = 0;
@@ -174,8 +180,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc256 = make_idesc_e4m3(128, 256, 0, 0);
-      constexpr uint32_t idesc128 = make_idesc_e4m3(128, 128, 0, 0);
+      constexpr uint32_t idesc256 = make_idesc_e4m3(128, 256, A_MN ? 1 : 0, 0);
+      constexpr uint32_t idesc128 = make_idesc_e4m3(128, 128, A_MN ? 1 : 0, 0);
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -205,7 +211,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t b_tap = box + row_in_box(kh) * W * 128;
 #pragma unroll
             for (int k = 0; k < kKBlockBytes / 32; ++k) {
-              const uint64_t adesc = make_smem_desc(w_tap + k * 32, 16, 1024);
+              // K-major A: a K step is 32 bytes along a row; MN-major A: 32 rows of 128 bytes.
+              const uint64_t adesc = A_MN ? make_smem_desc(w_tap + k * 4096, Cfg::kWTapBytes, 1024)
+                                          : make_smem_desc(w_tap + k * 32, 16, 1024);
               const uint64_t bdesc = make_smem_desc(b_tap + k * 32, 16, 1024);
               umma_f8(d_tmem, adesc, bdesc, idesc, first ? 0u : 1u);
               first = false;

@@ -307,10 +307,10 @@ int launch_halo_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   return FP8_OK;
 }
 
-template <int W>
+template <int W, bool A_MN = false>
 int launch_halo_t(const CUtensorMap& ma, const CUtensorMap& mw, HaloTParams p, int sm_count, cudaStream_t stream) {
   using Cfg = HaloTConfig<W>;
-  auto kern = conv_halo_t_fp8_kernel<W>;
+  auto kern = conv_halo_t_fp8_kernel<W, A_MN>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   // Every CTA keeps one column tile's weights resident: a whole number of CTAs per column tile.
   const int per_n = std::max(1, std::min(sm_count / p.num_n_tiles, p.full_tiles));
@@ -318,6 +318,24 @@ int launch_halo_t(const CUtensorMap& ma, const CUtensorMap& mw, HaloTParams p, i
   kern<<<per_n * p.num_n_tiles, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mw, p);
   count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
+  return FP8_OK;
+}
+
+// The forward's weights [Cout][3][3][Cin] as a 3-D map (Cin, tap, Cout) with box
+// (128, 1, 128): one tap's 128 x 128 block, Cout rows of 128 Cin bytes (the
+// data-grad's MN-major A operand).
+int make_map_weight_taps(CUtensorMap* map, const void* wq, int cout, int cin) {
+  EncodeTiledFn enc;
+  if (int s = get_encode_fn(&enc)) return s;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cin), 9u, static_cast<cuuint64_t>(cout)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cin), static_cast<cuuint64_t>(9) * cin};
+  cuuint32_t box[3] = {128u, 1u, 128u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(wq), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FP8_REQUIRE(r == CUDA_SUCCESS, FP8_ERR_CUDA, "cuTensorMapEncodeTiled(weight taps %dx9x%d) failed: %d", cout, cin,
+              (int)r);
   return FP8_OK;
 }
 
@@ -333,13 +351,17 @@ bool halo_t_applies(int height, int width, int c_red, int n_out, const void* out
 // [n_out][9*c_red]; out: NHWC bf16 [B*H*W][n_out].
 int launch_conv_halo(const void* act, const void* wmat, void* out, const float* sa, const float* sb,
                      const void* bias, int epilogue, int batch, int height, int width, int c_red, int n_out,
-                     bool fwd, int* err, int sm_count, cudaStream_t stream) {
+                     bool fwd, int* err, int sm_count, cudaStream_t stream, bool w_natural = false) {
   const int rows = 128 / width;
   const int64_t M = static_cast<int64_t>(batch) * height * width;
   if ((g_conv_algo == 0 || g_conv_algo == 4) && halo_t_applies(height, width, c_red, n_out, out)) {
     CUtensorMap ma, mw;
     if (int s = make_map_conv_halo(&ma, act, batch, height, width, c_red, 2 * rows)) return s;
-    if (int s = make_map_2d(&mw, wmat, n_out, 9ll * c_red, 128)) return s;
+    if (w_natural) {  // data-grad on the forward's [Cout = c_red][3][3][Cin = n_out] weights
+      if (int s = make_map_weight_taps(&mw, wmat, c_red, n_out)) return s;
+    } else {
+      if (int s = make_map_2d(&mw, wmat, n_out, 9ll * c_red, 128)) return s;
+    }
     HaloTParams t{};
     t.num_n_tiles = n_out / 128;
     t.full_tiles = static_cast<int>(M / 256);
@@ -353,9 +375,14 @@ int launch_conv_halo(const void* act, const void* wmat, void* out, const float* 
     t.out = static_cast<__nv_bfloat16*>(out);
     t.epilogue = epilogue;
     t.err = err;
+    if (w_natural) {
+      if (width == 32) return launch_halo_t<32, true>(ma, mw, t, sm_count, stream);
+      return launch_halo_t<16, true>(ma, mw, t, sm_count, stream);
+    }
     if (width == 32) return launch_halo_t<32>(ma, mw, t, sm_count, stream);
     return launch_halo_t<16>(ma, mw, t, sm_count, stream);
   }
+  FP8_REQUIRE(!w_natural, FP8_ERR_UNSUPPORTED, "natural-layout weights need the transposed halo kernel");
   const bool resident = (c_red == 128);
   // CTA pairs (only on request: measured slower than the single-CTA kernel on
   // config 2): 128 reduced channels, whole 128-column tiles, 256-pixel tiles
@@ -1237,6 +1264,52 @@ int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
+}
+
+}  // extern "C"
+
+// ======================================================================== data-grad on the forward's weights
+namespace {
+// Whether fp8_conv3x3_dgrad_w reads wq in place (the transposed halo kernel);
+// dx is 16-byte aligned by the entry point's own check.
+bool dgrad_reads_w_in_place(int height, int width, int cin, int cout) {
+  return (g_conv_algo == 0 || g_conv_algo == 4) && halo_applies(height, width) &&
+         (width == 32 || width == 16) && cout == 128 && cin % 128 == 0 && (height * width) % 256 == 0;
+}
+}  // namespace
+
+extern "C" {
+
+size_t fp8_conv3x3_dgrad_w_workspace_bytes(int batch, int height, int width, int cin, int cout) {
+  (void)batch;
+  if (cin <= 0 || cout <= 0 || dgrad_reads_w_in_place(height, width, cin, cout)) return 0;
+  return static_cast<size_t>(9) * cin * cout;
+}
+
+int fp8_conv3x3_dgrad_w(const void* dyq, const void* wq, void* dx, const float* sdy, const float* sw, int batch,
+                        int height, int width, int cin, int cout, void* workspace, size_t workspace_bytes,
+                        fp8_stream_t stream) {
+  ConvTile t;
+  if (int s = check_conv_args(batch, height, width, cin, cout, &t)) return s;
+  if (int s = check_scale_ptrs(sdy, sw)) return s;
+  FP8_REQUIRE(dyq && wq && dx, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(dyq, 16) && aligned(wq, 16) && aligned(dx, 16), FP8_ERR_INVALID_ARGUMENT,
+              "conv tensors must be 16-byte aligned");
+  const bool in_place = dgrad_reads_w_in_place(height, width, cin, cout);
+  const size_t need = in_place ? 0 : static_cast<size_t>(9) * cin * cout;
+  FP8_REQUIRE(in_place || (workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16)),
+              FP8_ERR_WORKSPACE, "data-grad workspace too small: need %zu bytes for the re-laid-out weights", need);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (in_place) {
+    DeviceState* st;
+    if (int s = device_state(&st)) return s;
+    if (int s = launch_conv_halo(dyq, wq, dx, sdy, sw, nullptr, kEpiNone, batch, height, width, cout, cin, false,
+                                 st->err_ptr, st->sm_count, cs, true))
+      return s;
+    return ok();
+  }
+  if (int s = fp8_conv_weight_transpose(wq, workspace, cout, cin, stream)) return s;
+  return fp8_conv3x3_dgrad(dyq, workspace, dx, sdy, sw, batch, height, width, cin, cout, stream);
 }
 
 }  // extern "C"

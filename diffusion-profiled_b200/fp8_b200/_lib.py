@@ -49,6 +49,12 @@ _SIGNATURES: dict[str, tuple] = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p],
     ),
+    "fp8_conv3x3_dgrad_w_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "fp8_conv3x3_dgrad_w": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t,
+         c_void_p],
+    ),
     "fp8_conv3x3_wgrad_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "fp8_conv3x3_wgrad": (
         c_int,

@@ -231,11 +231,13 @@ def conv3x3_dgrad(dyq: torch.Tensor, wq: torch.Tensor, sdy: torch.Tensor, sw: to
         raise RuntimeError(f"weight shape {tuple(wq.shape)} does not match Cout={cout} 3x3")
     dx = torch.empty((b, cin, h, w), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
     with torch.cuda.device(dev):
-        wt = torch.empty((cin, 9 * cout), device=dev, dtype=FP8_DTYPE)  # [Cin][3][3][Cout]
-        _lib.call("fp8_conv_weight_transpose", _ptr(wq), _ptr(wt), cout, cin, _stream(dev))
+        # The weights are read in place where the kernel allows it (no workspace);
+        # otherwise the library re-lays them out to [Cin][3][3][Cout] in the workspace.
+        ws_bytes = _lib.load().fp8_conv3x3_dgrad_w_workspace_bytes(b, h, w, cin, cout)
+        ws = torch.empty((ws_bytes,), device=dev, dtype=torch.uint8) if ws_bytes else None
         _lib.call(
-            "fp8_conv3x3_dgrad", _ptr(dyq), _ptr(wt), _ptr(dx), _ptr(sdy), _ptr(sw), b, h, w, cin, cout,
-            _stream(dev),
+            "fp8_conv3x3_dgrad_w", _ptr(dyq), _ptr(wq), _ptr(dx), _ptr(sdy), _ptr(sw), b, h, w, cin, cout,
+            _ptr(ws), ws_bytes, _stream(dev),
         )
     return dx
 

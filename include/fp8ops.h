@@ -133,6 +133,18 @@ int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8
 int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, const float* sw, const void* bias,
                     int epilogue, int batch, int height, int width, int cin, int cout, fp8_stream_t stream);
 
+/* Workspace bytes of fp8_conv3x3_dgrad_w (0 when it reads wq in place). */
+size_t fp8_conv3x3_dgrad_w_workspace_bytes(int batch, int height, int width, int cin, int cout);
+
+/* fp8_conv3x3_dgrad on the forward's weights wq [Cout][3][3][Cin]: where the
+ * transposed halo kernel applies (Cout = 128 at 32x32 and 16x16) it reads wq in
+ * place as an MN-major operand; otherwise it writes the [Cin][3][3][Cout]
+ * re-layout into the workspace first.  Same result as fp8_conv_weight_transpose
+ * followed by fp8_conv3x3_dgrad (reference fp8_kernels.py:671-709). */
+int fp8_conv3x3_dgrad_w(const void* dyq, const void* wq, void* dx, const float* sdy, const float* sw, int batch,
+                        int height, int width, int cin, int cout, void* workspace, size_t workspace_bytes,
+                        fp8_stream_t stream);
+
 /* dx[n,h,w,ci] = sum_{kh,kw,co} dyq[n,h+1-kh,w+1-kw,co] * wq[co,kh,kw,ci] * sdy * sw
  * dyq: NHWC e4m3 [B][H][W][Cout]; wq_t: [Cin][3][3][Cout] (fp8_conv_weight_transpose
  * of the forward's wq); dx: NHWC bf16 [B][H][W][Cin].

@@ -148,3 +148,19 @@ def test_ctypes_signatures_match_header_arity():
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), (name, len(params), len(args))
     assert ctypes.sizeof(ctypes.c_size_t) == 8
+
+
+def test_dgrad_w_workspace_sizing_and_check():
+    """The data-grad on the forward's weights needs no workspace where it reads
+    them in place (Cout = 128 at 32x32 / 16x16) and 9*Cin*Cout bytes otherwise;
+    a missing workspace is rejected on the host."""
+    lib = _lib.load()
+    assert lib.fp8_conv3x3_dgrad_w_workspace_bytes(4, 32, 32, 256, 128) == 0
+    assert lib.fp8_conv3x3_dgrad_w_workspace_bytes(4, 16, 16, 128, 128) == 0
+    assert lib.fp8_conv3x3_dgrad_w_workspace_bytes(4, 32, 32, 128, 256) == 9 * 128 * 256
+    assert lib.fp8_conv3x3_dgrad_w_workspace_bytes(4, 8, 8, 256, 256) == 9 * 256 * 256
+    fake = c_void_p(1 << 20)  # 16-byte aligned, never dereferenced: the call fails before any device work
+    status, code, msg = _status_and_message(
+        lib.fp8_conv3x3_dgrad_w, fake, fake, fake, fake, fake, 2, 8, 8, 256, 256, c_void_p(0), 0, c_void_p(0)
+    )
+    assert status == _lib.FP8_ERR_WORKSPACE and code == status and "workspace" in msg

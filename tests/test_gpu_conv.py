@@ -269,3 +269,43 @@ def test_conv_wgrad_tap_and_halo_paths(cuda, algo, cin, cout, h, w):
         _lib.set_conv_algo(0)
     assert oracle.max_rel_err(dw, ref) <= TOL
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("cin,h,w,b", [(128, 32, 32, 2), (256, 32, 32, 40), (256, 16, 16, 8), (512, 16, 16, 4)])
+def test_dgrad_reads_forward_weights_in_place(cuda, cin, h, w, b):
+    """Cout = 128: the transposed halo kernel takes the forward's weights
+    [Cout][3][3][Cin] as an MN-major operand.  Same products in the same order as
+    the re-laid-out [Cin][3][3][Cout] path, so the results are bit-identical."""
+    from ctypes import c_void_p
+
+    from fp8_b200 import _lib, ops
+
+    cout = 128
+    lib = _lib.load()
+    assert lib.fp8_conv3x3_dgrad_w_workspace_bytes(b, h, w, cin, cout) == 0
+    dyq, sdy = _rand_q((b, cout, h, w), seed=91 + cin, device=cuda, scale=1e-2)
+    wq, sw = _rand_q((cout, cin, 3, 3), seed=92 + h, device=cuda, scale=0.05)
+    p = lambda t: c_void_p(t.data_ptr())  # noqa: E731
+    st = c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
+    wt = torch.empty((cin, 9 * cout), device=cuda, dtype=torch.float8_e4m3fn)
+    _lib.call("fp8_conv_weight_transpose", p(wq), p(wt), cout, cin, st)
+    dx2 = torch.empty_like(dx)
+    _lib.call("fp8_conv3x3_dgrad", p(dyq), p(wt), p(dx2), p(sdy), p(sw), b, h, w, cin, cout, st)
+    torch.cuda.synchronize()
+    assert torch.equal(dx.view(torch.int16), dx2.view(torch.int16))
+    assert oracle.max_rel_err(dx, oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())) <= TOL
+    assert ops.device_error() == 0
+
+
+def test_dgrad_w_workspace_path(cuda):
+    """Cout = 256: the weights are re-laid out into the caller's workspace first."""
+    from fp8_b200 import _lib, ops
+
+    b, cin, cout, h, w = 2, 128, 256, 32, 32
+    assert _lib.load().fp8_conv3x3_dgrad_w_workspace_bytes(b, h, w, cin, cout) == 9 * cin * cout
+    dyq, sdy = _rand_q((b, cout, h, w), seed=95, device=cuda, scale=1e-2)
+    wq, sw = _rand_q((cout, cin, 3, 3), seed=96, device=cuda, scale=0.05)
+    dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
+    assert oracle.max_rel_err(dx, oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())) <= TOL
+    assert ops.device_error() == 0
