@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-unet", action="store_true", help="skip the UNet training-step measurement")
+    ap.add_argument("--pdl", type=int, default=0, choices=(0, 1, 2),
+                    help="programmatic dependent launch: 0 off (default), 1 tensor-core kernels, 2 every kernel")
     ap.add_argument("--bucket-mb", type=float, default=None,
                     help="gradient all-reduce bucket size of the data-parallel UNet step (MB of bf16)")
     ap.add_argument("--unet-steps", type=int, default=30, help="timed UNet training steps")
@@ -194,6 +196,8 @@ def run_b200(args) -> None:
     import fp8_b200  # noqa: F401  (loads libfp8ops.so, fails loudly without it)
     from fp8_b200 import _lib, ops
     from fp8_b200.fp8_kernels import triton_conv2d_fp8
+
+    _lib.set_pdl(args.pdl)
 
     batch = args.batch
     flops_conv = conv_flops(batch)
@@ -330,6 +334,8 @@ def run_b200(args) -> None:
                 "global_batch": batch * world,
                 **SHAPE,
                 "scaling": "current (per-tensor amax of X, W, dY each step)",
+                "launch": ("plain stream order", "programmatic dependent launch of the tensor-core kernels",
+                           "programmatic dependent launch of every kernel")[args.pdl],
                 "flops_per_step": step_flops,
                 "l2": f"{len(sets)} rotating input sets; per-step working set > 126 MB L2",
                 "parallelism": f"replicas x{world} (no collective on the path)",
@@ -547,19 +553,59 @@ def time_e2e(args, dev, world, conv_api, step_flops) -> dict:
     d2h = y_h.numel() * 2 + ((dx_h.numel() + dw_h.numel()) * 2 if args.workload == "layer" else 0)
     train = args.workload == "layer"
 
-    def one():
-        x = x_h.to(dev, non_blocking=True).permute(*nchw).requires_grad_(train)
-        wt = w_h.to(dev, non_blocking=True).permute(*nchw).requires_grad_(train)
-        y = conv_api(x, wt)
-        y_h.copy_(y.permute(*nhwc), non_blocking=True)
-        if train:
-            dy = dy_h.to(dev, non_blocking=True).permute(*nchw)
-            gx, gw = torch.autograd.grad(y, (x, wt), dy)
-            dx_h.copy_(gx.permute(*nhwc), non_blocking=True)
-            dw_h.copy_(gw.permute(*nhwc), non_blocking=True)
+    # Steps are pipelined over three streams, as a serving loop would run them:
+    # the host->device copy of step i+1 and the device->host copy of step i-1
+    # overlap the compute of step i (the two copy directions use separate copy
+    # engines).  Every step still copies all of its inputs in and all of its
+    # results out inside the timed region.
+    comp = torch.cuda.current_stream(dev)
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    slots = 2
+    x_d = [torch.empty(x_h.shape, dtype=torch.bfloat16, device=dev) for _ in range(slots)]
+    w_d = [torch.empty(w_h.shape, dtype=torch.bfloat16, device=dev) for _ in range(slots)]
+    dy_d = [torch.empty(dy_h.shape, dtype=torch.bfloat16, device=dev) for _ in range(slots)]
+    ready = [torch.cuda.Event() for _ in range(slots)]
+    free = [torch.cuda.Event() for _ in range(slots)]
 
-    for _ in range(3):
-        one()
+    def h2d_step(i):
+        s = i % slots
+        with torch.cuda.stream(copy_in):
+            copy_in.wait_event(free[s])  # step i - slots has finished reading this slot
+            x_d[s].copy_(x_h, non_blocking=True)
+            w_d[s].copy_(w_h, non_blocking=True)
+            if train:
+                dy_d[s].copy_(dy_h, non_blocking=True)
+            ready[s].record(copy_in)
+
+    def compute_step(i):
+        s = i % slots
+        comp.wait_event(ready[s])
+        x = x_d[s].permute(*nchw).requires_grad_(train)
+        wt = w_d[s].permute(*nchw).requires_grad_(train)
+        y = conv_api(x, wt)
+        outs = [(y, y_h)]
+        if train:
+            gx, gw = torch.autograd.grad(y, (x, wt), dy_d[s].permute(*nchw))
+            outs += [(gx, dx_h), (gw, dw_h)]
+        free[s].record(comp)
+        copy_out.wait_stream(comp)
+        with torch.cuda.stream(copy_out):
+            for t, host in outs:
+                host.copy_(t.permute(*nhwc), non_blocking=True)
+                t.record_stream(copy_out)
+
+    def run(n):
+        copy_in.wait_stream(comp)
+        for i in range(min(slots, n)):
+            h2d_step(i)
+        for i in range(n):
+            compute_step(i)
+            if i + slots < n:
+                h2d_step(i + slots)
+        comp.wait_stream(copy_out)
+        comp.wait_stream(copy_in)
+
+    run(3)
     torch.cuda.synchronize()
     k = max(5, min(args.steps, 50))
     if world > 1:
@@ -567,8 +613,7 @@ def time_e2e(args, dev, world, conv_api, step_flops) -> dict:
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record()
-    for _ in range(k):
-        one()
+    run(k)
     ev1.record()
     torch.cuda.synchronize()
     t = torch.tensor([ev0.elapsed_time(ev1)], device=dev, dtype=torch.float64)
@@ -578,7 +623,8 @@ def time_e2e(args, dev, world, conv_api, step_flops) -> dict:
     return {"value": round(world * step_flops * k / (ms * 1e-3) / 1e12, 3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": k,
             "ms_per_step": round(ms / k, 4),
-            "path": "fp8_kernels.triton_conv2d_fp8 + torch.autograd.grad, pinned host buffers"}
+            "path": ("fp8_kernels.triton_conv2d_fp8 + torch.autograd.grad, pinned host buffers; "
+                     "copies in / compute / copies out of consecutive steps on three streams")}
 
 
 # ============================================================================ CPU oracle (baseline / reference arm)

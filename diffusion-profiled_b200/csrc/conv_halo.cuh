@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_sync();
 
   // Column shift of the A box for column tap kw, and row shift (in image rows)
   // inside the box for row tap kh.  Forward reads input (h + kh - 1, w + kw - 1);
@@ -407,6 +408,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_sync();
 
   auto col_shift = [&](int kw) { return p.fwd ? kw - 1 : 1 - kw; };
   auto row_in_box = [&](int kh) { return p.fwd ? kh : 2 - kh; };

@@ -128,6 +128,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_sync();
 
   // Forward reads input (h + kh - 1, w + kw - 1); data-grad reads dY (h + 1 - kh, w + 1 - kw).
   auto col_shift = [&](int kw) { return p.fwd ? kw - 1 : 1 - kw; };

@@ -194,6 +194,46 @@ int make_map_conv(CUtensorMap* map, const void* ptr, int batch, int height, int 
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Programmatic dependent launch: 0 = plain stream order (the default), 1 = the
+// tensor-core kernels, 2 = every kernel.  Each kernel waits for its predecessor
+// (pdl_sync / pdl_wait) before touching global memory, so the attribute only
+// lets its CTAs start, and run their prologue, while the previous kernel's CTAs
+// drain.  Measured on B200: a conv kernel following another conv kernel gains
+// 0.5-1 us, but the quantize -> conv chains of a training step gain nothing
+// (their streaming kernels leave no SM free early), so it is off by default.
+int g_pdl = 0;
+
+enum KernelClass { kStreamingKernel = 0, kTensorKernel = 1 };
+
+// Launch `kern` on `stream`, with programmatic stream serialization when enabled
+// for its class, optionally as clusters of `cluster_x` CTAs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          int cluster_x, KernelClass cls, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (g_pdl == 2 || (g_pdl == 1 && cls == kTensorKernel)) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Batched byte transpose dst[b][c][r] = src[b][r][c]; whole 16-byte-aligned
 // 64x64 tiles take the vectorised kernel.
 int launch_transpose(const void* src, void* dst, int64_t rows, int64_t cols, int64_t src_ld, int64_t dst_ld,
@@ -204,14 +244,14 @@ int launch_transpose(const void* src, void* dst, int64_t rows, int64_t cols, int
   const bool tiles16 = rows % kTransTile == 0 && cols % kTransTile == 0 && src_ld % 16 == 0 && dst_ld % 16 == 0 &&
                        src_bstride % 16 == 0 && dst_bstride % 16 == 0 && aligned(src, 16) && aligned(dst, 16);
   if (tiles16)
-    transpose_u8_tiles16_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(src),
-                                                           static_cast<uint8_t*>(dst), src_ld, dst_ld, src_bstride,
-                                                           dst_bstride);
+    FP8_CUDA_TRY(launch_kernel(transpose_u8_tiles16_kernel, grid, dim3(256), 0, stream, 1, kStreamingKernel,
+                               static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), src_ld, dst_ld,
+                               src_bstride, dst_bstride));
   else
-    transpose_u8_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst),
-                                                  rows, cols, src_ld, dst_ld, src_bstride, dst_bstride);
+    FP8_CUDA_TRY(launch_kernel(transpose_u8_kernel, grid, dim3(256), 0, stream, 1, kStreamingKernel,
+                               static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, cols, src_ld, dst_ld,
+                               src_bstride, dst_bstride));
   count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
 
@@ -263,9 +303,9 @@ int launch_halo_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensor
   } else {
     grid = std::min(sm_count, p.num_m_tiles * p.num_n_tiles);
   }
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
+  FP8_CUDA_TRY(launch_kernel(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1, kTensorKernel, ma, mb,
+                             mo, p));
   count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
 
@@ -301,8 +341,8 @@ int launch_halo_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   // Every pair keeps one column tile's weights resident: a whole number of pairs per column tile.
   const int pair_tiles = p.num_m_tiles / 2;
   const int per_n = std::max(1, std::min(max_pairs / p.num_n_tiles, pair_tiles));
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * per_n * p.num_n_tiles), 1, 1);
-  FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, p));
+  FP8_CUDA_TRY(launch_kernel(kern, dim3(static_cast<unsigned>(2 * per_n * p.num_n_tiles)), dim3(kGemmThreads),
+                             Cfg::kSmemBytes, stream, 2, kTensorKernel, ma, mb, mo, p));
   count_launches(1);
   return FP8_OK;
 }
@@ -315,9 +355,9 @@ int launch_halo_t(const CUtensorMap& ma, const CUtensorMap& mw, HaloTParams p, i
   // Every CTA keeps one column tile's weights resident: a whole number of CTAs per column tile.
   const int per_n = std::max(1, std::min(sm_count / p.num_n_tiles, p.full_tiles));
   p.whole_tiles = (p.full_tiles / per_n) * per_n;
-  kern<<<per_n * p.num_n_tiles, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mw, p);
+  FP8_CUDA_TRY(launch_kernel(kern, dim3(per_n * p.num_n_tiles), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1,
+                             kTensorKernel, ma, mw, p));
   count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
 
@@ -429,9 +469,9 @@ int launch_kgemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   auto kern = kgemm_fp8_kernel<BM_SUB, BN, STAGES>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   const int grid = p.num_tiles < sm_count ? p.num_tiles : sm_count;
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mo, p);
+  FP8_CUDA_TRY(launch_kernel(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1, kTensorKernel, ma, mb,
+                             mo, p));
   count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
 
@@ -497,9 +537,9 @@ int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, const CUtens
   using Cfg = WGradConfig<G, HALO>;
   auto kern = wgrad_fp8_kernel<G, HALO>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-  kern<<<p.num_tiles * p.splits, kGemmThreads, Cfg::kSmemBytes, stream>>>(mdy, mb, mp, p);
+  FP8_CUDA_TRY(launch_kernel(kern, dim3(p.num_tiles * p.splits), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1,
+                             kTensorKernel, mdy, mb, mp, p));
   count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
 
@@ -555,10 +595,9 @@ int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const 
   int64_t blocks = (n4 + 255) / 256;
   if (blocks > 4 * sm_count) blocks = 4 * sm_count;
   if (blocks < 1) blocks = 1;
-  wgrad_reduce_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(partials, splits, count, sa, sb,
-                                                                    static_cast<__nv_bfloat16*>(out));
+  FP8_CUDA_TRY(launch_kernel(wgrad_reduce_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, 1,
+                             kStreamingKernel, partials, splits, count, sa, sb, static_cast<__nv_bfloat16*>(out)));
   count_launches(1);
-  FP8_CUDA_TRY(cudaGetLastError());
   return FP8_OK;
 }
 
@@ -586,9 +625,10 @@ int launch_gn_fwd(const TX* x, const GnShape& sh, float* part, const GnActParams
                                     static_cast<int>(s1)));
   FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_fwd_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(s2)));
-  gn_stats_kernel<TX><<<sh.n * sh.slices, kGnThreads, s1, cs>>>(x, sh, part);
-  gn_act_fwd_kernel<TX><<<sh.n * sh.slices, kGnThreads, s2, cs>>>(x, sh, part, q, stats,
-                                                                   static_cast<uint16_t*>(out));
+  const dim3 grid(static_cast<unsigned>(sh.n * sh.slices)), block(kGnThreads);
+  FP8_CUDA_TRY(launch_kernel(gn_stats_kernel<TX>, grid, block, s1, cs, 1, kStreamingKernel, x, sh, part));
+  FP8_CUDA_TRY(launch_kernel(gn_act_fwd_kernel<TX>, grid, block, s2, cs, 1, kStreamingKernel, x, sh,
+                             static_cast<const float*>(part), q, stats, static_cast<uint16_t*>(out)));
   count_launches(2);
   return FP8_OK;
 }
@@ -600,8 +640,11 @@ int launch_gn_bwd(const TX* x, const uint16_t* dy, const GnShape& sh, const floa
                                     static_cast<int>(s1)));
   FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_apply_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(s2)));
-  gn_act_bwd_reduce_kernel<TX><<<sh.n * sh.slices, kGnThreads, s1, cs>>>(x, dy, sh, stats, q, part);
-  gn_act_bwd_apply_kernel<TX><<<sh.n * sh.slices, kGnThreads, s2, cs>>>(x, dy, sh, stats, q, part, totals, dx);
+  const dim3 grid(static_cast<unsigned>(sh.n * sh.slices)), block(kGnThreads);
+  FP8_CUDA_TRY(launch_kernel(gn_act_bwd_reduce_kernel<TX>, grid, block, s1, cs, 1, kStreamingKernel, x, dy, sh, stats,
+                             q, part));
+  FP8_CUDA_TRY(launch_kernel(gn_act_bwd_apply_kernel<TX>, grid, block, s2, cs, 1, kStreamingKernel, x, dy, sh, stats, q,
+                             static_cast<const float*>(part), totals, dx));
   count_launches(2);
   return FP8_OK;
 }
@@ -646,8 +689,9 @@ int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const floa
                   const float* prev_scale, float* scale_out, float* partials_out, int* err, cudaStream_t cs) {
   FP8_CUDA_TRY(cudaFuncSetAttribute(quant_stream_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kStreamSmemBytes)));
-  quant_stream_kernel<KIND><<<grid, kStreamThreads, kStreamSmemBytes, cs>>>(x, q, n, partials_in, n_partials,
-                                                                             prev_scale, scale_out, partials_out, err);
+  FP8_CUDA_TRY(launch_kernel(quant_stream_kernel<KIND>, dim3(grid), dim3(kStreamThreads), kStreamSmemBytes, cs, 1,
+                             kStreamingKernel, x, q, n, partials_in, n_partials, prev_scale, scale_out, partials_out,
+                             err));
   return FP8_OK;
 }
 
@@ -663,9 +707,11 @@ int launch_quantize_current(const uint16_t* x, uint8_t* q, float* scale_out, flo
                                                   st->err_ptr, cs))
       return s;
   } else {
-    amax_partials_kernel<<<parts, kQuantThreads, 0, cs>>>(x, n, partials);
-    quantize_cast_kernel<kCurrent>
-        <<<cast_blocks, kQuantThreads, 0, cs>>>(x, q, n, partials, parts, nullptr, scale_out, nullptr);
+    FP8_CUDA_TRY(launch_kernel(amax_partials_kernel, dim3(parts), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel, x, n,
+                               partials));
+    FP8_CUDA_TRY(launch_kernel(quantize_cast_kernel<kCurrent>, dim3(cast_blocks), dim3(kQuantThreads), 0, cs, 1,
+                               kStreamingKernel, x, q, n, static_cast<const float*>(partials), parts,
+                               static_cast<const float*>(nullptr), scale_out, static_cast<float*>(nullptr)));
   }
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
@@ -835,10 +881,12 @@ int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_sca
                                                   st->err_ptr, cs))
       return s;
   } else {
-    quantize_cast_kernel<kDelayed>
-        <<<parts, kQuantThreads, 0, cs>>>(x, q, n, nullptr, 0, prev_scale, nullptr, partials);
+    FP8_CUDA_TRY(launch_kernel(quantize_cast_kernel<kDelayed>, dim3(parts), dim3(kQuantThreads), 0, cs, 1,
+                               kStreamingKernel, x, q, n, static_cast<const float*>(nullptr), 0, prev_scale,
+                               static_cast<float*>(nullptr), partials));
   }
-  finalize_scale_kernel<<<1, kQuantThreads, 0, cs>>>(partials, parts, scale_curr_out);
+  FP8_CUDA_TRY(launch_kernel(finalize_scale_kernel, dim3(1), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
+                             static_cast<const float*>(partials), parts, scale_curr_out));
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
@@ -1110,6 +1158,12 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
   return ok();
 }
 
+int fp8_set_pdl(int mode) {
+  FP8_REQUIRE(mode >= 0 && mode <= 2, FP8_ERR_INVALID_ARGUMENT, "pdl mode must be 0, 1 or 2");
+  g_pdl = mode;
+  return ok();
+}
+
 int fp8_set_conv_algo(int algo) {
   FP8_REQUIRE(algo >= 0 && algo <= 4, FP8_ERR_INVALID_ARGUMENT, "conv algo must be 0 (auto), 1, 2, 3 or 4");
   g_conv_algo = algo;
@@ -1259,8 +1313,10 @@ int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const
                                     static_cast<int>(kStreamSmemBytes)));
   FP8_CUDA_TRY(cudaFuncSetAttribute(quant_multi_cast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kStreamSmemBytes)));
-  quant_multi_amax_kernel<<<parts, kStreamThreads, kStreamSmemBytes, cs>>>(m, partials, st->err_ptr);
-  quant_multi_cast_kernel<<<cast_blocks, kStreamThreads, kStreamSmemBytes, cs>>>(m, partials, parts, st->err_ptr);
+  FP8_CUDA_TRY(launch_kernel(quant_multi_amax_kernel, dim3(parts), dim3(kStreamThreads), kStreamSmemBytes, cs, 1,
+                             kStreamingKernel, m, partials, st->err_ptr));
+  FP8_CUDA_TRY(launch_kernel(quant_multi_cast_kernel, dim3(cast_blocks), dim3(kStreamThreads), kStreamSmemBytes, cs, 1,
+                             kStreamingKernel, m, static_cast<const float*>(partials), parts, st->err_ptr));
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();

@@ -117,6 +117,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_sync();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -268,6 +269,7 @@ __global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restri
                                                            int64_t count, const float* __restrict__ sa,
                                                            const float* __restrict__ sb,
                                                            __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   const float scale = __ldg(sa) * __ldg(sb);
   const int64_t n4 = count >> 2;
   const float4* p4 = reinterpret_cast<const float4*>(partials);

@@ -214,6 +214,7 @@ template <typename TX>
 __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const TX* __restrict__ x, GnShape s,
                                                               float* __restrict__ part) {
   extern __shared__ float gn_smem[];
+  pdl_wait();
   const GnThread t = gn_thread(s);
   float acc[2][8] = {};
   if (t.r < t.rows) {
@@ -324,6 +325,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __rest
                                                                 float* __restrict__ stats,
                                                                 uint16_t* __restrict__ out) {
   extern __shared__ float gn_smem[];
+  pdl_wait();
   float* mean_g = gn_smem;
   float* rstd_g = mean_g + s.groups;
   float* A = rstd_g + s.groups;
@@ -389,6 +391,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
     GnActParams q, float* __restrict__ part) {
   extern __shared__ float gn_smem[];
+  pdl_wait();
   float* A = gn_smem;
   float* B = A + s.c;
   float* az = B + s.c;
@@ -469,6 +472,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
     GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx) {
   extern __shared__ float gn_smem[];
+  pdl_wait();
   float* A = gn_smem;
   float* B = A + s.c;
   float* az = B + s.c;

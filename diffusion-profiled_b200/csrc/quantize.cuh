@@ -198,6 +198,7 @@ __device__ __forceinline__ uint2 cast_vec(const uint4& a, const Div& d) {
 // Pass 1 of current scaling: |x| max per CTA.
 __global__ void __launch_bounds__(kQuantThreads) amax_partials_kernel(const uint16_t* __restrict__ x, int64_t n,
                                                                       float* __restrict__ partials) {
+  pdl_wait();
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
   float m = 0.0f;
@@ -228,6 +229,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
     int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
     float* __restrict__ partials_out) {
+  pdl_wait();
   float s;
   if (MODE == kCurrent) {
     s = fold_partials_to_scale(partials_in, n_partials);
@@ -246,6 +248,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
 
 __global__ void __launch_bounds__(kQuantThreads) finalize_scale_kernel(const float* __restrict__ partials,
                                                                        int n_partials, float* __restrict__ scale_out) {
+  pdl_wait();
   const float s = fold_partials_to_scale(partials, n_partials);
   if (threadIdx.x == 0) *scale_out = s;
 }
@@ -393,6 +396,7 @@ __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
     int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
     float* __restrict__ partials_out, int* err) {
   extern __shared__ __align__(128) uint8_t stream_smem[];
+  pdl_wait();
   uint8_t* bufs = stream_smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stream_smem + kStreamStages * kStreamChunkBytes);
   uint64_t* empty = full + kStreamStages;
@@ -493,6 +497,7 @@ __device__ __forceinline__ void multi_init(uint64_t* full, uint64_t* empty, int*
 __global__ void __launch_bounds__(kStreamThreads) quant_multi_amax_kernel(MultiQuant m, float* __restrict__ partials,
                                                                           int* err) {
   extern __shared__ __align__(128) uint8_t stream_smem[];
+  pdl_wait();
   uint8_t* bufs = stream_smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stream_smem + kStreamStages * kStreamChunkBytes);
   uint64_t* empty = full + kStreamStages;
@@ -542,6 +547,7 @@ __global__ void __launch_bounds__(kStreamThreads) quant_multi_cast_kernel(MultiQ
                                                                           const float* __restrict__ partials,
                                                                           int n_partials, int* err) {
   extern __shared__ __align__(128) uint8_t stream_smem[];
+  pdl_wait();
   uint8_t* bufs = stream_smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stream_smem + kStreamStages * kStreamChunkBytes);
   uint64_t* empty = full + kStreamStages;
@@ -627,6 +633,7 @@ __global__ void __launch_bounds__(256) transpose_u8_kernel(const uint8_t* __rest
                                                            int64_t dst_ld, int64_t src_bstride,
                                                            int64_t dst_bstride) {
   __shared__ uint8_t tile[kTransTile][kTransTile + 4];
+  pdl_wait();
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kTransTile;
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * kTransTile;
   const uint8_t* s = src + static_cast<int64_t>(blockIdx.z) * src_bstride;
@@ -652,6 +659,7 @@ __global__ void __launch_bounds__(256) transpose_u8_tiles16_kernel(const uint8_t
                                                                    int64_t dst_ld, int64_t src_bstride,
                                                                    int64_t dst_bstride) {
   __shared__ __align__(16) uint8_t tile[kTransTile][kTransTile + 4];
+  pdl_wait();
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kTransTile;
   const int64_t c0 = static_cast<int64_t>(blockIdx.y) * kTransTile;
   const uint8_t* s = src + static_cast<int64_t>(blockIdx.z) * src_bstride;

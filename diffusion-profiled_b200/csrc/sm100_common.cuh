@@ -58,6 +58,24 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch.  Every kernel of this library calls pdl_sync()
+// before its first access to global memory: it waits until the previous kernel
+// on the stream has completed and its writes are visible, then allows the next
+// kernel's CTAs to be scheduled as this grid's CTAs exit (so their prologue —
+// barrier init, TMEM allocation, descriptor prefetch — overlaps this grid's
+// tail).  Because the trigger follows the wait, a kernel that passed pdl_sync()
+// also knows that every earlier kernel on the stream has completed.  Both
+// instructions are no-ops for a launch without programmatic serialization.
+__device__ __forceinline__ void pdl_sync() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// The wait alone: the next kernel may start only once this grid has exited (its
+// implicit trigger).  For kernels that share SMs with their successor's CTAs,
+// whose early arrival would only compete for the SM.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

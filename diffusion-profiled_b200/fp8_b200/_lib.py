@@ -83,6 +83,7 @@ _SIGNATURES: dict[str, tuple] = {
                                c_float, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                c_size_t, c_void_p]),
     "fp8_set_conv_algo": (c_int, [c_int]),
+    "fp8_set_pdl": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()
@@ -150,6 +151,12 @@ def kernel_launch_count() -> int:
 
 def set_tile_override(bm_sub: int = 0, bn: int = 0, wgrad_group: int = 0) -> None:
     check(load().fp8_set_tile_override(bm_sub, bn, wgrad_group), "fp8_set_tile_override")
+
+
+def set_pdl(mode: int = 0) -> None:
+    """0: plain stream order (the default); 1: programmatic dependent launch of
+    the tensor-core kernels; 2: of every kernel."""
+    check(load().fp8_set_pdl(int(mode)), "fp8_set_pdl")
 
 
 def set_conv_algo(algo: int = 0) -> None:

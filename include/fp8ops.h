@@ -202,6 +202,15 @@ int fp8_set_tile_override(int bm_sub, int bn, int wgrad_group);
  * Process-wide; meant for benchmarks and tests. */
 int fp8_set_conv_algo(int algo);
 
+/* Programmatic dependent launch.  Every kernel of the library waits for the
+ * previous kernel on its stream (griddepcontrol.wait) before its first global
+ * memory access; a kernel launched with programmatic stream serialization can
+ * therefore start, and set up shared memory, barriers and tensor memory, while
+ * the previous kernel drains.  mode 0 = plain stream order (the default), 1 = the
+ * attribute on the tensor-core kernels, 2 = on every kernel.  Process-wide;
+ * meant for benchmarks and tests. */
+int fp8_set_pdl(int mode);
+
 /* Tuning override for the quantize grids: CTAs per SM of the amax pass and of
  * the cast pass (1..8; 0 restores the built-in choice).  Process-wide. */
 int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);

@@ -309,3 +309,42 @@ def test_dgrad_w_workspace_path(cuda):
     dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
     assert oracle.max_rel_err(dx, oracle.conv_dx(dyq.cpu(), wq.cpu(), sdy.item(), sw.item())) <= TOL
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_launch_modes_give_the_same_results(cuda, mode):
+    """Programmatic dependent launch only changes when CTAs may start: a
+    quantize -> fwd -> quantize -> dX -> dW chain gives the same bytes as plain
+    stream order (dW up to the order of its fp32 split-K additions, i.e. one
+    bf16 rounding step)."""
+    from fp8_b200 import _lib, ops
+
+    g = torch.Generator().manual_seed(123)
+    x = torch.randn(8, 128, 32, 32, generator=g).to(torch.bfloat16).to(cuda).contiguous(
+        memory_format=torch.channels_last)
+    w = (torch.randn(128, 128, 3, 3, generator=g) * 0.05).to(torch.bfloat16).to(cuda).contiguous(
+        memory_format=torch.channels_last)
+    dy = (torch.randn(8, 128, 32, 32, generator=g) * 1e-2).to(torch.bfloat16).to(cuda).contiguous(
+        memory_format=torch.channels_last)
+
+    def chain():
+        xq, sx, wq, sw = ops.quantize_current_pair(x, w)
+        y = ops.conv3x3_fwd(xq, wq, sx, sw)
+        dyq, sdy = ops.quantize_current(dy)
+        dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
+        dw = ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+        torch.cuda.synchronize()
+        return dict(xq=xq.view(torch.uint8), sx=sx, y=y, dyq=dyq.view(torch.uint8), sdy=sdy, dx=dx, dw=dw)
+
+    ref = chain()
+    try:
+        _lib.set_pdl(mode)
+        got = chain()
+    finally:
+        _lib.set_pdl(0)
+    for k in ("xq", "sx", "y", "dyq", "sdy", "dx"):
+        assert torch.equal(ref[k], got[k]), k
+    a, b = ref["dw"].float(), got["dw"].float()
+    excess = (a - b).abs() - (2.0 ** -7 * a.abs() + 1e-4 * a.abs().max())
+    assert excess.max().item() <= 0.0, excess.max().item()
+    assert ops.device_error() == 0
