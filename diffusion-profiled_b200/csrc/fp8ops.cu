@@ -618,17 +618,17 @@ size_t gn_workspace(int n, int hw, int c, int sm_count) {
   return static_cast<size_t>(n) * gn_slices(n, hw, c, sm_count) * 3 * c * sizeof(float);
 }
 
-template <typename TX>
-int launch_gn_fwd(const TX* x, const GnShape& sh, float* part, const GnActParams& q, float* stats, void* out,
+template <typename TX, bool QUANT>
+int launch_gn_fwd(const TX* x, const GnShape& sh, float* part, const GnActParams& q, float* stats, const GnOut& o,
                   size_t s1, size_t s2, cudaStream_t cs) {
   FP8_CUDA_TRY(cudaFuncSetAttribute(gn_stats_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(s1)));
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_fwd_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_fwd_kernel<TX, QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(s2)));
   const dim3 grid(static_cast<unsigned>(sh.n * sh.slices)), block(kGnThreads);
   FP8_CUDA_TRY(launch_kernel(gn_stats_kernel<TX>, grid, block, s1, cs, 1, kStreamingKernel, x, sh, part));
-  FP8_CUDA_TRY(launch_kernel(gn_act_fwd_kernel<TX>, grid, block, s2, cs, 1, kStreamingKernel, x, sh,
-                             static_cast<const float*>(part), q, stats, static_cast<uint16_t*>(out)));
+  FP8_CUDA_TRY(launch_kernel(gn_act_fwd_kernel<TX, QUANT>, grid, block, s2, cs, 1, kStreamingKernel, x, sh,
+                             static_cast<const float*>(part), q, stats, o));
   count_launches(2);
   return FP8_OK;
 }
@@ -1208,11 +1208,57 @@ int fp8_gn_act_fwd(const void* x, int x_fp32, const float* gamma, const float* b
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
+  const GnOut o{static_cast<uint16_t*>(out), nullptr, nullptr, nullptr};
   if (x_fp32) {
-    if (int s = launch_gn_fwd(static_cast<const float*>(x), sh, part, q, stats, out, s1, s2, cs)) return s;
+    if (int s = launch_gn_fwd<float, false>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, cs)) return s;
   } else {
-    if (int s = launch_gn_fwd(static_cast<const uint16_t*>(x), sh, part, q, stats, out, s1, s2, cs)) return s;
+    if (int s = launch_gn_fwd<uint16_t, false>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2, cs))
+      return s;
   }
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  (void)cudaGetLastError();
+  if (n <= 0 || hw <= 0 || c < 8) return 0;
+  if (sms <= 0) sms = 148;
+  const int slices = gn_slices(n, hw, c, sms);
+  // group-norm partials, then one amax partial per apply CTA (16-byte aligned)
+  return gn_workspace(n, hw, c, sms) + ((static_cast<size_t>(n) * slices * sizeof(float) + 15) & ~size_t(15));
+}
+
+int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                         int film_ld, const int64_t* seed, float p, float eps, const float* prev_scale,
+                         float* stats, void* q_e4m3, float* scale_curr_out, int n, int hw, int c, int groups,
+                         void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+  if (int s = check_gn_args(x, q_e4m3, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
+  FP8_REQUIRE(stats != nullptr && prev_scale != nullptr && scale_curr_out != nullptr, FP8_ERR_INVALID_ARGUMENT,
+              "NULL stats or scale");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  GnShape sh{n, hw, c, groups, gn_slices(n, hw, c, st->sm_count)};
+  const size_t gn_bytes = gn_workspace(n, hw, c, st->sm_count);
+  const size_t need = gn_bytes + ((static_cast<size_t>(n) * sh.slices * sizeof(float) + 15) & ~size_t(15));
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
+              "group-norm workspace too small: need %zu bytes", need);
+  GnActParams q{gamma, beta, static_cast<const uint16_t*>(film), film_ld, seed, p, eps};
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  float* amax_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gn_bytes);
+  const GnOut o{nullptr, static_cast<uint8_t*>(q_e4m3), prev_scale, amax_part};
+  const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
+  if (x_fp32) {
+    if (int s = launch_gn_fwd<float, true>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, cs)) return s;
+  } else {
+    if (int s = launch_gn_fwd<uint16_t, true>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2, cs))
+      return s;
+  }
+  FP8_CUDA_TRY(launch_kernel(finalize_scale_kernel, dim3(1), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
+                             static_cast<const float*>(amax_part), n * sh.slices, scale_curr_out));
+  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }

@@ -28,6 +28,7 @@
 // graph draws a new mask each replay when the caller advances it.
 #pragma once
 
+#include "quantize.cuh"
 #include "sm100_common.cuh"
 
 namespace fp8b {
@@ -319,41 +320,29 @@ __device__ __forceinline__ void gn_coeffs(const GnShape& s, const GnActParams& q
 }
 
 // stats[n * 2G + {0, G} + g] = mean, rstd (written by slice 0 of each sample).
-template <typename TX>
-__global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __restrict__ x, GnShape s,
-                                                                const float* __restrict__ part, GnActParams q,
-                                                                float* __restrict__ stats,
-                                                                uint16_t* __restrict__ out) {
-  extern __shared__ float gn_smem[];
-  pdl_wait();
-  float* mean_g = gn_smem;
-  float* rstd_g = mean_g + s.groups;
-  float* A = rstd_g + s.groups;
-  float* B = A + s.c;
-  float* ch_mean = B + s.c;
-  float* ch_m2 = ch_mean + s.c;
-  const GnThread t = gn_thread(s);
-  gn_group_stats(x, part, s, t.n, q.eps, mean_g, rstd_g, ch_mean, ch_m2);
-  if (blockIdx.x % s.slices == 0)
-    for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
-      stats[static_cast<int64_t>(t.n) * 2 * s.groups + g] = mean_g[g];
-      stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g] = rstd_g[g];
-    }
-  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, nullptr, nullptr);
-  if (t.r >= t.rows) return;
-  float a[8], b[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    a[k] = A[t.v * 8 + k];
-    b[k] = B[t.v * 8 + k];
-  }
-  const bool drop = q.seed != nullptr && q.p > 0.0f;
-  const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
-  const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
-  const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
-  const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
-  const TX* xs = x + base * 8;
-  uint4* os = reinterpret_cast<uint4*>(out) + base;
+// Output of the apply pass.  QUANT = false: the bf16 activations.  QUANT =
+// true (the input of a delayed-scaling FP8 conv): their e4m3 bytes, cast with
+// the previous scale exactly as the delayed quantize pass casts a bf16 tensor
+// (reference quantize_fp8_delayed, fp8_kernels.py:518-556), and each CTA's max
+// |bf16 activation| for the current scale; the bf16 tensor is never written.
+struct GnOut {
+  uint16_t* bf16;           // NHWC bf16 (QUANT = false)
+  uint8_t* q;               // NHWC e4m3 (QUANT = true)
+  const float* prev_scale;  // dequant scale of the cast (QUANT = true)
+  float* amax_part;         // [grid] per-CTA max |activation| (QUANT = true)
+};
+
+// Plain bf16 stores: the Div of the non-quantizing instantiation.
+struct NoCast {};
+
+// The streaming loop of the apply pass over this thread's pixel rows; returns
+// the packed max |bf16 activation| (QUANT) or 0.
+template <typename TX, bool QUANT, class Div>
+__device__ __forceinline__ uint32_t gn_apply_rows(const TX* __restrict__ xs, const GnThread& t, int64_t base,
+                                                  const float (&a)[8], const float (&b)[8], bool drop,
+                                                  uint64_t seed, uint32_t thresh, float keep_scale, const GnOut& o,
+                                                  const Div& div) {
+  uint32_t m2 = 0u;
   for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollFwd * t.rows) {
     XVec<TX> v[kGnUnrollFwd];
 #pragma unroll
@@ -375,8 +364,65 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __rest
         const float act = silu_f32(z) * keep_scale;
         f[k] = (keep >> k) & 1u ? act : 0.0f;
       }
-      os[vi] = pack8(f);
+      const uint4 h = pack8(f);
+      if constexpr (QUANT) {
+        m2 = bf16x2_max(m2, absmax_vec2(h));
+        reinterpret_cast<uint2*>(o.q)[base + vi] = cast_vec(h, div);
+      } else {
+        reinterpret_cast<uint4*>(o.bf16)[base + vi] = h;
+      }
     }
+  }
+  return m2;
+}
+
+template <typename TX, bool QUANT>
+__global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __restrict__ x, GnShape s,
+                                                                const float* __restrict__ part, GnActParams q,
+                                                                float* __restrict__ stats, GnOut o) {
+  extern __shared__ float gn_smem[];
+  pdl_wait();
+  float* mean_g = gn_smem;
+  float* rstd_g = mean_g + s.groups;
+  float* A = rstd_g + s.groups;
+  float* B = A + s.c;
+  float* ch_mean = B + s.c;
+  float* ch_m2 = ch_mean + s.c;
+  const GnThread t = gn_thread(s);
+  gn_group_stats(x, part, s, t.n, q.eps, mean_g, rstd_g, ch_mean, ch_m2);
+  if (blockIdx.x % s.slices == 0)
+    for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
+      stats[static_cast<int64_t>(t.n) * 2 * s.groups + g] = mean_g[g];
+      stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g] = rstd_g[g];
+    }
+  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, nullptr, nullptr);
+  uint32_t m2 = 0u;
+  if (t.r < t.rows) {
+    float a[8], b[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      a[k] = A[t.v * 8 + k];
+      b[k] = B[t.v * 8 + k];
+    }
+    const bool drop = q.seed != nullptr && q.p > 0.0f;
+    const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
+    const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
+    const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
+    const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
+    const TX* xs = x + base * 8;
+    if constexpr (QUANT) {
+      // the scale is uniform over the grid, so the choice never diverges
+      const float sc = *o.prev_scale;
+      m2 = markstein_applies(sc)
+               ? gn_apply_rows<TX, true>(xs, t, base, a, b, drop, seed, thresh, keep_scale, o, make_markstein(sc))
+               : gn_apply_rows<TX, true>(xs, t, base, a, b, drop, seed, thresh, keep_scale, o, DivF64(sc));
+    } else {
+      gn_apply_rows<TX, false>(xs, t, base, a, b, drop, seed, thresh, keep_scale, o, NoCast{});
+    }
+  }
+  if constexpr (QUANT) {
+    const float m = block_max<kGnThreads>(unpack_max2(m2));
+    if (threadIdx.x == 0) o.amax_part[blockIdx.x] = m;
   }
 }
 

@@ -6,11 +6,14 @@ The reference ResBlock (unet.py:149-160) computes ``silu(norm1(x))`` before
 elementwise passes).  :func:`group_norm_act` does each chain in one statistics
 pass and one apply pass over the bf16 NHWC activation (and two passes
 backward), through ``fp8_b200::gn_act_fwd`` / ``gn_act_bwd``.
+:class:`GroupNormActConvFP8` goes one step further where the chain feeds a
+delayed-scaling FP8 conv: the apply pass writes the conv's e4m3 input directly.
 """
 
 from __future__ import annotations
 
 import torch
+from torch.amp.autocast_mode import custom_bwd, custom_fwd
 
 from . import ops
 
@@ -30,15 +33,65 @@ class GroupNormAct(torch.autograd.Function):
         p, eps, groups, film_shape = ctx.cfg
         dout = dout.to(torch.bfloat16)
         dx, totals = ops.gn_act_bwd(x, dout, gamma, beta, film2, seed, stats, p, eps, groups)
-        c = x.shape[1]
-        sc = 1.0 if film2 is None else film2[:, :c].float() + 1.0
-        t_df, t_dfz, t_dfx = totals.unbind(1)  # [N, C] each
-        dgamma = (sc * t_dfx).sum(0)
-        dbeta = (sc * t_df).sum(0)
-        dfilm = None
-        if film2 is not None:
-            dfilm = torch.cat([t_dfz, t_df], dim=1).to(film2.dtype).reshape(film_shape)
+        dgamma, dbeta, dfilm = _norm_param_grads(totals, film2, x.shape[1], film_shape)
         return dx, dgamma, dbeta, dfilm, None, None, None, None
+
+
+def _norm_param_grads(totals: torch.Tensor, film2: torch.Tensor | None, c: int, film_shape):
+    """(dgamma, dbeta, dfilm) from the per-(n, c) sums of the backward pass."""
+    sc = 1.0 if film2 is None else film2[:, :c].float() + 1.0
+    t_df, t_dfz, t_dfx = totals.unbind(1)  # [N, C] each
+    dfilm = None
+    if film2 is not None:
+        dfilm = torch.cat([t_dfz, t_df], dim=1).to(film2.dtype).reshape(film_shape)
+    return (sc * t_dfx).sum(0), (sc * t_df).sum(0), dfilm
+
+
+class GroupNormActConvFP8(torch.autograd.Function):
+    """``conv3x3_fp8(dropout(silu((film_scale + 1) * GroupNorm(x) + film_shift)))`` with delayed scaling.
+
+    The reference quantizes the conv input with the previous scale as the first
+    step of its FP8 conv (Conv2dFP8Specialized.forward, fp8_kernels.py:835-845,
+    on the activation of unet.py:151 / 157-159).  Here the group-norm apply pass
+    writes those e4m3 bytes itself (``fp8_b200::gn_act_quant_fwd``), so the bf16
+    activation is neither written nor read back; the conv and its backward are
+    those of Conv2dFP8Specialized, and the activation gradient feeds the fused
+    group-norm backward.  Returns ``(y, x_scale_curr, w_scale_curr)`` like the
+    delayed branch of ``triton_conv2d_fp8``; the dY scale is written into
+    ``dy_window`` at ``window_pos`` in backward (fp8_kernels.py:883-889)."""
+
+    @staticmethod
+    @custom_fwd(device_type="cuda")
+    def forward(ctx, x, gamma, beta, film, seed, weight, x_hist, w_hist, dy_window, window_pos, p: float,
+                eps: float, groups: int):
+        film2 = None if film is None else film.reshape(film.shape[0], -1)
+        xq, x_scale_curr, stats = ops.gn_act_quant_fwd(x, gamma, beta, film2, seed, x_hist, p, eps, groups)
+        w = weight.to(torch.bfloat16)
+        if not w.is_contiguous(memory_format=torch.channels_last):
+            w = w.contiguous(memory_format=torch.channels_last)
+        wq, w_scale_curr = ops.quantize_delayed(w, w_hist)
+        dy_hist = torch.max(dy_window)
+        y = ops.conv3x3_fwd(xq, wq, x_hist, w_hist)
+        ctx.save_for_backward(x, gamma, beta, film2, seed, stats, xq, wq, x_hist, w_hist, dy_hist)
+        ctx.dy_window = dy_window
+        ctx.window_pos = window_pos
+        ctx.cfg = (p, eps, groups, None if film is None else film.shape)
+        ctx.mark_non_differentiable(x_scale_curr, w_scale_curr)
+        return y, x_scale_curr, w_scale_curr
+
+    @staticmethod
+    @custom_bwd(device_type="cuda")
+    def backward(ctx, dy, _dx_scale, _dw_scale):
+        x, gamma, beta, film2, seed, stats, xq, wq, x_hist, w_hist, dy_hist = ctx.saved_tensors
+        p, eps, groups, film_shape = ctx.cfg
+        dy = dy.to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+        dyq, dy_scale_curr = ops.quantize_delayed(dy, dy_hist)
+        ctx.dy_window.scatter_(0, ctx.window_pos.unsqueeze(0), dy_scale_curr.unsqueeze(0))
+        d_act = ops.conv3x3_dgrad(dyq, wq, dy_hist, w_hist)
+        dw = ops.conv3x3_wgrad(xq, dyq, x_hist, dy_hist)
+        dx, totals = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
+        dgamma, dbeta, dfilm = _norm_param_grads(totals, film2, x.shape[1], film_shape)
+        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None
 
 
 def group_norm_act(x: torch.Tensor, norm: torch.nn.GroupNorm, film: torch.Tensor | None = None,

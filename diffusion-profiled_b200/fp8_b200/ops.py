@@ -427,6 +427,38 @@ def _(x, gamma, beta, film, seed, p, eps, groups):
             x.new_empty((x.shape[0], 2, groups), dtype=torch.float32))
 
 
+@torch.library.custom_op("fp8_b200::gn_act_quant_fwd", mutates_args=())
+def gn_act_quant_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
+                     seed: torch.Tensor | None, prev_scale: torch.Tensor, p: float, eps: float,
+                     groups: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """gn_act_fwd fused with quantize_fp8_delayed of its output -> (e4m3 channels_last, current scale, stats).
+
+    The e4m3 bytes and the scale are bit for bit those of
+    ``quantize_fp8_delayed(gn_act_fwd(...)[0], prev_scale)`` (fp8_kernels.py:518-556);
+    the bf16 activation itself is never written."""
+    dev = _require_cuda(x, gamma, beta)
+    n, c, hw = _gn_check(x, gamma, beta, film, groups)
+    _check_scale(prev_scale, dev, "prev_scale")
+    q = torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.channels_last)
+    scale = torch.empty((), device=dev, dtype=torch.float32)
+    stats = torch.empty((n, 2, groups), device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_gn_act_quant_workspace_bytes(n, hw, c) // 4, 4), device=dev,
+                         dtype=torch.float32)
+        _lib.check(lib.fp8_gn_act_quant_fwd(
+            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed),
+            float(p), float(eps), _ptr(prev_scale), _ptr(stats), _ptr(q), _ptr(scale), n, hw, c, groups, _ptr(ws),
+            ws.numel() * 4, _stream(dev)), "fp8_gn_act_quant_fwd")
+    return q, scale, stats
+
+
+@gn_act_quant_fwd.register_fake
+def _(x, gamma, beta, film, seed, prev_scale, p, eps, groups):
+    return (torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.channels_last),
+            x.new_empty((), dtype=torch.float32), x.new_empty((x.shape[0], 2, groups), dtype=torch.float32))
+
+
 @torch.library.custom_op("fp8_b200::gn_act_bwd", mutates_args=())
 def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
                film: torch.Tensor | None, seed: torch.Tensor | None, stats: torch.Tensor, p: float, eps: float,

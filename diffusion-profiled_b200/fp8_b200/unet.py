@@ -28,7 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
-from .norm import fused_norm_supported, group_norm_act
+from .norm import GroupNormActConvFP8, fused_norm_supported, group_norm_act
 
 
 @dataclass
@@ -98,6 +98,29 @@ class Conv2dFP8(nn.Module):
         return out
 
 
+    def forward_normed(self, x: torch.Tensor, norm: nn.GroupNorm, film: torch.Tensor | None = None, p: float = 0.0,
+                       seed: torch.Tensor | None = None) -> torch.Tensor:
+        """``self(group_norm_act(x, norm, film, p, seed))``.  With delayed scaling the
+        group-norm pass writes this conv's e4m3 input itself (GroupNormActConvFP8)."""
+        if not (self.scaling_type == "delayed" and self.uses_fp8(x) and fused_norm_supported(x, norm)):
+            return self(group_norm_act(x, norm, film, p, seed))
+        if p > 0.0 and seed is None:
+            raise ValueError("dropout needs a seed tensor")
+        x = x.contiguous(memory_format=torch.channels_last)
+        with torch.no_grad():
+            x_hist = torch.max(self.amax_window_acts)
+            w_hist = torch.max(self.amax_window_weights)
+        out, x_scale, w_scale = GroupNormActConvFP8.apply(
+            x, norm.weight, norm.bias, film, seed if p > 0.0 else None, self.conv.weight, x_hist, w_hist,
+            self.amax_window_dy, self.window_pos, float(p), float(norm.eps), int(norm.num_groups))
+        with torch.no_grad():
+            idx = self.window_pos.unsqueeze(0)
+            self.amax_window_weights.scatter_(0, idx, w_scale.unsqueeze(0))
+            self.amax_window_acts.scatter_(0, idx, x_scale.unsqueeze(0))
+            self.window_pos.add_(1).remainder_(self.amax_history)
+        return out
+
+
 class TimeEmbed(nn.Module):
     """Per-block projection of the time embedding to a (scale, shift) pair."""
 
@@ -137,10 +160,10 @@ class ResidualBlock(nn.Module):
     def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
         emb = self.t_embed_wb(t)
         if self.fused_norm and fused_norm_supported(x, self.norm1):
-            h = self.conv_1(group_norm_act(x, self.norm1))
+            h = self.conv_1.forward_normed(x, self.norm1)
             if fused_norm_supported(h, self.norm2) and emb.dtype == torch.bfloat16:
                 p = self.dropout.p if self.training else 0.0
-                h = self.conv_2(group_norm_act(h, self.norm2, emb, p, self._next_seed() if p > 0.0 else None))
+                h = self.conv_2.forward_normed(h, self.norm2, emb, p, self._next_seed() if p > 0.0 else None)
                 return (self.skip_connection(x) + h) / math.sqrt(2.0)
         else:
             h = self.conv_1(F.silu(self.norm1(x)))

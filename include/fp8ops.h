@@ -242,6 +242,23 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
                    float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
                    size_t workspace_bytes, fp8_stream_t stream);
 
+/* Workspace bytes of fp8_gn_act_quant_fwd. */
+size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c);
+
+/* fp8_gn_act_fwd fused with the delayed-scaling quantize of its output, for the
+ * FP8 conv that consumes it (the conv input x of reference
+ * Conv2dFP8Specialized.forward, fp8_kernels.py:835-845, is
+ * silu(norm1(x)) / dropout(silu((scale+1)*norm2(h)+shift)), unet.py:151, 157-159):
+ *   q_e4m3[i]       = e4m3(clamp(bf16(a[i]) / *prev_scale, -448, 448))
+ *   *scale_curr_out = amax|bf16(a)| / 448 (1.0 when the amax is 0)
+ * bit for bit what fp8_gn_act_fwd followed by fp8_quantize_delayed gives, in one
+ * statistics pass, one apply pass that writes only the e4m3 bytes, and a
+ * one-CTA finalize.  stats as in fp8_gn_act_fwd (for the backward). */
+int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                         int film_ld, const int64_t* seed, float p, float eps, const float* prev_scale,
+                         float* stats, void* q_e4m3, float* scale_curr_out, int n, int hw, int c, int groups,
+                         void* workspace, size_t workspace_bytes, fp8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

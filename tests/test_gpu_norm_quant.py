@@ -1,0 +1,113 @@
+"""GPU parity: group norm -> (FiLM) -> SiLU -> (dropout) fused with the delayed
+e4m3 quantize of its output, and the residual-block conv built on it.
+
+Bars: the e4m3 bytes and the current scale equal, bit for bit, the CPU oracle's
+delayed quantize (fp8_oracle.quantize_delayed, the restatement of
+quantize_fp8_delayed, fp8_kernels.py:518-556) of the bf16 activation that the
+unfused group-norm op writes; the fused residual-block conv gives the same
+forward bytes, input and norm gradients as the unfused path, and dW within one
+bf16 rounding step (its split-K additions have no fixed order)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import fp8_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(128, 32, 32), (256, 16, 16), (256, 32, 32), (512, 8, 8), (512, 16, 16)]
+
+
+def _inputs(n, c, h, w, film, seed, device, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(n, c, h, w, generator=g) * 2 + 0.5).to(dtype).contiguous(memory_format=torch.channels_last)
+    norm = torch.nn.GroupNorm(32, c)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.2 * torch.randn(c, generator=g))
+        norm.bias.copy_(0.1 * torch.randn(c, generator=g))
+    f = (0.3 * torch.randn(n, 2 * c, generator=g)).to(torch.bfloat16) if film else None
+    return x.to(device), norm.to(device), None if f is None else f.to(device)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("film,p", [(False, 0.0), (True, 0.0), (True, 0.1)])
+@pytest.mark.parametrize("c,h,w", SHAPES)
+def test_gn_act_quant_matches_oracle_on_the_unfused_activation(cuda, c, h, w, film, p, dtype):
+    from fp8_b200 import ops
+
+    x, norm, f = _inputs(4, c, h, w, film, seed=c + h + int(10 * p), device=cuda, dtype=dtype)
+    seed = torch.tensor(1234 + c, dtype=torch.int64, device=cuda) if p > 0 else None
+    args = (x, norm.weight, norm.bias, f, seed)
+    a, stats_ref = ops.gn_act_fwd(*args, p, norm.eps, 32)
+    amax = a.float().abs().max().item()
+    for prev in (amax / 448.0 * 0.7, amax / 448.0 * 3.0, 0.0, 2.0 ** -70):
+        prev_t = torch.tensor(prev, dtype=torch.float32, device=cuda)
+        q, s_curr, stats = ops.gn_act_quant_fwd(*args, prev_t, p, norm.eps, 32)
+        q_ref, s_ref = oracle.quantize_delayed(a.cpu(), np.float32(prev))
+        got = q.cpu().view(torch.uint8).permute(0, 2, 3, 1).reshape(-1).numpy()
+        assert np.array_equal(got, q_ref), f"prev={prev}: {np.count_nonzero(got != q_ref)} bytes differ"
+        assert s_curr.item() == float(s_ref)
+        assert torch.equal(stats, stats_ref)
+    assert ops.device_error() == 0
+
+
+def _block_pair(cuda, cin, cout, fused):
+    from fp8_b200.unet import ResidualBlock, UNetConfig
+
+    cfg = UNetConfig(fp8_convs_enabled=True, fp8_scaling_type="delayed", fused_norm=True, p_drop=0.1)
+    torch.manual_seed(0)
+    blk = ResidualBlock(cfg, cin, cout, p_drop=0.1).to(cuda).to(memory_format=torch.channels_last)
+    with torch.no_grad():
+        torch.nn.init.normal_(blk.conv_2.conv.weight, std=0.02)
+        for m in (blk.conv_1, blk.conv_2):  # calibrated windows, as after warm-up
+            m.amax_window_acts.fill_(0.01)
+            m.amax_window_weights.fill_(0.0005)
+            m.amax_window_dy.fill_(1e-5)
+        blk.dropout_seed.fill_(77)
+    if not fused:  # the unfused path: group norm op, then the FP8 conv module
+        from fp8_b200.norm import group_norm_act
+
+        for m in (blk.conv_1, blk.conv_2):
+            m.forward_normed = (lambda mod: lambda x, norm, film=None, p=0.0, seed=None:
+                                mod(group_norm_act(x, norm, film, p, seed)))(m)
+    return blk
+
+
+@pytest.mark.parametrize("cin,cout,h", [(128, 128, 32), (128, 256, 16), (256, 256, 16)])
+def test_fused_residual_block_matches_unfused(cuda, cin, cout, h):
+    """ResidualBlock with delayed scaling: GroupNormActConvFP8 vs group_norm_act + Conv2dFP8."""
+    g = torch.Generator().manual_seed(cin + h)
+    x0 = torch.randn(4, cin, h, h, generator=g).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    t0 = torch.randn(4, 512, generator=g).to(torch.bfloat16)
+    dout = (torch.randn(4, cout, h, h, generator=g) * 0.1).to(torch.bfloat16).contiguous(
+        memory_format=torch.channels_last)
+    res = {}
+    for fused in (True, False):
+        blk = _block_pair(cuda, cin, cout, fused)
+        x = x0.to(cuda).requires_grad_(True)
+        t = t0.to(cuda)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = blk(x, t)
+        y.backward(dout.to(cuda))
+        torch.cuda.synchronize()
+        res[fused] = dict(
+            y=y.detach(), dx=x.grad.detach(),
+            g1=blk.norm1.weight.grad, b1=blk.norm1.bias.grad, g2=blk.norm2.weight.grad, b2=blk.norm2.bias.grad,
+            temb=blk.t_embed_wb.mlp.weight.grad, w1=blk.conv_1.conv.weight.grad, w2=blk.conv_2.conv.weight.grad,
+            win=torch.cat([m.amax_window_acts[:2] for m in (blk.conv_1, blk.conv_2)]
+                          + [m.amax_window_dy[:2] for m in (blk.conv_1, blk.conv_2)]
+                          + [m.amax_window_weights[:2] for m in (blk.conv_1, blk.conv_2)]),
+        )
+    a, b = res[True], res[False]
+    assert torch.equal(a["y"], b["y"])
+    assert torch.equal(a["win"], b["win"])
+    # dW of conv_2 feeds nothing else; conv_1's input gradient goes through conv_2's dX only
+    for k in ("w1", "w2"):
+        ref = b[k].float()
+        excess = (a[k].float() - ref).abs() - (2.0 ** -7 * ref.abs() + 1e-4 * ref.abs().max())
+        assert excess.max().item() <= 0.0, k
+    for k in ("dx", "g1", "b1", "g2", "b2", "temb"):
+        assert oracle.max_rel_err(a[k], b[k]) <= 1e-6, k
