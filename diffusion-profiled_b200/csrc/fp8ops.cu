@@ -20,6 +20,7 @@
 #include "conv_halo.cuh"
 #include "conv_halo_t.cuh"
 #include "groupnorm.cuh"
+#include "layernorm.cuh"
 
 using namespace fp8b;
 
@@ -602,49 +603,68 @@ int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const 
 }
 
 // ------------------------------------------------------------------ group norm helpers
-// CTAs per sample: about three per SM over the batch, each with at least one
-// row step of pixels.
-#ifndef FP8_GN_CTAS_PER_SM
-#define FP8_GN_CTAS_PER_SM 3
-#endif
-int gn_slices(int n, int hw, int c, int sm_count) {
+// CTAs per sample.  Each kernel gets as many as one wave of it holds (its
+// occupancy x SMs, rounded down to whole CTAs per sample: a second, partial
+// wave would cost a whole wave's time), with at least one row step of pixels
+// each.  The partial sums of one kernel are merged by the next with the
+// writer's count (GnShape::part_slices), so the two may differ.
+int gn_slices_cap(int n, int hw, int c, int sm_count) {
   const int rows = kGnThreads / (c / 8);
-  int s = (FP8_GN_CTAS_PER_SM * sm_count + n - 1) / std::max(n, 1);
-  s = std::min(s, std::max(1, hw / rows));
-  return std::max(s, 1);
+  return std::max(1, std::min(8 * sm_count / std::max(n, 1), hw / rows));
+}
+
+template <typename K>
+int gn_kernel_slices(K kern, size_t smem, int n, int hw, int c, int sm_count, int* slices) {
+  int occ = 0;
+  FP8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGnThreads, smem));
+  const int s = occ * sm_count / std::max(n, 1);
+  *slices = std::max(1, std::min(s, gn_slices_cap(n, hw, c, sm_count)));
+  return FP8_OK;
 }
 
 size_t gn_workspace(int n, int hw, int c, int sm_count) {
-  return static_cast<size_t>(n) * gn_slices(n, hw, c, sm_count) * 3 * c * sizeof(float);
+  return static_cast<size_t>(n) * gn_slices_cap(n, hw, c, sm_count) * 3 * c * sizeof(float);
 }
 
 template <typename TX, bool QUANT>
-int launch_gn_fwd(const TX* x, const GnShape& sh, float* part, const GnActParams& q, float* stats, const GnOut& o,
-                  size_t s1, size_t s2, cudaStream_t cs) {
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_stats_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s1)));
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_fwd_kernel<TX, QUANT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s2)));
-  const dim3 grid(static_cast<unsigned>(sh.n * sh.slices)), block(kGnThreads);
-  FP8_CUDA_TRY(launch_kernel(gn_stats_kernel<TX>, grid, block, s1, cs, 1, kStreamingKernel, x, sh, part));
-  FP8_CUDA_TRY(launch_kernel(gn_act_fwd_kernel<TX, QUANT>, grid, block, s2, cs, 1, kStreamingKernel, x, sh,
+int launch_gn_fwd(const TX* x, GnShape sh, float* part, const GnActParams& q, float* stats, const GnOut& o,
+                  size_t s1, size_t s2, int sm_count, cudaStream_t cs, int* apply_ctas = nullptr) {
+  auto k1 = gn_stats_kernel<TX>;
+  auto k2 = gn_act_fwd_kernel<TX, QUANT>;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s1)));
+  FP8_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s2)));
+  int sl1 = 1, sl2 = 1;
+  if (int s = gn_kernel_slices(k1, s1, sh.n, sh.hw, sh.c, sm_count, &sl1)) return s;
+  if (int s = gn_kernel_slices(k2, s2, sh.n, sh.hw, sh.c, sm_count, &sl2)) return s;
+  const dim3 block(kGnThreads);
+  sh.slices = sh.part_slices = sl1;
+  FP8_CUDA_TRY(launch_kernel(k1, dim3(static_cast<unsigned>(sh.n * sl1)), block, s1, cs, 1, kStreamingKernel, x, sh,
+                             part));
+  sh.slices = sl2;
+  FP8_CUDA_TRY(launch_kernel(k2, dim3(static_cast<unsigned>(sh.n * sl2)), block, s2, cs, 1, kStreamingKernel, x, sh,
                              static_cast<const float*>(part), q, stats, o));
+  if (apply_ctas != nullptr) *apply_ctas = sh.n * sl2;
   count_launches(2);
   return FP8_OK;
 }
 
 template <typename TX>
-int launch_gn_bwd(const TX* x, const uint16_t* dy, const GnShape& sh, const float* stats, const GnActParams& q,
-                  float* part, float* totals, TX* dx, size_t s1, size_t s2, cudaStream_t cs) {
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_reduce_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s1)));
-  FP8_CUDA_TRY(cudaFuncSetAttribute(gn_act_bwd_apply_kernel<TX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(s2)));
-  const dim3 grid(static_cast<unsigned>(sh.n * sh.slices)), block(kGnThreads);
-  FP8_CUDA_TRY(launch_kernel(gn_act_bwd_reduce_kernel<TX>, grid, block, s1, cs, 1, kStreamingKernel, x, dy, sh, stats,
-                             q, part));
-  FP8_CUDA_TRY(launch_kernel(gn_act_bwd_apply_kernel<TX>, grid, block, s2, cs, 1, kStreamingKernel, x, dy, sh, stats, q,
-                             static_cast<const float*>(part), totals, dx));
+int launch_gn_bwd(const TX* x, const uint16_t* dy, GnShape sh, const float* stats, const GnActParams& q,
+                  float* part, float* totals, TX* dx, size_t s1, size_t s2, int sm_count, cudaStream_t cs) {
+  auto k1 = gn_act_bwd_reduce_kernel<TX>;
+  auto k2 = gn_act_bwd_apply_kernel<TX>;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s1)));
+  FP8_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s2)));
+  int sl1 = 1, sl2 = 1;
+  if (int s = gn_kernel_slices(k1, s1, sh.n, sh.hw, sh.c, sm_count, &sl1)) return s;
+  if (int s = gn_kernel_slices(k2, s2, sh.n, sh.hw, sh.c, sm_count, &sl2)) return s;
+  const dim3 block(kGnThreads);
+  sh.slices = sh.part_slices = sl1;
+  FP8_CUDA_TRY(launch_kernel(k1, dim3(static_cast<unsigned>(sh.n * sl1)), block, s1, cs, 1, kStreamingKernel, x, dy,
+                             sh, stats, q, part));
+  sh.slices = sl2;
+  FP8_CUDA_TRY(launch_kernel(k2, dim3(static_cast<unsigned>(sh.n * sl2)), block, s2, cs, 1, kStreamingKernel, x, dy,
+                             sh, stats, q, static_cast<const float*>(part), totals, dx));
   count_launches(2);
   return FP8_OK;
 }
@@ -1203,16 +1223,18 @@ int fp8_gn_act_fwd(const void* x, int x_fp32, const float* gamma, const float* b
   const size_t need = gn_workspace(n, hw, c, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
               "group-norm workspace too small: need %zu bytes", need);
-  GnShape sh{n, hw, c, groups, gn_slices(n, hw, c, st->sm_count)};
+  const GnShape sh{n, hw, c, groups, 1, 1};
   GnActParams q{gamma, beta, static_cast<const uint16_t*>(film), film_ld, seed, p, eps};
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
   const GnOut o{static_cast<uint16_t*>(out), nullptr, nullptr, nullptr};
   if (x_fp32) {
-    if (int s = launch_gn_fwd<float, false>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, cs)) return s;
+    if (int s = launch_gn_fwd<float, false>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, st->sm_count,
+                                               cs)) return s;
   } else {
-    if (int s = launch_gn_fwd<uint16_t, false>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2, cs))
+    if (int s = launch_gn_fwd<uint16_t, false>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2,
+                                                  st->sm_count, cs))
       return s;
   }
   FP8_CUDA_TRY(cudaGetLastError());
@@ -1225,7 +1247,7 @@ size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c) {
   (void)cudaGetLastError();
   if (n <= 0 || hw <= 0 || c < 8) return 0;
   if (sms <= 0) sms = 148;
-  const int slices = gn_slices(n, hw, c, sms);
+  const int slices = gn_slices_cap(n, hw, c, sms);
   // group-norm partials, then one amax partial per apply CTA (16-byte aligned)
   return gn_workspace(n, hw, c, sms) + ((static_cast<size_t>(n) * slices * sizeof(float) + 15) & ~size_t(15));
 }
@@ -1239,9 +1261,10 @@ int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const fl
               "NULL stats or scale");
   DeviceState* st;
   if (int s = device_state(&st)) return s;
-  GnShape sh{n, hw, c, groups, gn_slices(n, hw, c, st->sm_count)};
+  const GnShape sh{n, hw, c, groups, 1, 1};
   const size_t gn_bytes = gn_workspace(n, hw, c, st->sm_count);
-  const size_t need = gn_bytes + ((static_cast<size_t>(n) * sh.slices * sizeof(float) + 15) & ~size_t(15));
+  const size_t need =
+      gn_bytes + ((static_cast<size_t>(n) * gn_slices_cap(n, hw, c, st->sm_count) * sizeof(float) + 15) & ~size_t(15));
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
               "group-norm workspace too small: need %zu bytes", need);
   GnActParams q{gamma, beta, static_cast<const uint16_t*>(film), film_ld, seed, p, eps};
@@ -1249,15 +1272,18 @@ int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const fl
   float* part = static_cast<float*>(workspace);
   float* amax_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gn_bytes);
   const GnOut o{nullptr, static_cast<uint8_t*>(q_e4m3), prev_scale, amax_part};
+  int apply_ctas = 0;
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
   if (x_fp32) {
-    if (int s = launch_gn_fwd<float, true>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, cs)) return s;
+    if (int s = launch_gn_fwd<float, true>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, st->sm_count,
+                                              cs, &apply_ctas)) return s;
   } else {
-    if (int s = launch_gn_fwd<uint16_t, true>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2, cs))
+    if (int s = launch_gn_fwd<uint16_t, true>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2,
+                                                 st->sm_count, cs, &apply_ctas))
       return s;
   }
   FP8_CUDA_TRY(launch_kernel(finalize_scale_kernel, dim3(1), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
-                             static_cast<const float*>(amax_part), n * sh.slices, scale_curr_out));
+                             static_cast<const float*>(amax_part), apply_ctas, scale_curr_out));
   count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
@@ -1275,7 +1301,7 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
   const size_t need = gn_workspace(n, hw, c, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
               "group-norm workspace too small: need %zu bytes", need);
-  GnShape sh{n, hw, c, groups, gn_slices(n, hw, c, st->sm_count)};
+  const GnShape sh{n, hw, c, groups, 1, 1};
   GnActParams q{gamma, beta, static_cast<const uint16_t*>(film), film_ld, seed, p, eps};
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
@@ -1283,11 +1309,11 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
   const uint16_t* ds = static_cast<const uint16_t*>(dy);
   if (x_fp32) {
     if (int s = launch_gn_bwd(static_cast<const float*>(x), ds, sh, stats, q, part, totals, static_cast<float*>(dx),
-                              s1, s2, cs))
+                              s1, s2, st->sm_count, cs))
       return s;
   } else {
     if (int s = launch_gn_bwd(static_cast<const uint16_t*>(x), ds, sh, stats, q, part, totals,
-                              static_cast<uint16_t*>(dx), s1, s2, cs))
+                              static_cast<uint16_t*>(dx), s1, s2, st->sm_count, cs))
       return s;
   }
   FP8_CUDA_TRY(cudaGetLastError());
@@ -1412,6 +1438,128 @@ int fp8_conv3x3_dgrad_w(const void* dyq, const void* wq, void* dx, const float* 
   }
   if (int s = fp8_conv_weight_transpose(wq, workspace, cout, cin, stream)) return s;
   return fp8_conv3x3_dgrad(dyq, workspace, dx, sdy, sw, batch, height, width, cin, cout, stream);
+}
+
+}  // extern "C"
+
+// ======================================================================== layer norm (attention tokens)
+namespace {
+
+int ln_vpl(int c) { return c <= 256 ? 1 : (c <= 512 ? 2 : 4); }
+
+int check_ln_args(const void* x, const void* out, const float* gamma, int64_t tokens, int c) {
+  FP8_REQUIRE(tokens >= 0 && c > 0, FP8_ERR_INVALID_ARGUMENT, "bad layer-norm sizes");
+  FP8_REQUIRE(c % 8 == 0 && c <= 1024, FP8_ERR_UNSUPPORTED, "layer norm needs c %% 8 == 0 and c <= 1024 (c=%d)", c);
+  FP8_REQUIRE(tokens == 0 || (x && out && gamma), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(aligned(x, 16) && aligned(out, 16), FP8_ERR_INVALID_ARGUMENT, "tokens must be 16-byte aligned");
+  return FP8_OK;
+}
+
+int ln_bwd_ctas(int64_t tokens, int sm_count) {
+  const int64_t need = (tokens + kLnWarps - 1) / kLnWarps;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, 4ll * sm_count)));
+}
+
+template <typename TX, int VPL>
+int launch_ln_fwd(const TX* x, const float* gamma, const float* beta, float eps, void* y, float* mr,
+                  int64_t tokens, int c, int sm_count, cudaStream_t cs) {
+  const int64_t need = (tokens + kLnWarps - 1) / kLnWarps;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(need, 8ll * sm_count)));
+  FP8_CUDA_TRY(launch_kernel(ln_fwd_kernel<TX, VPL>, dim3(grid), dim3(kLnThreads), 0, cs, 1, kStreamingKernel, x,
+                             gamma, beta, tokens, c, eps, static_cast<uint16_t*>(y), reinterpret_cast<float2*>(mr)));
+  count_launches(1);
+  return FP8_OK;
+}
+
+template <typename TX, int VPL>
+int launch_ln_bwd(const TX* x, const uint16_t* dy, const float* gamma, const float* mr, TX* dx, float* dgamma,
+                  float* dbeta, float* part, int64_t tokens, int c, int sm_count, cudaStream_t cs) {
+  const int parts = ln_bwd_ctas(tokens, sm_count);
+  const size_t smem = static_cast<size_t>(kLnWarps) * 2 * c * sizeof(float);
+  FP8_CUDA_TRY(cudaFuncSetAttribute(ln_bwd_kernel<TX, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+  FP8_CUDA_TRY(launch_kernel(ln_bwd_kernel<TX, VPL>, dim3(parts), dim3(kLnThreads), smem, cs, 1, kStreamingKernel, x,
+                             dy, gamma, reinterpret_cast<const float2*>(mr), tokens, c, dx, part));
+  FP8_CUDA_TRY(launch_kernel(ln_param_reduce_kernel, dim3((2 * c + kLnWarps - 1) / kLnWarps), dim3(kLnThreads), 0, cs,
+                             1, kStreamingKernel, static_cast<const float*>(part), parts, c, dgamma, dbeta));
+  count_launches(2);
+  return FP8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fp8_layer_norm_workspace_bytes(int64_t tokens, int c) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  (void)cudaGetLastError();
+  if (tokens <= 0 || c <= 0) return 0;
+  if (sms <= 0) sms = 148;
+  return static_cast<size_t>(ln_bwd_ctas(tokens, sms)) * 2 * c * sizeof(float);
+}
+
+int fp8_layer_norm_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, float eps, void* y_bf16,
+                       float* mean_rstd, int64_t tokens, int c, fp8_stream_t stream) {
+  if (int s = check_ln_args(x, y_bf16, gamma, tokens, c)) return s;
+  FP8_REQUIRE(tokens == 0 || (beta && mean_rstd), FP8_ERR_INVALID_ARGUMENT, "NULL beta / statistics");
+  FP8_REQUIRE(eps > 0.0f, FP8_ERR_INVALID_ARGUMENT, "eps must be > 0");
+  if (tokens == 0) return ok();
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const int vpl = ln_vpl(c);
+  int s = FP8_OK;
+  if (x_fp32) {
+    const float* xf = static_cast<const float*>(x);
+    s = vpl == 1 ? launch_ln_fwd<float, 1>(xf, gamma, beta, eps, y_bf16, mean_rstd, tokens, c, st->sm_count, cs)
+        : vpl == 2 ? launch_ln_fwd<float, 2>(xf, gamma, beta, eps, y_bf16, mean_rstd, tokens, c, st->sm_count, cs)
+                   : launch_ln_fwd<float, 4>(xf, gamma, beta, eps, y_bf16, mean_rstd, tokens, c, st->sm_count, cs);
+  } else {
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    s = vpl == 1 ? launch_ln_fwd<uint16_t, 1>(xb, gamma, beta, eps, y_bf16, mean_rstd, tokens, c, st->sm_count, cs)
+        : vpl == 2 ? launch_ln_fwd<uint16_t, 2>(xb, gamma, beta, eps, y_bf16, mean_rstd, tokens, c, st->sm_count, cs)
+                   : launch_ln_fwd<uint16_t, 4>(xb, gamma, beta, eps, y_bf16, mean_rstd, tokens, c, st->sm_count, cs);
+  }
+  if (s) return s;
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+int fp8_layer_norm_bwd(const void* x, int x_fp32, const void* dy_bf16, const float* gamma, const float* mean_rstd,
+                       void* dx, float* dgamma, float* dbeta, int64_t tokens, int c, void* workspace,
+                       size_t workspace_bytes, fp8_stream_t stream) {
+  if (int s = check_ln_args(x, dx, gamma, tokens, c)) return s;
+  FP8_REQUIRE(tokens == 0 || (dy_bf16 && aligned(dy_bf16, 16) && mean_rstd && dgamma && dbeta),
+              FP8_ERR_INVALID_ARGUMENT, "NULL or unaligned dy / statistics / parameter gradients");
+  if (tokens == 0) return ok();
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  const size_t need = static_cast<size_t>(ln_bwd_ctas(tokens, st->sm_count)) * 2 * c * sizeof(float);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
+              "layer-norm workspace too small: need %zu bytes", need);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  const uint16_t* dy = static_cast<const uint16_t*>(dy_bf16);
+  const int vpl = ln_vpl(c);
+  const int sms = st->sm_count;
+  int s = FP8_OK;
+  if (x_fp32) {
+    const float* xf = static_cast<const float*>(x);
+    float* d = static_cast<float*>(dx);
+    s = vpl == 1 ? launch_ln_bwd<float, 1>(xf, dy, gamma, mean_rstd, d, dgamma, dbeta, part, tokens, c, sms, cs)
+        : vpl == 2 ? launch_ln_bwd<float, 2>(xf, dy, gamma, mean_rstd, d, dgamma, dbeta, part, tokens, c, sms, cs)
+                   : launch_ln_bwd<float, 4>(xf, dy, gamma, mean_rstd, d, dgamma, dbeta, part, tokens, c, sms, cs);
+  } else {
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    uint16_t* d = static_cast<uint16_t*>(dx);
+    s = vpl == 1 ? launch_ln_bwd<uint16_t, 1>(xb, dy, gamma, mean_rstd, d, dgamma, dbeta, part, tokens, c, sms, cs)
+        : vpl == 2 ? launch_ln_bwd<uint16_t, 2>(xb, dy, gamma, mean_rstd, d, dgamma, dbeta, part, tokens, c, sms, cs)
+                   : launch_ln_bwd<uint16_t, 4>(xb, dy, gamma, mean_rstd, d, dgamma, dbeta, part, tokens, c, sms, cs);
+  }
+  if (s) return s;
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
 }
 
 }  // extern "C"

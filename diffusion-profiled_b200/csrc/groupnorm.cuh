@@ -34,7 +34,7 @@
 namespace fp8b {
 
 #ifndef FP8_GN_THREADS
-#define FP8_GN_THREADS 256
+#define FP8_GN_THREADS 512
 #endif
 #ifndef FP8_GN_UF
 #define FP8_GN_UF 4
@@ -42,13 +42,17 @@ namespace fp8b {
 #ifndef FP8_GN_UB
 #define FP8_GN_UB 2
 #endif
+#ifndef FP8_GN_MINB_BWD
+#define FP8_GN_MINB_BWD 1
+#endif
 constexpr int kGnThreads = FP8_GN_THREADS;
 constexpr int kGnUnrollFwd = FP8_GN_UF;  // pixel rows per step, forward kernels
 constexpr int kGnUnrollBwd = FP8_GN_UB;  // pixel rows per step, backward kernels
 
 struct GnShape {
   int n, hw, c, groups;
-  int slices;  // CTAs per sample
+  int slices;       // CTAs per sample of this kernel
+  int part_slices;  // CTAs per sample of the kernel that wrote the partial sums this kernel reads
 };
 
 __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
@@ -259,8 +263,8 @@ __device__ __forceinline__ void gn_group_stats(const TX* __restrict__ x, const f
   const float cnt = static_cast<float>(s.hw);
   for (int c = threadIdx.x; c < s.c; c += blockDim.x) {
     float s1 = 0.0f, s2 = 0.0f;
-    for (int k = 0; k < s.slices; ++k) {
-      const float* pp = part + (static_cast<int64_t>(n) * s.slices + k) * 2 * s.c;
+    for (int k = 0; k < s.part_slices; ++k) {
+      const float* pp = part + (static_cast<int64_t>(n) * s.part_slices + k) * 2 * s.c;
       s1 += pp[c];
       s2 += pp[s.c + c];
     }
@@ -433,7 +437,7 @@ struct GnBwdElem {
 
 // part[(n * slices + slice) * 3C + {0, C, 2C} + c] = sum df, sum df * z, sum df * xhat
 template <typename TX>
-__global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
+__global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_reduce_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
     GnActParams q, float* __restrict__ part) {
   extern __shared__ float gn_smem[];
@@ -496,7 +500,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float f = fmaf(a[k], xf[k], b[k]);
-          const float sg = 1.0f / (1.0f + __expf(-f));
+          const float sg = sigmoid_f32(f);
           const float du = (keep >> k) & 1u ? gf[k] * keep_scale : 0.0f;
           const float df = du * sg * fmaf(f, 1.0f - sg, 1.0f);
           acc[0][k] += df;
@@ -514,7 +518,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_reduce_kernel(
 // totals[n * 3C + {0, C, 2C} + c] = sum df, sum df z, sum df xhat over the sample
 // (written by slice 0); dx as above.
 template <typename TX>
-__global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
+__global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
     GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx) {
   extern __shared__ float gn_smem[];
@@ -539,7 +543,8 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
   const bool first = blockIdx.x % s.slices == 0;
   for (int i = threadIdx.x; i < 3 * s.c; i += blockDim.x) {
     float v = 0.0f;
-    for (int k = 0; k < s.slices; ++k) v += part[(static_cast<int64_t>(t.n) * s.slices + k) * 3 * s.c + i];
+    for (int k = 0; k < s.part_slices; ++k)
+      v += part[(static_cast<int64_t>(t.n) * s.part_slices + k) * 3 * s.c + i];
     tot[i] = v;
     if (first) totals[static_cast<int64_t>(t.n) * 3 * s.c + i] = v;
   }
@@ -607,7 +612,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_bwd_apply_kernel(
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const float f = fmaf(a[k], xf[k], b[k]);
-        const float sg = 1.0f / (1.0f + __expf(-f));
+        const float sg = sigmoid_f32(f);
         const float du = (keep >> k) & 1u ? gf[k] * keep_scale : 0.0f;
         const float df = du * sg * fmaf(f, 1.0f - sg, 1.0f);
         const float xhat = (xf[k] - mu[k]) * rs[k];

@@ -380,7 +380,11 @@ __host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N, int a_mn_ma
 __device__ __forceinline__ float bf16_lo_f(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-__device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
+// SiLU and the logistic function with the fast exponential and reciprocal
+// (relative error a few fp32 ulps; the results are rounded to bf16).  For
+// v < -88 the exponential overflows to inf and both return (-)0.
+__device__ __forceinline__ float sigmoid_f32(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
+__device__ __forceinline__ float silu_f32(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);

@@ -79,6 +79,14 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_gn_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_fwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_float,
                                c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "fp8_layer_norm_fwd": (
+        c_int, [c_void_p, c_int, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "fp8_layer_norm_workspace_bytes": (c_size_t, [c_int64, c_int]),
+    "fp8_layer_norm_bwd": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
+         c_size_t, c_void_p],
+    ),
     "fp8_gn_act_quant_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_quant_fwd": (
         c_int,

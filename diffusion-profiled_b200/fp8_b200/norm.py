@@ -111,3 +111,36 @@ def fused_norm_supported(x: torch.Tensor, norm: torch.nn.GroupNorm) -> bool:
     c = x.shape[1]
     return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and x.dim() == 4 and c % 8 == 0 and c <= 512
             and c % norm.num_groups == 0 and norm.affine and norm.weight.dtype == torch.float32)
+
+
+class LayerNormBf16(torch.autograd.Function):
+    """nn.LayerNorm over the last dim with a bf16 output (``fp8_b200::layer_norm_fwd``).
+
+    The reference's attention norm (unet.py:174, :187) runs in fp32 under autocast
+    and its only consumer, the qkv projection, casts the result to bf16; this op
+    returns that bf16 tensor directly and computes the parameter gradients with
+    per-CTA partial sums instead of a separate column reduction."""
+
+    @staticmethod
+    def forward(ctx, x, gamma, beta, eps: float):
+        y, mr = ops.layer_norm_fwd(x, gamma, beta, eps)
+        ctx.save_for_backward(x, gamma, mr)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, gamma, mr = ctx.saved_tensors
+        dx, dgamma, dbeta = ops.layer_norm_bwd(x, dy, gamma, mr)
+        return dx, dgamma, dbeta, None
+
+
+def layer_norm_bf16(x: torch.Tensor, norm: torch.nn.LayerNorm) -> torch.Tensor:
+    """``norm(x)`` as bf16 for a contiguous bf16 / fp32 CUDA ``x``."""
+    return LayerNormBf16.apply(x.contiguous(), norm.weight, norm.bias, float(norm.eps))
+
+
+def fused_layer_norm_supported(x: torch.Tensor, norm: torch.nn.LayerNorm) -> bool:
+    c = x.shape[-1]
+    return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and c % 8 == 0 and c <= 1024
+            and norm.elementwise_affine and norm.weight is not None and norm.bias is not None
+            and norm.weight.dtype == torch.float32 and len(norm.normalized_shape) == 1)

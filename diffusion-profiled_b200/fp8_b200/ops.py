@@ -427,6 +427,62 @@ def _(x, gamma, beta, film, seed, p, eps, groups):
             x.new_empty((x.shape[0], 2, groups), dtype=torch.float32))
 
 
+def _ln_check(x: torch.Tensor, gamma: torch.Tensor) -> tuple[int, int]:
+    if x.dtype not in (torch.bfloat16, torch.float32) or not x.is_contiguous():
+        raise RuntimeError("layer norm expects a contiguous bfloat16 or float32 tensor")
+    c = x.shape[-1]
+    if gamma.dtype != torch.float32 or gamma.shape != (c,):
+        raise RuntimeError(f"layer-norm weight must be float32 [{c}]")
+    return x.numel() // max(c, 1), c
+
+
+@torch.library.custom_op("fp8_b200::layer_norm_fwd", mutates_args=())
+def layer_norm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                   eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """LayerNorm over the last dim -> (bf16 y, fp32 [tokens, 2] mean / rstd); nn.LayerNorm of unet.py:174."""
+    dev = _require_cuda(x, gamma, beta)
+    tokens, c = _ln_check(x, gamma)
+    y = torch.empty(x.shape, device=dev, dtype=torch.bfloat16)
+    mr = torch.empty((tokens, 2), device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_layer_norm_fwd", _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), float(eps),
+                  _ptr(y), _ptr(mr), tokens, c, _stream(dev))
+    return y, mr
+
+
+@layer_norm_fwd.register_fake
+def _(x, gamma, beta, eps):
+    return x.new_empty(x.shape, dtype=torch.bfloat16), x.new_empty((x.numel() // x.shape[-1], 2), dtype=torch.float32)
+
+
+@torch.library.custom_op("fp8_b200::layer_norm_bwd", mutates_args=())
+def layer_norm_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor,
+                   mean_rstd: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Backward of layer_norm_fwd -> (dx in x's dtype, dgamma, dbeta)."""
+    dev = _require_cuda(x, dy, gamma, mean_rstd)
+    tokens, c = _ln_check(x, gamma)
+    dy = dy.to(torch.bfloat16).contiguous()
+    if dy.shape != x.shape:
+        raise RuntimeError("dy must be shaped like x")
+    dx = torch.empty_like(x)
+    dgamma = torch.empty((c,), device=dev, dtype=torch.float32)
+    dbeta = torch.empty((c,), device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.fp8_layer_norm_workspace_bytes(tokens, c)
+        ws = torch.empty((max(ws_bytes // 4, 4),), device=dev, dtype=torch.float32)
+        _lib.check(lib.fp8_layer_norm_bwd(
+            _ptr(x), int(x.dtype == torch.float32), _ptr(dy), _ptr(gamma), _ptr(mean_rstd), _ptr(dx), _ptr(dgamma),
+            _ptr(dbeta), tokens, c, _ptr(ws), ws.numel() * 4, _stream(dev)), "fp8_layer_norm_bwd")
+    return dx, dgamma, dbeta
+
+
+@layer_norm_bwd.register_fake
+def _(x, dy, gamma, mean_rstd):
+    c = x.shape[-1]
+    return torch.empty_like(x), x.new_empty((c,), dtype=torch.float32), x.new_empty((c,), dtype=torch.float32)
+
+
 @torch.library.custom_op("fp8_b200::gn_act_quant_fwd", mutates_args=())
 def gn_act_quant_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
                      seed: torch.Tensor | None, prev_scale: torch.Tensor, p: float, eps: float,

@@ -28,7 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
-from .norm import GroupNormActConvFP8, fused_norm_supported, group_norm_act
+from .norm import GroupNormActConvFP8, fused_layer_norm_supported, fused_norm_supported, group_norm_act, layer_norm_bf16
 
 
 @dataclass
@@ -178,6 +178,7 @@ class CHWAttention(nn.Module):
 
     def __init__(self, config: UNetConfig, hidden_size: int):
         super().__init__()
+        self.fused_norm = config.fused_norm
         self.nh = config.n_heads
         self.qkv = nn.Linear(hidden_size, 3 * hidden_size, bias=False)
         self.out = nn.Linear(hidden_size, hidden_size, bias=False)
@@ -186,7 +187,11 @@ class CHWAttention(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         b, c, h, w = x.shape
-        tokens = self.norm(x.flatten(2).transpose(1, 2))  # [B, HW, C]
+        tokens = x.flatten(2).transpose(1, 2)  # [B, HW, C]
+        if self.fused_norm and tokens.is_contiguous() and fused_layer_norm_supported(tokens, self.norm):
+            tokens = layer_norm_bf16(tokens, self.norm)  # bf16, what the qkv projection consumes
+        else:
+            tokens = self.norm(tokens)
         q, k, v = self.qkv(tokens).chunk(3, dim=-1)
         heads = lambda z: z.unflatten(-1, (self.nh, c // self.nh)).transpose(1, 2)  # noqa: E731
         o = F.scaled_dot_product_attention(heads(q), heads(k), heads(v))

@@ -242,6 +242,26 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
                    float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
                    size_t workspace_bytes, fp8_stream_t stream);
 
+/* LayerNorm over the last dimension of `tokens` rows of c channels (the
+ * attention-block norm of reference unet.py:174, :187, nn.LayerNorm(C) with
+ * elementwise affine): y = bf16((x - mean) * rstd * gamma + beta), rstd =
+ * 1 / sqrt(biased var + eps).  The reference computes it in fp32 under autocast
+ * and the qkv projection casts it to bf16; this writes the bf16 directly.
+ * x is bf16 (x_fp32 = 0) or fp32; mean_rstd: fp32 [tokens][2] for the backward.
+ * c % 8 == 0, c <= 1024; x, y 16-byte aligned. */
+int fp8_layer_norm_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, float eps, void* y_bf16,
+                       float* mean_rstd, int64_t tokens, int c, fp8_stream_t stream);
+
+/* Workspace bytes of fp8_layer_norm_bwd. */
+size_t fp8_layer_norm_workspace_bytes(int64_t tokens, int c);
+
+/* Backward of fp8_layer_norm_fwd: dx (x's dtype) from the bf16 dy, and the
+ * parameter gradients dgamma = sum_t dy * xhat, dbeta = sum_t dy (fp32 [c],
+ * overwritten; summed per CTA and then over CTAs in a fixed order). */
+int fp8_layer_norm_bwd(const void* x, int x_fp32, const void* dy_bf16, const float* gamma, const float* mean_rstd,
+                       void* dx, float* dgamma, float* dbeta, int64_t tokens, int c, void* workspace,
+                       size_t workspace_bytes, fp8_stream_t stream);
+
 /* Workspace bytes of fp8_gn_act_quant_fwd. */
 size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c);
 

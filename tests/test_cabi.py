@@ -164,3 +164,13 @@ def test_dgrad_w_workspace_sizing_and_check():
         lib.fp8_conv3x3_dgrad_w, fake, fake, fake, fake, fake, 2, 8, 8, 256, 256, c_void_p(0), 0, c_void_p(0)
     )
     assert status == _lib.FP8_ERR_WORKSPACE and code == status and "workspace" in msg
+
+
+def test_layer_norm_rejects_bad_channels_without_touching_cuda():
+    lib = _lib.load()
+    fake = c_void_p(1 << 20)
+    status, code, msg = _status_and_message(
+        lib.fp8_layer_norm_fwd, fake, 0, fake, fake, ctypes.c_float(1e-5), fake, fake, 64, 12, c_void_p(0)
+    )
+    assert status == _lib.FP8_ERR_UNSUPPORTED and code == status and "c % 8" in msg
+    assert lib.fp8_layer_norm_workspace_bytes(0, 256) == 0
