@@ -521,7 +521,8 @@ def time_unet(args, dev, world, fp8: bool) -> dict:
             "unit": "imgs/s", "ms_per_step": round(ms, 4), "steps": args.unet_steps, "batch_per_gpu": args.batch,
             "global_batch": args.batch * world, "n_gpus": world, "mean_loss": round(loss, 4),
             "fp8": ("whitelisted 3x3 convs, delayed scaling" if fp8 else "off (bf16 autocast)"),
-            "norm_activation": ("fused GroupNorm/FiLM/SiLU/dropout kernels" if fp8 else "torch ops (reference)"),
+            "norm_activation": ("fused GroupNorm/FiLM/SiLU/dropout kernels (the FP8 conv input written as e4m3), "
+                                "LayerNorm kernels in the attention blocks" if fp8 else "torch ops (reference)"),
             "conv_modules": n_fp8, "allreduce_bf16_bytes_per_step": allreduce,
             "step": "noise + UNet fwd/bwd (bf16 autocast) + grad all-reduce + clip 1.0 + fused AdamW 2e-4 + EMA, "
                     "one CUDA graph replay"}
