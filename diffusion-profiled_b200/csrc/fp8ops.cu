@@ -1563,3 +1563,20 @@ int fp8_layer_norm_bwd(const void* x, int x_fp32, const void* dy_bf16, const flo
 }
 
 }  // extern "C"
+
+extern "C" int fp8_gn_param_grads(const float* totals, const void* film, int film_ld, int n, int c, float* dgamma,
+                                  float* dbeta, void* dfilm, int dfilm_ld, fp8_stream_t stream) {
+  FP8_REQUIRE(n > 0 && c > 0, FP8_ERR_INVALID_ARGUMENT, "bad sizes");
+  FP8_REQUIRE(totals && dgamma && dbeta, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
+  FP8_REQUIRE(film == nullptr || (film_ld >= 2 * c && dfilm != nullptr && dfilm_ld >= 2 * c),
+              FP8_ERR_INVALID_ARGUMENT, "FiLM gradients need film_ld, dfilm_ld >= 2c and a dfilm buffer");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  (void)st;
+  FP8_CUDA_TRY(launch_kernel(gn_param_grads_kernel, dim3((c + 255) / 256), dim3(256), 0,
+                             reinterpret_cast<cudaStream_t>(stream), 1, kStreamingKernel, totals,
+                             static_cast<const uint16_t*>(film), film_ld, n, c, dgamma, dbeta,
+                             static_cast<uint16_t*>(dfilm), dfilm_ld));
+  count_launches(1);
+  return ok();
+}

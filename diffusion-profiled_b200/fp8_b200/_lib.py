@@ -87,6 +87,8 @@ _SIGNATURES: dict[str, tuple] = {
         [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
          c_size_t, c_void_p],
     ),
+    "fp8_gn_param_grads": (
+        c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "fp8_gn_act_quant_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_quant_fwd": (
         c_int,

@@ -32,19 +32,13 @@ class GroupNormAct(torch.autograd.Function):
         x, gamma, beta, film2, seed, stats = ctx.saved_tensors
         p, eps, groups, film_shape = ctx.cfg
         dout = dout.to(torch.bfloat16)
-        dx, totals = ops.gn_act_bwd(x, dout, gamma, beta, film2, seed, stats, p, eps, groups)
-        dgamma, dbeta, dfilm = _norm_param_grads(totals, film2, x.shape[1], film_shape)
-        return dx, dgamma, dbeta, dfilm, None, None, None, None
+        dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, dout, gamma, beta, film2, seed, stats, p, eps, groups)
+        return dx, dgamma, dbeta, _film_grad(dfilm, film_shape), None, None, None, None
 
 
-def _norm_param_grads(totals: torch.Tensor, film2: torch.Tensor | None, c: int, film_shape):
-    """(dgamma, dbeta, dfilm) from the per-(n, c) sums of the backward pass."""
-    sc = 1.0 if film2 is None else film2[:, :c].float() + 1.0
-    t_df, t_dfz, t_dfx = totals.unbind(1)  # [N, C] each
-    dfilm = None
-    if film2 is not None:
-        dfilm = torch.cat([t_dfz, t_df], dim=1).to(film2.dtype).reshape(film_shape)
-    return (sc * t_dfx).sum(0), (sc * t_df).sum(0), dfilm
+def _film_grad(dfilm: torch.Tensor, film_shape):
+    """The FiLM gradient in the FiLM input's shape (None without FiLM)."""
+    return None if film_shape is None else dfilm.reshape(film_shape)
 
 
 class GroupNormActConvFP8(torch.autograd.Function):
@@ -89,9 +83,8 @@ class GroupNormActConvFP8(torch.autograd.Function):
         ctx.dy_window.scatter_(0, ctx.window_pos.unsqueeze(0), dy_scale_curr.unsqueeze(0))
         d_act = ops.conv3x3_dgrad(dyq, wq, dy_hist, w_hist)
         dw = ops.conv3x3_wgrad(xq, dyq, x_hist, dy_hist)
-        dx, totals = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
-        dgamma, dbeta, dfilm = _norm_param_grads(totals, film2, x.shape[1], film_shape)
-        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None
+        dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
+        return dx, dgamma, dbeta, _film_grad(dfilm, film_shape), None, dw, None, None, None, None, None, None, None
 
 
 def group_norm_act(x: torch.Tensor, norm: torch.nn.GroupNorm, film: torch.Tensor | None = None,

@@ -518,8 +518,9 @@ def _(x, gamma, beta, film, seed, prev_scale, p, eps, groups):
 @torch.library.custom_op("fp8_b200::gn_act_bwd", mutates_args=())
 def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
                film: torch.Tensor | None, seed: torch.Tensor | None, stats: torch.Tensor, p: float, eps: float,
-               groups: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Backward of gn_act_fwd -> (dx in x's dtype, channels_last; totals [N, 3, C]: sums of df, df*z, df*xhat)."""
+               groups: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Backward of gn_act_fwd -> (dx in x's dtype, channels_last; dgamma, dbeta fp32 [C]; dfilm bf16 [N, 2C], or
+    an empty tensor without FiLM)."""
     dev = _require_cuda(x, dy, gamma, beta, stats)
     n, c, hw = _gn_check(x, gamma, beta, film, groups)
     dy = dy.contiguous(memory_format=torch.channels_last)
@@ -534,10 +535,18 @@ def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: tor
             _ptr(x), int(x.dtype == torch.float32), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps),
             _ptr(stats), _ptr(totals), _ptr(dx), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)),
             "fp8_gn_act_bwd")
-    return dx, totals
+        dgamma = torch.empty((c,), device=dev, dtype=torch.float32)
+        dbeta = torch.empty((c,), device=dev, dtype=torch.float32)
+        dfilm = torch.empty((n, 2 * c) if film is not None else (0,), device=dev, dtype=torch.bfloat16)
+        _lib.check(lib.fp8_gn_param_grads(_ptr(totals), _ptr(film), 2 * c, n, c, _ptr(dgamma), _ptr(dbeta),
+                                          _ptr(dfilm) if film is not None else None, 2 * c, _stream(dev)),
+                   "fp8_gn_param_grads")
+    return dx, dgamma, dbeta, dfilm
 
 
 @gn_act_bwd.register_fake
 def _(x, dy, gamma, beta, film, seed, stats, p, eps, groups):
-    return (torch.empty_like(x, memory_format=torch.channels_last),
-            x.new_empty((x.shape[0], 3, x.shape[1]), dtype=torch.float32))
+    n, c = x.shape[0], x.shape[1]
+    return (torch.empty_like(x, memory_format=torch.channels_last), x.new_empty((c,), dtype=torch.float32),
+            x.new_empty((c,), dtype=torch.float32),
+            x.new_empty((n, 2 * c) if film is not None else (0,), dtype=torch.bfloat16))
