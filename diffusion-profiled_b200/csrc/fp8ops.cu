@@ -629,8 +629,9 @@ size_t gn_workspace(int n, int hw, int c, int sm_count) {
 template <typename TX, bool QUANT>
 int launch_gn_fwd(const TX* x, GnShape sh, float* part, const GnActParams& q, float* stats, const GnOut& o,
                   size_t s1, size_t s2, int sm_count, cudaStream_t cs, int* apply_ctas = nullptr) {
+  const bool drop = q.seed != nullptr && q.p > 0.0f;
   auto k1 = gn_stats_kernel<TX>;
-  auto k2 = gn_act_fwd_kernel<TX, QUANT>;
+  auto k2 = drop ? gn_act_fwd_kernel<TX, QUANT, true> : gn_act_fwd_kernel<TX, QUANT, false>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s1)));
   FP8_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s2)));
   int sl1 = 1, sl2 = 1;
@@ -651,8 +652,9 @@ int launch_gn_fwd(const TX* x, GnShape sh, float* part, const GnActParams& q, fl
 template <typename TX>
 int launch_gn_bwd(const TX* x, const uint16_t* dy, GnShape sh, const float* stats, const GnActParams& q,
                   float* part, float* totals, TX* dx, size_t s1, size_t s2, int sm_count, cudaStream_t cs) {
-  auto k1 = gn_act_bwd_reduce_kernel<TX>;
-  auto k2 = gn_act_bwd_apply_kernel<TX>;
+  const bool drop = q.seed != nullptr && q.p > 0.0f;
+  auto k1 = drop ? gn_act_bwd_reduce_kernel<TX, true> : gn_act_bwd_reduce_kernel<TX, false>;
+  auto k2 = drop ? gn_act_bwd_apply_kernel<TX, true> : gn_act_bwd_apply_kernel<TX, false>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s1)));
   FP8_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s2)));
   int sl1 = 1, sl2 = 1;

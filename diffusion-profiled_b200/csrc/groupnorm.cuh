@@ -45,6 +45,9 @@ namespace fp8b {
 #ifndef FP8_GN_MINB_BWD
 #define FP8_GN_MINB_BWD 1
 #endif
+#ifndef FP8_GN_MINB_FWD
+#define FP8_GN_MINB_FWD 1
+#endif
 constexpr int kGnThreads = FP8_GN_THREADS;
 constexpr int kGnUnrollFwd = FP8_GN_UF;  // pixel rows per step, forward kernels
 constexpr int kGnUnrollBwd = FP8_GN_UB;  // pixel rows per step, backward kernels
@@ -207,10 +210,10 @@ __host__ __device__ constexpr size_t gn_reduce_smem(int c, int nv) {
 __host__ __device__ constexpr size_t gn_stats_smem(int c) { return gn_reduce_smem(c, 2); }
 __host__ __device__ constexpr size_t gn_fwd_smem(int c, int g) { return (2 * static_cast<size_t>(g) + 4 * c) * 4; }
 __host__ __device__ constexpr size_t gn_bwd_reduce_smem(int c, int g) {
-  return (4 * static_cast<size_t>(c) + 2 * g) * 4 + gn_reduce_smem(c, 3);
+  return (2 * static_cast<size_t>(c) + 2 * g) * 4 + gn_reduce_smem(c, 2);
 }
 __host__ __device__ constexpr size_t gn_bwd_apply_smem(int c, int g) {
-  return (8 * static_cast<size_t>(c) + 4 * g) * 4;
+  return (5 * static_cast<size_t>(c) + 4 * g) * 4;
 }
 
 // ------------------------------------------------------------------ statistics
@@ -341,11 +344,10 @@ struct NoCast {};
 
 // The streaming loop of the apply pass over this thread's pixel rows; returns
 // the packed max |bf16 activation| (QUANT) or 0.
-template <typename TX, bool QUANT, class Div>
+template <typename TX, bool QUANT, bool DROP, class Div>
 __device__ __forceinline__ uint32_t gn_apply_rows(const TX* __restrict__ xs, const GnThread& t, int64_t base,
-                                                  const float (&a)[8], const float (&b)[8], bool drop,
-                                                  uint64_t seed, uint32_t thresh, float keep_scale, const GnOut& o,
-                                                  const Div& div) {
+                                                  const float (&a)[8], const float (&b)[8], uint64_t seed,
+                                                  uint32_t thresh, float keep_scale, const GnOut& o, const Div& div) {
   uint32_t m2 = 0u;
   for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollFwd * t.rows) {
     XVec<TX> v[kGnUnrollFwd];
@@ -361,12 +363,14 @@ __device__ __forceinline__ uint32_t gn_apply_rows(const TX* __restrict__ xs, con
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
       float f[8];
       unpack_x8(v[u], f);
-      const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
+      const uint32_t keep = DROP ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float z = fmaf(a[k], f[k], b[k]);
-        const float act = silu_f32(z) * keep_scale;
-        f[k] = (keep >> k) & 1u ? act : 0.0f;
+        const float act = silu_f32(fmaf(a[k], f[k], b[k]));
+        if constexpr (DROP)
+          f[k] = (keep >> k) & 1u ? act * keep_scale : 0.0f;
+        else
+          f[k] = act;
       }
       const uint4 h = pack8(f);
       if constexpr (QUANT) {
@@ -380,8 +384,8 @@ __device__ __forceinline__ uint32_t gn_apply_rows(const TX* __restrict__ xs, con
   return m2;
 }
 
-template <typename TX, bool QUANT>
-__global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __restrict__ x, GnShape s,
+template <typename TX, bool QUANT, bool DROP>
+__global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_FWD) gn_act_fwd_kernel(const TX* __restrict__ x, GnShape s,
                                                                 const float* __restrict__ part, GnActParams q,
                                                                 float* __restrict__ stats, GnOut o) {
   extern __shared__ float gn_smem[];
@@ -408,20 +412,19 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __rest
       a[k] = A[t.v * 8 + k];
       b[k] = B[t.v * 8 + k];
     }
-    const bool drop = q.seed != nullptr && q.p > 0.0f;
-    const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
+    const uint64_t seed = DROP ? static_cast<uint64_t>(*q.seed) : 0ull;
     const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
-    const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
+    const float keep_scale = DROP ? 1.0f / (1.0f - q.p) : 1.0f;
     const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
     const TX* xs = x + base * 8;
     if constexpr (QUANT) {
       // the scale is uniform over the grid, so the choice never diverges
       const float sc = *o.prev_scale;
       m2 = markstein_applies(sc)
-               ? gn_apply_rows<TX, true>(xs, t, base, a, b, drop, seed, thresh, keep_scale, o, make_markstein(sc))
-               : gn_apply_rows<TX, true>(xs, t, base, a, b, drop, seed, thresh, keep_scale, o, DivF64(sc));
+               ? gn_apply_rows<TX, true, DROP>(xs, t, base, a, b, seed, thresh, keep_scale, o, make_markstein(sc))
+               : gn_apply_rows<TX, true, DROP>(xs, t, base, a, b, seed, thresh, keep_scale, o, DivF64(sc));
     } else {
-      gn_apply_rows<TX, false>(xs, t, base, a, b, drop, seed, thresh, keep_scale, o, NoCast{});
+      gn_apply_rows<TX, false, DROP>(xs, t, base, a, b, seed, thresh, keep_scale, o, NoCast{});
     }
   }
   if constexpr (QUANT) {
@@ -430,13 +433,39 @@ __global__ void __launch_bounds__(kGnThreads) gn_act_fwd_kernel(const TX* __rest
   }
 }
 
-// Recompute, per element of one 8-channel vector: z, f, and df = dL/df.
-struct GnBwdElem {
-  float z, df, xhat;
+// Per-thread constants of the backward passes for its 8 channels: the affine
+// map f = a x + b and xhat = rs x + nmr (nmr = -mean * rs).
+struct GnBwdCoeffs {
+  float a[8], b[8], rs[8], nmr[8];
 };
 
-// part[(n * slices + slice) * 3C + {0, C, 2C} + c] = sum df, sum df * z, sum df * xhat
-template <typename TX>
+__device__ __forceinline__ void gn_bwd_coeffs(const GnThread& t, const GnShape& s, const float* A, const float* B,
+                                              const float* mean_g, const float* rstd_g, GnBwdCoeffs& k) {
+  const int cg = s.c / s.groups;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = t.v * 8 + j;
+    const int g = c / cg;
+    k.a[j] = A[c];
+    k.b[j] = B[c];
+    k.rs[j] = rstd_g[g];
+    k.nmr[j] = -mean_g[g] * rstd_g[g];
+  }
+}
+
+// df = dL/df for one element: the activation's derivative (silu' = sg (1 + f (1 - sg)))
+// times the incoming gradient, scaled by the dropout keep factor when DROP.
+template <bool DROP>
+__device__ __forceinline__ float gn_df(float f, float g, uint32_t keep, int k, float keep_scale) {
+  const float sg = sigmoid_f32(f);
+  float du = g;
+  if constexpr (DROP) du = (keep >> k) & 1u ? g * keep_scale : 0.0f;
+  return du * sg * fmaf(f, 1.0f - sg, 1.0f);
+}
+
+// part[(n * slices + slice) * 2C + {0, C} + c] = sum df, sum df * xhat.  (The FiLM
+// scale gradient's sum of df * z follows from these: z = gamma xhat + beta.)
+template <typename TX, bool DROP>
 __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_reduce_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
     GnActParams q, float* __restrict__ part) {
@@ -444,37 +473,24 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_reduce
   pdl_wait();
   float* A = gn_smem;
   float* B = A + s.c;
-  float* az = B + s.c;
-  float* bz = az + s.c;
-  float* mean_g = bz + s.c;
+  float* mean_g = B + s.c;
   float* rstd_g = mean_g + s.groups;
   float* buf = rstd_g + s.groups;
   const GnThread t = gn_thread(s);
-  float* red = buf + static_cast<size_t>(t.rows) * 3 * s.c;
+  float* red = buf + static_cast<size_t>(t.rows) * 2 * s.c;
   for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
     mean_g[g] = stats[static_cast<int64_t>(t.n) * 2 * s.groups + g];
     rstd_g[g] = stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g];
   }
   __syncthreads();
-  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, az, bz);
-  float acc[3][8] = {};
+  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, nullptr, nullptr);
+  float acc[2][8] = {};
   if (t.r < t.rows) {
-    const int cg = s.c / s.groups;
-    float a[8], b[8], za[8], zb[8], mu[8], rs[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int c = t.v * 8 + k;
-      a[k] = A[c];
-      b[k] = B[c];
-      za[k] = az[c];
-      zb[k] = bz[c];
-      mu[k] = mean_g[c / cg];
-      rs[k] = rstd_g[c / cg];
-    }
-    const bool drop = q.seed != nullptr && q.p > 0.0f;
-    const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
+    GnBwdCoeffs k;
+    gn_bwd_coeffs(t, s, A, B, mean_g, rstd_g, k);
+    const uint64_t seed = DROP ? static_cast<uint64_t>(*q.seed) : 0ull;
     const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
-    const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
+    const float keep_scale = DROP ? 1.0f / (1.0f - q.p) : 1.0f;
     const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
     const TX* xs = x + base * 8;
     const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
@@ -496,28 +512,25 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_reduce
         float xf[8], gf[8];
         unpack_x8(vx[u], xf);
         unpack8(vd[u], gf);
-        const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
+        const uint32_t keep = DROP ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float f = fmaf(a[k], xf[k], b[k]);
-          const float sg = sigmoid_f32(f);
-          const float du = (keep >> k) & 1u ? gf[k] * keep_scale : 0.0f;
-          const float df = du * sg * fmaf(f, 1.0f - sg, 1.0f);
-          acc[0][k] += df;
-          acc[1][k] = fmaf(df, fmaf(za[k], xf[k], zb[k]), acc[1][k]);
-          acc[2][k] = fmaf(df, (xf[k] - mu[k]) * rs[k], acc[2][k]);
+        for (int j = 0; j < 8; ++j) {
+          const float df = gn_df<DROP>(fmaf(k.a[j], xf[j], k.b[j]), gf[j], keep, j, keep_scale);
+          acc[0][j] += df;
+          acc[1][j] = fmaf(df, fmaf(xf[j], k.rs[j], k.nmr[j]), acc[1][j]);
         }
       }
     }
   }
-  gn_reduce_rows<3>(t, s, acc, buf, red);
-  float* out = part + static_cast<int64_t>(blockIdx.x) * 3 * s.c;
-  for (int i = threadIdx.x; i < 3 * s.c; i += blockDim.x) out[i] = red[i];
+  gn_reduce_rows<2>(t, s, acc, buf, red);
+  float* out = part + static_cast<int64_t>(blockIdx.x) * 2 * s.c;
+  for (int i = threadIdx.x; i < 2 * s.c; i += blockDim.x) out[i] = red[i];
 }
 
 // totals[n * 3C + {0, C, 2C} + c] = sum df, sum df z, sum df xhat over the sample
-// (written by slice 0); dx as above.
-template <typename TX>
+// (written by slice 0); dx = rstd * (gamma (s+1) df - mean_g[gamma (s+1) df]
+// - xhat * mean_g[gamma (s+1) df xhat]).
+template <typename TX, bool DROP>
 __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
     GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx) {
@@ -525,12 +538,10 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
   pdl_wait();
   float* A = gn_smem;
   float* B = A + s.c;
-  float* az = B + s.c;
-  float* bz = az + s.c;
-  float* mean_g = bz + s.c;
+  float* mean_g = B + s.c;
   float* rstd_g = mean_g + s.groups;
-  float* tot = rstd_g + s.groups;  // [3][C]
-  float* g1 = tot + 3 * s.c;       // [G] mean over the group of gamma (s+1) df
+  float* tot = rstd_g + s.groups;  // [2][C]: sum df, sum df xhat
+  float* g1 = tot + 2 * s.c;       // [G] mean over the group of gamma (s+1) df
   float* g2 = g1 + s.groups;       // [G] mean over the group of gamma (s+1) df xhat
   float* gs = g2 + s.groups;       // [C] gamma_c (s_nc + 1)
   const GnThread t = gn_thread(s);
@@ -539,14 +550,13 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
     rstd_g[g] = stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g];
   }
   __syncthreads();
-  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, az, bz);
+  gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, nullptr, nullptr);
   const bool first = blockIdx.x % s.slices == 0;
-  for (int i = threadIdx.x; i < 3 * s.c; i += blockDim.x) {
+  for (int i = threadIdx.x; i < 2 * s.c; i += blockDim.x) {
     float v = 0.0f;
     for (int k = 0; k < s.part_slices; ++k)
-      v += part[(static_cast<int64_t>(t.n) * s.part_slices + k) * 3 * s.c + i];
+      v += part[(static_cast<int64_t>(t.n) * s.part_slices + k) * 2 * s.c + i];
     tot[i] = v;
-    if (first) totals[static_cast<int64_t>(t.n) * 3 * s.c + i] = v;
   }
   for (int c = threadIdx.x; c < s.c; c += blockDim.x) {
     float sc = 1.0f;
@@ -555,6 +565,13 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
     gs[c] = q.gamma[c] * sc;
   }
   __syncthreads();
+  if (first)
+    for (int c = threadIdx.x; c < s.c; c += blockDim.x) {
+      float* tn = totals + static_cast<int64_t>(t.n) * 3 * s.c;
+      tn[c] = tot[c];
+      tn[s.c + c] = fmaf(q.gamma[c], tot[s.c + c], q.beta[c] * tot[c]);  // sum df z, z = gamma xhat + beta
+      tn[2 * s.c + c] = tot[s.c + c];
+    }
   const int cg = s.c / s.groups;
   const float inv_m = 1.0f / (static_cast<float>(s.hw) * static_cast<float>(cg));
   for (int g = threadIdx.x; g < s.groups; g += blockDim.x) {
@@ -562,30 +579,27 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
     for (int j = 0; j < cg; ++j) {
       const int c = g * cg + j;
       s1 = fmaf(gs[c], tot[c], s1);
-      s3 = fmaf(gs[c], tot[2 * s.c + c], s3);
+      s3 = fmaf(gs[c], tot[s.c + c], s3);
     }
     g1[g] = s1 * inv_m;
     g2[g] = s3 * inv_m;
   }
   __syncthreads();
   if (t.r >= t.rows) return;
-  float a[8], b[8], mu[8], rs[8], gk[8], m1[8], m2[8];
+  GnBwdCoeffs k;
+  gn_bwd_coeffs(t, s, A, B, mean_g, rstd_g, k);
+  float gk[8], m1[8], m2[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int c = t.v * 8 + k;
+  for (int j = 0; j < 8; ++j) {
+    const int c = t.v * 8 + j;
     const int g = c / cg;
-    a[k] = A[c];
-    b[k] = B[c];
-    mu[k] = mean_g[g];
-    rs[k] = rstd_g[g];
-    gk[k] = gs[c];
-    m1[k] = g1[g];
-    m2[k] = g2[g];
+    gk[j] = gs[c];
+    m1[j] = g1[g];
+    m2[j] = g2[g];
   }
-  const bool drop = q.seed != nullptr && q.p > 0.0f;
-  const uint64_t seed = drop ? static_cast<uint64_t>(*q.seed) : 0ull;
+  const uint64_t seed = DROP ? static_cast<uint64_t>(*q.seed) : 0ull;
   const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
-  const float keep_scale = drop ? 1.0f / (1.0f - q.p) : 1.0f;
+  const float keep_scale = DROP ? 1.0f / (1.0f - q.p) : 1.0f;
   const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
   const TX* xs = x + base * 8;
   const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
@@ -608,15 +622,12 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
       float xf[8], gf[8], o[8];
       unpack_x8(vx[u], xf);
       unpack8(vd[u], gf);
-      const uint32_t keep = drop ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
+      const uint32_t keep = DROP ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float f = fmaf(a[k], xf[k], b[k]);
-        const float sg = sigmoid_f32(f);
-        const float du = (keep >> k) & 1u ? gf[k] * keep_scale : 0.0f;
-        const float df = du * sg * fmaf(f, 1.0f - sg, 1.0f);
-        const float xhat = (xf[k] - mu[k]) * rs[k];
-        o[k] = rs[k] * (gk[k] * df - m1[k] - xhat * m2[k]);
+      for (int j = 0; j < 8; ++j) {
+        const float df = gn_df<DROP>(fmaf(k.a[j], xf[j], k.b[j]), gf[j], keep, j, keep_scale);
+        const float xhat = fmaf(xf[j], k.rs[j], k.nmr[j]);
+        o[j] = k.rs[j] * (gk[j] * df - m1[j] - xhat * m2[j]);
       }
       store_x8(os, vi, o);
     }
