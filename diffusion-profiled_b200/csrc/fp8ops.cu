@@ -21,6 +21,7 @@
 #include "conv_halo_t.cuh"
 #include "groupnorm.cuh"
 #include "layernorm.cuh"
+#include "resample.cuh"
 
 using namespace fp8b;
 
@@ -1582,3 +1583,133 @@ extern "C" int fp8_gn_param_grads(const float* totals, const void* film, int fil
   count_launches(1);
   return ok();
 }
+
+// ======================================================================== resampling + concatenation
+namespace {
+
+unsigned resample_grid(int64_t vectors, int sm_count) {
+  const int64_t blocks = (vectors + kResampleThreads - 1) / kResampleThreads;
+  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(blocks, 16ll * sm_count)));
+}
+
+int check_resample(const void* p, int dtype, const char* what) {
+  FP8_REQUIRE(dtype == 0 || dtype == 1, FP8_ERR_INVALID_ARGUMENT, "%s dtype must be 0 (bf16) or 1 (fp32)", what);
+  FP8_REQUIRE(p != nullptr && aligned(p, 16), FP8_ERR_INVALID_ARGUMENT, "%s must be non-NULL and 16-byte aligned",
+              what);
+  return FP8_OK;
+}
+
+template <typename TA, typename TS, typename TO>
+int launch_up_cat(const void* a, const void* s, void* y, int n, int h, int w, int c1, int c2, int f, bool bwd,
+                  int sm_count, cudaStream_t cs) {
+  const int64_t vecs = static_cast<int64_t>(n) * h * w * (c1 + c2) / 8;
+  if (!bwd) {
+    FP8_CUDA_TRY(launch_kernel(up_cat_kernel<TA, TS, TO>, dim3(resample_grid(vecs, sm_count)), dim3(kResampleThreads),
+                               0, cs, 1, kStreamingKernel, static_cast<const TA*>(a), static_cast<const TS*>(s), n, h,
+                               w, c1, c2, f, static_cast<TO*>(y)));
+  } else {  // a, s are the gradients (outputs); y is the incoming gradient
+    FP8_CUDA_TRY(launch_kernel(up_cat_bwd_kernel<TA, TS, TO>, dim3(resample_grid(vecs, sm_count)),
+                               dim3(kResampleThreads), 0, cs, 1, kStreamingKernel, static_cast<const TO*>(y), n, h, w,
+                               c1, c2, f, static_cast<TA*>(const_cast<void*>(a)),
+                               static_cast<TS*>(const_cast<void*>(s))));
+  }
+  count_launches(1);
+  return FP8_OK;
+}
+
+template <typename TA, typename TS>
+int up_cat_out(int y_dtype, const void* a, const void* s, void* y, int n, int h, int w, int c1, int c2, int f,
+               bool bwd, int sms, cudaStream_t cs) {
+  return y_dtype ? launch_up_cat<TA, TS, float>(a, s, y, n, h, w, c1, c2, f, bwd, sms, cs)
+                 : launch_up_cat<TA, TS, uint16_t>(a, s, y, n, h, w, c1, c2, f, bwd, sms, cs);
+}
+
+int up_cat_dispatch(int a_dtype, int s_dtype, int y_dtype, const void* a, const void* s, void* y, int n, int h, int w,
+                    int c1, int c2, int f, bool bwd, int sms, cudaStream_t cs) {
+  if (a_dtype)
+    return s_dtype ? up_cat_out<float, float>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs)
+                   : up_cat_out<float, uint16_t>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs);
+  return s_dtype ? up_cat_out<uint16_t, float>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs)
+                 : up_cat_out<uint16_t, uint16_t>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs);
+}
+
+int check_up_cat(int n, int h, int w, int c1, int c2, int factor) {
+  FP8_REQUIRE(n > 0 && h > 0 && w > 0 && c1 > 0 && c2 > 0, FP8_ERR_INVALID_ARGUMENT, "bad sizes");
+  FP8_REQUIRE(c1 % 8 == 0 && c2 % 8 == 0, FP8_ERR_UNSUPPORTED, "channel counts must be multiples of 8");
+  FP8_REQUIRE((factor == 1 || factor == 2) && h % factor == 0 && w % factor == 0, FP8_ERR_UNSUPPORTED,
+              "factor must be 1 or 2 and divide the output size");
+  return FP8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fp8_resample_down2(const void* x, int x_dtype, float* y, int n, int h, int w, int c, fp8_stream_t stream) {
+  FP8_REQUIRE(n > 0 && h > 0 && w > 0 && c > 0, FP8_ERR_INVALID_ARGUMENT, "bad sizes");
+  FP8_REQUIRE(c % 8 == 0 && h % 2 == 0 && w % 2 == 0, FP8_ERR_UNSUPPORTED, "needs c %% 8 == 0 and even h, w");
+  if (int s = check_resample(x, x_dtype, "x")) return s;
+  if (int s = check_resample(y, 1, "y")) return s;
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 grid(resample_grid(static_cast<int64_t>(n) * (h / 2) * (w / 2) * c / 8, st->sm_count));
+  if (x_dtype)
+    FP8_CUDA_TRY(launch_kernel(down2_kernel<float>, grid, dim3(kResampleThreads), 0, cs, 1, kStreamingKernel,
+                               static_cast<const float*>(x), n, h, w, c, y));
+  else
+    FP8_CUDA_TRY(launch_kernel(down2_kernel<uint16_t>, grid, dim3(kResampleThreads), 0, cs, 1, kStreamingKernel,
+                               static_cast<const uint16_t*>(x), n, h, w, c, y));
+  count_launches(1);
+  return ok();
+}
+
+int fp8_resample_down2_bwd(const float* dy, void* dx, int dx_dtype, int n, int h, int w, int c,
+                           fp8_stream_t stream) {
+  FP8_REQUIRE(n > 0 && h > 0 && w > 0 && c > 0, FP8_ERR_INVALID_ARGUMENT, "bad sizes");
+  FP8_REQUIRE(c % 8 == 0 && h % 2 == 0 && w % 2 == 0, FP8_ERR_UNSUPPORTED, "needs c %% 8 == 0 and even h, w");
+  if (int s = check_resample(dy, 1, "dy")) return s;
+  if (int s = check_resample(dx, dx_dtype, "dx")) return s;
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 grid(resample_grid(static_cast<int64_t>(n) * h * w * c / 8, st->sm_count));
+  if (dx_dtype)
+    FP8_CUDA_TRY(launch_kernel(down2_bwd_kernel<float>, grid, dim3(kResampleThreads), 0, cs, 1, kStreamingKernel, dy,
+                               n, h, w, c, static_cast<float*>(dx)));
+  else
+    FP8_CUDA_TRY(launch_kernel(down2_bwd_kernel<uint16_t>, grid, dim3(kResampleThreads), 0, cs, 1, kStreamingKernel,
+                               dy, n, h, w, c, static_cast<uint16_t*>(dx)));
+  count_launches(1);
+  return ok();
+}
+
+int fp8_up_cat(const void* a, int a_dtype, const void* s, int s_dtype, void* y, int y_dtype, int n, int h, int w,
+               int c1, int c2, int factor, fp8_stream_t stream) {
+  if (int r = check_up_cat(n, h, w, c1, c2, factor)) return r;
+  if (int r = check_resample(a, a_dtype, "a")) return r;
+  if (int r = check_resample(s, s_dtype, "s")) return r;
+  if (int r = check_resample(y, y_dtype, "y")) return r;
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, a, s, y, n, h, w, c1, c2, factor, false, st->sm_count,
+                              reinterpret_cast<cudaStream_t>(stream)))
+    return r;
+  return ok();
+}
+
+int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds, int s_dtype, int n, int h, int w,
+                   int c1, int c2, int factor, fp8_stream_t stream) {
+  if (int r = check_up_cat(n, h, w, c1, c2, factor)) return r;
+  if (int r = check_resample(dy, y_dtype, "dy")) return r;
+  if (int r = check_resample(da, a_dtype, "da")) return r;
+  if (int r = check_resample(ds, s_dtype, "ds")) return r;
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, da, ds, const_cast<void*>(dy), n, h, w, c1, c2, factor, true,
+                              st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+    return r;
+  return ok();
+}
+
+}  // extern "C"

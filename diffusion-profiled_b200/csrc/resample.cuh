@@ -1,0 +1,142 @@
+// resample.cuh — the UNet's nearest-neighbour resampling and skip concatenation
+// on NHWC activations, in the dtypes the reference produces under bf16 autocast
+// (reference unet.py:368-383: F.interpolate(x, scale_factor=0.5 / 2.0,
+// mode="nearest") runs in fp32 under autocast, so its output is fp32 whatever
+// the input; torch.cat promotes to the widest input dtype).
+//
+//   down2      : y[n, h, w, c] = fp32(x[n, 2h, 2w, c])                  (scale 0.5)
+//   down2 bwd  : dx[n, h, w, c] = (h, w even) ? dy[n, h/2, w/2, c] : 0   (in x's dtype)
+//   up_cat     : y[n, h, w, 0:C1]      = a[n, h/f, w/f, :]               (f = 2, or 1: no resampling)
+//                y[n, h, w, C1:C1+C2]  = s[n, h, w, :]
+//   up_cat bwd : da[n, h, w, c] = sum over the f x f block of dy[.., c]  (fp32 sum, rounded to a's dtype)
+//                ds[n, h, w, c] = dy[n, h, w, C1 + c]                    (in s's dtype)
+//
+// One kernel per direction: the autocast casts, the separate resampling pass
+// and the concatenation copy become one read and one write of each element.
+// Each thread moves vectors of 8 channels (C1, C2 multiples of 8).
+#pragma once
+
+#include "groupnorm.cuh"
+
+namespace fp8b {
+
+constexpr int kResampleThreads = 256;
+
+// 8 channels of type T at vector index vi (8 elements per vector) as fp32, and back.
+template <typename T>
+__device__ __forceinline__ void load8f(const T* __restrict__ p, int64_t vi, float (&f)[8]) {
+  unpack_x8(load_x8(p, vi), f);
+}
+
+template <typename TX>
+__global__ void __launch_bounds__(kResampleThreads) down2_kernel(const TX* __restrict__ x, int n, int h, int w,
+                                                                 int c, float* __restrict__ y) {
+  pdl_wait();
+  const int ho = h / 2, wo = w / 2, vecs = c / 8;
+  const int64_t total = static_cast<int64_t>(n) * ho * wo * vecs;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = static_cast<int>(i % vecs);
+    const int64_t pix = i / vecs;
+    const int wq = static_cast<int>(pix % wo);
+    const int64_t r = pix / wo;
+    const int hq = static_cast<int>(r % ho);
+    const int64_t img = r / ho;
+    const int64_t src = ((img * h + 2 * hq) * w + 2 * wq) * vecs + v;
+    float f[8];
+    load8f(x, src, f);
+    store_x8(y, i, f);
+  }
+}
+
+template <typename TX>
+__global__ void __launch_bounds__(kResampleThreads) down2_bwd_kernel(const float* __restrict__ dy, int n, int h,
+                                                                     int w, int c, TX* __restrict__ dx) {
+  pdl_wait();
+  const int ho = h / 2, wo = w / 2, vecs = c / 8;
+  const int64_t total = static_cast<int64_t>(n) * h * w * vecs;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = static_cast<int>(i % vecs);
+    const int64_t pix = i / vecs;
+    const int wi = static_cast<int>(pix % w);
+    const int64_t r = pix / w;
+    const int hi = static_cast<int>(r % h);
+    const int64_t img = r / h;
+    float f[8];
+    if (((hi | wi) & 1) == 0 && hi / 2 < ho && wi / 2 < wo) {
+      load8f(dy, ((img * ho + hi / 2) * wo + wi / 2) * vecs + v, f);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = 0.0f;
+    }
+    store_x8(dx, i, f);
+  }
+}
+
+// y has C1 + C2 channels at (h, w); a is (h / f, w / f) with C1 channels; s is (h, w) with C2.
+template <typename TA, typename TS, typename TO>
+__global__ void __launch_bounds__(kResampleThreads) up_cat_kernel(const TA* __restrict__ a, const TS* __restrict__ s,
+                                                                  int n, int h, int w, int c1, int c2, int f,
+                                                                  TO* __restrict__ y) {
+  pdl_wait();
+  const int v1 = c1 / 8, vecs = (c1 + c2) / 8;
+  const int ha = h / f, wa = w / f;
+  const int64_t total = static_cast<int64_t>(n) * h * w * vecs;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = static_cast<int>(i % vecs);
+    const int64_t pix = i / vecs;
+    float e[8];
+    if (v < v1) {
+      const int wi = static_cast<int>(pix % w);
+      const int64_t r = pix / w;
+      const int hi = static_cast<int>(r % h);
+      const int64_t img = r / h;
+      load8f(a, ((img * ha + hi / f) * wa + wi / f) * v1 + v, e);
+    } else {
+      load8f(s, pix * (vecs - v1) + (v - v1), e);
+    }
+    store_x8(y, i, e);
+  }
+}
+
+template <typename TA, typename TS, typename TO>
+__global__ void __launch_bounds__(kResampleThreads) up_cat_bwd_kernel(const TO* __restrict__ dy, int n, int h, int w,
+                                                                      int c1, int c2, int f, TA* __restrict__ da,
+                                                                      TS* __restrict__ ds) {
+  pdl_wait();
+  const int v1 = c1 / 8, v2 = c2 / 8, vecs = v1 + v2;
+  const int ha = h / f, wa = w / f;
+  const int64_t total_a = static_cast<int64_t>(n) * ha * wa * v1;
+  const int64_t total_s = static_cast<int64_t>(n) * h * w * v2;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total_a + total_s;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (i < total_a) {
+      const int v = static_cast<int>(i % v1);
+      const int64_t pix = i / v1;
+      const int wq = static_cast<int>(pix % wa);
+      const int64_t r = pix / wa;
+      const int hq = static_cast<int>(r % ha);
+      const int64_t img = r / ha;
+      float acc[8] = {};
+      for (int di = 0; di < f; ++di)
+        for (int dj = 0; dj < f; ++dj) {
+          float e[8];
+          load8f(dy, ((img * h + hq * f + di) * w + wq * f + dj) * vecs + v, e);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[k] += e[k];
+        }
+      store_x8(da, i, acc);
+    } else {
+      const int64_t j = i - total_a;
+      const int v = static_cast<int>(j % v2);
+      const int64_t pix = j / v2;
+      float e[8];
+      load8f(dy, pix * vecs + v1 + v, e);
+      store_x8(ds, j, e);
+    }
+  }
+}
+
+}  // namespace fp8b

@@ -89,6 +89,14 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "fp8_gn_param_grads": (
         c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "fp8_resample_down2": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "fp8_resample_down2_bwd": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "fp8_up_cat": (
+        c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                c_void_p]),
+    "fp8_up_cat_bwd": (
+        c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                c_void_p]),
     "fp8_gn_act_quant_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_quant_fwd": (
         c_int,

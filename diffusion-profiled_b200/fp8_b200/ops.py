@@ -483,6 +483,104 @@ def _(x, dy, gamma, mean_rstd):
     return torch.empty_like(x), x.new_empty((c,), dtype=torch.float32), x.new_empty((c,), dtype=torch.float32)
 
 
+_DT = {torch.bfloat16: 0, torch.float32: 1}
+
+
+def _resample_check(t: torch.Tensor, name: str) -> None:
+    if t.dtype not in _DT or t.dim() != 4 or not t.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError(f"{name} must be a channels_last bfloat16 / float32 NCHW tensor")
+
+
+@torch.library.custom_op("fp8_b200::resample_down2", mutates_args=())
+def resample_down2(x: torch.Tensor) -> torch.Tensor:
+    """Nearest downsampling by 2 -> fp32 (F.interpolate(scale_factor=0.5) under bf16 autocast, unet.py:368)."""
+    dev = _require_cuda(x)
+    _resample_check(x, "x")
+    n, c, h, w = x.shape
+    y = torch.empty((n, c, h // 2, w // 2), device=dev, dtype=torch.float32, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_resample_down2", _ptr(x), _DT[x.dtype], _ptr(y), n, h, w, c, _stream(dev))
+    return y
+
+
+@resample_down2.register_fake
+def _(x):
+    n, c, h, w = x.shape
+    return x.new_empty((n, c, h // 2, w // 2), dtype=torch.float32).contiguous(memory_format=torch.channels_last)
+
+
+@torch.library.custom_op("fp8_b200::resample_down2_bwd", mutates_args=())
+def resample_down2_bwd(dy: torch.Tensor, h: int, w: int, x_fp32: bool) -> torch.Tensor:
+    """Gradient of resample_down2: dy at the even pixels, zeros elsewhere, in the input's dtype."""
+    dev = _require_cuda(dy)
+    dy = dy.float().contiguous(memory_format=torch.channels_last)
+    n, c = dy.shape[0], dy.shape[1]
+    dt = torch.float32 if x_fp32 else torch.bfloat16
+    dx = torch.empty((n, c, h, w), device=dev, dtype=dt, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_resample_down2_bwd", _ptr(dy), _ptr(dx), _DT[dt], n, h, w, c, _stream(dev))
+    return dx
+
+
+@resample_down2_bwd.register_fake
+def _(dy, h, w, x_fp32):
+    dt = torch.float32 if x_fp32 else torch.bfloat16
+    return dy.new_empty((dy.shape[0], dy.shape[1], h, w), dtype=dt).contiguous(memory_format=torch.channels_last)
+
+
+@torch.library.custom_op("fp8_b200::up_cat", mutates_args=())
+def up_cat(a: torch.Tensor, s: torch.Tensor, factor: int, out_fp32: bool) -> torch.Tensor:
+    """cat([upsample_nearest(a, factor), s], dim=1) in one pass (unet.py:379-383); fp32 or bf16 out."""
+    dev = _require_cuda(a, s)
+    _resample_check(a, "a")
+    _resample_check(s, "s")
+    n, c1, ha, wa = a.shape
+    c2, h, w = s.shape[1], s.shape[2], s.shape[3]
+    if (s.shape[0], h, w) != (n, ha * factor, wa * factor):
+        raise RuntimeError("a upsampled by factor must match s in batch and spatial size")
+    dt = torch.float32 if out_fp32 else torch.bfloat16
+    y = torch.empty((n, c1 + c2, h, w), device=dev, dtype=dt, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_up_cat", _ptr(a), _DT[a.dtype], _ptr(s), _DT[s.dtype], _ptr(y), _DT[dt], n, h, w, c1, c2,
+                  factor, _stream(dev))
+    return y
+
+
+@up_cat.register_fake
+def _(a, s, factor, out_fp32):
+    dt = torch.float32 if out_fp32 else torch.bfloat16
+    return a.new_empty((a.shape[0], a.shape[1] + s.shape[1], s.shape[2], s.shape[3]), dtype=dt).contiguous(
+        memory_format=torch.channels_last)
+
+
+@torch.library.custom_op("fp8_b200::up_cat_bwd", mutates_args=())
+def up_cat_bwd(dy: torch.Tensor, c1: int, factor: int, a_fp32: bool,
+               s_fp32: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gradients of up_cat: (block sums of dy[:, :c1] in a's dtype, dy[:, c1:] in s's dtype)."""
+    dev = _require_cuda(dy)
+    dy = dy.contiguous(memory_format=torch.channels_last)
+    _resample_check(dy, "dy")
+    n, c, h, w = dy.shape
+    ta = torch.float32 if a_fp32 else torch.bfloat16
+    ts = torch.float32 if s_fp32 else torch.bfloat16
+    da = torch.empty((n, c1, h // factor, w // factor), device=dev, dtype=ta, memory_format=torch.channels_last)
+    ds = torch.empty((n, c - c1, h, w), device=dev, dtype=ts, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_up_cat_bwd", _ptr(dy), _DT[dy.dtype], _ptr(da), _DT[ta], _ptr(ds), _DT[ts], n, h, w, c1,
+                  c - c1, factor, _stream(dev))
+    return da, ds
+
+
+@up_cat_bwd.register_fake
+def _(dy, c1, factor, a_fp32, s_fp32):
+    n, c, h, w = dy.shape
+    ta = torch.float32 if a_fp32 else torch.bfloat16
+    ts = torch.float32 if s_fp32 else torch.bfloat16
+    cl = torch.channels_last
+    return (dy.new_empty((n, c1, h // factor, w // factor), dtype=ta).contiguous(memory_format=cl),
+            dy.new_empty((n, c - c1, h, w), dtype=ts).contiguous(memory_format=cl))
+
+
 @torch.library.custom_op("fp8_b200::gn_act_quant_fwd", mutates_args=())
 def gn_act_quant_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
                      seed: torch.Tensor | None, prev_scale: torch.Tensor, p: float, eps: float,

@@ -1,0 +1,69 @@
+"""Nearest-neighbour resampling and skip concatenation of the UNet as single passes.
+
+The reference UNet (unet.py:366-383) downsamples with
+``F.interpolate(x, scale_factor=0.5, mode="nearest")``, upsamples with
+``scale_factor=2.0`` and concatenates the skip with ``torch.cat(dim=1)``.  Under
+bf16 autocast ``F.interpolate`` runs in fp32 (its input is cast up first, its
+output is fp32) and ``torch.cat`` promotes to the wider dtype, so those lines
+cost a cast pass, a resampling pass and a concatenation copy.
+:func:`downsample_nearest` and :func:`upsample_cat` produce the same values and
+dtypes in one read and one write per element (``fp8_b200::resample_down2`` /
+``up_cat`` and their backward ops).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+class _Down2(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        ctx.shape = (x.shape[2], x.shape[3], x.dtype == torch.float32)
+        return ops.resample_down2(x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        h, w, x_fp32 = ctx.shape
+        return ops.resample_down2_bwd(dy, h, w, x_fp32)
+
+
+class _UpCat(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, s, factor: int, out_fp32: bool):
+        ctx.cfg = (a.shape[1], factor, a.dtype == torch.float32, s.dtype == torch.float32)
+        return ops.up_cat(a, s, factor, out_fp32)
+
+    @staticmethod
+    def backward(ctx, dy):
+        c1, factor, a_fp32, s_fp32 = ctx.cfg
+        da, ds = ops.up_cat_bwd(dy, c1, factor, a_fp32, s_fp32)
+        return da, ds, None, None
+
+
+def resample_supported(*ts: torch.Tensor) -> bool:
+    return all(t.is_cuda and t.dim() == 4 and t.dtype in (torch.bfloat16, torch.float32) and t.shape[1] % 8 == 0
+               and t.is_contiguous(memory_format=torch.channels_last) for t in ts)
+
+
+def downsample_nearest(x: torch.Tensor) -> torch.Tensor:
+    """``F.interpolate(x, scale_factor=0.5, mode="nearest")`` as bf16 autocast computes it (fp32 out)."""
+    if not (resample_supported(x) and x.shape[2] % 2 == 0 and x.shape[3] % 2 == 0
+            and (torch.is_autocast_enabled("cuda") or x.dtype == torch.float32)):
+        return torch.nn.functional.interpolate(x, scale_factor=0.5, mode="nearest")
+    return _Down2.apply(x)
+
+
+def upsample_cat(a: torch.Tensor, s: torch.Tensor, factor: int) -> torch.Tensor:
+    """``torch.cat([F.interpolate(a, scale_factor=factor, mode="nearest") if factor > 1 else a, s], dim=1)``."""
+    autocast = torch.is_autocast_enabled("cuda")
+    if not resample_supported(a, s) or factor not in (1, 2):
+        up = torch.nn.functional.interpolate(a, scale_factor=float(factor), mode="nearest") if factor > 1 else a
+        return torch.cat([up, s], dim=1)
+    up_fp32 = a.dtype == torch.float32 or (factor > 1 and autocast)
+    return _UpCat.apply(a, s, factor, up_fp32 or s.dtype == torch.float32)
+
+
+__all__ = ["downsample_nearest", "upsample_cat", "resample_supported"]

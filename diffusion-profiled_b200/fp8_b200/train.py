@@ -249,10 +249,14 @@ class GraphedTrainStep:
 
 
 def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16,), p_drop: float = 0.1,
-                device: torch.device | str = "cuda", seed: int = 0, fused_norm: bool = True) -> UNet:
+                device: torch.device | str = "cuda", seed: int = 0, fused_norm: bool = True,
+                fused_resample: bool | None = None) -> UNet:
+    """The reference UNet; ``fused_norm`` / ``fused_resample`` (default: as ``fused_norm``) route its
+    norm -> activation chains and its resampling + concatenation to this library's kernels."""
     torch.manual_seed(seed)
     cfg = UNetConfig(fp8_convs_enabled=fp8, fp8_scaling_type=scaling, attn_resolutions=list(attn_resolutions),
-                     p_drop=p_drop, fused_norm=fused_norm)
+                     p_drop=p_drop, fused_norm=fused_norm,
+                     fused_resample=fused_norm if fused_resample is None else fused_resample)
     model = UNet(cfg).to(memory_format=torch.channels_last)
     return model.to(device)
 

@@ -28,6 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
+from .resample import downsample_nearest, upsample_cat
 from .norm import GroupNormActConvFP8, fused_layer_norm_supported, fused_norm_supported, group_norm_act, layer_norm_bf16
 
 
@@ -48,6 +49,8 @@ class UNetConfig:
     # (fp8_b200.norm) where the activation is a bf16 CUDA tensor; the reference's
     # separate torch ops otherwise.  No parameters or buffers depend on it.
     fused_norm: bool = True
+    # nearest resampling + skip concatenation as single passes (fp8_b200.resample)
+    fused_resample: bool = True
 
     def as_dict(self):
         return asdict(self)
@@ -264,14 +267,20 @@ class UNet(nn.Module):
         t_emb = self.time_embed(self._timestep(t))
         act = self.conv_in(x)
         skips = []
+        fused = self.config.fused_resample
         for i, stage in enumerate(self.down_stages):
-            act = stage(F.interpolate(act, scale_factor=0.5, mode="nearest") if i > 0 else act, t_emb)
+            if i > 0:
+                act = downsample_nearest(act) if fused else F.interpolate(act, scale_factor=0.5, mode="nearest")
+            act = stage(act, t_emb)
             skips.append(act)
         act = self.mid(act, t_emb)
         for i, stage in enumerate(self.up_stages):
             h = skips.pop()
-            up = F.interpolate(act, scale_factor=2.0, mode="nearest") if i > 0 else act
-            act = stage(torch.cat([up, h], dim=1), t_emb)
+            if fused:
+                act = stage(upsample_cat(act, h, 2 if i > 0 else 1), t_emb)
+            else:
+                up = F.interpolate(act, scale_factor=2.0, mode="nearest") if i > 0 else act
+                act = stage(torch.cat([up, h], dim=1), t_emb)
         if self.config.fused_norm and fused_norm_supported(act, self.out[0]):
             return self.out[2](group_norm_act(act, self.out[0]))
         return self.out(act)

@@ -271,6 +271,26 @@ int fp8_layer_norm_bwd(const void* x, int x_fp32, const void* dy_bf16, const flo
 int fp8_gn_param_grads(const float* totals, const void* film, int film_ld, int n, int c, float* dgamma,
                        float* dbeta, void* dfilm, int dfilm_ld, fp8_stream_t stream);
 
+/* Nearest-neighbour resampling of the UNet (reference unet.py:368-383,
+ * F.interpolate(..., mode="nearest"), which bf16 autocast runs in fp32) on NHWC
+ * tensors; dtype codes: 0 = bf16, 1 = fp32.  c, c1, c2 multiples of 8; all
+ * tensors 16-byte aligned.
+ * fp8_resample_down2     : y (fp32) [n][h/2][w/2][c] = x[n][2i][2j][c] (scale 0.5)
+ * fp8_resample_down2_bwd : dx [n][h][w][c] = dy at even (i, j), else 0 (dx dtype given)
+ * fp8_up_cat     : y [n][h][w][c1 + c2] = (a[n][i/f][j/f][:], s[n][i][j][:]) with f = 2
+ *                  (upsample, scale 2) or 1, in y's dtype: the upsample and the
+ *                  skip concatenation (torch.cat, which promotes to the wider dtype)
+ *                  as one pass
+ * fp8_up_cat_bwd : da = fp32 sum of dy over each f x f block (channels 0..c1),
+ *                  ds = dy channels c1..c1+c2, each in its own dtype */
+int fp8_resample_down2(const void* x, int x_dtype, float* y, int n, int h, int w, int c, fp8_stream_t stream);
+int fp8_resample_down2_bwd(const float* dy, void* dx, int dx_dtype, int n, int h, int w, int c,
+                           fp8_stream_t stream);
+int fp8_up_cat(const void* a, int a_dtype, const void* s, int s_dtype, void* y, int y_dtype, int n, int h, int w,
+               int c1, int c2, int factor, fp8_stream_t stream);
+int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds, int s_dtype, int n, int h, int w,
+                   int c1, int c2, int factor, fp8_stream_t stream);
+
 /* Workspace bytes of fp8_gn_act_quant_fwd. */
 size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c);
 

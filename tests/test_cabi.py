@@ -174,3 +174,12 @@ def test_layer_norm_rejects_bad_channels_without_touching_cuda():
     )
     assert status == _lib.FP8_ERR_UNSUPPORTED and code == status and "c % 8" in msg
     assert lib.fp8_layer_norm_workspace_bytes(0, 256) == 0
+
+
+def test_resample_rejects_bad_channels_without_touching_cuda():
+    lib = _lib.load()
+    fake = c_void_p(1 << 20)
+    status, code, msg = _status_and_message(lib.fp8_up_cat, fake, 0, fake, 0, fake, 1, 2, 8, 8, 12, 8, 2, c_void_p(0))
+    assert status == _lib.FP8_ERR_UNSUPPORTED and code == status and "multiples of 8" in msg
+    status, code, msg = _status_and_message(lib.fp8_resample_down2, fake, 0, fake, 2, 7, 8, 16, c_void_p(0))
+    assert status == _lib.FP8_ERR_UNSUPPORTED and "even" in msg

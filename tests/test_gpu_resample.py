@@ -1,0 +1,84 @@
+"""GPU parity: the UNet's nearest resampling + skip concatenation kernels
+(fp8_b200.resample) against F.interpolate / torch.cat under bf16 autocast, as the
+reference calls them (unet.py:366-383).
+
+Resampling copies values, so the forward outputs (values and dtypes) must be
+identical; the downsample gradient too.  The upsample gradient sums 2x2 blocks
+in fp32, where the summation order may differ from torch's: within one rounding
+step of the gradient's dtype."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(shape, dtype, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(dtype).to(device).contiguous(memory_format=torch.channels_last)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(128, 256, 32, 32), (4, 128, 16, 16), (3, 8, 2, 6)])
+def test_downsample_matches_interpolate_under_autocast(cuda, shape, dtype):
+    from fp8_b200.resample import downsample_nearest
+
+    x0 = _t(shape, dtype, sum(shape), cuda)
+    dy = _t((shape[0], shape[1], shape[2] // 2, shape[3] // 2), torch.float32, 7, cuda)
+    outs = []
+    for fn in (downsample_nearest, lambda x: F.interpolate(x, scale_factor=0.5, mode="nearest")):
+        x = x0.clone().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = fn(x)
+        y.backward(dy)
+        outs.append((y.detach(), x.grad))
+    (y1, g1), (y2, g2) = outs
+    assert y1.dtype == y2.dtype == torch.float32 and torch.equal(y1, y2)
+    assert g1.dtype == g2.dtype == dtype and torch.equal(g1, g2)
+
+
+@pytest.mark.parametrize("factor", [1, 2])
+@pytest.mark.parametrize("da,ds", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
+                                   (torch.float32, torch.float32), (torch.bfloat16, torch.float32)])
+def test_upsample_cat_matches_torch_under_autocast(cuda, factor, da, ds):
+    from fp8_b200.resample import upsample_cat
+
+    n, c1, c2, h = 8, 256, 128, 32
+    a0 = _t((n, c1, h // factor, h // factor), da, 11, cuda)
+    s0 = _t((n, c2, h, h), ds, 12, cuda)
+    outs = []
+    for fused in (True, False):
+        a = a0.clone().requires_grad_(True)
+        s = s0.clone().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            if fused:
+                y = upsample_cat(a, s, factor)
+            else:
+                up = F.interpolate(a, scale_factor=2.0, mode="nearest") if factor > 1 else a
+                y = torch.cat([up, s], dim=1)
+        dy = _t(y.shape, y.dtype, 13, cuda)
+        y.backward(dy)
+        outs.append((y.detach(), a.grad, s.grad))
+    (y1, a1, s1), (y2, a2, s2) = outs
+    assert y1.dtype == y2.dtype and torch.equal(y1, y2)
+    assert s1.dtype == s2.dtype == ds and torch.equal(s1, s2)
+    assert a1.dtype == a2.dtype == da
+    tol = 2.0 ** -7 if da == torch.bfloat16 else 1e-6
+    assert ((a1.float() - a2.float()).abs() <= tol * a2.float().abs() + 1e-30).all()
+
+
+def test_unet_forward_identical_with_fused_resampling(cuda):
+    """The whole UNet forward gives the same bytes with the fused resampling (it only copies values)."""
+    from fp8_b200.train import build_model
+
+    x = (torch.rand(4, 3, 32, 32) * 2 - 1).to(cuda).contiguous(memory_format=torch.channels_last)
+    t = torch.randint(0, 1000, (4,)).to(cuda)
+    ys = []
+    for fused in (True, False):
+        m = build_model(fp8=False, device=cuda, seed=0, fused_resample=fused).eval()
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            ys.append(m(x, t))
+    assert torch.equal(ys[0], ys[1])
