@@ -1576,7 +1576,7 @@ extern "C" int fp8_gn_param_grads(const float* totals, const void* film, int fil
   DeviceState* st;
   if (int s = device_state(&st)) return s;
   (void)st;
-  FP8_CUDA_TRY(launch_kernel(gn_param_grads_kernel, dim3((c + 255) / 256), dim3(256), 0,
+  FP8_CUDA_TRY(launch_kernel(gn_param_grads_kernel, dim3((c + 31) / 32), dim3(32 * kGnParamLanes), 0,
                              reinterpret_cast<cudaStream_t>(stream), 1, kStreamingKernel, totals,
                              static_cast<const uint16_t*>(film), film_ld, n, c, dgamma, dbeta,
                              static_cast<uint16_t*>(dfilm), dfilm_ld));

@@ -637,31 +637,47 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
 // Parameter gradients from the per-(n, c) totals of the backward:
 //   dgamma_c = sum_n (s_nc + 1) * T[n][2C + c],  dbeta_c = sum_n (s_nc + 1) * T[n][c]
 //   dfilm[n] = (T[n][C:2C], T[n][0:C]) as bf16     (the scale, then the shift gradient)
-// with s = 0 and no dfilm without FiLM.  One thread per channel, n in order.
-__global__ void __launch_bounds__(256) gn_param_grads_kernel(const float* __restrict__ totals,
-                                                             const uint16_t* __restrict__ film, int film_ld, int n,
-                                                             int c, float* __restrict__ dgamma,
-                                                             float* __restrict__ dbeta, uint16_t* __restrict__ dfilm,
-                                                             int dfilm_ld) {
+// with s = 0 and no dfilm without FiLM.  A CTA covers 32 channels with 8 lanes
+// of samples (n = lane, lane + 8, ...; coalesced rows), then sums the 8 lanes in
+// order (deterministic).
+constexpr int kGnParamLanes = 8;
+
+__global__ void __launch_bounds__(32 * kGnParamLanes) gn_param_grads_kernel(
+    const float* __restrict__ totals, const uint16_t* __restrict__ film, int film_ld, int n, int c,
+    float* __restrict__ dgamma, float* __restrict__ dbeta, uint16_t* __restrict__ dfilm, int dfilm_ld) {
+  __shared__ float red[2][kGnParamLanes][32];
   pdl_wait();
-  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
-  if (ch >= c) return;
+  const int cl = threadIdx.x & 31, lane = threadIdx.x >> 5;
+  const int ch = blockIdx.x * 32 + cl;
   float g = 0.0f, b = 0.0f;
-  for (int i = 0; i < n; ++i) {
-    const float* t = totals + static_cast<int64_t>(i) * 3 * c;
-    const float t_df = t[ch], t_dfz = t[c + ch], t_dfx = t[2 * c + ch];
-    float sc = 1.0f;
-    if (film != nullptr) {
-      sc += __uint_as_float(static_cast<uint32_t>(film[static_cast<int64_t>(i) * film_ld + ch]) << 16);
-      uint16_t* d = dfilm + static_cast<int64_t>(i) * dfilm_ld;
-      d[ch] = static_cast<uint16_t>(pack_bf16x2(t_dfz, 0.0f) & 0xFFFFu);
-      d[c + ch] = static_cast<uint16_t>(pack_bf16x2(t_df, 0.0f) & 0xFFFFu);
+  if (ch < c) {
+    for (int i = lane; i < n; i += kGnParamLanes) {
+      const float* t = totals + static_cast<int64_t>(i) * 3 * c;
+      const float t_df = t[ch], t_dfz = t[c + ch], t_dfx = t[2 * c + ch];
+      float sc = 1.0f;
+      if (film != nullptr) {
+        sc += __uint_as_float(static_cast<uint32_t>(film[static_cast<int64_t>(i) * film_ld + ch]) << 16);
+        uint16_t* d = dfilm + static_cast<int64_t>(i) * dfilm_ld;
+        d[ch] = static_cast<uint16_t>(pack_bf16x2(t_dfz, 0.0f) & 0xFFFFu);
+        d[c + ch] = static_cast<uint16_t>(pack_bf16x2(t_df, 0.0f) & 0xFFFFu);
+      }
+      g = fmaf(sc, t_dfx, g);
+      b = fmaf(sc, t_df, b);
     }
-    g = fmaf(sc, t_dfx, g);
-    b = fmaf(sc, t_df, b);
   }
-  dgamma[ch] = g;
-  dbeta[ch] = b;
+  red[0][lane][cl] = g;
+  red[1][lane][cl] = b;
+  __syncthreads();
+  if (lane == 0 && ch < c) {
+    float sg = 0.0f, sb = 0.0f;
+#pragma unroll
+    for (int l = 0; l < kGnParamLanes; ++l) {
+      sg += red[0][l][cl];
+      sb += red[1][l][cl];
+    }
+    dgamma[ch] = sg;
+    dbeta[ch] = sb;
+  }
 }
 
 }  // namespace fp8b

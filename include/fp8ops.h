@@ -267,7 +267,7 @@ int fp8_layer_norm_bwd(const void* x, int x_fp32, const void* dy_bf16, const flo
  *   dgamma[c] = sum_n (s + 1) * T[n][2c..], dbeta[c] = sum_n (s + 1) * T[n][0..]
  * with s the FiLM scale (0 without FiLM), and with FiLM the bf16 gradient of
  * its (scale, shift) rows, dfilm[n] = (T[n][c..2c), T[n][0..c)).  One launch;
- * sums over n in order (deterministic).  film / dfilm may be NULL together. */
+ * fixed summation order (deterministic).  film / dfilm may be NULL together. */
 int fp8_gn_param_grads(const float* totals, const void* film, int film_ld, int n, int c, float* dgamma,
                        float* dbeta, void* dfilm, int dfilm_ld, fp8_stream_t stream);
 
