@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-unet", action="store_true", help="skip the UNet training-step measurement")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the per-config sweep (linear configs 1 / 3, conv at batch 512, delayed quantize)")
     ap.add_argument("--pdl", type=int, default=0, choices=(0, 1, 2),
                     help="programmatic dependent launch: 0 off (default), 1 tensor-core kernels, 2 every kernel")
     ap.add_argument("--bucket-mb", type=float, default=None,
@@ -288,6 +290,10 @@ def run_b200(args) -> None:
         clocks["reasons"] = reasons
         clocks["ranks"] = world
 
+    sweep = None
+    if rank == 0 and not args.no_sweep:
+        sweep = time_sweep(args, dev)
+
     # ------------------------------------------------------------------ end to end (host buffers)
     e2e = None
     if not args.no_e2e:
@@ -351,6 +357,7 @@ def run_b200(args) -> None:
             "e2e": e2e,
             "cpu_baseline": cpu,
             "unet_train": unet,
+            "sweep": annotate_sweep(sweep, peaks) if sweep else None,
         }
         print(json.dumps(line), file=result_out, flush=True)
     if world > 1:
@@ -442,6 +449,105 @@ def time_kernels(args, dev, w, sets) -> dict:
         out[name] = {"ms": round(ms, 6), "calls": replays * per_graph, "operand_sets": n_sets}
         del g
     return out
+
+
+def _time_calls(fn, n_sets: int, replays: int, dev) -> float:
+    """ms per call of fn(i): graph-replayed, cycling over n_sets operand sets (each graph 2 * n_sets calls)."""
+    per_graph = 2 * n_sets
+    for i in range(n_sets):
+        fn(i)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g):
+            for k in range(per_graph):
+                fn(k % n_sets)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    ms = _time_graph_loop([g], replays) / per_graph
+    del g
+    return ms
+
+
+def time_sweep(args, dev) -> dict:
+    """BASELINE configs 1, 3 and 5 (conv at batch 512, widths 128 / 256) and the delayed quantize, op by op.
+
+    Operands rotate over enough sets that one pass exceeds L2; inputs already quantized (the
+    quantize is timed on its own).  Work per call: 2*M*N*K FLOP; algorithmic bytes: the e4m3
+    operands read once plus the bf16 output written once."""
+    from fp8_b200 import ops
+
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(0)
+    cl = torch.channels_last
+
+    def rnd(shape, std=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * std).to(torch.bfloat16)
+
+    # config 5: the config-2 conv at batch 512, widths 128 and 256
+    for c in (128, 256):
+        b, hw = 512, 32
+        n_sets = 2
+        xs = [ops.quantize_current(rnd((b, c, hw, hw)).contiguous(memory_format=cl)) for _ in range(n_sets)]
+        dys = [ops.quantize_current(rnd((b, c, hw, hw), 1e-2).contiguous(memory_format=cl))
+               for _ in range(n_sets)]
+        wq, sw = ops.quantize_current(rnd((c, c, 3, 3), 0.05).contiguous(memory_format=cl))
+        flops = 2.0 * b * hw * hw * c * 9 * c
+        name = f"conv3x3 B=512 {c}->{c} 32x32"
+        fns = {
+            "fwd": lambda i: ops.conv3x3_fwd(xs[i][0], wq, xs[i][1], sw),
+            "dgrad": lambda i: ops.conv3x3_dgrad(dys[i][0], wq, dys[i][1], sw),
+            "wgrad": lambda i: ops.conv3x3_wgrad(xs[i][0], dys[i][0], xs[i][1], dys[i][1]),
+        }
+        for op, fn in fns.items():
+            ms = _time_calls(fn, n_sets, 20, dev)
+            out[f"{name} {op}"] = {"ms": round(ms, 5), "flop": flops, "bytes": None}
+        del xs, dys
+        torch.cuda.empty_cache()
+
+    # configs 1 and 3: the FP8 linears (x [M, K] @ W^T, W in nn.Linear [N, K] layout), bias on config 1
+    for name, m, k, n, bias in (("linear config 1 (4096x512 @ 512x2048 + bias)", 4096, 512, 2048, True),
+                                ("attn qkv config 3 (32768x256 @ 256x768)", 32768, 256, 768, False),
+                                ("attn out config 3 (32768x256 @ 256x256)", 32768, 256, 256, False)):
+        per_set = m * k + m * n * 2
+        n_sets = max(2, -(-3 * 126 * 2**20 // per_set))
+        xs = [ops.quantize_current(rnd((m, k))) for _ in range(n_sets)]
+        wq, sw = ops.quantize_current(rnd((n, k), 0.02))
+        bvec = rnd((n,), 0.01) if bias else None
+        epi = ops.EPILOGUE_BIAS if bias else ops.EPILOGUE_NONE
+        ms = _time_calls(lambda i: ops.gemm(xs[i][0], wq, xs[i][1], sw, bvec, epi), n_sets, 50, dev)
+        out[name] = {"ms": round(ms, 5), "flop": 2.0 * m * n * k, "bytes": m * k + n * k + 2 * m * n + (2 * n if bias else 0)}
+        del xs
+
+    # the delayed quantize (one pass: 2 B read + 1 B written per element) at config 2's X
+    n_el = 128 * 128 * 32 * 32
+    n_sets = 4
+    xs = [rnd((128, 128, 32, 32)).contiguous(memory_format=cl) for _ in range(n_sets)]
+    prev = torch.tensor(0.01, device=dev)
+    ms = _time_calls(lambda i: ops.quantize_delayed(xs[i], prev), n_sets, 50, dev)
+    out["quantize delayed config 2 X (16.8 M elements)"] = {"ms": round(ms, 5), "flop": None, "bytes": 3 * n_el}
+    del xs
+    torch.cuda.empty_cache()
+    return out
+
+
+def annotate_sweep(sweep: dict, peaks: dict) -> dict:
+    """Adds TFLOP/s and GB/s with their fractions of the measured peaks (FP8 = 2 x bf16 burst)."""
+    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    res = {}
+    for name, r in sweep.items():
+        e = dict(r)
+        s = r["ms"] * 1e-3
+        if r["flop"]:
+            e["tflops"] = round(r["flop"] / s / 1e12, 1)
+            e["frac_fp8_peak"] = round(e["tflops"] / fp8_peak, 4)
+        if r["bytes"]:
+            e["gbs"] = round(r["bytes"] / s / 1e9, 1)
+            e["frac_hbm"] = round(e["gbs"] / peaks["hbm_gbs"], 4)
+        res[name] = e
+    return res
 
 
 def roofline(kernels: dict, peaks: dict, batch: int) -> dict | None:
