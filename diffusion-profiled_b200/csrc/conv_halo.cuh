@@ -281,6 +281,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BN; c += 64) {
         uint32_t r[64];
+        const uint4 bias_chunk = load_bias_chunk(p.epilogue, p.bias, nt * BN + c, p.N, lane);
         const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols + c;
         tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
@@ -295,7 +296,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue, p.bias + n0 + 8 * j);
+          const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue,
+                                     p.epilogue != kEpiNone ? bias_vec(bias_chunk, j) : make_uint4(0u, 0u, 0u, 0u));
           st_shared_v4(sbuf + swizzle128_offset(lane, j), o.x, o.y, o.z, o.w);
         }
         fence_proxy_async_smem();
@@ -519,6 +521,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < 128; c += 64) {
         uint32_t r[64];
+        const uint4 bias_chunk = load_bias_chunk(p.epilogue, p.bias, nt_fixed * 128 + c, p.N, lane);
         const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + acc * 128 + c;
         tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
@@ -533,7 +536,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue, p.bias + n0 + 8 * j);
+          const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue,
+                                     p.epilogue != kEpiNone ? bias_vec(bias_chunk, j) : make_uint4(0u, 0u, 0u, 0u));
           st_shared_v4(sbuf + swizzle128_offset(lane, j), o.x, o.y, o.z, o.w);
         }
         fence_proxy_async_smem();

@@ -68,13 +68,27 @@ struct KGemmConfig {
   static_assert(kSmemBytes <= 232448, "smem");
 };
 
+// The bias of the 64 output columns n0 .. n0 + 63 spread over lanes 0..7 (one
+// 8-column vector each).  Loaded at the top of a chunk, before the accumulator
+// is read, so the load latency overlaps the TMEM load instead of sitting in
+// the store loop; bias_vec() hands vector j to every lane.
+__device__ __forceinline__ uint4 load_bias_chunk(int epi, const __nv_bfloat16* bias, int n0, int n_total, int lane) {
+  uint4 b = make_uint4(0u, 0u, 0u, 0u);
+  if (epi != kEpiNone && lane < 8 && n0 + lane * 8 < n_total)
+    b = __ldg(reinterpret_cast<const uint4*>(bias + n0 + lane * 8));
+  return b;
+}
+__device__ __forceinline__ uint4 bias_vec(const uint4& chunk, int j) {
+  return make_uint4(__shfl_sync(0xffffffffu, chunk.x, j), __shfl_sync(0xffffffffu, chunk.y, j),
+                    __shfl_sync(0xffffffffu, chunk.z, j), __shfl_sync(0xffffffffu, chunk.w, j));
+}
+
 // 8 consecutive output columns of one row: scale, optional bias / SiLU, bf16x8.
-__device__ __forceinline__ uint4 epilogue8(const uint32_t* acc, float scale, int epi, const __nv_bfloat16* bias8) {
+__device__ __forceinline__ uint4 epilogue8(const uint32_t* acc, float scale, int epi, const uint4& b) {
   float v[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(acc[i]) * scale;
   if (epi != kEpiNone) {
-    const uint4 b = __ldg(reinterpret_cast<const uint4*>(bias8));
     const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -259,6 +273,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < BN; c += 64) {
           uint32_t r[64];
+          const uint4 bias_chunk = load_bias_chunk(p.epilogue, p.bias, nt * BN + c, p.N, lane);
           const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols + sub * BN + c;
           tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
@@ -275,7 +290,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue, p.bias + n0 + 8 * j);
+            const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue,
+                                     p.epilogue != kEpiNone ? bias_vec(bias_chunk, j) : make_uint4(0u, 0u, 0u, 0u));
             st_shared_v4(sbuf + swizzle128_offset(lane, j), o.x, o.y, o.z, o.w);
           }
           fence_proxy_async_smem();
