@@ -709,7 +709,7 @@ int quant_grid(int64_t n, bool vec, int blocks_per_sm, int sm_count) {
 
 template <int KIND>
 int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const float* partials_in, int n_partials,
-                  const float* prev_scale, float* scale_out, float* partials_out, int* err, cudaStream_t cs) {
+                  DelayedSource prev_scale, float* scale_out, float* partials_out, int* err, cudaStream_t cs) {
   FP8_CUDA_TRY(cudaFuncSetAttribute(quant_stream_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kStreamSmemBytes)));
   FP8_CUDA_TRY(launch_kernel(quant_stream_kernel<KIND>, dim3(grid), dim3(kStreamThreads), kStreamSmemBytes, cs, 1,
@@ -723,18 +723,18 @@ int launch_quantize_current(const uint16_t* x, uint8_t* q, float* scale_out, flo
                             bool vec, const DeviceState* st, cudaStream_t cs) {
   const int cast_blocks = quant_grid(n, vec, g_quant_cast_bps, st->sm_count);
   if (vec) {
-    if (int s = launch_stream<kStreamAmax>(parts, x, nullptr, n, nullptr, 0, nullptr, nullptr, partials,
+    if (int s = launch_stream<kStreamAmax>(parts, x, nullptr, n, nullptr, 0, DelayedSource{}, nullptr, partials,
                                            st->err_ptr, cs))
       return s;
-    if (int s = launch_stream<kStreamCastCurrent>(cast_blocks, x, q, n, partials, parts, nullptr, scale_out, nullptr,
-                                                  st->err_ptr, cs))
+    if (int s = launch_stream<kStreamCastCurrent>(cast_blocks, x, q, n, partials, parts, DelayedSource{}, scale_out,
+                                                  nullptr, st->err_ptr, cs))
       return s;
   } else {
     FP8_CUDA_TRY(launch_kernel(amax_partials_kernel, dim3(parts), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel, x, n,
                                partials));
     FP8_CUDA_TRY(launch_kernel(quantize_cast_kernel<kCurrent>, dim3(cast_blocks), dim3(kQuantThreads), 0, cs, 1,
-                               kStreamingKernel, x, q, n, static_cast<const float*>(partials), parts,
-                               static_cast<const float*>(nullptr), scale_out, static_cast<float*>(nullptr)));
+                               kStreamingKernel, x, q, n, static_cast<const float*>(partials), parts, DelayedSource{},
+                               scale_out, static_cast<float*>(nullptr)));
   }
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
@@ -880,12 +880,14 @@ int fp8_quantize_current_noalloc(const void* x_bf16, void* q_e4m3, float* scale_
   return ok();
 }
 
-int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_scale, float* scale_curr_out,
-                         void* workspace, size_t workspace_bytes, int64_t n, fp8_stream_t stream) {
+namespace {
+// One delayed cast: the scale comes from `src` (a previous scale or the max of a
+// scale history), the tensor's own scale goes to *scale_curr_out and / or into
+// the history (`wu`).
+int quantize_delayed_impl(const void* x_bf16, void* q_e4m3, const DelayedSource& src, float* scale_curr_out,
+                          const WindowUpdate& wu, void* workspace, size_t workspace_bytes, int64_t n,
+                          fp8_stream_t stream) {
   FP8_REQUIRE(n >= 0, FP8_ERR_INVALID_ARGUMENT, "n must be >= 0");
-  FP8_REQUIRE(prev_scale != nullptr && aligned(prev_scale, 4), FP8_ERR_INVALID_ARGUMENT, "bad prev_scale");
-  FP8_REQUIRE(scale_curr_out != nullptr && aligned(scale_curr_out, 4), FP8_ERR_INVALID_ARGUMENT,
-              "bad scale_curr_out");
   FP8_REQUIRE(n == 0 || (x_bf16 != nullptr && q_e4m3 != nullptr), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(aligned(x_bf16, 2), FP8_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
   DeviceState* st;
@@ -900,19 +902,46 @@ int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_sca
   const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
   uint8_t* q = static_cast<uint8_t*>(q_e4m3);
   if (vec) {
-    if (int s = launch_stream<kStreamCastDelayed>(parts, x, q, n, nullptr, 0, prev_scale, nullptr, partials,
-                                                  st->err_ptr, cs))
+    if (int s = launch_stream<kStreamCastDelayed>(parts, x, q, n, nullptr, 0, src, nullptr, partials, st->err_ptr,
+                                                  cs))
       return s;
   } else {
     FP8_CUDA_TRY(launch_kernel(quantize_cast_kernel<kDelayed>, dim3(parts), dim3(kQuantThreads), 0, cs, 1,
-                               kStreamingKernel, x, q, n, static_cast<const float*>(nullptr), 0, prev_scale,
+                               kStreamingKernel, x, q, n, static_cast<const float*>(nullptr), 0, src,
                                static_cast<float*>(nullptr), partials));
   }
   FP8_CUDA_TRY(launch_kernel(finalize_scale_kernel, dim3(1), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
-                             static_cast<const float*>(partials), parts, scale_curr_out));
+                             static_cast<const float*>(partials), parts, scale_curr_out, wu));
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
+}
+
+int check_window(const float* window, int window_len, const int64_t* window_pos, const float* used) {
+  FP8_REQUIRE(window != nullptr && aligned(window, 4) && window_len > 0, FP8_ERR_INVALID_ARGUMENT,
+              "bad scale history");
+  FP8_REQUIRE(window_pos != nullptr && aligned(window_pos, 8), FP8_ERR_INVALID_ARGUMENT, "bad history position");
+  FP8_REQUIRE(used != nullptr && aligned(used, 4), FP8_ERR_INVALID_ARGUMENT, "bad scale_used_out");
+  return FP8_OK;
+}
+}  // namespace
+
+int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_scale, float* scale_curr_out,
+                         void* workspace, size_t workspace_bytes, int64_t n, fp8_stream_t stream) {
+  FP8_REQUIRE(prev_scale != nullptr && aligned(prev_scale, 4), FP8_ERR_INVALID_ARGUMENT, "bad prev_scale");
+  FP8_REQUIRE(scale_curr_out != nullptr && aligned(scale_curr_out, 4), FP8_ERR_INVALID_ARGUMENT,
+              "bad scale_curr_out");
+  return quantize_delayed_impl(x_bf16, q_e4m3, DelayedSource{prev_scale, nullptr, 0, nullptr}, scale_curr_out,
+                               WindowUpdate{}, workspace, workspace_bytes, n, stream);
+}
+
+int fp8_quantize_delayed_window(const void* x_bf16, void* q_e4m3, float* window, int window_len,
+                                int64_t* window_pos, int advance, float* scale_used_out, void* workspace,
+                                size_t workspace_bytes, int64_t n, fp8_stream_t stream) {
+  if (int s = check_window(window, window_len, window_pos, scale_used_out)) return s;
+  return quantize_delayed_impl(x_bf16, q_e4m3, DelayedSource{nullptr, window, window_len, scale_used_out}, nullptr,
+                               WindowUpdate{window, window_pos, window_len, advance ? 1 : 0}, workspace,
+                               workspace_bytes, n, stream);
 }
 
 int fp8_transpose_2d(const void* src, void* dst, int64_t rows, int64_t cols, fp8_stream_t stream) {
@@ -1231,7 +1260,7 @@ int fp8_gn_act_fwd(const void* x, int x_fp32, const float* gamma, const float* b
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
-  const GnOut o{static_cast<uint16_t*>(out), nullptr, nullptr, nullptr};
+  const GnOut o{static_cast<uint16_t*>(out), nullptr, DelayedSource{}, nullptr};
   if (x_fp32) {
     if (int s = launch_gn_fwd<float, false>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, st->sm_count,
                                                cs)) return s;
@@ -1255,13 +1284,13 @@ size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c) {
   return gn_workspace(n, hw, c, sms) + ((static_cast<size_t>(n) * slices * sizeof(float) + 15) & ~size_t(15));
 }
 
-int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
-                         int film_ld, const int64_t* seed, float p, float eps, const float* prev_scale,
-                         float* stats, void* q_e4m3, float* scale_curr_out, int n, int hw, int c, int groups,
-                         void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+namespace {
+int gn_act_quant_impl(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                      int film_ld, const int64_t* seed, float p, float eps, const DelayedSource& src, float* stats,
+                      void* q_e4m3, float* scale_curr_out, const WindowUpdate& wu, int n, int hw, int c, int groups,
+                      void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
   if (int s = check_gn_args(x, q_e4m3, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
-  FP8_REQUIRE(stats != nullptr && prev_scale != nullptr && scale_curr_out != nullptr, FP8_ERR_INVALID_ARGUMENT,
-              "NULL stats or scale");
+  FP8_REQUIRE(stats != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats");
   DeviceState* st;
   if (int s = device_state(&st)) return s;
   const GnShape sh{n, hw, c, groups, 1, 1};
@@ -1274,22 +1303,46 @@ int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const fl
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   float* amax_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gn_bytes);
-  const GnOut o{nullptr, static_cast<uint8_t*>(q_e4m3), prev_scale, amax_part};
+  const GnOut o{nullptr, static_cast<uint8_t*>(q_e4m3), src, amax_part};
   int apply_ctas = 0;
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
   if (x_fp32) {
     if (int s = launch_gn_fwd<float, true>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, st->sm_count,
-                                              cs, &apply_ctas)) return s;
+                                           cs, &apply_ctas))
+      return s;
   } else {
     if (int s = launch_gn_fwd<uint16_t, true>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2,
-                                                 st->sm_count, cs, &apply_ctas))
+                                              st->sm_count, cs, &apply_ctas))
       return s;
   }
   FP8_CUDA_TRY(launch_kernel(finalize_scale_kernel, dim3(1), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
-                             static_cast<const float*>(amax_part), apply_ctas, scale_curr_out));
+                             static_cast<const float*>(amax_part), apply_ctas, scale_curr_out, wu));
   count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
+}
+}  // namespace
+
+int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                         int film_ld, const int64_t* seed, float p, float eps, const float* prev_scale,
+                         float* stats, void* q_e4m3, float* scale_curr_out, int n, int hw, int c, int groups,
+                         void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+  FP8_REQUIRE(prev_scale != nullptr && scale_curr_out != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL scale");
+  return gn_act_quant_impl(x, x_fp32, gamma, beta, film, film_ld, seed, p, eps,
+                           DelayedSource{prev_scale, nullptr, 0, nullptr}, stats, q_e4m3, scale_curr_out,
+                           WindowUpdate{}, n, hw, c, groups, workspace, workspace_bytes, stream);
+}
+
+int fp8_gn_act_quant_fwd_window(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                                int film_ld, const int64_t* seed, float p, float eps, float* window, int window_len,
+                                int64_t* window_pos, int advance, float* scale_used_out, float* stats, void* q_e4m3,
+                                int n, int hw, int c, int groups, void* workspace, size_t workspace_bytes,
+                                fp8_stream_t stream) {
+  if (int s = check_window(window, window_len, window_pos, scale_used_out)) return s;
+  return gn_act_quant_impl(x, x_fp32, gamma, beta, film, film_ld, seed, p, eps,
+                           DelayedSource{nullptr, window, window_len, scale_used_out}, stats, q_e4m3, nullptr,
+                           WindowUpdate{window, window_pos, window_len, advance ? 1 : 0}, n, hw, c, groups, workspace,
+                           workspace_bytes, stream);
 }
 
 int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,

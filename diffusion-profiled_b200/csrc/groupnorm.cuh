@@ -335,7 +335,7 @@ __device__ __forceinline__ void gn_coeffs(const GnShape& s, const GnActParams& q
 struct GnOut {
   uint16_t* bf16;           // NHWC bf16 (QUANT = false)
   uint8_t* q;               // NHWC e4m3 (QUANT = true)
-  const float* prev_scale;  // dequant scale of the cast (QUANT = true)
+  DelayedSource prev_scale;  // the scale of the cast (QUANT = true)
   float* amax_part;         // [grid] per-CTA max |activation| (QUANT = true)
 };
 
@@ -403,6 +403,9 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_FWD) gn_act_fwd_kernel
       stats[static_cast<int64_t>(t.n) * 2 * s.groups + g] = mean_g[g];
       stats[static_cast<int64_t>(t.n) * 2 * s.groups + s.groups + g] = rstd_g[g];
     }
+  // the delayed scale first: with a scale history every thread takes part in its max
+  float sc = 1.0f;
+  if constexpr (QUANT) sc = delayed_scale<kGnThreads>(o.prev_scale);
   gn_coeffs(s, q, t.n, mean_g, rstd_g, A, B, nullptr, nullptr);
   uint32_t m2 = 0u;
   if (t.r < t.rows) {
@@ -419,7 +422,6 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_FWD) gn_act_fwd_kernel
     const TX* xs = x + base * 8;
     if constexpr (QUANT) {
       // the scale is uniform over the grid, so the choice never diverges
-      const float sc = *o.prev_scale;
       m2 = markstein_applies(sc)
                ? gn_apply_rows<TX, true, DROP>(xs, t, base, a, b, seed, thresh, keep_scale, o, make_markstein(sc))
                : gn_apply_rows<TX, true, DROP>(xs, t, base, a, b, seed, thresh, keep_scale, o, DivF64(sc));

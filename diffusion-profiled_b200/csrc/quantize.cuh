@@ -159,6 +159,28 @@ __device__ __forceinline__ float scale_from_amax(float amax) {
   return amax > 0.0f ? __fdiv_rn(amax, kE4M3Max) : 1.0f;
 }
 
+// The scale a delayed cast divides by: *prev, or -- when window != nullptr --
+// the max of window[0 .. len), the reference's torch.max over a module's scale
+// history (unet.py:69-91, fp8_kernels.py:841-853), which CTA 0 also writes to
+// *used (the dequantisation scale of the cast bytes, read by the contraction
+// that consumes them).  Every thread of the CTA must call delayed_scale().
+struct DelayedSource {
+  const float* prev;
+  const float* window;
+  int len;
+  float* used;
+};
+
+// The history update after a delayed cast: window[*pos] = this tensor's scale,
+// then (advance) *pos = (*pos + 1) % len -- the scatter and the position step of
+// the reference module (unet.py:80-91), done by the one-CTA finalize kernel.
+struct WindowUpdate {
+  float* window;
+  int64_t* pos;
+  int len;
+  int advance;
+};
+
 // Fold `count` partial maxima into the tensor scale (every CTA does this; the
 // partials are a few KB and L2 resident).
 template <int NT = kQuantThreads>
@@ -166,6 +188,16 @@ __device__ __forceinline__ float fold_partials_to_scale(const float* __restrict_
   float m = 0.0f;
   for (int i = threadIdx.x; i < count; i += NT) m = fmaxf(m, partials[i]);
   return scale_from_amax(block_max<NT>(m));
+}
+
+template <int NT = kQuantThreads>
+__device__ __forceinline__ float delayed_scale(const DelayedSource& d) {
+  if (d.window == nullptr) return *d.prev;  // uniform over the grid
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < d.len; i += NT) m = fmaxf(m, d.window[i]);
+  m = block_max<NT>(m);
+  if (d.used != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *d.used = m;
+  return m;
 }
 
 // |x| maxima kept packed: two running bf16 maxima per 32-bit word (clearing
@@ -227,15 +259,14 @@ __device__ __forceinline__ float cast_loop(const uint16_t* __restrict__ x, uint8
 template <int MODE>
 __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
-    int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
-    float* __restrict__ partials_out) {
+    int n_partials, DelayedSource prev_scale, float* __restrict__ scale_out, float* __restrict__ partials_out) {
   pdl_wait();
   float s;
   if (MODE == kCurrent) {
     s = fold_partials_to_scale(partials_in, n_partials);
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
   } else {
-    s = *prev_scale;
+    s = delayed_scale(prev_scale);
   }
   // s is uniform over the grid, so the branch never diverges.
   const float m = markstein_applies(s) ? cast_loop<MODE>(x, q, n, make_markstein(s))
@@ -247,10 +278,18 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
 }
 
 __global__ void __launch_bounds__(kQuantThreads) finalize_scale_kernel(const float* __restrict__ partials,
-                                                                       int n_partials, float* __restrict__ scale_out) {
+                                                                       int n_partials, float* __restrict__ scale_out,
+                                                                       WindowUpdate wu) {
   pdl_wait();
   const float s = fold_partials_to_scale(partials, n_partials);
-  if (threadIdx.x == 0) *scale_out = s;
+  if (threadIdx.x == 0) {
+    if (scale_out != nullptr) *scale_out = s;
+    if (wu.window != nullptr) {
+      const int64_t p = *wu.pos;
+      wu.window[p] = s;
+      if (wu.advance) *wu.pos = (p + 1) % wu.len;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- streaming passes
@@ -393,8 +432,8 @@ __device__ __forceinline__ float stream_body(const uint16_t* __restrict__ x, uin
 template <int KIND>
 __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
-    int n_partials, const float* __restrict__ prev_scale, float* __restrict__ scale_out,
-    float* __restrict__ partials_out, int* err) {
+    int n_partials, DelayedSource prev_scale, float* __restrict__ scale_out, float* __restrict__ partials_out,
+    int* err) {
   extern __shared__ __align__(128) uint8_t stream_smem[];
   pdl_wait();
   uint8_t* bufs = stream_smem;
@@ -414,7 +453,7 @@ __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
     s = fold_partials_to_scale<kStreamThreads>(partials_in, n_partials);  // contains __syncthreads
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
   } else {
-    if (KIND == kStreamCastDelayed) s = *prev_scale;
+    if (KIND == kStreamCastDelayed) s = delayed_scale<kStreamThreads>(prev_scale);
     __syncthreads();
   }
   float m;

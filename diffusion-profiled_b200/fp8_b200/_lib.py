@@ -97,6 +97,14 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_up_cat_bwd": (
         c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                 c_void_p]),
+    "fp8_quantize_delayed_window": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_int64,
+                c_void_p]),
+    "fp8_gn_act_quant_fwd_window": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_float, c_void_p, c_int, c_void_p,
+         c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    ),
     "fp8_gn_act_quant_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_quant_fwd": (
         c_int,

@@ -1,0 +1,83 @@
+"""Delayed-scaling FP8 convs with the scale histories kept and updated on the device.
+
+The reference keeps, per FP8 conv, three scale histories (``amax_window_acts``,
+``amax_window_weights``, ``amax_window_dy``, 1024 scales each) and a position
+(unet.py:50-56, 69-91; fp8_kernels.py:841-853, 883-889).  Every call it takes
+``torch.max`` of each history, casts with those scales, scatters the new x / w
+scales at the position, advances it, and in backward scatters the dY scale at
+the advanced position -- eight small launches per conv besides the casts.  Here
+the cast kernels take the max of the history themselves and the one-CTA
+finalize that computes a tensor's scale writes it into the history and steps
+the position (``fp8_b200::quantize_delayed_window`` / ``gn_act_quant_fwd_window``),
+so the histories, the scales used and the bytes are the same and the
+bookkeeping costs no launch of its own.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch.amp.autocast_mode import custom_bwd, custom_fwd
+
+from . import ops
+
+
+def _weight_bf16(weight: torch.Tensor) -> torch.Tensor:
+    w = weight.to(torch.bfloat16)
+    return w if w.is_contiguous(memory_format=torch.channels_last) else w.contiguous(memory_format=torch.channels_last)
+
+
+def _conv_backward(ctx, dy, xq, wq, sx, sw):
+    dy = dy.to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    # the dY scale lands at the position the forward already advanced (fp8_kernels.py:883-889)
+    dyq, sdy = ops.quantize_delayed_window(dy, ctx.win_dy, ctx.pos, False)
+    return ops.conv3x3_dgrad(dyq, wq, sdy, sw), ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+
+
+class ConvFP8Delayed(torch.autograd.Function):
+    """``Conv2dFP8Specialized`` (delayed branch) plus the module's history update, on device histories."""
+
+    @staticmethod
+    @custom_fwd(device_type="cuda")
+    def forward(ctx, x, weight, win_x, win_w, win_dy, pos):
+        x = x.to(torch.bfloat16)
+        xq, sx = ops.quantize_delayed_window(x, win_x, pos, False)
+        wq, sw = ops.quantize_delayed_window(_weight_bf16(weight), win_w, pos, True)
+        ctx.save_for_backward(xq, wq, sx, sw)
+        ctx.win_dy, ctx.pos = win_dy, pos
+        return ops.conv3x3_fwd(xq, wq, sx, sw)
+
+    @staticmethod
+    @custom_bwd(device_type="cuda")
+    def backward(ctx, dy):
+        xq, wq, sx, sw = ctx.saved_tensors
+        dx, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
+        return dx, dw, None, None, None, None
+
+
+class GroupNormActConvFP8Delayed(torch.autograd.Function):
+    """``GroupNormActConvFP8`` on device histories: the group-norm pass casts with max(win_x)."""
+
+    @staticmethod
+    @custom_fwd(device_type="cuda")
+    def forward(ctx, x, gamma, beta, film, seed, weight, win_x, win_w, win_dy, pos, p: float, eps: float,
+                groups: int):
+        film2 = None if film is None else film.reshape(film.shape[0], -1)
+        xq, sx, stats = ops.gn_act_quant_fwd_window(x, gamma, beta, film2, seed, win_x, pos, False, p, eps, groups)
+        wq, sw = ops.quantize_delayed_window(_weight_bf16(weight), win_w, pos, True)
+        ctx.save_for_backward(x, gamma, beta, film2, seed, stats, xq, wq, sx, sw)
+        ctx.win_dy, ctx.pos = win_dy, pos
+        ctx.cfg = (p, eps, groups, None if film is None else film.shape)
+        return ops.conv3x3_fwd(xq, wq, sx, sw)
+
+    @staticmethod
+    @custom_bwd(device_type="cuda")
+    def backward(ctx, dy):
+        x, gamma, beta, film2, seed, stats, xq, wq, sx, sw = ctx.saved_tensors
+        p, eps, groups, film_shape = ctx.cfg
+        d_act, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
+        dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
+        dfilm = None if film_shape is None else dfilm.reshape(film_shape)
+        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None
+
+
+__all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed"]

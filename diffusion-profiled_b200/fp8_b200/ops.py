@@ -144,6 +144,46 @@ def _(x, prev_scale):
     )
 
 
+def _check_window(window: torch.Tensor, pos: torch.Tensor, dev: torch.device) -> None:
+    if window.device != dev or window.dtype != torch.float32 or window.dim() != 1 or not window.is_contiguous():
+        raise RuntimeError("the scale history must be a contiguous 1-D float32 tensor on the input's device")
+    if pos.device != dev or pos.dtype != torch.int64 or pos.numel() != 1:
+        raise RuntimeError("the history position must be a one-element int64 tensor on the input's device")
+
+
+@torch.library.custom_op("fp8_b200::quantize_delayed_window", mutates_args=("window", "pos"))
+def quantize_delayed_window(x: torch.Tensor, window: torch.Tensor, pos: torch.Tensor,
+                            advance: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Delayed cast with the scale history on the device -> (e4m3, scale used).
+
+    Casts with ``max(window)`` (the reference module's ``torch.max(amax_window)``),
+    then stores this tensor's own scale at ``window[pos]`` and, if ``advance``,
+    steps ``pos`` (unet.py:69-91).  Bit for bit ``quantize_delayed(x, window.max())``
+    followed by the module's scatter / position update."""
+    dev = _require_cuda(x, window, pos)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"quantize expects bfloat16, got {x.dtype}")
+    if not (x.is_contiguous() or x.is_contiguous(memory_format=torch.channels_last)):
+        raise RuntimeError("quantize expects a dense (contiguous or channels_last) tensor")
+    _check_window(window, pos, dev)
+    q = torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format)
+    used = torch.empty((), device=dev, dtype=torch.float32)
+    n = x.numel()
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_quantize_workspace_bytes(n) // 4, 1), device=dev, dtype=torch.float32)
+        _lib.check(lib.fp8_quantize_delayed_window(
+            _ptr(x), _ptr(q), _ptr(window), window.numel(), _ptr(pos), int(advance), _ptr(used), _ptr(ws),
+            ws.numel() * 4, n, _stream(dev)), "fp8_quantize_delayed_window")
+    return q, used
+
+
+@quantize_delayed_window.register_fake
+def _(x, window, pos, advance):
+    return (torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format),
+            x.new_empty((), dtype=torch.float32))
+
+
 # ----------------------------------------------------------------------------- transposes
 @torch.library.custom_op("fp8_b200::transpose_2d", mutates_args=())
 def transpose_2d(src: torch.Tensor) -> torch.Tensor:
@@ -605,6 +645,34 @@ def gn_act_quant_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, f
             float(p), float(eps), _ptr(prev_scale), _ptr(stats), _ptr(q), _ptr(scale), n, hw, c, groups, _ptr(ws),
             ws.numel() * 4, _stream(dev)), "fp8_gn_act_quant_fwd")
     return q, scale, stats
+
+
+@torch.library.custom_op("fp8_b200::gn_act_quant_fwd_window", mutates_args=("window", "pos"))
+def gn_act_quant_fwd_window(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
+                            seed: torch.Tensor | None, window: torch.Tensor, pos: torch.Tensor, advance: bool,
+                            p: float, eps: float, groups: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """gn_act_quant_fwd with the scale history on the device -> (e4m3, scale used, stats)."""
+    dev = _require_cuda(x, gamma, beta)
+    n, c, hw = _gn_check(x, gamma, beta, film, groups)
+    _check_window(window, pos, dev)
+    q = torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.channels_last)
+    used = torch.empty((), device=dev, dtype=torch.float32)
+    stats = torch.empty((n, 2, groups), device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_gn_act_quant_workspace_bytes(n, hw, c) // 4, 4), device=dev,
+                         dtype=torch.float32)
+        _lib.check(lib.fp8_gn_act_quant_fwd_window(
+            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed),
+            float(p), float(eps), _ptr(window), window.numel(), _ptr(pos), int(advance), _ptr(used), _ptr(stats),
+            _ptr(q), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)), "fp8_gn_act_quant_fwd_window")
+    return q, used, stats
+
+
+@gn_act_quant_fwd_window.register_fake
+def _(x, gamma, beta, film, seed, window, pos, advance, p, eps, groups):
+    return (torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.channels_last),
+            x.new_empty((), dtype=torch.float32), x.new_empty((x.shape[0], 2, groups), dtype=torch.float32))
 
 
 @gn_act_quant_fwd.register_fake

@@ -27,6 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
 from .resample import downsample_nearest, upsample_cat
 from .norm import GroupNormActConvFP8, fused_layer_norm_supported, fused_norm_supported, group_norm_act, layer_norm_bf16
@@ -51,6 +52,10 @@ class UNetConfig:
     fused_norm: bool = True
     # nearest resampling + skip concatenation as single passes (fp8_b200.resample)
     fused_resample: bool = True
+    # delayed scaling: the kernels read and update the scale histories on the
+    # device (fp8_b200.delayed) instead of torch.max / scatter launches per conv;
+    # the histories, scales and results are the same
+    device_scale_history: bool = True
 
     def as_dict(self):
         return asdict(self)
@@ -60,8 +65,9 @@ class Conv2dFP8(nn.Module):
     """3x3 / pad 1 conv; FP8 for whitelisted shapes, bf16 ``nn.Conv2d`` otherwise."""
 
     def __init__(self, in_channels: int, out_channels: int, fp8_convs_enabled: bool, scaling_type: str = "current",
-                 amax_history: int | None = None):
+                 amax_history: int | None = None, device_scale_history: bool = True):
         super().__init__()
+        self.device_scale_history = device_scale_history
         if scaling_type not in ("current", "delayed"):
             raise ValueError(f"unknown FP8 scaling type {scaling_type!r}")
         self.conv = nn.Conv2d(in_channels, out_channels, (3, 3), stride=1, padding=1, bias=False)
@@ -87,6 +93,9 @@ class Conv2dFP8(nn.Module):
         x = x.contiguous(memory_format=torch.channels_last)
         if self.scaling_type == "current":
             return triton_conv2d_fp8(x, self.conv.weight)
+        if self.device_scale_history:
+            return ConvFP8Delayed.apply(x, self.conv.weight, self.amax_window_acts, self.amax_window_weights,
+                                        self.amax_window_dy, self.window_pos)
         with torch.no_grad():
             x_hist = torch.max(self.amax_window_acts)
             w_hist = torch.max(self.amax_window_weights)
@@ -110,6 +119,11 @@ class Conv2dFP8(nn.Module):
         if p > 0.0 and seed is None:
             raise ValueError("dropout needs a seed tensor")
         x = x.contiguous(memory_format=torch.channels_last)
+        if self.device_scale_history:
+            return GroupNormActConvFP8Delayed.apply(
+                x, norm.weight, norm.bias, film, seed if p > 0.0 else None, self.conv.weight, self.amax_window_acts,
+                self.amax_window_weights, self.amax_window_dy, self.window_pos, float(p), float(norm.eps),
+                int(norm.num_groups))
         with torch.no_grad():
             x_hist = torch.max(self.amax_window_acts)
             w_hist = torch.max(self.amax_window_weights)
@@ -139,7 +153,7 @@ class ResidualBlock(nn.Module):
     def __init__(self, config: UNetConfig, in_chann: int, out_chann: int, p_drop: float = 0.0):
         super().__init__()
         conv = dict(fp8_convs_enabled=config.fp8_convs_enabled, scaling_type=config.fp8_scaling_type,
-                    amax_history=config.fp8_amax_history)
+                    amax_history=config.fp8_amax_history, device_scale_history=config.device_scale_history)
         self.conv_1 = Conv2dFP8(in_chann, out_chann, **conv)
         self.conv_2 = Conv2dFP8(out_chann, out_chann, **conv)
         self.norm1 = nn.GroupNorm(32, in_chann)

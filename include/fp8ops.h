@@ -291,6 +291,25 @@ int fp8_up_cat(const void* a, int a_dtype, const void* s, int s_dtype, void* y, 
 int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds, int s_dtype, int n, int h, int w,
                    int c1, int c2, int factor, fp8_stream_t stream);
 
+/* Delayed scaling with the scale history kept on the device (reference
+ * Conv2dFP8 bookkeeping, unet.py:69-91, fp8_kernels.py:841-853, 883-889):
+ * the cast divides by max(window[0 .. window_len)) -- the module's
+ * torch.max(amax_window) -- and writes that value to *scale_used_out (the
+ * dequantisation scale of q, for the contraction); afterwards this tensor's
+ * own scale (amax/448, 1.0 for amax 0) is stored at window[*window_pos] and,
+ * when `advance`, *window_pos = (*window_pos + 1) % window_len.  One cast pass
+ * plus a one-CTA finalize; no torch.max / scatter / position launches. */
+int fp8_quantize_delayed_window(const void* x_bf16, void* q_e4m3, float* window, int window_len,
+                                int64_t* window_pos, int advance, float* scale_used_out, void* workspace,
+                                size_t workspace_bytes, int64_t n, fp8_stream_t stream);
+
+/* fp8_gn_act_quant_fwd with the scale history of fp8_quantize_delayed_window. */
+int fp8_gn_act_quant_fwd_window(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
+                                int film_ld, const int64_t* seed, float p, float eps, float* window, int window_len,
+                                int64_t* window_pos, int advance, float* scale_used_out, float* stats, void* q_e4m3,
+                                int n, int hw, int c, int groups, void* workspace, size_t workspace_bytes,
+                                fp8_stream_t stream);
+
 /* Workspace bytes of fp8_gn_act_quant_fwd. */
 size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c);
 

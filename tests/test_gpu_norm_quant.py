@@ -67,10 +67,11 @@ def _block_pair(cuda, cin, cout, fused):
             m.amax_window_weights.fill_(0.0005)
             m.amax_window_dy.fill_(1e-5)
         blk.dropout_seed.fill_(77)
-    if not fused:  # the unfused path: group norm op, then the FP8 conv module
+    if not fused:  # the unfused path: group norm op, then the FP8 conv module with the torch bookkeeping
         from fp8_b200.norm import group_norm_act
 
         for m in (blk.conv_1, blk.conv_2):
+            m.device_scale_history = False
             m.forward_normed = (lambda mod: lambda x, norm, film=None, p=0.0, seed=None:
                                 mod(group_norm_act(x, norm, film, p, seed)))(m)
     return blk
@@ -78,7 +79,9 @@ def _block_pair(cuda, cin, cout, fused):
 
 @pytest.mark.parametrize("cin,cout,h", [(128, 128, 32), (128, 256, 16), (256, 256, 16)])
 def test_fused_residual_block_matches_unfused(cuda, cin, cout, h):
-    """ResidualBlock with delayed scaling: GroupNormActConvFP8 vs group_norm_act + Conv2dFP8."""
+    """ResidualBlock with delayed scaling, three steps: the group-norm pass writing the e4m3 input and
+    the device-side scale histories (GroupNormActConvFP8Delayed) vs group_norm_act + Conv2dFP8 with
+    the reference's torch.max / scatter bookkeeping.  Same output bytes, histories and positions."""
     g = torch.Generator().manual_seed(cin + h)
     x0 = torch.randn(4, cin, h, h, generator=g).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
     t0 = torch.randn(4, 512, generator=g).to(torch.bfloat16)
@@ -87,19 +90,22 @@ def test_fused_residual_block_matches_unfused(cuda, cin, cout, h):
     res = {}
     for fused in (True, False):
         blk = _block_pair(cuda, cin, cout, fused)
-        x = x0.to(cuda).requires_grad_(True)
-        t = t0.to(cuda)
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            y = blk(x, t)
-        y.backward(dout.to(cuda))
+        for it in range(3):  # the histories advance and their maxima change between steps
+            x = (x0 * (1.0 + 0.5 * it)).to(cuda).requires_grad_(True)
+            t = t0.to(cuda)
+            blk.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                y = blk(x, t)
+            y.backward(dout.to(cuda) * (1.0 + it))
         torch.cuda.synchronize()
         res[fused] = dict(
             y=y.detach(), dx=x.grad.detach(),
             g1=blk.norm1.weight.grad, b1=blk.norm1.bias.grad, g2=blk.norm2.weight.grad, b2=blk.norm2.bias.grad,
             temb=blk.t_embed_wb.mlp.weight.grad, w1=blk.conv_1.conv.weight.grad, w2=blk.conv_2.conv.weight.grad,
-            win=torch.cat([m.amax_window_acts[:2] for m in (blk.conv_1, blk.conv_2)]
-                          + [m.amax_window_dy[:2] for m in (blk.conv_1, blk.conv_2)]
-                          + [m.amax_window_weights[:2] for m in (blk.conv_1, blk.conv_2)]),
+            win=torch.cat([m.amax_window_acts[:5] for m in (blk.conv_1, blk.conv_2)]
+                          + [m.amax_window_dy[:5] for m in (blk.conv_1, blk.conv_2)]
+                          + [m.amax_window_weights[:5] for m in (blk.conv_1, blk.conv_2)]
+                          + [m.window_pos.view(1).float() for m in (blk.conv_1, blk.conv_2)]),
         )
     a, b = res[True], res[False]
     assert torch.equal(a["y"], b["y"])
@@ -111,3 +117,35 @@ def test_fused_residual_block_matches_unfused(cuda, cin, cout, h):
         assert excess.max().item() <= 0.0, k
     for k in ("dx", "g1", "b1", "g2", "b2", "temb"):
         assert oracle.max_rel_err(a[k], b[k]) <= 1e-6, k
+
+
+def test_device_scale_history_matches_torch_bookkeeping(cuda):
+    """Conv2dFP8 (delayed) alone: ConvFP8Delayed vs the reference's bookkeeping around triton_conv2d_fp8,
+    over several steps (the dY scale lands one slot after the x / w scales, as in the reference)."""
+    from fp8_b200.unet import Conv2dFP8
+
+    g = torch.Generator().manual_seed(5)
+    x0 = torch.randn(8, 256, 16, 16, generator=g).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    mods = []
+    for dev_hist in (True, False):
+        torch.manual_seed(0)
+        m = Conv2dFP8(256, 256, True, "delayed", 1024, device_scale_history=dev_hist).to(cuda)
+        with torch.no_grad():
+            m.window_pos.fill_(1022)  # wraps around during the test
+        mods.append(m)
+    outs = {}
+    for m, key in zip(mods, ("device", "torch")):
+        ys = []
+        for it in range(4):
+            x = (x0 * (1.0 + it)).to(cuda).requires_grad_(True)
+            y = m(x)
+            y.backward(torch.ones_like(y) * 1e-3 * (it + 1))
+            ys.append((y.detach(), x.grad))
+        torch.cuda.synchronize()
+        outs[key] = (ys, m.amax_window_acts.clone(), m.amax_window_weights.clone(), m.amax_window_dy.clone(),
+                     m.window_pos.clone())
+    a, b = outs["device"], outs["torch"]
+    for (ya, ga), (yb, gb) in zip(a[0], b[0]):
+        assert torch.equal(ya, yb) and torch.equal(ga, gb)
+    for u, v in zip(a[1:], b[1:]):
+        assert torch.equal(u, v)
