@@ -1766,3 +1766,63 @@ int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds,
 }
 
 }  // extern "C"
+
+// ======================================================================== batched weight quantize
+namespace {
+int weight_chunks(int64_t n) { return static_cast<int>((n + kWeightChunk - 1) / kWeightChunk); }
+}  // namespace
+
+extern "C" {
+
+size_t fp8_quantize_weights_delayed_workspace_bytes(int count, const int64_t* n) {
+  if (count <= 0 || n == nullptr) return 0;
+  size_t chunks = 0;
+  for (int t = 0; t < count; ++t) chunks += n[t] > 0 ? static_cast<size_t>(weight_chunks(n[t])) : 0;
+  return chunks * sizeof(float);
+}
+
+int fp8_quantize_weights_delayed(int count, const float* const* w, void* const* q, const int64_t* n,
+                                 float* const* windows, int window_len, const int64_t* const* pos,
+                                 float* const* scale_used, void* workspace, size_t workspace_bytes,
+                                 fp8_stream_t stream) {
+  FP8_REQUIRE(count > 0 && count <= kMaxBatchWeights, FP8_ERR_UNSUPPORTED, "1..%d weights per call",
+              kMaxBatchWeights);
+  FP8_REQUIRE(w && q && n && windows && pos && scale_used && window_len > 0, FP8_ERR_INVALID_ARGUMENT,
+              "NULL argument");
+  WeightBatch b{};
+  b.count = count;
+  b.window_len = window_len;
+  int chunks = 0;
+  for (int t = 0; t < count; ++t) {
+    FP8_REQUIRE(n[t] > 0 && n[t] < (1ll << 31), FP8_ERR_INVALID_ARGUMENT, "weight %d: bad size", t);
+    FP8_REQUIRE(w[t] && aligned(w[t], 4) && q[t] && aligned(q[t], 2) && windows[t] && aligned(windows[t], 4) &&
+                    pos[t] && aligned(pos[t], 8) && scale_used[t] && aligned(scale_used[t], 4),
+                FP8_ERR_INVALID_ARGUMENT, "weight %d: NULL or unaligned pointer", t);
+    b.w[t] = w[t];
+    b.q[t] = static_cast<uint8_t*>(q[t]);
+    b.window[t] = windows[t];
+    b.pos[t] = pos[t];
+    b.used[t] = scale_used[t];
+    b.n[t] = n[t];
+    b.chunk_begin[t] = chunks;
+    chunks += weight_chunks(n[t]);
+  }
+  b.chunk_begin[count] = chunks;
+  FP8_REQUIRE(workspace != nullptr && aligned(workspace, 4) && workspace_bytes >= chunks * sizeof(float),
+              FP8_ERR_WORKSPACE, "workspace too small: need %zu bytes", chunks * sizeof(float));
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  (void)st;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  float* partials = static_cast<float*>(workspace);
+  FP8_CUDA_TRY(launch_kernel(weight_window_max_kernel, dim3(count), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
+                             b));
+  FP8_CUDA_TRY(launch_kernel(weight_cast_kernel, dim3(chunks), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel, b,
+                             partials));
+  FP8_CUDA_TRY(launch_kernel(weight_finalize_kernel, dim3(count), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
+                             b, static_cast<const float*>(partials)));
+  count_launches(3);
+  return ok();
+}
+
+}  // extern "C"

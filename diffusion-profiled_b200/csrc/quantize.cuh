@@ -716,4 +716,90 @@ __global__ void __launch_bounds__(256) transpose_u8_tiles16_kernel(const uint8_t
   *reinterpret_cast<uint4*>(d + (c0 + row) * dst_ld + r0 + seg) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// ---------------------------------------------------------------- batched weight quantize
+// The delayed quantize of many fp32 weight tensors at once (every FP8 conv of a
+// model, once per step): each weight is rounded to bf16 -- the reference's
+// weight.to(bfloat16), fp8_kernels.py:836 -- then cast exactly as the delayed
+// quantize casts a bf16 tensor, with its module's scale history max as the scale;
+// its own scale goes into that history at the module's position, which is not
+// advanced (the module's activation quantize writes at the same position and
+// advances it, so the histories end up as the reference's per-call bookkeeping
+// leaves them).  Three launches for all tensors: history maxima, cast (one
+// |w| partial per chunk), finalize.
+constexpr int kMaxBatchWeights = 64;
+constexpr int kWeightChunk = 4096;  // elements per chunk (16 KB of fp32)
+
+struct WeightBatch {
+  const float* w[kMaxBatchWeights];
+  uint8_t* q[kMaxBatchWeights];
+  float* window[kMaxBatchWeights];
+  const int64_t* pos[kMaxBatchWeights];
+  float* used[kMaxBatchWeights];  // the scale each tensor is cast with (its history max)
+  int64_t n[kMaxBatchWeights];
+  int chunk_begin[kMaxBatchWeights + 1];
+  int count;
+  int window_len;
+};
+static_assert(sizeof(WeightBatch) < 4096, "kernel parameter size");
+
+__device__ __forceinline__ int weight_of_chunk(const WeightBatch& b, int k) {
+  int lo = 0, hi = b.count - 1;  // last t with chunk_begin[t] <= k
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.chunk_begin[mid] <= k) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// One CTA per tensor: used[t] = max(window[t][0 .. len)).
+__global__ void __launch_bounds__(kQuantThreads) weight_window_max_kernel(WeightBatch b) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  const DelayedSource d{nullptr, b.window[t], b.window_len, nullptr};
+  const float m = delayed_scale<kQuantThreads>(d);
+  if (threadIdx.x == 0) *b.used[t] = m;
+}
+
+// One CTA per chunk of kWeightChunk elements; partials[k] = max |bf16(w)| of chunk k.
+__global__ void __launch_bounds__(kQuantThreads) weight_cast_kernel(WeightBatch b, float* __restrict__ partials) {
+  pdl_wait();
+  const int k = blockIdx.x;
+  const int t = weight_of_chunk(b, k);
+  const int64_t begin = static_cast<int64_t>(k - b.chunk_begin[t]) * kWeightChunk;
+  const int64_t end = min(begin + kWeightChunk, b.n[t]);
+  const float s = *b.used[t];
+  const float* __restrict__ w = b.w[t];
+  uint8_t* __restrict__ q = b.q[t];
+  float m = 0.0f;
+  // pairs of elements: round to bf16 (RN), |.| max, cast the pair
+  auto body = [&](const auto& div) {
+    for (int64_t i = begin + 2 * threadIdx.x; i < end; i += 2 * kQuantThreads) {
+      const float f0 = w[i];
+      const float f1 = i + 1 < end ? w[i + 1] : 0.0f;
+      const uint32_t word = pack_bf16x2(f0, f1);
+      m = fmaxf(m, unpack_max2(word & kAbsMask2));
+      const uint32_t bytes = div.word(word);
+      if (i + 1 < end)  // i is even and q 2-byte aligned: one 16-bit store
+        *reinterpret_cast<uint16_t*>(q + i) = static_cast<uint16_t>(bytes & 0xFFFFu);
+      else
+        q[i] = static_cast<uint8_t>(bytes & 0xFFu);
+    }
+  };
+  if (markstein_applies(s))  // uniform over the CTA
+    body(make_markstein(s));
+  else
+    body(DivF64(s));
+  m = block_max(m);
+  if (threadIdx.x == 0) partials[k] = m;
+}
+
+// One CTA per tensor: its scale from its chunks' partials, stored at window[pos].
+__global__ void __launch_bounds__(kQuantThreads) weight_finalize_kernel(WeightBatch b,
+                                                                         const float* __restrict__ partials) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  const float s = fold_partials_to_scale(partials + b.chunk_begin[t], b.chunk_begin[t + 1] - b.chunk_begin[t]);
+  if (threadIdx.x == 0) b.window[t][*b.pos[t]] = s;
+}
+
 }  // namespace fp8b

@@ -105,6 +105,12 @@ _SIGNATURES: dict[str, tuple] = {
         [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_float, c_void_p, c_int, c_void_p,
          c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
     ),
+    "fp8_quantize_weights_delayed_workspace_bytes": (c_size_t, [c_int, POINTER(c_int64)]),
+    "fp8_quantize_weights_delayed": (
+        c_int,
+        [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int64), POINTER(c_void_p), c_int, POINTER(c_void_p),
+         POINTER(c_void_p), c_void_p, c_size_t, c_void_p],
+    ),
     "fp8_gn_act_quant_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_quant_fwd": (
         c_int,

@@ -33,15 +33,23 @@ def _conv_backward(ctx, dy, xq, wq, sx, sw):
     return ops.conv3x3_dgrad(dyq, wq, sdy, sw), ops.conv3x3_wgrad(xq, dyq, sx, sdy)
 
 
+def _weight_q(weight, win_w, pos, pre):
+    """The e4m3 weight and its scale: from the step's batched weight quantize when given
+    (``pre = (wq, sw)``, history written, position to be stepped here), else quantized now."""
+    if pre is not None:
+        return pre
+    return ops.quantize_delayed_window(_weight_bf16(weight), win_w, pos, False)
+
+
 class ConvFP8Delayed(torch.autograd.Function):
     """``Conv2dFP8Specialized`` (delayed branch) plus the module's history update, on device histories."""
 
     @staticmethod
     @custom_fwd(device_type="cuda")
-    def forward(ctx, x, weight, win_x, win_w, win_dy, pos):
+    def forward(ctx, x, weight, win_x, win_w, win_dy, pos, pre=None):
         x = x.to(torch.bfloat16)
-        xq, sx = ops.quantize_delayed_window(x, win_x, pos, False)
-        wq, sw = ops.quantize_delayed_window(_weight_bf16(weight), win_w, pos, True)
+        wq, sw = _weight_q(weight, win_w, pos, pre)
+        xq, sx = ops.quantize_delayed_window(x, win_x, pos, True)
         ctx.save_for_backward(xq, wq, sx, sw)
         ctx.win_dy, ctx.pos = win_dy, pos
         return ops.conv3x3_fwd(xq, wq, sx, sw)
@@ -51,7 +59,7 @@ class ConvFP8Delayed(torch.autograd.Function):
     def backward(ctx, dy):
         xq, wq, sx, sw = ctx.saved_tensors
         dx, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
-        return dx, dw, None, None, None, None
+        return dx, dw, None, None, None, None, None
 
 
 class GroupNormActConvFP8Delayed(torch.autograd.Function):
@@ -60,10 +68,10 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
     @staticmethod
     @custom_fwd(device_type="cuda")
     def forward(ctx, x, gamma, beta, film, seed, weight, win_x, win_w, win_dy, pos, p: float, eps: float,
-                groups: int):
+                groups: int, pre=None):
         film2 = None if film is None else film.reshape(film.shape[0], -1)
-        xq, sx, stats = ops.gn_act_quant_fwd_window(x, gamma, beta, film2, seed, win_x, pos, False, p, eps, groups)
-        wq, sw = ops.quantize_delayed_window(_weight_bf16(weight), win_w, pos, True)
+        wq, sw = _weight_q(weight, win_w, pos, pre)
+        xq, sx, stats = ops.gn_act_quant_fwd_window(x, gamma, beta, film2, seed, win_x, pos, True, p, eps, groups)
         ctx.save_for_backward(x, gamma, beta, film2, seed, stats, xq, wq, sx, sw)
         ctx.win_dy, ctx.pos = win_dy, pos
         ctx.cfg = (p, eps, groups, None if film is None else film.shape)
@@ -77,7 +85,27 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
         d_act, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
         dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
         dfilm = None if film_shape is None else dfilm.reshape(film_shape)
-        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None
+        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None, None
 
 
-__all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed"]
+def quantize_conv_weights(convs) -> None:
+    """Quantize the weights of delayed-scaling FP8 conv modules in one batch (three launches).
+
+    Each module then finds ``(wq, sw)`` in ``_pre_weight`` for its next forward.  The weight
+    histories are written at the modules' positions, which the modules' activation quantize
+    then uses and steps, exactly as a per-call weight quantize would leave them."""
+    if not convs:
+        return
+    weights = []
+    for m in convs:
+        w = m.conv.weight.detach()
+        weights.append(w if w.is_contiguous(memory_format=torch.channels_last)
+                       else w.contiguous(memory_format=torch.channels_last))
+    out = ops.quantize_weights_delayed(weights, [m.amax_window_weights for m in convs],
+                                       [m.window_pos for m in convs])
+    k = len(convs)
+    for i, m in enumerate(convs):
+        m._pre_weight = (out[i], out[k + i])
+
+
+__all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed", "quantize_conv_weights"]

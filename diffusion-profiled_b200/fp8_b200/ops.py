@@ -14,7 +14,7 @@ Layouts: 4-D activations and conv weights are channels_last (physically NHWC /
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_void_p
+from ctypes import c_int64, c_void_p
 
 import torch
 
@@ -182,6 +182,45 @@ def quantize_delayed_window(x: torch.Tensor, window: torch.Tensor, pos: torch.Te
 def _(x, window, pos, advance):
     return (torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.preserve_format),
             x.new_empty((), dtype=torch.float32))
+
+
+@torch.library.custom_op("fp8_b200::quantize_weights_delayed", mutates_args=("windows",))
+def quantize_weights_delayed(weights: list[torch.Tensor], windows: list[torch.Tensor],
+                             positions: list[torch.Tensor]) -> list[torch.Tensor]:
+    """Delayed quantize of many fp32 weights in three launches -> [q_0 .. q_{n-1}, scale_0 .. scale_{n-1}].
+
+    Weight t is rounded to bf16, cast with ``max(windows[t])`` (returned as scale_t) and its own scale
+    stored at ``windows[t][positions[t]]``; positions are not advanced (the activation quantize of the
+    same module does that).  Bytes equal ``quantize_delayed_window(weights[t].bfloat16(), ...)``."""
+    count = len(weights)
+    if count == 0 or len(windows) != count or len(positions) != count:
+        raise RuntimeError("weights, windows and positions must be non-empty lists of one length")
+    dev = _require_cuda(*weights)
+    lens = {int(w.numel()) for w in windows}
+    if len(lens) != 1:
+        raise RuntimeError("all scale histories must have one length")
+    for w, win, pos in zip(weights, windows, positions):
+        if w.dtype != torch.float32 or not (w.is_contiguous() or w.is_contiguous(memory_format=torch.channels_last)):
+            raise RuntimeError("weights must be dense float32 tensors")
+        _check_window(win, pos, dev)
+    qs = [torch.empty_like(w, dtype=FP8_DTYPE, memory_format=torch.preserve_format) for w in weights]
+    used = [torch.empty((), device=dev, dtype=torch.float32) for _ in weights]
+    arr = lambda ts: (c_void_p * count)(*[t.data_ptr() for t in ts])  # noqa: E731
+    n = (c_int64 * count)(*[w.numel() for w in weights])
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_quantize_weights_delayed_workspace_bytes(count, n) // 4, 1), device=dev,
+                         dtype=torch.float32)
+        _lib.check(lib.fp8_quantize_weights_delayed(
+            count, arr(weights), arr(qs), n, arr(windows), lens.pop(), arr(positions), arr(used), _ptr(ws),
+            ws.numel() * 4, _stream(dev)), "fp8_quantize_weights_delayed")
+    return qs + used
+
+
+@quantize_weights_delayed.register_fake
+def _(weights, windows, positions):
+    return ([torch.empty_like(w, dtype=FP8_DTYPE, memory_format=torch.preserve_format) for w in weights]
+            + [w.new_empty((), dtype=torch.float32) for w in weights])
 
 
 # ----------------------------------------------------------------------------- transposes

@@ -27,7 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed
+from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed, quantize_conv_weights
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
 from .resample import downsample_nearest, upsample_cat
 from .norm import GroupNormActConvFP8, fused_layer_norm_supported, fused_norm_supported, group_norm_act, layer_norm_bf16
@@ -68,6 +68,8 @@ class Conv2dFP8(nn.Module):
                  amax_history: int | None = None, device_scale_history: bool = True):
         super().__init__()
         self.device_scale_history = device_scale_history
+        self._pre_weight = None  # (wq, sw) from a batched weight quantize, for the next forward
+        self.used_fp8_delayed = False  # whether the last forward ran the delayed FP8 path
         if scaling_type not in ("current", "delayed"):
             raise ValueError(f"unknown FP8 scaling type {scaling_type!r}")
         self.conv = nn.Conv2d(in_channels, out_channels, (3, 3), stride=1, padding=1, bias=False)
@@ -94,8 +96,10 @@ class Conv2dFP8(nn.Module):
         if self.scaling_type == "current":
             return triton_conv2d_fp8(x, self.conv.weight)
         if self.device_scale_history:
+            pre, self._pre_weight = self._pre_weight, None
+            self.used_fp8_delayed = True
             return ConvFP8Delayed.apply(x, self.conv.weight, self.amax_window_acts, self.amax_window_weights,
-                                        self.amax_window_dy, self.window_pos)
+                                        self.amax_window_dy, self.window_pos, pre)
         with torch.no_grad():
             x_hist = torch.max(self.amax_window_acts)
             w_hist = torch.max(self.amax_window_weights)
@@ -120,10 +124,12 @@ class Conv2dFP8(nn.Module):
             raise ValueError("dropout needs a seed tensor")
         x = x.contiguous(memory_format=torch.channels_last)
         if self.device_scale_history:
+            pre, self._pre_weight = self._pre_weight, None
+            self.used_fp8_delayed = True
             return GroupNormActConvFP8Delayed.apply(
                 x, norm.weight, norm.bias, film, seed if p > 0.0 else None, self.conv.weight, self.amax_window_acts,
                 self.amax_window_weights, self.amax_window_dy, self.window_pos, float(p), float(norm.eps),
-                int(norm.num_groups))
+                int(norm.num_groups), pre)
         with torch.no_grad():
             x_hist = torch.max(self.amax_window_acts)
             w_hist = torch.max(self.amax_window_weights)
@@ -278,6 +284,21 @@ class UNet(nn.Module):
         return emb
 
     def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        # The weights of the delayed-scaling FP8 convs that ran last time are quantized in one batch
+        # (identical bytes and histories to quantizing each inside its conv).
+        batch = getattr(self, "_fp8_delayed_convs", None)
+        if batch:
+            quantize_conv_weights(batch)
+        out = self._forward(x, t)
+        convs = [m for m in self.modules() if isinstance(m, Conv2dFP8) and m.used_fp8_delayed]
+        for m in convs:
+            m.used_fp8_delayed = False
+        for m in batch or ():
+            m._pre_weight = None  # a conv that did not run must not keep this step's weights
+        self._fp8_delayed_convs = convs if len(convs) <= 64 else None
+        return out
+
+    def _forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
         t_emb = self.time_embed(self._timestep(t))
         act = self.conv_in(x)
         skips = []

@@ -303,6 +303,20 @@ int fp8_quantize_delayed_window(const void* x_bf16, void* q_e4m3, float* window,
                                 int64_t* window_pos, int advance, float* scale_used_out, void* workspace,
                                 size_t workspace_bytes, int64_t n, fp8_stream_t stream);
 
+/* The delayed quantize of up to 64 fp32 weight tensors in three launches (all FP8
+ * conv weights of a model, once per step): tensor t is rounded to bf16 (the
+ * reference's weight.to(bfloat16), fp8_kernels.py:836), cast with
+ * max(windows[t][0 .. window_len)) -- written to *scale_used[t] -- and its own
+ * scale stored at windows[t][*pos[t]]; the positions are not advanced (the
+ * module's activation quantize, fp8_quantize_delayed_window with advance = 1,
+ * writes at the same position and steps it).  Same bytes and histories as one
+ * fp8_quantize_delayed_window per weight.  Pointer arrays are host memory. */
+size_t fp8_quantize_weights_delayed_workspace_bytes(int count, const int64_t* n);
+int fp8_quantize_weights_delayed(int count, const float* const* w, void* const* q, const int64_t* n,
+                                 float* const* windows, int window_len, const int64_t* const* pos,
+                                 float* const* scale_used, void* workspace, size_t workspace_bytes,
+                                 fp8_stream_t stream);
+
 /* fp8_gn_act_quant_fwd with the scale history of fp8_quantize_delayed_window. */
 int fp8_gn_act_quant_fwd_window(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
                                 int film_ld, const int64_t* seed, float p, float eps, float* window, int window_len,

@@ -149,3 +149,34 @@ def test_device_scale_history_matches_torch_bookkeeping(cuda):
         assert torch.equal(ya, yb) and torch.equal(ga, gb)
     for u, v in zip(a[1:], b[1:]):
         assert torch.equal(u, v)
+
+
+def test_batched_weight_quantize_matches_per_conv(cuda):
+    """UNet forward/backward steps with the per-step batched weight quantize give the same outputs,
+    histories and positions as quantizing each weight inside its conv (the first forward of a model)."""
+    from fp8_b200.train import build_model
+    from fp8_b200.unet import Conv2dFP8
+
+    x = (torch.rand(4, 3, 32, 32) * 2 - 1).to(cuda).contiguous(memory_format=torch.channels_last)
+    t = torch.randint(0, 1000, (4,)).to(cuda)
+    runs = []
+    for batched in (True, False):
+        m = build_model(fp8=True, scaling="delayed", device=cuda, seed=0, p_drop=0.0)
+        outs = []
+        for step in range(3):
+            if not batched:
+                m._fp8_delayed_convs = None  # every step quantizes inside the convs
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                y = m(x * (1 + step), t)
+            y.float().square().mean().backward()
+            outs.append(y.detach())
+        convs = [c for c in m.modules() if isinstance(c, Conv2dFP8)]
+        hist = torch.cat([torch.cat([c.amax_window_weights[:4], c.amax_window_acts[:4], c.amax_window_dy[:4],
+                                     c.window_pos.view(1).float()]) for c in convs])
+        grads = torch.cat([c.conv.weight.grad.flatten()[:64].float() for c in convs if c.conv.weight.grad is not None])
+        runs.append((outs, hist, grads))
+    (oa, ha, ga), (ob, hb, gb) = runs
+    for u, v in zip(oa, ob):
+        assert torch.equal(u, v)
+    assert torch.equal(ha, hb)
+    assert ((ga - gb).abs() <= 2.0 ** -7 * gb.abs() + 1e-4 * gb.abs().max()).all()
