@@ -591,7 +591,7 @@ def time_unet(args, dev, world, fp8: bool) -> dict:
     # the B200 path: FP8 convs + fused norm/activation ops; the comparison: the
     # reference's bf16 model with its torch ops
     model = build_model(fp8=fp8, scaling="delayed", device=dev, seed=0, fused_norm=fp8)
-    cfg = TrainConfig(batch_size=args.batch)
+    cfg = TrainConfig(batch_size=args.batch, fused_optimizer=fp8)  # the reference-ops arm keeps torch's AdamW
     if args.bucket_mb:
         cfg.allreduce_bucket_mb = args.bucket_mb
     step = GraphedTrainStep(model, cfg, dev)
@@ -628,9 +628,14 @@ def time_unet(args, dev, world, fp8: bool) -> dict:
             "global_batch": args.batch * world, "n_gpus": world, "mean_loss": round(loss, 4),
             "fp8": ("whitelisted 3x3 convs, delayed scaling" if fp8 else "off (bf16 autocast)"),
             "norm_activation": ("fused GroupNorm/FiLM/SiLU/dropout kernels (the FP8 conv input written as e4m3), "
-                                "LayerNorm kernels in the attention blocks" if fp8 else "torch ops (reference)"),
+                                "LayerNorm kernels in the attention blocks, fused nearest resampling + skip "
+                                "concatenation" if fp8 else "torch ops (reference)"),
+            "scale_history": ("device-side (the casts read and update the histories; batched weight quantize)"
+                              if fp8 else None),
+            "optimizer": ("clip + AdamW + EMA in one pass (fp8_b200.optim)" if fp8
+                          else "clip_grad_norm_ + torch fused AdamW + foreach EMA"),
             "conv_modules": n_fp8, "allreduce_bf16_bytes_per_step": allreduce,
-            "step": "noise + UNet fwd/bwd (bf16 autocast) + grad all-reduce + clip 1.0 + fused AdamW 2e-4 + EMA, "
+            "step": "noise + UNet fwd/bwd (bf16 autocast) + grad all-reduce + clip 1.0 + AdamW 2e-4 + EMA, "
                     "one CUDA graph replay"}
 
 

@@ -22,6 +22,7 @@
 #include "groupnorm.cuh"
 #include "layernorm.cuh"
 #include "resample.cuh"
+#include "optim.cuh"
 
 using namespace fp8b;
 
@@ -1822,6 +1823,99 @@ int fp8_quantize_weights_delayed(int count, const float* const* w, void* const* 
   FP8_CUDA_TRY(launch_kernel(weight_finalize_kernel, dim3(count), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
                              b, static_cast<const float*>(partials)));
   count_launches(3);
+  return ok();
+}
+
+}  // extern "C"
+
+// ======================================================================== clip + AdamW + EMA
+namespace {
+int opt_chunks(int64_t n) { return static_cast<int>((n + kOptChunk - 1) / kOptChunk); }
+
+// Groups of at most kOptTensors tensors: [first, last) ranges into the caller's arrays.
+template <typename F>
+int for_each_group(int count, F&& f) {
+  for (int first = 0; first < count; first += kOptTensors)
+    if (int s = f(first, std::min(count, first + kOptTensors))) return s;
+  return FP8_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t fp8_adamw_ema_workspace_bytes(int count, const int64_t* n) {
+  if (count <= 0 || n == nullptr) return 0;
+  size_t chunks = 0;
+  for (int t = 0; t < count; ++t) chunks += n[t] > 0 ? static_cast<size_t>(opt_chunks(n[t])) : 0;
+  return 16 + chunks * sizeof(float);
+}
+
+int fp8_adamw_ema_step(int count, float* const* params, const float* const* grads, float* const* exp_avg,
+                       float* const* exp_avg_sq, float* const* ema, const int64_t* n, float* step, float lr,
+                       float beta1, float beta2, float eps, float weight_decay, float ema_beta, float max_grad_norm,
+                       void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+  FP8_REQUIRE(count > 0, FP8_ERR_INVALID_ARGUMENT, "no parameters");
+  FP8_REQUIRE(params && grads && exp_avg && exp_avg_sq && n && step, FP8_ERR_INVALID_ARGUMENT, "NULL argument");
+  FP8_REQUIRE(aligned(step, 4), FP8_ERR_INVALID_ARGUMENT, "step must be a 4-byte aligned float");
+  int64_t chunks = 0;
+  for (int t = 0; t < count; ++t) {
+    FP8_REQUIRE(n[t] > 0 && n[t] < (1ll << 31), FP8_ERR_INVALID_ARGUMENT, "tensor %d: bad size", t);
+    FP8_REQUIRE(params[t] && grads[t] && exp_avg[t] && exp_avg_sq[t], FP8_ERR_INVALID_ARGUMENT,
+                "tensor %d: NULL pointer", t);
+    chunks += opt_chunks(n[t]);
+  }
+  FP8_REQUIRE(workspace != nullptr && aligned(workspace, 16) &&
+                  workspace_bytes >= 16 + static_cast<size_t>(chunks) * sizeof(float),
+              FP8_ERR_WORKSPACE, "workspace too small: need %zu bytes", 16 + static_cast<size_t>(chunks) * 4);
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  (void)st;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  float* coef = static_cast<float*>(workspace);
+  float* partials = coef + 4;
+  auto group = [&](int first, int last, OptGroup* g) {
+    *g = OptGroup{};
+    g->count = last - first;
+    int c = 0;
+    for (int t = first; t < last; ++t) {
+      const int i = t - first;
+      g->p[i] = params[t];
+      g->g[i] = grads[t];
+      g->m[i] = exp_avg[t];
+      g->v[i] = exp_avg_sq[t];
+      g->ema[i] = ema != nullptr ? ema[t] : nullptr;
+      g->n[i] = n[t];
+      g->chunk_begin[i] = c;
+      c += opt_chunks(n[t]);
+    }
+    g->chunk_begin[g->count] = c;
+    return c;
+  };
+  int part0 = 0;
+  if (max_grad_norm > 0.0f) {
+    if (int s = for_each_group(count, [&](int first, int last) {
+          OptGroup g;
+          const int c = group(first, last, &g);
+          FP8_CUDA_TRY(launch_kernel(opt_sumsq_kernel, dim3(c), dim3(kOptThreads), 0, cs, 1, kStreamingKernel, g,
+                                     partials, part0));
+          part0 += c;
+          count_launches(1);
+          return FP8_OK;
+        }))
+      return s;
+  }
+  FP8_CUDA_TRY(launch_kernel(opt_norm_kernel, dim3(1), dim3(kOptThreads), 0, cs, 1, kStreamingKernel,
+                             static_cast<const float*>(partials), part0, max_grad_norm, coef, step));
+  count_launches(1);
+  const OptHyper h{lr, beta1, beta2, eps, weight_decay, ema_beta, max_grad_norm, coef, step};
+  if (int s = for_each_group(count, [&](int first, int last) {
+        OptGroup g;
+        const int c = group(first, last, &g);
+        FP8_CUDA_TRY(launch_kernel(opt_update_kernel, dim3(c), dim3(kOptThreads), 0, cs, 1, kStreamingKernel, g, h));
+        count_launches(1);
+        return FP8_OK;
+      }))
+    return s;
   return ok();
 }
 

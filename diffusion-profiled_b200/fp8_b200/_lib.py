@@ -111,6 +111,13 @@ _SIGNATURES: dict[str, tuple] = {
         [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int64), POINTER(c_void_p), c_int, POINTER(c_void_p),
          POINTER(c_void_p), c_void_p, c_size_t, c_void_p],
     ),
+    "fp8_adamw_ema_workspace_bytes": (c_size_t, [c_int, POINTER(c_int64)]),
+    "fp8_adamw_ema_step": (
+        c_int,
+        [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
+         POINTER(c_int64), c_void_p, c_float, c_float, c_float, c_float, c_float, c_float, c_float, c_void_p,
+         c_size_t, c_void_p],
+    ),
     "fp8_gn_act_quant_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_quant_fwd": (
         c_int,

@@ -317,6 +317,18 @@ int fp8_quantize_weights_delayed(int count, const float* const* w, void* const* 
                                  float* const* scale_used, void* workspace, size_t workspace_bytes,
                                  fp8_stream_t stream);
 
+/* The training step's tail in one pass over the parameters: gradient clipping
+ * to max_grad_norm (torch.nn.utils.clip_grad_norm_; none when <= 0), AdamW
+ * (decoupled weight decay, bias corrections from the device step count, which
+ * this call increments) and, when ema != NULL, the EMA of the weights after the
+ * update, ema = RN(ema * ema_beta) + RN((1 - ema_beta) * p) (reference
+ * ddpm.py:20-25).  fp32 tensors; pointer arrays are host memory. */
+size_t fp8_adamw_ema_workspace_bytes(int count, const int64_t* n);
+int fp8_adamw_ema_step(int count, float* const* params, const float* const* grads, float* const* exp_avg,
+                       float* const* exp_avg_sq, float* const* ema, const int64_t* n, float* step, float lr,
+                       float beta1, float beta2, float eps, float weight_decay, float ema_beta, float max_grad_norm,
+                       void* workspace, size_t workspace_bytes, fp8_stream_t stream);
+
 /* fp8_gn_act_quant_fwd with the scale history of fp8_quantize_delayed_window. */
 int fp8_gn_act_quant_fwd_window(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
                                 int film_ld, const int64_t* seed, float p, float eps, float* window, int window_len,
