@@ -1920,3 +1920,70 @@ int fp8_adamw_ema_step(int count, float* const* params, const float* const* grad
 }
 
 }  // extern "C"
+
+// ======================================================================== residual joins
+namespace {
+template <typename TA, typename TB, typename TO>
+int launch_add_scale(const void* a, const void* b, void* y, int64_t vecs, float inv, bool bwd, int sms,
+                     cudaStream_t cs) {
+  const dim3 grid(resample_grid(vecs, sms)), block(kResampleThreads);
+  if (!bwd)
+    FP8_CUDA_TRY(launch_kernel(add_scale_kernel<TA, TB, TO>, grid, block, 0, cs, 1, kStreamingKernel,
+                               static_cast<const TA*>(a), static_cast<const TB*>(b), vecs, inv, static_cast<TO*>(y)));
+  else  // a, b: the two gradients; y: the incoming gradient
+    FP8_CUDA_TRY(launch_kernel(add_scale_bwd_kernel<TA, TB, TO>, grid, block, 0, cs, 1, kStreamingKernel,
+                               static_cast<const TO*>(y), vecs, inv, static_cast<TA*>(const_cast<void*>(a)),
+                               static_cast<TB*>(const_cast<void*>(b))));
+  count_launches(1);
+  return FP8_OK;
+}
+
+template <typename TA, typename TB>
+int add_scale_out(int y_dtype, const void* a, const void* b, void* y, int64_t vecs, float inv, bool bwd, int sms,
+                  cudaStream_t cs) {
+  return y_dtype ? launch_add_scale<TA, TB, float>(a, b, y, vecs, inv, bwd, sms, cs)
+                 : launch_add_scale<TA, TB, uint16_t>(a, b, y, vecs, inv, bwd, sms, cs);
+}
+
+int add_scale_dispatch(int a_dtype, int b_dtype, int y_dtype, const void* a, const void* b, void* y, int64_t n,
+                       float inv, bool bwd, int sms, cudaStream_t cs) {
+  const int64_t vecs = n / 8;
+  if (a_dtype)
+    return b_dtype ? add_scale_out<float, float>(y_dtype, a, b, y, vecs, inv, bwd, sms, cs)
+                   : add_scale_out<float, uint16_t>(y_dtype, a, b, y, vecs, inv, bwd, sms, cs);
+  return b_dtype ? add_scale_out<uint16_t, float>(y_dtype, a, b, y, vecs, inv, bwd, sms, cs)
+                 : add_scale_out<uint16_t, uint16_t>(y_dtype, a, b, y, vecs, inv, bwd, sms, cs);
+}
+}  // namespace
+
+extern "C" {
+
+int fp8_add_scale(const void* a, int a_dtype, const void* b, int b_dtype, void* y, int y_dtype, int64_t n,
+                  float inv_divisor, fp8_stream_t stream) {
+  FP8_REQUIRE(n > 0 && n % 8 == 0, FP8_ERR_UNSUPPORTED, "n must be a positive multiple of 8");
+  if (int r = check_resample(a, a_dtype, "a")) return r;
+  if (int r = check_resample(b, b_dtype, "b")) return r;
+  if (int r = check_resample(y, y_dtype, "y")) return r;
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  if (int r = add_scale_dispatch(a_dtype, b_dtype, y_dtype, a, b, y, n, inv_divisor, false, st->sm_count,
+                                 reinterpret_cast<cudaStream_t>(stream)))
+    return r;
+  return ok();
+}
+
+int fp8_add_scale_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* db, int b_dtype, int64_t n,
+                      float inv_divisor, fp8_stream_t stream) {
+  FP8_REQUIRE(n > 0 && n % 8 == 0, FP8_ERR_UNSUPPORTED, "n must be a positive multiple of 8");
+  if (int r = check_resample(dy, y_dtype, "dy")) return r;
+  if (int r = check_resample(da, a_dtype, "da")) return r;
+  if (int r = check_resample(db, b_dtype, "db")) return r;
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  if (int r = add_scale_dispatch(a_dtype, b_dtype, y_dtype, da, db, const_cast<void*>(dy), n, inv_divisor, true,
+                                 st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+    return r;
+  return ok();
+}
+
+}  // extern "C"

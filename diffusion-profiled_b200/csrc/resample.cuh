@@ -139,4 +139,49 @@ __global__ void __launch_bounds__(kResampleThreads) up_cat_bwd_kernel(const TO* 
   }
 }
 
+// ---------------------------------------------------------------- residual joins
+// y = (a + b) / sqrt(2) as the reference's bf16-autocast ops compute it
+// (unet.py:161 and :203, `(skip + h) / math.sqrt(2.0)`): the sum rounded to the
+// result dtype TO (the wider of the two), then multiplied by inv = RN32(1 / RN32(sqrt 2))
+// -- torch divides a tensor by a host scalar as a multiplication by its
+// reciprocal in fp32 -- and rounded to TO again.  Backward: g = RN_TO(dy * inv),
+// handed to a and b in their own dtypes.  Element-wise on dense tensors of one
+// memory layout, 8 elements per thread.
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  if constexpr (sizeof(T) == 2) return __uint_as_float(pack_bf16x2(v, 0.0f) << 16);
+  return v;
+}
+
+template <typename TA, typename TB, typename TO>
+__global__ void __launch_bounds__(kResampleThreads) add_scale_kernel(const TA* __restrict__ a, const TB* __restrict__ b,
+                                                                     int64_t vecs, float inv, TO* __restrict__ y) {
+  pdl_wait();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vecs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float fa[8], fb[8];
+    load8f(a, i, fa);
+    load8f(b, i, fb);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) fa[k] = round_to<TO>(fa[k] + fb[k]) * inv;
+    store_x8(y, i, fa);
+  }
+}
+
+template <typename TA, typename TB, typename TO>
+__global__ void __launch_bounds__(kResampleThreads) add_scale_bwd_kernel(const TO* __restrict__ dy, int64_t vecs,
+                                                                         float inv, TA* __restrict__ da,
+                                                                         TB* __restrict__ db) {
+  pdl_wait();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vecs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float g[8];
+    load8f(dy, i, g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] = round_to<TO>(g[k] * inv);
+    store_x8(da, i, g);
+    store_x8(db, i, g);
+  }
+}
+
 }  // namespace fp8b

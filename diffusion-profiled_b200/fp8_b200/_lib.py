@@ -118,6 +118,8 @@ _SIGNATURES: dict[str, tuple] = {
          POINTER(c_int64), c_void_p, c_float, c_float, c_float, c_float, c_float, c_float, c_float, c_void_p,
          c_size_t, c_void_p],
     ),
+    "fp8_add_scale": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int64, c_float, c_void_p]),
+    "fp8_add_scale_bwd": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int64, c_float, c_void_p]),
     "fp8_gn_act_quant_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "fp8_gn_act_quant_fwd": (
         c_int,

@@ -660,6 +660,44 @@ def _(dy, c1, factor, a_fp32, s_fp32):
             dy.new_empty((n, c - c1, h, w), dtype=ts).contiguous(memory_format=cl))
 
 
+@torch.library.custom_op("fp8_b200::add_scale", mutates_args=())
+def add_scale(a: torch.Tensor, b: torch.Tensor, inv: float) -> torch.Tensor:
+    """RN(RN(a + b) * inv) in the wider dtype of a and b (same shape and dense layout)."""
+    dev = _require_cuda(a, b)
+    dt = torch.promote_types(a.dtype, b.dtype)
+    y = torch.empty_like(a, dtype=dt)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_add_scale", _ptr(a), _DT[a.dtype], _ptr(b), _DT[b.dtype], _ptr(y), _DT[dt], a.numel(),
+                  float(inv), _stream(dev))
+    return y
+
+
+@add_scale.register_fake
+def _(a, b, inv):
+    return torch.empty_like(a, dtype=torch.promote_types(a.dtype, b.dtype))
+
+
+@torch.library.custom_op("fp8_b200::add_scale_bwd", mutates_args=())
+def add_scale_bwd(dy: torch.Tensor, inv: float, a_fp32: bool, b_fp32: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gradients of add_scale: RN(dy * inv) in each input's dtype."""
+    dev = _require_cuda(dy)
+    if dy.dtype not in _DT or not (dy.is_contiguous() or (dy.dim() == 4 and dy.is_contiguous(
+            memory_format=torch.channels_last))):
+        dy = dy.contiguous(memory_format=torch.channels_last) if dy.dim() == 4 else dy.contiguous()
+    da = torch.empty_like(dy, dtype=torch.float32 if a_fp32 else torch.bfloat16)
+    db = torch.empty_like(dy, dtype=torch.float32 if b_fp32 else torch.bfloat16)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_add_scale_bwd", _ptr(dy), _DT[dy.dtype], _ptr(da), _DT[da.dtype], _ptr(db), _DT[db.dtype],
+                  dy.numel(), float(inv), _stream(dev))
+    return da, db
+
+
+@add_scale_bwd.register_fake
+def _(dy, inv, a_fp32, b_fp32):
+    return (torch.empty_like(dy, dtype=torch.float32 if a_fp32 else torch.bfloat16),
+            torch.empty_like(dy, dtype=torch.float32 if b_fp32 else torch.bfloat16))
+
+
 @torch.library.custom_op("fp8_b200::gn_act_quant_fwd", mutates_args=())
 def gn_act_quant_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
                      seed: torch.Tensor | None, prev_scale: torch.Tensor, p: float, eps: float,

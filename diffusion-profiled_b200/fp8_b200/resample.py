@@ -8,14 +8,20 @@ output is fp32) and ``torch.cat`` promotes to the wider dtype, so those lines
 cost a cast pass, a resampling pass and a concatenation copy.
 :func:`downsample_nearest` and :func:`upsample_cat` produce the same values and
 dtypes in one read and one write per element (``fp8_b200::resample_down2`` /
-``up_cat`` and their backward ops).
+``up_cat`` and their backward ops).  :func:`residual_join` does the residual
+``(skip + h) / math.sqrt(2.0)`` the same way.
 """
 
 from __future__ import annotations
 
+import math
+
+import numpy as np
 import torch
 
 from . import ops
+
+_FLOATS = (torch.bfloat16, torch.float32)
 
 
 class _Down2(torch.autograd.Function):
@@ -66,4 +72,32 @@ def upsample_cat(a: torch.Tensor, s: torch.Tensor, factor: int) -> torch.Tensor:
     return _UpCat.apply(a, s, factor, up_fp32 or s.dtype == torch.float32)
 
 
-__all__ = ["downsample_nearest", "upsample_cat", "resample_supported"]
+class _AddScale(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b, inv: float):
+        ctx.cfg = (a.dtype, b.dtype, inv)
+        return ops.add_scale(a, b, inv)
+
+    @staticmethod
+    def backward(ctx, dy):
+        ta, tb, inv = ctx.cfg
+        da, db = ops.add_scale_bwd(dy, inv, ta == torch.float32, tb == torch.float32)
+        return da, db, None
+
+
+def _same_dense_layout(a: torch.Tensor, b: torch.Tensor) -> bool:
+    if a.shape != b.shape or a.stride() != b.stride():
+        return False
+    return a.is_contiguous() or (a.dim() == 4 and a.is_contiguous(memory_format=torch.channels_last))
+
+
+def residual_join(a: torch.Tensor, b: torch.Tensor, divisor: float = math.sqrt(2.0)) -> torch.Tensor:
+    """``(a + b) / divisor`` as one pass, with the dtype and the two roundings of the torch ops (unet.py:161, :203)."""
+    if not (a.is_cuda and b.is_cuda and a.dtype in _FLOATS and b.dtype in _FLOATS and _same_dense_layout(a, b)
+            and a.numel() % 8 == 0 and a.numel() > 0):
+        return (a + b) / divisor
+    inv = float(np.float32(1.0) / np.float32(divisor))  # torch: a host scalar divisor becomes an fp32 reciprocal
+    return _AddScale.apply(a, b, inv)
+
+
+__all__ = ["downsample_nearest", "upsample_cat", "resample_supported", "residual_join"]

@@ -29,7 +29,7 @@ import torch.nn.functional as F
 
 from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed, quantize_conv_weights
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
-from .resample import downsample_nearest, upsample_cat
+from .resample import downsample_nearest, residual_join, upsample_cat
 from .norm import GroupNormActConvFP8, fused_layer_norm_supported, fused_norm_supported, group_norm_act, layer_norm_bf16
 
 
@@ -56,6 +56,8 @@ class UNetConfig:
     # device (fp8_b200.delayed) instead of torch.max / scatter launches per conv;
     # the histories, scales and results are the same
     device_scale_history: bool = True
+    # the residual joins (skip + h) / sqrt(2) as one pass (fp8_b200.resample.residual_join)
+    fused_residual: bool = True
 
     def as_dict(self):
         return asdict(self)
@@ -171,6 +173,7 @@ class ResidualBlock(nn.Module):
         self.dropout = nn.Dropout(p_drop)
         nn.init.zeros_(self.conv_2.conv.weight)
         self.fused_norm = config.fused_norm
+        self.fused_residual = config.fused_residual
         # dropout mask seed of the fused path (device scalar, advanced every
         # training forward so a captured graph draws a new mask each replay)
         self.register_buffer("dropout_seed", torch.randint(0, 2**62, (), dtype=torch.int64), persistent=False)
@@ -187,12 +190,17 @@ class ResidualBlock(nn.Module):
             if fused_norm_supported(h, self.norm2) and emb.dtype == torch.bfloat16:
                 p = self.dropout.p if self.training else 0.0
                 h = self.conv_2.forward_normed(h, self.norm2, emb, p, self._next_seed() if p > 0.0 else None)
-                return (self.skip_connection(x) + h) / math.sqrt(2.0)
+                return self._join(x, h)
         else:
             h = self.conv_1(F.silu(self.norm1(x)))
         scale, shift = torch.chunk(emb, chunks=2, dim=1)
         h = (scale + 1) * self.norm2(h) + shift
         h = self.conv_2(self.dropout(F.silu(h)))
+        return self._join(x, h)
+
+    def _join(self, x: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+        if self.fused_residual:
+            return residual_join(self.skip_connection(x), h)
         return (self.skip_connection(x) + h) / math.sqrt(2.0)
 
 
@@ -202,6 +210,7 @@ class CHWAttention(nn.Module):
     def __init__(self, config: UNetConfig, hidden_size: int):
         super().__init__()
         self.fused_norm = config.fused_norm
+        self.fused_residual = config.fused_residual
         self.nh = config.n_heads
         self.qkv = nn.Linear(hidden_size, 3 * hidden_size, bias=False)
         self.out = nn.Linear(hidden_size, hidden_size, bias=False)
@@ -219,7 +228,10 @@ class CHWAttention(nn.Module):
         heads = lambda z: z.unflatten(-1, (self.nh, c // self.nh)).transpose(1, 2)  # noqa: E731
         o = F.scaled_dot_product_attention(heads(q), heads(k), heads(v))
         o = self.out(o.transpose(1, 2).flatten(2))  # [B, HW, C]
-        return (o.transpose(1, 2).reshape(b, c, h, w) + x) / math.sqrt(2.0)
+        o = o.transpose(1, 2).reshape(b, c, h, w)
+        if self.fused_residual:
+            return residual_join(o, x)
+        return (o + x) / math.sqrt(2.0)
 
 
 class Stage(nn.Module):

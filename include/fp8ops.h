@@ -336,6 +336,17 @@ int fp8_gn_act_quant_fwd_window(const void* x, int x_fp32, const float* gamma, c
                                 int n, int hw, int c, int groups, void* workspace, size_t workspace_bytes,
                                 fp8_stream_t stream);
 
+/* The UNet's residual join y = (a + b) / d (reference unet.py:161, :203 with
+ * d = sqrt 2) as its bf16-autocast ops compute it: the sum rounded to y's dtype,
+ * then times inv_divisor = RN32(1 / d), rounded again (torch divides by a host
+ * scalar as a multiplication by its fp32 reciprocal).  The backward writes
+ * g = RN_y(dy * inv_divisor) to da and db in their own dtypes.  n elements of
+ * one dense layout, n % 8 == 0; dtype codes as fp8_up_cat. */
+int fp8_add_scale(const void* a, int a_dtype, const void* b, int b_dtype, void* y, int y_dtype, int64_t n,
+                  float inv_divisor, fp8_stream_t stream);
+int fp8_add_scale_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* db, int b_dtype, int64_t n,
+                      float inv_divisor, fp8_stream_t stream);
+
 /* Workspace bytes of fp8_gn_act_quant_fwd. */
 size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c);
 

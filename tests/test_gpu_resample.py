@@ -82,3 +82,25 @@ def test_unet_forward_identical_with_fused_resampling(cuda):
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
             ys.append(m(x, t))
     assert torch.equal(ys[0], ys[1])
+
+
+@pytest.mark.parametrize("ta,tb", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.bfloat16),
+                                   (torch.bfloat16, torch.float32), (torch.float32, torch.float32)])
+def test_residual_join_matches_torch_bitwise(cuda, ta, tb):
+    """(a + b) / math.sqrt(2.0) as the reference's ops compute it, forward and backward, bit for bit."""
+    import math
+
+    from fp8_b200.resample import residual_join
+
+    a0 = _t((16, 256, 16, 16), ta, 21, cuda)
+    b0 = _t((16, 256, 16, 16), tb, 22, cuda)
+    res = []
+    for fused in (True, False):
+        a = a0.clone().requires_grad_(True)
+        b = b0.clone().requires_grad_(True)
+        y = residual_join(a, b) if fused else (a + b) / math.sqrt(2.0)
+        dy = _t(y.shape, y.dtype, 23, cuda)
+        y.backward(dy)
+        res.append((y.detach(), a.grad, b.grad))
+    for u, v in zip(*res):
+        assert u.dtype == v.dtype and torch.equal(u, v)
