@@ -472,10 +472,15 @@ def _gn_check(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: to
     n, c, h, w = x.shape
     if gamma.dtype != torch.float32 or beta.dtype != torch.float32 or gamma.numel() != c or beta.numel() != c:
         raise RuntimeError("gamma / beta must be float32 [C]")
-    if film is not None and (film.dtype != torch.bfloat16 or film.shape[0] != n or film.numel() != n * 2 * c
-                             or not film.is_contiguous()):
-        raise RuntimeError("film must be a contiguous bfloat16 [N, 2C] (scale, shift) tensor")
+    if film is not None and (film.dtype != torch.bfloat16 or film.dim() != 2 or tuple(film.shape) != (n, 2 * c)
+                             or film.stride(1) != 1 or film.stride(0) < 2 * c):
+        raise RuntimeError("film must be a bfloat16 [N, 2C] (scale, shift) tensor with unit column stride")
     return n, c, h * w
+
+
+def _film_ld(film: torch.Tensor | None, c: int) -> int:
+    """Row pitch of the FiLM rows (they may be a column slice of all blocks' projections)."""
+    return 2 * c if film is None else film.stride(0)
 
 
 @torch.library.custom_op("fp8_b200::gn_act_fwd", mutates_args=())
@@ -495,7 +500,7 @@ def gn_act_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: t
     with torch.cuda.device(dev):
         ws = torch.empty(max(lib.fp8_gn_workspace_bytes(n, hw, c) // 4, 4), device=dev, dtype=torch.float32)
         _lib.check(lib.fp8_gn_act_fwd(
-            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps), _ptr(stats),
+            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), _film_ld(film, c), _ptr(seed), float(p), float(eps), _ptr(stats),
             _ptr(out), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)), "fp8_gn_act_fwd")
     return out, stats
 
@@ -718,7 +723,7 @@ def gn_act_quant_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, f
         ws = torch.empty(max(lib.fp8_gn_act_quant_workspace_bytes(n, hw, c) // 4, 4), device=dev,
                          dtype=torch.float32)
         _lib.check(lib.fp8_gn_act_quant_fwd(
-            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed),
+            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), _film_ld(film, c), _ptr(seed),
             float(p), float(eps), _ptr(prev_scale), _ptr(stats), _ptr(q), _ptr(scale), n, hw, c, groups, _ptr(ws),
             ws.numel() * 4, _stream(dev)), "fp8_gn_act_quant_fwd")
     return q, scale, stats
@@ -740,7 +745,7 @@ def gn_act_quant_fwd_window(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Te
         ws = torch.empty(max(lib.fp8_gn_act_quant_workspace_bytes(n, hw, c) // 4, 4), device=dev,
                          dtype=torch.float32)
         _lib.check(lib.fp8_gn_act_quant_fwd_window(
-            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed),
+            _ptr(x), int(x.dtype == torch.float32), _ptr(gamma), _ptr(beta), _ptr(film), _film_ld(film, c), _ptr(seed),
             float(p), float(eps), _ptr(window), window.numel(), _ptr(pos), int(advance), _ptr(used), _ptr(stats),
             _ptr(q), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)), "fp8_gn_act_quant_fwd_window")
     return q, used, stats
@@ -775,13 +780,13 @@ def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: tor
     with torch.cuda.device(dev):
         ws = torch.empty(max(lib.fp8_gn_workspace_bytes(n, hw, c) // 4, 4), device=dev, dtype=torch.float32)
         _lib.check(lib.fp8_gn_act_bwd(
-            _ptr(x), int(x.dtype == torch.float32), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), 2 * c, _ptr(seed), float(p), float(eps),
+            _ptr(x), int(x.dtype == torch.float32), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), _film_ld(film, c), _ptr(seed), float(p), float(eps),
             _ptr(stats), _ptr(totals), _ptr(dx), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)),
             "fp8_gn_act_bwd")
         dgamma = torch.empty((c,), device=dev, dtype=torch.float32)
         dbeta = torch.empty((c,), device=dev, dtype=torch.float32)
         dfilm = torch.empty((n, 2 * c) if film is not None else (0,), device=dev, dtype=torch.bfloat16)
-        _lib.check(lib.fp8_gn_param_grads(_ptr(totals), _ptr(film), 2 * c, n, c, _ptr(dgamma), _ptr(dbeta),
+        _lib.check(lib.fp8_gn_param_grads(_ptr(totals), _ptr(film), _film_ld(film, c), n, c, _ptr(dgamma), _ptr(dbeta),
                                           _ptr(dfilm) if film is not None else None, 2 * c, _stream(dev)),
                    "fp8_gn_param_grads")
     return dx, dgamma, dbeta, dfilm

@@ -276,7 +276,8 @@ def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16
     cfg = UNetConfig(fp8_convs_enabled=fp8, fp8_scaling_type=scaling, attn_resolutions=list(attn_resolutions),
                      p_drop=p_drop, fused_norm=fused_norm,
                      fused_resample=fused_norm if fused_resample is None else fused_resample,
-                     fused_residual=fused_norm if fused_resample is None else fused_resample)
+                     fused_residual=fused_norm if fused_resample is None else fused_resample,
+                     batched_time_embed=fused_norm if fused_resample is None else fused_resample)
     model = UNet(cfg).to(memory_format=torch.channels_last)
     return model.to(device)
 

@@ -58,6 +58,9 @@ class UNetConfig:
     device_scale_history: bool = True
     # the residual joins (skip + h) / sqrt(2) as one pass (fp8_b200.resample.residual_join)
     fused_residual: bool = True
+    # every block's time-embedding projection (all of them read the same embedding)
+    # as one GEMM over the concatenated weights, instead of one small GEMM per block
+    batched_time_embed: bool = True
 
     def as_dict(self):
         return asdict(self)
@@ -174,6 +177,7 @@ class ResidualBlock(nn.Module):
         nn.init.zeros_(self.conv_2.conv.weight)
         self.fused_norm = config.fused_norm
         self.fused_residual = config.fused_residual
+        self._emb = None  # this block's time-embedding projection, when the UNet computed it in a batch
         # dropout mask seed of the fused path (device scalar, advanced every
         # training forward so a captured graph draws a new mask each replay)
         self.register_buffer("dropout_seed", torch.randint(0, 2**62, (), dtype=torch.int64), persistent=False)
@@ -184,7 +188,9 @@ class ResidualBlock(nn.Module):
         return seed
 
     def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
-        emb = self.t_embed_wb(t)
+        emb, self._emb = self._emb, None  # set by the UNet's batched projection
+        if emb is None:
+            emb = self.t_embed_wb(t)
         if self.fused_norm and fused_norm_supported(x, self.norm1):
             h = self.conv_1.forward_normed(x, self.norm1)
             if fused_norm_supported(h, self.norm2) and emb.dtype == torch.bfloat16:
@@ -310,8 +316,18 @@ class UNet(nn.Module):
         self._fp8_delayed_convs = convs if len(convs) <= 64 else None
         return out
 
+    def _batched_time_embeds(self, t_emb: torch.Tensor) -> None:
+        """One GEMM for all blocks' ``t_embed_wb`` projections (same input); each block gets its column slice."""
+        blocks = [m for m in self.modules() if isinstance(m, ResidualBlock)]
+        weights = [b.t_embed_wb.mlp.weight for b in blocks]
+        e = F.linear(t_emb, torch.cat(weights, dim=0))
+        for b, part in zip(blocks, torch.split(e, [w.shape[0] for w in weights], dim=1)):
+            b._emb = part[:, :, None, None]
+
     def _forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
         t_emb = self.time_embed(self._timestep(t))
+        if self.config.batched_time_embed:
+            self._batched_time_embeds(t_emb)
         act = self.conv_in(x)
         skips = []
         fused = self.config.fused_resample

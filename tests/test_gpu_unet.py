@@ -181,3 +181,30 @@ def test_fused_norm_unet_as_accurate_as_torch_ops(cuda):
     g_fused = np.median([rel(grads[0][n], grads[2][n]) for n in names])
     g_torch = np.median([rel(grads[1][n], grads[2][n]) for n in names])
     assert g_fused <= 1.5 * g_torch + 1e-3, (g_fused, g_torch)
+
+
+def test_batched_time_embedding_matches_per_block(cuda):
+    """One GEMM for all blocks' time-embedding projections gives the UNet output and gradients of the
+    per-block projections (max relative error <= 1e-2: the GEMMs' summation order may differ)."""
+    from fp8_b200.train import build_model
+
+    x = (torch.rand(4, 3, 32, 32) * 2 - 1).to(cuda).contiguous(memory_format=torch.channels_last)
+    t = torch.randint(0, 1000, (4,)).to(cuda)
+    res = []
+    for batched in (True, False):
+        m = build_model(fp8=False, device=cuda, seed=0, p_drop=0.0)
+        m.config.batched_time_embed = batched
+        with torch.no_grad():  # the zero-initialised branches would give zero gradients everywhere
+            torch.manual_seed(1)
+            for mod in m.modules():
+                if isinstance(mod, torch.nn.Conv2d) and not mod.weight.any():
+                    torch.nn.init.normal_(mod.weight, std=0.02)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = m(x, t)
+        y.float().square().mean().backward()
+        blk = m.down_stages[0].blocks[0]
+        res.append((y.detach(), blk.t_embed_wb.mlp.weight.grad.clone(), m.time_embed[0].weight.grad.clone()))
+    (ya, wa, ta), (yb, wb, tb) = res
+    # the GEMMs may sum in another order: within bf16 rounding of the projections
+    for u, v in ((ya, yb), (wa, wb), (ta, tb)):
+        assert ((u - v).abs().max() / v.abs().max()).item() <= 1e-2
