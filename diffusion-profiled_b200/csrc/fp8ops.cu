@@ -491,13 +491,17 @@ void choose_kgemm_tile(const KGemmShape& s, int sm_count, int* bm_sub, int* bn) 
     if (*bm_sub == 2 && *bn == 64) *bm_sub = 1;
     return;
   }
+  // The widest column tile that still gives about a wave of tiles (>= 80 % of the
+  // SMs): narrow N = 64 MMAs lose to the per-stage commit bubble, so 128 tiles of
+  // N = 128 beat 256 of N = 64 (8x8 convs at B = 128: 11.4 vs 17.3 us); with
+  // fewer tiles than that at every width, the narrowest (most tiles).
   const int64_t m_tiles = (s.M + 127) / 128;
   *bm_sub = 1;
   for (int cand : {256, 128, 64}) {
     if (s.N % cand != 0 && !(cand == 64 && s.N % 32 == 0)) continue;
     const int64_t tiles = m_tiles * ((s.N + cand - 1) / cand);
     *bn = cand;
-    if (tiles >= sm_count) return;
+    if (tiles * 5 >= static_cast<int64_t>(sm_count) * 4) return;
   }
 }
 
