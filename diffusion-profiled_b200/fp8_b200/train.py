@@ -57,34 +57,45 @@ def diffusion_loss(model: torch.nn.Module, x: torch.Tensor, sched: LinearSchedul
 class BucketedAllReduce:
     """Average gradients across ranks in bf16 buckets, overlapped with backward.
 
-    Buckets are filled in reverse parameter order (roughly the order backward
-    produces gradients).  For each bucket a hook counts the gradients that have
-    been accumulated; the last one launches, on ``comm_stream``, the pack to a
-    flat bf16 buffer (one cat), the all-reduce (NCCL averages in the collective;
-    other backends sum, then scale), and the unpack into the fp32 gradients (one
-    multi-tensor copy).  ``finish()`` makes the current stream wait for the side
-    stream.
+    Buckets first follow the reverse parameter order; the first backward records
+    the order in which gradients actually become ready, and the buckets are then
+    rebuilt in that order (as DDP does), so a bucket does not wait for a gradient
+    that backward produces last (e.g. the time-embedding weights, whose gradients
+    come from one GEMM at the very end).  For each bucket a hook counts the
+    gradients that have been accumulated; the last one launches, on
+    ``comm_stream``, the pack to a flat bf16 buffer (one cat), the all-reduce
+    (NCCL averages in the collective; other backends sum, then scale), and the
+    unpack into the fp32 gradients (one multi-tensor copy).  ``finish()`` makes
+    the current stream wait for the side stream.
     """
 
     def __init__(self, params: list[torch.nn.Parameter], group=None, bucket_bytes: int = 25 << 20):
         self.group = group
         self.world = dist.get_world_size(group)
         self.params = [p for p in params if p.requires_grad]
+        self.bucket_bytes = bucket_bytes
         # CPU tensors (gloo, host-side tests) reduce synchronously, without a side stream.
         self.comm_stream = torch.cuda.Stream(self.params[0].device) if self.params[0].is_cuda else None
+        self.avg_in_collective = dist.get_backend(group) == "nccl"
+        self._build(list(reversed(self.params)))
+        self.order: list[torch.nn.Parameter] | None = []  # readiness order of the first backward
+        self.handles = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
+        self.launched = 0
+
+    def _build(self, ordered: list[torch.nn.Parameter]) -> None:
         self.buckets: list[list[torch.nn.Parameter]] = []
         cur, size = [], 0
-        for p in reversed(self.params):
+        for p in ordered:
             cur.append(p)
             size += p.numel() * 2
-            if size >= bucket_bytes:
+            if size >= self.bucket_bytes:
                 self.buckets.append(cur)
                 cur, size = [], 0
         if cur:
             self.buckets.append(cur)
         self.flat = [torch.empty(sum(p.numel() for p in b), device=b[0].device, dtype=torch.bfloat16)
                      for b in self.buckets]
-        self.pending = [0] * len(self.buckets)
+        self.pending = [len(b) for b in self.buckets]
         self.bucket_of = {}
         for i, b in enumerate(self.buckets):
             for p in b:
@@ -97,9 +108,6 @@ class BucketedAllReduce:
                 vs.append(flat[off:off + p.numel()].view(p.shape))
                 off += p.numel()
             self.views.append(vs)
-        self.avg_in_collective = dist.get_backend(group) == "nccl"
-        self.handles = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
-        self.launched = 0
 
     def bytes_per_step(self) -> int:
         return sum(f.numel() * 2 for f in self.flat)
@@ -109,6 +117,8 @@ class BucketedAllReduce:
         self.launched = 0
 
     def _on_grad(self, p: torch.nn.Parameter) -> None:
+        if self.order is not None:
+            self.order.append(p)
         i = self.bucket_of[p]
         self.pending[i] -= 1
         if self.pending[i] == 0:
@@ -138,6 +148,18 @@ class BucketedAllReduce:
             raise RuntimeError(f"only {self.launched} of {len(self.buckets)} gradient buckets were reduced")
         if self.comm_stream is not None:
             torch.cuda.current_stream(self.flat[0].device).wait_stream(self.comm_stream)
+        if self.order is not None:
+            order, self.order = self.order, None
+            index = {p: i for i, p in enumerate(self.params)}
+            ids = [index[p] for p in order] if len(order) == len(self.params) and len(set(order)) == len(order) \
+                else []
+            box = [ids]
+            dist.broadcast_object_list(box, src=dist.get_global_rank(self.group, 0) if self.group else 0,
+                                       group=self.group)  # every rank buckets in rank 0's order
+            if box[0]:
+                if self.comm_stream is not None:
+                    torch.cuda.current_stream(self.flat[0].device).synchronize()  # old buffers are idle
+                self._build([self.params[i] for i in box[0]])
 
     def remove(self) -> None:
         for h in self.handles:
