@@ -165,4 +165,6 @@ def main(reference_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {Path(__file__).name} <checkout of the reference repository>")
+    main(sys.argv[1])
