@@ -61,6 +61,11 @@ class UNetConfig:
     # every block's time-embedding projection (all of them read the same embedding)
     # as one GEMM over the concatenated weights, instead of one small GEMM per block
     batched_time_embed: bool = True
+    # FP8 also for the 3x3 convs outside SUPPORTED_UNET_SHAPES whose channel counts
+    # the kernels take (multiples of 128; here the 512 -> 256 conv at 4x4), with
+    # delayed scaling on device histories.  Off by default: the reference runs them
+    # in bf16.
+    fp8_extended_shapes: bool = False
 
     def as_dict(self):
         return asdict(self)
@@ -70,9 +75,10 @@ class Conv2dFP8(nn.Module):
     """3x3 / pad 1 conv; FP8 for whitelisted shapes, bf16 ``nn.Conv2d`` otherwise."""
 
     def __init__(self, in_channels: int, out_channels: int, fp8_convs_enabled: bool, scaling_type: str = "current",
-                 amax_history: int | None = None, device_scale_history: bool = True):
+                 amax_history: int | None = None, device_scale_history: bool = True, extended_shapes: bool = False):
         super().__init__()
         self.device_scale_history = device_scale_history
+        self.extended_shapes = extended_shapes
         self._pre_weight = None  # (wq, sw) from a batched weight quantize, for the next forward
         self.used_fp8_delayed = False  # whether the last forward ran the delayed FP8 path
         if scaling_type not in ("current", "delayed"):
@@ -92,7 +98,12 @@ class Conv2dFP8(nn.Module):
 
     def uses_fp8(self, x: torch.Tensor) -> bool:
         key = (x.shape[1], self.conv.weight.shape[0], x.shape[2], x.shape[3])
-        return self.fp8_convs_enabled and key in SUPPORTED_UNET_SHAPES
+        if not self.fp8_convs_enabled:
+            return False
+        if key in SUPPORTED_UNET_SHAPES:
+            return True
+        return (self.extended_shapes and self.scaling_type == "delayed" and self.device_scale_history
+                and key[0] % 128 == 0 and key[1] % 128 == 0)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not self.uses_fp8(x):
@@ -164,7 +175,8 @@ class ResidualBlock(nn.Module):
     def __init__(self, config: UNetConfig, in_chann: int, out_chann: int, p_drop: float = 0.0):
         super().__init__()
         conv = dict(fp8_convs_enabled=config.fp8_convs_enabled, scaling_type=config.fp8_scaling_type,
-                    amax_history=config.fp8_amax_history, device_scale_history=config.device_scale_history)
+                    amax_history=config.fp8_amax_history, device_scale_history=config.device_scale_history,
+                    extended_shapes=config.fp8_extended_shapes)
         self.conv_1 = Conv2dFP8(in_chann, out_chann, **conv)
         self.conv_2 = Conv2dFP8(out_chann, out_chann, **conv)
         self.norm1 = nn.GroupNorm(32, in_chann)

@@ -208,3 +208,31 @@ def test_batched_time_embedding_matches_per_block(cuda):
     # the GEMMs may sum in another order: within bf16 rounding of the projections
     for u, v in ((ya, yb), (wa, wb), (ta, tb)):
         assert ((u - v).abs().max() / v.abs().max()).item() <= 1e-2
+
+
+def test_fp8_extended_shapes_run_the_remaining_convs_in_fp8(cuda):
+    """With fp8_extended_shapes the 512 -> 256 conv at 4x4 (outside SUPPORTED_UNET_SHAPES) runs in FP8 too;
+    the step trains like the default configuration (loss within 2 % after a few steps)."""
+    from fp8_b200.train import build_model
+    from fp8_b200.unet import Conv2dFP8
+
+    x = (torch.rand(8, 3, 32, 32) * 2 - 1).to(cuda).contiguous(memory_format=torch.channels_last)
+    t = torch.randint(0, 1000, (8,)).to(cuda)
+    losses = {}
+    for ext in (False, True):
+        m = build_model(fp8=True, scaling="delayed", device=cuda, seed=0, p_drop=0.0)
+        m.config.fp8_extended_shapes = ext
+        for mod in m.modules():
+            if isinstance(mod, Conv2dFP8):
+                mod.extended_shapes = ext
+        opt = torch.optim.AdamW(m.parameters(), lr=2e-4)
+        for _ in range(4):
+            opt.zero_grad()
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = (m(x, t).float() - x).square().mean()
+            loss.backward()
+            opt.step()
+        fp8_mods = [mod for mod in m.modules() if isinstance(mod, Conv2dFP8) and mod.window_pos.item() > 0]
+        losses[ext] = (loss.item(), len(fp8_mods))
+    assert losses[True][1] > losses[False][1]  # more convs took the FP8 path
+    assert abs(losses[True][0] - losses[False][0]) <= 0.02 * abs(losses[False][0])
