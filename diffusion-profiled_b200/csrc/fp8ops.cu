@@ -29,6 +29,13 @@ using namespace fp8b;
 // Device-side error word (one per device that loads this library).
 __device__ int g_fp8_device_error = 0;
 
+// Tickets of the last-CTA scale folds (ScaleFold), zero between launches.  Each
+// launch that folds gets the next counter of the ring, so launches that can run
+// at the same time (other streams) use different counters unless more than
+// kFoldCounters folding launches were issued between them.
+constexpr int kFoldCounters = 8192;
+__device__ unsigned int g_fold_counters[kFoldCounters];
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -72,6 +79,8 @@ int ok() {
 struct DeviceState {
   int sm_count = 0;
   int* err_ptr = nullptr;
+  unsigned int* fold_base = nullptr;  // g_fold_counters on this device
+  std::atomic<unsigned int> fold_next{0};
   bool init = false;
 };
 DeviceState g_dev[kMaxDevices];
@@ -89,11 +98,18 @@ int device_state(DeviceState** out) {
       void* p = nullptr;
       FP8_CUDA_TRY(cudaGetSymbolAddress(&p, g_fp8_device_error));
       st.err_ptr = static_cast<int*>(p);
+      FP8_CUDA_TRY(cudaGetSymbolAddress(&p, g_fold_counters));
+      st.fold_base = static_cast<unsigned int*>(p);
       st.init = true;
     }
   }
   *out = &st;
   return FP8_OK;
+}
+
+// The counter of the next launch that folds a scale in its last CTA.
+unsigned int* fold_counter(DeviceState* st) {
+  return st->fold_base + st->fold_next.fetch_add(1, std::memory_order_relaxed) % kFoldCounters;
 }
 
 // ------------------------------------------------------------------ TMA tensor maps
@@ -597,13 +613,18 @@ int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, i
 }
 
 int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const float* sa, const float* sb,
-                        void* out, int sm_count, cudaStream_t stream) {
+                        void* out, int sm_count, cudaStream_t stream, bool f32_out = false) {
   const int64_t n4 = count / 4;
   int64_t blocks = (n4 + 255) / 256;
   if (blocks > 4 * sm_count) blocks = 4 * sm_count;
   if (blocks < 1) blocks = 1;
-  FP8_CUDA_TRY(launch_kernel(wgrad_reduce_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, 1,
-                             kStreamingKernel, partials, splits, count, sa, sb, static_cast<__nv_bfloat16*>(out)));
+  if (f32_out)
+    FP8_CUDA_TRY(launch_kernel(wgrad_reduce_kernel<float>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                               1, kStreamingKernel, partials, splits, count, sa, sb, static_cast<float*>(out)));
+  else
+    FP8_CUDA_TRY(launch_kernel(wgrad_reduce_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                               stream, 1, kStreamingKernel, partials, splits, count, sa, sb,
+                               static_cast<__nv_bfloat16*>(out)));
   count_launches(1);
   return FP8_OK;
 }
@@ -634,7 +655,7 @@ size_t gn_workspace(int n, int hw, int c, int sm_count) {
 
 template <typename TX, bool QUANT>
 int launch_gn_fwd(const TX* x, GnShape sh, float* part, const GnActParams& q, float* stats, const GnOut& o,
-                  size_t s1, size_t s2, int sm_count, cudaStream_t cs, int* apply_ctas = nullptr) {
+                  size_t s1, size_t s2, int sm_count, cudaStream_t cs) {
   const bool drop = q.seed != nullptr && q.p > 0.0f;
   auto k1 = gn_stats_kernel<TX>;
   auto k2 = drop ? gn_act_fwd_kernel<TX, QUANT, true> : gn_act_fwd_kernel<TX, QUANT, false>;
@@ -650,7 +671,6 @@ int launch_gn_fwd(const TX* x, GnShape sh, float* part, const GnActParams& q, fl
   sh.slices = sl2;
   FP8_CUDA_TRY(launch_kernel(k2, dim3(static_cast<unsigned>(sh.n * sl2)), block, s2, cs, 1, kStreamingKernel, x, sh,
                              static_cast<const float*>(part), q, stats, o));
-  if (apply_ctas != nullptr) *apply_ctas = sh.n * sl2;
   count_launches(2);
   return FP8_OK;
 }
@@ -714,12 +734,13 @@ int quant_grid(int64_t n, bool vec, int blocks_per_sm, int sm_count) {
 
 template <int KIND>
 int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const float* partials_in, int n_partials,
-                  DelayedSource prev_scale, float* scale_out, float* partials_out, int* err, cudaStream_t cs) {
+                  DelayedSource prev_scale, float* scale_out, float* partials_out, int* err, cudaStream_t cs,
+                  ScaleFold fold = ScaleFold{}) {
   FP8_CUDA_TRY(cudaFuncSetAttribute(quant_stream_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kStreamSmemBytes)));
   FP8_CUDA_TRY(launch_kernel(quant_stream_kernel<KIND>, dim3(grid), dim3(kStreamThreads), kStreamSmemBytes, cs, 1,
                              kStreamingKernel, x, q, n, partials_in, n_partials, prev_scale, scale_out, partials_out,
-                             err));
+                             err, fold));
   return FP8_OK;
 }
 
@@ -739,7 +760,7 @@ int launch_quantize_current(const uint16_t* x, uint8_t* q, float* scale_out, flo
                                partials));
     FP8_CUDA_TRY(launch_kernel(quantize_cast_kernel<kCurrent>, dim3(cast_blocks), dim3(kQuantThreads), 0, cs, 1,
                                kStreamingKernel, x, q, n, static_cast<const float*>(partials), parts, DelayedSource{},
-                               scale_out, static_cast<float*>(nullptr)));
+                               scale_out, static_cast<float*>(nullptr), ScaleFold{}));
   }
   count_launches(2);
   FP8_CUDA_TRY(cudaGetLastError());
@@ -906,18 +927,17 @@ int quantize_delayed_impl(const void* x_bf16, void* q_e4m3, const DelayedSource&
   float* partials = static_cast<float*>(workspace);
   const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
   uint8_t* q = static_cast<uint8_t*>(q_e4m3);
+  const ScaleFold fold{fold_counter(st), scale_curr_out, wu};
   if (vec) {
     if (int s = launch_stream<kStreamCastDelayed>(parts, x, q, n, nullptr, 0, src, nullptr, partials, st->err_ptr,
-                                                  cs))
+                                                  cs, fold))
       return s;
   } else {
     FP8_CUDA_TRY(launch_kernel(quantize_cast_kernel<kDelayed>, dim3(parts), dim3(kQuantThreads), 0, cs, 1,
                                kStreamingKernel, x, q, n, static_cast<const float*>(nullptr), 0, src,
-                               static_cast<float*>(nullptr), partials));
+                               static_cast<float*>(nullptr), partials, fold));
   }
-  FP8_CUDA_TRY(launch_kernel(finalize_scale_kernel, dim3(1), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
-                             static_cast<const float*>(partials), parts, scale_curr_out, wu));
-  count_launches(2);
+  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }
@@ -1074,9 +1094,10 @@ size_t fp8_conv3x3_wgrad_workspace_bytes(int batch, int height, int width, int c
   return static_cast<size_t>(cout) * 9 * cin * sizeof(float);
 }
 
-int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx, const float* sdy, int batch,
-                      int height, int width, int cin, int cout, int split_k, void* workspace,
-                      size_t workspace_bytes, fp8_stream_t stream) {
+namespace {
+int conv3x3_wgrad_impl(const void* xq, const void* dyq, void* dw, bool f32_out, const float* sx, const float* sdy,
+                       int batch, int height, int width, int cin, int cout, int split_k, void* workspace,
+                       size_t workspace_bytes, fp8_stream_t stream) {
   ConvTile t;
   if (int s = check_conv_args(batch, height, width, cin, cout, &t)) return s;
   if (int s = check_scale_ptrs(sx, sdy)) return s;
@@ -1115,9 +1136,25 @@ int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx
   p.err = st->err_ptr;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   if (int s = launch_wgrad(mdy, mx, p, w.group, cs, halo)) return s;
-  if (int s = launch_wgrad_reduce(p.acc, 1, static_cast<int64_t>(cout) * 9 * cin, sx, sdy, dw, st->sm_count, cs))
+  if (int s = launch_wgrad_reduce(p.acc, 1, static_cast<int64_t>(cout) * 9 * cin, sx, sdy, dw, st->sm_count, cs,
+                                  f32_out))
     return s;
   return ok();
+}
+}  // namespace
+
+int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx, const float* sdy, int batch,
+                      int height, int width, int cin, int cout, int split_k, void* workspace,
+                      size_t workspace_bytes, fp8_stream_t stream) {
+  return conv3x3_wgrad_impl(xq, dyq, dw, false, sx, sdy, batch, height, width, cin, cout, split_k, workspace,
+                            workspace_bytes, stream);
+}
+
+int fp8_conv3x3_wgrad_f32(const void* xq, const void* dyq, float* dw, const float* sx, const float* sdy, int batch,
+                          int height, int width, int cin, int cout, int split_k, void* workspace,
+                          size_t workspace_bytes, fp8_stream_t stream) {
+  return conv3x3_wgrad_impl(xq, dyq, dw, true, sx, sdy, batch, height, width, cin, cout, split_k, workspace,
+                            workspace_bytes, stream);
 }
 
 int fp8_gemm(const void* a, const void* b, void* out, const float* sa, const float* sb, const void* bias,
@@ -1265,7 +1302,7 @@ int fp8_gn_act_fwd(const void* x, int x_fp32, const float* gamma, const float* b
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
-  const GnOut o{static_cast<uint16_t*>(out), nullptr, DelayedSource{}, nullptr};
+  const GnOut o{static_cast<uint16_t*>(out), nullptr, DelayedSource{}, nullptr, ScaleFold{}};
   if (x_fp32) {
     if (int s = launch_gn_fwd<float, false>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, st->sm_count,
                                                cs)) return s;
@@ -1308,21 +1345,18 @@ int gn_act_quant_impl(const void* x, int x_fp32, const float* gamma, const float
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   float* amax_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gn_bytes);
-  const GnOut o{nullptr, static_cast<uint8_t*>(q_e4m3), src, amax_part};
-  int apply_ctas = 0;
+  const GnOut o{nullptr, static_cast<uint8_t*>(q_e4m3), src, amax_part,
+                ScaleFold{fold_counter(st), scale_curr_out, wu}};
   const size_t s1 = gn_stats_smem(c), s2 = gn_fwd_smem(c, groups);
   if (x_fp32) {
     if (int s = launch_gn_fwd<float, true>(static_cast<const float*>(x), sh, part, q, stats, o, s1, s2, st->sm_count,
-                                           cs, &apply_ctas))
+                                           cs))
       return s;
   } else {
     if (int s = launch_gn_fwd<uint16_t, true>(static_cast<const uint16_t*>(x), sh, part, q, stats, o, s1, s2,
-                                              st->sm_count, cs, &apply_ctas))
+                                              st->sm_count, cs))
       return s;
   }
-  FP8_CUDA_TRY(launch_kernel(finalize_scale_kernel, dim3(1), dim3(kQuantThreads), 0, cs, 1, kStreamingKernel,
-                             static_cast<const float*>(amax_part), apply_ctas, scale_curr_out, wu));
-  count_launches(1);
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }
@@ -1658,37 +1692,37 @@ int check_resample(const void* p, int dtype, const char* what) {
 }
 
 template <typename TA, typename TS, typename TO>
-int launch_up_cat(const void* a, const void* s, void* y, int n, int h, int w, int c1, int c2, int f, bool bwd,
-                  int sm_count, cudaStream_t cs) {
+int launch_up_cat(const void* a, const void* s, void* y, void* y16, int n, int h, int w, int c1, int c2, int f,
+                  bool bwd, int sm_count, cudaStream_t cs) {
   const int64_t vecs = static_cast<int64_t>(n) * h * w * (c1 + c2) / 8;
   if (!bwd) {
     FP8_CUDA_TRY(launch_kernel(up_cat_kernel<TA, TS, TO>, dim3(resample_grid(vecs, sm_count)), dim3(kResampleThreads),
                                0, cs, 1, kStreamingKernel, static_cast<const TA*>(a), static_cast<const TS*>(s), n, h,
-                               w, c1, c2, f, static_cast<TO*>(y)));
-  } else {  // a, s are the gradients (outputs); y is the incoming gradient
+                               w, c1, c2, f, static_cast<TO*>(y), static_cast<uint16_t*>(y16)));
+  } else {  // a, s are the gradients (outputs); y (and y16) the incoming gradients
     FP8_CUDA_TRY(launch_kernel(up_cat_bwd_kernel<TA, TS, TO>, dim3(resample_grid(vecs, sm_count)),
-                               dim3(kResampleThreads), 0, cs, 1, kStreamingKernel, static_cast<const TO*>(y), n, h, w,
-                               c1, c2, f, static_cast<TA*>(const_cast<void*>(a)),
-                               static_cast<TS*>(const_cast<void*>(s))));
+                               dim3(kResampleThreads), 0, cs, 1, kStreamingKernel, static_cast<const TO*>(y),
+                               static_cast<const uint16_t*>(y16), n, h, w, c1, c2, f,
+                               static_cast<TA*>(const_cast<void*>(a)), static_cast<TS*>(const_cast<void*>(s))));
   }
   count_launches(1);
   return FP8_OK;
 }
 
 template <typename TA, typename TS>
-int up_cat_out(int y_dtype, const void* a, const void* s, void* y, int n, int h, int w, int c1, int c2, int f,
-               bool bwd, int sms, cudaStream_t cs) {
-  return y_dtype ? launch_up_cat<TA, TS, float>(a, s, y, n, h, w, c1, c2, f, bwd, sms, cs)
-                 : launch_up_cat<TA, TS, uint16_t>(a, s, y, n, h, w, c1, c2, f, bwd, sms, cs);
+int up_cat_out(int y_dtype, const void* a, const void* s, void* y, void* y16, int n, int h, int w, int c1, int c2,
+               int f, bool bwd, int sms, cudaStream_t cs) {
+  return y_dtype ? launch_up_cat<TA, TS, float>(a, s, y, y16, n, h, w, c1, c2, f, bwd, sms, cs)
+                 : launch_up_cat<TA, TS, uint16_t>(a, s, y, y16, n, h, w, c1, c2, f, bwd, sms, cs);
 }
 
-int up_cat_dispatch(int a_dtype, int s_dtype, int y_dtype, const void* a, const void* s, void* y, int n, int h, int w,
-                    int c1, int c2, int f, bool bwd, int sms, cudaStream_t cs) {
+int up_cat_dispatch(int a_dtype, int s_dtype, int y_dtype, const void* a, const void* s, void* y, void* y16, int n,
+                    int h, int w, int c1, int c2, int f, bool bwd, int sms, cudaStream_t cs) {
   if (a_dtype)
-    return s_dtype ? up_cat_out<float, float>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs)
-                   : up_cat_out<float, uint16_t>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs);
-  return s_dtype ? up_cat_out<uint16_t, float>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs)
-                 : up_cat_out<uint16_t, uint16_t>(y_dtype, a, s, y, n, h, w, c1, c2, f, bwd, sms, cs);
+    return s_dtype ? up_cat_out<float, float>(y_dtype, a, s, y, y16, n, h, w, c1, c2, f, bwd, sms, cs)
+                   : up_cat_out<float, uint16_t>(y_dtype, a, s, y, y16, n, h, w, c1, c2, f, bwd, sms, cs);
+  return s_dtype ? up_cat_out<uint16_t, float>(y_dtype, a, s, y, y16, n, h, w, c1, c2, f, bwd, sms, cs)
+                 : up_cat_out<uint16_t, uint16_t>(y_dtype, a, s, y, y16, n, h, w, c1, c2, f, bwd, sms, cs);
 }
 
 int check_up_cat(int n, int h, int w, int c1, int c2, int factor) {
@@ -1750,8 +1784,8 @@ int fp8_up_cat(const void* a, int a_dtype, const void* s, int s_dtype, void* y, 
   if (int r = check_resample(y, y_dtype, "y")) return r;
   DeviceState* st;
   if (int r = device_state(&st)) return r;
-  if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, a, s, y, n, h, w, c1, c2, factor, false, st->sm_count,
-                              reinterpret_cast<cudaStream_t>(stream)))
+  if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, a, s, y, nullptr, n, h, w, c1, c2, factor, false,
+                              st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
     return r;
   return ok();
 }
@@ -1764,8 +1798,38 @@ int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds,
   if (int r = check_resample(ds, s_dtype, "ds")) return r;
   DeviceState* st;
   if (int r = device_state(&st)) return r;
-  if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, da, ds, const_cast<void*>(dy), n, h, w, c1, c2, factor, true,
-                              st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+  if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, da, ds, const_cast<void*>(dy), nullptr, n, h, w, c1, c2,
+                              factor, true, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
+    return r;
+  return ok();
+}
+
+int fp8_up_cat_pair(const void* a, int a_dtype, const void* s, int s_dtype, float* y, void* y_bf16, int n, int h,
+                    int w, int c1, int c2, int factor, fp8_stream_t stream) {
+  if (int r = check_up_cat(n, h, w, c1, c2, factor)) return r;
+  if (int r = check_resample(a, a_dtype, "a")) return r;
+  if (int r = check_resample(s, s_dtype, "s")) return r;
+  if (int r = check_resample(y, 1, "y")) return r;
+  if (int r = check_resample(y_bf16, 0, "y_bf16")) return r;
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  if (int r = up_cat_dispatch(a_dtype, s_dtype, 1, a, s, y, y_bf16, n, h, w, c1, c2, factor, false, st->sm_count,
+                              reinterpret_cast<cudaStream_t>(stream)))
+    return r;
+  return ok();
+}
+
+int fp8_up_cat_pair_bwd(const float* dy, const void* dy_bf16, void* da, int a_dtype, void* ds, int s_dtype, int n,
+                        int h, int w, int c1, int c2, int factor, fp8_stream_t stream) {
+  if (int r = check_up_cat(n, h, w, c1, c2, factor)) return r;
+  if (int r = check_resample(dy, 1, "dy")) return r;
+  if (int r = check_resample(dy_bf16, 0, "dy_bf16")) return r;
+  if (int r = check_resample(da, a_dtype, "da")) return r;
+  if (int r = check_resample(ds, s_dtype, "ds")) return r;
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  if (int r = up_cat_dispatch(a_dtype, s_dtype, 1, da, ds, const_cast<float*>(dy), const_cast<void*>(dy_bf16), n, h,
+                              w, c1, c2, factor, true, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
     return r;
   return ok();
 }

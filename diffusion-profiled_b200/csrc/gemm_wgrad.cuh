@@ -265,10 +265,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // dW[i] = bf16( (sum_s partials[s][i]) * sx * sdy ), i over rows*cols (multiple of 4):
 // the reference's reduce (fp8_kernels.py:463-468) — sum the splits, then scale.
 // With the in-L2 split reduction there is one "split" (the accumulator).
+// OutT = float stores the same bf16 values widened to fp32: the gradient an fp32
+// weight receives when autograd casts the bf16 gradient to the weight's dtype.
+template <typename OutT>
 __global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restrict__ partials, int splits,
                                                            int64_t count, const float* __restrict__ sa,
-                                                           const float* __restrict__ sb,
-                                                           __nv_bfloat16* __restrict__ out) {
+                                                           const float* __restrict__ sb, OutT* __restrict__ out) {
   pdl_wait();
   const float scale = __ldg(sa) * __ldg(sb);
   const int64_t n4 = count >> 2;
@@ -286,7 +288,13 @@ __global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restri
     uint2 o;
     o.x = pack_bf16x2(acc.x * scale, acc.y * scale);
     o.y = pack_bf16x2(acc.z * scale, acc.w * scale);
-    reinterpret_cast<uint2*>(out)[i] = o;
+    if constexpr (sizeof(OutT) == 2) {
+      reinterpret_cast<uint2*>(out)[i] = o;
+    } else {  // fp32 holding the bf16 values (exact widening)
+      reinterpret_cast<float4*>(out)[i] =
+          make_float4(__uint_as_float(o.x << 16), __uint_as_float(o.x & 0xFFFF0000u), __uint_as_float(o.y << 16),
+                      __uint_as_float(o.y & 0xFFFF0000u));
+    }
   }
 }
 

@@ -337,6 +337,7 @@ struct GnOut {
   uint8_t* q;               // NHWC e4m3 (QUANT = true)
   DelayedSource prev_scale;  // the scale of the cast (QUANT = true)
   float* amax_part;         // [grid] per-CTA max |activation| (QUANT = true)
+  ScaleFold fold;           // the last CTA folds amax_part into the current scale (QUANT = true)
 };
 
 // Plain bf16 stores: the Div of the non-quantizing instantiation.
@@ -432,6 +433,7 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_FWD) gn_act_fwd_kernel
   if constexpr (QUANT) {
     const float m = block_max<kGnThreads>(unpack_max2(m2));
     if (threadIdx.x == 0) o.amax_part[blockIdx.x] = m;
+    fold_scale_if_last<kGnThreads>(o.amax_part, o.fold);
   }
 }
 

@@ -15,9 +15,10 @@
 //   cast pass : every CTA folds the partials into amax and the scale (the
 //               reference's separate finalize launch disappears), CTA 0
 //               publishes the scale, then casts.
-// Delayed scaling (quantize_fp8_delayed, :518-556) is one pass plus a 1-CTA fold:
-//   cast pass             : cast with the previous scale and emit amax partials
-//   finalize_scale_kernel : partials -> current scale
+// Delayed scaling (quantize_fp8_delayed, :518-556) is one pass:
+//   cast pass : cast with the previous scale, one amax partial per CTA; the
+//               last CTA to finish folds the partials into the current scale
+//               (fold_scale_if_last)
 // Each pass exists twice: quant_stream_kernel (bulk copies through shared
 // memory; 16-byte aligned x, 8-byte aligned q) and the scalar grid-stride
 // amax_partials_kernel / quantize_cast_kernel for any other alignment.
@@ -173,7 +174,7 @@ struct DelayedSource {
 
 // The history update after a delayed cast: window[*pos] = this tensor's scale,
 // then (advance) *pos = (*pos + 1) % len -- the scatter and the position step of
-// the reference module (unet.py:80-91), done by the one-CTA finalize kernel.
+// the reference module (unet.py:80-91), done by the CTA that folds the scale.
 struct WindowUpdate {
   float* window;
   int64_t* pos;
@@ -222,6 +223,47 @@ __device__ __forceinline__ uint2 cast_vec(const uint4& a, const Div& d) {
   return make_uint2(cast4(a.x, a.y, d), cast4(a.z, a.w, d));
 }
 
+// The tensor's own scale, folded by the last CTA of the launch that wrote the
+// partial maxima (no separate one-CTA launch).  Every CTA stores its partial,
+// fences, and takes a ticket from `counter`; the CTA with the last ticket sees
+// every partial (each was fenced before its ticket), folds them into the scale,
+// stores it to *scale_out and into the history (`wu`), and sets the counter back
+// to zero for the next launch that is given it.  No CTA waits for another.
+struct ScaleFold {
+  unsigned int* counter;  // zero when the launch starts; zero again when it ends
+  float* scale_out;       // may be null
+  WindowUpdate wu;        // window == null: no history update
+};
+
+__device__ __forceinline__ void store_scale(float s, float* scale_out, const WindowUpdate& wu) {
+  if (scale_out != nullptr) *scale_out = s;
+  if (wu.window != nullptr) {
+    const int64_t p = *wu.pos;
+    wu.window[p] = s;
+    if (wu.advance) *wu.pos = (p + 1) % wu.len;
+  }
+}
+
+// Every thread of every CTA, after thread 0 stored partials[blockIdx.x].
+template <int NT>
+__device__ __forceinline__ void fold_scale_if_last(const float* partials, const ScaleFold& f) {
+  __shared__ unsigned int ticket;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    ticket = atomicAdd(f.counter, 1u);
+  }
+  __syncthreads();
+  if (ticket != gridDim.x - 1) return;  // uniform over the CTA
+  __threadfence();
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += NT) m = fmaxf(m, __ldcg(partials + i));
+  const float s = scale_from_amax(block_max<NT>(m));
+  if (threadIdx.x == 0) {
+    store_scale(s, f.scale_out, f.wu);
+    *f.counter = 0u;
+  }
+}
+
 // ---------------------------------------------------------------- scalar passes
 // Grid-stride, one element per thread and step: the path for x that is not
 // 16-byte aligned or q that is not 8-byte aligned (views with an odd offset).
@@ -259,7 +301,8 @@ __device__ __forceinline__ float cast_loop(const uint16_t* __restrict__ x, uint8
 template <int MODE>
 __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
-    int n_partials, DelayedSource prev_scale, float* __restrict__ scale_out, float* __restrict__ partials_out) {
+    int n_partials, DelayedSource prev_scale, float* __restrict__ scale_out, float* __restrict__ partials_out,
+    ScaleFold fold) {
   pdl_wait();
   float s;
   if (MODE == kCurrent) {
@@ -274,21 +317,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_cast_kernel(
   if (MODE == kDelayed) {
     const float bm = block_max(m);
     if (threadIdx.x == 0) partials_out[blockIdx.x] = bm;
-  }
-}
-
-__global__ void __launch_bounds__(kQuantThreads) finalize_scale_kernel(const float* __restrict__ partials,
-                                                                       int n_partials, float* __restrict__ scale_out,
-                                                                       WindowUpdate wu) {
-  pdl_wait();
-  const float s = fold_partials_to_scale(partials, n_partials);
-  if (threadIdx.x == 0) {
-    if (scale_out != nullptr) *scale_out = s;
-    if (wu.window != nullptr) {
-      const int64_t p = *wu.pos;
-      wu.window[p] = s;
-      if (wu.advance) *wu.pos = (p + 1) % wu.len;
-    }
+    if (fold.counter != nullptr) fold_scale_if_last<kQuantThreads>(partials_out, fold);
   }
 }
 
@@ -303,7 +332,8 @@ __global__ void __launch_bounds__(kQuantThreads) finalize_scale_kernel(const flo
 // CTA 0 also handles the n % 8 tail elements with plain loads.
 //   kStreamAmax        : |x| max per CTA                         -> partials_out
 //   kStreamCastCurrent : scale = fold(partials_in), cast; CTA 0 -> scale_out
-//   kStreamCastDelayed : cast with *prev_scale, |x| max per CTA  -> partials_out
+//   kStreamCastDelayed : cast with *prev_scale, |x| max per CTA  -> partials_out,
+//                        folded into the current scale by the last CTA
 enum StreamKind : int { kStreamAmax = 0, kStreamCastCurrent = 1, kStreamCastDelayed = 2 };
 
 #ifndef FP8_STREAM_CHUNK_BYTES
@@ -433,7 +463,7 @@ template <int KIND>
 __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
     int n_partials, DelayedSource prev_scale, float* __restrict__ scale_out, float* __restrict__ partials_out,
-    int* err) {
+    int* err, ScaleFold fold) {
   extern __shared__ __align__(128) uint8_t stream_smem[];
   pdl_wait();
   uint8_t* bufs = stream_smem;
@@ -464,6 +494,7 @@ __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
   if (KIND != kStreamCastCurrent) {
     const float bm = block_max<kStreamThreads>(m);
     if (threadIdx.x == 0) partials_out[blockIdx.x] = bm;
+    if (KIND == kStreamCastDelayed && fold.counter != nullptr) fold_scale_if_last<kStreamThreads>(partials_out, fold);
   }
 }
 

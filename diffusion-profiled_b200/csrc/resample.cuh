@@ -10,6 +10,8 @@
 //                y[n, h, w, C1:C1+C2]  = s[n, h, w, :]
 //   up_cat bwd : da[n, h, w, c] = sum over the f x f block of dy[.., c]  (fp32 sum, rounded to a's dtype)
 //                ds[n, h, w, c] = dy[n, h, w, C1 + c]                    (in s's dtype)
+//   pair       : up_cat with y fp32 and also y16 = bf16(y); its backward takes
+//                dy + dy16 (fp32 sum) as the gradient of y
 //
 // One kernel per direction: the autocast casts, the separate resampling pass
 // and the concatenation copy become one read and one write of each element.
@@ -75,10 +77,12 @@ __global__ void __launch_bounds__(kResampleThreads) down2_bwd_kernel(const float
 }
 
 // y has C1 + C2 channels at (h, w); a is (h / f, w / f) with C1 channels; s is (h, w) with C2.
+// y16 (may be null): a second output, bf16(y) -- the copy bf16 autocast makes of
+// an fp32 y for the 1x1 skip conv that reads it -- written in the same pass.
 template <typename TA, typename TS, typename TO>
 __global__ void __launch_bounds__(kResampleThreads) up_cat_kernel(const TA* __restrict__ a, const TS* __restrict__ s,
                                                                   int n, int h, int w, int c1, int c2, int f,
-                                                                  TO* __restrict__ y) {
+                                                                  TO* __restrict__ y, uint16_t* __restrict__ y16) {
   pdl_wait();
   const int v1 = c1 / 8, vecs = (c1 + c2) / 8;
   const int ha = h / f, wa = w / f;
@@ -98,13 +102,29 @@ __global__ void __launch_bounds__(kResampleThreads) up_cat_kernel(const TA* __re
       load8f(s, pix * (vecs - v1) + (v - v1), e);
     }
     store_x8(y, i, e);
+    if (y16 != nullptr) store_x8(y16, i, e);
+  }
+}
+
+// dy16 (may be null): the gradient of the y16 output, added to dy in fp32 first
+// (the sum autograd forms for a tensor read twice), element by element.
+template <typename TO>
+__device__ __forceinline__ void load_dy8(const TO* __restrict__ dy, const uint16_t* __restrict__ dy16, int64_t vi,
+                                         float (&e)[8]) {
+  load8f(dy, vi, e);
+  if (dy16 != nullptr) {
+    float g[8];
+    load8f(dy16, vi, g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) e[k] += g[k];
   }
 }
 
 template <typename TA, typename TS, typename TO>
-__global__ void __launch_bounds__(kResampleThreads) up_cat_bwd_kernel(const TO* __restrict__ dy, int n, int h, int w,
-                                                                      int c1, int c2, int f, TA* __restrict__ da,
-                                                                      TS* __restrict__ ds) {
+__global__ void __launch_bounds__(kResampleThreads) up_cat_bwd_kernel(const TO* __restrict__ dy,
+                                                                      const uint16_t* __restrict__ dy16, int n, int h,
+                                                                      int w, int c1, int c2, int f,
+                                                                      TA* __restrict__ da, TS* __restrict__ ds) {
   pdl_wait();
   const int v1 = c1 / 8, v2 = c2 / 8, vecs = v1 + v2;
   const int ha = h / f, wa = w / f;
@@ -123,7 +143,7 @@ __global__ void __launch_bounds__(kResampleThreads) up_cat_bwd_kernel(const TO* 
       for (int di = 0; di < f; ++di)
         for (int dj = 0; dj < f; ++dj) {
           float e[8];
-          load8f(dy, ((img * h + hq * f + di) * w + wq * f + dj) * vecs + v, e);
+          load_dy8(dy, dy16, ((img * h + hq * f + di) * w + wq * f + dj) * vecs + v, e);
 #pragma unroll
           for (int k = 0; k < 8; ++k) acc[k] += e[k];
         }
@@ -133,7 +153,7 @@ __global__ void __launch_bounds__(kResampleThreads) up_cat_bwd_kernel(const TO* 
       const int v = static_cast<int>(j % v2);
       const int64_t pix = j / v2;
       float e[8];
-      load8f(dy, pix * vecs + v1 + v, e);
+      load_dy8(dy, dy16, pix * vecs + v1 + v, e);
       store_x8(ds, j, e);
     }
   }

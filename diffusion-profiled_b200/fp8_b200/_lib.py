@@ -61,6 +61,11 @@ _SIGNATURES: dict[str, tuple] = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
          c_size_t, c_void_p],
     ),
+    "fp8_conv3x3_wgrad_f32": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+         c_size_t, c_void_p],
+    ),
     "fp8_gemm": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p],
@@ -97,6 +102,14 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_up_cat_bwd": (
         c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                 c_void_p]),
+    "fp8_up_cat_pair": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p],
+    ),
+    "fp8_up_cat_pair_bwd": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p],
+    ),
     "fp8_quantize_delayed_window": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_int64,
                 c_void_p]),

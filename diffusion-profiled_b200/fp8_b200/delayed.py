@@ -30,7 +30,9 @@ def _conv_backward(ctx, dy, xq, wq, sx, sw):
     dy = dy.to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
     # the dY scale lands at the position the forward already advanced (fp8_kernels.py:883-889)
     dyq, sdy = ops.quantize_delayed_window(dy, ctx.win_dy, ctx.pos, False)
-    return ops.conv3x3_dgrad(dyq, wq, sdy, sw), ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+    # an fp32 weight gets the bf16 dW widened by the reduce pass, not by an autograd cast
+    widen = ctx.w_dtype == torch.float32
+    return ops.conv3x3_dgrad(dyq, wq, sdy, sw), ops.conv3x3_wgrad(xq, dyq, sx, sdy, 0, widen)
 
 
 def _weight_q(weight, win_w, pos, pre):
@@ -51,7 +53,7 @@ class ConvFP8Delayed(torch.autograd.Function):
         wq, sw = _weight_q(weight, win_w, pos, pre)
         xq, sx = ops.quantize_delayed_window(x, win_x, pos, True)
         ctx.save_for_backward(xq, wq, sx, sw)
-        ctx.win_dy, ctx.pos = win_dy, pos
+        ctx.win_dy, ctx.pos, ctx.w_dtype = win_dy, pos, weight.dtype
         return ops.conv3x3_fwd(xq, wq, sx, sw)
 
     @staticmethod
@@ -73,7 +75,7 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
         wq, sw = _weight_q(weight, win_w, pos, pre)
         xq, sx, stats = ops.gn_act_quant_fwd_window(x, gamma, beta, film2, seed, win_x, pos, True, p, eps, groups)
         ctx.save_for_backward(x, gamma, beta, film2, seed, stats, xq, wq, sx, sw)
-        ctx.win_dy, ctx.pos = win_dy, pos
+        ctx.win_dy, ctx.pos, ctx.w_dtype = win_dy, pos, weight.dtype
         ctx.cfg = (p, eps, groups, None if film is None else film.shape)
         return ops.conv3x3_fwd(xq, wq, sx, sw)
 

@@ -331,9 +331,13 @@ def _(dyq, wq, sdy, sw):
 
 @torch.library.custom_op("fp8_b200::conv3x3_wgrad", mutates_args=())
 def conv3x3_wgrad(
-    xq: torch.Tensor, dyq: torch.Tensor, sx: torch.Tensor, sdy: torch.Tensor, split_k: int = 0
+    xq: torch.Tensor, dyq: torch.Tensor, sx: torch.Tensor, sdy: torch.Tensor, split_k: int = 0, widen: bool = False
 ) -> torch.Tensor:
-    """bf16 channels_last weight gradient [Cout, Cin, 3, 3] (fp8_kernels.py:723-808)."""
+    """bf16 channels_last weight gradient [Cout, Cin, 3, 3] (fp8_kernels.py:723-808).
+
+    ``widen=True``: the same bf16 values stored as fp32, which is what an fp32 weight's
+    gradient becomes when autograd casts the bf16 result (fp8_kernels.py:875-913) to the
+    weight's dtype -- written by the reduce pass itself, with no cast launch."""
     dev = _require_cuda(xq, dyq)
     _check_conv_operand(xq, "x")
     _check_conv_operand(dyq, "dy")
@@ -343,25 +347,28 @@ def conv3x3_wgrad(
     cout = dyq.shape[1]
     if (dyq.shape[0], dyq.shape[2], dyq.shape[3]) != (b, h, w):
         raise RuntimeError("x and dy batch/spatial dims differ")
-    dw = torch.empty((cout, cin, 3, 3), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    dt = torch.float32 if widen else torch.bfloat16
+    dw = torch.empty((cout, cin, 3, 3), device=dev, dtype=dt, memory_format=torch.channels_last)
     lib = _lib.load()
+    fn = "fp8_conv3x3_wgrad_f32" if widen else "fp8_conv3x3_wgrad"
     with torch.cuda.device(dev):
         ws_bytes = lib.fp8_conv3x3_wgrad_workspace_bytes(b, h, w, cin, cout, split_k)
         ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
         _lib.check(
-            lib.fp8_conv3x3_wgrad(
+            getattr(lib, fn)(
                 _ptr(xq), _ptr(dyq), _ptr(dw), _ptr(sx), _ptr(sdy), b, h, w, cin, cout, split_k, _ptr(ws),
                 ws.numel() * 4, _stream(dev),
             ),
-            "fp8_conv3x3_wgrad",
+            fn,
         )
     return dw
 
 
 @conv3x3_wgrad.register_fake
-def _(xq, dyq, sx, sdy, split_k=0):
+def _(xq, dyq, sx, sdy, split_k=0, widen=False):
     return torch.empty(
-        (dyq.shape[1], xq.shape[1], 3, 3), device=xq.device, dtype=torch.bfloat16, memory_format=torch.channels_last
+        (dyq.shape[1], xq.shape[1], 3, 3), device=xq.device, dtype=torch.float32 if widen else torch.bfloat16,
+        memory_format=torch.channels_last
     )
 
 
@@ -657,6 +664,65 @@ def up_cat_bwd(dy: torch.Tensor, c1: int, factor: int, a_fp32: bool,
 
 @up_cat_bwd.register_fake
 def _(dy, c1, factor, a_fp32, s_fp32):
+    n, c, h, w = dy.shape
+    ta = torch.float32 if a_fp32 else torch.bfloat16
+    ts = torch.float32 if s_fp32 else torch.bfloat16
+    cl = torch.channels_last
+    return (dy.new_empty((n, c1, h // factor, w // factor), dtype=ta).contiguous(memory_format=cl),
+            dy.new_empty((n, c - c1, h, w), dtype=ts).contiguous(memory_format=cl))
+
+
+@torch.library.custom_op("fp8_b200::up_cat_pair", mutates_args=())
+def up_cat_pair(a: torch.Tensor, s: torch.Tensor, factor: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(y, bf16(y)) for the fp32 y of up_cat: the concatenation and the copy bf16 autocast
+    makes of it for the next block's 1x1 skip conv (unet.py:139, 161), in one pass."""
+    dev = _require_cuda(a, s)
+    _resample_check(a, "a")
+    _resample_check(s, "s")
+    n, c1, ha, wa = a.shape
+    c2, h, w = s.shape[1], s.shape[2], s.shape[3]
+    if (s.shape[0], h, w) != (n, ha * factor, wa * factor):
+        raise RuntimeError("a upsampled by factor must match s in batch and spatial size")
+    y = torch.empty((n, c1 + c2, h, w), device=dev, dtype=torch.float32, memory_format=torch.channels_last)
+    y16 = torch.empty((n, c1 + c2, h, w), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_up_cat_pair", _ptr(a), _DT[a.dtype], _ptr(s), _DT[s.dtype], _ptr(y), _ptr(y16), n, h, w, c1,
+                  c2, factor, _stream(dev))
+    return y, y16
+
+
+@up_cat_pair.register_fake
+def _(a, s, factor):
+    shape = (a.shape[0], a.shape[1] + s.shape[1], s.shape[2], s.shape[3])
+    cl = torch.channels_last
+    return (a.new_empty(shape, dtype=torch.float32).contiguous(memory_format=cl),
+            a.new_empty(shape, dtype=torch.bfloat16).contiguous(memory_format=cl))
+
+
+@torch.library.custom_op("fp8_b200::up_cat_pair_bwd", mutates_args=())
+def up_cat_pair_bwd(dy: torch.Tensor, dy16: torch.Tensor, c1: int, factor: int, a_fp32: bool,
+                    s_fp32: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gradients of up_cat_pair: up_cat_bwd of dy + dy16 (summed in fp32, as autograd sums them)."""
+    dev = _require_cuda(dy, dy16)
+    dy = dy.contiguous(memory_format=torch.channels_last)
+    dy16 = dy16.contiguous(memory_format=torch.channels_last)
+    _resample_check(dy, "dy")
+    _resample_check(dy16, "dy16")
+    if dy.dtype != torch.float32 or dy16.dtype != torch.bfloat16 or dy.shape != dy16.shape:
+        raise RuntimeError("dy must be float32 and dy16 bfloat16 of one shape")
+    n, c, h, w = dy.shape
+    ta = torch.float32 if a_fp32 else torch.bfloat16
+    ts = torch.float32 if s_fp32 else torch.bfloat16
+    da = torch.empty((n, c1, h // factor, w // factor), device=dev, dtype=ta, memory_format=torch.channels_last)
+    ds = torch.empty((n, c - c1, h, w), device=dev, dtype=ts, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_up_cat_pair_bwd", _ptr(dy), _ptr(dy16), _ptr(da), _DT[ta], _ptr(ds), _DT[ts], n, h, w, c1,
+                  c - c1, factor, _stream(dev))
+    return da, ds
+
+
+@up_cat_pair_bwd.register_fake
+def _(dy, dy16, c1, factor, a_fp32, s_fp32):
     n, c, h, w = dy.shape
     ta = torch.float32 if a_fp32 else torch.bfloat16
     ts = torch.float32 if s_fp32 else torch.bfloat16

@@ -49,6 +49,19 @@ class _UpCat(torch.autograd.Function):
         return da, ds, None, None
 
 
+class _UpCatPair(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, s, factor: int):
+        ctx.cfg = (a.shape[1], factor, a.dtype == torch.float32, s.dtype == torch.float32)
+        return ops.up_cat_pair(a, s, factor)
+
+    @staticmethod
+    def backward(ctx, dy, dy16):
+        c1, factor, a_fp32, s_fp32 = ctx.cfg
+        da, ds = ops.up_cat_pair_bwd(dy, dy16, c1, factor, a_fp32, s_fp32)
+        return da, ds, None
+
+
 def resample_supported(*ts: torch.Tensor) -> bool:
     return all(t.is_cuda and t.dim() == 4 and t.dtype in (torch.bfloat16, torch.float32) and t.shape[1] % 8 == 0
                and t.is_contiguous(memory_format=torch.channels_last) for t in ts)
@@ -70,6 +83,17 @@ def upsample_cat(a: torch.Tensor, s: torch.Tensor, factor: int) -> torch.Tensor:
         return torch.cat([up, s], dim=1)
     up_fp32 = a.dtype == torch.float32 or (factor > 1 and autocast)
     return _UpCat.apply(a, s, factor, up_fp32 or s.dtype == torch.float32)
+
+
+def upsample_cat_pair(a: torch.Tensor, s: torch.Tensor, factor: int) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """``(y, y.to(torch.bfloat16))`` for ``y = upsample_cat(a, s, factor)`` when y is fp32 (bf16
+    autocast), both from one pass; ``(y, None)`` otherwise.  The bf16 copy is what autocast gives
+    the 1x1 skip conv of the block that reads y (unet.py:139, 161)."""
+    autocast = torch.is_autocast_enabled("cuda")
+    if resample_supported(a, s) and factor in (1, 2) and autocast:
+        if a.dtype == torch.float32 or s.dtype == torch.float32 or factor > 1:
+            return _UpCatPair.apply(a, s, factor)
+    return upsample_cat(a, s, factor), None
 
 
 class _AddScale(torch.autograd.Function):
@@ -100,4 +124,4 @@ def residual_join(a: torch.Tensor, b: torch.Tensor, divisor: float = math.sqrt(2
     return _AddScale.apply(a, b, inv)
 
 
-__all__ = ["downsample_nearest", "upsample_cat", "resample_supported", "residual_join"]
+__all__ = ["downsample_nearest", "upsample_cat", "upsample_cat_pair", "resample_supported", "residual_join"]

@@ -295,11 +295,10 @@ def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16
     """The reference UNet; ``fused_norm`` / ``fused_resample`` (default: as ``fused_norm``) route its
     norm -> activation chains and its resampling + concatenation to this library's kernels."""
     torch.manual_seed(seed)
+    fr = fused_norm if fused_resample is None else fused_resample
     cfg = UNetConfig(fp8_convs_enabled=fp8, fp8_scaling_type=scaling, attn_resolutions=list(attn_resolutions),
-                     p_drop=p_drop, fused_norm=fused_norm,
-                     fused_resample=fused_norm if fused_resample is None else fused_resample,
-                     fused_residual=fused_norm if fused_resample is None else fused_resample,
-                     batched_time_embed=fused_norm if fused_resample is None else fused_resample)
+                     p_drop=p_drop, fused_norm=fused_norm, fused_resample=fr, fused_residual=fr,
+                     batched_time_embed=fr, fused_skip_cast=fr)
     model = UNet(cfg).to(memory_format=torch.channels_last)
     return model.to(device)
 

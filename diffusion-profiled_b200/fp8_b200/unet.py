@@ -29,7 +29,7 @@ import torch.nn.functional as F
 
 from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed, quantize_conv_weights
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
-from .resample import downsample_nearest, residual_join, upsample_cat
+from .resample import downsample_nearest, residual_join, upsample_cat, upsample_cat_pair
 from .norm import GroupNormActConvFP8, fused_layer_norm_supported, fused_norm_supported, group_norm_act, layer_norm_bf16
 
 
@@ -66,6 +66,10 @@ class UNetConfig:
     # delayed scaling on device histories.  Off by default: the reference runs them
     # in bf16.
     fp8_extended_shapes: bool = False
+    # an up stage's fp32 input (upsample + skip concatenation) and the bf16 copy autocast
+    # makes of it for the first block's 1x1 skip conv, written by one pass; their two
+    # gradients summed by the backward of that pass (needs fused_resample)
+    fused_skip_cast: bool = True
 
     def as_dict(self):
         return asdict(self)
@@ -190,6 +194,7 @@ class ResidualBlock(nn.Module):
         self.fused_norm = config.fused_norm
         self.fused_residual = config.fused_residual
         self._emb = None  # this block's time-embedding projection, when the UNet computed it in a batch
+        self._skip_in = None  # bf16 copy of the input for the 1x1 skip conv, when the UNet made one
         # dropout mask seed of the fused path (device scalar, advanced every
         # training forward so a captured graph draws a new mask each replay)
         self.register_buffer("dropout_seed", torch.randint(0, 2**62, (), dtype=torch.int64), persistent=False)
@@ -217,9 +222,11 @@ class ResidualBlock(nn.Module):
         return self._join(x, h)
 
     def _join(self, x: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+        skip_in, self._skip_in = self._skip_in, None
+        skip = self.skip_connection(x if skip_in is None else skip_in)
         if self.fused_residual:
-            return residual_join(self.skip_connection(x), h)
-        return (self.skip_connection(x) + h) / math.sqrt(2.0)
+            return residual_join(skip, h)
+        return (skip + h) / math.sqrt(2.0)
 
 
 class CHWAttention(nn.Module):
@@ -352,7 +359,12 @@ class UNet(nn.Module):
         for i, stage in enumerate(self.up_stages):
             h = skips.pop()
             if fused:
-                act = stage(upsample_cat(act, h, 2 if i > 0 else 1), t_emb)
+                blk = stage.blocks[0]
+                if self.config.fused_skip_cast and isinstance(blk.skip_connection, nn.Conv2d):
+                    y, blk._skip_in = upsample_cat_pair(act, h, 2 if i > 0 else 1)
+                else:
+                    y = upsample_cat(act, h, 2 if i > 0 else 1)
+                act = stage(y, t_emb)
             else:
                 up = F.interpolate(act, scale_factor=2.0, mode="nearest") if i > 0 else act
                 act = stage(torch.cat([up, h], dim=1), t_emb)

@@ -170,6 +170,15 @@ int fp8_conv3x3_wgrad(const void* xq, const void* dyq, void* dw, const float* sx
                       int height, int width, int cin, int cout, int split_k, void* workspace,
                       size_t workspace_bytes, fp8_stream_t stream);
 
+/* fp8_conv3x3_wgrad with dw fp32 [Cout][3][3][Cin] (16-byte aligned): the same
+ * bf16 values, widened.  That is the gradient the reference's fp32 conv weight
+ * receives: Conv2dFP8Specialized.backward returns the bf16 dW
+ * (fp8_kernels.py:875-913) and autograd casts it to the parameter's dtype; here
+ * the reduce pass writes it directly, with no separate cast launch. */
+int fp8_conv3x3_wgrad_f32(const void* xq, const void* dyq, float* dw, const float* sx, const float* sdy, int batch,
+                          int height, int width, int cin, int cout, int split_k, void* workspace,
+                          size_t workspace_bytes, fp8_stream_t stream);
+
 /* --------------------------------------------------------------- FP8 linear */
 
 /* out[m,n] = epi( sum_k a[m,k] * b[n,k] * sa * sb ), a: [M][K] e4m3, b: [N][K]
@@ -291,6 +300,17 @@ int fp8_up_cat(const void* a, int a_dtype, const void* s, int s_dtype, void* y, 
 int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds, int s_dtype, int n, int h, int w,
                    int c1, int c2, int factor, fp8_stream_t stream);
 
+/* fp8_up_cat with an fp32 y and a second output y_bf16 = bf16(y) (round to
+ * nearest even): the concatenation the next residual block normalises and the
+ * copy bf16 autocast makes of it for that block's 1x1 skip conv (reference
+ * unet.py:139, 161, an nn.Conv2d reading the fp32 tensor), in one pass.
+ * fp8_up_cat_pair_bwd: the gradient of y is dy + dy_bf16 (fp32 sum, the one
+ * autograd forms for the two readers), then as fp8_up_cat_bwd. */
+int fp8_up_cat_pair(const void* a, int a_dtype, const void* s, int s_dtype, float* y, void* y_bf16, int n, int h,
+                    int w, int c1, int c2, int factor, fp8_stream_t stream);
+int fp8_up_cat_pair_bwd(const float* dy, const void* dy_bf16, void* da, int a_dtype, void* ds, int s_dtype, int n,
+                        int h, int w, int c1, int c2, int factor, fp8_stream_t stream);
+
 /* Delayed scaling with the scale history kept on the device (reference
  * Conv2dFP8 bookkeeping, unet.py:69-91, fp8_kernels.py:841-853, 883-889):
  * the cast divides by max(window[0 .. window_len)) -- the module's
@@ -298,7 +318,7 @@ int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds,
  * dequantisation scale of q, for the contraction); afterwards this tensor's
  * own scale (amax/448, 1.0 for amax 0) is stored at window[*window_pos] and,
  * when `advance`, *window_pos = (*window_pos + 1) % window_len.  One cast pass
- * plus a one-CTA finalize; no torch.max / scatter / position launches. */
+ * whose last CTA folds the scale; no torch.max / scatter / position launches. */
 int fp8_quantize_delayed_window(const void* x_bf16, void* q_e4m3, float* window, int window_len,
                                 int64_t* window_pos, int advance, float* scale_used_out, void* workspace,
                                 size_t workspace_bytes, int64_t n, fp8_stream_t stream);
@@ -357,8 +377,8 @@ size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c);
  *   q_e4m3[i]       = e4m3(clamp(bf16(a[i]) / *prev_scale, -448, 448))
  *   *scale_curr_out = amax|bf16(a)| / 448 (1.0 when the amax is 0)
  * bit for bit what fp8_gn_act_fwd followed by fp8_quantize_delayed gives, in one
- * statistics pass, one apply pass that writes only the e4m3 bytes, and a
- * one-CTA finalize.  stats as in fp8_gn_act_fwd (for the backward). */
+ * statistics pass and one apply pass that writes only the e4m3 bytes and whose
+ * last CTA folds the scale.  stats as in fp8_gn_act_fwd (for the backward). */
 int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const float* beta, const void* film,
                          int film_ld, const int64_t* seed, float p, float eps, const float* prev_scale,
                          float* stats, void* q_e4m3, float* scale_curr_out, int n, int hw, int c, int groups,

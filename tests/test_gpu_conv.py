@@ -110,6 +110,26 @@ def test_conv_wgrad_all_unet_shapes(cuda, cin, cout, h, w):
     assert oracle.max_rel_err(dw, ref) <= TOL
 
 
+@pytest.mark.parametrize("cin,cout,h,w", [(128, 128, 32, 32), (256, 256, 8, 8), (512, 256, 16, 16)])
+def test_conv_wgrad_widened_fp32(cuda, cin, cout, h, w):
+    """widen=True: fp32 dW holding bf16 values (what autograd stores for an fp32 weight), equal to
+    the bf16 result widened up to the unordered split-K additions (one bf16 step), and within the
+    oracle tolerance."""
+    from fp8_b200 import ops
+
+    b = max(2, 2048 // (h * w))
+    xq, sx = _rand_q((b, cin, h, w), seed=cin + h, device=cuda)
+    dyq, sdy = _rand_q((b, cout, h, w), seed=cout + w + 1, device=cuda, scale=1e-2)
+    dw32 = ops.conv3x3_wgrad(xq, dyq, sx, sdy, 0, True)
+    dw16 = ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+    assert dw32.dtype == torch.float32 and dw32.is_contiguous(memory_format=torch.channels_last)
+    assert torch.equal(dw32.bfloat16().float(), dw32)  # bf16 values
+    ref16 = dw16.float()
+    assert ((dw32 - ref16).abs() <= 2.0 ** -7 * ref16.abs() + 1e-4 * ref16.abs().max()).all()
+    ref = oracle.conv_dw(xq.cpu(), dyq.cpu(), sx.item(), sdy.item())
+    assert oracle.max_rel_err(dw32, ref) <= TOL
+
+
 @pytest.mark.parametrize("split_k", [1, 3, 7])
 def test_conv_wgrad_split_counts(cuda, split_k):
     from fp8_b200 import ops

@@ -224,3 +224,55 @@ def test_quantize_current_pair_unaligned_falls_back(cuda):
         q_ref, s_ref = oracle.quantize_current(t.cpu())
         assert np.float32(s.item()).tobytes() == s_ref.tobytes()
         assert np.array_equal(_bytes(q), q_ref)
+
+
+def test_quantize_delayed_scale_fold_over_the_counter_ring(cuda):
+    """The current scale is folded by the last CTA of the cast launch, on a ticket counter that each launch
+    takes from a ring and leaves at zero.  More launches than the ring holds, with grids from 1 CTA to many
+    (ragged sizes and the scalar path included): every scale equals amax / 448 of its own tensor."""
+    from fp8_b200 import ops
+
+    sizes = [8, 13, 4096, 65536 + 5, 1 << 20, 3 * (1 << 21)]
+    xs = [_gen((n,), seed=100 + i, scale=0.5 + i) for i, n in enumerate(sizes)]
+    xs.append(_gen((4097,), seed=99, scale=3.0)[1:])  # 2 bytes off alignment: the scalar kernel
+    xs.append(torch.zeros(4096, dtype=torch.bfloat16, device=cuda))  # amax 0: scale 1
+    amax = [np.float32(x.float().abs().max().item()) for x in xs]
+    expect = torch.tensor([a / np.float32(448.0) if a > 0 else np.float32(1.0) for a in amax], device=cuda)
+    prev = torch.tensor(0.01, dtype=torch.float32, device=cuda)
+    got = []
+    for i in range(8192 + 64):
+        _, s = ops.quantize_delayed(xs[i % len(xs)], prev)
+        got.append(s)
+    got = torch.stack(got).view(-1, 1)
+    torch.cuda.synchronize()
+    n = len(xs)
+    for k in range(n):
+        assert torch.equal(got[k::n].view(-1), expect[k].expand(got[k::n].numel())), k
+    assert ops.device_error() == 0
+
+
+def test_quantize_delayed_window_replayed_in_cuda_graph(cuda):
+    """The fold inside a captured graph: each replay writes the new scale at the history position and steps it."""
+    from fp8_b200 import ops
+
+    x = _gen((16, 128, 32, 32), seed=41)
+    win = torch.zeros(8, dtype=torch.float32, device=cuda)
+    win[0] = 0.02
+    pos = torch.zeros((), dtype=torch.int64, device=cuda)
+    ops.quantize_delayed_window(x, win, pos, True)  # warm-up outside capture: pos -> 1
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        q, used = ops.quantize_delayed_window(x, win, pos, True)
+    scales = []
+    for r in range(3):
+        x.copy_(_gen((16, 128, 32, 32), seed=42 + r, scale=1.0 + r))
+        prev_max = win.max().item()
+        g.replay()
+        torch.cuda.synchronize()
+        q_ref, s_ref = oracle.quantize_delayed(x.cpu(), np.float32(prev_max))
+        assert np.array_equal(_bytes(q), q_ref)
+        assert used.item() == np.float32(prev_max)
+        scales.append(s_ref)
+        assert pos.item() == 2 + r
+        assert win[1 + r].item() == float(s_ref)

@@ -70,6 +70,70 @@ def test_upsample_cat_matches_torch_under_autocast(cuda, factor, da, ds):
     assert ((a1.float() - a2.float()).abs() <= tol * a2.float().abs() + 1e-30).all()
 
 
+@pytest.mark.parametrize("factor", [1, 2])
+@pytest.mark.parametrize("da,ds", [(torch.bfloat16, torch.bfloat16), (torch.bfloat16, torch.float32),
+                                   (torch.float32, torch.float32)])
+def test_upsample_cat_pair_matches_cat_and_autocast_copy(cuda, factor, da, ds):
+    """upsample_cat_pair = (cat of the upsampled a and s, its bf16 copy) bit for bit, and its backward takes
+    the sum of both outputs' gradients as autograd forms it: ds bitwise, da within one rounding step."""
+    from fp8_b200.resample import upsample_cat_pair
+
+    if factor == 1 and da == ds == torch.bfloat16:
+        pytest.skip("no fp32 output: the pair is not formed")
+    n, c1, c2, h = 8, 256, 128, 16
+    a0 = _t((n, c1, h // factor, h // factor), da, 21, cuda)
+    s0 = _t((n, c2, h, h), ds, 22, cuda)
+    dy = _t((n, c1 + c2, h, h), torch.float32, 23, cuda)
+    dy16 = _t((n, c1 + c2, h, h), torch.bfloat16, 24, cuda)
+    outs = []
+    for fused in (True, False):
+        a = a0.clone().requires_grad_(True)
+        s = s0.clone().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            if fused:
+                y, y16 = upsample_cat_pair(a, s, factor)
+            else:
+                up = F.interpolate(a, scale_factor=2.0, mode="nearest") if factor > 1 else a
+                y = torch.cat([up, s], dim=1)
+                y16 = y.to(torch.bfloat16)
+        torch.autograd.backward([y, y16], [dy, dy16])
+        outs.append((y.detach(), y16.detach(), a.grad, s.grad))
+    (y1, q1, a1, s1), (y2, q2, a2, s2) = outs
+    assert y1.dtype == y2.dtype == torch.float32 and torch.equal(y1, y2)
+    assert q1.dtype == q2.dtype == torch.bfloat16 and torch.equal(q1, q2)
+    assert q1.is_contiguous(memory_format=torch.channels_last)
+    assert s1.dtype == s2.dtype == ds and torch.equal(s1, s2)
+    assert a1.dtype == a2.dtype == da
+    tol = 2.0 ** -7 if da == torch.bfloat16 else 1e-6
+    assert ((a1.float() - a2.float()).abs() <= tol * a2.float().abs() + 1e-30).all()
+
+
+def test_unet_with_paired_skip_cast_matches_separate_cast(cuda):
+    """The UNet with the up stages' skip-conv copy made by the up_cat pass: the same output bytes, and
+    gradients within bf16 rounding of the separate cast + gradient sum."""
+    from fp8_b200.train import build_model
+
+    x = (torch.rand(4, 3, 32, 32) * 2 - 1).to(cuda).contiguous(memory_format=torch.channels_last)
+    t = torch.randint(0, 1000, (4,)).to(cuda)
+    res = []
+    for paired in (True, False):
+        m = build_model(fp8=False, device=cuda, seed=0, p_drop=0.0)
+        m.config.fused_skip_cast = paired
+        with torch.no_grad():  # the zero-initialised branches would give zero gradients everywhere
+            torch.manual_seed(1)
+            for mod in m.modules():
+                if isinstance(mod, torch.nn.Conv2d) and not mod.weight.any():
+                    torch.nn.init.normal_(mod.weight, std=0.02)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = m(x, t)
+        y.float().square().mean().backward()
+        res.append((y.detach(), m.conv_in.weight.grad.clone(), m.up_stages[-1].blocks[0].skip_connection.weight.grad))
+    (ya, ia, sa), (yb, ib, sb) = res
+    assert torch.equal(ya, yb)
+    for u, v in ((ia, ib), (sa, sb)):
+        assert ((u - v).abs().max() / v.abs().max()).item() <= 1e-2
+
+
 def test_unet_forward_identical_with_fused_resampling(cuda):
     """The whole UNet forward gives the same bytes with the fused resampling (it only copies values)."""
     from fp8_b200.train import build_model
