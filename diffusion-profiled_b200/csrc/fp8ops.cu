@@ -23,6 +23,7 @@
 #include "layernorm.cuh"
 #include "resample.cuh"
 #include "optim.cuh"
+#include "cast_batch.cuh"
 
 using namespace fp8b;
 
@@ -2051,6 +2052,43 @@ int fp8_add_scale_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* 
   if (int r = add_scale_dispatch(a_dtype, b_dtype, y_dtype, da, db, const_cast<void*>(dy), n, inv_divisor, true,
                                  st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
     return r;
+  return ok();
+}
+
+// ======================================================================== batched casts
+int fp8_cast_batch(int count, const void* const* src, void* const* dst, const int64_t* n, int to_bf16,
+                   fp8_stream_t stream) {
+  FP8_REQUIRE(count > 0 && count <= kCastTensors, FP8_ERR_UNSUPPORTED, "1..%d tensors per call", kCastTensors);
+  FP8_REQUIRE(src && dst && n, FP8_ERR_INVALID_ARGUMENT, "NULL argument");
+  CastBatch b{};
+  b.count = count;
+  int64_t chunks = 0;
+  for (int t = 0; t < count; ++t) {
+    FP8_REQUIRE(n[t] >= 0, FP8_ERR_INVALID_ARGUMENT, "tensor %d: negative size", t);
+    FP8_REQUIRE(n[t] == 0 || (src[t] != nullptr && dst[t] != nullptr), FP8_ERR_INVALID_ARGUMENT,
+                "tensor %d: NULL pointer", t);
+    FP8_REQUIRE(aligned(src[t], to_bf16 ? 4 : 2) && aligned(dst[t], to_bf16 ? 2 : 4), FP8_ERR_INVALID_ARGUMENT,
+                "tensor %d: misaligned for its dtype", t);
+    b.src[t] = src[t];
+    b.dst[t] = dst[t];
+    b.n[t] = n[t];
+    b.chunk_begin[t] = static_cast<int>(chunks);
+    chunks += (n[t] + kCastChunk - 1) / kCastChunk;
+    FP8_REQUIRE(chunks < (1ll << 30), FP8_ERR_UNSUPPORTED, "tensors too large");
+  }
+  b.chunk_begin[count] = static_cast<int>(chunks);
+  if (chunks == 0) return ok();
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  (void)st;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (to_bf16)
+    FP8_CUDA_TRY(launch_kernel(cast_batch_kernel<true>, dim3(static_cast<unsigned>(chunks)), dim3(kCastThreads), 0, cs,
+                               1, kStreamingKernel, b));
+  else
+    FP8_CUDA_TRY(launch_kernel(cast_batch_kernel<false>, dim3(static_cast<unsigned>(chunks)), dim3(kCastThreads), 0,
+                               cs, 1, kStreamingKernel, b));
+  count_launches(1);
   return ok();
 }
 

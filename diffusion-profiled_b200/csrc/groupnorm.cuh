@@ -641,20 +641,22 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
 // Parameter gradients from the per-(n, c) totals of the backward:
 //   dgamma_c = sum_n (s_nc + 1) * T[n][2C + c],  dbeta_c = sum_n (s_nc + 1) * T[n][c]
 //   dfilm[n] = (T[n][C:2C], T[n][0:C]) as bf16     (the scale, then the shift gradient)
-// with s = 0 and no dfilm without FiLM.  A CTA covers 32 channels with 8 lanes
-// of samples (n = lane, lane + 8, ...; coalesced rows), then sums the 8 lanes in
-// order (deterministic).
-constexpr int kGnParamLanes = 8;
+// with s = 0 and no dfilm without FiLM.  A CTA covers 32 channels with 32 lanes
+// of samples (n = lane, lane + 32, ...; coalesced rows, four samples' loads in
+// flight per thread), then two threads per channel sum the 32 lanes in order
+// (deterministic).
+constexpr int kGnParamLanes = 32;
 
 __global__ void __launch_bounds__(32 * kGnParamLanes) gn_param_grads_kernel(
     const float* __restrict__ totals, const uint16_t* __restrict__ film, int film_ld, int n, int c,
     float* __restrict__ dgamma, float* __restrict__ dbeta, uint16_t* __restrict__ dfilm, int dfilm_ld) {
-  __shared__ float red[2][kGnParamLanes][32];
+  __shared__ float red[2][kGnParamLanes][33];
   pdl_wait();
   const int cl = threadIdx.x & 31, lane = threadIdx.x >> 5;
   const int ch = blockIdx.x * 32 + cl;
   float g = 0.0f, b = 0.0f;
   if (ch < c) {
+#pragma unroll 4
     for (int i = lane; i < n; i += kGnParamLanes) {
       const float* t = totals + static_cast<int64_t>(i) * 3 * c;
       const float t_df = t[ch], t_dfz = t[c + ch], t_dfx = t[2 * c + ch];
@@ -672,15 +674,11 @@ __global__ void __launch_bounds__(32 * kGnParamLanes) gn_param_grads_kernel(
   red[0][lane][cl] = g;
   red[1][lane][cl] = b;
   __syncthreads();
-  if (lane == 0 && ch < c) {
-    float sg = 0.0f, sb = 0.0f;
+  if (lane < 2 && ch < c) {  // lane 0: dgamma, lane 1: dbeta
+    float sum = 0.0f;
 #pragma unroll
-    for (int l = 0; l < kGnParamLanes; ++l) {
-      sg += red[0][l][cl];
-      sb += red[1][l][cl];
-    }
-    dgamma[ch] = sg;
-    dbeta[ch] = sb;
+    for (int l = 0; l < kGnParamLanes; ++l) sum += red[lane][l][cl];
+    (lane == 0 ? dgamma : dbeta)[ch] = sum;
   }
 }
 

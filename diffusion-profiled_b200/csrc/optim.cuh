@@ -53,6 +53,15 @@ __device__ __forceinline__ int opt_tensor_of(const OptGroup& b, int k) {
   return lo;
 }
 
+// Whether tensor t's chunks can move as float4 (every pointer 16-byte aligned;
+// chunk starts are multiples of kOptChunk, so of 4 elements).
+__device__ __forceinline__ bool opt_vec_ok(const OptGroup& b, int t) {
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(b.p[t]) | reinterpret_cast<uintptr_t>(b.g[t]) |
+                         reinterpret_cast<uintptr_t>(b.m[t]) | reinterpret_cast<uintptr_t>(b.v[t]) |
+                         reinterpret_cast<uintptr_t>(b.ema[t]);
+  return (bits & 15u) == 0;
+}
+
 // partials[part0 + k] = sum of g^2 over chunk k of this group.
 __global__ void __launch_bounds__(kOptThreads) opt_sumsq_kernel(OptGroup b, float* __restrict__ partials, int part0) {
   pdl_wait();
@@ -63,7 +72,19 @@ __global__ void __launch_bounds__(kOptThreads) opt_sumsq_kernel(OptGroup b, floa
   const int64_t end = min(begin + kOptChunk, b.n[t]);
   const float* __restrict__ g = b.g[t];
   float s = 0.0f;
-  for (int64_t i = begin + threadIdx.x; i < end; i += kOptThreads) s = fmaf(g[i], g[i], s);
+  int64_t tail = begin;
+  if ((reinterpret_cast<uintptr_t>(g) & 15u) == 0) {
+    const int64_t end4 = begin + ((end - begin) & ~int64_t(3));
+    for (int64_t i = begin + 4 * threadIdx.x; i < end4; i += 4 * kOptThreads) {
+      const float4 v = *reinterpret_cast<const float4*>(g + i);
+      s = fmaf(v.x, v.x, s);
+      s = fmaf(v.y, v.y, s);
+      s = fmaf(v.z, v.z, s);
+      s = fmaf(v.w, v.w, s);
+    }
+    tail = end4;
+  }
+  for (int64_t i = tail + threadIdx.x; i < end; i += kOptThreads) s = fmaf(g[i], g[i], s);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
@@ -97,35 +118,74 @@ __global__ void __launch_bounds__(kOptThreads) opt_norm_kernel(const float* __re
   }
 }
 
+// The per-step constants of the update.
+struct AdamConsts {
+  float coef, bc2_sqrt, step_size, decay, one_m_b1, beta2, one_m_b2, eps, ema_beta, one_m_ema;
+};
+
+// One element: clip, decoupled decay, moments, step, then the EMA of the new weight.
+__device__ __forceinline__ void adamw_ema_elem(const AdamConsts& k, float& p, float g, float& m, float& v, float* e) {
+  const float gi = g * k.coef;
+  float pi = p * k.decay;
+  float mi = fmaf(k.one_m_b1, gi - m, m);
+  const float vi = fmaf(v, k.beta2, k.one_m_b2 * gi * gi);
+  pi -= k.step_size * mi / (sqrtf(vi) / k.bc2_sqrt + k.eps);
+  p = pi;
+  m = mi;
+  v = vi;
+  if (e != nullptr) *e = __fadd_rn(__fmul_rn(*e, k.ema_beta), __fmul_rn(k.one_m_ema, pi));
+}
+
 __global__ void __launch_bounds__(kOptThreads) opt_update_kernel(OptGroup b, OptHyper h) {
   pdl_wait();
   const int k = blockIdx.x;
   const int t = opt_tensor_of(b, k);
   const int64_t begin = static_cast<int64_t>(k - b.chunk_begin[t]) * kOptChunk;
   const int64_t end = min(begin + kOptChunk, b.n[t]);
-  const float coef = *h.coef;
   const float step = *h.step;
-  const float bc1 = 1.0f - powf(h.beta1, step);
-  const float bc2_sqrt = sqrtf(1.0f - powf(h.beta2, step));
-  const float step_size = h.lr / bc1;
-  const float decay = 1.0f - h.lr * h.weight_decay;
-  const float one_m_ema = 1.0f - h.ema_beta;
+  AdamConsts c;
+  c.coef = *h.coef;
+  c.bc2_sqrt = sqrtf(1.0f - powf(h.beta2, step));
+  c.step_size = h.lr / (1.0f - powf(h.beta1, step));
+  c.decay = 1.0f - h.lr * h.weight_decay;
+  c.one_m_b1 = 1.0f - h.beta1;
+  c.beta2 = h.beta2;
+  c.one_m_b2 = 1.0f - h.beta2;
+  c.eps = h.eps;
+  c.ema_beta = h.ema_beta;
+  c.one_m_ema = 1.0f - h.ema_beta;
   float* __restrict__ p = b.p[t];
   const float* __restrict__ g = b.g[t];
   float* __restrict__ m = b.m[t];
   float* __restrict__ v = b.v[t];
   float* __restrict__ e = b.ema[t];
-  for (int64_t i = begin + threadIdx.x; i < end; i += kOptThreads) {
-    const float gi = g[i] * coef;
-    float pi = p[i] * decay;
-    float mi = m[i];
-    mi = fmaf(1.0f - h.beta1, gi - mi, mi);
-    const float vi = fmaf(v[i], h.beta2, (1.0f - h.beta2) * gi * gi);
-    pi -= step_size * mi / (sqrtf(vi) / bc2_sqrt + h.eps);
+  int64_t tail = begin;
+  if (opt_vec_ok(b, t)) {  // uniform over the CTA
+    const int64_t end4 = begin + ((end - begin) & ~int64_t(3));
+    for (int64_t i = begin + 4 * threadIdx.x; i < end4; i += 4 * kOptThreads) {
+      float4 pv = *reinterpret_cast<const float4*>(p + i);
+      const float4 gv = *reinterpret_cast<const float4*>(g + i);
+      float4 mv = *reinterpret_cast<const float4*>(m + i);
+      float4 vv = *reinterpret_cast<const float4*>(v + i);
+      float4 ev = e != nullptr ? *reinterpret_cast<const float4*>(e + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float* ep = e != nullptr ? &ev.x : nullptr;
+      adamw_ema_elem(c, pv.x, gv.x, mv.x, vv.x, ep);
+      adamw_ema_elem(c, pv.y, gv.y, mv.y, vv.y, ep ? &ev.y : nullptr);
+      adamw_ema_elem(c, pv.z, gv.z, mv.z, vv.z, ep ? &ev.z : nullptr);
+      adamw_ema_elem(c, pv.w, gv.w, mv.w, vv.w, ep ? &ev.w : nullptr);
+      *reinterpret_cast<float4*>(p + i) = pv;
+      *reinterpret_cast<float4*>(m + i) = mv;
+      *reinterpret_cast<float4*>(v + i) = vv;
+      if (e != nullptr) *reinterpret_cast<float4*>(e + i) = ev;
+    }
+    tail = end4;
+  }
+  for (int64_t i = tail + threadIdx.x; i < end; i += kOptThreads) {
+    float pi = p[i], mi = m[i], vi = v[i];
+    adamw_ema_elem(c, pi, g[i], mi, vi, e != nullptr ? e + i : nullptr);
     p[i] = pi;
     m[i] = mi;
     v[i] = vi;
-    if (e != nullptr) e[i] = __fadd_rn(__fmul_rn(e[i], h.ema_beta), __fmul_rn(one_m_ema, pi));
   }
 }
 

@@ -102,6 +102,7 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_up_cat_bwd": (
         c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                 c_void_p]),
+    "fp8_cast_batch": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "fp8_up_cat_pair": (
         c_int,
         [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p],

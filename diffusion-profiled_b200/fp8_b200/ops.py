@@ -223,6 +223,64 @@ def _(weights, windows, positions):
             + [w.new_empty((), dtype=torch.float32) for w in weights])
 
 
+# ----------------------------------------------------------------------------- batched casts
+def _cast_call(srcs: list[torch.Tensor], dsts: list[torch.Tensor], to_bf16: bool, dev: torch.device) -> None:
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        for i in range(0, len(srcs), 64):  # fp8_cast_batch takes 64 tensors per call
+            s, d = srcs[i:i + 64], dsts[i:i + 64]
+            k = len(s)
+            _lib.check(lib.fp8_cast_batch(k, (c_void_p * k)(*[t.data_ptr() for t in s]),
+                                          (c_void_p * k)(*[t.data_ptr() for t in d]),
+                                          (c_int64 * k)(*[t.numel() for t in s]), int(to_bf16), _stream(dev)),
+                       "fp8_cast_batch")
+
+
+def _dense(t: torch.Tensor) -> bool:
+    return t.is_contiguous() or (t.dim() == 4 and t.is_contiguous(memory_format=torch.channels_last))
+
+
+@torch.library.custom_op("fp8_b200::cast_batch", mutates_args=())
+def cast_batch(srcs: list[torch.Tensor], to_bf16: bool) -> list[torch.Tensor]:
+    """Each tensor cast fp32 -> bf16 (``to_bf16``) or bf16 -> fp32, same shape and strides, in one
+    launch per 64 tensors: the values of ``t.to(dtype)``."""
+    if not srcs:
+        return []
+    dev = _require_cuda(*srcs)
+    want = torch.float32 if to_bf16 else torch.bfloat16
+    for t in srcs:
+        if t.dtype != want or not _dense(t):
+            raise RuntimeError(f"cast_batch expects dense {want} tensors")
+    dst_dt = torch.bfloat16 if to_bf16 else torch.float32
+    dsts = [torch.empty_like(t, dtype=dst_dt) for t in srcs]
+    _cast_call(srcs, dsts, to_bf16, dev)
+    return dsts
+
+
+@cast_batch.register_fake
+def _(srcs, to_bf16):
+    return [torch.empty_like(t, dtype=torch.bfloat16 if to_bf16 else torch.float32) for t in srcs]
+
+
+@torch.library.custom_op("fp8_b200::cast_cat_bf16", mutates_args=())
+def cast_cat_bf16(srcs: list[torch.Tensor]) -> torch.Tensor:
+    """``torch.cat(srcs, dim=0).to(torch.bfloat16)`` for contiguous 2-D fp32 tensors of one width,
+    written directly (one launch, no fp32 concatenation)."""
+    dev = _require_cuda(*srcs)
+    cols = srcs[0].shape[1] if srcs and srcs[0].dim() == 2 else -1
+    for t in srcs:
+        if t.dtype != torch.float32 or t.dim() != 2 or t.shape[1] != cols or not t.is_contiguous():
+            raise RuntimeError("cast_cat_bf16 expects contiguous 2-D float32 tensors of one width")
+    out = torch.empty((sum(t.shape[0] for t in srcs), cols), device=dev, dtype=torch.bfloat16)
+    _cast_call(srcs, list(torch.split(out, [t.shape[0] for t in srcs], dim=0)), True, dev)
+    return out
+
+
+@cast_cat_bf16.register_fake
+def _(srcs):
+    return srcs[0].new_empty((sum(t.shape[0] for t in srcs), srcs[0].shape[1]), dtype=torch.bfloat16)
+
+
 # ----------------------------------------------------------------------------- transposes
 @torch.library.custom_op("fp8_b200::transpose_2d", mutates_args=())
 def transpose_2d(src: torch.Tensor) -> torch.Tensor:

@@ -298,7 +298,7 @@ def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16
     fr = fused_norm if fused_resample is None else fused_resample
     cfg = UNetConfig(fp8_convs_enabled=fp8, fp8_scaling_type=scaling, attn_resolutions=list(attn_resolutions),
                      p_drop=p_drop, fused_norm=fused_norm, fused_resample=fr, fused_residual=fr,
-                     batched_time_embed=fr, fused_skip_cast=fr)
+                     batched_time_embed=fr, fused_skip_cast=fr, batched_weight_cast=fr)
     model = UNet(cfg).to(memory_format=torch.channels_last)
     return model.to(device)
 

@@ -30,6 +30,7 @@ import torch.nn.functional as F
 from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed, quantize_conv_weights
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
 from .resample import downsample_nearest, residual_join, upsample_cat, upsample_cat_pair
+from .weights import batch_cast_applies, cast_cat_weights_bf16, cast_weights_bf16
 from .norm import GroupNormActConvFP8, fused_layer_norm_supported, fused_norm_supported, group_norm_act, layer_norm_bf16
 
 
@@ -70,6 +71,10 @@ class UNetConfig:
     # makes of it for the first block's 1x1 skip conv, written by one pass; their two
     # gradients summed by the backward of that pass (needs fused_resample)
     fused_skip_cast: bool = True
+    # the bf16 copies autocast makes of the bf16 layers' fp32 weights (attention projections,
+    # 1x1 skip convs, time-embedding linears), and the casts of their gradients back, one
+    # launch each way per step (fp8_b200.weights)
+    batched_weight_cast: bool = True
 
     def as_dict(self):
         return asdict(self)
@@ -195,6 +200,7 @@ class ResidualBlock(nn.Module):
         self.fused_residual = config.fused_residual
         self._emb = None  # this block's time-embedding projection, when the UNet computed it in a batch
         self._skip_in = None  # bf16 copy of the input for the 1x1 skip conv, when the UNet made one
+        self._skip_w16 = None  # bf16 copy of the skip conv's weight, when the UNet made one
         # dropout mask seed of the fused path (device scalar, advanced every
         # training forward so a captured graph draws a new mask each replay)
         self.register_buffer("dropout_seed", torch.randint(0, 2**62, (), dtype=torch.int64), persistent=False)
@@ -223,7 +229,9 @@ class ResidualBlock(nn.Module):
 
     def _join(self, x: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
         skip_in, self._skip_in = self._skip_in, None
-        skip = self.skip_connection(x if skip_in is None else skip_in)
+        w16, self._skip_w16 = self._skip_w16, None
+        src = x if skip_in is None else skip_in
+        skip = self.skip_connection(src) if w16 is None else F.conv2d(src, w16, self.skip_connection.bias)
         if self.fused_residual:
             return residual_join(skip, h)
         return (skip + h) / math.sqrt(2.0)
@@ -241,6 +249,7 @@ class CHWAttention(nn.Module):
         self.out = nn.Linear(hidden_size, hidden_size, bias=False)
         self.norm = nn.LayerNorm(hidden_size)
         nn.init.zeros_(self.out.weight)
+        self._w16 = None  # bf16 copies of (qkv, out) weights, when the UNet made them
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         b, c, h, w = x.shape
@@ -249,10 +258,13 @@ class CHWAttention(nn.Module):
             tokens = layer_norm_bf16(tokens, self.norm)  # bf16, what the qkv projection consumes
         else:
             tokens = self.norm(tokens)
-        q, k, v = self.qkv(tokens).chunk(3, dim=-1)
+        w16, self._w16 = self._w16, None
+        qkv = self.qkv(tokens) if w16 is None else F.linear(tokens, w16[0], self.qkv.bias)
+        q, k, v = qkv.chunk(3, dim=-1)
         heads = lambda z: z.unflatten(-1, (self.nh, c // self.nh)).transpose(1, 2)  # noqa: E731
         o = F.scaled_dot_product_attention(heads(q), heads(k), heads(v))
-        o = self.out(o.transpose(1, 2).flatten(2))  # [B, HW, C]
+        o = o.transpose(1, 2).flatten(2)
+        o = self.out(o) if w16 is None else F.linear(o, w16[1], self.out.bias)  # [B, HW, C]
         o = o.transpose(1, 2).reshape(b, c, h, w)
         if self.fused_residual:
             return residual_join(o, x)
@@ -312,6 +324,7 @@ class UNet(nn.Module):
         half = base // 2
         freqs = torch.exp(-torch.arange(half, dtype=torch.float32) * (math.log(10000.0) / half))
         self.register_buffer("freqs", freqs, persistent=False)
+        self._time_w16 = None  # bf16 time-MLP weights from the step's batched cast
 
     def _timestep(self, t: torch.Tensor) -> torch.Tensor:
         emb = t[:, None].float() * self.freqs[None]
@@ -326,6 +339,7 @@ class UNet(nn.Module):
         batch = getattr(self, "_fp8_delayed_convs", None)
         if batch:
             quantize_conv_weights(batch)
+        self._time_w16 = self._cast_bf16_weights() if self.config.batched_weight_cast else None
         out = self._forward(x, t)
         convs = [m for m in self.modules() if isinstance(m, Conv2dFP8) and m.used_fp8_delayed]
         for m in convs:
@@ -335,16 +349,45 @@ class UNet(nn.Module):
         self._fp8_delayed_convs = convs if len(convs) <= 64 else None
         return out
 
+    def _cast_bf16_weights(self):
+        """One batched bf16 cast of the weights of the layers that run in bf16: each attention's
+        (qkv, out), each 1x1 skip conv, and the time MLP (returned).  None when they would not be
+        cast (autocast off, or any of them swapped for an FP8 layer)."""
+        attns = [m for m in self.modules() if isinstance(m, CHWAttention)]
+        skips = [m for m in self.modules() if isinstance(m, ResidualBlock) and isinstance(m.skip_connection, nn.Conv2d)]
+        mlp = (self.time_embed[0], self.time_embed[2])
+        lins = [lin for a in attns for lin in (a.qkv, a.out)] + list(mlp)
+        if any(type(lin) is not nn.Linear for lin in lins):
+            return None
+        weights = [lin.weight for lin in lins] + [b.skip_connection.weight for b in skips]
+        if not batch_cast_applies(weights):
+            return None
+        w16 = cast_weights_bf16(weights)
+        for i, a in enumerate(attns):
+            a._w16 = (w16[2 * i], w16[2 * i + 1])
+        k = 2 * len(attns) + 2
+        for b, w in zip(skips, w16[k:]):
+            b._skip_w16 = w
+        return w16[k - 2], w16[k - 1]
+
     def _batched_time_embeds(self, t_emb: torch.Tensor) -> None:
         """One GEMM for all blocks' ``t_embed_wb`` projections (same input); each block gets its column slice."""
         blocks = [m for m in self.modules() if isinstance(m, ResidualBlock)]
         weights = [b.t_embed_wb.mlp.weight for b in blocks]
-        e = F.linear(t_emb, torch.cat(weights, dim=0))
+        if self.config.batched_weight_cast and batch_cast_applies(weights) and all(w.is_contiguous() for w in weights):
+            e = F.linear(t_emb, cast_cat_weights_bf16(weights))
+        else:
+            e = F.linear(t_emb, torch.cat(weights, dim=0))
         for b, part in zip(blocks, torch.split(e, [w.shape[0] for w in weights], dim=1)):
             b._emb = part[:, :, None, None]
 
     def _forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
-        t_emb = self.time_embed(self._timestep(t))
+        w16, self._time_w16 = self._time_w16, None
+        if w16 is None:
+            t_emb = self.time_embed(self._timestep(t))
+        else:  # time_embed = Linear, SiLU, Linear, SiLU on the batch-cast weights
+            h = F.silu(F.linear(self._timestep(t), w16[0], self.time_embed[0].bias))
+            t_emb = F.silu(F.linear(h, w16[1], self.time_embed[2].bias))
         if self.config.batched_time_embed:
             self._batched_time_embeds(t_emb)
         act = self.conv_in(x)

@@ -384,6 +384,17 @@ int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const fl
                          float* stats, void* q_e4m3, float* scale_curr_out, int n, int hw, int c, int groups,
                          void* workspace, size_t workspace_bytes, fp8_stream_t stream);
 
+/* ------------------------------------------------------------ batched casts */
+
+/* dst[t][i] = src[t][i] for count (1..64) dense tensors of n[t] elements, one
+ * launch: to_bf16 != 0 casts fp32 -> bf16 (round to nearest even), else bf16
+ * -> fp32 (exact).  Replaces the per-weight casts bf16 autocast makes for the
+ * reference's bf16 layers (attention projections unet.py:171-172, 1x1 skip
+ * convs :139, time-embedding linears :101, :331-336) and the casts of their
+ * bf16 weight gradients back to the fp32 parameters' dtype. */
+int fp8_cast_batch(int count, const void* const* src, void* const* dst, const int64_t* n, int to_bf16,
+                   fp8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -183,3 +183,14 @@ def test_resample_rejects_bad_channels_without_touching_cuda():
     assert status == _lib.FP8_ERR_UNSUPPORTED and code == status and "multiples of 8" in msg
     status, code, msg = _status_and_message(lib.fp8_resample_down2, fake, 0, fake, 2, 7, 8, 16, c_void_p(0))
     assert status == _lib.FP8_ERR_UNSUPPORTED and "even" in msg
+
+
+def test_cast_batch_validates_without_touching_cuda():
+    lib = _lib.load()
+    arr = (c_void_p * 1)(c_void_p(1 << 20))
+    n = (ctypes.c_int64 * 1)(16)
+    status, code, msg = _status_and_message(lib.fp8_cast_batch, 65, arr, arr, n, 1, c_void_p(0))
+    assert status == _lib.FP8_ERR_UNSUPPORTED and code == status and "1..64" in msg
+    odd = (c_void_p * 1)(c_void_p((1 << 20) + 2))  # fp32 source 2 bytes off alignment
+    status, code, msg = _status_and_message(lib.fp8_cast_batch, 1, odd, arr, n, 1, c_void_p(0))
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "misaligned" in msg

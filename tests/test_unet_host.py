@@ -38,6 +38,23 @@ def test_forward_shape_without_fp8_on_cpu():
     assert torch.count_nonzero(y) == 0  # the output conv is zero-initialised (unet.py:355-357)
 
 
+def test_swap_linears_replaces_the_unet_linears_and_keeps_the_state_dict():
+    """The nn.Linear swap of the FP8 linear API: attention qkv / out projections, the blocks' time-embedding
+    projections and the time MLP become FP8Linear sharing their parameters; the state_dict is unchanged."""
+    from fp8_b200.linear import FP8Linear, swap_linears
+
+    torch.manual_seed(0)
+    model = UNet(UNetConfig(fp8_convs_enabled=True, fp8_scaling_type="delayed"))
+    before = {k: v.data_ptr() for k, v in model.state_dict().items()}
+    n_lin = sum(isinstance(m, torch.nn.Linear) for m in model.modules())
+    assert swap_linears(model) == n_lin == 7 * 2 + 22 + 2
+    assert all(isinstance(m, FP8Linear) for m in model.modules() if isinstance(m, torch.nn.Linear))
+    after = {k: v.data_ptr() for k, v in model.state_dict().items()}
+    assert after == before  # same keys, same tensors
+    model2 = UNet(UNetConfig())
+    assert swap_linears(model2, lambda name, lin: name in ("qkv", "out")) == 14
+
+
 def test_fp8_dispatch_follows_whitelist():
     model = UNet(UNetConfig(fp8_convs_enabled=True))
     convs = fp8_conv_modules(model)
