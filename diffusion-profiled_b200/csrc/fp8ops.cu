@@ -2093,3 +2093,70 @@ int fp8_cast_batch(int count, const void* const* src, void* const* dst, const in
 }
 
 }  // extern "C"
+
+// ======================================================================== join backward + dY quantize
+namespace {
+int add_scale_quant_grid(int64_t n, int sm_count) {
+  const int64_t per_cta = static_cast<int64_t>(kResampleThreads) * kJoinUnroll;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n / 8 + per_cta - 1) / per_cta, 4ll * sm_count)));
+}
+
+template <typename TA, typename TO>
+int launch_add_scale_bwd_quant(const void* dy, void* da, void* db, void* dbq, const DelayedSource& src,
+                               float* partials, const ScaleFold& fold, int64_t n, float inv, int grid,
+                               cudaStream_t cs) {
+  FP8_CUDA_TRY(launch_kernel(add_scale_bwd_quant_kernel<TA, TO>, dim3(static_cast<unsigned>(grid)),
+                             dim3(kResampleThreads), 0, cs, 1, kStreamingKernel, static_cast<const TO*>(dy), n / 8,
+                             inv, static_cast<TA*>(da), static_cast<uint16_t*>(db), static_cast<uint8_t*>(dbq), src,
+                             partials, fold));
+  count_launches(1);
+  return FP8_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t fp8_add_scale_bwd_quant_workspace_bytes(int64_t n) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  (void)cudaGetLastError();
+  if (n <= 0 || n % 8 != 0) return 0;
+  if (sms <= 0) sms = 148;
+  return static_cast<size_t>(add_scale_quant_grid(n, sms)) * sizeof(float);
+}
+
+int fp8_add_scale_bwd_quant(const void* dy, int y_dtype, void* da, int a_dtype, void* db_bf16, void* dbq_e4m3,
+                            float* window, int window_len, int64_t* window_pos, float* scale_used_out, int64_t n,
+                            float inv_divisor, void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+  FP8_REQUIRE(n > 0 && n % 8 == 0, FP8_ERR_UNSUPPORTED, "n must be a positive multiple of 8");
+  if (int r = check_resample(dy, y_dtype, "dy")) return r;
+  if (int r = check_resample(da, a_dtype, "da")) return r;
+  if (int r = check_resample(db_bf16, 0, "db")) return r;
+  FP8_REQUIRE(dbq_e4m3 != nullptr && aligned(dbq_e4m3, 16), FP8_ERR_INVALID_ARGUMENT,
+              "dbq must be non-NULL and 16-byte aligned");
+  if (int r = check_window(window, window_len, window_pos, scale_used_out)) return r;
+  DeviceState* st;
+  if (int r = device_state(&st)) return r;
+  const int grid = add_scale_quant_grid(n, st->sm_count);
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= grid * sizeof(float) && aligned(workspace, 4),
+              FP8_ERR_WORKSPACE, "join workspace too small: need %zu bytes", grid * sizeof(float));
+  const DelayedSource src{nullptr, window, window_len, scale_used_out};
+  const ScaleFold fold{fold_counter(st), nullptr, WindowUpdate{window, window_pos, window_len, 0}};
+  float* partials = static_cast<float*>(workspace);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  int r;
+  if (a_dtype)
+    r = y_dtype ? launch_add_scale_bwd_quant<float, float>(dy, da, db_bf16, dbq_e4m3, src, partials, fold, n,
+                                                            inv_divisor, grid, cs)
+                : launch_add_scale_bwd_quant<float, uint16_t>(dy, da, db_bf16, dbq_e4m3, src, partials, fold, n,
+                                                               inv_divisor, grid, cs);
+  else
+    r = y_dtype ? launch_add_scale_bwd_quant<uint16_t, float>(dy, da, db_bf16, dbq_e4m3, src, partials, fold, n,
+                                                               inv_divisor, grid, cs)
+                : launch_add_scale_bwd_quant<uint16_t, uint16_t>(dy, da, db_bf16, dbq_e4m3, src, partials, fold, n,
+                                                                  inv_divisor, grid, cs);
+  if (r) return r;
+  return ok();
+}
+
+}  // extern "C"

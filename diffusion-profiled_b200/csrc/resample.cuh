@@ -204,4 +204,59 @@ __global__ void __launch_bounds__(kResampleThreads) add_scale_bwd_kernel(const T
   }
 }
 
+// The join's backward when b is the bf16 output of a delayed-scaling FP8 conv:
+// db is also written as e4m3, cast with max(window) exactly as that conv's
+// backward would cast its output gradient (fp8_quantize_delayed_window with
+// advance = 0, reference fp8_kernels.py:883-889), with one |db| max per CTA that
+// the last CTA folds into db's scale (stored at window[*pos]; pos is kept).
+// Fewer, longer-lived CTAs than the plain passes (each first reduces the scale
+// history), with kJoinUnroll vectors of dy in flight per thread.
+constexpr int kJoinUnroll = 4;
+
+template <typename TA, typename TO, class Div>
+__device__ __forceinline__ uint32_t add_scale_bwd_quant_loop(const TO* __restrict__ dy, int64_t vecs, float inv,
+                                                             TA* __restrict__ da, uint16_t* __restrict__ db,
+                                                             uint8_t* __restrict__ dbq, const Div& div) {
+  uint32_t m2 = 0u;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < vecs;
+       i0 += kJoinUnroll * stride) {
+    XVec<TO> v[kJoinUnroll];
+#pragma unroll
+    for (int u = 0; u < kJoinUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      v[u] = i < vecs ? load_x8(dy, i) : zero_x8<TO>();
+    }
+#pragma unroll
+    for (int u = 0; u < kJoinUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= vecs) break;
+      float g[8];
+      unpack_x8(v[u], g);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) g[k] = round_to<TO>(g[k] * inv);
+      store_x8(da, i, g);
+      const uint4 h = pack8(g);
+      reinterpret_cast<uint4*>(db)[i] = h;
+      m2 = bf16x2_max(m2, absmax_vec2(h));
+      reinterpret_cast<uint2*>(dbq)[i] = cast_vec(h, div);
+    }
+  }
+  return m2;
+}
+
+template <typename TA, typename TO>
+__global__ void __launch_bounds__(kResampleThreads) add_scale_bwd_quant_kernel(
+    const TO* __restrict__ dy, int64_t vecs, float inv, TA* __restrict__ da, uint16_t* __restrict__ db,
+    uint8_t* __restrict__ dbq, DelayedSource src, float* __restrict__ partials, ScaleFold fold) {
+  pdl_wait();
+  const float s = delayed_scale<kResampleThreads>(src);
+  const uint32_t m2 = markstein_applies(s)  // s is uniform over the grid
+                          ? add_scale_bwd_quant_loop(dy, vecs, inv, da, db, dbq, make_markstein(s))
+                          : add_scale_bwd_quant_loop(dy, vecs, inv, da, db, dbq, DivF64(s));
+  const float m = block_max<kResampleThreads>(unpack_max2(m2));
+  if (threadIdx.x == 0) partials[blockIdx.x] = m;
+  fold_scale_if_last<kResampleThreads>(partials, fold);
+}
+
 }  // namespace fp8b

@@ -102,6 +102,12 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_up_cat_bwd": (
         c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                 c_void_p]),
+    "fp8_add_scale_bwd_quant_workspace_bytes": (c_size_t, [c_int64]),
+    "fp8_add_scale_bwd_quant": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int64,
+         c_float, c_void_p, c_size_t, c_void_p],
+    ),
     "fp8_cast_batch": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "fp8_up_cat_pair": (
         c_int,

@@ -26,10 +26,34 @@ def _weight_bf16(weight: torch.Tensor) -> torch.Tensor:
     return w if w.is_contiguous(memory_format=torch.channels_last) else w.contiguous(memory_format=torch.channels_last)
 
 
+def hand_off_dy(conv, db: torch.Tensor, dbq: torch.Tensor, sdy: torch.Tensor) -> None:
+    """Give the FP8 conv module ``conv`` the e4m3 cast of its output gradient ``db``, made (with the
+    history update) by the op that produced ``db``; its backward then skips its own quantize."""
+    conv._dy_handoff = (db, dbq, sdy)
+
+
+def _take_dy(owner, dy: torch.Tensor):
+    """(dyq, sdy) handed to ``owner`` for exactly this gradient tensor, else None.  The entry holds
+    ``db`` alive, so equal storage, shape and strides mean it is that tensor."""
+    entry = getattr(owner, "_dy_handoff", None) if owner is not None else None
+    if entry is None:
+        return None
+    owner._dy_handoff = None
+    db, dbq, sdy = entry
+    if (dy.data_ptr() == db.data_ptr() and dy.dtype == db.dtype and dy.shape == db.shape
+            and dy.stride() == db.stride()):
+        return dbq, sdy
+    return None
+
+
 def _conv_backward(ctx, dy, xq, wq, sx, sw):
-    dy = dy.to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
-    # the dY scale lands at the position the forward already advanced (fp8_kernels.py:883-889)
-    dyq, sdy = ops.quantize_delayed_window(dy, ctx.win_dy, ctx.pos, False)
+    pre = _take_dy(ctx.owner, dy)
+    if pre is not None:  # cast (and its history update) done by the producer of dy
+        dyq, sdy = pre
+    else:
+        dy = dy.to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+        # the dY scale lands at the position the forward already advanced (fp8_kernels.py:883-889)
+        dyq, sdy = ops.quantize_delayed_window(dy, ctx.win_dy, ctx.pos, False)
     # an fp32 weight gets the bf16 dW widened by the reduce pass, not by an autograd cast
     widen = ctx.w_dtype == torch.float32
     return ops.conv3x3_dgrad(dyq, wq, sdy, sw), ops.conv3x3_wgrad(xq, dyq, sx, sdy, 0, widen)
@@ -48,7 +72,8 @@ class ConvFP8Delayed(torch.autograd.Function):
 
     @staticmethod
     @custom_fwd(device_type="cuda")
-    def forward(ctx, x, weight, win_x, win_w, win_dy, pos, pre=None):
+    def forward(ctx, x, weight, win_x, win_w, win_dy, pos, pre=None, owner=None):
+        ctx.owner = owner
         x = x.to(torch.bfloat16)
         wq, sw = _weight_q(weight, win_w, pos, pre)
         xq, sx = ops.quantize_delayed_window(x, win_x, pos, True)
@@ -61,7 +86,7 @@ class ConvFP8Delayed(torch.autograd.Function):
     def backward(ctx, dy):
         xq, wq, sx, sw = ctx.saved_tensors
         dx, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
-        return dx, dw, None, None, None, None, None
+        return dx, dw, None, None, None, None, None, None
 
 
 class GroupNormActConvFP8Delayed(torch.autograd.Function):
@@ -70,7 +95,8 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
     @staticmethod
     @custom_fwd(device_type="cuda")
     def forward(ctx, x, gamma, beta, film, seed, weight, win_x, win_w, win_dy, pos, p: float, eps: float,
-                groups: int, pre=None):
+                groups: int, pre=None, owner=None):
+        ctx.owner = owner
         film2 = None if film is None else film.reshape(film.shape[0], -1)
         wq, sw = _weight_q(weight, win_w, pos, pre)
         xq, sx, stats = ops.gn_act_quant_fwd_window(x, gamma, beta, film2, seed, win_x, pos, True, p, eps, groups)
@@ -87,7 +113,7 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
         d_act, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
         dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
         dfilm = None if film_shape is None else dfilm.reshape(film_shape)
-        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None, None
+        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None, None, None
 
 
 def quantize_conv_weights(convs) -> None:
@@ -110,4 +136,4 @@ def quantize_conv_weights(convs) -> None:
         m._pre_weight = (out[i], out[k + i])
 
 
-__all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed", "quantize_conv_weights"]
+__all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed", "quantize_conv_weights", "hand_off_dy"]

@@ -827,6 +827,41 @@ def _(dy, inv, a_fp32, b_fp32):
             torch.empty_like(dy, dtype=torch.float32 if b_fp32 else torch.bfloat16))
 
 
+@torch.library.custom_op("fp8_b200::add_scale_bwd_quant", mutates_args=("window",))
+def add_scale_bwd_quant(dy: torch.Tensor, inv: float, a_fp32: bool, window: torch.Tensor,
+                        pos: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """add_scale_bwd with b bf16, plus db's delayed e4m3 cast -> (da, db, dbq, scale used).
+
+    dbq and the scale used are those of ``quantize_delayed_window(db, window, pos, False)`` (the
+    backward quantize of the FP8 conv whose output is b), and db's own scale lands at
+    ``window[pos]`` as there; db is not read again."""
+    dev = _require_cuda(dy, window, pos)
+    _check_window(window, pos, dev)
+    if dy.dim() != 4 or dy.dtype not in _DT:
+        raise RuntimeError("add_scale_bwd_quant expects a 4-D bfloat16 / float32 gradient")
+    dy = dy.contiguous(memory_format=torch.channels_last)
+    da = torch.empty_like(dy, dtype=torch.float32 if a_fp32 else torch.bfloat16)
+    db = torch.empty_like(dy, dtype=torch.bfloat16)
+    dbq = torch.empty_like(dy, dtype=FP8_DTYPE)
+    used = torch.empty((), device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_add_scale_bwd_quant_workspace_bytes(dy.numel()) // 4, 1), device=dev,
+                         dtype=torch.float32)
+        _lib.call("fp8_add_scale_bwd_quant", _ptr(dy), _DT[dy.dtype], _ptr(da), _DT[da.dtype], _ptr(db), _ptr(dbq),
+                  _ptr(window), window.numel(), _ptr(pos), _ptr(used), dy.numel(), float(inv), _ptr(ws),
+                  ws.numel() * 4, _stream(dev))
+    return da, db, dbq, used
+
+
+@add_scale_bwd_quant.register_fake
+def _(dy, inv, a_fp32, window, pos):
+    cl = torch.channels_last
+    return (torch.empty_like(dy, dtype=torch.float32 if a_fp32 else torch.bfloat16, memory_format=cl),
+            torch.empty_like(dy, dtype=torch.bfloat16, memory_format=cl),
+            torch.empty_like(dy, dtype=FP8_DTYPE, memory_format=cl), dy.new_empty((), dtype=torch.float32))
+
+
 @torch.library.custom_op("fp8_b200::gn_act_quant_fwd", mutates_args=())
 def gn_act_quant_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, film: torch.Tensor | None,
                      seed: torch.Tensor | None, prev_scale: torch.Tensor, p: float, eps: float,

@@ -20,6 +20,7 @@ import numpy as np
 import torch
 
 from . import ops
+from .delayed import hand_off_dy
 
 _FLOATS = (torch.bfloat16, torch.float32)
 
@@ -98,15 +99,22 @@ def upsample_cat_pair(a: torch.Tensor, s: torch.Tensor, factor: int) -> tuple[to
 
 class _AddScale(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a, b, inv: float):
+    def forward(ctx, a, b, inv: float, dy_target=None):
         ctx.cfg = (a.dtype, b.dtype, inv)
+        ctx.dy_target = dy_target
         return ops.add_scale(a, b, inv)
 
     @staticmethod
     def backward(ctx, dy):
         ta, tb, inv = ctx.cfg
-        da, db = ops.add_scale_bwd(dy, inv, ta == torch.float32, tb == torch.float32)
-        return da, db, None
+        conv = ctx.dy_target
+        if conv is not None and tb == torch.bfloat16 and dy.dim() == 4:
+            da, db, dbq, sdy = ops.add_scale_bwd_quant(dy, inv, ta == torch.float32, conv.amax_window_dy,
+                                                       conv.window_pos)
+            hand_off_dy(conv, db, dbq, sdy)
+        else:
+            da, db = ops.add_scale_bwd(dy, inv, ta == torch.float32, tb == torch.float32)
+        return da, db, None, None
 
 
 def _same_dense_layout(a: torch.Tensor, b: torch.Tensor) -> bool:
@@ -115,13 +123,17 @@ def _same_dense_layout(a: torch.Tensor, b: torch.Tensor) -> bool:
     return a.is_contiguous() or (a.dim() == 4 and a.is_contiguous(memory_format=torch.channels_last))
 
 
-def residual_join(a: torch.Tensor, b: torch.Tensor, divisor: float = math.sqrt(2.0)) -> torch.Tensor:
-    """``(a + b) / divisor`` as one pass, with the dtype and the two roundings of the torch ops (unet.py:161, :203)."""
+def residual_join(a: torch.Tensor, b: torch.Tensor, divisor: float = math.sqrt(2.0), dy_target=None) -> torch.Tensor:
+    """``(a + b) / divisor`` as one pass, with the dtype and the two roundings of the torch ops (unet.py:161, :203).
+
+    ``dy_target``: the delayed-scaling FP8 conv module whose output is ``b``; the backward then also
+    writes the e4m3 cast of b's gradient, with that conv's dY history update, and hands it over
+    (fp8_b200.delayed.hand_off_dy)."""
     if not (a.is_cuda and b.is_cuda and a.dtype in _FLOATS and b.dtype in _FLOATS and _same_dense_layout(a, b)
             and a.numel() % 8 == 0 and a.numel() > 0):
         return (a + b) / divisor
     inv = float(np.float32(1.0) / np.float32(divisor))  # torch: a host scalar divisor becomes an fp32 reciprocal
-    return _AddScale.apply(a, b, inv)
+    return _AddScale.apply(a, b, inv, dy_target)
 
 
 __all__ = ["downsample_nearest", "upsample_cat", "upsample_cat_pair", "resample_supported", "residual_join"]

@@ -89,7 +89,9 @@ class Conv2dFP8(nn.Module):
         self.device_scale_history = device_scale_history
         self.extended_shapes = extended_shapes
         self._pre_weight = None  # (wq, sw) from a batched weight quantize, for the next forward
-        self.used_fp8_delayed = False  # whether the last forward ran the delayed FP8 path
+        self.used_fp8_delayed = False  # whether a forward since the UNet's last one ran the delayed FP8 path
+        self.last_fp8_delayed = False  # whether the latest forward did (on device scale histories)
+        self._dy_handoff = None  # (dy, e4m3 dy, scale) from the op that produced this conv's output gradient
         if scaling_type not in ("current", "delayed"):
             raise ValueError(f"unknown FP8 scaling type {scaling_type!r}")
         self.conv = nn.Conv2d(in_channels, out_channels, (3, 3), stride=1, padding=1, bias=False)
@@ -115,6 +117,7 @@ class Conv2dFP8(nn.Module):
                 and key[0] % 128 == 0 and key[1] % 128 == 0)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        self.last_fp8_delayed = False
         if not self.uses_fp8(x):
             return self.conv(x)
         x = x.contiguous(memory_format=torch.channels_last)
@@ -122,9 +125,9 @@ class Conv2dFP8(nn.Module):
             return triton_conv2d_fp8(x, self.conv.weight)
         if self.device_scale_history:
             pre, self._pre_weight = self._pre_weight, None
-            self.used_fp8_delayed = True
+            self.used_fp8_delayed = self.last_fp8_delayed = True
             return ConvFP8Delayed.apply(x, self.conv.weight, self.amax_window_acts, self.amax_window_weights,
-                                        self.amax_window_dy, self.window_pos, pre)
+                                        self.amax_window_dy, self.window_pos, pre, self)
         with torch.no_grad():
             x_hist = torch.max(self.amax_window_acts)
             w_hist = torch.max(self.amax_window_weights)
@@ -143,6 +146,7 @@ class Conv2dFP8(nn.Module):
                        seed: torch.Tensor | None = None) -> torch.Tensor:
         """``self(group_norm_act(x, norm, film, p, seed))``.  With delayed scaling the
         group-norm pass writes this conv's e4m3 input itself (GroupNormActConvFP8)."""
+        self.last_fp8_delayed = False
         if not (self.scaling_type == "delayed" and self.uses_fp8(x) and fused_norm_supported(x, norm)):
             return self(group_norm_act(x, norm, film, p, seed))
         if p > 0.0 and seed is None:
@@ -150,11 +154,11 @@ class Conv2dFP8(nn.Module):
         x = x.contiguous(memory_format=torch.channels_last)
         if self.device_scale_history:
             pre, self._pre_weight = self._pre_weight, None
-            self.used_fp8_delayed = True
+            self.used_fp8_delayed = self.last_fp8_delayed = True
             return GroupNormActConvFP8Delayed.apply(
                 x, norm.weight, norm.bias, film, seed if p > 0.0 else None, self.conv.weight, self.amax_window_acts,
                 self.amax_window_weights, self.amax_window_dy, self.window_pos, float(p), float(norm.eps),
-                int(norm.num_groups), pre)
+                int(norm.num_groups), pre, self)
         with torch.no_grad():
             x_hist = torch.max(self.amax_window_acts)
             w_hist = torch.max(self.amax_window_weights)
@@ -233,7 +237,9 @@ class ResidualBlock(nn.Module):
         src = x if skip_in is None else skip_in
         skip = self.skip_connection(src) if w16 is None else F.conv2d(src, w16, self.skip_connection.bias)
         if self.fused_residual:
-            return residual_join(skip, h)
+            # h is conv_2's output: when that ran the delayed FP8 path, the join's backward also makes
+            # the e4m3 cast of h's gradient for conv_2's backward
+            return residual_join(skip, h, dy_target=self.conv_2 if self.conv_2.last_fp8_delayed else None)
         return (skip + h) / math.sqrt(2.0)
 
 

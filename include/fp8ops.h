@@ -367,6 +367,19 @@ int fp8_add_scale(const void* a, int a_dtype, const void* b, int b_dtype, void* 
 int fp8_add_scale_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* db, int b_dtype, int64_t n,
                       float inv_divisor, fp8_stream_t stream);
 
+/* fp8_add_scale_bwd where b is the bf16 output of a delayed-scaling FP8 conv:
+ * db (bf16) is also written as e4m3 to dbq, cast with max(window[0 ..
+ * window_len)) -- which goes to *scale_used_out -- and db's own scale (amax /
+ * 448) is stored at window[*window_pos] with the position kept: bit for bit
+ * what the conv's backward gets from fp8_quantize_delayed_window(db, window,
+ * window_pos, advance = 0) (reference Conv2dFP8Specialized.backward,
+ * fp8_kernels.py:875-889), without reading db again.  Workspace:
+ * fp8_add_scale_bwd_quant_workspace_bytes(n). */
+size_t fp8_add_scale_bwd_quant_workspace_bytes(int64_t n);
+int fp8_add_scale_bwd_quant(const void* dy, int y_dtype, void* da, int a_dtype, void* db_bf16, void* dbq_e4m3,
+                            float* window, int window_len, int64_t* window_pos, float* scale_used_out, int64_t n,
+                            float inv_divisor, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
+
 /* Workspace bytes of fp8_gn_act_quant_fwd. */
 size_t fp8_gn_act_quant_workspace_bytes(int n, int hw, int c);
 

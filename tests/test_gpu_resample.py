@@ -168,3 +168,46 @@ def test_residual_join_matches_torch_bitwise(cuda, ta, tb):
         res.append((y.detach(), a.grad, b.grad))
     for u, v in zip(*res):
         assert u.dtype == v.dtype and torch.equal(u, v)
+
+
+@pytest.mark.parametrize("ta,ty", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32)])
+def test_join_backward_quantize_matches_separate_quantize(cuda, ta, ty):
+    """add_scale_bwd_quant = add_scale_bwd + the FP8 conv's backward quantize of db
+    (quantize_delayed_window(db, window, pos, advance=False)): same gradients, e4m3 bytes, scale used,
+    history and position."""
+    from fp8_b200 import ops
+
+    dy = _t((8, 256, 16, 16), ty, 31, cuda)
+    inv = 0.70710677
+    res = []
+    for fused in (True, False):
+        win = torch.zeros(16, device=cuda)
+        win[:5] = torch.tensor([1e-3, 4e-3, 2e-3, 0.0, 1e-4])
+        pos = torch.tensor(3, dtype=torch.int64, device=cuda)
+        if fused:
+            da, db, dbq, used = ops.add_scale_bwd_quant(dy, inv, ta == torch.float32, win, pos)
+        else:
+            da, db = ops.add_scale_bwd(dy, inv, ta == torch.float32, False)
+            dbq, used = ops.quantize_delayed_window(db, win, pos, False)
+        res.append((da, db, dbq.view(torch.uint8), used, win, pos))
+    for u, v in zip(*res):
+        assert u.dtype == v.dtype and torch.equal(u, v)
+    assert res[0][0].dtype == ta and res[0][1].dtype == torch.bfloat16
+    assert res[0][5].item() == 3  # the position is not stepped
+
+
+def test_dy_handoff_is_taken_once_and_only_for_its_tensor(cuda):
+    from fp8_b200.delayed import _take_dy, hand_off_dy
+    from fp8_b200.unet import Conv2dFP8
+
+    conv = Conv2dFP8(128, 128, True, "delayed", 16).to(cuda)
+    db = torch.randn(2, 128, 8, 8, device=cuda).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    dbq = torch.zeros_like(db, dtype=torch.float8_e4m3fn)
+    s = torch.tensor(0.5, device=cuda)
+    hand_off_dy(conv, db, dbq, s)
+    assert _take_dy(conv, db.clone()) is None  # another tensor: not used, and the entry is dropped
+    assert _take_dy(conv, db) is None
+    hand_off_dy(conv, db, dbq, s)
+    got = _take_dy(conv, db)
+    assert got is not None and got[0] is dbq and got[1] is s
+    assert _take_dy(conv, db) is None  # taken once
