@@ -678,10 +678,17 @@ int launch_gn_fwd(const TX* x, GnShape sh, float* part, const GnActParams& q, fl
 
 template <typename TX>
 int launch_gn_bwd(const TX* x, const uint16_t* dy, GnShape sh, const float* stats, const GnActParams& q,
-                  float* part, float* totals, TX* dx, size_t s1, size_t s2, int sm_count, cudaStream_t cs) {
+                  float* part, float* totals, TX* dx, size_t s1, size_t s2, int sm_count, cudaStream_t cs,
+                  const GnOut* quant = nullptr) {
   const bool drop = q.seed != nullptr && q.p > 0.0f;
   auto k1 = drop ? gn_act_bwd_reduce_kernel<TX, true> : gn_act_bwd_reduce_kernel<TX, false>;
-  auto k2 = drop ? gn_act_bwd_apply_kernel<TX, true> : gn_act_bwd_apply_kernel<TX, false>;
+  auto k2 = drop ? gn_act_bwd_apply_kernel<TX, true, false> : gn_act_bwd_apply_kernel<TX, false, false>;
+  if (quant != nullptr) {
+    if constexpr (sizeof(TX) == 2)
+      k2 = drop ? gn_act_bwd_apply_kernel<TX, true, true> : gn_act_bwd_apply_kernel<TX, false, true>;
+    else
+      return set_error(FP8_ERR_UNSUPPORTED, "the e4m3 group-norm gradient needs a bf16 x");
+  }
   FP8_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s1)));
   FP8_CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(s2)));
   int sl1 = 1, sl2 = 1;
@@ -693,7 +700,8 @@ int launch_gn_bwd(const TX* x, const uint16_t* dy, GnShape sh, const float* stat
                              sh, stats, q, part));
   sh.slices = sl2;
   FP8_CUDA_TRY(launch_kernel(k2, dim3(static_cast<unsigned>(sh.n * sl2)), block, s2, cs, 1, kStreamingKernel, x, dy,
-                             sh, stats, q, static_cast<const float*>(part), totals, dx));
+                             sh, stats, q, static_cast<const float*>(part), totals, dx,
+                             quant != nullptr ? *quant : GnOut{nullptr, nullptr, DelayedSource{}, nullptr, ScaleFold{}}));
   count_launches(2);
   return FP8_OK;
 }
@@ -1412,6 +1420,39 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
                               static_cast<uint16_t*>(dx), s1, s2, st->sm_count, cs))
       return s;
   }
+  FP8_CUDA_TRY(cudaGetLastError());
+  return ok();
+}
+
+size_t fp8_gn_act_bwd_quant_workspace_bytes(int n, int hw, int c) { return fp8_gn_act_quant_workspace_bytes(n, hw, c); }
+
+int fp8_gn_act_bwd_quant(const void* x, const void* dy, const float* gamma, const float* beta, const void* film,
+                         int film_ld, const int64_t* seed, float p, float eps, const float* stats, float* totals,
+                         void* dx, void* dxq, float* window, int window_len, int64_t* window_pos,
+                         float* scale_used_out, int n, int hw, int c, int groups, void* workspace,
+                         size_t workspace_bytes, fp8_stream_t stream) {
+  if (int s = check_gn_args(x, dx, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
+  FP8_REQUIRE(dy != nullptr && aligned(dy, 16), FP8_ERR_INVALID_ARGUMENT, "dy must be 16-byte aligned");
+  FP8_REQUIRE(dxq != nullptr && aligned(dxq, 16), FP8_ERR_INVALID_ARGUMENT, "dxq must be 16-byte aligned");
+  FP8_REQUIRE(stats != nullptr && totals != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats / totals");
+  if (int s = check_window(window, window_len, window_pos, scale_used_out)) return s;
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  const size_t gn_bytes = gn_workspace(n, hw, c, st->sm_count);
+  const size_t need =
+      gn_bytes + ((static_cast<size_t>(n) * gn_slices_cap(n, hw, c, st->sm_count) * sizeof(float) + 15) & ~size_t(15));
+  FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
+              "group-norm workspace too small: need %zu bytes", need);
+  const GnShape sh{n, hw, c, groups, 1, 1};
+  GnActParams q{gamma, beta, static_cast<const uint16_t*>(film), film_ld, seed, p, eps};
+  float* part = static_cast<float*>(workspace);
+  float* amax_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gn_bytes);
+  const GnOut o{nullptr, static_cast<uint8_t*>(dxq), DelayedSource{nullptr, window, window_len, scale_used_out},
+                amax_part, ScaleFold{fold_counter(st), nullptr, WindowUpdate{window, window_pos, window_len, 0}}};
+  if (int s = launch_gn_bwd(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(dy), sh, stats, q, part,
+                            totals, static_cast<uint16_t*>(dx), gn_bwd_reduce_smem(c, groups),
+                            gn_bwd_apply_smem(c, groups), st->sm_count, reinterpret_cast<cudaStream_t>(stream), &o))
+    return s;
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
 }

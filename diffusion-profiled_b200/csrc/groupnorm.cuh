@@ -531,15 +531,81 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_reduce
   for (int i = threadIdx.x; i < 2 * s.c; i += blockDim.x) out[i] = red[i];
 }
 
+// Per-thread group terms of the backward apply for its 8 channels.
+struct GnBwdGroup {
+  float gk[8], m1[8], m2[8];
+};
+
+// The streaming loop of the backward apply over this thread's pixel rows.  QUANT:
+// dx (bf16) is also cast to e4m3 with `div`; returns the packed max |dx|.
+template <typename TX, bool DROP, bool QUANT, class Div>
+__device__ __forceinline__ uint32_t gn_bwd_apply_rows(const TX* __restrict__ x, const uint16_t* __restrict__ dy,
+                                                      TX* __restrict__ dx, const GnShape& s, const GnThread& t,
+                                                      const GnActParams& q, const GnBwdCoeffs& k,
+                                                      const GnBwdGroup& gm, const GnOut& o, const Div& div) {
+  const uint64_t seed = DROP ? static_cast<uint64_t>(*q.seed) : 0ull;
+  const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
+  const float keep_scale = DROP ? 1.0f / (1.0f - q.p) : 1.0f;
+  const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
+  const TX* xs = x + base * 8;
+  const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
+  TX* os = dx + base * 8;
+  uint32_t qm = 0u;
+  for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollBwd * t.rows) {
+    XVec<TX> vx[kGnUnrollBwd];
+    uint4 vd[kGnUnrollBwd];
+#pragma unroll
+    for (int u = 0; u < kGnUnrollBwd; ++u) {
+      const int pu = p + u * t.rows;
+      const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
+      vx[u] = pu < t.p1 ? load_x8(xs, vi) : zero_x8<TX>();
+      vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kGnUnrollBwd; ++u) {
+      const int pu = p + u * t.rows;
+      if (pu >= t.p1) break;
+      const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
+      float xf[8], gf[8], r[8];
+      unpack_x8(vx[u], xf);
+      unpack8(vd[u], gf);
+      const uint32_t keep = DROP ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float df = gn_df<DROP>(fmaf(k.a[j], xf[j], k.b[j]), gf[j], keep, j, keep_scale);
+        const float xhat = fmaf(xf[j], k.rs[j], k.nmr[j]);
+        r[j] = k.rs[j] * (gm.gk[j] * df - gm.m1[j] - xhat * gm.m2[j]);
+      }
+      if constexpr (QUANT) {
+        const uint4 h = pack8(r);
+        reinterpret_cast<uint4*>(os)[vi] = h;
+        qm = bf16x2_max(qm, absmax_vec2(h));
+        reinterpret_cast<uint2*>(o.q)[base + vi] = cast_vec(h, div);
+      } else {
+        store_x8(os, vi, r);
+      }
+    }
+  }
+  return qm;
+}
+
 // totals[n * 3C + {0, C, 2C} + c] = sum df, sum df z, sum df xhat over the sample
 // (written by slice 0); dx = rstd * (gamma (s+1) df - mean_g[gamma (s+1) df]
-// - xhat * mean_g[gamma (s+1) df xhat]).
-template <typename TX, bool DROP>
+// - xhat * mean_g[gamma (s+1) df xhat]).  QUANT (the input of a delayed-scaling
+// FP8 conv's output gradient, x being that conv's bf16 output): dx is also cast to
+// e4m3 with the delayed scale of o.prev_scale, exactly as the conv's backward
+// quantize would cast it, and the last CTA folds the per-CTA max |dx| into dx's
+// scale (o.fold).
+template <typename TX, bool DROP, bool QUANT>
 __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
-    GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx) {
+    GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx, GnOut o) {
+  static_assert(!QUANT || sizeof(TX) == 2, "the e4m3 dx is cast from a bf16 dx");
   extern __shared__ float gn_smem[];
   pdl_wait();
+  // the delayed scale of the e4m3 dx first: with a scale history every thread takes part in its max
+  float qs = 1.0f;
+  if constexpr (QUANT) qs = delayed_scale<kGnThreads>(o.prev_scale);
   float* A = gn_smem;
   float* B = A + s.c;
   float* mean_g = B + s.c;
@@ -589,52 +655,31 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
     g2[g] = s3 * inv_m;
   }
   __syncthreads();
-  if (t.r >= t.rows) return;
-  GnBwdCoeffs k;
-  gn_bwd_coeffs(t, s, A, B, mean_g, rstd_g, k);
-  float gk[8], m1[8], m2[8];
+  uint32_t qm = 0u;
+  if (t.r < t.rows) {
+    GnBwdCoeffs k;
+    gn_bwd_coeffs(t, s, A, B, mean_g, rstd_g, k);
+    GnBwdGroup gm;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int c = t.v * 8 + j;
-    const int g = c / cg;
-    gk[j] = gs[c];
-    m1[j] = g1[g];
-    m2[j] = g2[g];
+    for (int j = 0; j < 8; ++j) {
+      const int c = t.v * 8 + j;
+      const int g = c / cg;
+      gm.gk[j] = gs[c];
+      gm.m1[j] = g1[g];
+      gm.m2[j] = g2[g];
+    }
+    if constexpr (QUANT) {
+      qm = markstein_applies(qs)  // uniform over the grid
+               ? gn_bwd_apply_rows<TX, DROP, true>(x, dy, dx, s, t, q, k, gm, o, make_markstein(qs))
+               : gn_bwd_apply_rows<TX, DROP, true>(x, dy, dx, s, t, q, k, gm, o, DivF64(qs));
+    } else {
+      gn_bwd_apply_rows<TX, DROP, false>(x, dy, dx, s, t, q, k, gm, o, NoCast{});
+    }
   }
-  const uint64_t seed = DROP ? static_cast<uint64_t>(*q.seed) : 0ull;
-  const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
-  const float keep_scale = DROP ? 1.0f / (1.0f - q.p) : 1.0f;
-  const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
-  const TX* xs = x + base * 8;
-  const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
-  TX* os = dx + base * 8;
-  for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollBwd * t.rows) {
-    XVec<TX> vx[kGnUnrollBwd];
-    uint4 vd[kGnUnrollBwd];
-#pragma unroll
-    for (int u = 0; u < kGnUnrollBwd; ++u) {
-      const int pu = p + u * t.rows;
-      const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
-      vx[u] = pu < t.p1 ? load_x8(xs, vi) : zero_x8<TX>();
-      vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int u = 0; u < kGnUnrollBwd; ++u) {
-      const int pu = p + u * t.rows;
-      if (pu >= t.p1) break;
-      const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
-      float xf[8], gf[8], o[8];
-      unpack_x8(vx[u], xf);
-      unpack8(vd[u], gf);
-      const uint32_t keep = DROP ? dropout_keep8(seed, (base + vi) * 8, thresh) : 0xFFu;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float df = gn_df<DROP>(fmaf(k.a[j], xf[j], k.b[j]), gf[j], keep, j, keep_scale);
-        const float xhat = fmaf(xf[j], k.rs[j], k.nmr[j]);
-        o[j] = k.rs[j] * (gk[j] * df - m1[j] - xhat * m2[j]);
-      }
-      store_x8(os, vi, o);
-    }
+  if constexpr (QUANT) {
+    const float m = block_max<kGnThreads>(unpack_max2(qm));
+    if (threadIdx.x == 0) o.amax_part[blockIdx.x] = m;
+    fold_scale_if_last<kGnThreads>(o.amax_part, o.fold);
   }
 }
 

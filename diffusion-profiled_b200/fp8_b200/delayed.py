@@ -95,8 +95,11 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
     @staticmethod
     @custom_fwd(device_type="cuda")
     def forward(ctx, x, gamma, beta, film, seed, weight, win_x, win_w, win_dy, pos, p: float, eps: float,
-                groups: int, pre=None, owner=None):
+                groups: int, pre=None, owner=None, x_owner=None):
         ctx.owner = owner
+        # x_owner: the delayed FP8 conv whose (bf16) output x is; the norm's backward then also makes
+        # the e4m3 cast of x's gradient for that conv's backward
+        ctx.x_owner = x_owner if x.dtype == torch.bfloat16 else None
         film2 = None if film is None else film.reshape(film.shape[0], -1)
         wq, sw = _weight_q(weight, win_w, pos, pre)
         xq, sx, stats = ops.gn_act_quant_fwd_window(x, gamma, beta, film2, seed, win_x, pos, True, p, eps, groups)
@@ -111,9 +114,15 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
         x, gamma, beta, film2, seed, stats, xq, wq, sx, sw = ctx.saved_tensors
         p, eps, groups, film_shape = ctx.cfg
         d_act, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
-        dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
+        conv = ctx.x_owner
+        if conv is not None:
+            dx, dgamma, dbeta, dfilm, dxq, sdx = ops.gn_act_bwd_quant(
+                x, d_act, gamma, beta, film2, seed, stats, p, eps, groups, conv.amax_window_dy, conv.window_pos)
+            hand_off_dy(conv, dx, dxq, sdx)
+        else:
+            dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
         dfilm = None if film_shape is None else dfilm.reshape(film_shape)
-        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None, None, None
+        return dx, dgamma, dbeta, dfilm, None, dw, None, None, None, None, None, None, None, None, None, None
 
 
 def quantize_conv_weights(convs) -> None:

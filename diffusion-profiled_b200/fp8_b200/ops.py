@@ -951,6 +951,54 @@ def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: tor
     return dx, dgamma, dbeta, dfilm
 
 
+@torch.library.custom_op("fp8_b200::gn_act_bwd_quant", mutates_args=("window",))
+def gn_act_bwd_quant(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                     film: torch.Tensor | None, seed: torch.Tensor | None, stats: torch.Tensor, p: float, eps: float,
+                     groups: int, window: torch.Tensor, pos: torch.Tensor
+                     ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """gn_act_bwd for a bf16 x, plus dx's delayed e4m3 cast -> (dx, dgamma, dbeta, dfilm, dxq, scale used).
+
+    dxq and the scale used are those of ``quantize_delayed_window(dx, window, pos, False)`` (the backward
+    quantize of the FP8 conv whose output is x), and dx's own scale lands at ``window[pos]``."""
+    dev = _require_cuda(x, dy, gamma, beta, stats, window, pos)
+    n, c, hw = _gn_check(x, gamma, beta, film, groups)
+    _check_window(window, pos, dev)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError("gn_act_bwd_quant expects a bfloat16 x")
+    dy = dy.contiguous(memory_format=torch.channels_last)
+    if dy.dtype != torch.bfloat16 or dy.shape != x.shape:
+        raise RuntimeError("dy must be a bfloat16 tensor shaped like x")
+    dx = torch.empty_like(x, memory_format=torch.channels_last)
+    dxq = torch.empty_like(x, dtype=FP8_DTYPE, memory_format=torch.channels_last)
+    used = torch.empty((), device=dev, dtype=torch.float32)
+    totals = torch.empty((n, 3, c), device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(lib.fp8_gn_act_bwd_quant_workspace_bytes(n, hw, c) // 4, 4), device=dev,
+                         dtype=torch.float32)
+        _lib.check(lib.fp8_gn_act_bwd_quant(
+            _ptr(x), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), _film_ld(film, c), _ptr(seed), float(p),
+            float(eps), _ptr(stats), _ptr(totals), _ptr(dx), _ptr(dxq), _ptr(window), window.numel(), _ptr(pos),
+            _ptr(used), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)), "fp8_gn_act_bwd_quant")
+        dgamma = torch.empty((c,), device=dev, dtype=torch.float32)
+        dbeta = torch.empty((c,), device=dev, dtype=torch.float32)
+        dfilm = torch.empty((n, 2 * c) if film is not None else (0,), device=dev, dtype=torch.bfloat16)
+        _lib.check(lib.fp8_gn_param_grads(_ptr(totals), _ptr(film), _film_ld(film, c), n, c, _ptr(dgamma), _ptr(dbeta),
+                                          _ptr(dfilm) if film is not None else None, 2 * c, _stream(dev)),
+                   "fp8_gn_param_grads")
+    return dx, dgamma, dbeta, dfilm, dxq, used
+
+
+@gn_act_bwd_quant.register_fake
+def _(x, dy, gamma, beta, film, seed, stats, p, eps, groups, window, pos):
+    n, c = x.shape[0], x.shape[1]
+    cl = torch.channels_last
+    return (torch.empty_like(x, memory_format=cl), x.new_empty((c,), dtype=torch.float32),
+            x.new_empty((c,), dtype=torch.float32),
+            x.new_empty((n, 2 * c) if film is not None else (0,), dtype=torch.bfloat16),
+            torch.empty_like(x, dtype=FP8_DTYPE, memory_format=cl), x.new_empty((), dtype=torch.float32))
+
+
 @gn_act_bwd.register_fake
 def _(x, dy, gamma, beta, film, seed, stats, p, eps, groups):
     n, c = x.shape[0], x.shape[1]

@@ -143,9 +143,11 @@ class Conv2dFP8(nn.Module):
 
 
     def forward_normed(self, x: torch.Tensor, norm: nn.GroupNorm, film: torch.Tensor | None = None, p: float = 0.0,
-                       seed: torch.Tensor | None = None) -> torch.Tensor:
+                       seed: torch.Tensor | None = None, x_owner: "Conv2dFP8 | None" = None) -> torch.Tensor:
         """``self(group_norm_act(x, norm, film, p, seed))``.  With delayed scaling the
-        group-norm pass writes this conv's e4m3 input itself (GroupNormActConvFP8)."""
+        group-norm pass writes this conv's e4m3 input itself (GroupNormActConvFP8).
+        ``x_owner``: the delayed FP8 conv that produced x, whose backward then receives the
+        e4m3 cast of x's gradient from the norm's backward."""
         self.last_fp8_delayed = False
         if not (self.scaling_type == "delayed" and self.uses_fp8(x) and fused_norm_supported(x, norm)):
             return self(group_norm_act(x, norm, film, p, seed))
@@ -158,7 +160,7 @@ class Conv2dFP8(nn.Module):
             return GroupNormActConvFP8Delayed.apply(
                 x, norm.weight, norm.bias, film, seed if p > 0.0 else None, self.conv.weight, self.amax_window_acts,
                 self.amax_window_weights, self.amax_window_dy, self.window_pos, float(p), float(norm.eps),
-                int(norm.num_groups), pre, self)
+                int(norm.num_groups), pre, self, x_owner)
         with torch.no_grad():
             x_hist = torch.max(self.amax_window_acts)
             w_hist = torch.max(self.amax_window_weights)
@@ -222,7 +224,8 @@ class ResidualBlock(nn.Module):
             h = self.conv_1.forward_normed(x, self.norm1)
             if fused_norm_supported(h, self.norm2) and emb.dtype == torch.bfloat16:
                 p = self.dropout.p if self.training else 0.0
-                h = self.conv_2.forward_normed(h, self.norm2, emb, p, self._next_seed() if p > 0.0 else None)
+                h = self.conv_2.forward_normed(h, self.norm2, emb, p, self._next_seed() if p > 0.0 else None,
+                                               x_owner=self.conv_1 if self.conv_1.last_fp8_delayed else None)
                 return self._join(x, h)
         else:
             h = self.conv_1(F.silu(self.norm1(x)))

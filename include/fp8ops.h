@@ -251,6 +251,21 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
                    float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
                    size_t workspace_bytes, fp8_stream_t stream);
 
+/* fp8_gn_act_bwd for a bf16 x that is the output of a delayed-scaling FP8 conv
+ * (the residual block's conv_1 before norm2, unet.py:151-159): dx (bf16) is
+ * also written as e4m3 to dxq, cast with max(window[0 .. window_len)) -- which
+ * goes to *scale_used_out -- and dx's own scale is stored at
+ * window[*window_pos] (position kept): bit for bit what that conv's backward
+ * gets from fp8_quantize_delayed_window(dx, window, window_pos, advance = 0)
+ * (reference fp8_kernels.py:875-889), without reading dx again.  Workspace:
+ * fp8_gn_act_bwd_quant_workspace_bytes. */
+size_t fp8_gn_act_bwd_quant_workspace_bytes(int n, int hw, int c);
+int fp8_gn_act_bwd_quant(const void* x, const void* dy, const float* gamma, const float* beta, const void* film,
+                         int film_ld, const int64_t* seed, float p, float eps, const float* stats, float* totals,
+                         void* dx, void* dxq, float* window, int window_len, int64_t* window_pos,
+                         float* scale_used_out, int n, int hw, int c, int groups, void* workspace,
+                         size_t workspace_bytes, fp8_stream_t stream);
+
 /* LayerNorm over the last dimension of `tokens` rows of c channels (the
  * attention-block norm of reference unet.py:174, :187, nn.LayerNorm(C) with
  * elementwise affine): y = bf16((x - mean) * rstd * gamma + beta), rstd =

@@ -72,7 +72,7 @@ def _block_pair(cuda, cin, cout, fused):
 
         for m in (blk.conv_1, blk.conv_2):
             m.device_scale_history = False
-            m.forward_normed = (lambda mod: lambda x, norm, film=None, p=0.0, seed=None:
+            m.forward_normed = (lambda mod: lambda x, norm, film=None, p=0.0, seed=None, x_owner=None:
                                 mod(group_norm_act(x, norm, film, p, seed)))(m)
     return blk
 
@@ -180,3 +180,35 @@ def test_batched_weight_quantize_matches_per_conv(cuda):
         assert torch.equal(u, v)
     assert torch.equal(ha, hb)
     assert ((ga - gb).abs() <= 2.0 ** -7 * gb.abs() + 1e-4 * gb.abs().max()).all()
+
+
+@pytest.mark.parametrize("film,p", [(False, 0.0), (True, 0.1)])
+@pytest.mark.parametrize("c,h,w", [(128, 32, 32), (256, 16, 16), (256, 8, 8)])
+def test_gn_act_bwd_quant_matches_bwd_then_conv_quantize(cuda, c, h, w, film, p):
+    """gn_act_bwd_quant = gn_act_bwd + the backward quantize of the FP8 conv that produced x
+    (quantize_delayed_window(dx, window, pos, advance=False)): the same gradients, e4m3 bytes, scale
+    used, history and position."""
+    from fp8_b200 import ops
+
+    x, norm, f = _inputs(4, c, h, w, film, seed=c + h + 3, device=cuda)
+    seed = torch.tensor(99, dtype=torch.int64, device=cuda) if p > 0 else None
+    _, stats = ops.gn_act_fwd(x, norm.weight, norm.bias, f, seed, p, norm.eps, 32)
+    g = torch.Generator().manual_seed(c)
+    dy = (torch.randn(x.shape, generator=g) * 1e-2).to(torch.bfloat16).to(cuda).contiguous(
+        memory_format=torch.channels_last)
+    res = []
+    for fused in (True, False):
+        win = torch.zeros(32, device=cuda)
+        win[:3] = torch.tensor([2e-6, 1e-5, 5e-6])
+        pos = torch.tensor(7, dtype=torch.int64, device=cuda)
+        args = (x, dy, norm.weight, norm.bias, f, seed, stats, p, norm.eps, 32)
+        if fused:
+            dx, dg, db, dfilm, dxq, used = ops.gn_act_bwd_quant(*args, win, pos)
+        else:
+            dx, dg, db, dfilm = ops.gn_act_bwd(*args)
+            dxq, used = ops.quantize_delayed_window(dx, win, pos, False)
+        res.append((dx, dg, db, dfilm, dxq.view(torch.uint8), used, win, pos))
+    for u, v in zip(*res):
+        assert u.dtype == v.dtype and torch.equal(u, v)
+    assert res[0][7].item() == 7
+    assert ops.device_error() == 0
