@@ -14,7 +14,13 @@
  * Reference interfaces (fattorib/diffusion-profiled, diffusion/fp8_kernels.py)
  * that each entry point replaces are cited per function.  The reference is
  * Python + Triton; its "FFI" is the Python call into the Triton launcher, so the
- * binding a maintainer adds is the ctypes layer shown in INTEGRATION.md.
+ * binding a maintainer adds is a ctypes layer (diffusion-profiled_b200/fp8_b200/
+ * _lib.py is that layer: one restype / argtypes entry per function below).
+ *
+ * Delayed-scaling casts fold their scale in the last CTA of the launch: each such
+ * launch takes the next of 8192 ticket counters (per device) in rotation and
+ * leaves it at zero.  Launches that can run at the same time (on different
+ * streams) must be fewer than 8192 folding launches apart in issue order.
  */
 #ifndef FP8OPS_H_
 #define FP8OPS_H_

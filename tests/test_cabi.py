@@ -194,3 +194,38 @@ def test_cast_batch_validates_without_touching_cuda():
     odd = (c_void_p * 1)(c_void_p((1 << 20) + 2))  # fp32 source 2 bytes off alignment
     status, code, msg = _status_and_message(lib.fp8_cast_batch, 1, odd, arr, n, 1, c_void_p(0))
     assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "misaligned" in msg
+
+
+def test_new_fused_entry_points_validate_without_touching_cuda():
+    """The producer-side dY casts, the paired up_cat and the widened dW reject bad arguments before any
+    CUDA call (status and message, no device work)."""
+    lib = _lib.load()
+    fake = c_void_p(1 << 20)
+    odd = c_void_p((1 << 20) + 8)
+    null = c_void_p(0)
+    # join backward + quantize: n not a multiple of 8; a NULL / misaligned e4m3 output; a bad history
+    status, code, msg = _status_and_message(lib.fp8_add_scale_bwd_quant, fake, 0, fake, 0, fake, fake, fake, 16,
+                                            fake, fake, 12, ctypes.c_float(0.7), fake, 64, null)
+    assert status == _lib.FP8_ERR_UNSUPPORTED and code == status and "multiple of 8" in msg
+    status, code, msg = _status_and_message(lib.fp8_add_scale_bwd_quant, fake, 0, fake, 0, fake, odd, fake, 16,
+                                            fake, fake, 64, ctypes.c_float(0.7), fake, 64, null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "dbq" in msg
+    status, code, msg = _status_and_message(lib.fp8_add_scale_bwd_quant, fake, 0, fake, 0, fake, fake, fake, 0,
+                                            fake, fake, 64, ctypes.c_float(0.7), fake, 64, null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "history" in msg
+    assert lib.fp8_add_scale_bwd_quant_workspace_bytes(12) == 0
+    # group-norm backward + quantize: unsupported channel count
+    status, code, msg = _status_and_message(
+        lib.fp8_gn_act_bwd_quant, fake, fake, fake, fake, null, 0, null, ctypes.c_float(0.0), ctypes.c_float(1e-5),
+        fake, fake, fake, fake, fake, 16, fake, fake, 2, 64, 12, 4, fake, 1 << 20, null)
+    assert status == _lib.FP8_ERR_UNSUPPORTED and "c % 8" in msg
+    # paired up_cat: a misaligned bf16 copy
+    status, code, msg = _status_and_message(lib.fp8_up_cat_pair, fake, 0, fake, 0, fake, odd, 1, 8, 8, 16, 16, 2, null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "y_bf16" in msg
+    status, code, msg = _status_and_message(lib.fp8_up_cat_pair_bwd, fake, null, fake, 0, fake, 0, 1, 8, 8, 16, 16, 2,
+                                            null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "dy_bf16" in msg
+    # widened dW: unsupported channels, as fp8_conv3x3_wgrad
+    status, code, msg = _status_and_message(lib.fp8_conv3x3_wgrad_f32, null, null, null, null, null, 2, 8, 8, 100, 128,
+                                            0, null, 0, null)
+    assert status == _lib.FP8_ERR_UNSUPPORTED and "multiples of 128" in msg
