@@ -679,7 +679,7 @@ int launch_gn_fwd(const TX* x, GnShape sh, float* part, const GnActParams& q, fl
 template <typename TX>
 int launch_gn_bwd(const TX* x, const uint16_t* dy, GnShape sh, const float* stats, const GnActParams& q,
                   float* part, float* totals, TX* dx, size_t s1, size_t s2, int sm_count, cudaStream_t cs,
-                  const GnOut* quant = nullptr) {
+                  const GnOut* quant = nullptr, const TX* dx_add = nullptr) {
   const bool drop = q.seed != nullptr && q.p > 0.0f;
   auto k1 = drop ? gn_act_bwd_reduce_kernel<TX, true> : gn_act_bwd_reduce_kernel<TX, false>;
   auto k2 = drop ? gn_act_bwd_apply_kernel<TX, true, false> : gn_act_bwd_apply_kernel<TX, false, false>;
@@ -701,7 +701,8 @@ int launch_gn_bwd(const TX* x, const uint16_t* dy, GnShape sh, const float* stat
   sh.slices = sl2;
   FP8_CUDA_TRY(launch_kernel(k2, dim3(static_cast<unsigned>(sh.n * sl2)), block, s2, cs, 1, kStreamingKernel, x, dy,
                              sh, stats, q, static_cast<const float*>(part), totals, dx,
-                             quant != nullptr ? *quant : GnOut{nullptr, nullptr, DelayedSource{}, nullptr, ScaleFold{}}));
+                             quant != nullptr ? *quant : GnOut{nullptr, nullptr, DelayedSource{}, nullptr, ScaleFold{}},
+                             dx_add));
   count_launches(2);
   return FP8_OK;
 }
@@ -1393,11 +1394,15 @@ int fp8_gn_act_quant_fwd_window(const void* x, int x_fp32, const float* gamma, c
                            workspace_bytes, stream);
 }
 
-int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,
-                   const void* film, int film_ld, const int64_t* seed, float p, float eps, const float* stats,
-                   float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
-                   size_t workspace_bytes, fp8_stream_t stream) {
+}  // extern "C"
+
+namespace {
+int gn_act_bwd_impl(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,
+                    const void* film, int film_ld, const int64_t* seed, float p, float eps, const float* stats,
+                    float* totals, const void* dx_add, void* dx, int n, int hw, int c, int groups, void* workspace,
+                    size_t workspace_bytes, fp8_stream_t stream) {
   if (int s = check_gn_args(x, dx, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
+  FP8_REQUIRE(dx_add == nullptr || aligned(dx_add, 16), FP8_ERR_INVALID_ARGUMENT, "dx_add must be 16-byte aligned");
   FP8_REQUIRE(dy != nullptr && aligned(dy, 16), FP8_ERR_INVALID_ARGUMENT, "dy must be 16-byte aligned");
   FP8_REQUIRE(stats != nullptr && totals != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats / totals");
   DeviceState* st;
@@ -1413,15 +1418,36 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
   const uint16_t* ds = static_cast<const uint16_t*>(dy);
   if (x_fp32) {
     if (int s = launch_gn_bwd(static_cast<const float*>(x), ds, sh, stats, q, part, totals, static_cast<float*>(dx),
-                              s1, s2, st->sm_count, cs))
+                              s1, s2, st->sm_count, cs, nullptr, static_cast<const float*>(dx_add)))
       return s;
   } else {
     if (int s = launch_gn_bwd(static_cast<const uint16_t*>(x), ds, sh, stats, q, part, totals,
-                              static_cast<uint16_t*>(dx), s1, s2, st->sm_count, cs))
+                              static_cast<uint16_t*>(dx), s1, s2, st->sm_count, cs, nullptr,
+                              static_cast<const uint16_t*>(dx_add)))
       return s;
   }
   FP8_CUDA_TRY(cudaGetLastError());
   return ok();
+}
+}  // namespace
+
+extern "C" {
+
+int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,
+                   const void* film, int film_ld, const int64_t* seed, float p, float eps, const float* stats,
+                   float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
+                   size_t workspace_bytes, fp8_stream_t stream) {
+  return gn_act_bwd_impl(x, x_fp32, dy, gamma, beta, film, film_ld, seed, p, eps, stats, totals, nullptr, dx, n, hw,
+                         c, groups, workspace, workspace_bytes, stream);
+}
+
+int fp8_gn_act_bwd_accumulate(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,
+                              const void* film, int film_ld, const int64_t* seed, float p, float eps,
+                              const float* stats, float* totals, const void* dx_add, void* dx, int n, int hw, int c,
+                              int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
+  FP8_REQUIRE(dx_add != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL dx_add");
+  return gn_act_bwd_impl(x, x_fp32, dy, gamma, beta, film, film_ld, seed, p, eps, stats, totals, dx_add, dx, n, hw,
+                         c, groups, workspace, workspace_bytes, stream);
 }
 
 size_t fp8_gn_act_bwd_quant_workspace_bytes(int n, int hw, int c) { return fp8_gn_act_quant_workspace_bytes(n, hw, c); }

@@ -87,6 +87,13 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   }
 }
 
+// v rounded to the storage type TX (bf16: round to nearest even; fp32: unchanged).
+template <typename TX>
+__device__ __forceinline__ float round_to_x(float v) {
+  if constexpr (sizeof(TX) == 2) return __uint_as_float(pack_bf16x2(v, 0.0f) << 16);
+  return v;
+}
+
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
                     pack_bf16x2(f[6], f[7]));
@@ -538,28 +545,35 @@ struct GnBwdGroup {
 
 // The streaming loop of the backward apply over this thread's pixel rows.  QUANT:
 // dx (bf16) is also cast to e4m3 with `div`; returns the packed max |dx|.
+// dx_add (may be null): a second gradient of x, added to dx in x's dtype (the sum
+// autograd forms when x has a second reader, e.g. the identity skip of a residual
+// block): dx = RN(RN(dx_norm) + dx_add).
 template <typename TX, bool DROP, bool QUANT, class Div>
 __device__ __forceinline__ uint32_t gn_bwd_apply_rows(const TX* __restrict__ x, const uint16_t* __restrict__ dy,
-                                                      TX* __restrict__ dx, const GnShape& s, const GnThread& t,
-                                                      const GnActParams& q, const GnBwdCoeffs& k,
-                                                      const GnBwdGroup& gm, const GnOut& o, const Div& div) {
+                                                      const TX* __restrict__ dx_add, TX* __restrict__ dx,
+                                                      const GnShape& s, const GnThread& t, const GnActParams& q,
+                                                      const GnBwdCoeffs& k, const GnBwdGroup& gm, const GnOut& o,
+                                                      const Div& div) {
   const uint64_t seed = DROP ? static_cast<uint64_t>(*q.seed) : 0ull;
   const uint32_t thresh = static_cast<uint32_t>(q.p * 65536.0f);
   const float keep_scale = DROP ? 1.0f / (1.0f - q.p) : 1.0f;
   const int64_t base = static_cast<int64_t>(t.n) * s.hw * t.vecs;
   const TX* xs = x + base * 8;
   const uint4* ds = reinterpret_cast<const uint4*>(dy) + base;
+  const TX* as = dx_add != nullptr ? dx_add + base * 8 : nullptr;
   TX* os = dx + base * 8;
   uint32_t qm = 0u;
   for (int p = t.p0 + t.r; p < t.p1; p += kGnUnrollBwd * t.rows) {
     XVec<TX> vx[kGnUnrollBwd];
     uint4 vd[kGnUnrollBwd];
+    XVec<TX> va[kGnUnrollBwd];
 #pragma unroll
     for (int u = 0; u < kGnUnrollBwd; ++u) {
       const int pu = p + u * t.rows;
       const int64_t vi = static_cast<int64_t>(pu) * t.vecs + t.v;
       vx[u] = pu < t.p1 ? load_x8(xs, vi) : zero_x8<TX>();
       vd[u] = pu < t.p1 ? __ldg(ds + vi) : make_uint4(0u, 0u, 0u, 0u);
+      va[u] = as != nullptr && pu < t.p1 ? load_x8(as, vi) : zero_x8<TX>();
     }
 #pragma unroll
     for (int u = 0; u < kGnUnrollBwd; ++u) {
@@ -575,6 +589,12 @@ __device__ __forceinline__ uint32_t gn_bwd_apply_rows(const TX* __restrict__ x, 
         const float df = gn_df<DROP>(fmaf(k.a[j], xf[j], k.b[j]), gf[j], keep, j, keep_scale);
         const float xhat = fmaf(xf[j], k.rs[j], k.nmr[j]);
         r[j] = k.rs[j] * (gm.gk[j] * df - gm.m1[j] - xhat * gm.m2[j]);
+      }
+      if (as != nullptr) {  // uniform over the grid
+        float af[8];
+        unpack_x8(va[u], af);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = round_to_x<TX>(r[j]) + af[j];
       }
       if constexpr (QUANT) {
         const uint4 h = pack8(r);
@@ -599,7 +619,8 @@ __device__ __forceinline__ uint32_t gn_bwd_apply_rows(const TX* __restrict__ x, 
 template <typename TX, bool DROP, bool QUANT>
 __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_kernel(
     const TX* __restrict__ x, const uint16_t* __restrict__ dy, GnShape s, const float* __restrict__ stats,
-    GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx, GnOut o) {
+    GnActParams q, const float* __restrict__ part, float* __restrict__ totals, TX* __restrict__ dx, GnOut o,
+    const TX* __restrict__ dx_add) {
   static_assert(!QUANT || sizeof(TX) == 2, "the e4m3 dx is cast from a bf16 dx");
   extern __shared__ float gn_smem[];
   pdl_wait();
@@ -670,10 +691,10 @@ __global__ void __launch_bounds__(kGnThreads, FP8_GN_MINB_BWD) gn_act_bwd_apply_
     }
     if constexpr (QUANT) {
       qm = markstein_applies(qs)  // uniform over the grid
-               ? gn_bwd_apply_rows<TX, DROP, true>(x, dy, dx, s, t, q, k, gm, o, make_markstein(qs))
-               : gn_bwd_apply_rows<TX, DROP, true>(x, dy, dx, s, t, q, k, gm, o, DivF64(qs));
+               ? gn_bwd_apply_rows<TX, DROP, true>(x, dy, dx_add, dx, s, t, q, k, gm, o, make_markstein(qs))
+               : gn_bwd_apply_rows<TX, DROP, true>(x, dy, dx_add, dx, s, t, q, k, gm, o, DivF64(qs));
     } else {
-      gn_bwd_apply_rows<TX, DROP, false>(x, dy, dx, s, t, q, k, gm, o, NoCast{});
+      gn_bwd_apply_rows<TX, DROP, false>(x, dy, dx_add, dx, s, t, q, k, gm, o, NoCast{});
     }
   }
   if constexpr (QUANT) {

@@ -32,6 +32,25 @@ def hand_off_dy(conv, db: torch.Tensor, dbq: torch.Tensor, sdy: torch.Tensor) ->
     conv._dy_handoff = (db, dbq, sdy)
 
 
+def hand_off_skip_grad(conv, x: torch.Tensor, dx: torch.Tensor) -> None:
+    """Give the fused group-norm conv ``conv`` (whose normalised input is ``x``) a second gradient of x,
+    which its backward adds to the norm's input gradient (``gn_act_bwd(..., dx_add=dx)``); the producer
+    of ``dx`` then returns no gradient for x itself."""
+    conv._dx_add = (x.data_ptr(), x.shape, x.dtype, dx)
+
+
+def _take_dx_add(owner, x: torch.Tensor):
+    entry = getattr(owner, "_dx_add", None) if owner is not None else None
+    if entry is None:
+        return None
+    owner._dx_add = None
+    ptr, shape, dtype, dx = entry
+    if ptr != x.data_ptr() or shape != x.shape or dtype != x.dtype:
+        # the producer returned no gradient for x, so dropping this one would lose it
+        raise RuntimeError("the skip gradient handed to this conv belongs to another tensor")
+    return dx
+
+
 def _take_dy(owner, dy: torch.Tensor):
     """(dyq, sdy) handed to ``owner`` for exactly this gradient tensor, else None.  The entry holds
     ``db`` alive, so equal storage, shape and strides mean it is that tensor."""
@@ -115,7 +134,11 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
         p, eps, groups, film_shape = ctx.cfg
         d_act, dw = _conv_backward(ctx, dy, xq, wq, sx, sw)
         conv = ctx.x_owner
-        if conv is not None:
+        dx_add = _take_dx_add(ctx.owner, x)  # the identity skip's gradient of x, from the residual join
+        if dx_add is not None:
+            dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups,
+                                                      dx_add)
+        elif conv is not None:
             dx, dgamma, dbeta, dfilm, dxq, sdx = ops.gn_act_bwd_quant(
                 x, d_act, gamma, beta, film2, seed, stats, p, eps, groups, conv.amax_window_dy, conv.window_pos)
             hand_off_dy(conv, dx, dxq, sdx)
@@ -145,4 +168,5 @@ def quantize_conv_weights(convs) -> None:
         m._pre_weight = (out[i], out[k + i])
 
 
-__all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed", "quantize_conv_weights", "hand_off_dy"]
+__all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed", "quantize_conv_weights", "hand_off_dy",
+           "hand_off_skip_grad"]

@@ -925,23 +925,33 @@ def _(x, gamma, beta, film, seed, prev_scale, p, eps, groups):
 @torch.library.custom_op("fp8_b200::gn_act_bwd", mutates_args=())
 def gn_act_bwd(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
                film: torch.Tensor | None, seed: torch.Tensor | None, stats: torch.Tensor, p: float, eps: float,
-               groups: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+               groups: int, dx_add: torch.Tensor | None = None
+               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """Backward of gn_act_fwd -> (dx in x's dtype, channels_last; dgamma, dbeta fp32 [C]; dfilm bf16 [N, 2C], or
-    an empty tensor without FiLM)."""
+    an empty tensor without FiLM).  ``dx_add``: a second gradient of x (x's dtype and shape), added to dx as
+    autograd would sum the two."""
     dev = _require_cuda(x, dy, gamma, beta, stats)
     n, c, hw = _gn_check(x, gamma, beta, film, groups)
     dy = dy.contiguous(memory_format=torch.channels_last)
     if dy.dtype != torch.bfloat16 or dy.shape != x.shape:
         raise RuntimeError("dy must be a bfloat16 tensor shaped like x")
+    if dx_add is not None:
+        dx_add = dx_add.contiguous(memory_format=torch.channels_last)
+        if dx_add.dtype != x.dtype or dx_add.shape != x.shape or dx_add.device != dev:
+            raise RuntimeError("dx_add must have x's dtype, shape and device")
     dx = torch.empty_like(x, memory_format=torch.channels_last)
     totals = torch.empty((n, 3, c), device=dev, dtype=torch.float32)
     lib = _lib.load()
     with torch.cuda.device(dev):
         ws = torch.empty(max(lib.fp8_gn_workspace_bytes(n, hw, c) // 4, 4), device=dev, dtype=torch.float32)
-        _lib.check(lib.fp8_gn_act_bwd(
-            _ptr(x), int(x.dtype == torch.float32), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film), _film_ld(film, c), _ptr(seed), float(p), float(eps),
-            _ptr(stats), _ptr(totals), _ptr(dx), n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev)),
-            "fp8_gn_act_bwd")
+        common = (_ptr(x), int(x.dtype == torch.float32), _ptr(dy), _ptr(gamma), _ptr(beta), _ptr(film),
+                  _film_ld(film, c), _ptr(seed), float(p), float(eps), _ptr(stats), _ptr(totals))
+        tail = (n, hw, c, groups, _ptr(ws), ws.numel() * 4, _stream(dev))
+        if dx_add is None:
+            _lib.check(lib.fp8_gn_act_bwd(*common, _ptr(dx), *tail), "fp8_gn_act_bwd")
+        else:
+            _lib.check(lib.fp8_gn_act_bwd_accumulate(*common, _ptr(dx_add), _ptr(dx), *tail),
+                       "fp8_gn_act_bwd_accumulate")
         dgamma = torch.empty((c,), device=dev, dtype=torch.float32)
         dbeta = torch.empty((c,), device=dev, dtype=torch.float32)
         dfilm = torch.empty((n, 2 * c) if film is not None else (0,), device=dev, dtype=torch.bfloat16)
@@ -1000,7 +1010,7 @@ def _(x, dy, gamma, beta, film, seed, stats, p, eps, groups, window, pos):
 
 
 @gn_act_bwd.register_fake
-def _(x, dy, gamma, beta, film, seed, stats, p, eps, groups):
+def _(x, dy, gamma, beta, film, seed, stats, p, eps, groups, dx_add=None):
     n, c = x.shape[0], x.shape[1]
     return (torch.empty_like(x, memory_format=torch.channels_last), x.new_empty((c,), dtype=torch.float32),
             x.new_empty((c,), dtype=torch.float32),

@@ -20,7 +20,7 @@ import numpy as np
 import torch
 
 from . import ops
-from .delayed import hand_off_dy
+from .delayed import hand_off_dy, hand_off_skip_grad
 
 _FLOATS = (torch.bfloat16, torch.float32)
 
@@ -99,9 +99,12 @@ def upsample_cat_pair(a: torch.Tensor, s: torch.Tensor, factor: int) -> tuple[to
 
 class _AddScale(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a, b, inv: float, dy_target=None):
+    def forward(ctx, a, b, inv: float, dy_target=None, skip_target=None):
         ctx.cfg = (a.dtype, b.dtype, inv)
         ctx.dy_target = dy_target
+        ctx.skip_target = skip_target
+        if skip_target is not None:
+            ctx.save_for_backward(a)
         return ops.add_scale(a, b, inv)
 
     @staticmethod
@@ -114,7 +117,11 @@ class _AddScale(torch.autograd.Function):
             hand_off_dy(conv, db, dbq, sdy)
         else:
             da, db = ops.add_scale_bwd(dy, inv, ta == torch.float32, tb == torch.float32)
-        return da, db, None, None
+        if ctx.skip_target is not None:  # a's gradient is added by the norm's backward of the block's conv_1
+            (a,) = ctx.saved_tensors
+            hand_off_skip_grad(ctx.skip_target, a, da)
+            da = None
+        return da, db, None, None, None
 
 
 def _same_dense_layout(a: torch.Tensor, b: torch.Tensor) -> bool:
@@ -123,17 +130,20 @@ def _same_dense_layout(a: torch.Tensor, b: torch.Tensor) -> bool:
     return a.is_contiguous() or (a.dim() == 4 and a.is_contiguous(memory_format=torch.channels_last))
 
 
-def residual_join(a: torch.Tensor, b: torch.Tensor, divisor: float = math.sqrt(2.0), dy_target=None) -> torch.Tensor:
+def residual_join(a: torch.Tensor, b: torch.Tensor, divisor: float = math.sqrt(2.0), dy_target=None,
+                  skip_target=None) -> torch.Tensor:
     """``(a + b) / divisor`` as one pass, with the dtype and the two roundings of the torch ops (unet.py:161, :203).
 
     ``dy_target``: the delayed-scaling FP8 conv module whose output is ``b``; the backward then also
     writes the e4m3 cast of b's gradient, with that conv's dY history update, and hands it over
-    (fp8_b200.delayed.hand_off_dy)."""
+    (fp8_b200.delayed.hand_off_dy).  ``skip_target``: the fused group-norm conv whose normalised input is
+    ``a`` itself; a's gradient is then added inside that conv's norm backward instead of by autograd
+    (fp8_b200.delayed.hand_off_skip_grad)."""
     if not (a.is_cuda and b.is_cuda and a.dtype in _FLOATS and b.dtype in _FLOATS and _same_dense_layout(a, b)
             and a.numel() % 8 == 0 and a.numel() > 0):
         return (a + b) / divisor
     inv = float(np.float32(1.0) / np.float32(divisor))  # torch: a host scalar divisor becomes an fp32 reciprocal
-    return _AddScale.apply(a, b, inv, dy_target)
+    return _AddScale.apply(a, b, inv, dy_target, skip_target)
 
 
 __all__ = ["downsample_nearest", "upsample_cat", "upsample_cat_pair", "resample_supported", "residual_join"]

@@ -92,6 +92,8 @@ class Conv2dFP8(nn.Module):
         self.used_fp8_delayed = False  # whether a forward since the UNet's last one ran the delayed FP8 path
         self.last_fp8_delayed = False  # whether the latest forward did (on device scale histories)
         self._dy_handoff = None  # (dy, e4m3 dy, scale) from the op that produced this conv's output gradient
+        self._dx_add = None  # a second gradient of the normalised input, from the residual join
+        self.last_fused_norm_input = None  # (data_ptr, shape, dtype) of x when forward_normed ran fused
         if scaling_type not in ("current", "delayed"):
             raise ValueError(f"unknown FP8 scaling type {scaling_type!r}")
         self.conv = nn.Conv2d(in_channels, out_channels, (3, 3), stride=1, padding=1, bias=False)
@@ -149,6 +151,7 @@ class Conv2dFP8(nn.Module):
         ``x_owner``: the delayed FP8 conv that produced x, whose backward then receives the
         e4m3 cast of x's gradient from the norm's backward."""
         self.last_fp8_delayed = False
+        self.last_fused_norm_input = None
         if not (self.scaling_type == "delayed" and self.uses_fp8(x) and fused_norm_supported(x, norm)):
             return self(group_norm_act(x, norm, film, p, seed))
         if p > 0.0 and seed is None:
@@ -157,6 +160,7 @@ class Conv2dFP8(nn.Module):
         if self.device_scale_history:
             pre, self._pre_weight = self._pre_weight, None
             self.used_fp8_delayed = self.last_fp8_delayed = True
+            self.last_fused_norm_input = (x.data_ptr(), x.shape, x.dtype)
             return GroupNormActConvFP8Delayed.apply(
                 x, norm.weight, norm.bias, film, seed if p > 0.0 else None, self.conv.weight, self.amax_window_acts,
                 self.amax_window_weights, self.amax_window_dy, self.window_pos, float(p), float(norm.eps),
@@ -241,8 +245,13 @@ class ResidualBlock(nn.Module):
         skip = self.skip_connection(src) if w16 is None else F.conv2d(src, w16, self.skip_connection.bias)
         if self.fused_residual:
             # h is conv_2's output: when that ran the delayed FP8 path, the join's backward also makes
-            # the e4m3 cast of h's gradient for conv_2's backward
-            return residual_join(skip, h, dy_target=self.conv_2 if self.conv_2.last_fp8_delayed else None)
+            # the e4m3 cast of h's gradient for conv_2's backward.  With an identity skip whose x conv_1's
+            # fused norm read as is, x's skip gradient is added inside that norm's backward.
+            key = (x.data_ptr(), x.shape, x.dtype)
+            skip_target = (self.conv_1 if isinstance(self.skip_connection, nn.Identity) and skip_in is None
+                           and self.conv_1.last_fused_norm_input == key else None)
+            return residual_join(skip, h, dy_target=self.conv_2 if self.conv_2.last_fp8_delayed else None,
+                                 skip_target=skip_target)
         return (skip + h) / math.sqrt(2.0)
 
 

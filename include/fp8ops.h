@@ -257,6 +257,15 @@ int fp8_gn_act_bwd(const void* x, int x_fp32, const void* dy, const float* gamma
                    float* totals, void* dx, int n, int hw, int c, int groups, void* workspace,
                    size_t workspace_bytes, fp8_stream_t stream);
 
+/* fp8_gn_act_bwd with a second gradient of x added: dx = RN(RN(dx_norm) +
+ * dx_add) in x's dtype, dx_add laid out like x (16-byte aligned).  That is the
+ * sum autograd forms for the input of a residual block with an identity skip,
+ * read by norm1 and by the join (unet.py:151, 161), without the separate add. */
+int fp8_gn_act_bwd_accumulate(const void* x, int x_fp32, const void* dy, const float* gamma, const float* beta,
+                              const void* film, int film_ld, const int64_t* seed, float p, float eps,
+                              const float* stats, float* totals, const void* dx_add, void* dx, int n, int hw, int c,
+                              int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
+
 /* fp8_gn_act_bwd for a bf16 x that is the output of a delayed-scaling FP8 conv
  * (the residual block's conv_1 before norm2, unet.py:151-159): dx (bf16) is
  * also written as e4m3 to dxq, cast with max(window[0 .. window_len)) -- which

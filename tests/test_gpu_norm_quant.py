@@ -212,3 +212,23 @@ def test_gn_act_bwd_quant_matches_bwd_then_conv_quantize(cuda, c, h, w, film, p)
         assert u.dtype == v.dtype and torch.equal(u, v)
     assert res[0][7].item() == 7
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gn_act_bwd_with_skip_gradient_matches_autograd_sum(cuda, dtype):
+    """gn_act_bwd(..., dx_add) = gn_act_bwd(...) + dx_add as autograd sums the two gradients of a tensor
+    read twice (in x's dtype), bit for bit."""
+    from fp8_b200 import ops
+
+    x, norm, f = _inputs(4, 256, 16, 16, True, seed=11, device=cuda, dtype=dtype)
+    seed = torch.tensor(5, dtype=torch.int64, device=cuda)
+    _, stats = ops.gn_act_fwd(x, norm.weight, norm.bias, f, seed, 0.1, norm.eps, 32)
+    g = torch.Generator().manual_seed(12)
+    dy = (torch.randn(x.shape, generator=g) * 1e-2).to(torch.bfloat16).to(cuda).contiguous(
+        memory_format=torch.channels_last)
+    add = (torch.randn(x.shape, generator=g) * 1e-2).to(dtype).to(cuda).contiguous(memory_format=torch.channels_last)
+    args = (x, dy, norm.weight, norm.bias, f, seed, stats, 0.1, norm.eps, 32)
+    dx, dg, db, dfilm = ops.gn_act_bwd(*args)
+    dx2, dg2, db2, dfilm2 = ops.gn_act_bwd(*args, add)
+    assert torch.equal(dx2, dx + add)
+    assert torch.equal(dg2, dg) and torch.equal(db2, db) and torch.equal(dfilm2, dfilm)
