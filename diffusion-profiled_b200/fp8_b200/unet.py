@@ -211,6 +211,7 @@ class ResidualBlock(nn.Module):
         self._emb = None  # this block's time-embedding projection, when the UNet computed it in a batch
         self._skip_in = None  # bf16 copy of the input for the 1x1 skip conv, when the UNet made one
         self._skip_w16 = None  # bf16 copy of the skip conv's weight, when the UNet made one
+        self._seed = None  # this step's dropout seed, when the UNet drew all blocks' seeds at once
         # dropout mask seed of the fused path (device scalar, advanced every
         # training forward so a captured graph draws a new mask each replay)
         self.register_buffer("dropout_seed", torch.randint(0, 2**62, (), dtype=torch.int64), persistent=False)
@@ -228,7 +229,10 @@ class ResidualBlock(nn.Module):
             h = self.conv_1.forward_normed(x, self.norm1)
             if fused_norm_supported(h, self.norm2) and emb.dtype == torch.bfloat16:
                 p = self.dropout.p if self.training else 0.0
-                h = self.conv_2.forward_normed(h, self.norm2, emb, p, self._next_seed() if p > 0.0 else None,
+                seed, self._seed = self._seed, None
+                if p > 0.0 and seed is None:
+                    seed = self._next_seed()
+                h = self.conv_2.forward_normed(h, self.norm2, emb, p, seed if p > 0.0 else None,
                                                x_owner=self.conv_1 if self.conv_1.last_fp8_delayed else None)
                 return self._join(x, h)
         else:
@@ -343,6 +347,12 @@ class UNet(nn.Module):
         freqs = torch.exp(-torch.arange(half, dtype=torch.float32) * (math.log(10000.0) / half))
         self.register_buffer("freqs", freqs, persistent=False)
         self._time_w16 = None  # bf16 time-MLP weights from the step's batched cast
+        # every residual block's dropout seed in one device vector: one clone and one increment per
+        # training step instead of one pair per block (advanced on the device, so a captured graph
+        # draws new masks each replay)
+        self._res_blocks = [m for m in self.modules() if isinstance(m, ResidualBlock)]
+        self.register_buffer("dropout_seed", torch.randint(0, 2**62, (len(self._res_blocks),), dtype=torch.int64),
+                             persistent=False)
 
     def _timestep(self, t: torch.Tensor) -> torch.Tensor:
         emb = t[:, None].float() * self.freqs[None]
@@ -358,7 +368,14 @@ class UNet(nn.Module):
         if batch:
             quantize_conv_weights(batch)
         self._time_w16 = self._cast_bf16_weights() if self.config.batched_weight_cast else None
+        if self.training and self.config.fused_norm and self._res_blocks:
+            seeds = self.dropout_seed.clone()
+            self.dropout_seed.add_(1)
+            for i, b in enumerate(self._res_blocks):
+                b._seed = seeds[i]
         out = self._forward(x, t)
+        for b in self._res_blocks:
+            b._seed = None
         convs = [m for m in self.modules() if isinstance(m, Conv2dFP8) and m.used_fp8_delayed]
         for m in convs:
             m.used_fp8_delayed = False
