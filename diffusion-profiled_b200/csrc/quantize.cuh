@@ -802,9 +802,22 @@ __global__ void __launch_bounds__(kQuantThreads) weight_cast_kernel(WeightBatch 
   const float* __restrict__ w = b.w[t];
   uint8_t* __restrict__ q = b.q[t];
   float m = 0.0f;
-  // pairs of elements: round to bf16 (RN), |.| max, cast the pair
+  // 8 elements per step where w is 16-byte and q 8-byte aligned (uniform per tensor), then pairs:
+  // round to bf16 (RN), |.| max, cast
+  const bool vec = ((reinterpret_cast<uintptr_t>(w) & 15u) | (reinterpret_cast<uintptr_t>(q) & 7u)) == 0;
+  const int64_t end8 = vec ? begin + ((end - begin) & ~int64_t(7)) : begin;
   auto body = [&](const auto& div) {
-    for (int64_t i = begin + 2 * threadIdx.x; i < end; i += 2 * kQuantThreads) {
+    uint32_t m2 = 0u;
+    for (int64_t i = begin + 8 * threadIdx.x; i < end8; i += 8 * kQuantThreads) {
+      const float4 a = *reinterpret_cast<const float4*>(w + i);
+      const float4 c = *reinterpret_cast<const float4*>(w + i + 4);
+      const uint4 h = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(c.x, c.y),
+                                 pack_bf16x2(c.z, c.w));
+      m2 = bf16x2_max(m2, absmax_vec2(h));
+      *reinterpret_cast<uint2*>(q + i) = cast_vec(h, div);
+    }
+    m = unpack_max2(m2);
+    for (int64_t i = end8 + 2 * threadIdx.x; i < end; i += 2 * kQuantThreads) {
       const float f0 = w[i];
       const float f1 = i + 1 < end ? w[i + 1] : 0.0f;
       const uint32_t word = pack_bf16x2(f0, f1);
