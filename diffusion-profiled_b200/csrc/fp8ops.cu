@@ -999,6 +999,34 @@ int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8
   return ok();
 }
 
+int fp8_conv_weight_transpose_batch(int count, const void* const* wq, void* const* wq_t, const int* cout,
+                                    const int* cin, fp8_stream_t stream) {
+  FP8_REQUIRE(count > 0 && count <= kMaxTransTensors, FP8_ERR_UNSUPPORTED, "1..%d weights per call",
+              kMaxTransTensors);
+  FP8_REQUIRE(wq && wq_t && cout && cin, FP8_ERR_INVALID_ARGUMENT, "NULL argument");
+  TransBatch b{};
+  b.count = count;
+  int64_t tiles = 0;
+  for (int t = 0; t < count; ++t) {
+    FP8_REQUIRE(cout[t] > 0 && cin[t] > 0 && cout[t] % kTransTile == 0 && cin[t] % kTransTile == 0,
+                FP8_ERR_UNSUPPORTED, "weight %d: Cout and Cin must be positive multiples of %d", t, kTransTile);
+    FP8_REQUIRE(wq[t] && wq_t[t] && aligned(wq[t], 16) && aligned(wq_t[t], 16), FP8_ERR_INVALID_ARGUMENT,
+                "weight %d: pointers must be non-NULL and 16-byte aligned", t);
+    b.src[t] = static_cast<const uint8_t*>(wq[t]);
+    b.dst[t] = static_cast<uint8_t*>(wq_t[t]);
+    b.cout[t] = cout[t];
+    b.cin[t] = cin[t];
+    b.tile_begin[t] = static_cast<int>(tiles);
+    tiles += 9ll * (cout[t] / kTransTile) * (cin[t] / kTransTile);
+    FP8_REQUIRE(tiles < (1ll << 31), FP8_ERR_UNSUPPORTED, "weights too large");
+  }
+  b.tile_begin[count] = static_cast<int>(tiles);
+  FP8_CUDA_TRY(launch_kernel(transpose_conv_weights_kernel, dim3(static_cast<unsigned>(tiles)), dim3(256), 0,
+                             reinterpret_cast<cudaStream_t>(stream), 1, kStreamingKernel, b));
+  count_launches(1);
+  return ok();
+}
+
 int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, const float* sw, const void* bias,
                     int epilogue, int batch, int height, int width, int cin, int cout, fp8_stream_t stream) {
   ConvTile t;

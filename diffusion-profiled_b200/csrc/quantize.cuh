@@ -747,6 +747,51 @@ __global__ void __launch_bounds__(256) transpose_u8_tiles16_kernel(const uint8_t
   *reinterpret_cast<uint4*>(d + (c0 + row) * dst_ld + r0 + seg) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// The data-grad re-layout of many conv weights in one launch: tensor t is
+// [Cout][9][Cin] e4m3 -> [Cin][9][Cout] (per tap a Cout x Cin transpose), the
+// layout fp8_conv3x3_dgrad reads; Cout and Cin multiples of 64, 16-byte aligned.
+// CTA k takes one 64x64 tile of one tap of one tensor (prefix sums in tile_begin).
+constexpr int kMaxTransTensors = 64;
+
+struct TransBatch {
+  const uint8_t* src[kMaxTransTensors];
+  uint8_t* dst[kMaxTransTensors];
+  int cout[kMaxTransTensors];
+  int cin[kMaxTransTensors];
+  int tile_begin[kMaxTransTensors + 1];
+  int count;
+};
+static_assert(sizeof(TransBatch) < 4000, "kernel parameter size");
+
+__global__ void __launch_bounds__(256) transpose_conv_weights_kernel(TransBatch b) {
+  __shared__ __align__(16) uint8_t tile[kTransTile][kTransTile + 4];
+  pdl_wait();
+  const int k = blockIdx.x;
+  int lo = 0, hi = b.count - 1;  // last t with tile_begin[t] <= k
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.tile_begin[mid] <= k) lo = mid; else hi = mid - 1;
+  }
+  const int t = lo, cout = b.cout[t], cin = b.cin[t];
+  const int local = k - b.tile_begin[t];
+  const int tr = cout / kTransTile, tc = cin / kTransTile;
+  const int tap = local / (tr * tc), rem = local % (tr * tc);
+  const int64_t r0 = static_cast<int64_t>(rem / tc) * kTransTile, c0 = static_cast<int64_t>(rem % tc) * kTransTile;
+  const int64_t src_ld = 9ll * cin, dst_ld = 9ll * cout;
+  const uint8_t* s = b.src[t] + static_cast<int64_t>(tap) * cin;
+  uint8_t* d = b.dst[t] + static_cast<int64_t>(tap) * cout;
+  const int row = threadIdx.x >> 2, seg = (threadIdx.x & 3) * 16;
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(s + (r0 + row) * src_ld + c0 + seg));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) tile[row][seg + i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+  __syncthreads();
+  uint32_t o[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i >> 2] |= static_cast<uint32_t>(tile[seg + i][row]) << (8 * (i & 3));
+  *reinterpret_cast<uint4*>(d + (c0 + row) * dst_ld + r0 + seg) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // ---------------------------------------------------------------- batched weight quantize
 // The delayed quantize of many fp32 weight tensors at once (every FP8 conv of a
 // model, once per step): each weight is rounded to bf16 -- the reference's

@@ -120,6 +120,7 @@ _SIGNATURES: dict[str, tuple] = {
         [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_float, c_void_p,
          c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
     ),
+    "fp8_conv_weight_transpose_batch": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "fp8_cast_batch": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "fp8_up_cat_pair": (
         c_int,

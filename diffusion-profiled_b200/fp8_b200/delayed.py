@@ -75,14 +75,19 @@ def _conv_backward(ctx, dy, xq, wq, sx, sw):
         dyq, sdy = ops.quantize_delayed_window(dy, ctx.win_dy, ctx.pos, False)
     # an fp32 weight gets the bf16 dW widened by the reduce pass, not by an autograd cast
     widen = ctx.w_dtype == torch.float32
-    return ops.conv3x3_dgrad(dyq, wq, sdy, sw), ops.conv3x3_wgrad(xq, dyq, sx, sdy, 0, widen)
+    # weights re-laid out for the data-grad by the step's batched transpose, when it made them
+    dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw) if ctx.wq_t is None else ops.conv3x3_dgrad_pre(dyq, ctx.wq_t, sdy, sw)
+    return dx, ops.conv3x3_wgrad(xq, dyq, sx, sdy, 0, widen)
 
 
-def _weight_q(weight, win_w, pos, pre):
+def _weight_q(ctx, weight, win_w, pos, pre):
     """The e4m3 weight and its scale: from the step's batched weight quantize when given
-    (``pre = (wq, sw)``, history written, position to be stepped here), else quantized now."""
+    (``pre = (wq, sw, wq_t)``, history written, position to be stepped here; wq_t the data-grad
+    layout or None), else quantized now.  Sets ``ctx.wq_t``."""
     if pre is not None:
-        return pre
+        ctx.wq_t = pre[2]
+        return pre[0], pre[1]
+    ctx.wq_t = None
     return ops.quantize_delayed_window(_weight_bf16(weight), win_w, pos, False)
 
 
@@ -94,7 +99,7 @@ class ConvFP8Delayed(torch.autograd.Function):
     def forward(ctx, x, weight, win_x, win_w, win_dy, pos, pre=None, owner=None):
         ctx.owner = owner
         x = x.to(torch.bfloat16)
-        wq, sw = _weight_q(weight, win_w, pos, pre)
+        wq, sw = _weight_q(ctx, weight, win_w, pos, pre)
         xq, sx = ops.quantize_delayed_window(x, win_x, pos, True)
         ctx.save_for_backward(xq, wq, sx, sw)
         ctx.win_dy, ctx.pos, ctx.w_dtype = win_dy, pos, weight.dtype
@@ -120,7 +125,7 @@ class GroupNormActConvFP8Delayed(torch.autograd.Function):
         # the e4m3 cast of x's gradient for that conv's backward
         ctx.x_owner = x_owner if x.dtype == torch.bfloat16 else None
         film2 = None if film is None else film.reshape(film.shape[0], -1)
-        wq, sw = _weight_q(weight, win_w, pos, pre)
+        wq, sw = _weight_q(ctx, weight, win_w, pos, pre)
         xq, sx, stats = ops.gn_act_quant_fwd_window(x, gamma, beta, film2, seed, win_x, pos, True, p, eps, groups)
         ctx.save_for_backward(x, gamma, beta, film2, seed, stats, xq, wq, sx, sw)
         ctx.win_dy, ctx.pos, ctx.w_dtype = win_dy, pos, weight.dtype
@@ -164,8 +169,11 @@ def quantize_conv_weights(convs) -> None:
     out = ops.quantize_weights_delayed(weights, [m.amax_window_weights for m in convs],
                                        [m.window_pos for m in convs])
     k = len(convs)
+    # the data-grad layout of the weights whose data-grad does not read them in place, one launch
+    relayout = [i for i, m in enumerate(convs) if getattr(m, "dgrad_relayout", False)]
+    wq_t = dict(zip(relayout, ops.transpose_conv_weights([out[i] for i in relayout])))
     for i, m in enumerate(convs):
-        m._pre_weight = (out[i], out[k + i])
+        m._pre_weight = (out[i], out[k + i], wq_t.get(i))
 
 
 __all__ = ["ConvFP8Delayed", "GroupNormActConvFP8Delayed", "quantize_conv_weights", "hand_off_dy",

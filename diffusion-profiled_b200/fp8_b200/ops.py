@@ -387,6 +387,63 @@ def _(dyq, wq, sdy, sw):
     )
 
 
+def dgrad_needs_relayout(b: int, h: int, w: int, cin: int, cout: int) -> bool:
+    """Whether conv3x3_dgrad re-lays the weights out for this geometry (else it reads them in place)."""
+    return _lib.load().fp8_conv3x3_dgrad_w_workspace_bytes(b, h, w, cin, cout) > 0
+
+
+@torch.library.custom_op("fp8_b200::transpose_conv_weights", mutates_args=())
+def transpose_conv_weights(wqs: list[torch.Tensor]) -> list[torch.Tensor]:
+    """Each e4m3 channels_last weight [Cout, Cin, 3, 3] re-laid out as [Cin][3][3][Cout] (a contiguous
+    [Cin, 9*Cout] tensor, the data-grad's B operand), in one launch per 64 weights."""
+    if not wqs:
+        return []
+    dev = _require_cuda(*wqs)
+    for t in wqs:
+        _check_conv_operand(t, "weight")
+    outs = [torch.empty((t.shape[1], 9 * t.shape[0]), device=dev, dtype=FP8_DTYPE) for t in wqs]
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        for i in range(0, len(wqs), 64):
+            src, dst = wqs[i:i + 64], outs[i:i + 64]
+            k = len(src)
+            _lib.check(lib.fp8_conv_weight_transpose_batch(
+                k, (c_void_p * k)(*[t.data_ptr() for t in src]), (c_void_p * k)(*[t.data_ptr() for t in dst]),
+                (ctypes.c_int * k)(*[t.shape[0] for t in src]), (ctypes.c_int * k)(*[t.shape[1] for t in src]),
+                _stream(dev)), "fp8_conv_weight_transpose_batch")
+    return outs
+
+
+@transpose_conv_weights.register_fake
+def _(wqs):
+    return [t.new_empty((t.shape[1], 9 * t.shape[0])) for t in wqs]
+
+
+@torch.library.custom_op("fp8_b200::conv3x3_dgrad_pre", mutates_args=())
+def conv3x3_dgrad_pre(dyq: torch.Tensor, wq_t: torch.Tensor, sdy: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    """conv3x3_dgrad with the weights already re-laid out by transpose_conv_weights ([Cin, 9*Cout])."""
+    dev = _require_cuda(dyq, wq_t)
+    _check_conv_operand(dyq, "dy")
+    _check_scale(sdy, dev, "dy_scale")
+    _check_scale(sw, dev, "weight_scale")
+    b, cout, h, w = dyq.shape
+    if wq_t.dtype != FP8_DTYPE or wq_t.dim() != 2 or not wq_t.is_contiguous() or wq_t.shape[1] != 9 * cout:
+        raise RuntimeError("wq_t must be a contiguous [Cin, 9*Cout] float8_e4m3fn tensor")
+    cin = wq_t.shape[0]
+    dx = torch.empty((b, cin, h, w), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        _lib.call("fp8_conv3x3_dgrad", _ptr(dyq), _ptr(wq_t), _ptr(dx), _ptr(sdy), _ptr(sw), b, h, w, cin, cout,
+                  _stream(dev))
+    return dx
+
+
+@conv3x3_dgrad_pre.register_fake
+def _(dyq, wq_t, sdy, sw):
+    b, _, h, w = dyq.shape
+    return torch.empty((b, wq_t.shape[0], h, w), device=dyq.device, dtype=torch.bfloat16,
+                       memory_format=torch.channels_last)
+
+
 @torch.library.custom_op("fp8_b200::conv3x3_wgrad", mutates_args=())
 def conv3x3_wgrad(
     xq: torch.Tensor, dyq: torch.Tensor, sx: torch.Tensor, sdy: torch.Tensor, split_k: int = 0, widen: bool = False

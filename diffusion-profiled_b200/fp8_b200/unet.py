@@ -27,6 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import ops
 from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed, quantize_conv_weights
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
 from .resample import downsample_nearest, residual_join, upsample_cat, upsample_cat_pair
@@ -94,6 +95,7 @@ class Conv2dFP8(nn.Module):
         self._dy_handoff = None  # (dy, e4m3 dy, scale) from the op that produced this conv's output gradient
         self._dx_add = None  # a second gradient of the normalised input, from the residual join
         self.last_fused_norm_input = None  # (data_ptr, shape, dtype) of x when forward_normed ran fused
+        self.dgrad_relayout = False  # whether the data-grad of the last delayed FP8 forward re-lays the weights out
         if scaling_type not in ("current", "delayed"):
             raise ValueError(f"unknown FP8 scaling type {scaling_type!r}")
         self.conv = nn.Conv2d(in_channels, out_channels, (3, 3), stride=1, padding=1, bias=False)
@@ -128,6 +130,8 @@ class Conv2dFP8(nn.Module):
         if self.device_scale_history:
             pre, self._pre_weight = self._pre_weight, None
             self.used_fp8_delayed = self.last_fp8_delayed = True
+            self.dgrad_relayout = ops.dgrad_needs_relayout(x.shape[0], x.shape[2], x.shape[3], x.shape[1],
+                                                           self.conv.weight.shape[0])
             return ConvFP8Delayed.apply(x, self.conv.weight, self.amax_window_acts, self.amax_window_weights,
                                         self.amax_window_dy, self.window_pos, pre, self)
         with torch.no_grad():
@@ -161,6 +165,8 @@ class Conv2dFP8(nn.Module):
             pre, self._pre_weight = self._pre_weight, None
             self.used_fp8_delayed = self.last_fp8_delayed = True
             self.last_fused_norm_input = (x.data_ptr(), x.shape, x.dtype)
+            self.dgrad_relayout = ops.dgrad_needs_relayout(x.shape[0], x.shape[2], x.shape[3], x.shape[1],
+                                                           self.conv.weight.shape[0])
             return GroupNormActConvFP8Delayed.apply(
                 x, norm.weight, norm.bias, film, seed if p > 0.0 else None, self.conv.weight, self.amax_window_acts,
                 self.amax_window_weights, self.amax_window_dy, self.window_pos, float(p), float(norm.eps),

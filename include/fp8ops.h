@@ -127,6 +127,13 @@ int fp8_transpose_2d(const void* src, void* dst, int64_t rows, int64_t cols, fp8
  * gathers W with strided loads (fp8_kernels.py:306-309). */
 int fp8_conv_weight_transpose(const void* wq, void* wq_t, int cout, int cin, fp8_stream_t stream);
 
+/* fp8_conv_weight_transpose of `count` (1..64) weights in one launch (Cout and
+ * Cin multiples of 64, 16-byte aligned): the re-laid-out weights of every
+ * data-grad of a training step, made once per step next to the batched weight
+ * quantize instead of inside each fp8_conv3x3_dgrad_w call. */
+int fp8_conv_weight_transpose_batch(int count, const void* const* wq, void* const* wq_t, const int* cout,
+                                    const int* cin, fp8_stream_t stream);
+
 /* ------------------------------------------------------------ 3x3 conv (pad 1) */
 
 /* y[n,h,w,co] = epi( sum_{kh,kw,ci} xq[n,h+kh-1,w+kw-1,ci] * wq[co,kh,kw,ci] * sx * sw )

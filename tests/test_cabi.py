@@ -229,3 +229,14 @@ def test_new_fused_entry_points_validate_without_touching_cuda():
     status, code, msg = _status_and_message(lib.fp8_conv3x3_wgrad_f32, null, null, null, null, null, 2, 8, 8, 100, 128,
                                             0, null, 0, null)
     assert status == _lib.FP8_ERR_UNSUPPORTED and "multiples of 128" in msg
+
+
+def test_weight_transpose_batch_validates_without_touching_cuda():
+    lib = _lib.load()
+    arr = (c_void_p * 1)(c_void_p(1 << 20))
+    dims = (ctypes.c_int * 1)(128)
+    bad = (ctypes.c_int * 1)(96)
+    status, code, msg = _status_and_message(lib.fp8_conv_weight_transpose_batch, 65, arr, arr, dims, dims, c_void_p(0))
+    assert status == _lib.FP8_ERR_UNSUPPORTED and "1..64" in msg
+    status, code, msg = _status_and_message(lib.fp8_conv_weight_transpose_batch, 1, arr, arr, bad, dims, c_void_p(0))
+    assert status == _lib.FP8_ERR_UNSUPPORTED and "multiples of 64" in msg

@@ -130,6 +130,26 @@ def test_conv_wgrad_widened_fp32(cuda, cin, cout, h, w):
     assert oracle.max_rel_err(dw32, ref) <= TOL
 
 
+def test_batched_weight_relayout_gives_the_same_dgrad(cuda):
+    """transpose_conv_weights (one launch for many weights) + conv3x3_dgrad_pre equal conv3x3_dgrad, which
+    re-lays each weight out itself, bit for bit, for the shapes whose data-grad does not read in place."""
+    from fp8_b200 import ops
+
+    shapes = [(256, 256, 8, 8), (512, 256, 8, 8), (256, 256, 4, 4), (256, 512, 4, 4), (128, 256, 16, 16)]
+    cases = []
+    for i, (cin, cout, h, w) in enumerate(shapes):
+        b = 16
+        wq, sw = _rand_q((cout, cin, 3, 3), seed=40 + i, device=cuda, scale=0.05)
+        dyq, sdy = _rand_q((b, cout, h, w), seed=50 + i, device=cuda, scale=1e-2)
+        cases.append((cin, cout, h, w, b, wq, sw, dyq, sdy))
+    need = [c for c in cases if ops.dgrad_needs_relayout(c[4], c[2], c[3], c[0], c[1])]
+    assert len(need) >= 3
+    wts = ops.transpose_conv_weights([c[5] for c in need])
+    for (cin, cout, h, w, b, wq, sw, dyq, sdy), wq_t in zip(need, wts):
+        assert wq_t.shape == (cin, 9 * cout)
+        assert torch.equal(ops.conv3x3_dgrad_pre(dyq, wq_t, sdy, sw), ops.conv3x3_dgrad(dyq, wq, sdy, sw))
+
+
 @pytest.mark.parametrize("split_k", [1, 3, 7])
 def test_conv_wgrad_split_counts(cuda, split_k):
     from fp8_b200 import ops
