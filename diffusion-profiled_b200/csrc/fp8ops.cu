@@ -82,7 +82,9 @@ struct DeviceState {
   int* err_ptr = nullptr;
   unsigned int* fold_base = nullptr;  // g_fold_counters on this device
   std::atomic<unsigned int> fold_next{0};
-  bool init = false;
+  // Set (release) after the fields above are written; a reader that sees it
+  // (acquire) sees them too.
+  std::atomic<bool> init{false};
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -92,16 +94,16 @@ int device_state(DeviceState** out) {
   FP8_CUDA_TRY(cudaGetDevice(&dev));
   FP8_REQUIRE(dev >= 0 && dev < kMaxDevices, FP8_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
   DeviceState& st = g_dev[dev];
-  if (!st.init) {
+  if (!st.init.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lock(g_dev_mu);
-    if (!st.init) {
+    if (!st.init.load(std::memory_order_relaxed)) {
       FP8_CUDA_TRY(cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev));
       void* p = nullptr;
       FP8_CUDA_TRY(cudaGetSymbolAddress(&p, g_fp8_device_error));
       st.err_ptr = static_cast<int*>(p);
       FP8_CUDA_TRY(cudaGetSymbolAddress(&p, g_fold_counters));
       st.fold_base = static_cast<unsigned int*>(p);
-      st.init = true;
+      st.init.store(true, std::memory_order_release);
     }
   }
   *out = &st;
@@ -330,7 +332,7 @@ int launch_halo_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensor
 }
 
 // Clusters of two CTAs that can be resident at once (cached per device).
-int g_pair_clusters[kMaxDevices] = {};
+std::atomic<int> g_pair_clusters[kMaxDevices] = {};
 
 template <int W>
 int launch_halo_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const HaloParams& p,
@@ -351,12 +353,12 @@ int launch_halo_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   cfg.numAttrs = 1;
   int dev = 0;
   FP8_CUDA_TRY(cudaGetDevice(&dev));
-  int max_pairs = (dev >= 0 && dev < kMaxDevices) ? g_pair_clusters[dev] : 0;
+  int max_pairs = (dev >= 0 && dev < kMaxDevices) ? g_pair_clusters[dev].load(std::memory_order_relaxed) : 0;
   if (max_pairs <= 0) {
     cfg.gridDim = dim3(static_cast<unsigned>(sm_count & ~1), 1, 1);
     FP8_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg));
     if (max_pairs <= 0) max_pairs = sm_count / 2;
-    if (dev >= 0 && dev < kMaxDevices) g_pair_clusters[dev] = max_pairs;
+    if (dev >= 0 && dev < kMaxDevices) g_pair_clusters[dev].store(max_pairs, std::memory_order_relaxed);
   }
   // Every pair keeps one column tile's weights resident: a whole number of pairs per column tile.
   const int pair_tiles = p.num_m_tiles / 2;
@@ -787,7 +789,7 @@ size_t quant_workspace_bytes(int sm_count) {
 // ======================================================================== C ABI
 extern "C" {
 
-int fp8_abi_version(void) { return 3; }
+int fp8_abi_version(void) { return 4; }
 
 int fp8_last_error(char* buf, size_t len) {
   if (buf != nullptr && len > 0) {
@@ -795,6 +797,43 @@ int fp8_last_error(char* buf, size_t len) {
     buf[len - 1] = 0;
   }
   return t_last_status;
+}
+
+}  // extern "C"
+
+// One CTA waits, through the kernels' bounded mbarrier wait, on a barrier that
+// nothing arrives on.  The wait gives up after limit_ns, records
+// kErrTimeoutSelfTest and raises the CTA abort flag; every thread then returns.
+// returned[0] = 1 when the waiting thread came back with "gave up".
+__global__ void wait_selftest_kernel(int* err, uint64_t limit_ns, int* returned) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool done = mbar_wait_limit(&bar, 0, &abort_flag, err, kErrTimeoutSelfTest, limit_ns);
+    returned[0] = done ? 2 : 1;
+  }
+  __syncthreads();
+}
+
+extern "C" {
+
+int fp8_selftest_wait_timeout(uint64_t limit_ns, int* returned, fp8_stream_t stream) {
+  FP8_REQUIRE(limit_ns > 0 && limit_ns <= 1000000000ull, FP8_ERR_INVALID_ARGUMENT,
+              "limit_ns must be in (0, 1e9]");
+  FP8_REQUIRE(returned != nullptr && aligned(returned, 4), FP8_ERR_INVALID_ARGUMENT, "bad returned pointer");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  count_launches(1);
+  FP8_CUDA_TRY(launch_kernel(wait_selftest_kernel, dim3(1), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream), 1,
+                             kStreamingKernel, st->err_ptr, limit_ns, returned));
+  return ok();
 }
 
 int fp8_device_error(int* code_out, fp8_stream_t stream) {
@@ -867,7 +906,7 @@ constexpr int kNoAllocPartials = 2048;
 static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
 
 namespace {
-float* g_noalloc_ptr[kMaxDevices] = {};
+std::atomic<float*> g_noalloc_ptr[kMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
 // Device address of g_noalloc_partials for the current device.  The host-side
@@ -877,15 +916,18 @@ int noalloc_scratch(float** out) {
   int dev = 0;
   FP8_CUDA_TRY(cudaGetDevice(&dev));
   FP8_REQUIRE(dev >= 0 && dev < kMaxDevices, FP8_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  float* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    ptr = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (ptr == nullptr) {
       void* p = nullptr;
       FP8_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_partials));
-      g_noalloc_ptr[dev] = static_cast<float*>(p);
+      ptr = static_cast<float*>(p);
+      g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
     }
   }
-  *out = g_noalloc_ptr[dev];
+  *out = ptr;
   return FP8_OK;
 }
 }  // namespace

@@ -37,6 +37,7 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 103,  // epilogue gave up waiting for a finished accumulator
   kErrTimeoutDrain = 104,     // teardown gave up waiting for in-flight async work
   kErrTimeoutQuant = 105,     // streaming quantize pass gave up waiting for a bulk copy / free stage
+  kErrTimeoutSelfTest = 199,  // the failure-path self test's wait gave up (expected)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -106,10 +107,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns false
-// (and makes sure the CTA abort flag is set) if the CTA is aborting or the
-// deadline passes.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+// (and makes sure the CTA abort flag is set) if the CTA is aborting or more
+// than limit_ns of wall time pass.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                int* err, int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t it = 0;
@@ -117,13 +118,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if ((++it & 31u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > FP8_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         record_error(err, code);
         return false;
       }
     }
   }
+}
+
+// The kernels' wait: mbar_wait_limit with the library-wide limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err, int code) {
+  return mbar_wait_limit(bar, parity, abort_flag, err, code, FP8_WAIT_TIMEOUT_NS);
 }
 
 // ---------------------------------------------------------------- TMA

@@ -59,6 +59,15 @@ int fp8_last_error(char* buf, size_t len);
  * `stream`.  *code_out = 0 means no device error was recorded. */
 int fp8_device_error(int* code_out, fp8_stream_t stream);
 
+/* Failure-path self test (no counterpart in the reference, which has no
+ * bounded waits).  Launches one CTA that waits, through the same bounded
+ * mbarrier wait every kernel of this library uses, on a barrier that nothing
+ * arrives on, with a limit of limit_ns (0 < limit_ns <= 1e9) instead of the
+ * kernels' 2 s.  The wait gives up, records error code 199 in the device error
+ * word and the kernel returns; *returned (device int) becomes 1.  The context
+ * stays usable.  Read the code with fp8_device_error. */
+int fp8_selftest_wait_timeout(uint64_t limit_ns, int* returned, fp8_stream_t stream);
+
 /* Number of streaming multiprocessors of the current device (launch sizing). */
 int fp8_sm_count(int* out);
 
@@ -82,10 +91,10 @@ int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, voi
 
 /* Allocation-free variant of fp8_quantize_current (same results, bit for bit).
  * No counterpart in the reference: it exists for callers that cannot allocate
- * device memory, e.g. code that runs while a CUDA graph is being captured (where
- * cudaMalloc is not allowed), runtimes whose device memory is entirely owned by
- * another allocator, or a foreign-language host with no device allocator of its
- * own.  It takes no workspace: its scratch (the per-CTA amax partials) is a
+ * device memory, e.g. a runtime whose device memory is entirely owned by
+ * another allocator (a host framework that reserves the whole device at start),
+ * or a foreign-language host reached over FFI that has no device allocator of
+ * its own.  It takes no workspace: its scratch (the per-CTA amax partials) is a
  * static 8 KB array inside this library, one per device, held until the process
  * exits.  Limit: that array has 2048 slots; a call whose amax pass would need
  * more (a device with more than 256 SMs) is rejected with FP8_ERR_UNSUPPORTED.
@@ -96,10 +105,6 @@ int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, voi
 int fp8_quantize_current_noalloc(const void* x_bf16, void* q_e4m3, float* scale_out, int64_t n,
                                  fp8_stream_t stream);
 
-/* Delayed scaling: q = e4m3(clamp(x / *prev_scale, +-448)) and
- * *scale_curr_out = scale of x's own amax.
- * Replaces quantize_fp8_delayed (fp8_kernels.py:518-556) and
- * partial_amax_kernel_delayed (:69-87) + finalize_amax_kernel (:90-102). */
 /* Workspace bytes of fp8_quantize_current_multi for `count` tensors. */
 size_t fp8_quantize_multi_workspace_bytes(int count);
 
@@ -112,6 +117,10 @@ size_t fp8_quantize_multi_workspace_bytes(int count);
 int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const* q_e4m3, float* const* scale_out,
                                const int64_t* n, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
 
+/* Delayed scaling: q = e4m3(clamp(x / *prev_scale, +-448)) and
+ * *scale_curr_out = scale of x's own amax.
+ * Replaces quantize_fp8_delayed (fp8_kernels.py:518-556) and
+ * partial_amax_kernel_delayed (:69-87) + finalize_amax_kernel (:90-102). */
 int fp8_quantize_delayed(const void* x_bf16, void* q_e4m3, const float* prev_scale, float* scale_curr_out,
                          void* workspace, size_t workspace_bytes, int64_t n, fp8_stream_t stream);
 

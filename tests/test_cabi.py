@@ -37,7 +37,7 @@ def test_binding_covers_every_declared_symbol():
 
 
 def test_abi_version():
-    assert _lib.load().fp8_abi_version() == 3
+    assert _lib.load().fp8_abi_version() == 4
 
 
 def _status_and_message(fn, *args):
@@ -240,3 +240,14 @@ def test_weight_transpose_batch_validates_without_touching_cuda():
     assert status == _lib.FP8_ERR_UNSUPPORTED and "1..64" in msg
     status, code, msg = _status_and_message(lib.fp8_conv_weight_transpose_batch, 1, arr, arr, bad, dims, c_void_p(0))
     assert status == _lib.FP8_ERR_UNSUPPORTED and "multiples of 64" in msg
+
+
+def test_selftest_wait_validates_without_touching_cuda():
+    lib = _lib.load()
+    null = c_void_p(0)
+    for limit in (0, 2_000_000_000):
+        status, code, msg = _status_and_message(lib.fp8_selftest_wait_timeout, ctypes.c_uint64(limit), c_void_p(16),
+                                                null)
+        assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "limit_ns" in msg
+    status, code, msg = _status_and_message(lib.fp8_selftest_wait_timeout, ctypes.c_uint64(1000), null, null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "returned" in msg
