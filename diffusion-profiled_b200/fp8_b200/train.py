@@ -40,12 +40,16 @@ class LinearSchedule:
         self.alpha_bars = torch.cumprod(1.0 - betas, dim=0).float().to(device)
         self.max_t = max_t
 
+    def mix(self, x: torch.Tensor, eps: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        """x_t = sqrt(abar_t) x + sqrt(1 - abar_t) eps (ddpm.py:199-202)."""
+        ab = self.alpha_bars[t][:, None, None, None]
+        return ab.sqrt() * x + (1.0 - ab).sqrt() * eps
+
     def noise(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """(x_t, eps, t) for a batch (ddpm.py:190-206)."""
         t = torch.randint(0, self.max_t, (x.shape[0],), device=x.device)
         eps = torch.randn_like(x)
-        ab = self.alpha_bars[t][:, None, None, None]
-        return ab.sqrt() * x + (1.0 - ab).sqrt() * eps, eps, t
+        return self.mix(x, eps, t), eps, t
 
 
 def diffusion_loss(model: torch.nn.Module, x: torch.Tensor, sched: LinearSchedule) -> torch.Tensor:
