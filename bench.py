@@ -305,8 +305,9 @@ def run_b200(args) -> None:
 
     unet = None
     if not args.no_unet:
-        unet = {"b200_path": time_unet(args, dev, world, fp8=True)}
+        unet = {"b200_path": time_unet(args, dev, world, fp8=True, scaling="delayed", skip_empty=True)}
         if world == 1:
+            unet["b200_path_current_scaling"] = time_unet(args, dev, world, fp8=True, scaling="current")
             unet["bf16_reference_ops"] = time_unet(args, dev, world, fp8=False)
             unet["speedup_vs_bf16_reference_ops"] = round(
                 unet["b200_path"]["value"] / unet["bf16_reference_ops"]["value"], 3)
@@ -580,9 +581,13 @@ def roofline(kernels: dict, peaks: dict, batch: int) -> dict | None:
             "algorithmic": f"3 B/elem = {work:.4g} B per call"}
 
 
-def time_unet(args, dev, world, fp8: bool) -> dict:
+def time_unet(args, dev, world, fp8: bool, scaling: str = "delayed", skip_empty: bool = False) -> dict:
     """BASELINE configs 4/5: the CUDA-graph UNet training step (B images per GPU,
-    data parallel with the bucketed bf16 all-reduce when world > 1)."""
+    data parallel with the bucketed bf16 all-reduce when world > 1).
+
+    ``skip_empty``: delayed scaling where an all-zero tensor records scale 0 in its
+    history (the configuration that meets the 200-step 2 % loss bar; the reference's
+    semantics record 1.0, which runs the same kernels at the same speed)."""
     import torch.distributed as dist
 
     from fp8_b200.train import GraphedTrainStep, TrainConfig, build_model, images_per_second
@@ -590,7 +595,7 @@ def time_unet(args, dev, world, fp8: bool) -> dict:
     rank = int(os.environ.get("RANK", "0"))
     # the B200 path: FP8 convs + fused norm/activation ops; the comparison: the
     # reference's bf16 model with its torch ops
-    model = build_model(fp8=fp8, scaling="delayed", device=dev, seed=0, fused_norm=fp8)
+    model = build_model(fp8=fp8, scaling=scaling, device=dev, seed=0, fused_norm=fp8, skip_empty=fp8 and skip_empty)
     cfg = TrainConfig(batch_size=args.batch, fused_optimizer=fp8)  # the reference-ops arm keeps torch's AdamW
     if args.bucket_mb:
         cfg.allreduce_bucket_mb = args.bucket_mb
@@ -626,12 +631,14 @@ def time_unet(args, dev, world, fp8: bool) -> dict:
     return {"metric": "UNet train imgs/s", "value": round(images_per_second(args.batch, world, ms), 1),
             "unit": "imgs/s", "ms_per_step": round(ms, 4), "steps": args.unet_steps, "batch_per_gpu": args.batch,
             "global_batch": args.batch * world, "n_gpus": world, "mean_loss": round(loss, 4),
-            "fp8": ("whitelisted 3x3 convs, delayed scaling" if fp8 else "off (bf16 autocast)"),
+            "fp8": (f"whitelisted 3x3 convs, {scaling} scaling"
+                    + (", all-zero tensors record scale 0 in the histories" if skip_empty and scaling == "delayed"
+                       else "") if fp8 else "off (bf16 autocast)"),
             "norm_activation": ("fused GroupNorm/FiLM/SiLU/dropout kernels (the FP8 conv input written as e4m3), "
                                 "LayerNorm kernels in the attention blocks, fused nearest resampling + skip "
                                 "concatenation" if fp8 else "torch ops (reference)"),
             "scale_history": ("device-side (the casts read and update the histories; batched weight quantize)"
-                              if fp8 else None),
+                              if fp8 and scaling == "delayed" else None),
             "optimizer": ("clip + AdamW + EMA in one pass (fp8_b200.optim)" if fp8
                           else "clip_grad_norm_ + torch fused AdamW + foreach EMA"),
             "conv_modules": n_fp8, "allreduce_bf16_bytes_per_step": allreduce,

@@ -225,6 +225,10 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 // (their streaming kernels leave no SM free early), so it is off by default.
 int g_pdl = 0;
 
+// History entry of an all-zero tensor in the delayed-scaling windows:
+// 0 = the reference's (its scale, 1.0), 1 = 0.0 (fp8_set_empty_tensor_history).
+int g_empty_zero = 0;
+
 enum KernelClass { kStreamingKernel = 0, kTensorKernel = 1 };
 
 // Launch `kern` on `stream`, with programmatic stream serialization when enabled
@@ -1017,7 +1021,7 @@ int fp8_quantize_delayed_window(const void* x_bf16, void* q_e4m3, float* window,
                                 size_t workspace_bytes, int64_t n, fp8_stream_t stream) {
   if (int s = check_window(window, window_len, window_pos, scale_used_out)) return s;
   return quantize_delayed_impl(x_bf16, q_e4m3, DelayedSource{nullptr, window, window_len, scale_used_out}, nullptr,
-                               WindowUpdate{window, window_pos, window_len, advance ? 1 : 0}, workspace,
+                               WindowUpdate{window, window_pos, window_len, advance ? 1 : 0, g_empty_zero}, workspace,
                                workspace_bytes, n, stream);
 }
 
@@ -1338,6 +1342,12 @@ int fp8_set_pdl(int mode) {
   return ok();
 }
 
+int fp8_set_empty_tensor_history(int mode) {
+  FP8_REQUIRE(mode == 0 || mode == 1, FP8_ERR_INVALID_ARGUMENT, "empty-tensor history mode must be 0 or 1");
+  g_empty_zero = mode;
+  return ok();
+}
+
 int fp8_set_conv_algo(int algo) {
   FP8_REQUIRE(algo >= 0 && algo <= 4, FP8_ERR_INVALID_ARGUMENT, "conv algo must be 0 (auto), 1, 2, 3 or 4");
   g_conv_algo = algo;
@@ -1460,7 +1470,7 @@ int fp8_gn_act_quant_fwd_window(const void* x, int x_fp32, const float* gamma, c
   if (int s = check_window(window, window_len, window_pos, scale_used_out)) return s;
   return gn_act_quant_impl(x, x_fp32, gamma, beta, film, film_ld, seed, p, eps,
                            DelayedSource{nullptr, window, window_len, scale_used_out}, stats, q_e4m3, nullptr,
-                           WindowUpdate{window, window_pos, window_len, advance ? 1 : 0}, n, hw, c, groups, workspace,
+                           WindowUpdate{window, window_pos, window_len, advance ? 1 : 0, g_empty_zero}, n, hw, c, groups, workspace,
                            workspace_bytes, stream);
 }
 
@@ -1544,7 +1554,7 @@ int fp8_gn_act_bwd_quant(const void* x, const void* dy, const float* gamma, cons
   float* part = static_cast<float*>(workspace);
   float* amax_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + gn_bytes);
   const GnOut o{nullptr, static_cast<uint8_t*>(dxq), DelayedSource{nullptr, window, window_len, scale_used_out},
-                amax_part, ScaleFold{fold_counter(st), nullptr, WindowUpdate{window, window_pos, window_len, 0}}};
+                amax_part, ScaleFold{fold_counter(st), nullptr, WindowUpdate{window, window_pos, window_len, 0, g_empty_zero}}};
   if (int s = launch_gn_bwd(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(dy), sh, stats, q, part,
                             totals, static_cast<uint16_t*>(dx), gn_bwd_reduce_smem(c, groups),
                             gn_bwd_apply_smem(c, groups), st->sm_count, reinterpret_cast<cudaStream_t>(stream), &o))
@@ -1999,6 +2009,7 @@ int fp8_quantize_weights_delayed(int count, const float* const* w, void* const* 
   WeightBatch b{};
   b.count = count;
   b.window_len = window_len;
+  b.empty_zero = g_empty_zero;
   int chunks = 0;
   for (int t = 0; t < count; ++t) {
     FP8_REQUIRE(n[t] > 0 && n[t] < (1ll << 31), FP8_ERR_INVALID_ARGUMENT, "weight %d: bad size", t);
@@ -2278,7 +2289,7 @@ int fp8_add_scale_bwd_quant(const void* dy, int y_dtype, void* da, int a_dtype, 
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= grid * sizeof(float) && aligned(workspace, 4),
               FP8_ERR_WORKSPACE, "join workspace too small: need %zu bytes", grid * sizeof(float));
   const DelayedSource src{nullptr, window, window_len, scale_used_out};
-  const ScaleFold fold{fold_counter(st), nullptr, WindowUpdate{window, window_pos, window_len, 0}};
+  const ScaleFold fold{fold_counter(st), nullptr, WindowUpdate{window, window_pos, window_len, 0, g_empty_zero}};
   float* partials = static_cast<float*>(workspace);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   int r;

@@ -180,7 +180,15 @@ struct WindowUpdate {
   int64_t* pos;
   int len;
   int advance;
+  // 0: the reference's entry for an all-zero tensor (its scale, 1.0); 1: 0.0,
+  // so that such a tensor adds nothing to the history's max
+  int empty_zero;
 };
+
+// The history entry of a tensor with this amax.
+__device__ __forceinline__ float history_entry(float amax, int empty_zero) {
+  return (empty_zero && !(amax > 0.0f)) ? 0.0f : scale_from_amax(amax);
+}
 
 // Fold `count` partial maxima into the tensor scale (every CTA does this; the
 // partials are a few KB and L2 resident).
@@ -235,11 +243,11 @@ struct ScaleFold {
   WindowUpdate wu;        // window == null: no history update
 };
 
-__device__ __forceinline__ void store_scale(float s, float* scale_out, const WindowUpdate& wu) {
-  if (scale_out != nullptr) *scale_out = s;
+__device__ __forceinline__ void store_scale(float amax, float* scale_out, const WindowUpdate& wu) {
+  if (scale_out != nullptr) *scale_out = scale_from_amax(amax);
   if (wu.window != nullptr) {
     const int64_t p = *wu.pos;
-    wu.window[p] = s;
+    wu.window[p] = history_entry(amax, wu.empty_zero);
     if (wu.advance) *wu.pos = (p + 1) % wu.len;
   }
 }
@@ -257,9 +265,9 @@ __device__ __forceinline__ void fold_scale_if_last(const float* partials, const 
   __threadfence();
   float m = 0.0f;
   for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += NT) m = fmaxf(m, __ldcg(partials + i));
-  const float s = scale_from_amax(block_max<NT>(m));
+  const float amax = block_max<NT>(m);
   if (threadIdx.x == 0) {
-    store_scale(s, f.scale_out, f.wu);
+    store_scale(amax, f.scale_out, f.wu);
     *f.counter = 0u;
   }
 }
@@ -815,6 +823,7 @@ struct WeightBatch {
   int chunk_begin[kMaxBatchWeights + 1];
   int count;
   int window_len;
+  int empty_zero;  // as WindowUpdate::empty_zero
 };
 static_assert(sizeof(WeightBatch) < 4096, "kernel parameter size");
 
@@ -887,8 +896,12 @@ __global__ void __launch_bounds__(kQuantThreads) weight_finalize_kernel(WeightBa
                                                                          const float* __restrict__ partials) {
   pdl_wait();
   const int t = blockIdx.x;
-  const float s = fold_partials_to_scale(partials + b.chunk_begin[t], b.chunk_begin[t + 1] - b.chunk_begin[t]);
-  if (threadIdx.x == 0) b.window[t][*b.pos[t]] = s;
+  const float* part = partials + b.chunk_begin[t];
+  const int count = b.chunk_begin[t + 1] - b.chunk_begin[t];
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < count; i += kQuantThreads) m = fmaxf(m, part[i]);
+  m = block_max<kQuantThreads>(m);
+  if (threadIdx.x == 0) b.window[t][*b.pos[t]] = history_entry(m, b.empty_zero);
 }
 
 }  // namespace fp8b

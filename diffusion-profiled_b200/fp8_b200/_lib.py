@@ -165,6 +165,7 @@ _SIGNATURES: dict[str, tuple] = {
                                c_size_t, c_void_p]),
     "fp8_set_conv_algo": (c_int, [c_int]),
     "fp8_set_pdl": (c_int, [c_int]),
+    "fp8_set_empty_tensor_history": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()
@@ -238,6 +239,12 @@ def set_pdl(mode: int = 0) -> None:
     """0: plain stream order (the default); 1: programmatic dependent launch of
     the tensor-core kernels; 2: of every kernel."""
     check(load().fp8_set_pdl(int(mode)), "fp8_set_pdl")
+
+
+def set_empty_tensor_history(mode: int = 0) -> None:
+    """0: an all-zero tensor records its scale 1.0 in the delayed-scaling histories (the
+    reference); 1: it records 0.0 (adds nothing to the history max)."""
+    check(load().fp8_set_empty_tensor_history(int(mode)), "fp8_set_empty_tensor_history")
 
 
 def set_conv_algo(algo: int = 0) -> None:

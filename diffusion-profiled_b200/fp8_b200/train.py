@@ -201,7 +201,8 @@ class EMA:
 class GraphedTrainStep:
     """The captured training step; ``step(images)`` copies the batch in and replays."""
 
-    def __init__(self, model: UNet, cfg: TrainConfig, device: torch.device, dp_group=None, use_graph: bool = True):
+    def __init__(self, model: UNet, cfg: TrainConfig, device: torch.device, dp_group=None, use_graph: bool = True,
+                 external_noise: bool = False):
         self.model = model
         self.cfg = cfg
         self.device = device
@@ -223,6 +224,11 @@ class GraphedTrainStep:
         cin, res = model.config.in_channels, model.config.in_resolution
         self.static_batch = torch.zeros(cfg.batch_size, cin, res, res, device=device).to(
             memory_format=torch.channels_last)
+        # external_noise: the step takes its timesteps and noise from these buffers (step(images, t, eps))
+        # instead of drawing them, so that runs of different models see the same draws
+        self.external_noise = external_noise
+        self.static_t = torch.zeros(cfg.batch_size, dtype=torch.int64, device=device)
+        self.static_eps = torch.zeros_like(self.static_batch)
         self.loss_acc = torch.zeros((), device=device)
         self.graph = None
         self.use_graph = use_graph
@@ -236,7 +242,11 @@ class GraphedTrainStep:
         if self.dp is not None:
             self.dp.start()
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
-            loss = diffusion_loss(self.model, self.static_batch, self.sched)
+            if self.external_noise:
+                x_t = self.sched.mix(self.static_batch, self.static_eps, self.static_t)
+                loss = F.mse_loss(self.model(x_t, self.static_t), self.static_eps)
+            else:
+                loss = diffusion_loss(self.model, self.static_batch, self.sched)
         self.loss_acc.add_(loss.detach())
         loss.backward()
         if self.dp is not None:
@@ -278,9 +288,14 @@ class GraphedTrainStep:
                 self._body()
         self.loss_acc.zero_()
 
-    def step(self, images: torch.Tensor | None = None) -> None:
+    def step(self, images: torch.Tensor | None = None, t: torch.Tensor | None = None,
+             eps: torch.Tensor | None = None) -> None:
         if images is not None:
             self.static_batch.copy_(images, non_blocking=True)
+        if t is not None:
+            self.static_t.copy_(t, non_blocking=True)
+        if eps is not None:
+            self.static_eps.copy_(eps, non_blocking=True)
         if self.graph is not None:
             self.graph.replay()
         else:
@@ -295,14 +310,19 @@ class GraphedTrainStep:
 
 def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16,), p_drop: float = 0.1,
                 device: torch.device | str = "cuda", seed: int = 0, fused_norm: bool = True,
-                fused_resample: bool | None = None) -> UNet:
+                fused_resample: bool | None = None, plain: bool = False, skip_empty: bool = False) -> UNet:
     """The reference UNet; ``fused_norm`` / ``fused_resample`` (default: as ``fused_norm``) route its
-    norm -> activation chains and its resampling + concatenation to this library's kernels."""
+    norm -> activation chains and its resampling + concatenation to this library's kernels.
+    ``plain``: the reference's op structure throughout (every FP8 conv a ``triton_conv2d_fp8`` call,
+    scale windows kept by torch ops in the module).  ``skip_empty``: ``fp8_history_skip_empty``."""
     torch.manual_seed(seed)
+    if plain:
+        fused_norm, fused_resample = False, False
     fr = fused_norm if fused_resample is None else fused_resample
     cfg = UNetConfig(fp8_convs_enabled=fp8, fp8_scaling_type=scaling, attn_resolutions=list(attn_resolutions),
                      p_drop=p_drop, fused_norm=fused_norm, fused_resample=fr, fused_residual=fr,
-                     batched_time_embed=fr, fused_skip_cast=fr, batched_weight_cast=fr)
+                     batched_time_embed=fr, fused_skip_cast=fr, batched_weight_cast=fr,
+                     device_scale_history=not plain, fp8_history_skip_empty=skip_empty)
     model = UNet(cfg).to(memory_format=torch.channels_last)
     return model.to(device)
 

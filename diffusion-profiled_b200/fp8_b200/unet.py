@@ -27,7 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import ops
+from . import _lib, ops
 from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed, quantize_conv_weights
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
 from .resample import downsample_nearest, residual_join, upsample_cat, upsample_cat_pair
@@ -76,6 +76,12 @@ class UNetConfig:
     # 1x1 skip convs, time-embedding linears), and the casts of their gradients back, one
     # launch each way per step (fp8_b200.weights)
     batched_weight_cast: bool = True
+    # delayed scaling: an all-zero tensor (conv_2's zero-initialised weight, or conv_1's output
+    # gradient on the first, uncalibrated step) records scale 0 instead of the reference's 1.0 in
+    # its history, so the history max is not held at 1.0 for the next fp8_amax_history steps
+    # (fp8_b200._lib.set_empty_tensor_history).  Off by default: the reference records 1.0.
+    # Needs device_scale_history.
+    fp8_history_skip_empty: bool = False
 
     def as_dict(self):
         return asdict(self)
@@ -321,6 +327,8 @@ class Stage(nn.Module):
 class UNet(nn.Module):
     def __init__(self, config: UNetConfig):
         super().__init__()
+        if config.fp8_history_skip_empty and not config.device_scale_history:
+            raise ValueError("fp8_history_skip_empty needs device_scale_history")
         self.config = config
         self.base_channs = base = config.base_hidden
         chans = [s * base for s in config.scales]
@@ -368,6 +376,10 @@ class UNet(nn.Module):
         return emb
 
     def forward(self, x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        cfg = self.config
+        if cfg.fp8_convs_enabled and cfg.fp8_scaling_type == "delayed" and cfg.device_scale_history:
+            # process-wide mode, read by the history-updating launches of this step (forward and backward)
+            _lib.set_empty_tensor_history(1 if cfg.fp8_history_skip_empty else 0)
         # The weights of the delayed-scaling FP8 convs that ran last time are quantized in one batch
         # (identical bytes and histories to quantizing each inside its conv).
         batch = getattr(self, "_fp8_delayed_convs", None)

@@ -242,6 +242,21 @@ int fp8_set_conv_algo(int algo);
  * meant for benchmarks and tests. */
 int fp8_set_pdl(int mode);
 
+/* What the delayed-scaling histories record for a tensor whose amax is 0 (an
+ * all-zero weight, or the all-zero output gradient of a layer whose only path
+ * back runs through FP8 convs on their first, uncalibrated call).
+ * mode 0 (default): the reference's entry, the tensor's scale 1.0
+ * (finalize_amax_kernel, fp8_kernels.py:90-102, stored by unet.py:84-89 and
+ * fp8_kernels.py:887-889); the history max then stays >= 1.0 for the next
+ * window-length calls and e4m3 flushes values below ~1e-3 of that tensor to 0.
+ * mode 1: 0.0, so the tensor adds nothing to the history max (the next cast
+ * uses the largest scale of the tensors that had values).  Applies to the
+ * entry points that update histories on the device (the *_window calls and
+ * fp8_quantize_weights_delayed); the scale outputs keep the reference value.
+ * Process-wide, read when a call launches its kernels (a captured CUDA graph
+ * keeps the mode it was captured with).  No counterpart in the reference. */
+int fp8_set_empty_tensor_history(int mode);
+
 /* Tuning override for the quantize grids: CTAs per SM of the amax pass and of
  * the cast pass (1..8; 0 restores the built-in choice).  Process-wide. */
 int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);

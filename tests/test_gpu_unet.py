@@ -99,20 +99,28 @@ def test_graphed_train_step_runs_and_updates(cuda):
     step.release()
 
 
-def _loss_curve(cuda, fp8: bool, steps: int, batch: int, scaling: str = "current",
-                fused_norm: bool = True) -> np.ndarray:
+LOSS_STEPS, LOSS_BATCH = 200, 128
+
+
+def _loss_curve(cuda, **model_kw) -> np.ndarray:
+    """200 CUDA-graph training steps (BASELINE config 4 architecture, synthetic uniform
+    images).  Timesteps and noise come from one seeded host generator, so every model
+    sees the same draws and the curves differ only by the models' arithmetic."""
     from fp8_b200.train import GraphedTrainStep, TrainConfig, build_model
 
-    model = build_model(fp8=fp8, scaling=scaling, device=cuda, seed=0, fused_norm=fused_norm)
-    step = GraphedTrainStep(model, TrainConfig(batch_size=batch), cuda)
+    model = build_model(device=cuda, seed=0, **model_kw)
+    step = GraphedTrainStep(model, TrainConfig(batch_size=LOSS_BATCH), cuda, external_noise=True)
     torch.manual_seed(1234)
     torch.cuda.manual_seed(1234)
     step.prepare()
     g = torch.Generator().manual_seed(7)
-    data = [(torch.rand(batch, 3, 32, 32, generator=g) * 2 - 1).to(cuda) for _ in range(8)]
+    data = [(torch.rand(LOSS_BATCH, 3, 32, 32, generator=g) * 2 - 1) for _ in range(8)]
+    gn = torch.Generator().manual_seed(99)
     losses = []
-    for i in range(steps):
-        step.step(data[i % len(data)])
+    for i in range(LOSS_STEPS):
+        t = torch.randint(0, 1000, (LOSS_BATCH,), generator=gn)
+        eps = torch.randn(LOSS_BATCH, 3, 32, 32, generator=gn)
+        step.step(data[i % len(data)].to(cuda), t.to(cuda), eps.to(cuda))
         losses.append(step.loss_acc.clone())
         step.loss_acc.zero_()
     torch.cuda.synchronize()
@@ -120,32 +128,69 @@ def _loss_curve(cuda, fp8: bool, steps: int, batch: int, scaling: str = "current
     return np.array([l.item() for l in losses])
 
 
-def test_fp8_loss_curve_within_2pct_of_bf16(cuda):
-    """200 training steps (BASELINE config 4 architecture, synthetic uniform images):
-    the B200 path (FP8 convs, current scaling as the reference's default unet.py:24,
-    fused norm/activation ops) against the reference's bf16 model (torch ops).
-
-    The curve is compared on its final 50 steps, where it has flattened: over
-    steps 100-200 the bf16 model alone spread 2.4 % across three seeds (mean
-    loss 0.1866-0.1911), over steps 150-200 0.3 % (0.1896-0.1901), with the
-    FP8 + fused path at 0.1882-0.1892 on two seeds."""
-    fp8 = _loss_curve(cuda, True, 200, 128, scaling="current")
-    bf16 = _loss_curve(cuda, False, 200, 128, fused_norm=False)
-    assert np.isfinite(fp8).all() and np.isfinite(bf16).all()
-    tail_fp8, tail_bf16 = fp8[-50:].mean(), bf16[-50:].mean()
-    assert tail_bf16 < bf16[:10].mean()  # it trains
-    rel = abs(tail_fp8 - tail_bf16) / tail_bf16
-    assert rel <= 0.02, (tail_fp8, tail_bf16, rel)
+def _curve_gap(curve: np.ndarray, ref: np.ndarray) -> tuple[float, float]:
+    """(mean over steps 50-200 of |MA10(curve) - MA10(ref)| / MA10(ref),
+        max over steps 50-200 of |MA50(curve) - MA50(ref)| / MA50(ref))."""
+    def ma(c, k):
+        return np.convolve(c, np.ones(k) / k, mode="valid")
+    m10, r10 = ma(curve, 10)[41:], ma(ref, 10)[41:]  # windows ending at steps 50 .. 200
+    m50, r50 = ma(curve, 50), ma(ref, 50)
+    return float(np.mean(np.abs(m10 - r10) / r10)), float(np.max(np.abs(m50 - r50) / r50))
 
 
-def test_delayed_scaling_trains(cuda):
-    """Delayed scaling (train.py's fastest config) keeps the max scale of the last
-    1024 steps, so early large gradients keep later small ones coarse; over the
-    first 200 steps its loss trails bf16 by ~10 % (measured) and it must still
-    train and stay finite."""
-    curve = _loss_curve(cuda, True, 200, 128, scaling="delayed")
-    assert np.isfinite(curve).all()
-    assert curve[-50:].mean() < 0.5 * curve[:10].mean()
+@pytest.fixture(scope="module")
+def loss_curves(cuda):
+    """The bf16 reference model (the reference's op structure, pinned to the reference's
+    unet.py by tests/test_gpu_unet_reference.py) and the B200 FP8 paths."""
+    return {
+        "bf16": _loss_curve(cuda, fp8=False, plain=True),
+        "fp8_current": _loss_curve(cuda, fp8=True, scaling="current"),
+        "fp8_delayed_skip_empty": _loss_curve(cuda, fp8=True, scaling="delayed", skip_empty=True),
+        "fp8_delayed": _loss_curve(cuda, fp8=True, scaling="delayed"),
+        "fp8_delayed_plain": _loss_curve(cuda, fp8=True, scaling="delayed", plain=True),
+    }
+
+
+# Measured on a B200 (mean MA10 gap, max MA50 gap): FP8 current 0.13 %, 1.0 %; delayed with
+# empty tensors recording 0 0.53 %, 1.8 %; the bf16 model with the fused norm kernels against
+# the same model on torch ops 0.48 %, 1.1 %; delayed with the reference's history semantics
+# 10.4 %, 16 % (fused) and 8.8 %, 16 % (the reference's op structure).
+CURVE_MEAN_TOL = 0.02
+CURVE_MA50_TOL = 0.03
+
+
+@pytest.mark.parametrize("name", ["fp8_current", "fp8_delayed_skip_empty"])
+def test_fp8_loss_curve_within_2pct_of_bf16(loss_curves, name):
+    """North-star loss bar: over 200 steps the FP8 curve stays within 2 % of bf16 (mean of
+    the 10-step moving average's relative gap over steps 50-200; the 50-step moving average
+    within 3 % everywhere).  Both FP8 scalings meet it: current scaling (unet.py:24's default)
+    and delayed scaling (train.py:230-231's fastest config) when an all-zero tensor records
+    scale 0 in its history."""
+    curve, ref = loss_curves[name], loss_curves["bf16"]
+    assert np.isfinite(curve).all() and np.isfinite(ref).all()
+    assert ref[-50:].mean() < 0.5 * ref[:10].mean()  # it trains
+    mean_gap, ma50_gap = _curve_gap(curve, ref)
+    print(f"{name}: mean MA10 gap {mean_gap:.4f}, max MA50 gap {ma50_gap:.4f}")
+    assert mean_gap <= CURVE_MEAN_TOL, (name, mean_gap)
+    assert ma50_gap <= CURVE_MA50_TOL, (name, ma50_gap)
+
+
+def test_delayed_gap_is_the_reference_history_semantics(loss_curves):
+    """With the reference's delayed-scaling bookkeeping, the first (uncalibrated) pass leaves
+    scale 1.0 (the scale of an all-zero tensor, finalize_amax_kernel) in the dY histories of
+    every conv_1 and in the weight histories of the zero-initialised conv_2s; the history max
+    keeps it for 1024 steps and e4m3 flushes those gradients / weights to zero.  The curve then
+    trails bf16 by well over 2 % -- on the reference's own op structure (plain) as on the fused
+    path -- and recording 0 for empty tensors removes the gap (test above)."""
+    ref = loss_curves["bf16"]
+    for name in ("fp8_delayed", "fp8_delayed_plain"):
+        curve = loss_curves[name]
+        assert np.isfinite(curve).all() and curve[-50:].mean() < 0.5 * curve[:10].mean()
+        mean_gap, _ = _curve_gap(curve, ref)
+        print(f"{name}: mean MA10 gap {mean_gap:.4f}")
+        assert mean_gap > 0.04, (name, mean_gap)
+    skip_gap, _ = _curve_gap(loss_curves["fp8_delayed_skip_empty"], ref)
+    assert skip_gap < 0.5 * _curve_gap(loss_curves["fp8_delayed"], ref)[0]
 
 
 def test_fused_norm_unet_as_accurate_as_torch_ops(cuda):
@@ -265,3 +310,34 @@ def test_unet_with_fp8_linears_trains_like_bf16_linears(cuda):
             qkv = m.up_stages[2].attns[0].qkv
             assert isinstance(qkv, FP8Linear) and qkv.weight.grad is not None and qkv.weight.grad.abs().sum() > 0
     assert abs(losses[True] - losses[False]) <= 0.02 * abs(losses[False])
+
+
+def test_empty_tensor_history_modes(cuda):
+    """fp8_set_empty_tensor_history: an all-zero tensor records scale 1.0 in its history (mode
+    0, the reference's finalize_amax_kernel value) or 0.0 (mode 1); a tensor with values records
+    its scale either way, and the scale outputs keep the reference value."""
+    from fp8_b200 import _lib, ops
+
+    zeros = torch.zeros(2, 128, 8, 8, dtype=torch.bfloat16, device=cuda).contiguous(memory_format=torch.channels_last)
+    vals = _bf16_cl(torch.randn(2, 128, 8, 8)).to(cuda)
+    w_zero = torch.zeros(128, 128, 3, 3, device=cuda).contiguous(memory_format=torch.channels_last)
+    w_vals = (torch.randn(128, 128, 3, 3) * 0.05).to(cuda).contiguous(memory_format=torch.channels_last)
+    try:
+        for mode, empty in ((0, 1.0), (1, 0.0)):
+            _lib.set_empty_tensor_history(mode)
+            win = torch.zeros(4, device=cuda)
+            pos = torch.zeros((), dtype=torch.int64, device=cuda)
+            ops.quantize_delayed_window(zeros, win, pos, True)
+            ops.quantize_delayed_window(vals, win, pos, True)
+            _, s_vals = oracle.quantize_tensor(vals.cpu())
+            assert win[0].item() == empty and win[1].item() == float(s_vals.item()), mode
+            assert int(pos.item()) == 2
+            wins = [torch.zeros(4, device=cuda), torch.zeros(4, device=cuda)]
+            poss = [torch.zeros((), dtype=torch.int64, device=cuda) for _ in range(2)]
+            ops.quantize_weights_delayed([w_zero, w_vals], wins, poss)
+            _, s_w = oracle.quantize_tensor(w_vals.to(torch.bfloat16).cpu())
+            assert wins[0][0].item() == empty and wins[1][0].item() == float(s_w.item()), mode
+            q, s = ops.quantize_delayed(zeros, torch.ones((), device=cuda))
+            assert s.item() == 1.0  # the op's scale output is the reference's in both modes
+    finally:
+        _lib.set_empty_tensor_history(0)

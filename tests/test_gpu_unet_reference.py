@@ -39,14 +39,18 @@ pytestmark = pytest.mark.gpu
 
 GOLDEN_DIR = Path(__file__).resolve().parent / "golden"
 
-# Tolerances against the fp32 CPU reference.  The B200 path computes the
-# non-FP8 layers in bf16 (autocast) and re-quantizes their outputs, so a few
-# e4m3 bytes per tensor land one step apart from the fp32 run's; measured
-# errors are well inside these.
-OUT_RTOL = 5e-2  # ||y - y_ref|| / ||y_ref||
-LOSS_RTOL = 2e-2
-GRAD_RTOL = 0.1  # per parameter, |n - n_ref| / n_ref and |<g - g_ref, r>| / n_ref, for 95 % of them
+# Tolerances.  The B200 path computes the non-FP8 layers in bf16 (autocast), so
+# the inputs of its FP8 convs differ from the fp32 reference run's by bf16
+# rounding and some e4m3 bytes land one step apart; through 44 FP8 convs these
+# flips add up to the same distance that separates the reference's own FP8 run
+# from its fp32 run on the same inputs (FP8 rounding noise, measured from the
+# fixture itself).  Outputs and gradients must stay within 1.5x that noise
+# floor; the loss within 1 %; scales to within bf16 noise; weight scales and
+# window positions exactly.
+NOISE_FACTOR = 1.5
+LOSS_RTOL = 1e-2
 SCALE_RTOL = 3e-2  # activation / dY scale windows
+UNCALIBRATED_RTOL = 5e-2  # first delayed pass: FP8 convs output 0, the rest is bf16 vs fp32
 
 
 def _gen():
@@ -103,22 +107,56 @@ def _grad_errors(model, ref: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     return np.abs(probe[:, 0] - ref[:, 0]) / scale, np.abs(probe[:, 1] - ref[:, 1]) / scale
 
 
-def _check_pass(y, loss, fx, tag: str, s: int, what: str) -> float:
+def _fp8_noise(fx) -> tuple[float, float, float]:
+    """How far the reference's FP8 run (current scaling) is from its fp32 run on the same
+    inputs: output rel L2 and the 95th percentiles of the per-parameter gradient errors."""
+    out = _rel_l2(torch.from_numpy(fx["cur_out"][0]), torch.from_numpy(fx["fp32_out"][0]))
+    ref = fx["fp32_grad_probe"]
+    scale = np.maximum(ref[:, 0], 1e-3 * ref[:, 0].max())
+    cur = fx["cur_grad_probe"]
+    return (out, float(np.percentile(np.abs(cur[:, 0] - ref[:, 0]) / scale, 95)),
+            float(np.percentile(np.abs(cur[:, 1] - ref[:, 1]) / scale, 95)))
+
+
+def _check_pass(y, loss, fx, tag: str, s: int, what: str, out_tol: float) -> float:
     ref_y = torch.from_numpy(fx[f"{tag}_out"][s])
     err = _rel_l2(y, ref_y)
     ref_loss = float(fx[f"{tag}_loss"][s])
-    print(f"{what} pass {s}: output rel L2 {err:.4f}, loss {loss:.5f} vs {ref_loss:.5f}")
-    assert err <= OUT_RTOL, (what, s, err)
+    print(f"{what} pass {s}: output rel L2 {err:.4f} (bound {out_tol:.4f}), loss {loss:.5f} vs {ref_loss:.5f}")
+    assert err <= out_tol, (what, s, err)
     assert abs(loss - ref_loss) <= LOSS_RTOL * ref_loss, (what, s, loss, ref_loss)
     return err
 
 
 def _check_grads(model, fx, tag: str, what: str) -> None:
+    _, n95, p95 = _fp8_noise(fx)
     en, ep = _grad_errors(model, fx[f"{tag}_grad_probe"])
-    print(f"{what} gradients: median norm err {np.median(en):.4f}, 95th pct {np.percentile(en, 95):.4f}, "
-          f"probe 95th pct {np.percentile(ep, 95):.4f}")
-    assert np.percentile(en, 95) <= GRAD_RTOL, (what, np.sort(en)[-10:])
-    assert np.percentile(ep, 95) <= GRAD_RTOL, (what, np.sort(ep)[-10:])
+    print(f"{what} gradients: norm err median {np.median(en):.4f} p95 {np.percentile(en, 95):.4f} "
+          f"(reference FP8 vs fp32 p95 {n95:.4f}); probe p95 {np.percentile(ep, 95):.4f} (reference {p95:.4f})")
+    assert np.percentile(en, 95) <= NOISE_FACTOR * n95 + 0.02, (what, np.sort(en)[-10:])
+    assert np.percentile(ep, 95) <= NOISE_FACTOR * p95 + 0.02, (what, np.sort(ep)[-10:])
+
+
+def test_fp32_unet_on_gpu_matches_reference(cuda, fx):
+    """FP8 off, fp32 without autocast (TF32 off): the torch-op path on the B200 computes
+    what the reference's unet.py computes, to fp32 accumulation order."""
+    prev = torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cudnn.allow_tf32 = torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        model = _model(cuda, False, "current", plain=True)
+        xt = torch.from_numpy(fx["fp32_xt_0"]).to(cuda).contiguous(memory_format=torch.channels_last)
+        t = torch.from_numpy(fx["fp32_t_0"]).to(cuda)
+        eps = torch.from_numpy(fx["fp32_eps_0"]).to(cuda)
+        y = model(xt, t)
+        loss = F.mse_loss(y, eps)
+        loss.backward()
+        err = _rel_l2(y.detach().cpu(), torch.from_numpy(fx["fp32_out"][0]))
+        assert err <= 1e-4, err
+        assert abs(loss.item() - float(fx["fp32_loss"][0])) <= 1e-5 * float(fx["fp32_loss"][0])
+        en, ep = _grad_errors(model, fx["fp32_grad_probe"])
+        assert en.max() <= 1e-3 and ep.max() <= 1e-3, (en.max(), ep.max())
+    finally:
+        torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 @pytest.mark.parametrize("plain", [True, False], ids=["plain", "fused"])
@@ -126,7 +164,7 @@ def test_current_scaling_unet_matches_reference(cuda, fx, plain):
     model = _model(cuda, True, "current", plain)
     y, loss = _pass(model, fx, "cur", 0, cuda)
     what = "plain" if plain else "fused"
-    _check_pass(y, loss, fx, "cur", 0, what)
+    _check_pass(y, loss, fx, "cur", 0, what, NOISE_FACTOR * _fp8_noise(fx)[0])
     _check_grads(model, fx, "cur", what)
 
 
@@ -138,7 +176,8 @@ def test_delayed_scaling_unet_matches_reference(cuda, fx, plain):
     what = "plain" if plain else "fused"
     for s in range(len(fx["del_loss"])):
         y, loss = _pass(model, fx, "del", s, cuda)
-        _check_pass(y, loss, fx, "del", s, what)
+        tol = UNCALIBRATED_RTOL if s == 0 else NOISE_FACTOR * _fp8_noise(fx)[0]
+        _check_pass(y, loss, fx, "del", s, what, tol)
     _check_grads(model, fx, "del", what)
 
     mods = dict(model.named_modules())
@@ -221,6 +260,9 @@ def test_drop_in_under_torch_compile_and_cuda_graph(cuda, fx):
     print("eager", eager, "compiled+graphed", graphed)
     for i, (a, b) in enumerate(zip(graphed, eager)):
         assert np.isfinite(a) and abs(a - b) <= 2e-2 * abs(b), (i, a, b)
+    advanced = 0
     for (na, a), (nb, b) in zip(model_c.named_buffers(), model_e.named_buffers()):
-        if na.endswith("window_pos"):
-            assert int(a.item()) == int(b.item()) == warm + steps, na
+        if na.endswith("window_pos"):  # FP8 convs step once per pass; the others never run FP8
+            assert int(a.item()) == int(b.item()) and int(b.item()) in (0, warm + steps), na
+            advanced += int(b.item()) == warm + steps
+    assert advanced >= 40
