@@ -24,6 +24,7 @@
 #include "resample.cuh"
 #include "optim.cuh"
 #include "cast_batch.cuh"
+#include "attention.cuh"
 
 using namespace fp8b;
 
@@ -2304,6 +2305,79 @@ int fp8_add_scale_bwd_quant(const void* dy, int y_dtype, void* da, int a_dtype, 
                 : launch_add_scale_bwd_quant<uint16_t, uint16_t>(dy, da, db_bf16, dbq_e4m3, src, partials, fold, n,
                                                                   inv_divisor, grid, cs);
   if (r) return r;
+  return ok();
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ FP8 attention
+namespace {
+int attn_check(const void* qkv, int batch, int seq, int heads, int head_dim, int ld_qkv, int ld_o) {
+  FP8_REQUIRE(head_dim == kAttnHeadDim, FP8_ERR_UNSUPPORTED, "attention head_dim must be %d", kAttnHeadDim);
+  FP8_REQUIRE(seq >= 16 && seq <= kAttnMaxSeq && seq % 16 == 0, FP8_ERR_UNSUPPORTED,
+              "attention sequence length must be a multiple of 16 in [16, %d]", kAttnMaxSeq);
+  FP8_REQUIRE(batch > 0 && heads > 0 && static_cast<int64_t>(batch) * heads <= (1 << 30), FP8_ERR_INVALID_ARGUMENT,
+              "bad batch / heads");
+  FP8_REQUIRE(ld_qkv >= 3 * heads * head_dim && ld_qkv % 8 == 0 && ld_o >= heads * head_dim && ld_o % 8 == 0,
+              FP8_ERR_INVALID_ARGUMENT, "row strides must cover the heads and be multiples of 8 elements");
+  FP8_REQUIRE(qkv != nullptr && aligned(qkv, 16), FP8_ERR_INVALID_ARGUMENT, "qkv must be 16-byte aligned");
+  return FP8_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int fp8_attention_fwd(const void* qkv, void* o, float* lse, float* scales, int batch, int seq, int heads,
+                      int head_dim, int ld_qkv, int ld_o, fp8_stream_t stream) {
+  if (int s = attn_check(qkv, batch, seq, heads, head_dim, ld_qkv, ld_o)) return s;
+  FP8_REQUIRE(o && aligned(o, 16) && lse && aligned(lse, 4) && scales && aligned(scales, 16), FP8_ERR_INVALID_ARGUMENT,
+              "o must be 16-byte aligned, lse 4-byte and scales 16-byte");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  AttnParams p{};
+  p.qkv = static_cast<const uint16_t*>(qkv);
+  p.o = static_cast<uint16_t*>(o);
+  p.lse = lse;
+  p.scales = scales;
+  p.seq = seq;
+  p.heads = heads;
+  p.ld_qkv = ld_qkv;
+  p.ld_o = ld_o;
+  p.err = st->err_ptr;
+  constexpr int smem = AttnFwdLayout::kSmemBytes;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  count_launches(1);
+  FP8_CUDA_TRY(launch_kernel(attn_fwd_fp8_kernel, dim3(static_cast<unsigned>(batch * heads)), dim3(kAttnThreads), smem,
+                             reinterpret_cast<cudaStream_t>(stream), 1, kTensorKernel, p));
+  return ok();
+}
+
+int fp8_attention_bwd(const void* qkv, const void* o, const void* dout, const float* lse, const float* scales,
+                      void* dqkv, int batch, int seq, int heads, int head_dim, int ld_qkv, int ld_o,
+                      fp8_stream_t stream) {
+  if (int s = attn_check(qkv, batch, seq, heads, head_dim, ld_qkv, ld_o)) return s;
+  FP8_REQUIRE(o && aligned(o, 16) && dout && aligned(dout, 16) && dqkv && aligned(dqkv, 16) && lse &&
+                  aligned(lse, 4) && scales && aligned(scales, 16),
+              FP8_ERR_INVALID_ARGUMENT, "o, dout and dqkv must be 16-byte aligned, lse 4-byte and scales 16-byte");
+  DeviceState* st;
+  if (int s = device_state(&st)) return s;
+  AttnParams p{};
+  p.qkv = static_cast<const uint16_t*>(qkv);
+  p.o_in = static_cast<const uint16_t*>(o);
+  p.dout = static_cast<const uint16_t*>(dout);
+  p.dqkv = static_cast<uint16_t*>(dqkv);
+  p.lse = const_cast<float*>(lse);
+  p.scales = const_cast<float*>(scales);
+  p.seq = seq;
+  p.heads = heads;
+  p.ld_qkv = ld_qkv;
+  p.ld_o = ld_o;
+  p.err = st->err_ptr;
+  constexpr int smem = AttnBwdLayout::kSmemBytes;
+  FP8_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  count_launches(1);
+  FP8_CUDA_TRY(launch_kernel(attn_bwd_kernel, dim3(static_cast<unsigned>(batch * heads)), dim3(kAttnThreads), smem,
+                             reinterpret_cast<cudaStream_t>(stream), 1, kTensorKernel, p));
   return ok();
 }
 

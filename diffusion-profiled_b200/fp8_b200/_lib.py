@@ -31,6 +31,10 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_device_error": (c_int, [POINTER(c_int), c_void_p]),
     "fp8_sm_count": (c_int, [POINTER(c_int)]),
     "fp8_selftest_wait_timeout": (c_int, [ctypes.c_uint64, c_void_p, c_void_p]),
+    "fp8_attention_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                  c_void_p]),
+    "fp8_attention_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                  c_int, c_int, c_int, c_void_p]),
     "fp8_kernel_launch_count": (c_int, [POINTER(ctypes.c_ulonglong)]),
     "fp8_quantize_workspace_bytes": (c_size_t, [c_int64]),
     "fp8_quantize_current": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int64, c_void_p]),

@@ -28,6 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib, ops
+from .attention import attention_supported, fp8_attention
 from .delayed import ConvFP8Delayed, GroupNormActConvFP8Delayed, quantize_conv_weights
 from .fp8_kernels import SUPPORTED_UNET_SHAPES, triton_conv2d_fp8
 from .resample import downsample_nearest, residual_join, upsample_cat, upsample_cat_pair
@@ -82,6 +83,10 @@ class UNetConfig:
     # (fp8_b200._lib.set_empty_tensor_history).  Off by default: the reference records 1.0.
     # Needs device_scale_history.
     fp8_history_skip_empty: bool = False
+    # the attention blocks' softmax(q k^T / sqrt(d)) v as the FP8 attention kernels
+    # (fp8_b200.attention: e4m3 q, k, v per image and head, FP8 QK^T and PV) instead of the
+    # reference's bf16 scaled_dot_product_attention (unet.py:197).  Off by default.
+    fp8_attention: bool = False
 
     def as_dict(self):
         return asdict(self)
@@ -278,6 +283,7 @@ class CHWAttention(nn.Module):
         super().__init__()
         self.fused_norm = config.fused_norm
         self.fused_residual = config.fused_residual
+        self.fp8_attention = config.fp8_attention
         self.nh = config.n_heads
         self.qkv = nn.Linear(hidden_size, 3 * hidden_size, bias=False)
         self.out = nn.Linear(hidden_size, hidden_size, bias=False)
@@ -294,10 +300,13 @@ class CHWAttention(nn.Module):
             tokens = self.norm(tokens)
         w16, self._w16 = self._w16, None
         qkv = self.qkv(tokens) if w16 is None else F.linear(tokens, w16[0], self.qkv.bias)
-        q, k, v = qkv.chunk(3, dim=-1)
-        heads = lambda z: z.unflatten(-1, (self.nh, c // self.nh)).transpose(1, 2)  # noqa: E731
-        o = F.scaled_dot_product_attention(heads(q), heads(k), heads(v))
-        o = o.transpose(1, 2).flatten(2)
+        if self.fp8_attention and attention_supported(qkv, self.nh):
+            o = fp8_attention(qkv, self.nh)  # [B, HW, C], heads side by side as the out projection reads them
+        else:
+            q, k, v = qkv.chunk(3, dim=-1)
+            heads = lambda z: z.unflatten(-1, (self.nh, c // self.nh)).transpose(1, 2)  # noqa: E731
+            o = F.scaled_dot_product_attention(heads(q), heads(k), heads(v))
+            o = o.transpose(1, 2).flatten(2)
         o = self.out(o) if w16 is None else F.linear(o, w16[1], self.out.bias)  # [B, HW, C]
         o = o.transpose(1, 2).reshape(b, c, h, w)
         if self.fused_residual:

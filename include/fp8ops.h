@@ -469,6 +469,35 @@ int fp8_gn_act_quant_fwd(const void* x, int x_fp32, const float* gamma, const fl
 int fp8_cast_batch(int count, const void* const* src, void* const* dst, const int64_t* n, int to_bf16,
                    fp8_stream_t stream);
 
+/* ------------------------------------------------------------ FP8 attention */
+
+/* FP8 self-attention of the attention blocks, forward.  Replaces
+ * F.scaled_dot_product_attention(q, k, v) with q, k, v = chunk(qkv, 3) split
+ * into `heads` heads of head_dim channels (diffusion/unet.py:189-199), which the
+ * reference runs in bf16; the reference has no FP8 attention kernel.
+ *   qkv:  bf16 [batch][seq][ld_qkv], q of head h at columns h*64, k at C + h*64,
+ *         v at 2C + h*64 (C = heads * 64) -- the qkv projection's output rows.
+ *   o:    bf16 [batch][seq][ld_o], head h at columns h*64 (the layout the
+ *         output projection reads).
+ *   lse:  fp32 [batch][heads][seq], log-sum-exp of each query's logits.
+ *   scales: fp32 [batch][heads][4], the e4m3 scales of q, k, v (amax/448 of each
+ *         head's slice) and 0.
+ * q, k and v are quantized per (image, head) with the reference's per-tensor
+ * rule (fp8_kernels.py:90-120), S = q k^T / sqrt(64) and O = P v run on the FP8
+ * tensor cores with P quantized as e4m3(p * 448); softmax in fp32.
+ * head_dim must be 64; seq a multiple of 16 in [16, 256]; qkv, o 16-byte
+ * aligned, ld_qkv and ld_o multiples of 8. */
+int fp8_attention_fwd(const void* qkv, void* o, float* lse, float* scales, int batch, int seq, int heads,
+                      int head_dim, int ld_qkv, int ld_o, fp8_stream_t stream);
+
+/* Backward of fp8_attention_fwd: dqkv (bf16, qkv's layout) from qkv, the
+ * forward's o, lse and scales and the output gradient dout (o's layout).  The
+ * gradient of the forward with straight-through quantizers, computed on the
+ * bf16 tensor cores from the e4m3 values of q, k and v. */
+int fp8_attention_bwd(const void* qkv, const void* o, const void* dout, const float* lse, const float* scales,
+                      void* dqkv, int batch, int seq, int heads, int head_dim, int ld_qkv, int ld_o,
+                      fp8_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

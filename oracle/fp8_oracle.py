@@ -214,6 +214,88 @@ def linear_dw(dyq, xq, sdy, sx) -> torch.Tensor:
     return _finish(acc, np.float32(np.float32(sdy) * np.float32(sx)))
 
 
+# ----------------------------------------------------------------------------- attention
+def _e4m3_values(x: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """e4m3 grid values of x / scale (fp32 IEEE divide, reference clamp, RNE cast)."""
+    with np.errstate(divide="ignore", invalid="ignore"):
+        t = x.astype(np.float32) / scale.astype(np.float32)
+    t = np.fmax(np.float32(-E4M3_MAX), np.fmin(t, np.float32(E4M3_MAX)))
+    return e4m3_decode(e4m3_encode(t))
+
+
+def _split_heads(qkv: torch.Tensor, heads: int) -> np.ndarray:
+    b, seq, c3 = qkv.shape
+    x = qkv.detach().cpu().float().numpy().reshape(b, seq, 3, heads, c3 // (3 * heads))
+    return x.transpose(2, 0, 3, 1, 4)  # [3, B, heads, L, 64]
+
+
+def attention_quantized(qkv: torch.Tensor, heads: int):
+    """Per (image, head): the e4m3 values of q, k, v and their scales amax/448 (1 if amax is 0),
+    the reference's per-tensor quantize rule (fp8_kernels.py:90-120) on each head slice."""
+    x = _split_heads(qkv, heads)
+    amax = np.abs(x).max(axis=(3, 4)).astype(np.float32)  # [3, B, heads]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        scale = np.where(amax > 0, amax / np.float32(E4M3_MAX), np.float32(1.0)).astype(np.float32)
+    vals = _e4m3_values(x, scale[..., None, None])
+    return vals, scale
+
+
+def attention_fwd(qkv: torch.Tensor, heads: int):
+    """FP8 attention forward as attn_fwd_fp8_kernel computes it -> (o bf16 [B, L, C], lse [B, heads, L],
+    scales [B, heads, 3]): S = q k^T (e4m3 values), p = exp((S - max) * sq sk / 8), l = sum p,
+    o = (e4m3(p * 448) v) * sv / (448 l)."""
+    vals, scale = attention_quantized(qkv, heads)
+    q, k, v = (vals[i].astype(np.float64) for i in range(3))
+    sv = scale[2].astype(np.float64)[..., None, None]
+    c = (np.float32(scale[0]) * np.float32(scale[1]) * np.float32(0.125)).astype(np.float64)[..., None, None]
+    s = q @ k.transpose(0, 1, 3, 2)
+    m = s.max(axis=-1, keepdims=True)
+    p = np.exp((s - m) * c)
+    l = p.sum(axis=-1, keepdims=True)
+    pq = e4m3_decode(e4m3_encode((p * 448.0).astype(np.float32))).astype(np.float64)
+    o = (pq @ v) * sv / (448.0 * l)  # [B, heads, L, 64]
+    b, h, seq, d = o.shape
+    o_t = torch.from_numpy(o.transpose(0, 2, 1, 3).reshape(b, seq, h * d).astype(np.float32)).to(torch.bfloat16)
+    lse = torch.from_numpy((m * c + np.log(l))[..., 0].astype(np.float32))
+    return o_t, lse, torch.from_numpy(scale.transpose(1, 2, 0).copy())
+
+
+def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, heads: int) -> torch.Tensor:
+    """attn_bwd_kernel's gradient -> d(qkv) bf16: P = exp(S c - lse), dP = sv dO v^T,
+    dS = P (dP - rowsum(dO o O)); P and dS rounded to bf16; dV = P^T dO, dK = sq/8 dS^T q,
+    dQ = sk/8 dS k (q, k, v their e4m3 values)."""
+    vals, scale = attention_quantized(qkv, heads)
+    q, k, v = (vals[i].astype(np.float64) for i in range(3))
+    b, seq, c = o.shape
+    d = c // heads
+    split = lambda t: t.detach().cpu().float().numpy().reshape(b, seq, heads, d).transpose(0, 2, 1, 3)  # noqa: E731
+    o_h, do_h = split(o).astype(np.float64), split(do).astype(np.float64)
+    cs = (np.float32(scale[0]) * np.float32(scale[1]) * np.float32(0.125)).astype(np.float64)[..., None, None]
+    sv = scale[2].astype(np.float64)[..., None, None]
+    s = q @ k.transpose(0, 1, 3, 2)
+    p = np.exp(s * cs - lse.detach().cpu().double().numpy()[..., None])
+    dp = (do_h @ v.transpose(0, 1, 3, 2)) * sv
+    delta = (do_h * o_h).sum(axis=-1, keepdims=True)
+    ds = p * (dp - delta)
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16).float().double().numpy()  # noqa: E731
+    p_b, ds_b = bf(p), bf(ds)
+    dv = p_b.transpose(0, 1, 3, 2) @ do_h
+    dk = (np.float32(0.125) * scale[0]).astype(np.float64)[..., None, None] * (ds_b.transpose(0, 1, 3, 2) @ q)
+    dq = (np.float32(0.125) * scale[1]).astype(np.float64)[..., None, None] * (ds_b @ k)
+    grads = np.stack([dq, dk, dv])  # [3, B, heads, L, d]
+    out = grads.transpose(1, 3, 0, 2, 4).reshape(b, seq, 3 * c)
+    return torch.from_numpy(out.astype(np.float32)).to(torch.bfloat16)
+
+
+def attention_exact(qkv: torch.Tensor, heads: int) -> torch.Tensor:
+    """Unquantized fp32 multi-head attention of the qkv projection output (the reference's
+    scaled_dot_product_attention, unet.py:197) -> o fp32 [B, L, C]."""
+    x = torch.from_numpy(_split_heads(qkv, heads).copy())
+    o = F.scaled_dot_product_attention(x[0], x[1], x[2])
+    b, h, seq, d = o.shape
+    return o.transpose(1, 2).reshape(b, seq, h * d)
+
+
 def max_rel_err(y: torch.Tensor, ref: torch.Tensor) -> float:
     """``max|y - ref| / max|ref|`` (the tolerance metric of the parity contract)."""
     y = y.detach().cpu().float()
@@ -243,4 +325,8 @@ __all__ = [
     "linear_dw",
     "max_rel_err",
     "round_bf16_toward_zero",
+    "attention_quantized",
+    "attention_fwd",
+    "attention_bwd",
+    "attention_exact",
 ]

@@ -251,3 +251,16 @@ def test_selftest_wait_validates_without_touching_cuda():
         assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "limit_ns" in msg
     status, code, msg = _status_and_message(lib.fp8_selftest_wait_timeout, ctypes.c_uint64(1000), null, null)
     assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "returned" in msg
+
+
+def test_attention_validates_without_touching_cuda():
+    lib = _lib.load()
+    null = c_void_p(0)
+    # head_dim 32, sequence 300, sequence 40: rejected before any CUDA call
+    for head_dim, seq in ((32, 256), (64, 300), (64, 40)):
+        status, code, msg = _status_and_message(lib.fp8_attention_fwd, c_void_p(16), c_void_p(16), c_void_p(16),
+                                                c_void_p(16), 2, seq, 4, head_dim, 768, 256, null)
+        assert status == _lib.FP8_ERR_UNSUPPORTED, (head_dim, seq, msg)
+    status, code, msg = _status_and_message(lib.fp8_attention_bwd, c_void_p(16), c_void_p(16), c_void_p(16),
+                                            c_void_p(16), c_void_p(16), c_void_p(16), 2, 256, 4, 64, 700, 256, null)
+    assert status == _lib.FP8_ERR_INVALID_ARGUMENT and "strides" in msg

@@ -45,11 +45,10 @@ GOLDEN_DIR = Path(__file__).resolve().parent / "golden"
 # flips add up to the same distance that separates the reference's own FP8 run
 # from its fp32 run on the same inputs (FP8 rounding noise, measured from the
 # fixture itself).  Outputs and gradients must stay within 1.5x that noise
-# floor; the loss within 1 %; scales to within bf16 noise; weight scales and
-# window positions exactly.
+# floor; the loss within 1 %; activation and dY scales within the same floor;
+# weight scales, the 1.0 sentinels and window positions exactly.
 NOISE_FACTOR = 1.5
 LOSS_RTOL = 1e-2
-SCALE_RTOL = 3e-2  # activation / dY scale windows
 UNCALIBRATED_RTOL = 5e-2  # first delayed pass: FP8 convs output 0, the rest is bf16 vs fp32
 
 
@@ -186,6 +185,8 @@ def test_delayed_scaling_unet_matches_reference(cuda, fx, plain):
     ref = fx["del_windows"]
     slots = ref.shape[2]
     sentinels = 0
+    # an activation / dY scale is one extreme element of its tensor: it carries the FP8 noise floor
+    scale_rtol = NOISE_FACTOR * _fp8_noise(fx)[0]
     for name, rw in zip(names, ref):
         m = mods[name]
         acts = m.amax_window_acts[:slots].cpu().numpy()
@@ -193,11 +194,11 @@ def test_delayed_scaling_unet_matches_reference(cuda, fx, plain):
         dys = m.amax_window_dy[:slots].cpu().numpy()
         assert int(m.window_pos.item()) == int(rw[3][0]), name
         np.testing.assert_array_equal(wts, rw[1], err_msg=f"{what} {name} weight scales")
-        np.testing.assert_allclose(acts, rw[0], rtol=SCALE_RTOL, atol=0, err_msg=f"{what} {name} input scales")
+        np.testing.assert_allclose(acts, rw[0], rtol=scale_rtol, atol=0, err_msg=f"{what} {name} input scales")
         one = rw[2] == 1.0
         sentinels += int(one.sum())
         np.testing.assert_array_equal(dys[one], rw[2][one], err_msg=f"{what} {name} dY sentinel")
-        np.testing.assert_allclose(dys[~one], rw[2][~one], rtol=SCALE_RTOL, atol=0, err_msg=f"{what} {name} dY scales")
+        np.testing.assert_allclose(dys[~one], rw[2][~one], rtol=scale_rtol, atol=0, err_msg=f"{what} {name} dY scales")
     assert sentinels > 0  # the reference's uncalibrated first pass leaves dY scale 1.0 behind
 
 

@@ -148,3 +148,26 @@ def test_golden_quantized_inputs_are_oracle_casts(golden, tag):
     dyt = c["dyt"]
     nhwc = golden[f"{tag}_dyq"].reshape(b * h * w, cout)
     assert np.array_equal(dyt, nhwc.T)  # reference transpose_fp8_2d_kernel semantics
+
+
+def test_attention_oracle_close_to_exact_attention():
+    """The FP8 attention restatement stays within e4m3 noise of exact fp32 attention
+    (forward and backward), and its per-head scales are the reference quantize's."""
+    g = torch.Generator().manual_seed(3)
+    qkv = torch.randn(2, 64, 768, generator=g).to(torch.bfloat16)
+    o, lse, sc = oracle.attention_fwd(qkv, 4)
+    ex = oracle.attention_exact(qkv, 4)
+    assert ((o.float() - ex).norm() / ex.norm()).item() < 0.1
+    heads = qkv.float().view(2, 64, 3, 4, 64)
+    for b in range(2):
+        for h in range(4):
+            for t in range(3):
+                _, s_ref = oracle.quantize_tensor(heads[b, :, t, h, :].to(torch.bfloat16).contiguous())
+                assert sc[b, h, t].item() == s_ref.item()
+    do = (torch.randn(2, 64, 256, generator=g) * 0.01).to(torch.bfloat16)
+    dqkv = oracle.attention_bwd(qkv, o, do, lse, 4)
+    x = qkv.float().requires_grad_(True)
+    xs = x.view(2, 64, 3, 4, 64).permute(2, 0, 3, 1, 4)
+    oe = torch.nn.functional.scaled_dot_product_attention(xs[0], xs[1], xs[2]).transpose(1, 2).reshape(2, 64, 256)
+    oe.backward(do.float())
+    assert ((dqkv.float() - x.grad).norm() / x.grad.norm()).item() < 0.1
