@@ -230,6 +230,10 @@ int g_pdl = 0;
 // 0 = the reference's (its scale, 1.0), 1 = 0.0 (fp8_set_empty_tensor_history).
 int g_empty_zero = 0;
 
+// Current-scaling quantize: 1 = the one-launch shared-memory-resident kernel where it
+// applies (default), 0 = always the two passes (fp8_set_quantize_resident).
+int g_quant_resident = 1;
+
 enum KernelClass { kStreamingKernel = 0, kTensorKernel = 1 };
 
 // Launch `kern` on `stream`, with programmatic stream serialization when enabled
@@ -762,9 +766,62 @@ int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const floa
 }
 
 // Current scaling: amax pass (parts CTAs, one partial each), then the cast pass.
+// The shared-memory-resident current quantize (quant_resident_kernel) for the
+// tensors of `m`, if it applies: every n a multiple of 8 (x 16-byte, q 8-byte
+// aligned: the caller's vec path), at least 4 MB in all (below that the two
+// passes are launch-bound either way), each CTA's slices within its shared
+// memory, and count * sm_count partial slots.  *launched = false otherwise.
+int launch_quant_resident(const MultiQuant& m, float* partials, size_t partial_slots, DeviceState* st,
+                          cudaStream_t cs, bool* launched) {
+  *launched = false;
+  const int G = st->sm_count;
+  int64_t bytes = 0, smem = 0;
+  for (int t = 0; t < m.count; ++t) {
+    if (m.n[t] % 8 != 0) return FP8_OK;
+    bytes += m.n[t] * 2;
+    smem += ((m.n[t] / 8 + G - 1) / G) * 16;
+  }
+  if (bytes < (4 << 20) || smem > kResSmemCap || partial_slots < static_cast<size_t>(m.count) * G) return FP8_OK;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(quant_resident_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kResSmemCap);
+  });
+  FP8_CUDA_TRY(attr);
+  unsigned int* arrive = fold_counter(st);
+  unsigned int* depart = fold_counter(st);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(G));
+  cfg.blockDim = dim3(kResThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = cs;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: they meet at a grid barrier
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_resident_kernel, m, partials, arrive, depart, st->err_ptr));
+  count_launches(1);
+  *launched = true;
+  return FP8_OK;
+}
+
 int launch_quantize_current(const uint16_t* x, uint8_t* q, float* scale_out, float* partials, int parts, int64_t n,
                             bool vec, const DeviceState* st, cudaStream_t cs) {
   const int cast_blocks = quant_grid(n, vec, g_quant_cast_bps, st->sm_count);
+  if (vec && g_quant_resident) {
+    MultiQuant m{};
+    m.count = 1;
+    m.x[0] = x;
+    m.q[0] = q;
+    m.scale_out[0] = scale_out;
+    m.n[0] = n;
+    bool launched = false;
+    if (int s = launch_quant_resident(m, partials, static_cast<size_t>(parts), const_cast<DeviceState*>(st), cs,
+                                      &launched))
+      return s;
+    if (launched) return FP8_OK;
+  }
   if (vec) {
     if (int s = launch_stream<kStreamAmax>(parts, x, nullptr, n, nullptr, 0, DelayedSource{}, nullptr, partials,
                                            st->err_ptr, cs))
@@ -1343,6 +1400,12 @@ int fp8_set_pdl(int mode) {
   return ok();
 }
 
+int fp8_set_quantize_resident(int enable) {
+  FP8_REQUIRE(enable == 0 || enable == 1, FP8_ERR_INVALID_ARGUMENT, "enable must be 0 or 1");
+  g_quant_resident = enable;
+  return ok();
+}
+
 int fp8_set_empty_tensor_history(int mode) {
   FP8_REQUIRE(mode == 0 || mode == 1, FP8_ERR_INVALID_ARGUMENT, "empty-tensor history mode must be 0 or 1");
   g_empty_zero = mode;
@@ -1625,6 +1688,11 @@ int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const
               static_cast<size_t>(count) * parts * sizeof(float));
   float* partials = static_cast<float*>(workspace);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (g_quant_resident) {
+    bool launched = false;
+    if (int s = launch_quant_resident(m, partials, workspace_bytes / sizeof(float), st, cs, &launched)) return s;
+    if (launched) return ok();
+  }
   FP8_CUDA_TRY(cudaFuncSetAttribute(quant_multi_amax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kStreamSmemBytes)));
   FP8_CUDA_TRY(cudaFuncSetAttribute(quant_multi_cast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -904,4 +904,145 @@ __global__ void __launch_bounds__(kQuantThreads) weight_finalize_kernel(WeightBa
   if (threadIdx.x == 0) b.window[t][*b.pos[t]] = history_entry(m, b.empty_zero);
 }
 
+
+// ---------------------------------------------------------------- shared-memory-resident current scaling
+// Current scaling of up to kMaxMultiTensors tensors in ONE launch when every
+// CTA's share of them fits in its shared memory (config 2's 33.5 MB activation
+// is 227 KB per SM on 148 SMs): one CTA per SM (cooperative launch, so all are
+// resident), each CTA bulk-loads its contiguous slice of every tensor into
+// shared memory in 16 KB pieces (all in flight at once), takes the slice's |x|
+// max per tensor as the pieces land, stores its partial maxima, meets the other
+// CTAs at a grid barrier, folds the partials into each tensor's scale and casts
+// its slice from shared memory.  x is read from HBM once and q written once,
+// instead of a read, a second read and a write by two launches.  Bytes and
+// scales are those of the two-pass kernels.
+constexpr int kResThreads = 512;
+constexpr int kResPiece = 16384;       // bytes per bulk copy / mbarrier
+constexpr int kResMaxPieces = 16;      // 256 KB > any CTA's shared memory
+constexpr int kResSmemCap = 232448 - 4096;  // dynamic bytes a CTA may use (static arrays and slack aside)
+
+// Vectors (8 elements) of tensor t owned by CTA c of G: [V c / G, V (c + 1) / G).
+__device__ __forceinline__ int64_t res_slice_begin(int64_t vecs, int c, int G) { return vecs * c / G; }
+
+// Bounded grid barrier for a cooperative launch: every CTA arrives once on
+// `arrive`; the CTA whose departure is the last sets both counters back to 0.
+// Returns false (and records kErrTimeoutQuant) if the others do not arrive in time.
+__device__ __forceinline__ bool res_grid_barrier(unsigned int* arrive, unsigned int* depart, int* err) {
+  __shared__ int passed;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(arrive, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    int ok = 1;
+    while (*reinterpret_cast<volatile unsigned int*>(arrive) < gridDim.x) {
+      if (globaltimer_ns() - t0 > FP8_WAIT_TIMEOUT_NS) {
+        record_error(err, kErrTimeoutQuant);
+        ok = 0;
+        break;
+      }
+    }
+    __threadfence();
+    if (ok && atomicAdd(depart, 1u) == gridDim.x - 1) {
+      *arrive = 0u;
+      *depart = 0u;
+    }
+    passed = ok;
+  }
+  __syncthreads();
+  return passed != 0;
+}
+
+__global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQuant m, float* __restrict__ partials,
+                                                                         unsigned int* arrive, unsigned int* depart,
+                                                                         int* err) {
+  extern __shared__ __align__(128) uint8_t res_smem[];
+  __shared__ __align__(8) uint64_t bars[kResMaxPieces];
+  __shared__ int abort_flag;
+  pdl_wait();
+  const int G = gridDim.x, c = blockIdx.x;
+  int64_t vbeg[kMaxMultiTensors], vcnt[kMaxMultiTensors], soff[kMaxMultiTensors];
+  int64_t total = 0;
+#pragma unroll
+  for (int t = 0; t < kMaxMultiTensors; ++t) {
+    const int64_t vecs = t < m.count ? (m.n[t] >> 3) : 0;
+    vbeg[t] = res_slice_begin(vecs, c, G);
+    vcnt[t] = res_slice_begin(vecs, c + 1, G) - vbeg[t];
+    soff[t] = total;
+    total += vcnt[t] * 16;
+  }
+  const int npieces = static_cast<int>((total + kResPiece - 1) / kResPiece);
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < npieces; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // piece i covers smem bytes [i * kResPiece, ...), possibly spanning tensors: one copy per (piece, tensor)
+    for (int i = 0; i < npieces; ++i) {
+      const int64_t p0 = static_cast<int64_t>(i) * kResPiece, p1 = min(total, p0 + kResPiece);
+      mbar_arrive_expect_tx(&bars[i], static_cast<uint32_t>(p1 - p0));
+#pragma unroll
+      for (int t = 0; t < kMaxMultiTensors; ++t) {
+        const int64_t a = max(p0, soff[t]), b = min(p1, soff[t] + vcnt[t] * 16);
+        if (t < m.count && a < b)
+          bulk_load_1d(res_smem + a, reinterpret_cast<const uint8_t*>(m.x[t] + vbeg[t] * 8) + (a - soff[t]),
+                       static_cast<uint32_t>(b - a), &bars[i]);
+      }
+    }
+  }
+  // |x| max per tensor, piece by piece as the copies land
+  uint32_t m2[kMaxMultiTensors] = {0u, 0u, 0u, 0u};
+  bool ok = true;
+  for (int i = 0; i < npieces; ++i) {
+    ok = __all_sync(0xffffffffu, mbar_wait(&bars[i], 0, &abort_flag, err, kErrTimeoutQuant));
+    if (!ok) break;
+    const int64_t p0 = static_cast<int64_t>(i) * kResPiece, p1 = min(total, p0 + kResPiece);
+    for (int64_t o = p0 + threadIdx.x * 16; o < p1; o += kResThreads * 16) {
+      const uint4 a = ld_shared_v4(res_smem + o);
+      int t = 0;
+#pragma unroll
+      for (int u = 1; u < kMaxMultiTensors; ++u)
+        if (u < m.count && o >= soff[u]) t = u;
+#pragma unroll
+      for (int u = 0; u < kMaxMultiTensors; ++u)
+        if (u == t) m2[u] = bf16x2_max(m2[u], absmax_vec2(a));
+    }
+  }
+  if (!__syncthreads_and(ok)) {
+    // let the copies still in flight land before the CTA exits (the other CTAs give up at the barrier)
+    volatile int never = 0;
+    if (threadIdx.x == 0)
+      for (int i = 0; i < npieces; ++i) mbar_wait(&bars[i], 0, &never, err, kErrTimeoutDrain);
+    __syncthreads();
+    return;
+  }
+#pragma unroll
+  for (int t = 0; t < kMaxMultiTensors; ++t) {
+    if (t < m.count) {
+      const float bm = block_max<kResThreads>(unpack_max2(m2[t]));
+      if (threadIdx.x == 0) partials[t * G + c] = bm;
+    }
+  }
+  if (!res_grid_barrier(arrive, depart, err)) return;
+#pragma unroll
+  for (int t = 0; t < kMaxMultiTensors; ++t) {
+    if (t >= m.count) continue;
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < G; i += kResThreads) mx = fmaxf(mx, __ldcg(partials + t * G + i));
+    const float s = scale_from_amax(block_max<kResThreads>(mx));
+    if (c == 0 && threadIdx.x == 0) *m.scale_out[t] = s;
+    uint2* qv = reinterpret_cast<uint2*>(m.q[t] + vbeg[t] * 8);
+    const uint8_t* src = res_smem + soff[t];
+    auto cast_all = [&](const auto& div) {
+      for (int64_t v = threadIdx.x; v < vcnt[t]; v += kResThreads) qv[v] = cast_vec(ld_shared_v4(src + v * 16), div);
+    };
+    if (markstein_applies(s))  // uniform over the grid
+      cast_all(make_markstein(s));
+    else
+      cast_all(DivF64(s));
+  }
+}
+
 }  // namespace fp8b

@@ -170,6 +170,7 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_set_conv_algo": (c_int, [c_int]),
     "fp8_set_pdl": (c_int, [c_int]),
     "fp8_set_empty_tensor_history": (c_int, [c_int]),
+    "fp8_set_quantize_resident": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()
@@ -249,6 +250,12 @@ def set_empty_tensor_history(mode: int = 0) -> None:
     """0: an all-zero tensor records its scale 1.0 in the delayed-scaling histories (the
     reference); 1: it records 0.0 (adds nothing to the history max)."""
     check(load().fp8_set_empty_tensor_history(int(mode)), "fp8_set_empty_tensor_history")
+
+
+def set_quantize_resident(enable: bool = True) -> None:
+    """Current-scaling quantize as one shared-memory-resident launch where it applies (default)
+    or always as two passes."""
+    check(load().fp8_set_quantize_resident(int(enable)), "fp8_set_quantize_resident")
 
 
 def set_conv_algo(algo: int = 0) -> None:

@@ -257,6 +257,14 @@ int fp8_set_pdl(int mode);
  * keeps the mode it was captured with).  No counterpart in the reference. */
 int fp8_set_empty_tensor_history(int mode);
 
+/* Current-scaling quantize (fp8_quantize_current, _multi, _noalloc) of aligned
+ * tensors with sizes that are multiples of 8: enable = 1 (default) runs it as one
+ * cooperative launch that keeps each SM's share of the tensors in shared memory
+ * between the amax and the cast (x read from memory once), where the shares fit
+ * and the tensors hold at least 4 MB; enable = 0 always uses the two passes.
+ * Same bytes and scales either way.  Process-wide; for benchmarks and tests. */
+int fp8_set_quantize_resident(int enable);
+
 /* Tuning override for the quantize grids: CTAs per SM of the amax pass and of
  * the cast pass (1..8; 0 restores the built-in choice).  Process-wide. */
 int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);

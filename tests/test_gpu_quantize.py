@@ -276,3 +276,50 @@ def test_quantize_delayed_window_replayed_in_cuda_graph(cuda):
         scales.append(s_ref)
         assert pos.item() == 2 + r
         assert win[1 + r].item() == float(s_ref)
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 32, 32), (64, 256, 16, 16), (1, 4, 1024, 1024)])
+def test_resident_quantize_matches_two_pass_and_oracle(cuda, shape):
+    """The one-launch shared-memory-resident current quantize (tensors of >= 4 MB whose
+    per-SM shares fit in shared memory) gives the two-pass kernels' and the oracle's bytes
+    and scales, alone and paired with a weight, eagerly and replayed from a CUDA graph."""
+    from fp8_b200 import _lib, ops
+
+    g = torch.Generator().manual_seed(sum(shape))
+    x = (torch.randn(*shape, generator=g) * 3.0).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    w = (torch.randn(128, 128, 3, 3, generator=g) * 0.05).to(torch.bfloat16).contiguous(
+        memory_format=torch.channels_last)
+    xd, wd = x.to(cuda), w.to(cuda)
+    qr, sr = oracle.quantize_tensor(x)
+    qwr, swr = oracle.quantize_tensor(w)
+    try:
+        results = {}
+        for resident in (True, False):
+            _lib.set_quantize_resident(resident)
+            q, s = ops.quantize_current(xd)
+            xq, sx, wq, sw = ops.quantize_current_pair(xd, wd)
+            results[resident] = (q, s, xq, sx, wq, sw)
+        _lib.set_quantize_resident(True)
+        # captured and replayed
+        static = xd.clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            ops.quantize_current(static)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            gq, gs = ops.quantize_current(static)
+        static.copy_(xd * 2)
+        graph.replay()
+        torch.cuda.synchronize()
+        q2r, s2r = oracle.quantize_tensor((x.float() * 2).to(torch.bfloat16).contiguous(
+            memory_format=torch.channels_last))
+    finally:
+        _lib.set_quantize_resident(True)
+    for q, s, xq, sx, wq, sw in results.values():
+        assert torch.equal(q.cpu().view(torch.uint8), qr.view(torch.uint8)) and s.item() == sr.item()
+        assert torch.equal(xq.cpu().view(torch.uint8), qr.view(torch.uint8)) and sx.item() == sr.item()
+        assert torch.equal(wq.cpu().view(torch.uint8), qwr.view(torch.uint8)) and sw.item() == swr.item()
+    assert torch.equal(gq.cpu().view(torch.uint8), q2r.view(torch.uint8)) and gs.item() == s2r.item()
+    assert _lib.device_error() == 0
