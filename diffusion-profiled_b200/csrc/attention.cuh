@@ -9,8 +9,9 @@
 // Forward (attn_fwd_fp8_kernel):
 //   * q, k, v of the pair are read from the qkv projection output [B][L][3C]
 //     (head h at columns h*64, C + h*64, 2C + h*64) and quantized per pair with
-//     the reference's per-tensor rule: s = amax/448 (1 if amax == 0),
-//     e4m3(x / s) saturating (fp8_kernels.py:90-120 applied to each head slice);
+//     the reference's per-tensor scale s = amax/448 (1 if amax == 0,
+//     fp8_kernels.py:90-102 applied to each head slice) and the cast
+//     e4m3(x * (1/s)) saturating (one multiply by the fp32 reciprocal);
 //   * S = Qq Kq^T on tcgen05 kind::f8f6f4 (M = 128 queries per tile, N = keys,
 //     K = 64), fp32 in TMEM;
 //   * softmax in fp32 from TMEM, one thread per query row: m = max_j S,
@@ -86,12 +87,18 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
 // Per-tensor scale of the reference quantize: amax/448 in IEEE fp32, 1 for amax 0.
 __device__ __forceinline__ float attn_scale(float amax) { return amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f; }
 
-// e4m3(clamp(x / s)) of the 8 bf16 of a 16-byte chunk -> 8 bytes, x / s exactly the IEEE
-// fp32 quotient (the quantize kernels' divide-free exact cast; Markstein for the usual
-// scales, an fp64 reciprocal otherwise -- uniform per CTA, no divergence).
-__device__ __forceinline__ uint2 quant8_bf16(const uint4& v, float s) {
-  return markstein_applies(s) ? cast_vec(v, make_markstein(s)) : cast_vec(v, DivF64(s));
+// The attention's cast of q, k, v: e4m3(RN(x * r)) with r = RN(1 / s) in fp32 (saturating at
+// +-448), one multiply per element -- the attention has no reference kernel whose division
+// bits it must match, and this cast is what the oracle restates.
+__device__ __forceinline__ uint2 quant8_bf16(const uint4& v, float r) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t b[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) b[i] = cvt_e4m3x2(bf16_lo_f(w[i]) * r, bf16_hi_f(w[i]) * r);
+  return make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
 }
+
+__device__ __forceinline__ float attn_recip(float s) { return __fdiv_rn(1.0f, s); }
 
 // 2^x (the SFU's approximation; relative error ~2^-22).
 __device__ __forceinline__ float exp2_approx(float x) {
@@ -100,23 +107,20 @@ __device__ __forceinline__ float exp2_approx(float x) {
   return y;
 }
 
-// e4m3 byte -> its value as fp32 (exact).
-__device__ __forceinline__ float e4m3_to_f32(uint32_t byte) {
-  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(byte & 0xFFu), __NV_E4M3);
-  return __half2float(__half(h));
+// Two e4m3 bytes (low byte first) -> the same two values as bf16x2 (exact: e4m3 values are
+// f16 and bf16 values).
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t two) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(two & 0xFFFFu)));
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+  return pack_bf16x2(f.x, f.y);
 }
 
-// The 8 bf16 of a chunk -> the bf16 of their e4m3 values e4m3(x / s) (exact in bf16).
-__device__ __forceinline__ uint4 quant_dequant8_bf16(const uint4& v, float s) {
-  const uint2 q = quant8_bf16(v, s);
-  const uint32_t bytes[2] = {q.x, q.y};
-  uint32_t out[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t word = bytes[i >> 1] >> ((i & 1) * 16);
-    out[i] = pack_bf16x2(e4m3_to_f32(word & 0xFFu), e4m3_to_f32((word >> 8) & 0xFFu));
-  }
-  return make_uint4(out[0], out[1], out[2], out[3]);
+// The 8 bf16 of a chunk -> the bf16 of their e4m3 values quant8_bf16(x, r) (exact in bf16).
+__device__ __forceinline__ uint4 quant_dequant8_bf16(const uint4& v, float r) {
+  const uint2 q = quant8_bf16(v, r);
+  return make_uint4(e4m3x2_to_bf16x2(q.x), e4m3x2_to_bf16x2(q.x >> 16), e4m3x2_to_bf16x2(q.y),
+                    e4m3x2_to_bf16x2(q.y >> 16));
 }
 
 __device__ __forceinline__ float bf16x8_absmax(const uint4& v) {
@@ -154,44 +158,59 @@ __device__ __forceinline__ uint32_t sw128_row_chunk(int row, int chunk) {
 }
 
 // ============================================================================ forward
+// One CTA per (image, head, 128-query tile): 96 KB of shared memory, 256 TMEM
+// columns and at most 128 registers per thread, so two CTAs share an SM and one
+// CTA's loads overlap the other's softmax.  Each CTA reads its pair's whole q
+// (for the per-pair scale), k and v.
 struct AttnFwdLayout {
-  static constexpr int kQ = 0;                  // 2 x 16 KB: q rows, 64 of 128 bytes used
-  static constexpr int kK = 32768;              // 2 x 16 KB: k rows
-  static constexpr int kVt = 65536;             // 2 x 8 KB: v^T, [d][keys], keys in 128-byte K blocks
-  static constexpr int kP = 81920;              // per query tile 2 x 16 KB: p, [query][keys]
-  static constexpr int kRed = kP + 2 * 32768;   // amax reduction scratch
-  static constexpr int kBar = kRed + 128;
-  static constexpr int kBytes = kBar + 128;
+  static constexpr int kQ = 0;          // 16 KB: this tile's q rows, 64 of 128 bytes used
+  static constexpr int kK = 16384;      // 2 x 16 KB: k rows (keys)
+  static constexpr int kVt = 49152;     // 2 x 8 KB: v^T, [d][keys], keys in 128-byte K blocks
+  static constexpr int kP = 65536;      // 2 x 16 KB: p, [query][keys]
+  static constexpr int kRed = 98304;    // row max / sum exchange [2][128] floats, amax scratch
+  static constexpr int kBar = kRed + 1024 + 128;
+  static constexpr int kBytes = kBar + 64;
   static constexpr int kSmemBytes = kBytes + 1024;  // + alignment slack
 };
-static_assert(AttnFwdLayout::kSmemBytes <= 232448, "attention forward smem");
+static_assert(2 * AttnFwdLayout::kSmemBytes <= 232448, "two attention-forward CTAs per SM");
+constexpr uint32_t kAttnFwdTmemCols = 256;
 
-__global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_fp8_kernel(const AttnParams p) {
+// |x| max of one tensor's head slice (rows < L, 16-byte chunks c = tid + 256 r).
+__device__ __forceinline__ float head_absmax(const uint16_t* col0, int L, int ld) {
+  uint32_t m2 = 0u;
+#pragma unroll 4
+  for (int c = threadIdx.x; c < L * 8; c += kAttnThreads)
+    m2 = bf16x2_max(m2, absmax_vec2(__ldg(reinterpret_cast<const uint4*>(col0 + static_cast<int64_t>(c >> 3) * ld +
+                                                                          (c & 7) * 8))));
+  return unpack_max2(m2);
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_fwd_fp8_kernel(const AttnParams p) {
   using Ly = AttnFwdLayout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + Ly::kRed);
+  float* red = reinterpret_cast<float*>(smem + Ly::kRed);  // [2][128] row partials, then amax scratch at +1024
   uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + Ly::kBar);
-  uint64_t* bar_o = bar_s + 1;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_o + 2);
+  uint64_t* bar_o = bar_s + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_o + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = p.seq;
   const int nkp = (L + 31) & ~31;  // keys, padded to the e4m3 K step
   const int nqt = (L + 127) >> 7;  // query tiles
-  const int b = blockIdx.x / p.heads, h = blockIdx.x - (blockIdx.x / p.heads) * p.heads;
+  const int pair = blockIdx.x / nqt, tile = blockIdx.x - pair * nqt;
+  const int b = pair / p.heads, h = pair - b * p.heads;
   const int C = p.heads * kAttnHeadDim;
 
   if (tid == 0) {
     mbar_init(bar_s, 1);
-    mbar_init(&bar_o[0], 1);
-    mbar_init(&bar_o[1], 1);
+    mbar_init(bar_o, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, kAttnTmemCols);
+    tmem_alloc(tmem_slot, kAttnFwdTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -200,172 +219,172 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_fp8_kernel(const Att
   const uint32_t tmem = *tmem_slot;
   pdl_wait();
 
-  // ---- load q, k, v of the pair (16-byte chunks: row = chunk / 8) and their maxima
+  // ---- per-pair scales from the whole head slices of q, k, v
   const uint16_t* src = p.qkv + static_cast<int64_t>(b) * L * p.ld_qkv + h * kAttnHeadDim;
-  // q, k: chunk c = tid + 256 r is row c / 8, channels 8 (c % 8) ..; v: this thread's 8
-  // consecutive keys vkey0 .. vkey0 + 7 at channels 8 vc16 .., for the transposed store
-  const int vkey0 = (tid >> 3) * 8, vc16 = tid & 7;
-  uint4 qv[8], kv[8], vv[8];
-  float amax[3] = {0.0f, 0.0f, 0.0f};
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int c = tid + kAttnThreads * r, row = c >> 3, col = (c & 7) * 8;
-    qv[r] = kv[r] = vv[r] = make_uint4(0, 0, 0, 0);
-    if (row < L) {
-      const uint16_t* s = src + static_cast<int64_t>(row) * p.ld_qkv + col;
-      qv[r] = __ldg(reinterpret_cast<const uint4*>(s));
-      kv[r] = __ldg(reinterpret_cast<const uint4*>(s + C));
-      amax[0] = fmaxf(amax[0], bf16x8_absmax(qv[r]));
-      amax[1] = fmaxf(amax[1], bf16x8_absmax(kv[r]));
-    }
-    if (vkey0 + r < L) {
-      vv[r] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(vkey0 + r) * p.ld_qkv + 2 * C +
-                                                   vc16 * 8));
-      amax[2] = fmaxf(amax[2], bf16x8_absmax(vv[r]));
-    }
-  }
-  block_max3(amax, red);
+  float amax[3] = {head_absmax(src, L, p.ld_qkv), head_absmax(src + C, L, p.ld_qkv),
+                   head_absmax(src + 2 * C, L, p.ld_qkv)};
+  block_max3(amax, red + 256);
   const float sq = attn_scale(amax[0]), sk = attn_scale(amax[1]), sv = attn_scale(amax[2]);
+  const float rq = attn_recip(sq), rk = attn_recip(sk), rv = attn_recip(sv);
 
-  // ---- quantize into the operand tiles (rows past L are zero)
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int c = tid + kAttnThreads * r, row = c >> 3, c16 = c & 7;
-    const uint32_t off = sw128_row_chunk(row, c16 >> 1) + (c16 & 1) * 8;
-    if (row < nqt * 128) {
-      const uint2 qb = row < L ? quant8_bf16(qv[r], sq) : make_uint2(0, 0);
-      *reinterpret_cast<uint2*>(smem + Ly::kQ + off) = qb;
-    }
-    if (row < nkp) {
-      const uint2 kb = row < L ? quant8_bf16(kv[r], sk) : make_uint2(0, 0);
-      *reinterpret_cast<uint2*>(smem + Ly::kK + off) = kb;
-    }
+  // ---- quantize into the operand tiles (second read of the slices: L1 / L2 hits)
+  for (int c = tid; c < 128 * 8; c += kAttnThreads) {  // this tile's q rows
+    const int r = c >> 3, c16 = c & 7, row = tile * 128 + r;
+    const uint2 qb = row < L ? quant8_bf16(__ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(row) *
+                                                                                 p.ld_qkv + c16 * 8)), rq)
+                             : make_uint2(0, 0);
+    *reinterpret_cast<uint2*>(smem + Ly::kQ + swizzle128_offset(r, c16 >> 1) + (c16 & 1) * 8) = qb;
   }
-  if (vkey0 < nkp) {
-    // v^T: byte e of key vkey0 + r goes to row d = 8 vc16 + e of the key's K block; the 8
-    // keys of this thread are 8 consecutive bytes of that row (keys past L are zero)
-    uint2 vb[8];
+  for (int c = tid; c < nkp * 8; c += kAttnThreads) {  // k rows
+    const int row = c >> 3, c16 = c & 7;
+    const uint2 kb = row < L ? quant8_bf16(__ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(row) *
+                                                                                 p.ld_qkv + C + c16 * 8)), rk)
+                             : make_uint2(0, 0);
+    *reinterpret_cast<uint2*>(smem + Ly::kK + sw128_row_chunk(row, c16 >> 1) + (c16 & 1) * 8) = kb;
+  }
+  {
+    // v^T: this thread's 8 consecutive keys vkey0 .. + 7 at channels 8 vc16 .. 8 vc16 + 7; byte e of
+    // key vkey0 + r goes to row d = 8 vc16 + e, so each row gets 8 consecutive bytes (keys past L: 0)
+    const int vkey0 = (tid >> 3) * 8, vc16 = tid & 7;
+    if (vkey0 < nkp) {
+      uint2 vb[8];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) vb[r] = vkey0 + r < L ? quant8_bf16(vv[r], sv) : make_uint2(0, 0);
-    const int kb_blk = vkey0 >> 7, kr = vkey0 & 127;
+      for (int r = 0; r < 8; ++r)
+        vb[r] = vkey0 + r < L ? quant8_bf16(__ldg(reinterpret_cast<const uint4*>(
+                                                src + static_cast<int64_t>(vkey0 + r) * p.ld_qkv + 2 * C + vc16 * 8)),
+                                            rv)
+                              : make_uint2(0, 0);
+      const int kb_blk = vkey0 >> 7, kr = vkey0 & 127;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      uint32_t lo = 0, hi = 0;
+      for (int e = 0; e < 8; ++e) {
+        uint32_t lo = 0, hi = 0;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        lo |= ((((e < 4 ? vb[r].x : vb[r].y) >> ((e & 3) * 8)) & 0xFFu) << (8 * r));
-        hi |= ((((e < 4 ? vb[r + 4].x : vb[r + 4].y) >> ((e & 3) * 8)) & 0xFFu) << (8 * r));
+        for (int r = 0; r < 4; ++r) {
+          lo |= ((((e < 4 ? vb[r].x : vb[r].y) >> ((e & 3) * 8)) & 0xFFu) << (8 * r));
+          hi |= ((((e < 4 ? vb[r + 4].x : vb[r + 4].y) >> ((e & 3) * 8)) & 0xFFu) << (8 * r));
+        }
+        const int d = vc16 * 8 + e;
+        const uint32_t o = kb_blk * 8192 + d * 128 + ((((kr >> 4) ^ (d & 7)) & 7) << 4) + (kr & 15);
+        *reinterpret_cast<uint2*>(smem + Ly::kVt + o) = make_uint2(lo, hi);
       }
-      const int d = vc16 * 8 + e;
-      const uint32_t o = kb_blk * 8192 + d * 128 + ((((kr >> 4) ^ (d & 7)) & 7) << 4) + (kr & 15);
-      *reinterpret_cast<uint2*>(smem + Ly::kVt + o) = make_uint2(lo, hi);
     }
   }
   fence_proxy_async_smem();
   __syncthreads();
 
-  // ---- S = Qq Kq^T for every query tile (TMEM columns [256 i, 256 i + nkp))
+  // ---- S = Qq Kq^T (TMEM columns [0, nkp))
   if (tid == 0) {
     tc_fence_after();
     const uint32_t idesc = make_idesc_e4m3(128, nkp, 0, 0);
     const uint32_t sa = smem_u32(smem + Ly::kQ), sb = smem_u32(smem + Ly::kK);
-    for (int i = 0; i < nqt; ++i)
 #pragma unroll
-      for (int k = 0; k < 2; ++k)
-        umma_f8(tmem + i * 256, make_smem_desc(sa + i * 16384 + k * 32, 16, 1024), make_smem_desc(sb + k * 32, 16, 1024),
-                idesc, k > 0 ? 1u : 0u);
+    for (int k = 0; k < 2; ++k)
+      umma_f8(tmem, make_smem_desc(sa + k * 32, 16, 1024), make_smem_desc(sb + k * 32, 16, 1024), idesc,
+              k > 0 ? 1u : 0u);
     umma_commit(bar_s);
   }
 
-  // ---- softmax, P, O per query tile: warps 4i .. 4i+3, one query row per thread
-  const int tile = warp >> 2, quad = warp & 3, r = quad * 32 + lane, qi = tile * 128 + r;
-  if (tile < nqt) {
-    const float c2 = sq * sk * 0.125f * 1.4426950408889634f;  // raw S -> log2 units
-    float m = -INFINITY, l = 0.0f;
-    bool ok = __all_sync(0xffffffffu, mbar_wait(bar_s, 0, abort_flag, p.err, kErrTimeoutEpilogue));
-    if (ok) {
-      tc_fence_after();
-      const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16) + tile * 256;
-      for (int cc = 0; cc < nkp; cc += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(trow + cc, v);
-        tmem_ld_wait();
+  // ---- softmax: query row r (lanes of quadrant warp % 4), 32-column chunks of parity half = warp / 4
+  const int quad = warp & 3, half = warp >> 2, r = quad * 32 + lane, qi = tile * 128 + r;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+  const float c2 = sq * sk * 0.125f * 1.4426950408889634f;  // raw S -> log2 units
+  const int nchunks = nkp >> 5;
+  bool ok = __all_sync(0xffffffffu, mbar_wait(bar_s, 0, abort_flag, p.err, kErrTimeoutEpilogue));
+  float m = -INFINITY, l = 0.0f;
+  if (ok) {
+    tc_fence_after();
+    for (int ch = half; ch < nchunks; ch += 2) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(trow + ch * 32, v);
+      tmem_ld_wait();
+      const int valid = min(32, L - ch * 32);  // keys of this chunk below L
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (cc + j < L) m = fmaxf(m, __uint_as_float(v[j]));
-      }
-      uint8_t* prow = smem + Ly::kP + tile * 32768;
-      for (int cc = 0; cc < nkp; cc += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(trow + cc, v);
-        tmem_ld_wait();
-        uint32_t packed[8];
+      for (int j = 0; j < 32; ++j)
+        if (j < valid) m = fmaxf(m, __uint_as_float(v[j]));
+    }
+  }
+  red[half * 128 + r] = m;
+  __syncthreads();
+  m = fmaxf(red[r], red[128 + r]);
+  // P scaled by 448 into e4m3: 448 p = 2^((S - m) c2 + log2 448); S - m first (exact near the
+  // max), so that large logits keep the offset
+  if (ok) {
+    for (int ch = half; ch < nchunks; ch += 2) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(trow + ch * 32, v);
+      tmem_ld_wait();
+      const int valid = qi < L ? min(32, L - ch * 32) : 0;
+      uint32_t packed[8];
+      if (valid == 32) {  // whole chunk inside the sequence: no masks
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           float pj[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const bool valid = qi < L && cc + j + e < L;
-            pj[e] = valid ? exp2_approx((__uint_as_float(v[j + e]) - m) * c2) : 0.0f;
+            pj[e] = exp2_approx(fmaf(__uint_as_float(v[j + e]) - m, c2, 8.807354922057604f));
             l += pj[e];
           }
-          packed[j >> 2] = uint32_t(cvt_e4m3x2(pj[0] * 448.0f, pj[1] * 448.0f)) |
-                           (uint32_t(cvt_e4m3x2(pj[2] * 448.0f, pj[3] * 448.0f)) << 16);
+          packed[j >> 2] = uint32_t(cvt_e4m3x2(pj[0], pj[1])) | (uint32_t(cvt_e4m3x2(pj[2], pj[3])) << 16);
         }
-        const int kblk = cc >> 7, kc = (cc & 127) >> 4;  // 16-byte chunks kc, kc + 1 of the row
-        uint8_t* base = prow + kblk * 16384;
-        *reinterpret_cast<uint4*>(base + swizzle128_offset(r, kc)) =
-            make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        *reinterpret_cast<uint4*>(base + swizzle128_offset(r, kc + 1)) =
-            make_uint4(packed[4], packed[5], packed[6], packed[7]);
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    named_barrier_sync(1 + tile, 128);
-    if (*abort_flag) ok = false;
-    if (ok && quad == 0 && lane == 0) {
-      tc_fence_after();
-      const uint32_t idesc = make_idesc_e4m3(128, kAttnHeadDim, 0, 0);
-      const uint32_t sp = smem_u32(smem + Ly::kP + tile * 32768), sv_t = smem_u32(smem + Ly::kVt);
-      for (int ks = 0; ks < nkp / 32; ++ks) {
-        const int kblk = ks >> 2, k = ks & 3;
-        umma_f8(tmem + tile * 256, make_smem_desc(sp + kblk * 16384 + k * 32, 16, 1024),
-                make_smem_desc(sv_t + kblk * 8192 + k * 32, 16, 1024), idesc, ks > 0 ? 1u : 0u);
-      }
-      umma_commit(&bar_o[tile]);
-    }
-    if (ok) ok = mbar_wait(&bar_o[tile], 0, abort_flag, p.err, kErrTimeoutEpilogue);
-    if (__all_sync(0xffffffffu, ok)) {
-      tc_fence_after();
-      const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16) + tile * 256;
-      uint32_t o0[32], o1[32];
-      tmem_ld_32x32b_x32(trow, o0);
-      tmem_ld_32x32b_x32(trow + 32, o1);
-      tmem_ld_wait();
-      if (qi < L) {
-        const float f = __fdiv_rn(sv, 448.0f * l);
-        uint16_t* dst = p.o + (static_cast<int64_t>(b) * L + qi) * p.ld_o + h * kAttnHeadDim;
+      } else {
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8)
-          reinterpret_cast<uint4*>(dst)[c8] =
-              make_uint4(pack_bf16x2(__uint_as_float(o0[8 * c8]) * f, __uint_as_float(o0[8 * c8 + 1]) * f),
-                         pack_bf16x2(__uint_as_float(o0[8 * c8 + 2]) * f, __uint_as_float(o0[8 * c8 + 3]) * f),
-                         pack_bf16x2(__uint_as_float(o0[8 * c8 + 4]) * f, __uint_as_float(o0[8 * c8 + 5]) * f),
-                         pack_bf16x2(__uint_as_float(o0[8 * c8 + 6]) * f, __uint_as_float(o0[8 * c8 + 7]) * f));
+        for (int j = 0; j < 32; j += 4) {
+          float pj[4];
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8)
-          reinterpret_cast<uint4*>(dst)[4 + c8] =
-              make_uint4(pack_bf16x2(__uint_as_float(o1[8 * c8]) * f, __uint_as_float(o1[8 * c8 + 1]) * f),
-                         pack_bf16x2(__uint_as_float(o1[8 * c8 + 2]) * f, __uint_as_float(o1[8 * c8 + 3]) * f),
-                         pack_bf16x2(__uint_as_float(o1[8 * c8 + 4]) * f, __uint_as_float(o1[8 * c8 + 5]) * f),
-                         pack_bf16x2(__uint_as_float(o1[8 * c8 + 6]) * f, __uint_as_float(o1[8 * c8 + 7]) * f));
-        p.lse[(static_cast<int64_t>(b) * p.heads + h) * L + qi] = m * (sq * sk * 0.125f) + logf(l);
+          for (int e = 0; e < 4; ++e) {
+            pj[e] = j + e < valid ? exp2_approx(fmaf(__uint_as_float(v[j + e]) - m, c2, 8.807354922057604f)) : 0.0f;
+            l += pj[e];
+          }
+          packed[j >> 2] = uint32_t(cvt_e4m3x2(pj[0], pj[1])) | (uint32_t(cvt_e4m3x2(pj[2], pj[3])) << 16);
+        }
       }
+      const int kblk = ch >> 2, kc = (ch & 3) * 2;  // 16-byte chunks kc, kc + 1 of the 128-byte row
+      uint8_t* base = smem + Ly::kP + kblk * 16384;
+      *reinterpret_cast<uint4*>(base + swizzle128_offset(r, kc)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      *reinterpret_cast<uint4*>(base + swizzle128_offset(r, kc + 1)) =
+          make_uint4(packed[4], packed[5], packed[6], packed[7]);
     }
   }
-  if (tid == 0) {
-    float* sc = p.scales + (static_cast<int64_t>(b) * p.heads + h) * 4;
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();  // every read of S is done and P is in shared memory
+  red[half * 128 + r] = l;
+  if (*abort_flag) ok = false;
+  if (ok && tid == 0) {
+    tc_fence_after();
+    const uint32_t idesc = make_idesc_e4m3(128, kAttnHeadDim, 0, 0);
+    const uint32_t sp = smem_u32(smem + Ly::kP), svt = smem_u32(smem + Ly::kVt);
+    for (int ks = 0; ks < nchunks; ++ks) {
+      const int kblk = ks >> 2, k = ks & 3;
+      umma_f8(tmem, make_smem_desc(sp + kblk * 16384 + k * 32, 16, 1024),
+              make_smem_desc(svt + kblk * 8192 + k * 32, 16, 1024), idesc, ks > 0 ? 1u : 0u);
+    }
+    umma_commit(bar_o);
+  }
+  __syncthreads();
+  l = red[r] + red[128 + r];  // sum of 448 p over the row
+  if (ok) ok = mbar_wait(bar_o, 0, abort_flag, p.err, kErrTimeoutEpilogue);
+  if (__all_sync(0xffffffffu, ok)) {
+    tc_fence_after();
+    uint32_t o[32];
+    tmem_ld_32x32b_x32(trow + half * 32, o);  // output channels [32 half, 32 half + 32)
+    tmem_ld_wait();
+    if (qi < L) {
+      const float f = __fdiv_rn(sv, l);
+      uint16_t* dst = p.o + (static_cast<int64_t>(b) * L + qi) * p.ld_o + h * kAttnHeadDim + half * 32;
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8)
+        reinterpret_cast<uint4*>(dst)[c8] =
+            make_uint4(pack_bf16x2(__uint_as_float(o[8 * c8]) * f, __uint_as_float(o[8 * c8 + 1]) * f),
+                       pack_bf16x2(__uint_as_float(o[8 * c8 + 2]) * f, __uint_as_float(o[8 * c8 + 3]) * f),
+                       pack_bf16x2(__uint_as_float(o[8 * c8 + 4]) * f, __uint_as_float(o[8 * c8 + 5]) * f),
+                       pack_bf16x2(__uint_as_float(o[8 * c8 + 6]) * f, __uint_as_float(o[8 * c8 + 7]) * f));
+      // lse of the logits S sq sk / 8:  m c + ln(l / 448)
+      if (half == 0) p.lse[static_cast<int64_t>(pair) * L + qi] = m * (sq * sk * 0.125f) + logf(l * (1.0f / 448.0f));
+    }
+  }
+  if (tid == 0 && tile == 0) {
+    float* sc = p.scales + static_cast<int64_t>(pair) * 4;
     sc[0] = sq;
     sc[1] = sk;
     sc[2] = sv;
@@ -375,7 +394,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_fp8_kernel(const Att
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, kAttnTmemCols);
+    tmem_dealloc(tmem, kAttnFwdTmemCols);
   }
 }
 
@@ -453,6 +472,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_bwd_kernel(const AttnPar
   const int64_t pair = static_cast<int64_t>(b) * p.heads + h;
   const float* sc = p.scales + pair * 4;
   const float sq = sc[0], sk = sc[1], sv = sc[2];
+  const float rq = attn_recip(sq), rk = attn_recip(sk), rv = attn_recip(sv);
   const uint16_t* src = p.qkv + static_cast<int64_t>(b) * L * p.ld_qkv + h * kAttnHeadDim;
   const uint16_t* dsrc = p.dout + static_cast<int64_t>(b) * L * p.ld_o + h * kAttnHeadDim;
   const uint16_t* osrc = p.o_in + static_cast<int64_t>(b) * L * p.ld_o + h * kAttnHeadDim;
@@ -464,9 +484,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_bwd_kernel(const AttnPar
     uint4 q = make_uint4(0, 0, 0, 0), k = q, v = q, d = q;
     if (row < L) {
       const uint16_t* s = src + static_cast<int64_t>(row) * p.ld_qkv + c16 * 8;
-      q = quant_dequant8_bf16(__ldg(reinterpret_cast<const uint4*>(s)), sq);
-      k = quant_dequant8_bf16(__ldg(reinterpret_cast<const uint4*>(s + C)), sk);
-      v = quant_dequant8_bf16(__ldg(reinterpret_cast<const uint4*>(s + 2 * C)), sv);
+      q = quant_dequant8_bf16(__ldg(reinterpret_cast<const uint4*>(s)), rq);
+      k = quant_dequant8_bf16(__ldg(reinterpret_cast<const uint4*>(s + C)), rk);
+      v = quant_dequant8_bf16(__ldg(reinterpret_cast<const uint4*>(s + 2 * C)), rv);
       d = __ldg(reinterpret_cast<const uint4*>(dsrc + static_cast<int64_t>(row) * p.ld_o + c16 * 8));
     }
     *reinterpret_cast<uint4*>(smem + Ly::kQ + off) = q;
@@ -496,7 +516,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_bwd_kernel(const AttnPar
   fence_proxy_async_smem();
   __syncthreads();
 
-  const float cs = sq * sk * 0.125f;  // raw S -> logits
+  const float cs2 = sq * sk * 0.125f * 1.4426950408889634f;  // raw S -> logits in log2 units
   const int quad = warp & 3, half = warp >> 2, r = quad * 32 + lane;
   const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
   const uint32_t sQ = smem_u32(smem + Ly::kQ), sK = smem_u32(smem + Ly::kK), sV = smem_u32(smem + Ly::kV),
@@ -525,7 +545,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_bwd_kernel(const AttnPar
       if (ok) {
         tc_fence_after();
         const int qi = i * 128 + r;
-        const float lse = lse_s[qi < kAttnMaxSeq ? qi : 0], delta = delta_s[qi < kAttnMaxSeq ? qi : 0];
+        const float lse2 = lse_s[qi < kAttnMaxSeq ? qi : 0] * 1.4426950408889634f;  // log2 units
+        const float delta = delta_s[qi < kAttnMaxSeq ? qi : 0];
 #pragma unroll 1
         for (int cc = 0; cc < 2; ++cc) {
           const int col0 = half * 64 + cc * 32;  // key column within the tile
@@ -543,8 +564,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_bwd_kernel(const AttnPar
             for (int e = 0; e < 2; ++e) {
               const int key = j * 128 + col0 + jj + e;
               const bool valid = col0 < nk && qi < L && key < L;
-              const float pe = valid ? exp2_approx((__uint_as_float(s[jj + e]) * cs - lse) * 1.4426950408889634f)
-                                     : 0.0f;
+              const float pe = valid ? exp2_approx(fmaf(__uint_as_float(s[jj + e]), cs2, -lse2)) : 0.0f;
               pv[e] = pe;
               dv[e] = valid ? pe * (__uint_as_float(dp[jj + e]) * sv - delta) : 0.0f;
             }

@@ -2415,7 +2415,8 @@ int fp8_attention_fwd(const void* qkv, void* o, float* lse, float* scales, int b
   constexpr int smem = AttnFwdLayout::kSmemBytes;
   FP8_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   count_launches(1);
-  FP8_CUDA_TRY(launch_kernel(attn_fwd_fp8_kernel, dim3(static_cast<unsigned>(batch * heads)), dim3(kAttnThreads), smem,
+  const int nqt = (seq + 127) / 128;
+  FP8_CUDA_TRY(launch_kernel(attn_fwd_fp8_kernel, dim3(static_cast<unsigned>(batch * heads * nqt)), dim3(kAttnThreads), smem,
                              reinterpret_cast<cudaStream_t>(stream), 1, kTensorKernel, p));
   return ok();
 }

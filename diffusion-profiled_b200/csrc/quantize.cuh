@@ -992,22 +992,24 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
       }
     }
   }
-  // |x| max per tensor, piece by piece as the copies land
+  // |x| max per tensor, piece by piece as the copies land (a piece is at most 2 vectors per thread)
   uint32_t m2[kMaxMultiTensors] = {0u, 0u, 0u, 0u};
   bool ok = true;
+  static_assert(kResPiece == 2 * 16 * kResThreads, "two vectors per thread per piece");
   for (int i = 0; i < npieces; ++i) {
     ok = __all_sync(0xffffffffu, mbar_wait(&bars[i], 0, &abort_flag, err, kErrTimeoutQuant));
     if (!ok) break;
-    const int64_t p0 = static_cast<int64_t>(i) * kResPiece, p1 = min(total, p0 + kResPiece);
-    for (int64_t o = p0 + threadIdx.x * 16; o < p1; o += kResThreads * 16) {
-      const uint4 a = ld_shared_v4(res_smem + o);
-      int t = 0;
+    const int64_t o0 = static_cast<int64_t>(i) * kResPiece + threadIdx.x * 16;
+    const int64_t o1 = o0 + kResThreads * 16;
+    const bool h0 = o0 < total, h1 = o1 < total;
+    const uint4 a0 = h0 ? ld_shared_v4(res_smem + o0) : make_uint4(0u, 0u, 0u, 0u);
+    const uint4 a1 = h1 ? ld_shared_v4(res_smem + o1) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t x0 = absmax_vec2(a0), x1 = absmax_vec2(a1);
 #pragma unroll
-      for (int u = 1; u < kMaxMultiTensors; ++u)
-        if (u < m.count && o >= soff[u]) t = u;
-#pragma unroll
-      for (int u = 0; u < kMaxMultiTensors; ++u)
-        if (u == t) m2[u] = bf16x2_max(m2[u], absmax_vec2(a));
+    for (int u = 0; u < kMaxMultiTensors; ++u) {
+      const int64_t lo = soff[u], hi = soff[u] + vcnt[u] * 16;  // empty for u >= count
+      if (o0 >= lo && o0 < hi) m2[u] = bf16x2_max(m2[u], x0);
+      if (o1 >= lo && o1 < hi) m2[u] = bf16x2_max(m2[u], x1);
     }
   }
   if (!__syncthreads_and(ok)) {
@@ -1036,7 +1038,16 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
     uint2* qv = reinterpret_cast<uint2*>(m.q[t] + vbeg[t] * 8);
     const uint8_t* src = res_smem + soff[t];
     auto cast_all = [&](const auto& div) {
-      for (int64_t v = threadIdx.x; v < vcnt[t]; v += kResThreads) qv[v] = cast_vec(ld_shared_v4(src + v * 16), div);
+      const int64_t nv = vcnt[t];
+      int64_t v = threadIdx.x;
+      for (; v + 3 * kResThreads < nv; v += 4 * kResThreads) {  // four independent vectors in flight
+        uint4 a[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a[j] = ld_shared_v4(src + (v + j * kResThreads) * 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) qv[v + j * kResThreads] = cast_vec(a[j], div);
+      }
+      for (; v < nv; v += kResThreads) qv[v] = cast_vec(ld_shared_v4(src + v * 16), div);
     };
     if (markstein_applies(s))  // uniform over the grid
       cast_all(make_markstein(s));

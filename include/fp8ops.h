@@ -491,7 +491,8 @@ int fp8_cast_batch(int count, const void* const* src, void* const* dst, const in
  *   scales: fp32 [batch][heads][4], the e4m3 scales of q, k, v (amax/448 of each
  *         head's slice) and 0.
  * q, k and v are quantized per (image, head) with the reference's per-tensor
- * rule (fp8_kernels.py:90-120), S = q k^T / sqrt(64) and O = P v run on the FP8
+ * scale s = amax/448 (fp8_kernels.py:90-102) as e4m3(x * (1/s)) (one multiply by
+ * the fp32 reciprocal), S = q k^T / sqrt(64) and O = P v run on the FP8
  * tensor cores with P quantized as e4m3(p * 448); softmax in fp32.
  * head_dim must be 64; seq a multiple of 16 in [16, 256]; qkv, o 16-byte
  * aligned, ld_qkv and ld_o multiples of 8. */

@@ -216,9 +216,10 @@ def linear_dw(dyq, xq, sdy, sx) -> torch.Tensor:
 
 # ----------------------------------------------------------------------------- attention
 def _e4m3_values(x: np.ndarray, scale: np.ndarray) -> np.ndarray:
-    """e4m3 grid values of x / scale (fp32 IEEE divide, reference clamp, RNE cast)."""
-    with np.errstate(divide="ignore", invalid="ignore"):
-        t = x.astype(np.float32) / scale.astype(np.float32)
+    """The attention kernels' cast: e4m3 grid values of RN(x * r), r = RN(1 / scale) in fp32,
+    saturating at +-448, round to nearest even."""
+    r = (np.float32(1.0) / scale.astype(np.float32)).astype(np.float32)
+    t = (x.astype(np.float32) * r).astype(np.float32)
     t = np.fmax(np.float32(-E4M3_MAX), np.fmin(t, np.float32(E4M3_MAX)))
     return e4m3_decode(e4m3_encode(t))
 
@@ -230,8 +231,9 @@ def _split_heads(qkv: torch.Tensor, heads: int) -> np.ndarray:
 
 
 def attention_quantized(qkv: torch.Tensor, heads: int):
-    """Per (image, head): the e4m3 values of q, k, v and their scales amax/448 (1 if amax is 0),
-    the reference's per-tensor quantize rule (fp8_kernels.py:90-120) on each head slice."""
+    """Per (image, head): the e4m3 values of q, k, v and their scales amax/448 (1 if amax is 0;
+    the reference's per-tensor scale, fp8_kernels.py:90-102, of each head slice), cast as
+    e4m3(x * (1/s))."""
     x = _split_heads(qkv, heads)
     amax = np.abs(x).max(axis=(3, 4)).astype(np.float32)  # [3, B, heads]
     with np.errstate(divide="ignore", invalid="ignore"):
