@@ -423,7 +423,7 @@ def time_kernels(args, dev, w, sets) -> dict:
         "conv3x3_dgrad (conv_halo_t_fp8_kernel, weights read in place)": lambda o: _lib.check(
             lib.fp8_conv3x3_dgrad_w(p(o["dyq"]), p(o["wq"]), p(o["dx"]), p(o["sdy"]), p(o["sw"]), b, h, wd, cin,
                                     cout, c_void_p(0), 0, stream()), "dgrad"),
-        "conv3x3_wgrad (memset + wgrad_fp8_kernel halo + convert)": lambda o: _lib.check(lib.fp8_conv3x3_wgrad(
+        "conv3x3_wgrad (accumulator memset + wgrad_fp8_kernel halo with the bf16 conversion)": lambda o: _lib.check(lib.fp8_conv3x3_wgrad(
             p(o["xq"]), p(o["dyq"]), p(o["dw"]), p(o["sx"]), p(o["sdy"]), b, h, wd, cin, cout, 0, p(o["ws"]),
             o["ws"].numel() * 4, stream()), "wgrad"),
     }
@@ -521,6 +521,21 @@ def time_sweep(args, dev) -> dict:
         ms = _time_calls(lambda i: ops.gemm(xs[i][0], wq, xs[i][1], sw, bvec, epi), n_sets, 50, dev)
         out[name] = {"ms": round(ms, 5), "flop": 2.0 * m * n * k, "bytes": m * k + n * k + 2 * m * n + (2 * n if bias else 0)}
         del xs
+        # the op end to end on bf16 inputs: the pair quantize of X and W (current scaling), then the GEMM
+        xb = [rnd((m, k)) for _ in range(n_sets)]
+        wb = rnd((n, k), 0.02)
+        ms_q = _time_calls(lambda i: ops.quantize_current_pair(xb[i], wb), n_sets, 50, dev)
+        out[f"{name}: quantize X + W"] = {"ms": round(ms_q, 5), "flop": None, "bytes": 3 * (m * k + n * k)}
+
+        def full(i):
+            xq, sx, wq2, sw2 = ops.quantize_current_pair(xb[i], wb)
+            return ops.gemm(xq, wq2, sx, sw2, bvec, epi)
+
+        ms_f = _time_calls(full, n_sets, 50, dev)
+        out[f"{name}: whole op (quantize X + W, GEMM)"] = {
+            "ms": round(ms_f, 5), "flop": 2.0 * m * n * k,
+            "bytes": 2 * (m * k + n * k) + 2 * m * n + (2 * n if bias else 0)}
+        del xb
 
     # the delayed quantize (one pass: 2 B read + 1 B written per element) at config 2's X
     n_el = 128 * 128 * 32 * 32
@@ -562,7 +577,7 @@ def roofline(kernels: dict, peaks: dict, batch: int) -> dict | None:
         "quantize_current (quant_stream_kernel amax + cast, 2 launches)": ("hbm", pix * cin * 3.0),  # read bf16 once + write e4m3
         "conv3x3_fwd (conv_halo_t_fp8_kernel)": ("tensor", flops),
         "conv3x3_dgrad (conv_halo_t_fp8_kernel, weights read in place)": ("tensor", flops),
-        "conv3x3_wgrad (memset + wgrad_fp8_kernel halo + convert)": ("tensor", flops),
+        "conv3x3_wgrad (accumulator memset + wgrad_fp8_kernel halo with the bf16 conversion)": ("tensor", flops),
     }
     name = max(kernels, key=lambda k: kernels[k]["ms"])
     bound, work = algo[name]

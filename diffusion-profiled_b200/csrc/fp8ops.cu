@@ -234,6 +234,10 @@ int g_empty_zero = 0;
 // applies (default), 0 = always the two passes (fp8_set_quantize_resident).
 int g_quant_resident = 1;
 
+// Weight gradient: 1 = the bf16 / fp32 conversion folded into the split-K kernel (a
+// cooperative launch) where the grid fits one CTA per SM (default), 0 = a separate launch.
+int g_wgrad_fused = 1;
+
 enum KernelClass { kStreamingKernel = 0, kTensorKernel = 1 };
 
 // Launch `kern` on `stream`, with programmatic stream serialization when enabled
@@ -572,8 +576,23 @@ int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, const CUtens
   using Cfg = WGradConfig<G, HALO>;
   auto kern = wgrad_fp8_kernel<G, HALO>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-  FP8_CUDA_TRY(launch_kernel(kern, dim3(p.num_tiles * p.splits), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1,
-                             kTensorKernel, mdy, mb, mp, p));
+  if (p.grid_arrive != nullptr) {
+    // fused conversion: every CTA must be resident for the grid barrier
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.num_tiles * p.splits));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mdy, mb, mp, p));
+  } else {
+    FP8_CUDA_TRY(launch_kernel(kern, dim3(p.num_tiles * p.splits), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1,
+                               kTensorKernel, mdy, mb, mp, p));
+  }
   count_launches(1);
   return FP8_OK;
 }
@@ -624,8 +643,28 @@ int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, i
   return set_error(FP8_ERR_UNSUPPORTED, "no weight-gradient instance for group=%d", group);
 }
 
+// Weight-gradient launch with the conversion folded in when the grid fits one CTA per SM
+// (g_wgrad_fused); otherwise the split-K kernel and then wgrad_reduce_kernel.
 int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const float* sa, const float* sb,
-                        void* out, int sm_count, cudaStream_t stream, bool f32_out = false) {
+                        void* out, int sm_count, cudaStream_t stream, bool f32_out);
+int launch_wgrad_converted(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, int group, cudaStream_t stream,
+                           bool halo, const float* sa, const float* sb, void* out, bool f32_out, DeviceState* st) {
+  if (g_wgrad_fused && p.num_tiles * p.splits <= st->sm_count) {
+    p.grid_arrive = fold_counter(st);
+    p.grid_depart = fold_counter(st);
+    p.scale_a = sa;
+    p.scale_b = sb;
+    p.out = out;
+    p.out_f32 = f32_out ? 1 : 0;
+    return launch_wgrad(mdy, mb, p, group, stream, halo);
+  }
+  if (int s = launch_wgrad(mdy, mb, p, group, stream, halo)) return s;
+  return launch_wgrad_reduce(p.acc, 1, static_cast<int64_t>(p.m_rows) * p.n_cols, sa, sb, out, st->sm_count, stream,
+                             f32_out);
+}
+
+int launch_wgrad_reduce(const float* partials, int splits, int64_t count, const float* sa, const float* sb,
+                        void* out, int sm_count, cudaStream_t stream, bool f32_out) {
   const int64_t n4 = count / 4;
   int64_t blocks = (n4 + 255) / 256;
   if (blocks > 4 * sm_count) blocks = 4 * sm_count;
@@ -1277,10 +1316,7 @@ int conv3x3_wgrad_impl(const void* xq, const void* dyq, void* dw, bool f32_out, 
   p.acc = static_cast<float*>(workspace);
   p.err = st->err_ptr;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  if (int s = launch_wgrad(mdy, mx, p, w.group, cs, halo)) return s;
-  if (int s = launch_wgrad_reduce(p.acc, 1, static_cast<int64_t>(cout) * 9 * cin, sx, sdy, dw, st->sm_count, cs,
-                                  f32_out))
-    return s;
+  if (int s = launch_wgrad_converted(mdy, mx, p, w.group, cs, halo, sx, sdy, dw, f32_out, st)) return s;
   return ok();
 }
 }  // namespace
@@ -1380,8 +1416,7 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
   p.acc = static_cast<float*>(workspace);
   p.err = st->err_ptr;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  if (int s = launch_wgrad(mdy, mx, p, w.group, cs)) return s;
-  if (int s = launch_wgrad_reduce(p.acc, 1, n * k, sdy, sx, dw, st->sm_count, cs)) return s;
+  if (int s = launch_wgrad_converted(mdy, mx, p, w.group, cs, false, sdy, sx, dw, false, st)) return s;
   return ok();
 }
 
@@ -1397,6 +1432,12 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
 int fp8_set_pdl(int mode) {
   FP8_REQUIRE(mode >= 0 && mode <= 2, FP8_ERR_INVALID_ARGUMENT, "pdl mode must be 0, 1 or 2");
   g_pdl = mode;
+  return ok();
+}
+
+int fp8_set_wgrad_fused(int enable) {
+  FP8_REQUIRE(enable == 0 || enable == 1, FP8_ERR_INVALID_ARGUMENT, "enable must be 0 or 1");
+  g_wgrad_fused = enable;
   return ok();
 }
 

@@ -78,6 +78,15 @@ __device__ __forceinline__ uint4 load_bias_chunk(int epi, const __nv_bfloat16* b
     b = __ldg(reinterpret_cast<const uint4*>(bias + n0 + lane * 8));
   return b;
 }
+// The bias of output columns n0 .. n0 + 8 * lanes - 1: lane l < lanes holds columns
+// n0 + 8l .. n0 + 8l + 7 (zeros past n_total or without a bias epilogue).
+__device__ __forceinline__ uint4 load_bias_tile(int epi, const __nv_bfloat16* bias, int n0, int n_total, int lane,
+                                                int lanes) {
+  uint4 b = make_uint4(0u, 0u, 0u, 0u);
+  if (epi != kEpiNone && lane < lanes && n0 + lane * 8 < n_total)
+    b = __ldg(reinterpret_cast<const uint4*>(bias + n0 + lane * 8));
+  return b;
+}
 __device__ __forceinline__ uint4 bias_vec(const uint4& chunk, int j) {
   return make_uint4(__shfl_sync(0xffffffffu, chunk.x, j), __shfl_sync(0xffffffffu, chunk.y, j),
                     __shfl_sync(0xffffffffu, chunk.z, j), __shfl_sync(0xffffffffu, chunk.w, j));
@@ -265,33 +274,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int nt = tile - mt * p.num_n_tiles;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      // The bias of the tile's BN columns (8 per lane, BN / 8 lanes), loaded before the accumulator
+      // wait so that its latency hides behind the MMAs.
+      const uint4 bias_tile = load_bias_tile(p.epilogue, p.bias, nt * BN, p.N, lane, BN / 8);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int sub = 0; sub < BM_SUB; ++sub) {
-        const int m0 = (mt * BM_SUB + sub) * kSubTileRows + quarter * 32;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 64) {
-          uint32_t r[64];
-          const uint4 bias_chunk = load_bias_chunk(p.epilogue, p.bias, nt * BN + c, p.N, lane);
-          const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols + sub * BN + c;
-          tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-          tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      // 64-column chunks ch = sub * (BN / 64) + c / 64; the TMEM load of chunk ch + 1 is issued
+      // before chunk ch is converted and stored (tcgen05.wait::ld then finds it done).
+      constexpr int kChunks = BM_SUB * (BN / 64);
+      const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols;
+      uint32_t r[2][64];
+      tmem_ld_32x32b_x32(tbase, *reinterpret_cast<uint32_t(*)[32]>(&r[0][0]));
+      tmem_ld_32x32b_x32(tbase + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[0][32]));
+      tmem_ld_wait();
+#pragma unroll
+      for (int ch = 0; ch < kChunks; ++ch) {
+        const int sub = ch / (BN / 64), c = (ch % (BN / 64)) * 64;
+        if (ch + 1 < kChunks) {
+          const uint32_t nx = tbase + (ch + 1) * 64;  // sub * BN + c of the next chunk
+          tmem_ld_32x32b_x32(nx, *reinterpret_cast<uint32_t(*)[32]>(&r[(ch + 1) & 1][0]));
+          tmem_ld_32x32b_x32(nx + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[(ch + 1) & 1][32]));
+        } else {
+          // every read of this accumulator is issued: hand it back to the MMA warp once they land
           tmem_ld_wait();
-          if (sub == BM_SUB - 1 && c + 64 >= BN) {
-            // last read of this accumulator: hand it back to the MMA warp
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[acc]);
-          }
-          const int n0 = nt * BN + c;
-          if (n0 >= p.N) continue;
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[acc]);
+        }
+        const int m0 = (mt * BM_SUB + sub) * kSubTileRows + quarter * 32;
+        const int n0 = nt * BN + c;
+        if (n0 < p.N) {
           uint8_t* sbuf = stage_buf + buf * kEpiBufBytes;
           if (lane == 0) bulk_wait_group_read<1>();  // this buffer's previous store has read smem
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const uint4 o = epilogue8(&r[8 * j], scale, p.epilogue,
-                                     p.epilogue != kEpiNone ? bias_vec(bias_chunk, j) : make_uint4(0u, 0u, 0u, 0u));
+            const uint4 o = epilogue8(&r[ch & 1][8 * j], scale, p.epilogue,
+                                     p.epilogue != kEpiNone ? bias_vec(bias_tile, (c >> 3) + j)
+                                                            : make_uint4(0u, 0u, 0u, 0u));
             st_shared_v4(sbuf + swizzle128_offset(lane, j), o.x, o.y, o.z, o.w);
           }
           fence_proxy_async_smem();
@@ -302,6 +321,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           buf ^= 1;
         }
+        if (ch + 1 < kChunks) tmem_ld_wait();
       }
     }
     if (lane == 0) bulk_wait_group<0>();

@@ -52,7 +52,36 @@ struct WGradParams {
   int m_rows;          // rows of dW (Cout or N)
   float* acc;          // [m_rows][n_cols] fp32, zeroed before the launch
   int* err;
+  // Fused conversion (cooperative launch, every CTA resident): after the last split's
+  // reduce-add, out = acc * (*scale_a) * (*scale_b) as bf16, or those bf16 values widened to
+  // fp32 (out_f32), each CTA converting its share after a grid barrier.  grid_arrive == null:
+  // the conversion is a separate launch (wgrad_reduce_kernel).
+  unsigned int* grid_arrive;
+  unsigned int* grid_depart;
+  const float* scale_a;
+  const float* scale_b;
+  void* out;
+  int out_f32;
 };
+
+// out[i] = convert(acc[i] * scale) for this CTA's share of the m_rows x n_cols accumulator
+// (four elements per step; the count is a multiple of 4).
+__device__ __forceinline__ void wgrad_convert_share(const WGradParams& p) {
+  const int64_t n4 = static_cast<int64_t>(p.m_rows) * p.n_cols / 4;
+  const int64_t per = (n4 + gridDim.x - 1) / gridDim.x;
+  const int64_t b = per * blockIdx.x, e = min(n4, b + per);
+  const float scale = __ldg(p.scale_a) * __ldg(p.scale_b);
+  const float4* a4 = reinterpret_cast<const float4*>(p.acc);
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+    const float4 v = __ldcg(a4 + i);
+    const uint32_t lo = pack_bf16x2(v.x * scale, v.y * scale), hi = pack_bf16x2(v.z * scale, v.w * scale);
+    if (p.out_f32)
+      reinterpret_cast<float4*>(p.out)[i] = make_float4(__uint_as_float(lo << 16), __uint_as_float(lo & 0xFFFF0000u),
+                                                        __uint_as_float(hi << 16), __uint_as_float(hi & 0xFFFF0000u));
+    else
+      reinterpret_cast<uint2*>(p.out)[i] = make_uint2(lo, hi);
+  }
+}
 
 constexpr int kMaxHaloBoxBytes = (128 / 32 + 2) * 32 * 128;  // W = 32 (W = 16 needs 20 KB)
 
@@ -252,6 +281,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (lane == 0) bulk_wait_group<0>();
     }
+    // the reduce-adds are complete; order them before the generic-proxy reads after the barrier
+    if (lane == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
   }
 
   tc_fence_before();
@@ -260,6 +291,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+  if (p.grid_arrive != nullptr && grid_barrier(p.grid_arrive, p.grid_depart, p.err, kErrTimeoutGrid))
+    wgrad_convert_share(p);
 }
 
 // dW[i] = bf16( (sum_s partials[s][i]) * sx * sdy ), i over rows*cols (multiple of 4):

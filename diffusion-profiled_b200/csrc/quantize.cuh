@@ -924,35 +924,6 @@ constexpr int kResSmemCap = 232448 - 4096;  // dynamic bytes a CTA may use (stat
 // Vectors (8 elements) of tensor t owned by CTA c of G: [V c / G, V (c + 1) / G).
 __device__ __forceinline__ int64_t res_slice_begin(int64_t vecs, int c, int G) { return vecs * c / G; }
 
-// Bounded grid barrier for a cooperative launch: every CTA arrives once on
-// `arrive`; the CTA whose departure is the last sets both counters back to 0.
-// Returns false (and records kErrTimeoutQuant) if the others do not arrive in time.
-__device__ __forceinline__ bool res_grid_barrier(unsigned int* arrive, unsigned int* depart, int* err) {
-  __shared__ int passed;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(arrive, 1u);
-    const uint64_t t0 = globaltimer_ns();
-    int ok = 1;
-    while (*reinterpret_cast<volatile unsigned int*>(arrive) < gridDim.x) {
-      if (globaltimer_ns() - t0 > FP8_WAIT_TIMEOUT_NS) {
-        record_error(err, kErrTimeoutQuant);
-        ok = 0;
-        break;
-      }
-    }
-    __threadfence();
-    if (ok && atomicAdd(depart, 1u) == gridDim.x - 1) {
-      *arrive = 0u;
-      *depart = 0u;
-    }
-    passed = ok;
-  }
-  __syncthreads();
-  return passed != 0;
-}
-
 __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQuant m, float* __restrict__ partials,
                                                                          unsigned int* arrive, unsigned int* depart,
                                                                          int* err) {
@@ -1027,7 +998,7 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
       if (threadIdx.x == 0) partials[t * G + c] = bm;
     }
   }
-  if (!res_grid_barrier(arrive, depart, err)) return;
+  if (!grid_barrier(arrive, depart, err, kErrTimeoutQuant)) return;
 #pragma unroll
   for (int t = 0; t < kMaxMultiTensors; ++t) {
     if (t >= m.count) continue;

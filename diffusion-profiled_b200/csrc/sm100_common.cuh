@@ -37,6 +37,7 @@ enum DeviceError : int {
   kErrTimeoutEpilogue = 103,  // epilogue gave up waiting for a finished accumulator
   kErrTimeoutDrain = 104,     // teardown gave up waiting for in-flight async work
   kErrTimeoutQuant = 105,     // streaming quantize pass gave up waiting for a bulk copy / free stage
+  kErrTimeoutGrid = 106,      // a CTA gave up waiting for the others at a grid barrier
   kErrTimeoutSelfTest = 199,  // the failure-path self test's wait gave up (expected)
 };
 
@@ -131,6 +132,36 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int code) {
   return mbar_wait_limit(bar, parity, abort_flag, err, code, FP8_WAIT_TIMEOUT_NS);
+}
+
+// ---------------------------------------------------------------- grid barrier
+// Bounded grid barrier for a cooperative launch: every CTA arrives once on
+// `arrive`; the CTA whose departure is the last sets both counters back to 0.
+// Returns false (and records `code`) if the others do not arrive in time.
+__device__ __forceinline__ bool grid_barrier(unsigned int* arrive, unsigned int* depart, int* err, int code) {
+  __shared__ int passed;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(arrive, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    int ok = 1;
+    while (*reinterpret_cast<volatile unsigned int*>(arrive) < gridDim.x) {
+      if (globaltimer_ns() - t0 > FP8_WAIT_TIMEOUT_NS) {
+        record_error(err, code);
+        ok = 0;
+        break;
+      }
+    }
+    __threadfence();
+    if (ok && atomicAdd(depart, 1u) == gridDim.x - 1) {
+      *arrive = 0u;
+      *depart = 0u;
+    }
+    passed = ok;
+  }
+  __syncthreads();
+  return passed != 0;
 }
 
 // ---------------------------------------------------------------- TMA

@@ -171,6 +171,7 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_set_pdl": (c_int, [c_int]),
     "fp8_set_empty_tensor_history": (c_int, [c_int]),
     "fp8_set_quantize_resident": (c_int, [c_int]),
+    "fp8_set_wgrad_fused": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()
@@ -256,6 +257,12 @@ def set_quantize_resident(enable: bool = True) -> None:
     """Current-scaling quantize as one shared-memory-resident launch where it applies (default)
     or always as two passes."""
     check(load().fp8_set_quantize_resident(int(enable)), "fp8_set_quantize_resident")
+
+
+def set_wgrad_fused(enable: bool = True) -> None:
+    """Weight gradients with the accumulator conversion folded into the split-K launch (default)
+    or as a second launch."""
+    check(load().fp8_set_wgrad_fused(int(enable)), "fp8_set_wgrad_fused")
 
 
 def set_conv_algo(algo: int = 0) -> None:

@@ -311,12 +311,13 @@ class GraphedTrainStep:
 def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16,), p_drop: float = 0.1,
                 device: torch.device | str = "cuda", seed: int = 0, fused_norm: bool = True,
                 fused_resample: bool | None = None, plain: bool = False, skip_empty: bool = False,
-                fp8_attention: bool = False) -> UNet:
+                fp8_attention: bool = False, extended_shapes: bool = False) -> UNet:
     """The reference UNet; ``fused_norm`` / ``fused_resample`` (default: as ``fused_norm``) route its
     norm -> activation chains and its resampling + concatenation to this library's kernels.
     ``plain``: the reference's op structure throughout (every FP8 conv a ``triton_conv2d_fp8`` call,
     scale windows kept by torch ops in the module).  ``skip_empty``: ``fp8_history_skip_empty``.
-    ``fp8_attention``: the attention blocks on the FP8 attention kernels."""
+    ``fp8_attention``: the attention blocks on the FP8 attention kernels.  ``extended_shapes``:
+    ``fp8_extended_shapes`` (FP8 also for the 3x3 convs outside the reference's whitelist)."""
     torch.manual_seed(seed)
     if plain:
         fused_norm, fused_resample = False, False
@@ -325,7 +326,7 @@ def build_model(fp8: bool = True, scaling: str = "delayed", attn_resolutions=(16
                      p_drop=p_drop, fused_norm=fused_norm, fused_resample=fr, fused_residual=fr,
                      batched_time_embed=fr, fused_skip_cast=fr, batched_weight_cast=fr,
                      device_scale_history=not plain, fp8_history_skip_empty=skip_empty,
-                     fp8_attention=fp8_attention)
+                     fp8_attention=fp8_attention, fp8_extended_shapes=extended_shapes)
     model = UNet(cfg).to(memory_format=torch.channels_last)
     return model.to(device)
 

@@ -388,3 +388,39 @@ def test_launch_modes_give_the_same_results(cuda, mode):
     excess = (a - b).abs() - (2.0 ** -7 * a.abs() + 1e-4 * a.abs().max())
     assert excess.max().item() <= 0.0, excess.max().item()
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_wgrad_conversion_fused_and_separate_agree(cuda, fused):
+    """The weight gradient with the accumulator conversion folded into the split-K launch
+    (cooperative, grid barrier) and as a separate launch: the oracle's dW, bf16 and widened fp32,
+    eagerly and from a CUDA graph."""
+    from fp8_b200 import _lib, ops
+
+    g = torch.Generator().manual_seed(41)
+    x = (torch.randn(32, 128, 32, 32, generator=g)).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
+    dy = (torch.randn(32, 128, 32, 32, generator=g) * 1e-2).to(torch.bfloat16).contiguous(
+        memory_format=torch.channels_last)
+    xq, sx = oracle.quantize_tensor(x)
+    dyq, sdy = oracle.quantize_tensor(dy)
+    ref = oracle.conv_dw(xq, dyq, sx, sdy)
+    try:
+        _lib.set_wgrad_fused(fused)
+        args = (xq.to(cuda), dyq.to(cuda), sx.to(cuda), sdy.to(cuda))
+        dw = ops.conv3x3_wgrad(*args, 0)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            ops.conv3x3_wgrad(*args, 0)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            dw_g = ops.conv3x3_wgrad(*args, 0)
+        graph.replay()
+        graph.replay()
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_wgrad_fused(True)
+    assert oracle.max_rel_err(dw, ref) <= TOL
+    assert oracle.max_rel_err(dw_g, ref) <= TOL
+    assert _lib.device_error() == 0

@@ -148,6 +148,8 @@ def loss_curves(cuda):
         "fp8_delayed_skip_empty": _loss_curve(cuda, fp8=True, scaling="delayed", skip_empty=True),
         "fp8_delayed_skip_empty_fp8_attention": _loss_curve(cuda, fp8=True, scaling="delayed", skip_empty=True,
                                                             fp8_attention=True),
+        "fp8_delayed_skip_empty_extended": _loss_curve(cuda, fp8=True, scaling="delayed", skip_empty=True,
+                                                       extended_shapes=True),
         "fp8_delayed": _loss_curve(cuda, fp8=True, scaling="delayed"),
         "fp8_delayed_plain": _loss_curve(cuda, fp8=True, scaling="delayed", plain=True),
     }
@@ -161,13 +163,15 @@ CURVE_MEAN_TOL = 0.02
 CURVE_MA50_TOL = 0.03
 
 
-@pytest.mark.parametrize("name", ["fp8_current", "fp8_delayed_skip_empty", "fp8_delayed_skip_empty_fp8_attention"])
+@pytest.mark.parametrize("name", ["fp8_current", "fp8_delayed_skip_empty", "fp8_delayed_skip_empty_fp8_attention",
+                                  "fp8_delayed_skip_empty_extended"])
 def test_fp8_loss_curve_within_2pct_of_bf16(loss_curves, name):
     """North-star loss bar: over 200 steps the FP8 curve stays within 2 % of bf16 (mean of
     the 10-step moving average's relative gap over steps 50-200; the 50-step moving average
     within 3 % everywhere).  Both FP8 scalings meet it: current scaling (unet.py:24's default)
     and delayed scaling (train.py:230-231's fastest config) when an all-zero tensor records
-    scale 0 in its history, also with the attention blocks on the FP8 attention kernels."""
+    scale 0 in its history, also with the attention blocks on the FP8 attention kernels and
+    with FP8 for the 512 -> 256 conv at 4x4 outside the reference's whitelist."""
     curve, ref = loss_curves[name], loss_curves["bf16"]
     assert np.isfinite(curve).all() and np.isfinite(ref).all()
     assert ref[-50:].mean() < 0.5 * ref[:10].mean()  # it trains
