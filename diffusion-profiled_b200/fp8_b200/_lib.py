@@ -259,9 +259,9 @@ def set_quantize_resident(enable: bool = True) -> None:
     check(load().fp8_set_quantize_resident(int(enable)), "fp8_set_quantize_resident")
 
 
-def set_wgrad_fused(enable: bool = True) -> None:
-    """Weight gradients with the accumulator conversion folded into the split-K launch (default)
-    or as a second launch."""
+def set_wgrad_fused(enable: bool = False) -> None:
+    """Weight gradients with the accumulator conversion folded into the split-K launch, or as a
+    second launch (the default)."""
     check(load().fp8_set_wgrad_fused(int(enable)), "fp8_set_wgrad_fused")
 
 

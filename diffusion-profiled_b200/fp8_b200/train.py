@@ -221,6 +221,13 @@ class GraphedTrainStep:
         self.dp = BucketedAllReduce(self.params, dp_group, int(cfg.allreduce_bucket_mb * (1 << 20))) \
             if dist.is_initialized() and \
             dist.get_world_size(dp_group) > 1 else None
+        if self.dp is not None and model.parameters().__next__().is_cuda:
+            # The one-launch variants (weight-gradient conversion, current quantize) are cooperative
+            # launches that need every SM; next to NCCL kernels on the comm stream they would wait for
+            # the all-reduce to drain instead of overlapping it, so data parallel uses the two-launch forms.
+            from . import _lib
+            _lib.set_wgrad_fused(False)
+            _lib.set_quantize_resident(False)
         cin, res = model.config.in_channels, model.config.in_resolution
         self.static_batch = torch.zeros(cfg.batch_size, cin, res, res, device=device).to(
             memory_format=torch.channels_last)

@@ -265,11 +265,12 @@ int fp8_set_empty_tensor_history(int mode);
  * Same bytes and scales either way.  Process-wide; for benchmarks and tests. */
 int fp8_set_quantize_resident(int enable);
 
-/* Weight gradients (fp8_conv3x3_wgrad, _f32, fp8_gemm_wgrad): enable = 1 (default)
- * folds the conversion of the fp32 split-K accumulator into the weight-gradient
- * launch (a cooperative launch whose CTAs meet at a grid barrier) when its grid
- * fits one CTA per SM; enable = 0 always converts in a second launch.  Same
- * results either way.  Process-wide; for benchmarks and tests. */
+/* Weight gradients (fp8_conv3x3_wgrad, _f32, fp8_gemm_wgrad): enable = 1 folds
+ * the conversion of the fp32 split-K accumulator into the weight-gradient launch
+ * (a cooperative launch whose CTAs meet at a grid barrier) when its grid fits one
+ * CTA per SM; enable = 0 (default: the barrier costs more than the launch it
+ * saves) converts in a second launch.  Same results either way.  Process-wide;
+ * for benchmarks and tests. */
 int fp8_set_wgrad_fused(int enable);
 
 /* Tuning override for the quantize grids: CTAs per SM of the amax pass and of

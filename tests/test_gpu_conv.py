@@ -420,7 +420,7 @@ def test_wgrad_conversion_fused_and_separate_agree(cuda, fused):
         graph.replay()
         torch.cuda.synchronize()
     finally:
-        _lib.set_wgrad_fused(True)
+        _lib.set_wgrad_fused(False)
     assert oracle.max_rel_err(dw, ref) <= TOL
     assert oracle.max_rel_err(dw_g, ref) <= TOL
     assert _lib.device_error() == 0
