@@ -240,9 +240,9 @@ int g_quant_resident = 1;
 // conversion launch they replace, 25.8 vs 24.6 us for the whole dW).
 int g_wgrad_fused = 0;
 
-// Halo weight gradients: 1 = the split-K partials of 4 CTAs combined through distributed
-// shared memory in a cluster before the L2 reduce-add (default), 0 = every CTA reduce-adds
-// its whole tile (fp8_set_wgrad_cluster).
+// Halo weight gradients: 1 = the split-K partials of a cluster's CTAs combined through
+// distributed shared memory before the L2 reduce-add, 0 = every CTA reduce-adds its whole
+// tile (default; fp8_set_wgrad_cluster).
 int g_wgrad_cluster = 0;
 constexpr int kWgradCluster = 2;
 bool wgrad_cluster_on() { return g_wgrad_cluster != 0 && g_wgrad_fused == 0; }

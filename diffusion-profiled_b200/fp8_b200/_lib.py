@@ -266,9 +266,9 @@ def set_wgrad_fused(enable: bool = False) -> None:
     check(load().fp8_set_wgrad_fused(int(enable)), "fp8_set_wgrad_fused")
 
 
-def set_wgrad_cluster(enable: bool = True) -> None:
+def set_wgrad_cluster(enable: bool = False) -> None:
     """Halo-mode conv weight gradients with the split-K partials of 2-CTA clusters combined in
-    distributed shared memory (default) or each CTA reduce-adding its whole tile."""
+    distributed shared memory, or each CTA reduce-adding its whole tile (the default)."""
     check(load().fp8_set_wgrad_cluster(int(enable)), "fp8_set_wgrad_cluster")
 
 

@@ -274,12 +274,12 @@ int fp8_set_quantize_resident(int enable);
 int fp8_set_wgrad_fused(int enable);
 
 /* Halo-mode conv weight gradients (3x3, 16x16 / 32x32 images, 3-box column groups):
- * enable = 1 (default) runs the split-K kernel as clusters of 2 CTAs on one output
+ * enable = 1 runs the split-K kernel as clusters of 2 CTAs on one output
  * tile that add their partial accumulators through distributed shared memory, so
  * that each reduce-adds half of the tile into L2 (the automatic split count is
- * rounded down to whole clusters that are resident at once); enable = 0: every CTA
- * reduce-adds its whole tile.  Same results up to the fp32 summation order.
- * Process-wide. */
+ * rounded down to whole clusters that are resident at once); enable = 0 (default):
+ * every CTA reduce-adds its whole tile.  Same results up to the fp32 summation
+ * order.  Process-wide. */
 int fp8_set_wgrad_cluster(int enable);
 
 /* Tuning override for the quantize grids: CTAs per SM of the amax pass and of
