@@ -240,18 +240,6 @@ int g_quant_resident = 1;
 // conversion launch they replace, 25.8 vs 24.6 us for the whole dW).
 int g_wgrad_fused = 0;
 
-// Halo weight gradients: 1 = the split-K partials of a cluster's CTAs combined through
-// distributed shared memory before the L2 reduce-add, 0 = every CTA reduce-adds its whole
-// tile (default; fp8_set_wgrad_cluster).
-int g_wgrad_cluster = 0;
-constexpr int kWgradCluster = 2;
-bool wgrad_cluster_on() { return g_wgrad_cluster != 0 && g_wgrad_fused == 0; }
-
-// Clusters of the halo weight-gradient kernel that can be resident at once (cached per
-// device); the split count is bounded by it so that the grid runs in one wave.
-std::atomic<int> g_wgrad_max_clusters[kMaxDevices] = {};
-int wgrad_max_clusters(int sm_count);
-
 enum KernelClass { kStreamingKernel = 0, kTensorKernel = 1 };
 
 // Launch `kern` on `stream`, with programmatic stream serialization when enabled
@@ -584,11 +572,11 @@ int check_conv_args(int batch, int height, int width, int cin, int cout, ConvTil
 }
 
 // ------------------------------------------------------------------ weight-gradient launch
-template <int G, bool HALO = false, int CL = 1>
+template <int G, bool HALO = false>
 int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, const CUtensorMap& mp, WGradParams p,
                      cudaStream_t stream) {
   using Cfg = WGradConfig<G, HALO>;
-  auto kern = wgrad_fp8_kernel<G, HALO, CL>;
+  auto kern = wgrad_fp8_kernel<G, HALO>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   if (p.grid_arrive != nullptr) {
     // fused conversion: every CTA must be resident for the grid barrier
@@ -604,38 +592,11 @@ int launch_wgrad_cfg(const CUtensorMap& mdy, const CUtensorMap& mb, const CUtens
     cfg.numAttrs = 1;
     FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mdy, mb, mp, p));
   } else {
-    FP8_CUDA_TRY(launch_kernel(kern, dim3(p.num_tiles * p.splits), dim3(kGemmThreads), Cfg::kSmemBytes, stream, CL,
+    FP8_CUDA_TRY(launch_kernel(kern, dim3(p.num_tiles * p.splits), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1,
                                kTensorKernel, mdy, mb, mp, p));
   }
   count_launches(1);
   return FP8_OK;
-}
-
-int wgrad_max_clusters(int sm_count) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return sm_count / kWgradCluster;
-  int n = g_wgrad_max_clusters[dev].load(std::memory_order_relaxed);
-  if (n > 0) return n;
-  using Cfg = WGradConfig<3, true>;
-  auto kern = wgrad_fp8_kernel<3, true, kWgradCluster>;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(sm_count - sm_count % kWgradCluster));
-  cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = kWgradCluster;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess ||
-      cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-    (void)cudaGetLastError();
-    n = sm_count / kWgradCluster / 2;  // conservative
-  }
-  g_wgrad_max_clusters[dev].store(n, std::memory_order_relaxed);
-  return n;
 }
 
 struct WGradPlan {
@@ -676,8 +637,6 @@ int launch_wgrad(const CUtensorMap& mdy, const CUtensorMap& mb, WGradParams p, i
   FP8_CUDA_TRY(cudaMemsetAsync(p.acc, 0, static_cast<size_t>(p.m_rows) * p.n_cols * sizeof(float), stream));
   if (halo) {
     FP8_REQUIRE(group == 3, FP8_ERR_UNSUPPORTED, "halo weight-gradient needs group 3, got %d", group);
-    if (p.grid_arrive == nullptr && p.splits % kWgradCluster == 0 && wgrad_cluster_on())
-      return launch_wgrad_cfg<3, true, kWgradCluster>(mdy, mb, mp, p, stream);
     return launch_wgrad_cfg<3, true>(mdy, mb, mp, p, stream);
   }
   if (group == 1) return launch_wgrad_cfg<1>(mdy, mb, mp, p, stream);
@@ -1331,19 +1290,12 @@ int conv3x3_wgrad_impl(const void* xq, const void* dyq, void* dw, bool f32_out, 
   DeviceState* st;
   if (int s = device_state(&st)) return s;
   const int64_t pixels = static_cast<int64_t>(batch) * height * width;
-  WGradPlan w = plan_wgrad(cout, 9ll * cin, pixels, split_k, st->sm_count);
+  const WGradPlan w = plan_wgrad(cout, 9ll * cin, pixels, split_k, st->sm_count);
   const size_t need = static_cast<size_t>(cout) * 9 * cin * sizeof(float);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
               "wgrad workspace too small: need %zu bytes", need);
   // Halo mode: 128-pixel K blocks of whole image rows of one image, 3-box groups.
   const bool halo = g_conv_algo != 1 && w.group == 3 && halo_applies(height, width);
-  // the automatic split count, rounded down to whole clusters that are resident at once
-  if (halo && split_k <= 0 && wgrad_cluster_on() && w.splits >= 2 * kWgradCluster) {
-    const int max_clusters = wgrad_max_clusters(st->sm_count);
-    int s2 = std::min(w.splits, max_clusters * kWgradCluster / std::max(1, w.num_tiles));
-    s2 -= s2 % kWgradCluster;
-    if (s2 >= 2 * kWgradCluster) w.splits = s2;
-  }
   CUtensorMap mdy, mx;
   if (int s = make_map_2d(&mdy, dyq, pixels, cout, 128)) return s;
   if (halo) {
@@ -1482,12 +1434,6 @@ int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm) {
 int fp8_set_pdl(int mode) {
   FP8_REQUIRE(mode >= 0 && mode <= 2, FP8_ERR_INVALID_ARGUMENT, "pdl mode must be 0, 1 or 2");
   g_pdl = mode;
-  return ok();
-}
-
-int fp8_set_wgrad_cluster(int enable) {
-  FP8_REQUIRE(enable == 0 || enable == 1, FP8_ERR_INVALID_ARGUMENT, "enable must be 0 or 1");
-  g_wgrad_cluster = enable;
   return ok();
 }
 

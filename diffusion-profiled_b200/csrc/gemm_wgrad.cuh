@@ -96,25 +96,11 @@ struct WGradConfig {
   static_assert(kSmemBytes <= 232448, "smem");
 };
 
-// Cluster exchange of the split-K partials (CL > 1): the CL CTAs of a cluster work on the
-// same tile (consecutive splits).  After every MMA of the cluster has finished (cluster
-// barrier), each CTA writes the columns of its accumulator that another CTA owns (the tile's
-// G * 128 columns are dealt out CL ways) into that CTA's now idle pipeline shared memory,
-// fp32 rows of kClRowBytes; after a second cluster barrier each CTA adds the CL - 1 received
-// partials to its own columns and reduce-adds only those into L2, so the L2 reduce traffic
-// is 1 / CL of one reduce-add per CTA.
-constexpr int kClRowPad = 16;  // bytes after each received row (keeps the 32 lanes' rows on distinct banks)
-
-template <int G, bool HALO = false, int CL = 1>
+template <int G, bool HALO = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     wgrad_fp8_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_acc, const WGradParams p) {
   using Cfg = WGradConfig<G, HALO>;
-  static_assert(CL == 1 || (G * 128) % (CL * 32) == 0, "each CTA owns whole 32-column chunks");
-  constexpr int kOwn = G * 128 / CL;                 // columns a CTA reduces
-  constexpr int kClRowBytes = kOwn * 4 + kClRowPad;  // one received fp32 row
-  constexpr int kClSlotBytes = 128 * kClRowBytes;    // one sender's partial
-  static_assert(CL == 1 || (CL - 1) * kClSlotBytes <= Cfg::kStages * Cfg::kStageBytes, "receive buffers");
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -130,11 +116,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // CL > 1: cluster q = blockIdx.x / CL holds splits (q / num_tiles) * CL + rank of tile q % num_tiles
-  const int crank = CL > 1 ? static_cast<int>(blockIdx.x % CL) : 0;
-  const int cq = CL > 1 ? static_cast<int>(blockIdx.x / CL) : static_cast<int>(blockIdx.x);
-  const int tile = cq % p.num_tiles;
-  const int split = CL > 1 ? (cq / p.num_tiles) * CL + crank : cq / p.num_tiles;
+  const int tile = blockIdx.x % p.num_tiles;
+  const int split = blockIdx.x / p.num_tiles;
   const int co_tile = tile / p.num_groups;
   const int group = tile - co_tile * p.num_groups;
   const int kb_begin = static_cast<int>((static_cast<int64_t>(split) * p.k_blocks) / p.splits);
@@ -164,7 +147,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_sync();
-  bool epi_ready = false;  // cluster mode: this epilogue warp's accumulator is complete
 
   if (warp == 0) {
     if (lane == 0) {
@@ -265,11 +247,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       volatile int never = 0;
       mbar_wait(drain_bar, 0, &never, p.err, kErrTimeoutDrain);
     }
-  } else if (CL > 1) {
-    // Cluster mode: wait for this CTA's accumulator here; the exchange runs below, where
-    // every thread of the CTA takes part in the cluster barriers.
-    epi_ready = __all_sync(0xffffffffu,
-                           kb_end > kb_begin && mbar_wait(tfull_bar, 0, abort_flag, p.err, kErrTimeoutEpilogue));
   } else {
     // Epilogue: this split's fp32 rows, 32 columns (128 B) at a time, staged
     // 128B-swizzled in shared memory and added into the accumulator by TMA.
@@ -306,80 +283,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     // the reduce-adds are complete; order them before the generic-proxy reads after the barrier
     if (lane == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
-  }
-
-  if constexpr (CL > 1) {
-    const bool epi = warp >= 2;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // accumulator row (TMEM lane) of this thread
-    const uint32_t trow = tmem_base + (uint32_t(quarter * 32) << 16);
-    // (1) every MMA of the cluster is done: the pipeline shared memory of every CTA is idle
-    tc_fence_before();
-    __syncthreads();
-    cluster_sync();
-    tc_fence_after();
-    if (epi && epi_ready) {
-      // (2) the columns owned by CTA q go into slot (rank < q ? rank : rank - 1) of q's buffer
-      const uint32_t local = smem_u32(smem);
-#pragma unroll 1
-      for (int q = 0; q < CL; ++q) {
-        if (q == crank) continue;
-        const int slot = crank < q ? crank : crank - 1;
-        const uint32_t dst = mapa_shared(local + slot * kClSlotBytes + row * kClRowBytes, q);
-#pragma unroll 1
-        for (int k = 0; k < kOwn; k += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(trow + q * kOwn + k, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            st_cluster_v4(dst + (k + 4 * j) * 4, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-        }
-      }
-    }
-    // (3) every partial has landed
-    __syncthreads();
-    cluster_sync();
-    if (epi && epi_ready) {
-      uint8_t* stage_buf = epi_smem + (warp - 2) * 2 * kEpiBufBytes;
-      const int row0 = co_tile * 128 + quarter * 32;
-      int buf = 0;
-#pragma unroll 1
-      for (int k = 0; k < kOwn; k += 32) {
-        const int c = crank * kOwn + k;  // tile column of this chunk
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(trow + c, r);
-        tmem_ld_wait();
-#pragma unroll 1
-        for (int slot = 0; slot < CL - 1; ++slot) {
-          const uint8_t* src = smem + slot * kClSlotBytes + row * kClRowBytes + k * 4;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint4 v = ld_shared_v4(src + 16 * j);
-            r[4 * j] = __float_as_uint(__uint_as_float(r[4 * j]) + __uint_as_float(v.x));
-            r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) + __uint_as_float(v.y));
-            r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) + __uint_as_float(v.z));
-            r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) + __uint_as_float(v.w));
-          }
-        }
-        uint8_t* sbuf = stage_buf + buf * kEpiBufBytes;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          st_shared_v4(sbuf + swizzle128_offset(lane, j), r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          const int col = HALO ? ((c >> 7) * 3 + group % 3) * p.cchunks * 128 + (group / 3) * 128 + (c & 127)
-                               : group * G * 128 + c;
-          tma_reduce_add_2d(&tmap_acc, sbuf, col, row0);
-          bulk_commit_group();
-        }
-        buf ^= 1;
-      }
-      if (lane == 0) bulk_wait_group<0>();
-    }
   }
 
   tc_fence_before();

@@ -172,7 +172,6 @@ _SIGNATURES: dict[str, tuple] = {
     "fp8_set_empty_tensor_history": (c_int, [c_int]),
     "fp8_set_quantize_resident": (c_int, [c_int]),
     "fp8_set_wgrad_fused": (c_int, [c_int]),
-    "fp8_set_wgrad_cluster": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()
@@ -264,12 +263,6 @@ def set_wgrad_fused(enable: bool = False) -> None:
     """Weight gradients with the accumulator conversion folded into the split-K launch, or as a
     second launch (the default)."""
     check(load().fp8_set_wgrad_fused(int(enable)), "fp8_set_wgrad_fused")
-
-
-def set_wgrad_cluster(enable: bool = False) -> None:
-    """Halo-mode conv weight gradients with the split-K partials of 2-CTA clusters combined in
-    distributed shared memory, or each CTA reduce-adding its whole tile (the default)."""
-    check(load().fp8_set_wgrad_cluster(int(enable)), "fp8_set_wgrad_cluster")
 
 
 def set_conv_algo(algo: int = 0) -> None:

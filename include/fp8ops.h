@@ -273,15 +273,6 @@ int fp8_set_quantize_resident(int enable);
  * for benchmarks and tests. */
 int fp8_set_wgrad_fused(int enable);
 
-/* Halo-mode conv weight gradients (3x3, 16x16 / 32x32 images, 3-box column groups):
- * enable = 1 runs the split-K kernel as clusters of 2 CTAs on one output
- * tile that add their partial accumulators through distributed shared memory, so
- * that each reduce-adds half of the tile into L2 (the automatic split count is
- * rounded down to whole clusters that are resident at once); enable = 0 (default):
- * every CTA reduce-adds its whole tile.  Same results up to the fp32 summation
- * order.  Process-wide. */
-int fp8_set_wgrad_cluster(int enable);
-
 /* Tuning override for the quantize grids: CTAs per SM of the amax pass and of
  * the cast pass (1..8; 0 restores the built-in choice).  Process-wide. */
 int fp8_set_quantize_override(int amax_blocks_per_sm, int cast_blocks_per_sm);

@@ -15,7 +15,6 @@ import fp8_oracle as oracle
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-2
-CLUSTER_DEFAULT = False  # the library's default for fp8_set_wgrad_cluster
 
 SUPPORTED = [
     (128, 128, 32, 32),
@@ -424,43 +423,4 @@ def test_wgrad_conversion_fused_and_separate_agree(cuda, fused):
         _lib.set_wgrad_fused(False)
     assert oracle.max_rel_err(dw, ref) <= TOL
     assert oracle.max_rel_err(dw_g, ref) <= TOL
-    assert _lib.device_error() == 0
-
-
-@pytest.mark.parametrize("shape", [(128, 128, 128, 32, 32), (16, 256, 256, 16, 16), (8, 512, 128, 32, 32)])
-def test_wgrad_cluster_exchange_matches_oracle(cuda, shape):
-    """Halo weight gradient with the split-K partials of 2-CTA clusters added through distributed
-    shared memory (the default) and without: both the oracle's dW, eagerly and from a CUDA graph."""
-    from fp8_b200 import _lib, ops
-
-    b, cin, cout, h, w = shape
-    g = torch.Generator().manual_seed(sum(shape))
-    x = torch.randn(b, cin, h, w, generator=g).to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
-    dy = (torch.randn(b, cout, h, w, generator=g) * 1e-2).to(torch.bfloat16).contiguous(
-        memory_format=torch.channels_last)
-    xq, sx = oracle.quantize_tensor(x)
-    dyq, sdy = oracle.quantize_tensor(dy)
-    ref = oracle.conv_dw(xq, dyq, sx, sdy)
-    args = (xq.to(cuda), dyq.to(cuda), sx.to(cuda), sdy.to(cuda))
-    outs = []
-    try:
-        for cluster in (True, False):
-            _lib.set_wgrad_cluster(cluster)
-            outs.append(ops.conv3x3_wgrad(*args, 0))
-        _lib.set_wgrad_cluster(True)  # the graph captures the cluster form
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            ops.conv3x3_wgrad(*args, 0)
-        torch.cuda.current_stream().wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            dw_g = ops.conv3x3_wgrad(*args, 0)
-        graph.replay()
-        torch.cuda.synchronize()
-        outs.append(dw_g)
-    finally:
-        _lib.set_wgrad_cluster(CLUSTER_DEFAULT)
-    for dw in outs:
-        assert oracle.max_rel_err(dw, ref) <= TOL
     assert _lib.device_error() == 0
