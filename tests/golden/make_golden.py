@@ -159,6 +159,8 @@ def main(reference_root: str) -> None:
     data.update(gen_conv_case(fk, "c128x8", batch=2, cin=128, cout=128, h=8, w=8, seed=1))
     data.update(gen_conv_case(fk, "c256x4", batch=8, cin=256, cout=256, h=4, w=4, seed=2))
     data.update(gen_conv_case(fk, "c128to256x16", batch=1, cin=128, cout=256, h=16, w=16, seed=3))
+    # config 2's layer (128 -> 128 at 32x32) at batch 2: the 32x32 halo kernels' shape
+    data.update(gen_conv_case(fk, "c128x32", batch=2, cin=128, cout=128, h=32, w=32, seed=4))
     out = HERE / "reference_kernels.npz"
     np.savez_compressed(out, **data)
     print(f"wrote {out} ({out.stat().st_size} bytes, {len(data)} arrays)")

@@ -58,7 +58,7 @@ def _golden_case(golden, tag, device):
     )
 
 
-@pytest.mark.parametrize("tag", ["c128x8", "c256x4", "c128to256x16"])
+@pytest.mark.parametrize("tag", ["c128x8", "c256x4", "c128to256x16", "c128x32"])
 def test_conv_matches_reference_kernel_outputs(cuda, golden, tag):
     from fp8_b200 import ops
 

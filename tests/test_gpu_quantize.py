@@ -148,7 +148,7 @@ def test_quantize_matches_golden_scales(cuda, golden, name):
 def test_transpose_2d_matches_reference_fixture(cuda, golden):
     from fp8_b200 import ops
 
-    for tag in ("c128x8", "c256x4", "c128to256x16"):
+    for tag in ("c128x8", "c256x4", "c128to256x16", "c128x32"):
         b, cin, cout, h, w = (int(v) for v in golden[f"{tag}_dims"])
         dyq = torch.from_numpy(golden[f"{tag}_dyq"].reshape(b * h * w, cout)).view(torch.float8_e4m3fn).to(cuda)
         t = ops.transpose_2d(dyq)

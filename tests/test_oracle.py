@@ -90,7 +90,7 @@ def test_quantize_scales_match_reference_kernels(golden, name):
     assert s_curr.tobytes() == golden[f"q_{name}_delayed_scale"].tobytes()
 
 
-CONV_CASES = ["c128x8", "c256x4", "c128to256x16"]
+CONV_CASES = ["c128x8", "c256x4", "c128to256x16", "c128x32"]
 
 
 def _conv_case(golden, tag):
