@@ -537,15 +537,21 @@ def time_sweep(args, dev) -> dict:
             "bytes": 2 * (m * k + n * k) + 2 * m * n + (2 * n if bias else 0)}
         del xb
 
-    # the delayed quantize (one pass: 2 B read + 1 B written per element) at config 2's X
-    n_el = 128 * 128 * 32 * 32
-    n_sets = 4
-    xs = [rnd((128, 128, 32, 32)).contiguous(memory_format=cl) for _ in range(n_sets)]
+    # the quantize at config 2's X and at 4x that size (batch 512), which separates the fixed
+    # cost of a launch (start-up, first bytes, tail) from the streaming rate: delayed is one pass
+    # (2 B read + 1 B written per element), current reads x twice (or once, shared-memory
+    # resident, where the per-SM shares fit) and writes once; both quoted on 3 B/element
     prev = torch.tensor(0.01, device=dev)
-    ms = _time_calls(lambda i: ops.quantize_delayed(xs[i], prev), n_sets, 50, dev)
-    out["quantize delayed config 2 X (16.8 M elements)"] = {"ms": round(ms, 5), "flop": None, "bytes": 3 * n_el}
-    del xs
-    torch.cuda.empty_cache()
+    for b, n_sets in ((128, 4), (512, 2)):
+        n_el = b * 128 * 32 * 32
+        xs = [rnd((b, 128, 32, 32)).contiguous(memory_format=cl) for _ in range(n_sets)]
+        tag = f"config 2 X, batch {b} ({n_el / 1e6:.1f} M elements)"
+        ms = _time_calls(lambda i: ops.quantize_delayed(xs[i], prev), n_sets, 50, dev)
+        out[f"quantize delayed {tag}"] = {"ms": round(ms, 5), "flop": None, "bytes": 3 * n_el}
+        ms = _time_calls(lambda i: ops.quantize_current(xs[i]), n_sets, 50, dev)
+        out[f"quantize current {tag}"] = {"ms": round(ms, 5), "flop": None, "bytes": 3 * n_el}
+        del xs
+        torch.cuda.empty_cache()
     return out
 
 

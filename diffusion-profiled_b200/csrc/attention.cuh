@@ -80,10 +80,6 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint6
       : "memory");
 }
 
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 // Per-tensor scale of the reference quantize: amax/448 in IEEE fp32, 1 for amax 0.
 __device__ __forceinline__ float attn_scale(float amax) { return amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f; }
 

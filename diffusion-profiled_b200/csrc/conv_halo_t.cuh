@@ -137,8 +137,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      // Weights, column tap by column tap (the order the MMA loop uses them).
-      for (int kw = 0; kw < 3; ++kw) {
+      // Weights, column tap by column tap (the order the MMA loop uses them), each group
+      // issued just before the first tile's box of the same column tap, so that the first
+      // MMAs wait for one weight group and one box rather than all 144 KB of weights.
+      // (Every CTA has at least one item: the grid is at most the tiles of a column tile.)
+      int w_issued = 0;
+      auto load_weights = [&](int kw) {
+        ++w_issued;
         mbar_arrive_expect_tx(&w_full[kw], 3 * Cfg::kWTapBytes);
         for (int kh = 0; kh < 3; ++kh) {
           const int tap = kh * 3 + kw;
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           else
             tma_load_2d(w_smem + tap * Cfg::kWTapBytes, &tmap_w, &w_full[kw], tap * kKBlockBytes, nt * 128);
         }
-      }
+      };
       int s = 0;
       uint32_t ph = 0;
       int64_t issued = 0;
@@ -158,6 +163,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int img = m0 / p.HW;
         const int h0 = (m0 - img * p.HW) / W;
         for (int kw = 0; kw < 3; ++kw) {
+          if (u == 0) load_weights(kw);
           if (!mbar_wait(&box_empty[s], ph ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         volatile int never = 0;
         for (int64_t k = (issued > AS ? issued - AS : 0); k < issued; ++k)
           mbar_wait(&box_full[k % AS], uint32_t((k / AS) & 1), &never, p.err, kErrTimeoutDrain);
-        for (int k = 0; k < 3; ++k) mbar_wait(&w_full[k], 0, &never, p.err, kErrTimeoutDrain);
+        for (int k = 0; k < w_issued; ++k) mbar_wait(&w_full[k], 0, &never, p.err, kErrTimeoutDrain);
       }
     }
   } else if (warp == 1) {

@@ -499,15 +499,15 @@ int launch_conv_halo(const void* act, const void* wmat, void* out, const float* 
 }
 
 // ------------------------------------------------------------------ K-major GEMM launch
-template <int BM_SUB, int BN, int STAGES>
+template <int BM_SUB, int BN, int STAGES, int EPI = kEpiWarps>
 int launch_kgemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, KGemmParams p,
                      int sm_count, cudaStream_t stream) {
-  using Cfg = KGemmConfig<BM_SUB, BN, STAGES>;
-  auto kern = kgemm_fp8_kernel<BM_SUB, BN, STAGES>;
+  using Cfg = KGemmConfig<BM_SUB, BN, STAGES, EPI>;
+  auto kern = kgemm_fp8_kernel<BM_SUB, BN, STAGES, EPI>;
   FP8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
   const int grid = p.num_tiles < sm_count ? p.num_tiles : sm_count;
-  FP8_CUDA_TRY(launch_kernel(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, 1, kTensorKernel, ma, mb,
-                             mo, p));
+  FP8_CUDA_TRY(launch_kernel(kern, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, 1, kTensorKernel, ma,
+                             mb, mo, p));
   count_launches(1);
   return FP8_OK;
 }
@@ -515,7 +515,12 @@ int launch_kgemm_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
 struct KGemmShape {
   int64_t M, N;
   int k_blocks;
+  bool plain = false;  // plain GEMM (no conv window)
 };
+
+// Plain GEMMs with at most this many 128-byte K blocks take the eight-epilogue-warp
+// instances (their tile time is the epilogue's) and column tiles of 256 or 128.
+constexpr int kShortKBlocks = 8;
 
 void choose_kgemm_tile(const KGemmShape& s, int sm_count, int* bm_sub, int* bn) {
   if (g_override_bn > 0 && s.N % g_override_bn == 0) {
@@ -531,6 +536,13 @@ void choose_kgemm_tile(const KGemmShape& s, int sm_count, int* bm_sub, int* bn) 
   // fewer tiles than that at every width, the narrowest (most tiles).
   const int64_t m_tiles = (s.M + 127) / 128;
   *bm_sub = 1;
+  // Short-K plain GEMMs: 256 columns where that gives about a wave, else 128 (their
+  // 64-column tiles measured slower: config 1 14.3 vs 11.3 / 9.1 us at 128 / 256, and the
+  // time-embedding GEMM 128 x 11264 x 512 5.7 vs 4.8 us at 128).
+  if (s.plain && s.k_blocks <= kShortKBlocks && s.N % 128 == 0) {
+    *bn = (s.N % 256 == 0 && m_tiles * (s.N / 256) * 5 >= static_cast<int64_t>(sm_count) * 4) ? 256 : 128;
+    return;
+  }
   for (int cand : {256, 128, 64}) {
     if (s.N % cand != 0 && !(cand == 64 && s.N % 32 == 0)) continue;
     const int64_t tiles = m_tiles * ((s.N + cand - 1) / cand);
@@ -546,6 +558,14 @@ int launch_kgemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap
   const int64_t tiles = m_tiles * p.num_n_tiles;
   FP8_REQUIRE(tiles < (1ll << 31), FP8_ERR_UNSUPPORTED, "too many tiles");
   p.num_tiles = static_cast<int>(tiles);
+  // Short reductions (plain GEMMs of a few K blocks): the epilogue, not the MMAs, sets the
+  // tile rate, so eight epilogue warps drain the accumulators (tiles of at least two
+  // 64-column chunks; a 64-column tile keeps four).
+  if (p.a_conv == 0 && p.k_blocks <= kShortKBlocks) {
+    if (bm_sub == 1 && bn == 128) return launch_kgemm_cfg<1, 128, 4, 8>(ma, mb, mo, p, sm_count, stream);
+    if (bm_sub == 1 && bn == 256) return launch_kgemm_cfg<1, 256, 3, 8>(ma, mb, mo, p, sm_count, stream);
+    if (bm_sub == 2 && bn == 128) return launch_kgemm_cfg<2, 128, 3, 8>(ma, mb, mo, p, sm_count, stream);
+  }
   if (bm_sub == 1 && bn == 64) return launch_kgemm_cfg<1, 64, 8>(ma, mb, mo, p, sm_count, stream);
   if (bm_sub == 1 && bn == 128) return launch_kgemm_cfg<1, 128, 6>(ma, mb, mo, p, sm_count, stream);
   if (bm_sub == 1 && bn == 256) return launch_kgemm_cfg<1, 256, 4>(ma, mb, mo, p, sm_count, stream);
@@ -1355,7 +1375,7 @@ int fp8_gemm(const void* a, const void* b, void* out, const float* sa, const flo
   if (int s = device_state(&st)) return s;
   const int k_blocks = static_cast<int>((k + 127) / 128);
   int bm_sub, bn;
-  choose_kgemm_tile({m, n, k_blocks}, st->sm_count, &bm_sub, &bn);
+  choose_kgemm_tile({m, n, k_blocks, true}, st->sm_count, &bm_sub, &bn);
   CUtensorMap ma, mb;
   if (int s = make_map_2d(&ma, a, m, k, 128)) return s;
   if (int s = make_map_2d(&mb, b, n, k, bn)) return s;

@@ -54,16 +54,24 @@ struct KGemmParams {
   int* err;
 };
 
-template <int BM_SUB, int BN, int STAGES>
+// EPI epilogue warps (4 or 8): with 8, two warps share each TMEM lane quarter and
+// take alternate 64-column chunks, which doubles the rate at which accumulators
+// are drained -- the limit of GEMMs with a short K (2-4 K blocks per tile), where
+// a tile's epilogue takes longer than its MMAs.
+template <int BM_SUB, int BN, int STAGES, int EPI = kEpiWarps>
 struct KGemmConfig {
   static_assert(BM_SUB == 1 || BM_SUB == 2, "BM_SUB");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(EPI == 4 || EPI == 8, "EPI");
+  static constexpr int kThreads = 64 + 32 * EPI;
   static constexpr int kBTileBytes = BN * kKBlockBytes;
   static constexpr int kStageBytes = BM_SUB * kATileBytes + kBTileBytes;
   static constexpr int kAccCols = BM_SUB * BN;            // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : 2 * kAccCols;  // power of two here
+  static constexpr int kEpiStageBytes = EPI * 2 * kEpiBufBytes;  // two staging buffers per epilogue warp
+  static constexpr int kBiasBytes = EPI * 64 * 4;                // a chunk's bias as fp32, one copy per warp
   static constexpr int kBarBytes = 1024;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiSmemBytes + kBarBytes + 1024;  // +1024 alignment
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kEpiStageBytes + kBiasBytes + kBarBytes + 1024;  // +1024 alignment
   static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
   static_assert(kSmemBytes <= 232448, "smem");
 };
@@ -78,18 +86,33 @@ __device__ __forceinline__ uint4 load_bias_chunk(int epi, const __nv_bfloat16* b
     b = __ldg(reinterpret_cast<const uint4*>(bias + n0 + lane * 8));
   return b;
 }
-// The bias of output columns n0 .. n0 + 8 * lanes - 1: lane l < lanes holds columns
-// n0 + 8l .. n0 + 8l + 7 (zeros past n_total or without a bias epilogue).
-__device__ __forceinline__ uint4 load_bias_tile(int epi, const __nv_bfloat16* bias, int n0, int n_total, int lane,
-                                                int lanes) {
-  uint4 b = make_uint4(0u, 0u, 0u, 0u);
-  if (epi != kEpiNone && lane < lanes && n0 + lane * 8 < n_total)
-    b = __ldg(reinterpret_cast<const uint4*>(bias + n0 + lane * 8));
-  return b;
-}
 __device__ __forceinline__ uint4 bias_vec(const uint4& chunk, int j) {
   return make_uint4(__shfl_sync(0xffffffffu, chunk.x, j), __shfl_sync(0xffffffffu, chunk.y, j),
                     __shfl_sync(0xffffffffu, chunk.z, j), __shfl_sync(0xffffffffu, chunk.w, j));
+}
+
+// 8 consecutive output columns of one row from fp32 accumulator bits: acc * scale, then
+// + bias (8 fp32 from shared memory) and SiLU, as packed f32x2 operations (the same two
+// roundings as the scalar form), bf16x8.
+__device__ __forceinline__ uint4 epilogue8_f32bias(const uint32_t* acc, float2 scale2, int epi, const float* bias8) {
+  float2 v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    v[i] = __fmul2_rn(make_float2(__uint_as_float(acc[2 * i]), __uint_as_float(acc[2 * i + 1])), scale2);
+  if (epi != kEpiNone) {
+    const float4 b0 = *reinterpret_cast<const float4*>(bias8);
+    const float4 b1 = *reinterpret_cast<const float4*>(bias8 + 4);
+    v[0] = __fadd2_rn(v[0], make_float2(b0.x, b0.y));
+    v[1] = __fadd2_rn(v[1], make_float2(b0.z, b0.w));
+    v[2] = __fadd2_rn(v[2], make_float2(b1.x, b1.y));
+    v[3] = __fadd2_rn(v[3], make_float2(b1.z, b1.w));
+    if (epi == kEpiBiasSilu) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = make_float2(silu_f32(v[i].x), silu_f32(v[i].y));
+    }
+  }
+  return make_uint4(pack_bf16x2(v[0].x, v[0].y), pack_bf16x2(v[1].x, v[1].y), pack_bf16x2(v[2].x, v[2].y),
+                    pack_bf16x2(v[3].x, v[3].y));
 }
 
 // 8 consecutive output columns of one row: scale, optional bias / SiLU, bf16x8.
@@ -113,15 +136,16 @@ __device__ __forceinline__ uint4 epilogue8(const uint32_t* acc, float scale, int
                     pack_bf16x2(v[6], v[7]));
 }
 
-template <int BM_SUB, int BN, int STAGES>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BM_SUB, int BN, int STAGES, int EPI = kEpiWarps>
+__global__ void __launch_bounds__(KGemmConfig<BM_SUB, BN, STAGES, EPI>::kThreads, 1)
     kgemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_out, const KGemmParams p) {
-  using Cfg = KGemmConfig<BM_SUB, BN, STAGES>;
+  using Cfg = KGemmConfig<BM_SUB, BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_smem = smem + STAGES * Cfg::kStageBytes;
-  uint8_t* bar_area = epi_smem + kEpiSmemBytes;
+  float* bias_smem = reinterpret_cast<float*>(epi_smem + Cfg::kEpiStageBytes);
+  uint8_t* bar_area = epi_smem + Cfg::kEpiStageBytes + Cfg::kBiasBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
@@ -140,7 +164,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], kEpiWarps * 32);
+      mbar_init(&tempty_bar[a], EPI * 32);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -264,9 +288,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // Warp w may read TMEM lanes [32 (w % 4), +32); with 8 epilogue warps the two warps
+    // of a lane quarter (w - 2 < 4 and w - 2 >= 4) take alternate 64-column chunks.
+    const int quarter = warp & 3;
+    constexpr int kPerQuarter = EPI / 4;
+    const int part = (warp - 2) / 4;
     uint8_t* stage_buf = epi_smem + (warp - 2) * 2 * kEpiBufBytes;
+    float* bias_w = bias_smem + (warp - 2) * 64;  // this warp's fp32 copy of the chunk's bias
     const float scale = __ldg(p.scale_a) * __ldg(p.scale_b);
+    const float2 scale2 = make_float2(scale, scale);
+    constexpr int kChunks = BM_SUB * (BN / 64);  // 64-column chunks per tile: ch = sub * (BN / 64) + c / 64
+    // every epilogue warp reads (and releases) at least one chunk of every tile, so that each
+    // accumulator use gets exactly EPI * 32 arrivals on its tempty barrier
+    static_assert(kChunks >= kPerQuarter, "fewer 64-column chunks than epilogue warps per lane quarter");
     int local = 0;
     int buf = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
@@ -274,43 +308,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int nt = tile - mt * p.num_n_tiles;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      // The bias of the tile's BN columns (8 per lane, BN / 8 lanes), loaded before the accumulator
-      // wait so that its latency hides behind the MMAs.
-      const uint4 bias_tile = load_bias_tile(p.epilogue, p.bias, nt * BN, p.N, lane, BN / 8);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      // 64-column chunks ch = sub * (BN / 64) + c / 64; the TMEM load of chunk ch + 1 is issued
-      // before chunk ch is converted and stored (tcgen05.wait::ld then finds it done).
-      constexpr int kChunks = BM_SUB * (BN / 64);
       const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + acc * Cfg::kAccCols;
-      uint32_t r[2][64];
-      tmem_ld_32x32b_x32(tbase, *reinterpret_cast<uint32_t(*)[32]>(&r[0][0]));
-      tmem_ld_32x32b_x32(tbase + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[0][32]));
-      tmem_ld_wait();
-#pragma unroll
-      for (int ch = 0; ch < kChunks; ++ch) {
+#pragma unroll 1
+      for (int ch = part; ch < kChunks; ch += kPerQuarter) {
         const int sub = ch / (BN / 64), c = (ch % (BN / 64)) * 64;
-        if (ch + 1 < kChunks) {
-          const uint32_t nx = tbase + (ch + 1) * 64;  // sub * BN + c of the next chunk
-          tmem_ld_32x32b_x32(nx, *reinterpret_cast<uint32_t(*)[32]>(&r[(ch + 1) & 1][0]));
-          tmem_ld_32x32b_x32(nx + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[(ch + 1) & 1][32]));
-        } else {
-          // every read of this accumulator is issued: hand it back to the MMA warp once they land
-          tmem_ld_wait();
+        const int m0 = (mt * BM_SUB + sub) * kSubTileRows + quarter * 32;
+        const int n0 = nt * BN + c;
+        // the chunk's 64 bias values (lane l: columns n0 + 2l, n0 + 2l + 1), loaded before the
+        // accumulator so that the load overlaps the TMEM read
+        uint32_t bw = 0u;
+        if (p.epilogue != kEpiNone && n0 + 2 * lane < p.N)
+          bw = __ldg(reinterpret_cast<const uint32_t*>(p.bias + n0 + 2 * lane));
+        uint32_t r[64];
+        tmem_ld_32x32b_x32(tbase + ch * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld_32x32b_x32(tbase + ch * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld_wait();
+        if (ch + kPerQuarter >= kChunks) {
+          // this warp's last read of the accumulator: hand it back to the MMA warp
           tc_fence_before();
           mbar_arrive(&tempty_bar[acc]);
         }
-        const int m0 = (mt * BM_SUB + sub) * kSubTileRows + quarter * 32;
-        const int n0 = nt * BN + c;
+        if (p.epilogue != kEpiNone) {
+          __syncwarp();  // every lane is done with the previous chunk's bias
+          *reinterpret_cast<float2*>(bias_w + 2 * lane) = make_float2(bf16_lo_f(bw), bf16_hi_f(bw));
+          __syncwarp();
+        }
         if (n0 < p.N) {
           uint8_t* sbuf = stage_buf + buf * kEpiBufBytes;
           if (lane == 0) bulk_wait_group_read<1>();  // this buffer's previous store has read smem
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const uint4 o = epilogue8(&r[ch & 1][8 * j], scale, p.epilogue,
-                                     p.epilogue != kEpiNone ? bias_vec(bias_tile, (c >> 3) + j)
-                                                            : make_uint4(0u, 0u, 0u, 0u));
+            const uint4 o = epilogue8_f32bias(&r[8 * j], scale2, p.epilogue, bias_w + 8 * j);
             st_shared_v4(sbuf + swizzle128_offset(lane, j), o.x, o.y, o.z, o.w);
           }
           fence_proxy_async_smem();
@@ -321,7 +352,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           buf ^= 1;
         }
-        if (ch + 1 < kChunks) tmem_ld_wait();
       }
     }
     if (lane == 0) bulk_wait_group<0>();

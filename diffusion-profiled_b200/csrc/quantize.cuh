@@ -135,8 +135,10 @@ __device__ __forceinline__ uint32_t DivF64::word(uint32_t w) const {
   return cvt_e4m3x2(scale_and_clamp(bf16_lo_f(w), *this), scale_and_clamp(bf16_hi_f(w), *this));
 }
 
-// Block-wide max of a non-negative value over NT threads; result valid in every thread.
-template <int NT = kQuantThreads>
+// Max of a non-negative value over threads 0 .. NT-1; result valid in each of them.
+// BAR = 0: all NT threads of the block (__syncthreads); BAR > 0: named barrier BAR over
+// the first NT threads only (the others may be busy elsewhere, e.g. a producer warp).
+template <int NT = kQuantThreads, int BAR = 0>
 __device__ __forceinline__ float block_max(float v) {
   static_assert(NT % 32 == 0 && NT <= 1024, "block size");
   __shared__ float red[NT / 32];
@@ -145,14 +147,14 @@ __device__ __forceinline__ float block_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) red[warp] = v;
-  __syncthreads();
+  if (BAR == 0) __syncthreads(); else named_barrier_sync(BAR, NT);
   if (warp == 0) {
     float w = lane < (NT / 32) ? red[lane] : 0.0f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
     if (lane == 0) result = w;
   }
-  __syncthreads();
+  if (BAR == 0) __syncthreads(); else named_barrier_sync(BAR, NT);
   return result;
 }
 
@@ -192,19 +194,19 @@ __device__ __forceinline__ float history_entry(float amax, int empty_zero) {
 
 // Fold `count` partial maxima into the tensor scale (every CTA does this; the
 // partials are a few KB and L2 resident).
-template <int NT = kQuantThreads>
+template <int NT = kQuantThreads, int BAR = 0>
 __device__ __forceinline__ float fold_partials_to_scale(const float* __restrict__ partials, int count) {
   float m = 0.0f;
   for (int i = threadIdx.x; i < count; i += NT) m = fmaxf(m, partials[i]);
-  return scale_from_amax(block_max<NT>(m));
+  return scale_from_amax(block_max<NT, BAR>(m));
 }
 
-template <int NT = kQuantThreads>
+template <int NT = kQuantThreads, int BAR = 0>
 __device__ __forceinline__ float delayed_scale(const DelayedSource& d) {
   if (d.window == nullptr) return *d.prev;  // uniform over the grid
   float m = 0.0f;
   for (int i = threadIdx.x; i < d.len; i += NT) m = fmaxf(m, d.window[i]);
-  m = block_max<NT>(m);
+  m = block_max<NT, BAR>(m);
   if (d.used != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *d.used = m;
   return m;
 }
@@ -444,20 +446,16 @@ __device__ __forceinline__ uint32_t stream_consume(const uint8_t* bufs, uint64_t
   return m2;
 }
 
-// Both roles plus the tail; returns this thread's |x| max (amax kinds).
+// Consumer side plus the tail; returns this thread's |x| max (amax kinds).  CTA 0's
+// consumers also handle the n % 8 tail elements with plain loads.
 template <int KIND, class Div>
-__device__ __forceinline__ float stream_body(const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n,
-                                             uint8_t* bufs, uint64_t* full, uint64_t* empty, const Div& div,
-                                             volatile int* abort_flag, int* err) {
-  const StreamShape sh = stream_shape(n);
-  float m = 0.0f;
-  if (threadIdx.x >= kStreamConsumers) {
-    if (threadIdx.x == kStreamConsumers) stream_produce(x, bufs, full, empty, sh, abort_flag, err);
-  } else {
-    m = unpack_max2(stream_consume<KIND>(bufs, full, empty, q, sh, div, abort_flag, err));
-  }
+__device__ __forceinline__ float stream_consume_all(const uint16_t* __restrict__ x, uint8_t* __restrict__ q,
+                                                    int64_t n, const uint8_t* bufs, uint64_t* full, uint64_t* empty,
+                                                    const StreamShape& sh, const Div& div, volatile int* abort_flag,
+                                                    int* err) {
+  float m = unpack_max2(stream_consume<KIND>(bufs, full, empty, q, sh, div, abort_flag, err));
   if (blockIdx.x == 0) {
-    for (int64_t i = (sh.main_bytes >> 1) + threadIdx.x; i < n; i += kStreamThreads) {
+    for (int64_t i = (sh.main_bytes >> 1) + threadIdx.x; i < n; i += kStreamConsumers) {
       const uint32_t w = x[i];
       if (KIND != kStreamCastCurrent) m = fmaxf(m, fabsf(__uint_as_float(w << 16)));
       if (KIND != kStreamAmax) q[i] = static_cast<uint8_t>(div.word(w) & 0xFFu);
@@ -466,7 +464,13 @@ __device__ __forceinline__ float stream_body(const uint16_t* __restrict__ x, uin
   return m;
 }
 
+// Named barrier of the consumer warps (the producer warp streams meanwhile).
+constexpr int kStreamConsumerBar = 1;
+
 // x 16-byte aligned, q 8-byte aligned.  Dynamic shared memory: kStreamSmemBytes.
+// The producer starts its copies as soon as the barriers exist; the consumers fold the
+// scale (current: the amax partials; delayed: the previous scale or the history max)
+// while the first chunks are in flight.
 template <int KIND>
 __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
     const uint16_t* __restrict__ x, uint8_t* __restrict__ q, int64_t n, const float* __restrict__ partials_in,
@@ -486,19 +490,24 @@ __global__ void __launch_bounds__(kStreamThreads) quant_stream_kernel(
     abort_flag = 0;
     fence_barrier_init();
   }
-  float s = 1.0f;
-  if (KIND == kStreamCastCurrent) {
-    s = fold_partials_to_scale<kStreamThreads>(partials_in, n_partials);  // contains __syncthreads
-    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
+  __syncthreads();
+  const StreamShape sh = stream_shape(n);
+  float m = 0.0f;
+  if (threadIdx.x >= kStreamConsumers) {
+    if (threadIdx.x == kStreamConsumers) stream_produce(x, bufs, full, empty, sh, &abort_flag, err);
   } else {
-    if (KIND == kStreamCastDelayed) s = delayed_scale<kStreamThreads>(prev_scale);
-    __syncthreads();
+    float s = 1.0f;
+    if (KIND == kStreamCastCurrent) {
+      s = fold_partials_to_scale<kStreamConsumers, kStreamConsumerBar>(partials_in, n_partials);
+      if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
+    } else if (KIND == kStreamCastDelayed) {
+      s = delayed_scale<kStreamConsumers, kStreamConsumerBar>(prev_scale);
+    }
+    if (KIND == kStreamAmax || !markstein_applies(s))  // s is uniform over the grid: no divergence
+      m = stream_consume_all<KIND>(x, q, n, bufs, full, empty, sh, DivF64(s), &abort_flag, err);
+    else
+      m = stream_consume_all<KIND>(x, q, n, bufs, full, empty, sh, make_markstein(s), &abort_flag, err);
   }
-  float m;
-  if (KIND == kStreamAmax || !markstein_applies(s))  // s is uniform over the grid: no divergence
-    m = stream_body<KIND>(x, q, n, bufs, full, empty, DivF64(s), &abort_flag, err);
-  else
-    m = stream_body<KIND>(x, q, n, bufs, full, empty, make_markstein(s), &abort_flag, err);
   if (KIND != kStreamCastCurrent) {
     const float bm = block_max<kStreamThreads>(m);
     if (threadIdx.x == 0) partials_out[blockIdx.x] = bm;
@@ -631,17 +640,18 @@ __global__ void __launch_bounds__(kStreamThreads) quant_multi_cast_kernel(MultiQ
   uint64_t* empty = full + kStreamStages;
   __shared__ int abort_flag;
   float sc[kMaxMultiTensors] = {1.0f, 1.0f, 1.0f, 1.0f};
-  for (int u = 0; u < m.count; ++u) {
-    const float su = fold_partials_to_scale<kStreamThreads>(partials + u * n_partials, n_partials);
-#pragma unroll
-    for (int w = 0; w < kMaxMultiTensors; ++w)
-      if (w == u) sc[w] = su;
-    if (blockIdx.x == 0 && threadIdx.x == 0) *m.scale_out[u] = su;
-  }
   multi_init(full, empty, &abort_flag);
   if (threadIdx.x == kStreamConsumers) {
-    multi_produce(m, bufs, full, empty, &abort_flag, err);
+    multi_produce(m, bufs, full, empty, &abort_flag, err);  // starts while the consumers fold the scales
   } else if (threadIdx.x < kStreamConsumers) {
+    for (int u = 0; u < m.count; ++u) {
+      const float su = fold_partials_to_scale<kStreamConsumers, kStreamConsumerBar>(partials + u * n_partials,
+                                                                                     n_partials);
+#pragma unroll
+      for (int w = 0; w < kMaxMultiTensors; ++w)
+        if (w == u) sc[w] = su;
+      if (blockIdx.x == 0 && threadIdx.x == 0) *m.scale_out[u] = su;
+    }
     const int t0 = threadIdx.x;
     int64_t i = 0;
     for (int64_t k = blockIdx.x; k < m.chunk_begin[m.count]; k += gridDim.x, ++i) {
@@ -684,13 +694,13 @@ __global__ void __launch_bounds__(kStreamThreads) quant_multi_cast_kernel(MultiQ
       }
     }
   }
-  if (blockIdx.x == 0) {
+  if (blockIdx.x == 0 && threadIdx.x < kStreamConsumers) {  // the tails, with the consumers' folded scales
     for (int u = 0; u < m.count; ++u) {
       float s = sc[0];
 #pragma unroll
       for (int w = 1; w < kMaxMultiTensors; ++w)
         if (w == u) s = sc[w];
-      for (int64_t e = (m.main_bytes[u] >> 1) + threadIdx.x; e < m.n[u]; e += kStreamThreads) {
+      for (int64_t e = (m.main_bytes[u] >> 1) + threadIdx.x; e < m.n[u]; e += kStreamConsumers) {
         const uint32_t wv = m.x[u][e];
         m.q[u][e] = static_cast<uint8_t>((markstein_applies(s) ? make_markstein(s).word(wv) : DivF64(s).word(wv)) &
                                          0xFFu);
@@ -963,24 +973,26 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
       }
     }
   }
-  // |x| max per tensor, piece by piece as the copies land (a piece is at most 2 vectors per thread)
+  // |x| max per tensor as the copies land: warp w takes pieces w, w + 16, ..., so each
+  // warp waits on its own pieces' barriers only; within a piece, the part of each
+  // tensor it holds (offsets are multiples of 16 bytes).
   uint32_t m2[kMaxMultiTensors] = {0u, 0u, 0u, 0u};
   bool ok = true;
-  static_assert(kResPiece == 2 * 16 * kResThreads, "two vectors per thread per piece");
-  for (int i = 0; i < npieces; ++i) {
-    ok = __all_sync(0xffffffffu, mbar_wait(&bars[i], 0, &abort_flag, err, kErrTimeoutQuant));
-    if (!ok) break;
-    const int64_t o0 = static_cast<int64_t>(i) * kResPiece + threadIdx.x * 16;
-    const int64_t o1 = o0 + kResThreads * 16;
-    const bool h0 = o0 < total, h1 = o1 < total;
-    const uint4 a0 = h0 ? ld_shared_v4(res_smem + o0) : make_uint4(0u, 0u, 0u, 0u);
-    const uint4 a1 = h1 ? ld_shared_v4(res_smem + o1) : make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t x0 = absmax_vec2(a0), x1 = absmax_vec2(a1);
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = warp; i < npieces; i += kResThreads / 32) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[i], 0, &abort_flag, err, kErrTimeoutQuant));
+      if (!ok) break;
+      const int64_t p0 = static_cast<int64_t>(i) * kResPiece, p1 = min(total, p0 + kResPiece);
 #pragma unroll
-    for (int u = 0; u < kMaxMultiTensors; ++u) {
-      const int64_t lo = soff[u], hi = soff[u] + vcnt[u] * 16;  // empty for u >= count
-      if (o0 >= lo && o0 < hi) m2[u] = bf16x2_max(m2[u], x0);
-      if (o1 >= lo && o1 < hi) m2[u] = bf16x2_max(m2[u], x1);
+      for (int u = 0; u < kMaxMultiTensors; ++u) {
+        const int64_t lo = max(p0, soff[u]), hi = min(p1, soff[u] + vcnt[u] * 16);  // empty for u >= count
+        uint32_t mu = 0u;
+#pragma unroll 4
+        for (int64_t o = lo + lane * 16; o < hi; o += 32 * 16)
+          mu = bf16x2_max(mu, absmax_vec2(ld_shared_v4(res_smem + o)));
+        m2[u] = bf16x2_max(m2[u], mu);
+      }
     }
   }
   if (!__syncthreads_and(ok)) {
