@@ -301,6 +301,15 @@ __global__ void __launch_bounds__(KGemmConfig<BM_SUB, BN, STAGES, EPI>::kThreads
     // every epilogue warp reads (and releases) at least one chunk of every tile, so that each
     // accumulator use gets exactly EPI * 32 arrivals on its tempty barrier
     static_assert(kChunks >= kPerQuarter, "fewer 64-column chunks than epilogue warps per lane quarter");
+    // Lane l's two bias values (columns 2l, 2l + 1) of chunk ch of tile t.  Each chunk's pair is
+    // loaded one chunk ahead (the first chunk of a tile at the end of the previous one), so the
+    // load latency hides behind a chunk's work instead of stalling the warp.
+    auto bias_pair = [&](int t, int ch) -> uint32_t {
+      if (p.epilogue == kEpiNone || t >= p.num_tiles) return 0u;
+      const int n = (t % p.num_n_tiles) * BN + (ch % (BN / 64)) * 64 + 2 * lane;
+      return n < p.N ? __ldg(reinterpret_cast<const uint32_t*>(p.bias + n)) : 0u;
+    };
+    uint32_t bw_next = bias_pair(blockIdx.x, part);
     int local = 0;
     int buf = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
@@ -316,11 +325,8 @@ __global__ void __launch_bounds__(KGemmConfig<BM_SUB, BN, STAGES, EPI>::kThreads
         const int sub = ch / (BN / 64), c = (ch % (BN / 64)) * 64;
         const int m0 = (mt * BM_SUB + sub) * kSubTileRows + quarter * 32;
         const int n0 = nt * BN + c;
-        // the chunk's 64 bias values (lane l: columns n0 + 2l, n0 + 2l + 1), loaded before the
-        // accumulator so that the load overlaps the TMEM read
-        uint32_t bw = 0u;
-        if (p.epilogue != kEpiNone && n0 + 2 * lane < p.N)
-          bw = __ldg(reinterpret_cast<const uint32_t*>(p.bias + n0 + 2 * lane));
+        const uint32_t bw = bw_next;
+        bw_next = ch + kPerQuarter < kChunks ? bias_pair(tile, ch + kPerQuarter) : bias_pair(tile + gridDim.x, part);
         uint32_t r[64];
         tmem_ld_32x32b_x32(tbase + ch * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld_32x32b_x32(tbase + ch * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
