@@ -830,10 +830,10 @@ int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const floa
 // The shared-memory-resident current quantize (quant_resident_kernel) for the
 // tensors of `m`, if it applies: every n a multiple of 8 (x 16-byte, q 8-byte
 // aligned: the caller's vec path), at least 4 MB in all (below that the two
-// passes are launch-bound either way), each CTA's slices within its shared
-// memory, and count * sm_count partial slots.  *launched = false otherwise.
-int launch_quant_resident(const MultiQuant& m, float* partials, size_t partial_slots, DeviceState* st,
-                          cudaStream_t cs, bool* launched) {
+// passes are launch-bound either way) and each CTA's slices within its shared
+// memory.  *launched = false otherwise.  It needs no workspace: the maxima meet in
+// one word per tensor from the library's pool of self-resetting counters.
+int launch_quant_resident(const MultiQuant& m, DeviceState* st, cudaStream_t cs, bool* launched) {
   *launched = false;
   const int G = st->sm_count;
   int64_t bytes = 0, smem = 0;
@@ -842,7 +842,7 @@ int launch_quant_resident(const MultiQuant& m, float* partials, size_t partial_s
     bytes += m.n[t] * 2;
     smem += ((m.n[t] / 8 + G - 1) / G) * 16;
   }
-  if (bytes < (4 << 20) || smem > kResSmemCap || partial_slots < static_cast<size_t>(m.count) * G) return FP8_OK;
+  if (bytes < (4 << 20) || smem > kResSmemCap) return FP8_OK;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
@@ -851,6 +851,8 @@ int launch_quant_resident(const MultiQuant& m, float* partials, size_t partial_s
   FP8_CUDA_TRY(attr);
   unsigned int* arrive = fold_counter(st);
   unsigned int* depart = fold_counter(st);
+  ResAmax am{};
+  for (int t = 0; t < m.count; ++t) am.word[t] = fold_counter(st);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(G));
   cfg.blockDim = dim3(kResThreads);
@@ -861,7 +863,7 @@ int launch_quant_resident(const MultiQuant& m, float* partials, size_t partial_s
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_resident_kernel, m, partials, arrive, depart, st->err_ptr));
+  FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_resident_kernel, m, arrive, depart, am, st->err_ptr));
   count_launches(1);
   *launched = true;
   return FP8_OK;
@@ -878,9 +880,7 @@ int launch_quantize_current(const uint16_t* x, uint8_t* q, float* scale_out, flo
     m.scale_out[0] = scale_out;
     m.n[0] = n;
     bool launched = false;
-    if (int s = launch_quant_resident(m, partials, static_cast<size_t>(parts), const_cast<DeviceState*>(st), cs,
-                                      &launched))
-      return s;
+    if (int s = launch_quant_resident(m, const_cast<DeviceState*>(st), cs, &launched)) return s;
     if (launched) return FP8_OK;
   }
   if (vec) {
@@ -1753,7 +1753,7 @@ int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   if (g_quant_resident) {
     bool launched = false;
-    if (int s = launch_quant_resident(m, partials, workspace_bytes / sizeof(float), st, cs, &launched)) return s;
+    if (int s = launch_quant_resident(m, st, cs, &launched)) return s;
     if (launched) return ok();
   }
   FP8_CUDA_TRY(cudaFuncSetAttribute(quant_multi_amax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

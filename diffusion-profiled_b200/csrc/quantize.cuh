@@ -934,9 +934,52 @@ constexpr int kResSmemCap = 232448 - 4096;  // dynamic bytes a CTA may use (stat
 // Vectors (8 elements) of tensor t owned by CTA c of G: [V c / G, V (c + 1) / G).
 __device__ __forceinline__ int64_t res_slice_begin(int64_t vecs, int c, int G) { return vecs * c / G; }
 
-__global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQuant m, float* __restrict__ partials,
-                                                                         unsigned int* arrive, unsigned int* depart,
-                                                                         int* err) {
+// One zeroed word per tensor for the CTAs' |x| maxima (atomic max of the fp32 bits:
+// non-negative floats order like their bit patterns); the grid barrier reads them and
+// the last CTA through it zeroes them again.
+struct ResAmax {
+  unsigned int* word[kMaxMultiTensors];
+};
+
+// Grid barrier of the resident quantize that also hands every CTA the tensors' maxima:
+// thread 0 arrives, waits (bounded) for the others, reads the words into amax_s and
+// departs; the last CTA to depart sets the counters and the words back to zero (every CTA
+// has read them before its departure).  Every CTA reads `count` words instead of all
+// CTAs' partial maxima (148 x 148 loads of the same few lines).
+__device__ __forceinline__ bool res_grid_barrier(unsigned int* arrive, unsigned int* depart, const ResAmax& am,
+                                                 int count, float* amax_s, int* err) {
+  __shared__ int passed;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(arrive, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    int ok = 1;
+    while (*reinterpret_cast<volatile unsigned int*>(arrive) < gridDim.x) {
+      if (globaltimer_ns() - t0 > FP8_WAIT_TIMEOUT_NS) {
+        record_error(err, kErrTimeoutQuant);
+        ok = 0;
+        break;
+      }
+    }
+    __threadfence();
+    if (ok) {
+      for (int t = 0; t < count; ++t)
+        amax_s[t] = __uint_as_float(*reinterpret_cast<volatile unsigned int*>(am.word[t]));
+      if (atomicAdd(depart, 1u) == gridDim.x - 1) {
+        *arrive = 0u;
+        *depart = 0u;
+        for (int t = 0; t < count; ++t) *am.word[t] = 0u;
+      }
+    }
+    passed = ok;
+  }
+  __syncthreads();
+  return passed != 0;
+}
+
+__global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQuant m, unsigned int* arrive,
+                                                                         unsigned int* depart, ResAmax am, int* err) {
   extern __shared__ __align__(128) uint8_t res_smem[];
   __shared__ __align__(8) uint64_t bars[kResMaxPieces];
   __shared__ int abort_flag;
@@ -1007,16 +1050,15 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
   for (int t = 0; t < kMaxMultiTensors; ++t) {
     if (t < m.count) {
       const float bm = block_max<kResThreads>(unpack_max2(m2[t]));
-      if (threadIdx.x == 0) partials[t * G + c] = bm;
+      if (threadIdx.x == 0) atomicMax(am.word[t], __float_as_uint(bm));
     }
   }
-  if (!grid_barrier(arrive, depart, err, kErrTimeoutQuant)) return;
+  __shared__ float amax_s[kMaxMultiTensors];
+  if (!res_grid_barrier(arrive, depart, am, m.count, amax_s, err)) return;
 #pragma unroll
   for (int t = 0; t < kMaxMultiTensors; ++t) {
     if (t >= m.count) continue;
-    float mx = 0.0f;
-    for (int i = threadIdx.x; i < G; i += kResThreads) mx = fmaxf(mx, __ldcg(partials + t * G + i));
-    const float s = scale_from_amax(block_max<kResThreads>(mx));
+    const float s = scale_from_amax(amax_s[t]);
     if (c == 0 && threadIdx.x == 0) *m.scale_out[t] = s;
     uint2* qv = reinterpret_cast<uint2*>(m.q[t] + vbeg[t] * 8);
     const uint8_t* src = res_smem + soff[t];
