@@ -414,7 +414,7 @@ def time_kernels(args, dev, w, sets) -> dict:
     torch.cuda.synchronize()
 
     calls = {
-        "quantize_current (quant_stream_kernel amax + cast, 2 launches)": lambda o: _lib.check(lib.fp8_quantize_current(
+        "quantize_current (quant_resident_kernel: one launch, x read once)": lambda o: _lib.check(lib.fp8_quantize_current(
             p(o["x"]), p(o["q_out"]), p(o["s_out"]), p(o["qws"]), o["qws"].numel() * 4, o["x"].numel(), stream()),
             "q"),
         "conv3x3_fwd (conv_halo_t_fp8_kernel)": lambda o: _lib.check(lib.fp8_conv3x3_fwd(
@@ -581,7 +581,7 @@ def roofline(kernels: dict, peaks: dict, batch: int) -> dict | None:
     cin, cout, h, w = SHAPE["cin"], SHAPE["cout"], SHAPE["h"], SHAPE["w"]
     pix = batch * h * w
     algo = {
-        "quantize_current (quant_stream_kernel amax + cast, 2 launches)": ("hbm", pix * cin * 3.0),  # read bf16 once + write e4m3
+        "quantize_current (quant_resident_kernel: one launch, x read once)": ("hbm", pix * cin * 3.0),  # read bf16 once + write e4m3
         "conv3x3_fwd (conv_halo_t_fp8_kernel)": ("tensor", flops),
         "conv3x3_dgrad (conv_halo_t_fp8_kernel, weights read in place)": ("tensor", flops),
         "conv3x3_wgrad (accumulator memset + wgrad_fp8_kernel halo with the bf16 conversion)": ("tensor", flops),

@@ -929,7 +929,10 @@ __global__ void __launch_bounds__(kQuantThreads) weight_finalize_kernel(WeightBa
 constexpr int kResThreads = 512;
 constexpr int kResPiece = 16384;       // bytes per bulk copy / mbarrier
 constexpr int kResMaxPieces = 16;      // 256 KB > any CTA's shared memory
-constexpr int kResSmemCap = 232448 - 4096;  // dynamic bytes a CTA may use (static arrays and slack aside)
+// Dynamic bytes a CTA may use: the 227 KB per-CTA limit less 1 KB for the kernel's static
+// arrays (barriers, reduction scratch; about 300 bytes).  Config 2's conv input and weight
+// together need 228,720 bytes per CTA on 148 SMs (226,720 + 2,000).
+constexpr int kResSmemCap = 232448 - 1024;
 
 // Vectors (8 elements) of tensor t owned by CTA c of G: [V c / G, V (c + 1) / G).
 __device__ __forceinline__ int64_t res_slice_begin(int64_t vecs, int c, int G) { return vecs * c / G; }

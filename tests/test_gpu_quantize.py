@@ -300,6 +300,11 @@ def test_resident_quantize_matches_two_pass_and_oracle(cuda, shape):
             xq, sx, wq, sw = ops.quantize_current_pair(xd, wd)
             results[resident] = (q, s, xq, sx, wq, sw)
         _lib.set_quantize_resident(True)
+        if shape == (128, 128, 32, 32):  # config 2's conv input and weight fit one resident launch together
+            n0 = _lib.kernel_launch_count()
+            ops.quantize_current_pair(xd, wd)
+            torch.cuda.synchronize()
+            assert _lib.kernel_launch_count() - n0 == 1
         # captured and replayed
         static = xd.clone()
         side = torch.cuda.Stream()
