@@ -138,7 +138,7 @@ int get_encode_fn(EncodeTiledFn* out) {
 
 // 2-D byte matrix [rows][cols] (cols contiguous), box = 128 bytes x box_rows, 128B swizzle.
 int make_map_2d(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
-  EncodeTiledFn enc;
+  EncodeTiledFn enc = nullptr;
   if (int s = get_encode_fn(&enc)) return s;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
@@ -157,7 +157,7 @@ int make_map_2d(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, i
 // Used for the epilogue TMA stores (bf16 outputs, fp32 split-K partials).
 int make_map_2d_store(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, int64_t rows,
                       int64_t cols, int64_t ld, int box_cols, int box_rows) {
-  EncodeTiledFn enc;
+  EncodeTiledFn enc = nullptr;
   if (int s = get_encode_fn(&enc)) return s;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * elem_bytes};
@@ -198,7 +198,7 @@ bool conv_tile(int height, int width, ConvTile* t) {
 // Out-of-range coordinates (the conv padding ring, images past the batch) read as 0.
 int make_map_conv(CUtensorMap* map, const void* ptr, int batch, int height, int width, int channels,
                   const ConvTile& t) {
-  EncodeTiledFn enc;
+  EncodeTiledFn enc = nullptr;
   if (int s = get_encode_fn(&enc)) return s;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(width),
                         static_cast<cuuint64_t>(height), static_cast<cuuint64_t>(batch)};
@@ -304,7 +304,7 @@ int g_conv_algo = 0;
 // 128-pixel tile plus one halo row on each side.
 int make_map_conv_halo(CUtensorMap* map, const void* ptr, int batch, int height, int width, int channels,
                        int rows_per_tile) {
-  EncodeTiledFn enc;
+  EncodeTiledFn enc = nullptr;
   if (int s = get_encode_fn(&enc)) return s;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(width),
                         static_cast<cuuint64_t>(height), static_cast<cuuint64_t>(batch)};
@@ -402,7 +402,7 @@ int launch_halo_t(const CUtensorMap& ma, const CUtensorMap& mw, HaloTParams p, i
 // (128, 1, 128): one tap's 128 x 128 block, Cout rows of 128 Cin bytes (the
 // data-grad's MN-major A operand).
 int make_map_weight_taps(CUtensorMap* map, const void* wq, int cout, int cin) {
-  EncodeTiledFn enc;
+  EncodeTiledFn enc = nullptr;
   if (int s = get_encode_fn(&enc)) return s;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(cin), 9u, static_cast<cuuint64_t>(cout)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(cin), static_cast<cuuint64_t>(9) * cin};
@@ -951,7 +951,7 @@ int fp8_selftest_wait_timeout(uint64_t limit_ns, int* returned, fp8_stream_t str
   FP8_REQUIRE(limit_ns > 0 && limit_ns <= 1000000000ull, FP8_ERR_INVALID_ARGUMENT,
               "limit_ns must be in (0, 1e9]");
   FP8_REQUIRE(returned != nullptr && aligned(returned, 4), FP8_ERR_INVALID_ARGUMENT, "bad returned pointer");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   count_launches(1);
   FP8_CUDA_TRY(launch_kernel(wait_selftest_kernel, dim3(1), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream), 1,
@@ -961,7 +961,7 @@ int fp8_selftest_wait_timeout(uint64_t limit_ns, int* returned, fp8_stream_t str
 
 int fp8_device_error(int* code_out, fp8_stream_t stream) {
   FP8_REQUIRE(code_out != nullptr, FP8_ERR_INVALID_ARGUMENT, "code_out is NULL");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   FP8_CUDA_TRY(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
   int code = 0;
@@ -982,7 +982,7 @@ int fp8_kernel_launch_count(unsigned long long* out) {
 
 int fp8_sm_count(int* out) {
   FP8_REQUIRE(out != nullptr, FP8_ERR_INVALID_ARGUMENT, "out is NULL");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   *out = st->sm_count;
   return ok();
@@ -1004,7 +1004,7 @@ int fp8_quantize_current(const void* x_bf16, void* q_e4m3, float* scale_out, voi
   FP8_REQUIRE(scale_out != nullptr && aligned(scale_out, 4), FP8_ERR_INVALID_ARGUMENT, "bad scale_out");
   FP8_REQUIRE(n == 0 || (x_bf16 != nullptr && q_e4m3 != nullptr), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(aligned(x_bf16, 2), FP8_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   const bool vec = aligned(x_bf16, 16) && aligned(q_e4m3, 8);
@@ -1063,7 +1063,7 @@ int fp8_quantize_current_noalloc(const void* x_bf16, void* q_e4m3, float* scale_
   FP8_REQUIRE(scale_out != nullptr && aligned(scale_out, 4), FP8_ERR_INVALID_ARGUMENT, "bad scale_out");
   FP8_REQUIRE(n == 0 || (x_bf16 != nullptr && q_e4m3 != nullptr), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(aligned(x_bf16, 2), FP8_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   float* partials = nullptr;
   if (int s = noalloc_scratch(&partials)) return s;
@@ -1091,7 +1091,7 @@ int quantize_delayed_impl(const void* x_bf16, void* q_e4m3, const DelayedSource&
   FP8_REQUIRE(n >= 0, FP8_ERR_INVALID_ARGUMENT, "n must be >= 0");
   FP8_REQUIRE(n == 0 || (x_bf16 != nullptr && q_e4m3 != nullptr), FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(aligned(x_bf16, 2), FP8_ERR_INVALID_ARGUMENT, "x must be 2-byte aligned");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   // The cast pass writes one partial per CTA, so its grid is the partial count.
@@ -1204,7 +1204,7 @@ int fp8_conv3x3_fwd(const void* xq, const void* wq, void* y, const float* sx, co
               "unknown epilogue %d", epilogue);
   FP8_REQUIRE(epilogue == FP8_EPILOGUE_NONE || (bias != nullptr && aligned(bias, 16)), FP8_ERR_INVALID_ARGUMENT,
               "bias epilogue needs a 16-byte aligned bias");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   if (g_conv_algo != 1 && halo_applies(height, width)) {
     if (int s = launch_conv_halo(xq, wq, y, sx, sw, bias, epilogue, batch, height, width, cin, cout, true,
@@ -1248,7 +1248,7 @@ int fp8_conv3x3_dgrad(const void* dyq, const void* wq_t, void* dx, const float* 
   FP8_REQUIRE(dyq && wq_t && dx, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(aligned(dyq, 16) && aligned(wq_t, 16) && aligned(dx, 16), FP8_ERR_INVALID_ARGUMENT,
               "conv tensors must be 16-byte aligned");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   if (g_conv_algo != 1 && halo_applies(height, width)) {
     if (int s = launch_conv_halo(dyq, wq_t, dx, sdy, sw, nullptr, kEpiNone, batch, height, width, cout, cin, false,
@@ -1307,7 +1307,7 @@ int conv3x3_wgrad_impl(const void* xq, const void* dyq, void* dw, bool f32_out, 
   FP8_REQUIRE(xq && dyq && dw, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(aligned(xq, 16) && aligned(dyq, 16) && aligned(dw, 16), FP8_ERR_INVALID_ARGUMENT,
               "conv tensors must be 16-byte aligned");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const int64_t pixels = static_cast<int64_t>(batch) * height * width;
   const WGradPlan w = plan_wgrad(cout, 9ll * cin, pixels, split_k, st->sm_count);
@@ -1371,7 +1371,7 @@ int fp8_gemm(const void* a, const void* b, void* out, const float* sa, const flo
               "unknown epilogue %d", epilogue);
   FP8_REQUIRE(epilogue == FP8_EPILOGUE_NONE || (bias != nullptr && aligned(bias, 16)), FP8_ERR_INVALID_ARGUMENT,
               "bias epilogue needs a 16-byte aligned bias");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const int k_blocks = static_cast<int>((k + 127) / 128);
   int bm_sub, bn;
@@ -1418,7 +1418,7 @@ int fp8_gemm_wgrad(const void* dy, const void* x, void* dw, const float* sdy, co
   FP8_REQUIRE(dy && x && dw, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(aligned(dy, 16) && aligned(x, 16) && aligned(dw, 16), FP8_ERR_INVALID_ARGUMENT,
               "GEMM tensors must be 16-byte aligned");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const WGradPlan w = plan_wgrad(n, k, m, split_k, st->sm_count);
   const size_t need = static_cast<size_t>(n) * k * sizeof(float);
@@ -1509,7 +1509,7 @@ int fp8_gn_act_fwd(const void* x, int x_fp32, const float* gamma, const float* b
                    int c, int groups, void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
   if (int s = check_gn_args(x, out, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
   FP8_REQUIRE(stats != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const size_t need = gn_workspace(n, hw, c, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
@@ -1550,7 +1550,7 @@ int gn_act_quant_impl(const void* x, int x_fp32, const float* gamma, const float
                       void* workspace, size_t workspace_bytes, fp8_stream_t stream) {
   if (int s = check_gn_args(x, q_e4m3, gamma, beta, n, hw, c, groups, film_ld, film, p, eps)) return s;
   FP8_REQUIRE(stats != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const GnShape sh{n, hw, c, groups, 1, 1};
   const size_t gn_bytes = gn_workspace(n, hw, c, st->sm_count);
@@ -1612,7 +1612,7 @@ int gn_act_bwd_impl(const void* x, int x_fp32, const void* dy, const float* gamm
   FP8_REQUIRE(dx_add == nullptr || aligned(dx_add, 16), FP8_ERR_INVALID_ARGUMENT, "dx_add must be 16-byte aligned");
   FP8_REQUIRE(dy != nullptr && aligned(dy, 16), FP8_ERR_INVALID_ARGUMENT, "dy must be 16-byte aligned");
   FP8_REQUIRE(stats != nullptr && totals != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats / totals");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const size_t need = gn_workspace(n, hw, c, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
@@ -1669,7 +1669,7 @@ int fp8_gn_act_bwd_quant(const void* x, const void* dy, const float* gamma, cons
   FP8_REQUIRE(dxq != nullptr && aligned(dxq, 16), FP8_ERR_INVALID_ARGUMENT, "dxq must be 16-byte aligned");
   FP8_REQUIRE(stats != nullptr && totals != nullptr, FP8_ERR_INVALID_ARGUMENT, "NULL stats / totals");
   if (int s = check_window(window, window_len, window_pos, scale_used_out)) return s;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const size_t gn_bytes = gn_workspace(n, hw, c, st->sm_count);
   const size_t need =
@@ -1724,7 +1724,7 @@ int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const
         return s;
     return ok();
   }
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   MultiQuant m{};
   m.count = count;
@@ -1804,7 +1804,7 @@ int fp8_conv3x3_dgrad_w(const void* dyq, const void* wq, void* dx, const float* 
               FP8_ERR_WORKSPACE, "data-grad workspace too small: need %zu bytes for the re-laid-out weights", need);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   if (in_place) {
-    DeviceState* st;
+    DeviceState* st = nullptr;
     if (int s = device_state(&st)) return s;
     if (int s = launch_conv_halo(dyq, wq, dx, sdy, sw, nullptr, kEpiNone, batch, height, width, cout, cin, false,
                                  st->err_ptr, st->sm_count, cs, true))
@@ -1880,7 +1880,7 @@ int fp8_layer_norm_fwd(const void* x, int x_fp32, const float* gamma, const floa
   FP8_REQUIRE(tokens == 0 || (beta && mean_rstd), FP8_ERR_INVALID_ARGUMENT, "NULL beta / statistics");
   FP8_REQUIRE(eps > 0.0f, FP8_ERR_INVALID_ARGUMENT, "eps must be > 0");
   if (tokens == 0) return ok();
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   const int vpl = ln_vpl(c);
@@ -1908,7 +1908,7 @@ int fp8_layer_norm_bwd(const void* x, int x_fp32, const void* dy_bf16, const flo
   FP8_REQUIRE(tokens == 0 || (dy_bf16 && aligned(dy_bf16, 16) && mean_rstd && dgamma && dbeta),
               FP8_ERR_INVALID_ARGUMENT, "NULL or unaligned dy / statistics / parameter gradients");
   if (tokens == 0) return ok();
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   const size_t need = static_cast<size_t>(ln_bwd_ctas(tokens, st->sm_count)) * 2 * c * sizeof(float);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned(workspace, 16), FP8_ERR_WORKSPACE,
@@ -1945,7 +1945,7 @@ extern "C" int fp8_gn_param_grads(const float* totals, const void* film, int fil
   FP8_REQUIRE(totals && dgamma && dbeta, FP8_ERR_INVALID_ARGUMENT, "NULL tensor");
   FP8_REQUIRE(film == nullptr || (film_ld >= 2 * c && dfilm != nullptr && dfilm_ld >= 2 * c),
               FP8_ERR_INVALID_ARGUMENT, "FiLM gradients need film_ld, dfilm_ld >= 2c and a dfilm buffer");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   (void)st;
   FP8_CUDA_TRY(launch_kernel(gn_param_grads_kernel, dim3((c + 31) / 32), dim3(32 * kGnParamLanes), 0,
@@ -2022,7 +2022,7 @@ int fp8_resample_down2(const void* x, int x_dtype, float* y, int n, int h, int w
   FP8_REQUIRE(c % 8 == 0 && h % 2 == 0 && w % 2 == 0, FP8_ERR_UNSUPPORTED, "needs c %% 8 == 0 and even h, w");
   if (int s = check_resample(x, x_dtype, "x")) return s;
   if (int s = check_resample(y, 1, "y")) return s;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   const dim3 grid(resample_grid(static_cast<int64_t>(n) * (h / 2) * (w / 2) * c / 8, st->sm_count));
@@ -2042,7 +2042,7 @@ int fp8_resample_down2_bwd(const float* dy, void* dx, int dx_dtype, int n, int h
   FP8_REQUIRE(c % 8 == 0 && h % 2 == 0 && w % 2 == 0, FP8_ERR_UNSUPPORTED, "needs c %% 8 == 0 and even h, w");
   if (int s = check_resample(dy, 1, "dy")) return s;
   if (int s = check_resample(dx, dx_dtype, "dx")) return s;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   const dim3 grid(resample_grid(static_cast<int64_t>(n) * h * w * c / 8, st->sm_count));
@@ -2062,7 +2062,7 @@ int fp8_up_cat(const void* a, int a_dtype, const void* s, int s_dtype, void* y, 
   if (int r = check_resample(a, a_dtype, "a")) return r;
   if (int r = check_resample(s, s_dtype, "s")) return r;
   if (int r = check_resample(y, y_dtype, "y")) return r;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, a, s, y, nullptr, n, h, w, c1, c2, factor, false,
                               st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
@@ -2076,7 +2076,7 @@ int fp8_up_cat_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* ds,
   if (int r = check_resample(dy, y_dtype, "dy")) return r;
   if (int r = check_resample(da, a_dtype, "da")) return r;
   if (int r = check_resample(ds, s_dtype, "ds")) return r;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   if (int r = up_cat_dispatch(a_dtype, s_dtype, y_dtype, da, ds, const_cast<void*>(dy), nullptr, n, h, w, c1, c2,
                               factor, true, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
@@ -2091,7 +2091,7 @@ int fp8_up_cat_pair(const void* a, int a_dtype, const void* s, int s_dtype, floa
   if (int r = check_resample(s, s_dtype, "s")) return r;
   if (int r = check_resample(y, 1, "y")) return r;
   if (int r = check_resample(y_bf16, 0, "y_bf16")) return r;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   if (int r = up_cat_dispatch(a_dtype, s_dtype, 1, a, s, y, y_bf16, n, h, w, c1, c2, factor, false, st->sm_count,
                               reinterpret_cast<cudaStream_t>(stream)))
@@ -2106,7 +2106,7 @@ int fp8_up_cat_pair_bwd(const float* dy, const void* dy_bf16, void* da, int a_dt
   if (int r = check_resample(dy_bf16, 0, "dy_bf16")) return r;
   if (int r = check_resample(da, a_dtype, "da")) return r;
   if (int r = check_resample(ds, s_dtype, "ds")) return r;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   if (int r = up_cat_dispatch(a_dtype, s_dtype, 1, da, ds, const_cast<float*>(dy), const_cast<void*>(dy_bf16), n, h,
                               w, c1, c2, factor, true, st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
@@ -2160,7 +2160,7 @@ int fp8_quantize_weights_delayed(int count, const float* const* w, void* const* 
   b.chunk_begin[count] = chunks;
   FP8_REQUIRE(workspace != nullptr && aligned(workspace, 4) && workspace_bytes >= chunks * sizeof(float),
               FP8_ERR_WORKSPACE, "workspace too small: need %zu bytes", chunks * sizeof(float));
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   (void)st;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
@@ -2216,7 +2216,7 @@ int fp8_adamw_ema_step(int count, float* const* params, const float* const* grad
   FP8_REQUIRE(workspace != nullptr && aligned(workspace, 16) &&
                   workspace_bytes >= 16 + static_cast<size_t>(chunks) * sizeof(float),
               FP8_ERR_WORKSPACE, "workspace too small: need %zu bytes", 16 + static_cast<size_t>(chunks) * 4);
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   (void)st;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
@@ -2313,7 +2313,7 @@ int fp8_add_scale(const void* a, int a_dtype, const void* b, int b_dtype, void* 
   if (int r = check_resample(a, a_dtype, "a")) return r;
   if (int r = check_resample(b, b_dtype, "b")) return r;
   if (int r = check_resample(y, y_dtype, "y")) return r;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   if (int r = add_scale_dispatch(a_dtype, b_dtype, y_dtype, a, b, y, n, inv_divisor, false, st->sm_count,
                                  reinterpret_cast<cudaStream_t>(stream)))
@@ -2327,7 +2327,7 @@ int fp8_add_scale_bwd(const void* dy, int y_dtype, void* da, int a_dtype, void* 
   if (int r = check_resample(dy, y_dtype, "dy")) return r;
   if (int r = check_resample(da, a_dtype, "da")) return r;
   if (int r = check_resample(db, b_dtype, "db")) return r;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   if (int r = add_scale_dispatch(a_dtype, b_dtype, y_dtype, da, db, const_cast<void*>(dy), n, inv_divisor, true,
                                  st->sm_count, reinterpret_cast<cudaStream_t>(stream)))
@@ -2358,7 +2358,7 @@ int fp8_cast_batch(int count, const void* const* src, void* const* dst, const in
   }
   b.chunk_begin[count] = static_cast<int>(chunks);
   if (chunks == 0) return ok();
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   (void)st;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
@@ -2415,7 +2415,7 @@ int fp8_add_scale_bwd_quant(const void* dy, int y_dtype, void* da, int a_dtype, 
   FP8_REQUIRE(dbq_e4m3 != nullptr && aligned(dbq_e4m3, 16), FP8_ERR_INVALID_ARGUMENT,
               "dbq must be non-NULL and 16-byte aligned");
   if (int r = check_window(window, window_len, window_pos, scale_used_out)) return r;
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int r = device_state(&st)) return r;
   const int grid = add_scale_quant_grid(n, st->sm_count);
   FP8_REQUIRE(workspace != nullptr && workspace_bytes >= grid * sizeof(float) && aligned(workspace, 4),
@@ -2463,7 +2463,7 @@ int fp8_attention_fwd(const void* qkv, void* o, float* lse, float* scales, int b
   if (int s = attn_check(qkv, batch, seq, heads, head_dim, ld_qkv, ld_o)) return s;
   FP8_REQUIRE(o && aligned(o, 16) && lse && aligned(lse, 4) && scales && aligned(scales, 16), FP8_ERR_INVALID_ARGUMENT,
               "o must be 16-byte aligned, lse 4-byte and scales 16-byte");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   AttnParams p{};
   p.qkv = static_cast<const uint16_t*>(qkv);
@@ -2491,7 +2491,7 @@ int fp8_attention_bwd(const void* qkv, const void* o, const void* dout, const fl
   FP8_REQUIRE(o && aligned(o, 16) && dout && aligned(dout, 16) && dqkv && aligned(dqkv, 16) && lse &&
                   aligned(lse, 4) && scales && aligned(scales, 16),
               FP8_ERR_INVALID_ARGUMENT, "o, dout and dqkv must be 16-byte aligned, lse 4-byte and scales 16-byte");
-  DeviceState* st;
+  DeviceState* st = nullptr;
   if (int s = device_state(&st)) return s;
   AttnParams p{};
   p.qkv = static_cast<const uint16_t*>(qkv);
