@@ -529,6 +529,8 @@ def time_sweep(args, dev) -> dict:
         out[f"quantize delayed {tag}"] = {"ms": round(ms, 5), "flop": None, "bytes": 3 * n_el}
         ms = _time_calls(lambda i: ops.quantize_current(xs[i]), n_sets, 50, dev)
         out[f"quantize current {tag}"] = {"ms": round(ms, 5), "flop": None, "bytes": 3 * n_el}
+        if b == 512:  # too large to stay in shared memory: two passes read x twice (5 B/element)
+            out[f"quantize current {tag}"]["bytes_moved"] = 5 * n_el
         del xs
         torch.cuda.empty_cache()
     # config 5: the config-2 conv at batch 512, widths 128 and 256 (last: these run the GPU at its
@@ -569,6 +571,9 @@ def annotate_sweep(sweep: dict, peaks: dict) -> dict:
         if r["bytes"]:
             e["gbs"] = round(r["bytes"] / s / 1e9, 1)
             e["frac_hbm"] = round(e["gbs"] / peaks["hbm_gbs"], 4)
+        if r.get("bytes_moved"):  # the bytes the kernels actually move, where they exceed the algorithmic ones
+            e["gbs_moved"] = round(r["bytes_moved"] / s / 1e9, 1)
+            e["frac_hbm_moved"] = round(e["gbs_moved"] / peaks["hbm_gbs"], 4)
         res[name] = e
     return res
 
