@@ -215,8 +215,7 @@ def run_b200(args) -> None:
         if args.workload == "fwd":
             return (y,)
         dyq, sdy = ops.quantize_current(dy)
-        dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
-        dw = ops.conv3x3_wgrad(xq, dyq, sx, sdy)
+        dx, dw = ops.conv3x3_backward(dyq, wq, sdy, sw, xq, sx)  # dW on a side stream beside dX, as in autograd
         return (y, dx, dw)
 
     # eager warm-up: sets kernel attributes, counts launches of one step

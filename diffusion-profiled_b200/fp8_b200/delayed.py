@@ -75,9 +75,9 @@ def _conv_backward(ctx, dy, xq, wq, sx, sw):
         dyq, sdy = ops.quantize_delayed_window(dy, ctx.win_dy, ctx.pos, False)
     # an fp32 weight gets the bf16 dW widened by the reduce pass, not by an autograd cast
     widen = ctx.w_dtype == torch.float32
-    # weights re-laid out for the data-grad by the step's batched transpose, when it made them
-    dx = ops.conv3x3_dgrad(dyq, wq, sdy, sw) if ctx.wq_t is None else ops.conv3x3_dgrad_pre(dyq, ctx.wq_t, sdy, sw)
-    return dx, ops.conv3x3_wgrad(xq, dyq, sx, sdy, 0, widen)
+    # weights re-laid out for the data-grad by the step's batched transpose, when it made them;
+    # dW runs on a side stream beside dX
+    return ops.conv3x3_backward(dyq, wq, sdy, sw, xq, sx, 0, widen, ctx.wq_t)
 
 
 def _weight_q(ctx, weight, win_w, pos, pre):

@@ -256,8 +256,14 @@ class Conv2dFP8Specialized(torch.autograd.Function):
         assert weight_fp8.is_contiguous(memory_format=torch.channels_last)
         assert x_fp8.is_contiguous(memory_format=torch.channels_last)
 
-        dx = conv2d_bwd_input_fp8_prequantized(dy_fp8, weight_fp8, dy_scale, weight_scale)
-        dw = conv2d_bwd_weight_fp8_prequantized(x_fp8, dy_fp8, x_scale, dy_scale)
+        # conv2d_bwd_input_fp8_prequantized and conv2d_bwd_weight_fp8_prequantized (their checks,
+        # then one op that runs dW on a side stream beside dX)
+        xgrad_shapes(dy_fp8, weight_fp8, FP8_DTYPE)
+        batch, cin, cout, height, width = wgrad_shapes(x_fp8, dy_fp8, FP8_DTYPE)
+        for scale in (dy_scale, weight_scale, x_scale):
+            torch_checks_scale(scale, dy_fp8.device)
+        split_k = DW_CONFIG_BY_SHAPE[(cin, cout, height, width)]
+        dx, dw = ops.conv3x3_backward(dy_fp8, weight_fp8, dy_scale, weight_scale, x_fp8, x_scale, int(split_k))
         return dx, dw, None, None, None
 
 

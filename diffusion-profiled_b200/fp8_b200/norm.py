@@ -81,8 +81,7 @@ class GroupNormActConvFP8(torch.autograd.Function):
         dy = dy.to(torch.bfloat16).contiguous(memory_format=torch.channels_last)
         dyq, dy_scale_curr = ops.quantize_delayed(dy, dy_hist)
         ctx.dy_window.scatter_(0, ctx.window_pos.unsqueeze(0), dy_scale_curr.unsqueeze(0))
-        d_act = ops.conv3x3_dgrad(dyq, wq, dy_hist, w_hist)
-        dw = ops.conv3x3_wgrad(xq, dyq, x_hist, dy_hist)
+        d_act, dw = ops.conv3x3_backward(dyq, wq, dy_hist, w_hist, xq, x_hist)  # dW beside dX
         dx, dgamma, dbeta, dfilm = ops.gn_act_bwd(x, d_act, gamma, beta, film2, seed, stats, p, eps, groups)
         return dx, dgamma, dbeta, _film_grad(dfilm, film_shape), None, dw, None, None, None, None, None, None, None
 

@@ -487,6 +487,88 @@ def _(xq, dyq, sx, sdy, split_k=0, widen=False):
     )
 
 
+# Per-device side stream of conv3x3_backward (the weight gradient runs there beside the data
+# gradient).  Created on first use outside a CUDA-graph capture; while a capture is in progress
+# and none exists yet, the two gradients run one after the other on the current stream.
+_SIDE_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _side_stream(dev: torch.device) -> torch.cuda.Stream | None:
+    s = _SIDE_STREAMS.get(dev.index)
+    if s is None and not torch.cuda.is_current_stream_capturing():
+        s = _SIDE_STREAMS[dev.index] = torch.cuda.Stream(dev)
+    return s
+
+
+@torch.library.custom_op("fp8_b200::conv3x3_backward", mutates_args=())
+def conv3x3_backward(
+    dyq: torch.Tensor, wq: torch.Tensor, sdy: torch.Tensor, sw: torch.Tensor, xq: torch.Tensor, sx: torch.Tensor,
+    split_k: int = 0, widen: bool = False, wq_t: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """(dx, dw) of the 3x3 conv: conv3x3_dgrad (or conv3x3_dgrad_pre with ``wq_t``) and
+    conv3x3_wgrad, the same results, with the weight gradient launched on a side stream so
+    that it overlaps the data gradient (the two are independent given the e4m3 operands; the
+    reference computes them one after the other, fp8_kernels.py:875-913).  Outputs and
+    workspaces are allocated on the current stream before the fork, and the current stream
+    waits for the side stream before the op returns, so callers see ordinary stream order."""
+    dev = _require_cuda(dyq, wq, xq)
+    _check_conv_operand(dyq, "dy")
+    _check_conv_operand(xq, "x")
+    _check_scale(sdy, dev, "dy_scale")
+    _check_scale(sw, dev, "weight_scale")
+    _check_scale(sx, dev, "x_scale")
+    b, cout, h, w = dyq.shape
+    cin = xq.shape[1]
+    if (xq.shape[0], xq.shape[2], xq.shape[3]) != (b, h, w):
+        raise RuntimeError("x and dy batch/spatial dims differ")
+    if wq_t is None:
+        _check_conv_operand(wq, "weight")
+        if tuple(wq.shape) != (cout, cin, 3, 3):
+            raise RuntimeError(f"weight shape {tuple(wq.shape)} does not match Cout={cout} Cin={cin} 3x3")
+    elif wq_t.dtype != FP8_DTYPE or tuple(wq_t.shape) != (cin, 9 * cout) or not wq_t.is_contiguous():
+        raise RuntimeError("wq_t must be a contiguous [Cin, 9*Cout] float8_e4m3fn tensor")
+    lib = _lib.load()
+    dx = torch.empty((b, cin, h, w), device=dev, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    dw = torch.empty((cout, cin, 3, 3), device=dev, dtype=torch.float32 if widen else torch.bfloat16,
+                     memory_format=torch.channels_last)
+    with torch.cuda.device(dev):
+        ws_w_bytes = lib.fp8_conv3x3_wgrad_workspace_bytes(b, h, w, cin, cout, split_k)
+        ws_w = torch.empty(max(ws_w_bytes // 4, 4), device=dev, dtype=torch.float32)
+        ws_d_bytes = lib.fp8_conv3x3_dgrad_w_workspace_bytes(b, h, w, cin, cout) if wq_t is None else 0
+        ws_d = torch.empty((ws_d_bytes,), device=dev, dtype=torch.uint8) if ws_d_bytes else None
+        cur = torch.cuda.current_stream(dev)
+        side = _side_stream(dev)
+        if side is not None:
+            side.wait_stream(cur)
+        fn = "fp8_conv3x3_wgrad_f32" if widen else "fp8_conv3x3_wgrad"
+        _lib.check(
+            getattr(lib, fn)(
+                _ptr(xq), _ptr(dyq), _ptr(dw), _ptr(sx), _ptr(sdy), b, h, w, cin, cout, split_k, _ptr(ws_w),
+                ws_w.numel() * 4, c_void_p((side if side is not None else cur).cuda_stream),
+            ),
+            fn,
+        )
+        if wq_t is None:
+            _lib.call("fp8_conv3x3_dgrad_w", _ptr(dyq), _ptr(wq), _ptr(dx), _ptr(sdy), _ptr(sw), b, h, w, cin, cout,
+                      _ptr(ws_d), ws_d_bytes, _stream(dev))
+        else:
+            _lib.call("fp8_conv3x3_dgrad", _ptr(dyq), _ptr(wq_t), _ptr(dx), _ptr(sdy), _ptr(sw), b, h, w, cin, cout,
+                      _stream(dev))
+        if side is not None:
+            cur.wait_stream(side)
+    return dx, dw
+
+
+@conv3x3_backward.register_fake
+def _(dyq, wq, sdy, sw, xq, sx, split_k=0, widen=False, wq_t=None):
+    b, cout, h, w = dyq.shape
+    cin = xq.shape[1]
+    dx = torch.empty((b, cin, h, w), device=dyq.device, dtype=torch.bfloat16, memory_format=torch.channels_last)
+    dw = torch.empty((cout, cin, 3, 3), device=dyq.device, dtype=torch.float32 if widen else torch.bfloat16,
+                     memory_format=torch.channels_last)
+    return dx, dw
+
+
 # ----------------------------------------------------------------------------- GEMM (linear)
 def _check_2d_fp8(t: torch.Tensor, name: str) -> None:
     if t.dim() != 2 or t.dtype != FP8_DTYPE or not t.is_contiguous():
@@ -579,6 +661,7 @@ __all__ = [
     "conv3x3_fwd",
     "conv3x3_dgrad",
     "conv3x3_wgrad",
+    "conv3x3_backward",
     "gemm",
     "gemm_wgrad",
     "device_error",

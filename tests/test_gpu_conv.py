@@ -424,3 +424,41 @@ def test_wgrad_conversion_fused_and_separate_agree(cuda, fused):
     assert oracle.max_rel_err(dw, ref) <= TOL
     assert oracle.max_rel_err(dw_g, ref) <= TOL
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("cin,cout,h,w", [(128, 128, 32, 32), (256, 256, 8, 8), (512, 256, 16, 16)])
+def test_conv3x3_backward_overlapped_matches_separate_ops(cuda, cin, cout, h, w):
+    """conv3x3_backward (dW on a side stream beside dX) gives conv3x3_dgrad's dx bit for bit and
+    conv3x3_wgrad's dw within the oracle tolerance, eagerly, widened to fp32, with pre-transposed
+    weights, and replayed from a CUDA graph (the fork and join are captured)."""
+    from fp8_b200 import ops
+
+    b = 4
+    xq, sx = _rand_q((b, cin, h, w), seed=301 + cin, device=cuda)
+    dyq, sdy = _rand_q((b, cout, h, w), seed=302 + cout, device=cuda, scale=1e-2)
+    wq, sw = _rand_q((cout, cin, 3, 3), seed=303 + h, device=cuda, scale=0.05)
+    dx_ref = ops.conv3x3_dgrad(dyq, wq, sdy, sw)
+    dw_oracle = oracle.conv_dw(xq.cpu(), dyq.cpu(), sx.item(), sdy.item())
+    dx, dw = ops.conv3x3_backward(dyq, wq, sdy, sw, xq, sx)
+    torch.cuda.synchronize()
+    assert torch.equal(dx.view(torch.int16), dx_ref.view(torch.int16))
+    assert dw.dtype == torch.bfloat16 and dw.is_contiguous(memory_format=torch.channels_last)
+    assert oracle.max_rel_err(dw, dw_oracle) <= TOL
+    _, dw32 = ops.conv3x3_backward(dyq, wq, sdy, sw, xq, sx, 0, True)
+    assert dw32.dtype == torch.float32 and oracle.max_rel_err(dw32, dw_oracle) <= TOL
+    wq_t = ops.transpose_conv_weights([wq])[0]
+    dx_pre, _ = ops.conv3x3_backward(dyq, wq, sdy, sw, xq, sx, 0, False, wq_t)
+    assert torch.equal(dx_pre.view(torch.int16), ops.conv3x3_dgrad_pre(dyq, wq_t, sdy, sw).view(torch.int16))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ops.conv3x3_backward(dyq, wq, sdy, sw, xq, sx)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gdx, gdw = ops.conv3x3_backward(dyq, wq, sdy, sw, xq, sx)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(gdx.view(torch.int16), dx_ref.view(torch.int16))
+    assert oracle.max_rel_err(gdw, dw_oracle) <= TOL
+    assert ops.device_error() == 0
