@@ -106,8 +106,11 @@ def _is_dense(t: torch.Tensor) -> bool:
 
 
 def amax_scale(vals_f32: np.ndarray) -> np.float32:
-    """finalize_amax_kernel (fp8_kernels.py:90-102): amax/448 in fp32, or 1.0 for amax == 0."""
-    a = np.float32(np.max(np.abs(vals_f32))) if vals_f32.size else np.float32(0.0)
+    """finalize_amax_kernel (fp8_kernels.py:90-102): amax/448 in fp32, or 1.0 for amax == 0.
+    The amax ignores NaN: the reference's tl.max (fp8_kernels.py:62, :98) reduces with the
+    GPU's max.f32, which returns the other operand when one is NaN (np.fmax); a tensor that
+    is all NaN gets scale 1.0 either way."""
+    a = np.float32(np.fmax.reduce(np.abs(vals_f32).ravel())) if vals_f32.size else np.float32(0.0)
     return np.float32(a / np.float32(E4M3_MAX)) if a > 0 else np.float32(1.0)
 
 

@@ -11,6 +11,11 @@
  *         whenever |q0| >= 2^-11 (below that both bytes are a signed zero).
  * Part 3: byte equality for all 65,536 bf16 bit patterns (NaN, inf, zeros,
  *         subnormals) against sampled scales across the window.
+ * Part 4: the form without the clamp that current scaling uses when the tensor
+ *         holds no NaN (quant_resident_kernel): s = RN(amax / 448) for a bf16
+ *         amax, byte = e4m3(q1) with the sign bit of x or'd in, for every bf16
+ *         x with |x| <= amax (|x / s| stays below 449, so no clamp is needed),
+ *         against sampled amax values and every binade's edges.
  * Prints the mismatch counts; exit status 0 only when all are zero. */
 #include <math.h>
 #include <stdint.h>
@@ -70,10 +75,15 @@ static uint8_t new_byte(float x, float s, float r, float lb) {
   return e4m3(f_of((b_of(q1) & 0x7FFFFFFFu) | (b_of(xc) & 0x80000000u)));
 }
 
+static uint8_t fast_byte(float x, float s, float r) {
+  return e4m3(markstein_q1(x, s, r)) | (signbit(x) ? 0x80 : 0x00);
+}
+
 int main(int argc, char** argv) {
   const uint32_t stride2 = argc > 1 ? (uint32_t)atoi(argv[1]) : 997u;
   const uint32_t stride3 = argc > 2 ? (uint32_t)atoi(argv[2]) : 65521u;
-  long long bad1 = 0, bad2 = 0, bad3 = 0, n1 = 0, n2 = 0, n3 = 0;
+  const uint32_t stride4 = argc > 3 ? (uint32_t)atoi(argv[3]) : 5u;
+  long long bad1 = 0, bad2 = 0, bad3 = 0, bad4 = 0, n1 = 0, n2 = 0, n3 = 0, n4 = 0;
 #pragma omp parallel for reduction(+ : bad1, n1) schedule(static)
   for (uint32_t sm = 0; sm < (1u << 23); ++sm) {
     const float s = f_of(0x3F800000u | sm);
@@ -117,7 +127,21 @@ int main(int argc, char** argv) {
       }
     }
   }
-  printf("pairs %lld mismatches %lld; exponent sweep %lld mismatches %lld; bytes %lld mismatches %lld\n", n1, bad1,
-         n2, bad2, n3, bad3);
-  return (bad1 == 0 && bad2 == 0 && bad3 == 0) ? 0 : 1;
+#pragma omp parallel for reduction(+ : bad4, n4) schedule(dynamic, 64)
+  for (uint32_t ab = 1; ab <= 0x7F7Fu; ++ab) {
+    if (ab % stride4 != 0 && (ab & 0x7Fu) != 0 && (ab & 0x7Fu) != 0x7Fu && ab != 0x7F7Fu) continue;
+    const float amax = f_of(ab << 16);
+    const float s = amax / 448.0f;
+    if (!(s >= 0x1p-60f && s <= 0x1p100f)) continue;
+    const float r = 1.0f / s;
+    for (uint32_t xb = 0; xb < 65536u; ++xb) {
+      const float x = f_of(xb << 16);
+      if (isnan(x) || fabsf(x) > amax) continue;
+      bad4 += fast_byte(x, s, r) != ref_byte(x, s);
+      n4++;
+    }
+  }
+  printf("pairs %lld mismatches %lld; exponent sweep %lld mismatches %lld; bytes %lld mismatches %lld; "
+         "no-clamp bytes %lld mismatches %lld\n", n1, bad1, n2, bad2, n3, bad3, n4, bad4);
+  return (bad1 == 0 && bad2 == 0 && bad3 == 0 && bad4 == 0) ? 0 : 1;
 }

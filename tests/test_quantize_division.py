@@ -1,7 +1,9 @@
 """CPU check that the GPU cast's fp32 division shortcut (quantize.cuh,
-DivMarkstein) equals IEEE division for every bf16 significand against every fp32
+CastMarkstein) equals IEEE division for every bf16 significand against every fp32
 scale significand, and across exponents at the edges of the scale window where
-the kernel uses it.  The C program is compiled with gcc and run here."""
+the kernel uses it; and that the form without the clamp (current scaling of a
+tensor without NaN) gives the reference bytes for every |x| <= amax.  The C
+program is compiled with gcc and run here."""
 
 from __future__ import annotations
 
@@ -23,3 +25,4 @@ def test_markstein_division_is_exact(tmp_path):
     out = subprocess.run([exe], capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stdout + out.stderr
     assert "mismatches 0; exponent sweep" in out.stdout and out.stdout.strip().endswith("mismatches 0")
+    assert "no-clamp bytes" in out.stdout
