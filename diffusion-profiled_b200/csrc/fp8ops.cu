@@ -832,8 +832,8 @@ int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const floa
 // aligned: the caller's vec path), at least 12 MB of bf16 in all (below that the
 // two passes measured faster: a 6.3 MB input + weight pair 9.0 vs 9.9 us, 4.2 MB
 // 7.7 vs 9.5 us; at 17 MB the resident launch wins, 12.3 vs 13.0 us) and each
-// CTA's slices within its shared memory.  *launched = false otherwise.  It needs no workspace: the maxima meet in
-// one word per tensor from the library's pool of self-resetting counters.
+// CTA's slices within its shared memory.  *launched = false otherwise.  It needs no workspace: the barrier and
+// the maxima use words from the library's pool of self-resetting counters.
 int launch_quant_resident(const MultiQuant& m, DeviceState* st, cudaStream_t cs, bool* launched) {
   *launched = false;
   const int G = st->sm_count;
@@ -850,10 +850,16 @@ int launch_quant_resident(const MultiQuant& m, DeviceState* st, cudaStream_t cs,
     attr = cudaFuncSetAttribute(quant_resident_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kResSmemCap);
   });
   FP8_CUDA_TRY(attr);
-  unsigned int* arrive = fold_counter(st);
-  unsigned int* depart = fold_counter(st);
-  ResAmax am{};
-  for (int t = 0; t < m.count; ++t) am.word[t] = fold_counter(st);
+  ResSlices sl{};
+  ResSync sy{};
+  sy.arrive = fold_counter(st);
+  sy.depart = fold_counter(st);
+  for (int t = 0; t < m.count; ++t) {
+    sl.vq[t] = (m.n[t] / 8) / G;
+    sl.vr[t] = static_cast<int>((m.n[t] / 8) % G);
+    sy.amax[t] = fold_counter(st);
+    sy.nan[t] = fold_counter(st);
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(G));
   cfg.blockDim = dim3(kResThreads);
@@ -864,7 +870,7 @@ int launch_quant_resident(const MultiQuant& m, DeviceState* st, cudaStream_t cs,
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_resident_kernel, m, arrive, depart, am, st->err_ptr));
+  FP8_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_resident_kernel, m, sl, sy, st->err_ptr));
   count_launches(1);
   *launched = true;
   return FP8_OK;

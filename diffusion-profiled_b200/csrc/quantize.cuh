@@ -921,11 +921,10 @@ __global__ void __launch_bounds__(kQuantThreads) weight_finalize_kernel(WeightBa
 // is 227 KB per SM on 148 SMs): one CTA per SM (cooperative launch, so all are
 // resident), each CTA bulk-loads its contiguous slice of every tensor into
 // shared memory in 16 KB pieces (all in flight at once), takes the slice's |x|
-// max per tensor as the pieces land, stores its partial maxima, meets the other
-// CTAs at a grid barrier, folds the partials into each tensor's scale and casts
-// its slice from shared memory.  x is read from HBM once and q written once,
-// instead of a read, a second read and a write by two launches.  Bytes and
-// scales are those of the two-pass kernels.
+// max per tensor as the pieces land, meets the other CTAs at a grid barrier that
+// hands every CTA the tensors' maxima, and casts its slice from shared memory.
+// x is read from HBM once and q written once, instead of a read, a second read
+// and a write by two launches.  Bytes and scales are those of the two-pass kernels.
 constexpr int kResThreads = 512;
 constexpr int kResPiece = 16384;       // bytes per bulk copy / mbarrier
 constexpr int kResMaxPieces = 16;      // 256 KB > any CTA's shared memory
@@ -934,71 +933,97 @@ constexpr int kResMaxPieces = 16;      // 256 KB > any CTA's shared memory
 // together need 228,720 bytes per CTA on 148 SMs (226,720 + 2,000).
 constexpr int kResSmemCap = 232448 - 1024;
 
-// Vectors (8 elements) of tensor t owned by CTA c of G: [V c / G, V (c + 1) / G).
-__device__ __forceinline__ int64_t res_slice_begin(int64_t vecs, int c, int G) { return vecs * c / G; }
-
-// One zeroed word per tensor for the CTAs' |x| maxima (atomic max of the fp32 bits:
-// non-negative floats order like their bit patterns); the grid barrier reads them and
-// the last CTA through it zeroes them again.
-struct ResAmax {
-  unsigned int* word[kMaxMultiTensors];
+// Slices: tensor t has vecs = vq * G + vr vectors of 8 elements (the host splits
+// it); CTA c of G owns [floor(vecs c / G), floor(vecs (c + 1) / G)), computed as
+// vq c + (vr c) / G with a 32-bit division (vr c < G^2): the 64-bit divisions
+// this replaces took 0.45 us of the kernel's start.
+struct ResSlices {
+  int64_t vq[kMaxMultiTensors];
+  int vr[kMaxMultiTensors];
 };
-
-// Grid barrier of the resident quantize that also hands every CTA the tensors' maxima:
-// thread 0 arrives, waits (bounded) for the others, reads the words into amax_s and
-// departs; the last CTA to depart sets the counters and the words back to zero (every CTA
-// has read them before its departure).  Every CTA reads `count` words instead of all
-// CTAs' partial maxima (148 x 148 loads of the same few lines).
-__device__ __forceinline__ bool res_grid_barrier(unsigned int* arrive, unsigned int* depart, const ResAmax& am,
-                                                 int count, float* amax_s, int* err) {
-  __shared__ int passed;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(arrive, 1u);
-    const uint64_t t0 = globaltimer_ns();
-    int ok = 1;
-    while (*reinterpret_cast<volatile unsigned int*>(arrive) < gridDim.x) {
-      if (globaltimer_ns() - t0 > FP8_WAIT_TIMEOUT_NS) {
-        record_error(err, kErrTimeoutQuant);
-        ok = 0;
-        break;
-      }
-    }
-    __threadfence();
-    if (ok) {
-      for (int t = 0; t < count; ++t)
-        amax_s[t] = __uint_as_float(*reinterpret_cast<volatile unsigned int*>(am.word[t]));
-      if (atomicAdd(depart, 1u) == gridDim.x - 1) {
-        *arrive = 0u;
-        *depart = 0u;
-        for (int t = 0; t < count; ++t) *am.word[t] = 0u;
-      }
-    }
-    passed = ok;
-  }
-  __syncthreads();
-  return passed != 0;
+__device__ __forceinline__ int64_t res_slice_begin(int64_t vq, int vr, int c, int G) {
+  return vq * c + static_cast<int64_t>(static_cast<unsigned>(vr * c) / static_cast<unsigned>(G));
 }
 
-__global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQuant m, unsigned int* arrive,
-                                                                         unsigned int* depart, ResAmax am, int* err) {
+// Words of the grid barrier, all zero when the launch starts and zeroed again by
+// the last CTA to take a departure ticket (every CTA takes it after its reads).
+// The CTAs' |x| maxima meet in one atomic-max word per tensor (non-negative
+// floats order like their bit patterns), and a CTA that saw a NaN sets the
+// tensor's NaN word.  A CTA publishes its maxima, then arrives with a release
+// add; thread 0 of every CTA polls `arrive` with acquire loads and then reads
+// the words.  The departure ticket's value is only needed at the kernel's end.
+struct ResSync {
+  unsigned int* arrive;
+  unsigned int* depart;
+  unsigned int* amax[kMaxMultiTensors];
+  unsigned int* nan[kMaxMultiTensors];
+};
+
+// NaN-propagating packed max (max.NaN): the |x| max that shows whether a share holds a NaN.
+__device__ __forceinline__ uint32_t bf16x2_max_nan(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t absmax_vec2_nan(const uint4& a) {
+  return bf16x2_max_nan(bf16x2_max_nan(a.x & kAbsMask2, a.y & kAbsMask2),
+                        bf16x2_max_nan(a.z & kAbsMask2, a.w & kAbsMask2));
+}
+__device__ __forceinline__ bool bf16x2_has_nan(uint32_t w) {
+  return (w & 0x7FFFu) > 0x7F80u || ((w >> 16) & 0x7FFFu) > 0x7F80u;
+}
+
+// CastMarkstein without the clamp, for current scaling of a tensor that holds no
+// NaN: s = RN(amax / 448) and |x| <= amax bound |x / s| by 448 (1 + 2^-23), inside
+// the range where Markstein's step is exact, and cvt.satfinite saturates the rest.
+// The sign of each byte is x's sign bit or'd in (one byte permute and one logic
+// op per four elements), which also makes -0 the byte 0x80 as the reference's
+// division does.  tests/quantize_division_check.c (part 4) compares the bytes
+// with the reference for every bf16 x with |x| <= amax over every bf16 amax in
+// the scale window.  Measured: the cast phase of config 2's input 5.5 -> 3.0 us.
+struct CastMarksteinNoClamp {
+  float2 r2, ns2;
+  __device__ __forceinline__ explicit CastMarksteinNoClamp(const CastMarkstein& m) : r2(m.r2), ns2(m.ns2) {}
+  // Four bf16 (w0 low, w0 high, w1 low, w1 high) -> four e4m3 bytes in that order.
+  __device__ __forceinline__ uint32_t quad(uint32_t w0, uint32_t w1) const {
+    const float2 xa = make_float2(__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u));
+    const float2 xb = make_float2(__uint_as_float(w1 << 16), __uint_as_float(w1 & 0xFFFF0000u));
+    float2 qa = f32x2_mul(xa, r2), qb = f32x2_mul(xb, r2);
+    const float2 ea = f32x2_fma(qa, ns2, xa), eb = f32x2_fma(qb, ns2, xb);
+    qa = f32x2_fma(ea, r2, qa);
+    qb = f32x2_fma(eb, r2, qb);
+    const uint32_t lo = cvt_e4m3x2(qa.x, qa.y), hi = cvt_e4m3x2(qb.x, qb.y);
+    return __byte_perm(lo, hi, 0x5410) | (__byte_perm(w0, w1, 0x7531) & 0x80808080u);
+  }
+};
+__device__ __forceinline__ uint2 cast_vec(const uint4& a, const CastMarksteinNoClamp& d) {
+  return make_uint2(d.quad(a.x, a.y), d.quad(a.z, a.w));
+}
+
+__global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQuant m, ResSlices sl, ResSync sy,
+                                                                         int* err) {
   extern __shared__ __align__(128) uint8_t res_smem[];
   __shared__ __align__(8) uint64_t bars[kResMaxPieces];
-  __shared__ int abort_flag;
+  __shared__ int abort_flag, passed;
+  __shared__ unsigned int cta_max[kMaxMultiTensors], cta_nan[kMaxMultiTensors];
+  __shared__ unsigned int all_max[kMaxMultiTensors], all_nan[kMaxMultiTensors];
   pdl_wait();
   const int G = gridDim.x, c = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int64_t vbeg[kMaxMultiTensors], vcnt[kMaxMultiTensors], soff[kMaxMultiTensors];
   int64_t total = 0;
 #pragma unroll
-  for (int t = 0; t < kMaxMultiTensors; ++t) {
-    const int64_t vecs = t < m.count ? (m.n[t] >> 3) : 0;
-    vbeg[t] = res_slice_begin(vecs, c, G);
-    vcnt[t] = res_slice_begin(vecs, c + 1, G) - vbeg[t];
+  for (int t = 0; t < kMaxMultiTensors; ++t) {  // vq = vr = 0 beyond m.count
+    vbeg[t] = res_slice_begin(sl.vq[t], sl.vr[t], c, G);
+    vcnt[t] = res_slice_begin(sl.vq[t], sl.vr[t], c + 1, G) - vbeg[t];
     soff[t] = total;
     total += vcnt[t] * 16;
   }
   const int npieces = static_cast<int>((total + kResPiece - 1) / kResPiece);
+  if (threadIdx.x < kMaxMultiTensors) {
+    cta_max[threadIdx.x] = 0u;
+    cta_nan[threadIdx.x] = 0u;
+  }
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int i = 0; i < npieces; ++i) mbar_init(&bars[i], 1);
@@ -1019,26 +1044,23 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
       }
     }
   }
-  // |x| max per tensor as the copies land: warp w takes pieces w, w + 16, ..., so each
-  // warp waits on its own pieces' barriers only; within a piece, the part of each
-  // tensor it holds (offsets are multiples of 16 bytes).
+  // |x| max per tensor (NaN-propagating) as the copies land: warp w takes pieces w,
+  // w + 16, ..., so each warp waits on its own pieces' barriers only; within a piece,
+  // the part of each tensor it holds (offsets are multiples of 16 bytes).
   uint32_t m2[kMaxMultiTensors] = {0u, 0u, 0u, 0u};
   bool ok = true;
-  {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = warp; i < npieces; i += kResThreads / 32) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars[i], 0, &abort_flag, err, kErrTimeoutQuant));
-      if (!ok) break;
-      const int64_t p0 = static_cast<int64_t>(i) * kResPiece, p1 = min(total, p0 + kResPiece);
+  for (int i = warp; i < npieces; i += kResThreads / 32) {
+    ok = __all_sync(0xffffffffu, mbar_wait(&bars[i], 0, &abort_flag, err, kErrTimeoutQuant));
+    if (!ok) break;
+    const int64_t p0 = static_cast<int64_t>(i) * kResPiece, p1 = min(total, p0 + kResPiece);
 #pragma unroll
-      for (int u = 0; u < kMaxMultiTensors; ++u) {
-        const int64_t lo = max(p0, soff[u]), hi = min(p1, soff[u] + vcnt[u] * 16);  // empty for u >= count
-        uint32_t mu = 0u;
+    for (int u = 0; u < kMaxMultiTensors; ++u) {
+      const int64_t lo = max(p0, soff[u]), hi = min(p1, soff[u] + vcnt[u] * 16);  // empty for u >= count
+      uint32_t mu = 0u;
 #pragma unroll 4
-        for (int64_t o = lo + lane * 16; o < hi; o += 32 * 16)
-          mu = bf16x2_max(mu, absmax_vec2(ld_shared_v4(res_smem + o)));
-        m2[u] = bf16x2_max(m2[u], mu);
-      }
+      for (int64_t o = lo + lane * 16; o < hi; o += 32 * 16)
+        mu = bf16x2_max_nan(mu, absmax_vec2_nan(ld_shared_v4(res_smem + o)));
+      m2[u] = bf16x2_max_nan(m2[u], mu);
     }
   }
   if (!__syncthreads_and(ok)) {
@@ -1049,19 +1071,70 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
     __syncthreads();
     return;
   }
+  // The CTA's max per tensor.  A thread whose share held a NaN takes its share's max
+  // again without NaN (bf16 max skips it, as the reference's amax does) and flags it.
 #pragma unroll
   for (int t = 0; t < kMaxMultiTensors; ++t) {
     if (t < m.count) {
-      const float bm = block_max<kResThreads>(unpack_max2(m2[t]));
-      if (threadIdx.x == 0) atomicMax(am.word[t], __float_as_uint(bm));
+      uint32_t mt = m2[t];
+      const bool nan = bf16x2_has_nan(mt);
+      if (nan) {
+        mt = 0u;
+        for (int i = warp; i < npieces; i += kResThreads / 32) {
+          const int64_t p0 = static_cast<int64_t>(i) * kResPiece, p1 = min(total, p0 + kResPiece);
+          const int64_t lo = max(p0, soff[t]), hi = min(p1, soff[t] + vcnt[t] * 16);
+          for (int64_t o = lo + lane * 16; o < hi; o += 32 * 16)
+            mt = bf16x2_max(mt, absmax_vec2(ld_shared_v4(res_smem + o)));
+        }
+      }
+      const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(unpack_max2(mt)));
+      const unsigned wn = __reduce_or_sync(0xffffffffu, nan ? 1u : 0u);
+      if (lane == 0) {
+        atomicMax(&cta_max[t], wm);
+        if (wn) cta_nan[t] = 1u;
+      }
     }
   }
-  __shared__ float amax_s[kMaxMultiTensors];
-  if (!res_grid_barrier(arrive, depart, am, m.count, amax_s, err)) return;
+  __syncthreads();
+  unsigned int ticket = 0u;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int t = 0; t < kMaxMultiTensors; ++t) {
+      if (t < m.count) {
+        atomicMax(sy.amax[t], cta_max[t]);
+        if (cta_nan[t]) atomicOr(sy.nan[t], 1u);
+      }
+    }
+    red_release_gpu_add_u32(sy.arrive, 1u);  // orders the maxima above before the arrival
+    int okb = 1;
+    if (ld_acquire_gpu_u32(sy.arrive) < static_cast<unsigned>(G)) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_gpu_u32(sy.arrive) < static_cast<unsigned>(G)) {
+        if (globaltimer_ns() - t0 > FP8_WAIT_TIMEOUT_NS) {
+          record_error(err, kErrTimeoutGrid);
+          okb = 0;
+          break;
+        }
+      }
+    }
+    if (okb) {
+#pragma unroll
+      for (int t = 0; t < kMaxMultiTensors; ++t) {
+        if (t < m.count) {
+          all_max[t] = ld_relaxed_gpu_u32(sy.amax[t]);
+          all_nan[t] = ld_relaxed_gpu_u32(sy.nan[t]);
+        }
+      }
+      ticket = atom_add_acq_rel_gpu_u32(sy.depart, 1u);
+    }
+    passed = okb;
+  }
+  __syncthreads();
+  if (!passed) return;
 #pragma unroll
   for (int t = 0; t < kMaxMultiTensors; ++t) {
     if (t >= m.count) continue;
-    const float s = scale_from_amax(amax_s[t]);
+    const float s = scale_from_amax(__uint_as_float(all_max[t]));
     if (c == 0 && threadIdx.x == 0) *m.scale_out[t] = s;
     uint2* qv = reinterpret_cast<uint2*>(m.q[t] + vbeg[t] * 8);
     const uint8_t* src = res_smem + soff[t];
@@ -1077,10 +1150,24 @@ __global__ void __launch_bounds__(kResThreads, 1) quant_resident_kernel(MultiQua
       }
       for (; v < nv; v += kResThreads) qv[v] = cast_vec(ld_shared_v4(src + v * 16), div);
     };
-    if (markstein_applies(s))  // uniform over the grid
+    if (!markstein_applies(s))  // s and all_nan are uniform over the grid
+      cast_all(DivF64(s));
+    else if (all_nan[t])
       cast_all(make_markstein(s));
     else
-      cast_all(DivF64(s));
+      cast_all(CastMarksteinNoClamp(make_markstein(s)));
+  }
+  // The last CTA to take a ticket zeroes the words (every CTA read them before its ticket).
+  if (threadIdx.x == 0 && ticket == static_cast<unsigned>(G) - 1u) {
+    *sy.arrive = 0u;
+#pragma unroll
+    for (int t = 0; t < kMaxMultiTensors; ++t) {
+      if (t < m.count) {
+        *sy.amax[t] = 0u;
+        *sy.nan[t] = 0u;
+      }
+    }
+    *sy.depart = 0u;
   }
 }
 

@@ -134,6 +134,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return mbar_wait_limit(bar, parity, abort_flag, err, code, FP8_WAIT_TIMEOUT_NS);
 }
 
+// ---------------------------------------------------------------- cross-CTA words
+// gpu-scope accesses (through L2, not the SM's L1) for words that the CTAs of one
+// grid exchange: a release add, an acquire load, relaxed loads and an
+// acquire-release ticket.
+__device__ __forceinline__ void red_release_gpu_add_u32(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned int ld_relaxed_gpu_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu_u32(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // ---------------------------------------------------------------- grid barrier
 // Bounded grid barrier for a cooperative launch: every CTA arrives once on
 // `arrive`; the CTA whose departure is the last sets both counters back to 0.

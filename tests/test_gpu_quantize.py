@@ -328,3 +328,45 @@ def test_resident_quantize_matches_two_pass_and_oracle(cuda, shape):
         assert torch.equal(wq.cpu().view(torch.uint8), qwr.view(torch.uint8)) and sw.item() == swr.item()
     assert torch.equal(gq.cpu().view(torch.uint8), q2r.view(torch.uint8)) and gs.item() == s2r.item()
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("kind", ["finite", "nan", "inf"])
+def test_resident_quantize_special_values(cuda, kind):
+    """The resident launch's three casts against the oracle at config 2's size: every finite
+    bf16 value with |x| <= 1024 and -0 in the tensor (no NaN: the cast without the clamp),
+    the same with NaN planted in several CTAs' slices (amax ignores NaN; the clamped cast),
+    and with +-inf (amax inf: the double-reciprocal cast); alone and paired with a weight."""
+    from fp8_b200 import _lib, ops
+
+    shape = (128, 128, 32, 32)
+    n = int(np.prod(shape))
+    g = torch.Generator().manual_seed(7)
+    flat = (torch.randn(n, generator=g) * 3.0).to(torch.bfloat16).view(torch.int16).numpy().copy()
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    vals = oracle.bf16_bits_to_f32(bits)
+    finite = bits[np.isfinite(vals) & (np.abs(vals) <= 1024.0)]
+    flat[12345:12345 + finite.size] = finite.view(np.int16)
+    flat[n - finite.size:] = finite[::-1].view(np.int16)
+    flat[[1, n // 2, n - finite.size - 2]] = np.int16(-32768)  # -0
+    if kind == "nan":
+        flat[[0, n // 3, 2 * n // 3 + 5, n - 1]] = np.array([0x7FC0, 0xFFC0, 0x7F81, 0xFFFF],
+                                                            dtype=np.uint16).view(np.int16)
+    if kind == "inf":
+        flat[[777, n // 2 + 1]] = np.array([0x7F80, 0xFF80], dtype=np.uint16).view(np.int16)
+    x = torch.from_numpy(flat).view(torch.bfloat16).reshape(shape)
+    w = (torch.randn(128, 128, 3, 3, generator=g) * 0.05).to(torch.bfloat16)
+    qr, sr = oracle.quantize_current(x)
+    qwr, swr = oracle.quantize_current(w)
+    xd, wd = x.to(cuda), w.to(cuda)
+    _lib.set_quantize_resident(True)
+    n0 = _lib.kernel_launch_count()
+    q, s = ops.quantize_current(xd)
+    xq, sx, wq, sw = ops.quantize_current_pair(xd, wd)
+    torch.cuda.synchronize()
+    assert _lib.kernel_launch_count() - n0 == 2  # one resident launch each
+    for got, gs, ref, rs in ((q, s, qr, sr), (xq, sx, qr, sr), (wq, sw, qwr, swr)):
+        assert np.float32(gs.item()).tobytes() == np.float32(rs).tobytes(), (kind, gs.item(), rs)
+        b = _bytes(got)
+        bad = np.nonzero(b != ref)[0]
+        assert bad.size == 0, f"{kind}: {bad.size} mismatches at {bad[:5]}: {b[bad[:5]]} vs {ref[bad[:5]]}"
+    assert _lib.device_error() == 0
