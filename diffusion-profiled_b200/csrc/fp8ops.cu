@@ -829,10 +829,11 @@ int launch_stream(int grid, const uint16_t* x, uint8_t* q, int64_t n, const floa
 // Current scaling: amax pass (parts CTAs, one partial each), then the cast pass.
 // The shared-memory-resident current quantize (quant_resident_kernel) for the
 // tensors of `m`, if it applies: every n a multiple of 8 (x 16-byte, q 8-byte
-// aligned: the caller's vec path), at least 12 MB of bf16 in all (below that the
-// two passes measured faster: a 6.3 MB input + weight pair 9.0 vs 9.9 us, 4.2 MB
-// 7.7 vs 9.5 us; at 17 MB the resident launch wins, 12.3 vs 13.0 us) and each
-// CTA's slices within its shared memory.  *launched = false otherwise.  It needs no workspace: the barrier and
+// aligned: the caller's vec path), at least 6 MB of bf16 in all (measured on one
+// box: a 6.3 MB input + weight pair 8.0-11.3 us vs 12.8 us for the two passes, an
+// 8.4 MB input 7.8-9.2 vs 10.1 us; a 4.2 MB input alone 7.0-9.9 vs 7.7 us, so
+// smaller tensors keep the two passes) and each CTA's slices within its shared
+// memory.  *launched = false otherwise.  It needs no workspace: the barrier and
 // the maxima use words from the library's pool of self-resetting counters.
 int launch_quant_resident(const MultiQuant& m, DeviceState* st, cudaStream_t cs, bool* launched) {
   *launched = false;
@@ -843,7 +844,7 @@ int launch_quant_resident(const MultiQuant& m, DeviceState* st, cudaStream_t cs,
     bytes += m.n[t] * 2;
     smem += ((m.n[t] / 8 + G - 1) / G) * 16;
   }
-  if (bytes < (12 << 20) || smem > kResSmemCap) return FP8_OK;
+  if (bytes < (6 << 20) || smem > kResSmemCap) return FP8_OK;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {

@@ -261,8 +261,8 @@ int fp8_set_empty_tensor_history(int mode);
  * tensors with sizes that are multiples of 8: enable = 1 (default) runs it as one
  * cooperative launch that keeps each SM's share of the tensors in shared memory
  * between the amax and the cast (x read from memory once), where the shares fit
- * and the tensors hold at least 12 MB of bf16 (below that the two passes are
- * faster); enable = 0 always uses the two passes.
+ * and the tensors hold at least 6 MB of bf16 (below that the two passes are
+ * about as fast); enable = 0 always uses the two passes.
  * Same bytes and scales either way.  Process-wide; for benchmarks and tests. */
 int fp8_set_quantize_resident(int enable);
 

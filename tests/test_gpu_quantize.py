@@ -168,14 +168,17 @@ def test_quantize_current_large_tensor(cuda):
 
 @pytest.mark.parametrize("shape", [(128, 128, 32, 32), (3, 5, 7, 11), (1, 1, 1, 8192 + 13)])
 def test_quantize_current_grid_override(cuda, shape):
-    """Other grid sizes of the two passes, selected through the tuning override."""
+    """Other grid sizes of the two passes, selected through the tuning override (the
+    resident launch off, so that large tensors take the two passes too)."""
     from fp8_b200 import _lib
 
     try:
+        _lib.set_quantize_resident(False)
         _lib.set_quantize_override(1, 3)
         _check_current(_gen(shape, seed=sum(shape), scale=3.0))
     finally:
         _lib.set_quantize_override(0, 0)
+        _lib.set_quantize_resident(True)
 
 
 def test_quantize_current_captured_in_cuda_graph(cuda):
@@ -278,9 +281,9 @@ def test_quantize_delayed_window_replayed_in_cuda_graph(cuda):
         assert win[1 + r].item() == float(s_ref)
 
 
-@pytest.mark.parametrize("shape", [(128, 128, 32, 32), (128, 256, 16, 16), (1, 8, 1024, 1024)])
+@pytest.mark.parametrize("shape", [(128, 128, 32, 32), (128, 256, 16, 16), (1, 8, 1024, 1024), (32, 128, 32, 32)])
 def test_resident_quantize_matches_two_pass_and_oracle(cuda, shape):
-    """The one-launch shared-memory-resident current quantize (tensors of >= 12 MB whose
+    """The one-launch shared-memory-resident current quantize (tensors of >= 6 MB whose
     per-SM shares fit in shared memory) gives the two-pass kernels' and the oracle's bytes
     and scales, alone and paired with a weight, eagerly and replayed from a CUDA graph."""
     from fp8_b200 import _lib, ops
