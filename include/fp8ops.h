@@ -113,7 +113,9 @@ size_t fp8_quantize_multi_workspace_bytes(int count);
  * gets exactly the bytes fp8_quantize_current would write.  The reference
  * quantizes a conv's input and weight back to back (fp8_kernels.py:642-650 ->
  * quantize_fp8 :559-601, twice); this is that pair in two launches instead of
- * four.  x[i], q[i], scale_out[i], n[i] as for fp8_quantize_current. */
+ * four, or in one where the shared-memory-resident form applies
+ * (fp8_set_quantize_resident).  x[i], q[i], scale_out[i], n[i] as for
+ * fp8_quantize_current. */
 int fp8_quantize_current_multi(int count, const void* const* x_bf16, void* const* q_e4m3, float* const* scale_out,
                                const int64_t* n, void* workspace, size_t workspace_bytes, fp8_stream_t stream);
 
