@@ -78,6 +78,16 @@ def test_scale_of_zero_tensor_is_one():
     assert s == np.float32(1.0) and not q.any()
 
 
+def test_amax_ignores_nan():
+    # fp8_kernels.py:62, :98: tl.max reduces with the GPU's max.f32, which returns the
+    # other operand when one is NaN; only an all-NaN tensor falls back to scale 1.0
+    v = np.array([1.5, np.nan, -7.0, 0.25], dtype=np.float32)
+    assert oracle.amax_scale(v) == np.float32(np.float32(7.0) / np.float32(448.0))
+    assert oracle.amax_scale(np.full(5, np.nan, dtype=np.float32)) == np.float32(1.0)
+    q = oracle.cast_with_scale(v, oracle.amax_scale(v))
+    assert q[1] == 0x7E and q[2] == 0xFE  # NaN -> +448 by the clamp; -amax -> -448
+
+
 @pytest.mark.parametrize("name", ["randn", "zeros", "pow2", "ragged", "tiny"])
 def test_quantize_scales_match_reference_kernels(golden, name):
     bits = golden[f"q_{name}_x"].reshape(-1)
